@@ -1,0 +1,142 @@
+/* C ABI of the B200-native TaoMemory attention operator (libtao_b200.so).
+ *
+ * Plain pointers, sizes and a CUDA stream passed as `void*`; no framework types.
+ * All tensors are device memory, bf16 (`uint16_t` storage), contiguous, in the
+ * layouts stated per entry point.  Every function returns TAO_OK or an error
+ * code; tao_last_error() gives the message of the last failing call on the
+ * calling host thread.
+ *
+ * Reference interfaces replaced (LaurenceLong/tao-memory, tao_attention/):
+ *   tao_stream_step       -> StreamCache.process + fusion (tao_stream.py:919-979,
+ *                            operator.py:70-127), batched over requests; the
+ *                            decode form is operator.py:130-137
+ *   tao_state_init        -> StreamCache.__init__ / reset (tao_stream.py:795-851)
+ *   tao_window_attention  -> flash_attention.flash_attn_func (flash_attention.py:16-37)
+ *                            in the windowed form of tao_stream.py:760-787
+ *   tao_train_forward     -> operator.tao_attention forward (operator.py:42-54)
+ *   tao_train_backward    -> its autograd backward (selected_read.py:175-187 and
+ *                            the torch autograd around it)
+ */
+#ifndef TAO_B200_H
+#define TAO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TAO_OK 0
+#define TAO_ERR_ARG 1        /* shape / width / alignment / capacity argument      */
+#define TAO_ERR_POSITION 2   /* position does not match the request's cursor       */
+#define TAO_ERR_SEAL 3       /* chunk crosses a fine seal boundary                 */
+#define TAO_ERR_CAPACITY 4   /* fine bank or route capacity too small              */
+#define TAO_ERR_CUDA 5       /* CUDA launch / runtime error                        */
+#define TAO_ERR_DEVICE 6     /* a kernel reported an error (bounded wait expired)  */
+
+/* Geometry of the preset (TaoConfig, config.py:7-19).  fine_tokens, local_keep and
+ * coarse_group must be 256, 512 and 8; the schedule fields are free.  route_cap is
+ * the length of the route-id arrays of every state passed to one call. */
+typedef struct TaoPolicy {
+  int32_t fine_tokens;
+  int32_t local_keep;
+  int32_t coarse_group;
+  int32_t route_period;
+  int32_t layer_stagger;
+  int32_t budget_root_scale;
+  int32_t budget_offset;
+  int32_t route_cap;
+} TaoPolicy;
+
+/* Device-resident descriptor of one request's one-layer state.  The host writes
+ * it (pointers, capacities, cursor) and the kernels update `position`, `n_route`,
+ * `n_chosen`, the counters and the buffers it points to.
+ *
+ * Buffers (H heads, D width, all bf16 unless noted):
+ *   k_ring, v_ring, rk_ring : [H][768][D]  exact local window, slot = position % 768
+ *   fine_c                  : [H][cap_fines][D][D]
+ *   fine_z                  : [H][cap_fines][D]
+ *   page_z, page_w          : [H][cap_fines/8 + 1][D]  page log-partition and its
+ *                             softmax over pages (the page-normalisation memo)
+ *   route_ids               : int32 [H][route_cap]   selected fines, rank order
+ *   route_pages             : int32 [H][route_cap]   pages kept by the page top-K
+ */
+typedef struct TaoState {
+  void* k_ring;
+  void* v_ring;
+  void* rk_ring;
+  void* fine_c;
+  void* fine_z;
+  void* page_z;
+  void* page_w;
+  int32_t* route_ids;
+  int32_t* route_pages;
+  int64_t position;
+  int32_t n_route;
+  int32_t n_chosen;
+  int32_t cap_fines;
+  int32_t route_cap;
+  int32_t layer_index;
+  int32_t heads;
+  int32_t width;
+  int32_t arrive;        /* internal: per-step arrival counter, keep 0 */
+  int32_t route_refreshes;
+  int32_t seal_events;
+} TaoState;
+
+const char* tao_last_error(void);
+int tao_version(void);
+size_t tao_state_sizeof(void);
+
+/* Bytes of workspace tao_stream_step needs for n_states requests of `tokens`
+ * new tokens each (tokens == 1 for decode). */
+size_t tao_stream_workspace_bytes(int n_states, int tokens, int heads, int width,
+                                  int route_cap, const TaoPolicy* policy);
+
+/* Advance n_states requests by `tokens` new tokens each.
+ *   states      : device array of n_states pointers to device TaoState
+ *   host_pos    : host array of the n_states cursors (validated: chunk must not
+ *                 cross a seal boundary; fine capacity must suffice)
+ *   host_cap    : host array of the n_states fine capacities
+ *   q,k,v,raw_q,raw_k,out : [n_states][tokens][H][D]
+ *   fusion_a, fusion_b    : [H][D][3]
+ *   alpha                 : history scale (gain = bf16(2 * alpha))
+ *   workspace             : tao_stream_workspace_bytes(...) bytes, 256-byte aligned
+ * Reference: StreamCache.process + pointwise fusion (tao_stream.py:919-979,
+ * operator.py:79-99). */
+int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
+                    const int32_t* host_cap, const TaoPolicy* policy, int tokens,
+                    int heads, int width, const void* q, const void* k, const void* v,
+                    const void* raw_q, const void* raw_k, const void* fusion_a,
+                    const void* fusion_b, float alpha, void* out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Read and clear the device error word of a workspace (synchronises `stream`).
+ * Returns TAO_OK or TAO_ERR_DEVICE; *flags receives the raw bits. */
+int tao_stream_check(void* workspace, int* flags, void* stream);
+
+/* Copy `count` ring slots of one request into a token-ordered [count][H][D] buffer
+ * (used by export).  first_position is the absolute position of the first token. */
+int tao_ring_gather(const void* ring, int heads, int width, int64_t first_position,
+                    int count, void* out, void* stream);
+/* Inverse of tao_ring_gather (used by import). */
+int tao_ring_scatter(void* ring, int heads, int width, int64_t first_position, int count,
+                     const void* in, void* stream);
+
+/* Recompute the page memo (page_z, page_w) of one device state from its fine_z for
+ * `sealed` fines (after import).  `state` is the device TaoState.  Reference:
+ * LayerState._prepare_q1_page_memo (tao_stream.py:399-416). */
+int tao_state_rebuild_memo(void* state, int heads, int width, int sealed, void* stream);
+
+/* Windowed causal attention used by training (tao_stream.py:760-787 semantics):
+ * query t sees keys [max(0, 256*floor(t/256) - 512), t].  q,k,v,out [B][T][H][D];
+ * lse: fp32 [B][H][T] (log-sum-exp of the scaled scores, saved for backward). */
+int tao_window_attention(const void* q, const void* k, const void* v, void* out,
+                         float* lse, int batch, int tokens, int heads, int width,
+                         void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TAO_B200_H */

@@ -1,0 +1,544 @@
+"""CPU oracle for the TaoMemory attention operator -- TEST INFRASTRUCTURE ONLY.
+
+This module restates the reference algorithm (LaurenceLong/tao-memory,
+``tao_attention/``) with plain PyTorch CPU tensor operations, keeping every
+bf16 rounding point of the reference.  Only ``tests/``, ``__graft_entry__.smoke()``
+and the ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it,
+and only as the checker or the timed CPU baseline.  The product package
+``tao_memory_b200`` never imports it and has no CPU fallback.
+
+Pinning: ``tests/golden/*.pt`` hold outputs of the unmodified reference run in a
+container where it was importable (script: ``tests/golden/make_golden.py``);
+``tests/test_oracle_golden.py`` checks this restatement against them.
+
+Scope: the preset path ``index_only_page_memo`` (``coarse_index_only=True``,
+``fine_writer="softmax"``), streaming prefill/decode for one request and
+training forward/backward for batch B.
+
+Rounding conventions (probed against torch CPU 2.11):
+* ``F.softmax``, ``Tensor.sum`` and ``Tensor.exp`` on bf16 compute in fp32 and
+  round once;
+* ``torch.logsumexp`` on bf16 is a composite (amax, sub, exp, sum, log, add)
+  that rounds to bf16 after every step.
+"""
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+BF16 = torch.bfloat16
+F32 = torch.float32
+
+
+def _r(x):
+    """Round an fp32 tensor to bf16 and back (a reference ``.to(bf16)`` point)."""
+    return x.to(BF16).to(F32)
+
+
+# --------------------------------------------------------------------------
+# Integer schedule (tao_stream.py:29-53, config.py:54-60)
+# --------------------------------------------------------------------------
+
+def budget(count, root_scale=2, offset=2):
+    if count <= 0:
+        return 0
+    square = root_scale * count
+    root = math.isqrt(square)
+    root += int(root * root < square)
+    return min(count, root + offset)
+
+
+def routed_counts(completed, pending, group=8, root_scale=2, offset=2):
+    """tao_stream.py:29-37."""
+    coarse_budget = budget(group * completed, root_scale, offset)
+    coarse = min(completed, (2 * coarse_budget + group - 1) // group)
+    eligible = group * coarse + pending
+    return coarse, eligible, min(eligible, budget(group * completed + pending,
+                                                  root_scale, offset))
+
+
+def topk_oldest(scores, count):
+    """Stable descending argsort; the lower (older) index wins exact ties
+    (tao_stream.py:50-53)."""
+    return scores.argsort(dim=-1, descending=True, stable=True)[
+        ..., :min(count, scores.shape[-1])]
+
+
+# --------------------------------------------------------------------------
+# Kernels restated (Triton -> torch CPU)
+# --------------------------------------------------------------------------
+
+def local_attention(q, k, v):
+    """Suffix-aligned causal SDPA on [B,T,H,D] (flash_attention.py:16-37)."""
+    query, key, value = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    if q.shape[1] == k.shape[1]:
+        out = F.scaled_dot_product_attention(query, key, value, is_causal=True)
+    elif q.shape[1] == 1:
+        out = F.scaled_dot_product_attention(query, key, value, is_causal=False)
+    else:
+        rows = k.shape[1] - q.shape[1] + torch.arange(q.shape[1])
+        cols = torch.arange(k.shape[1])
+        allowed = cols[None, :] <= rows[:, None]
+        out = F.scaled_dot_product_attention(query, key, value, attn_mask=allowed,
+                                             is_causal=False)
+    return out.transpose(1, 2)
+
+
+def seal_block(raw_k, v):
+    """Softmax fine writer for one block [B,256,H,D] -> z [B,H,D], C [B,H,D,D]
+    (tao_stream.py:66-76)."""
+    dt = raw_k.dtype
+    maximum = raw_k.amax(dim=1, keepdim=True)
+    exponent = (raw_k - maximum).exp().to(dt)
+    partition = exponent.sum(dim=1, keepdim=True).to(dt)
+    prob = (exponent / partition).to(dt)
+    z = (maximum.squeeze(1) + partition.squeeze(1).log()).to(dt)
+    with torch.autocast(device_type="cpu", enabled=False):
+        c = torch.einsum("bthd,bthe->bhde", prob, v).to(dt)
+    return z, c
+
+
+def seal_all(raw_k, v, fine=256):
+    """Training writer over all complete blocks but the last (tao_stream.py:80-123):
+    returns z [B,H,S,D], C [B,H,S,D,D] with S = T//fine - 1."""
+    b, total, heads, d = raw_k.shape
+    s = total // fine - 1
+    keys = raw_k[:, :s * fine].reshape(b, s, fine, heads, d)
+    values = v[:, :s * fine].reshape(b, s, fine, heads, d)
+    dt = raw_k.dtype
+    maximum = keys.amax(dim=2, keepdim=True)
+    exponent = (keys - maximum).exp().to(dt)
+    partition = exponent.sum(dim=2, keepdim=True).to(dt)
+    prob = (exponent / partition).to(dt)
+    z = (maximum.squeeze(2) + partition.squeeze(2).log()).to(dt)
+    with torch.autocast(device_type="cpu", enabled=False):
+        c = torch.einsum("bsihd,bsihe->bhsde", prob, values).to(dt)
+    return z.permute(0, 2, 1, 3), c
+
+
+def fine_read(hv, page_z, fine_z, selected_id, fine_c, group=8):
+    """query_fresh_fine.py:30-69 restated.
+
+    hv [B,Q,H,P,D], page_z [B,H,P,D], fine_z [B,H,S,D], selected_id [B,Q,H,M],
+    fine_c [B,H,S,D,D] -> (channel [B,Q,H,M,D], num, den, fine).
+    """
+    b, q, h, p, d = hv.shape
+    m = selected_id.shape[-1]
+    ids = selected_id.expand(b, q, h, m)
+    page = ids // group
+    idx = ids[..., None].expand(b, q, h, m, d)
+    z = fine_z[:, None].expand(b, q, h, -1, d).gather(3, idx).float()
+    pz = page_z[:, None].expand(b, q, h, -1, d).gather(3, page[..., None].expand(b, q, h, m, d)).float()
+    hvs = hv.gather(3, page[..., None].expand(b, q, h, m, d)).float()
+    w = _r(torch.exp(_r(z - pz)))
+    ch = _r(hvs * w)
+    bi = torch.arange(b)[:, None, None, None]
+    hi = torch.arange(h)[None, None, :, None]
+    csel = fine_c[bi, hi, ids].float()
+    acc = torch.einsum("bqhmd,bqhmde->bqhe", ch, csel)
+    num = acc.to(hv.dtype)
+    chan = ch.to(hv.dtype)
+    den = chan.sum(-1).sum(-1, keepdim=True).to(hv.dtype)
+    return chan, num, den, (num / den).to(hv.dtype)
+
+
+def fusion_scores(raw_q, a, b, coarse_present, fine_present):
+    """fusion_pointwise.py:10-47 restated -> [B,T,H,D,3] in raw_q.dtype."""
+    lb = math.log(int(coarse_present) + int(fine_present)) if (coarse_present or fine_present) else 0.0
+    qf = raw_q.float()[..., None]
+    s = _r(_r(_r(a.float()) * qf) + _r(b.float()))
+    s0 = _r(s[..., 0] + _r(torch.tensor(lb)))
+    s1 = s[..., 1] if coarse_present else torch.full_like(s0, -math.inf)
+    s2 = s[..., 2] if fine_present else torch.full_like(s0, -math.inf)
+    return torch.stack((s0, s1, s2), -1).to(raw_q.dtype)
+
+
+def fusion_weighted_sum(rho, local, coarse, fine, gain):
+    """fusion_pointwise.py:50-92 restated (every cast kept)."""
+    g = gain.float()
+    rl, rc, rf = (rho[..., i].float() for i in range(3))
+    lt = _r(rl * _r(2.0 * local.float()))
+    ct = _r(rc * _r(g * coarse.float()))
+    ft = _r(rf * _r(g * fine.float()))
+    return _r(_r(lt + ct) + ft).to(local.dtype)
+
+
+def fuse_inference(raw_q, local, fine, fa, fb, alpha, fine_on):
+    """operator.py:86-99: 3-way pointwise gate; no history -> local."""
+    if not fine_on:
+        return local
+    score = fusion_scores(raw_q, fa, fb, False, True)
+    rho = F.softmax(score, dim=-1).to(raw_q.dtype)
+    gain = torch.full((), 2 * alpha, dtype=raw_q.dtype)
+    return fusion_weighted_sum(rho, local, torch.zeros_like(fine), fine, gain)
+
+
+# --------------------------------------------------------------------------
+# Streaming state (tao_stream.py:126-527, 790-1094) -- preset path only
+# --------------------------------------------------------------------------
+
+class OracleStream:
+    """One request's one-layer state: exact local window + sealed fines + pages."""
+
+    FINE, KEEP, GROUP, PERIOD, STAGGER = 256, 512, 8, 24, 2
+
+    def __init__(self, layer_index=0):
+        self.layer_index = layer_index
+        self.position = 0
+        self.local = None              # (k, v, raw_k) [1,L,H,D]
+        self.pages = []                # (page_z [1,H,D], fine_z [1,H,8,D])
+        self.pending = []              # fine_z [1,H,D]
+        self.fine_c = None             # [1,H,S,D,D]
+        self.route_ids = None          # (chosen_page [1,1,H,K], selected_id [1,1,H,M]) int64
+        self.state_version = 0
+        self.route_refreshes = 0
+        self.fine_seal_events = 0
+
+    @property
+    def serve_limit(self):
+        return self.KEEP + self.FINE
+
+    def next_chunk(self, desired):
+        current = 0 if self.local is None else self.local[0].shape[1]
+        return min(desired, self.FINE, self.serve_limit - current)
+
+    # -- history ---------------------------------------------------------
+    def _page_tables(self, dtype):
+        page_z = [pz for pz, _ in self.pages]
+        fine_z = [fz for _, fz in self.pages]
+        if self.pending:
+            pending_z = torch.stack(self.pending, dim=2)
+            page_z.append(torch.logsumexp(pending_z, dim=2).to(dtype))
+            fine_z.append(pending_z)
+        page_z = torch.stack(page_z, dim=2)
+        return page_z, torch.cat(fine_z, dim=2)
+
+    def _route(self, hv, page_z, fine_z):
+        """Anchor routing (tao_stream.py:310-357); hv [1,1,H,P,D]."""
+        b, length, heads, _, d = hv.shape
+        completed, pending = len(self.pages), len(self.pending)
+        coarse, _, count = routed_counts(completed, pending, self.GROUP)
+        pages, ids = [], []
+        chosen = None
+        if coarse:
+            mass = hv[..., :completed, :].sum(-1)
+            chosen = topk_oldest(mass, coarse).sort(-1).values
+            seg = torch.arange(self.GROUP)
+            pages.append(chosen.unsqueeze(-1).expand(b, length, heads, coarse, self.GROUP)
+                         .reshape(b, length, heads, coarse * self.GROUP))
+            ids.append((chosen.unsqueeze(-1) * self.GROUP + seg)
+                       .reshape(b, length, heads, coarse * self.GROUP))
+        if pending:
+            pid = torch.arange(pending).view(1, 1, 1, pending).expand(b, length, heads, pending)
+            pages.append(torch.full_like(pid, completed))
+            ids.append(completed * self.GROUP + pid)
+        pages = torch.cat(pages, -1)
+        ids = torch.cat(ids, -1)
+        zc = fine_z[:, None].expand(-1, length, -1, -1, -1).gather(3, ids[..., None].expand(-1, -1, -1, -1, d))
+        pzc = page_z[:, None].expand(-1, length, -1, -1, -1).gather(3, pages[..., None].expand(-1, -1, -1, -1, d))
+        weight = (zc - pzc).exp().to(hv.dtype)
+        channel = hv.gather(3, pages[..., None].expand(-1, -1, -1, -1, d))
+        mass = (channel * weight).to(hv.dtype).sum(-1)
+        selected = topk_oldest(mass, count)
+        selected_id = ids.gather(-1, selected)
+        self.route_ids = (chosen if coarse else pages[..., :0], selected_id)
+
+    def _read_segment(self, raw_q, refresh):
+        dtype = raw_q.dtype
+        h = F.softmax(raw_q, dim=-1).to(dtype)
+        page_z, fine_z = self._page_tables(dtype)
+        page_weight = F.softmax(page_z, dim=2).to(dtype)
+        hv = (h.unsqueeze(3) * page_weight[:, None]).to(dtype)
+        if refresh:
+            self._route(hv[:, :1], page_z, fine_z)
+        ids = self.route_ids[1].expand(-1, raw_q.shape[1], -1, -1)
+        return fine_read(hv, page_z, fine_z, ids, self.fine_c, self.GROUP)[-1]
+
+    def read(self, raw_q, position):
+        """_read_progressive (tao_stream.py:196-227); returns (fine, fine_on)."""
+        if not self.pages and not self.pending:
+            return torch.zeros_like(raw_q), False
+        first_fine = self.serve_limit
+        first_turn = first_fine + self.STAGGER * self.layer_index
+        out = []
+        offset = 0
+        while offset < raw_q.shape[1]:
+            absolute = position + offset
+            refresh = (absolute == first_fine or
+                       (absolute >= first_turn and (absolute - first_turn) % self.PERIOD == 0))
+            nxt = (first_turn if absolute < first_turn else
+                   first_turn + self.PERIOD * ((absolute - first_turn) // self.PERIOD + 1))
+            count = min(raw_q.shape[1] - offset, nxt - absolute)
+            out.append(self._read_segment(raw_q[:, offset:offset + count], refresh))
+            if refresh:
+                self.route_refreshes += 1
+            offset += count
+        return torch.cat(out, dim=1), True
+
+    def seal(self, raw_k, v):
+        """LayerState.seal/append_fine (tao_stream.py:435-512), index-only pages."""
+        z, c = seal_block(raw_k, v)
+        self.state_version += 1
+        c = c.unsqueeze(2)
+        self.fine_c = c if self.fine_c is None else torch.cat((self.fine_c, c), dim=2)
+        self.pending.append(z)
+        if len(self.pending) == self.GROUP:
+            zs = torch.stack(self.pending, dim=2)
+            self.pages.append((torch.logsumexp(zs, dim=2).to(zs.dtype), zs))
+            self.pending = []
+
+    # -- one chunk (StreamCache.process, tao_stream.py:919-979) ----------
+    def process(self, raw_q, raw_k, q, k, v):
+        if self.local is None:
+            ak, av, ar = k, v, raw_k
+        else:
+            ak = torch.cat((self.local[0], k), 1)
+            av = torch.cat((self.local[1], v), 1)
+            ar = torch.cat((self.local[2], raw_k), 1)
+        if ak.shape[1] > self.serve_limit:
+            raise ValueError("chunk crosses a fine seal boundary")
+        local = local_attention(q, ak, av)
+        fine, fine_on = self.read(raw_q, self.position)
+        if ak.shape[1] == self.serve_limit:
+            self.fine_seal_events += 1
+            self.seal(ar[:, :self.FINE], av[:, :self.FINE])
+            self.local = (ak[:, -self.KEEP:].clone(), av[:, -self.KEEP:].clone(),
+                          ar[:, -self.KEEP:].clone())
+        else:
+            self.local = (ak, av, ar)
+        return local, fine, fine_on
+
+    def step(self, q, k, v, raw_q, raw_k, fa, fb, alpha):
+        """tao_attention_prefill (operator.py:70-127): chunked at seal boundaries."""
+        outs = []
+        start = 0
+        while start < q.shape[1]:
+            width = self.next_chunk(q.shape[1] - start)
+            sl = slice(start, start + width)
+            local, fine, fine_on = self.process(raw_q[:, sl], raw_k[:, sl], q[:, sl], k[:, sl], v[:, sl])
+            outs.append(fuse_inference(raw_q[:, sl], local, fine, fa, fb, alpha, fine_on))
+            self.position += width
+            start += width
+        return torch.cat(outs, dim=1)
+
+    # -- snapshot in the reference's dictionary format -------------------
+    def export(self):
+        """StreamCache.export keys (tao_stream.py:853-877)."""
+        clone = lambda t: t.detach().clone()
+        return {
+            "layer_index": self.layer_index,
+            "position": self.position,
+            "local": None if self.local is None else tuple(map(clone, self.local)),
+            "packed_fine_c": None if self.fine_c is None else clone(self.fine_c),
+            "pages": [(clone(pz), None, clone(fz)) for pz, fz in self.pages],
+            "pending_z": [clone(z) for z in self.pending],
+            "route_ids": None if self.route_ids is None else tuple(map(clone, self.route_ids)),
+            "state_version": self.state_version,
+            "route_refreshes": self.route_refreshes,
+            "fine_seal_events": self.fine_seal_events,
+        }
+
+    @classmethod
+    def from_export(cls, saved):
+        st = cls(saved["layer_index"])
+        st.position = saved["position"]
+        cpu = lambda t: t.detach().to("cpu").clone()
+        st.local = None if saved["local"] is None else tuple(map(cpu, saved["local"]))
+        st.fine_c = None if saved["packed_fine_c"] is None else cpu(saved["packed_fine_c"])
+        st.pages = [(cpu(pz), cpu(fz)) for pz, _, fz in saved["pages"]]
+        st.pending = [cpu(z) for z in saved["pending_z"]]
+        st.route_ids = None if saved["route_ids"] is None else tuple(map(cpu, saved["route_ids"]))
+        st.state_version = saved["state_version"]
+        st.route_refreshes = saved.get("route_refreshes", 0)
+        st.fine_seal_events = saved.get("fine_seal_events", 0)
+        return st
+
+
+# --------------------------------------------------------------------------
+# Training read (tao_stream.py:530-787) and tao_attention (operator.py:21-54)
+# --------------------------------------------------------------------------
+
+class _SelectedRead(torch.autograd.Function):
+    """selected_read.py:156-187 restated: forward N/D and the reference adjoints
+    with their bf16 rounding points (dA, dhv in slot order, dw, per-tile dC)."""
+
+    @staticmethod
+    def forward(ctx, hv, w, ids, pages, fine_c):
+        # hv [B,Q,H,P,D]; w [B,H,S,D]; ids/pages [B,Q,H,M]; fine_c [B,H,S,D,D]
+        b, q, h, m = ids.shape
+        d = hv.shape[-1]
+        hvs = hv.gather(3, pages[..., None].expand(b, q, h, m, d)).float()
+        ws = w[:, None].expand(b, q, h, -1, d).gather(3, ids[..., None].expand(b, q, h, m, d)).float()
+        a = _r(hvs * ws)
+        bi = torch.arange(b)[:, None, None, None]
+        hi = torch.arange(h)[None, None, :, None]
+        csel = fine_c[bi, hi, ids].float()
+        num = torch.einsum("bqhmd,bqhmde->bqhe", a, csel).to(hv.dtype)
+        den = _r(a.sum(-1)).sum(-1, keepdim=True).to(hv.dtype)
+        ctx.save_for_backward(hv, w, ids, pages, fine_c)
+        return num, den
+
+    @staticmethod
+    def backward(ctx, gn, gd):
+        hv, w, ids, pages, fine_c = ctx.saved_tensors
+        b, q, h, m = ids.shape
+        d = hv.shape[-1]
+        p = hv.shape[3]
+        bi = torch.arange(b)[:, None, None, None]
+        hi = torch.arange(h)[None, None, :, None]
+        csel = fine_c[bi, hi, ids].float()                       # b,q,h,m,d,e
+        gnf = gn.float()
+        # dA = bf16(bf16(g . C^T) + gd)  (selected_read.py:55-77)
+        nda = _r(torch.einsum("bqhe,bqhmde->bqhmd", gnf, csel))
+        da = _r(nda + gd.float()[..., None])                      # [b,q,h,m,d] (gd [b,q,h,1])
+        ws = w[:, None].expand(b, q, h, -1, d).gather(3, ids[..., None].expand(b, q, h, m, d)).float()
+        hvs = hv.gather(3, pages[..., None].expand(b, q, h, m, d)).float()
+        # dhv: per page, bf16 accumulation in slot order (selected_read.py:80-97)
+        dhv = torch.zeros(b, q, h, p, d)
+        prod = _r(da * ws)
+        for slot in range(m):
+            onehot = F.one_hot(pages[..., slot], p).bool()        # b,q,h,p
+            dhv = torch.where(onehot[..., None], _r(dhv + prod[..., slot, None, :]), dhv)
+        # dw: fp32 sum of bf16(dA*hv) over selected pairs (selected_read.py:100-122)
+        prod_w = _r(da * hvs)
+        dw = torch.zeros(b, h, w.shape[2], d)
+        dw.index_put_((bi.expand(b, q, h, m), hi.expand(b, q, h, m), ids), prod_w, accumulate=True)
+        # dC: per fine, bf16(sum over this example's pairs of a^T g) (selected_read.py:125-153)
+        a = _r(hvs * ws)
+        outer = torch.einsum("bqhmd,bqhe->bqhmde", a, gnf)
+        dc = torch.zeros(b, h, fine_c.shape[2], d, d)
+        dc.index_put_((bi.expand(b, q, h, m), hi.expand(b, q, h, m), ids), outer, accumulate=True)
+        dc = _r(dc)
+        return dhv.to(hv.dtype), dw.to(w.dtype), None, None, dc.to(fine_c.dtype)
+
+
+def _local_training(q, k, v, fine=256, keep=512):
+    """_local_training_corrected_4k (tao_stream.py:760-787)."""
+    b, total, heads, d = q.shape
+    if total < 3 * fine or total % fine:
+        parts = []
+        for start in range(0, total, fine):
+            end = min(total, start + fine)
+            old = max(0, start - keep)
+            parts.append(local_attention(q[:, start:end], k[:, old:end], v[:, old:end]))
+        return torch.cat(parts, dim=1)
+    first = local_attention(q[:, :256], k[:, :256], v[:, :256])
+    second = local_attention(q[:, 256:512], k[:, :512], v[:, :512])
+    n = total // 256 - 2
+    query = q[:, 512:].reshape(b * n, 256, heads, d)
+    keys = k.unfold(1, 768, 256).permute(0, 1, 4, 2, 3).reshape(b * n, 768, heads, d)
+    values = v.unfold(1, 768, 256).permute(0, 1, 4, 2, 3).reshape(b * n, 768, heads, d)
+    later = local_attention(query, keys, values)
+    return torch.cat((first, second, later.reshape(b, total - 512, heads, d)), dim=1)
+
+
+def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8):
+    """_read_training_group for one 256-query tile (tao_stream.py:596-665)."""
+    b, length, heads, d = query.shape
+    dt = query.dtype
+    h = F.softmax(query, dim=-1).to(dt)
+    page_weight = F.softmax(page_z, dim=2).to(dt)
+    hv = (h.unsqueeze(3) * page_weight[:, None]).to(dt)
+    coarse, _, count = routed_counts(completed, pending, group)
+    visible = completed * group + pending
+    with torch.no_grad():
+        cand_pages, cand_ids = [], []
+        if coarse:
+            mass = hv[..., :completed, :].sum(-1)
+            chosen = topk_oldest(mass, coarse).sort(-1).values
+            seg = torch.arange(group)
+            cand_pages.append(chosen.unsqueeze(-1).expand(b, length, heads, coarse, group)
+                              .reshape(b, length, heads, coarse * group))
+            cand_ids.append((chosen.unsqueeze(-1) * group + seg).reshape(b, length, heads, coarse * group))
+        if pending:
+            pid = torch.arange(pending).view(1, 1, 1, pending).expand(b, length, heads, pending)
+            cand_pages.append(torch.full_like(pid, completed))
+            cand_ids.append(completed * group + pid)
+        cand_pages = torch.cat(cand_pages, -1)
+        cand_ids = torch.cat(cand_ids, -1)
+    fine_page = torch.arange(fine_z.shape[2]) // group
+    seg_w = (fine_z - page_z.index_select(2, fine_page)).exp().to(dt)
+    with torch.no_grad():
+        hvd, wd = hv.detach(), seg_w.detach()
+        u = cand_ids.shape[-1]
+        ch = (hvd.gather(3, cand_pages[..., None].expand(b, length, heads, u, d)).float()
+              * wd[:, None].expand(b, length, heads, -1, d).gather(3, cand_ids[..., None].expand(b, length, heads, u, d)).float()).to(BF16)
+        scores = ch.sum(-1).masked_fill(cand_ids >= visible, -torch.inf)
+        sel = topk_oldest(scores, count)
+        sel_id = cand_ids.gather(-1, sel)
+        sel_page = cand_pages.gather(-1, sel)
+    num, den = _SelectedRead.apply(hv, seg_w, sel_id, sel_page, fine_c)
+    return (num / den).to(dt), sel_id
+
+
+def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False):
+    """read_training (tao_stream.py:668-757) with route_interval=1; returns
+    (local, fine, [selected ids per tile])."""
+    local = _local_training(q, k, v)
+    b, total, heads, d = q.shape
+    if total <= keep_plus(fine):
+        return local, torch.zeros_like(local), []
+    fine_z, fine_c = seal_all(raw_k, v, fine)
+    fine_parts, ids = [], []
+    for tile, query in enumerate(raw_q.split(fine, dim=1)):
+        visible = max(0, tile - 2)
+        if not visible:
+            fine_parts.append(torch.zeros_like(query))
+            continue
+        completed, pending = divmod(visible, group)
+        pz = []
+        if completed:
+            zc = fine_z[:, :, :completed * group].reshape(b, heads, completed, group, d)
+            pz.append(torch.logsumexp(zc, dim=3).to(fine_z.dtype))
+        if pending:
+            zp = fine_z[:, :, completed * group:visible].reshape(b, heads, 1, pending, d)
+            pz.append(torch.logsumexp(zp, dim=3).to(fine_z.dtype))
+        page_z = torch.cat(pz, dim=2)
+        out, sel = _tile_read(query, page_z, fine_z[:, :, :visible], fine_c[:, :, :visible],
+                              completed, pending, group)
+        fine_parts.append(out)
+        if keep_ids:
+            ids.append(sel)
+    return local, torch.cat(fine_parts, dim=1), ids
+
+
+def keep_plus(fine):
+    return 512 + fine
+
+
+def fuse_training(local, raw_q, fine, fine_present, fa, fb, alpha):
+    """operator._fuse_training (operator.py:21-39) with the index-only preset
+    (coarse never present)."""
+    dtype = raw_q.dtype
+    score = (fa.to(dtype) * raw_q.unsqueeze(-1)).to(dtype)
+    score = (score + fb.to(dtype)).to(dtype)
+    count = fine_present.to(torch.int32)
+    local_bias = count.clamp_min(1).to(dtype).log().to(dtype)
+    coarse_present = torch.zeros_like(fine_present)
+    score = torch.stack(((score[..., 0] + local_bias).to(dtype), score[..., 1], score[..., 2]), -1)
+    score = torch.stack((score[..., 0], score[..., 1].masked_fill(~coarse_present, -torch.inf),
+                         score[..., 2].masked_fill(~fine_present, -torch.inf)), -1)
+    rho = F.softmax(score, dim=-1).to(dtype)
+    gain = torch.full((), 2 * alpha, dtype=dtype)
+    coarse = torch.zeros_like(local)
+    lt = (rho[..., 0] * (2 * local).to(dtype)).to(dtype)
+    ct = (rho[..., 1] * (gain * coarse).to(dtype)).to(dtype)
+    ft = (rho[..., 2] * (gain * fine).to(dtype)).to(dtype)
+    fused = ((lt + ct).to(dtype) + ft).to(dtype)
+    return torch.where(fine_present, fused, local)
+
+
+def tao_attention(q, k, v, raw_q, raw_k, fa, fb, alpha):
+    """operator.tao_attention (operator.py:42-54), index-only preset.  ``alpha``
+    may be a float or a per-head sequence (heads are independent, so per-head
+    alpha equals one reference call per head slice)."""
+    local, fine, _ = training_read(raw_q, raw_k, v, q, k)
+    positions = torch.arange(q.shape[1])[None, :, None, None]
+    present = positions >= 768
+    if isinstance(alpha, (int, float)):
+        return fuse_training(local, raw_q, fine, present, fa, fb, alpha)
+    outs = [fuse_training(local[:, :, i:i + 1], raw_q[:, :, i:i + 1], fine[:, :, i:i + 1],
+                          present, fa[i:i + 1], fb[i:i + 1], float(alpha[i]))
+            for i in range(q.shape[2])]
+    return torch.cat(outs, dim=2)

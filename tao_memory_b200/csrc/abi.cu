@@ -1,0 +1,381 @@
+// extern "C" entry points of libtao_b200.so (declared in include/tao_b200.h).
+//
+// Host side: argument validation with the reference's error cases
+// (operator.py:77-78, tao_stream.py:931-932), workspace carving, grid sizing and
+// kernel launches on the caller's stream.  No allocation happens here: state
+// buffers and the workspace are owned by the caller.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/tao_b200.h"
+#include "stream_kernels.cuh"
+#include "window_attention.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TAO_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return TAO_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// --- host mirrors of the device schedule (common.cuh) ---------------------
+int h_budget(int count, const TaoPolicy& p) {
+  if (count <= 0) return 0;
+  long long sq = (long long)p.budget_root_scale * count;
+  long long r = 0;
+  {
+    long long lo = 0, hi = 1;
+    while (hi * hi <= sq) hi <<= 1;
+    while (lo < hi) {
+      long long mid = (lo + hi + 1) / 2;
+      if (mid * mid <= sq) lo = mid; else hi = mid - 1;
+    }
+    r = lo;
+  }
+  if (r * r < sq) ++r;
+  long long b = r + p.budget_offset;
+  return (int)(b < count ? b : count);
+}
+int h_sealed_at(long long pos) { return pos >= 768 ? (int)((pos - 768) / 256) + 1 : 0; }
+long long h_window_start(long long pos) { return pos < 768 ? 0 : 256LL * ((pos - 512) / 256); }
+
+int fpc_for(int width) { return width == 64 ? 4 : 1; }
+int kblocks_for(int width) { return width == 64 ? 6 : 12; }
+
+struct Layout {
+  size_t err, slot_ids, slot_pages, slot_n, local_part, local_out, fine_part, total;
+  int nslot, msplit, kblocks;
+};
+
+// Route slots: slot 0 = routes stored in the state, then one per refresh anchor
+// of the chunk (at most ceil(w / period) periodic turns plus position 768).
+int nslot_for(int w, int period) {
+  int n = 1 + (w + period - 1) / period + 1;
+  return n < 1 + w ? n : 1 + w;
+}
+
+Layout make_layout(int R, int w, int H, int D, int route_cap, int msplit_decode, int period) {
+  Layout L{};
+  L.nslot = nslot_for(w, period);
+  L.kblocks = kblocks_for(D);
+  L.msplit = (w == 1) ? msplit_decode : 1;
+  size_t off = 0;
+  L.err = off;
+  off = align256(off + 256);
+  L.slot_ids = off;
+  off = align256(off + (size_t)R * H * L.nslot * route_cap * 4);
+  L.slot_pages = off;
+  off = align256(off + (size_t)R * H * L.nslot * route_cap * 4);
+  L.slot_n = off;
+  off = align256(off + (size_t)R * L.nslot * 2 * 4);
+  L.local_part = off;
+  if (w == 1) off = align256(off + (size_t)R * H * L.kblocks * (D + 2) * 4);
+  L.local_out = off;
+  if (w > 1) off = align256(off + (size_t)R * w * H * D * 2);
+  L.fine_part = off;
+  off = align256(off + (size_t)R * w * H * L.msplit * (D + 1) * 4);
+  L.total = off;
+  return L;
+}
+
+float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+}  // namespace
+
+namespace {
+
+template <typename F>
+int set_smem(F* fn, size_t bytes) {
+  if (bytes > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return fail(TAO_ERR_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+  }
+  return TAO_OK;
+}
+
+template <int D>
+int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
+  using namespace tao;
+  int rc;
+  // prep: append + routing
+  const size_t prep_smem = (size_t)D * 4 + (size_t)a.pmax * 4 + (size_t)(8 * a.pmax + 8) * 8 + (size_t)a.pmax * 8;
+  if ((rc = set_smem(prep_kernel<D>, prep_smem))) return rc;
+  prep_kernel<D><<<dim3(a.R * a.H, L.nslot), 256, prep_smem, s>>>(a);
+  if ((rc = check_launch("prep_kernel"))) return rc;
+  if (a.w == 1) {
+    using Cfg = DecodeCfg<D>;
+    const size_t main_smem = (size_t)Cfg::FPC * D * D * 2 + (size_t)Cfg::FPC * D * 4;
+    if ((rc = set_smem(decode_main_kernel<D>, main_smem))) return rc;
+    decode_main_kernel<D><<<dim3(a.R * a.H, a.kblocks + a.msplit), 128, main_smem, s>>>(a);
+    if ((rc = check_launch("decode_main_kernel"))) return rc;
+  } else {
+    WinAttnParams p{};
+    p.q = a.q;
+    p.out = a.local_out;
+    p.q_batch_stride = (long long)a.w * a.H * D;
+    p.q_row_stride = (long long)a.H * D;
+    p.o_batch_stride = p.q_batch_stride;
+    p.o_row_stride = p.q_row_stride;
+    p.k_row_stride = D;
+    p.k_head_stride = (long long)kWindow * D;
+    p.heads = a.H;
+    p.nq = a.w;
+    p.ring = 1;
+    p.states = a.states;
+    const size_t attn_smem = (size_t)(64 + 4 * 64) * D * 2;
+    if ((rc = set_smem(window_attention_kernel<D>, attn_smem))) return rc;
+    window_attention_kernel<D><<<dim3((a.w + 63) / 64, a.R * a.H), 128, attn_smem, s>>>(p);
+    if ((rc = check_launch("window_attention_kernel"))) return rc;
+    const size_t pf_smem = (size_t)2 * D * D * 2 + (size_t)(2 * 16 * D + 2 * D) * 4;
+    if ((rc = set_smem(prefill_fine_kernel<D>, pf_smem))) return rc;
+    prefill_fine_kernel<D><<<dim3(a.R * a.H, (a.w + 15) / 16), 128, pf_smem, s>>>(a);
+    if ((rc = check_launch("prefill_fine_kernel"))) return rc;
+  }
+  const size_t fin_smem = (size_t)2 * kFine * D * 2 + (size_t)2 * D * 4;
+  if ((rc = set_smem(finalize_kernel<D>, fin_smem))) return rc;
+  finalize_kernel<D><<<a.R * a.H, 256, fin_smem, s>>>(a);
+  return check_launch("finalize_kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tao_last_error(void) { return g_last_error.c_str(); }
+
+int tao_version(void) { return 1; }
+
+size_t tao_state_sizeof(void) { return sizeof(TaoState); }
+
+size_t tao_stream_workspace_bytes(int n_states, int tokens, int heads, int width, int route_cap,
+                                  const TaoPolicy* policy) {
+  if (n_states <= 0 || tokens <= 0 || heads <= 0 || (width != 64 && width != 128) ||
+      route_cap <= 0 || !policy || policy->route_period <= 0)
+    return 0;
+  const int fpc = fpc_for(width);
+  return make_layout(n_states, tokens, heads, width, route_cap, (route_cap + fpc - 1) / fpc,
+                     policy->route_period)
+      .total;
+}
+
+int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
+                    const int32_t* host_cap, const TaoPolicy* policy, int tokens, int heads,
+                    int width, const void* q, const void* k, const void* v, const void* raw_q,
+                    const void* raw_k, const void* fusion_a, const void* fusion_b, float alpha,
+                    void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!states || n_states <= 0 || !host_pos || !host_cap || !policy)
+    return fail(TAO_ERR_ARG, "null state, cursor, capacity or policy array");
+  if (width != 64 && width != 128)
+    return fail(TAO_ERR_ARG, "head width must be 64 or 128, got %d", width);
+  if (heads <= 0) return fail(TAO_ERR_ARG, "heads must be positive");
+  if (tokens <= 0 || tokens > 256)
+    return fail(TAO_ERR_ARG, "tokens per call must be in [1, 256], got %d", tokens);
+  if (policy->fine_tokens != 256 || policy->local_keep != 512 || policy->coarse_group != 8)
+    return fail(TAO_ERR_ARG, "kernels are specialised for fine_tokens=256, local_keep=512, coarse_group=8");
+  if (policy->route_period <= 0 || policy->layer_stagger < 0 || policy->budget_root_scale <= 0 ||
+      policy->budget_offset < 0)
+    return fail(TAO_ERR_ARG, "invalid routing policy");
+  const void* ptrs[] = {q, k, v, raw_q, raw_k, fusion_a, fusion_b, out, workspace};
+  for (const void* p : ptrs)
+    if (!p) return fail(TAO_ERR_ARG, "null tensor pointer");
+  for (const void* p : {q, k, v, raw_q, raw_k, (const void*)out})
+    if (!aligned16(p)) return fail(TAO_ERR_ARG, "token tensors must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(TAO_ERR_ARG, "workspace must be 256-byte aligned");
+
+  int route_cap = -1, pmax = 1, mbound = 1;
+  for (int r = 0; r < n_states; ++r) {
+    const long long pos = host_pos[r];
+    if (pos < 0) return fail(TAO_ERR_POSITION, "negative position");
+    const long long start = h_window_start(pos);
+    if (pos + tokens - start > 768)
+      return fail(TAO_ERR_SEAL, "chunk crosses a fine seal boundary");
+    const int S = h_sealed_at(pos);
+    const bool seal = (pos + tokens - start) == 768;
+    const int cap = host_cap[r];
+    if (cap <= 0 || cap % 8) return fail(TAO_ERR_ARG, "fine capacity must be a positive multiple of 8");
+    if (S + (seal ? 1 : 0) > cap)
+      return fail(TAO_ERR_CAPACITY, "fine bank capacity %d too small for %d fines", cap, S + 1);
+    const int pm = cap / 8 + 1;
+    if (pm > pmax) pmax = pm;
+    const int mb = h_budget(cap, *policy);
+    if (mb > mbound) mbound = mb;
+  }
+  route_cap = policy->route_cap;
+  if (route_cap <= 0) return fail(TAO_ERR_ARG, "policy.route_cap must be positive");
+  if (mbound > route_cap) mbound = route_cap;
+  const size_t prep_smem = (size_t)width * 4 + (size_t)pmax * 4 + (size_t)(8 * pmax + 8) * 8 + (size_t)pmax * 8;
+  if (prep_smem > 200 * 1024) return fail(TAO_ERR_CAPACITY, "fine capacity too large for the route kernel");
+
+  const int fpc = fpc_for(width);
+  const Layout L = make_layout(n_states, tokens, heads, width, route_cap, (mbound + fpc - 1) / fpc,
+                               policy->route_period);
+  if (workspace_bytes < L.total)
+    return fail(TAO_ERR_ARG, "workspace too small: %zu < %zu", workspace_bytes, L.total);
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  tao::StepArgs a{};
+  a.states = reinterpret_cast<TaoState* const*>(states);
+  a.R = n_states;
+  a.w = tokens;
+  a.H = heads;
+  a.pol = {policy->route_period, policy->layer_stagger, policy->budget_root_scale, policy->budget_offset};
+  a.q = static_cast<const tao::bf16*>(q);
+  a.k = static_cast<const tao::bf16*>(k);
+  a.v = static_cast<const tao::bf16*>(v);
+  a.raw_q = static_cast<const tao::bf16*>(raw_q);
+  a.raw_k = static_cast<const tao::bf16*>(raw_k);
+  a.fa = static_cast<const tao::bf16*>(fusion_a);
+  a.fb = static_cast<const tao::bf16*>(fusion_b);
+  a.gain = bf16_round(2.0f * alpha);
+  a.out = static_cast<tao::bf16*>(out);
+  a.err = reinterpret_cast<int*>(ws + L.err);
+  a.nslot = L.nslot;
+  a.route_cap = route_cap;
+  a.slot_ids = reinterpret_cast<int32_t*>(ws + L.slot_ids);
+  a.slot_pages = reinterpret_cast<int32_t*>(ws + L.slot_pages);
+  a.slot_n = reinterpret_cast<int32_t*>(ws + L.slot_n);
+  a.kblocks = L.kblocks;
+  a.msplit = L.msplit;
+  a.local_part = reinterpret_cast<float*>(ws + L.local_part);
+  a.local_out = reinterpret_cast<tao::bf16*>(ws + L.local_out);
+  a.fine_part = reinterpret_cast<float*>(ws + L.fine_part);
+  a.pmax = pmax;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return width == 64 ? launch_step<64>(a, L, s) : launch_step<128>(a, L, s);
+}
+
+int tao_stream_check(void* workspace, int* flags, void* stream) {
+  if (!workspace) return fail(TAO_ERR_ARG, "null workspace");
+  int host = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(&host, workspace, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && host) e = cudaMemsetAsync(workspace, 0, sizeof(int), s);
+  if (e != cudaSuccess) return fail(TAO_ERR_CUDA, "check: %s", cudaGetErrorString(e));
+  if (flags) *flags = host;
+  if (host) return fail(TAO_ERR_DEVICE, "device error flags 0x%x", host);
+  return TAO_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+template <int D>
+__global__ void ring_copy_kernel(tao::bf16* ring, tao::bf16* flat, int H, long long first, int count,
+                                 int to_flat) {
+  // flat [count][H][D] <-> ring [H][768][D]
+  const long long n = (long long)count * H * (D / 8);
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(idx % (D / 8));
+    const int h = (int)((idx / (D / 8)) % H);
+    const long long t = idx / ((long long)(D / 8) * H);
+    uint4* rp = reinterpret_cast<uint4*>(ring + ((long long)h * tao::kWindow + (first + t) % tao::kWindow) * D) + c;
+    uint4* fp = reinterpret_cast<uint4*>(flat + (t * H + h) * D) + c;
+    if (to_flat) *fp = *rp; else *rp = *fp;
+  }
+}
+
+int ring_copy(void* ring, void* flat, int heads, int width, long long first, int count, int to_flat,
+              void* stream) {
+  if (!ring || !flat || heads <= 0 || count < 0 || count > 768 || first < 0)
+    return fail(TAO_ERR_ARG, "bad ring copy arguments");
+  if (width != 64 && width != 128) return fail(TAO_ERR_ARG, "head width must be 64 or 128");
+  if (count == 0) return TAO_OK;
+  const long long n = (long long)count * heads * (width / 8);
+  const int blocks = (int)((n + 255) / 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (width == 64)
+    ring_copy_kernel<64><<<blocks, 256, 0, s>>>((tao::bf16*)ring, (tao::bf16*)flat, heads, first, count, to_flat);
+  else
+    ring_copy_kernel<128><<<blocks, 256, 0, s>>>((tao::bf16*)ring, (tao::bf16*)flat, heads, first, count, to_flat);
+  return check_launch("ring_copy_kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int tao_ring_gather(const void* ring, int heads, int width, int64_t first_position, int count,
+                    void* out, void* stream) {
+  return ring_copy(const_cast<void*>(ring), out, heads, width, first_position, count, 1, stream);
+}
+
+int tao_ring_scatter(void* ring, int heads, int width, int64_t first_position, int count,
+                     const void* in, void* stream) {
+  return ring_copy(ring, const_cast<void*>(in), heads, width, first_position, count, 0, stream);
+}
+
+int tao_state_rebuild_memo(void* state, int heads, int width, int sealed, void* stream) {
+  if (!state || heads <= 0 || sealed < 0) return fail(TAO_ERR_ARG, "bad memo rebuild arguments");
+  if (width != 64 && width != 128) return fail(TAO_ERR_ARG, "head width must be 64 or 128");
+  if (sealed == 0) return TAO_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (width == 64)
+    tao::memo_rebuild_kernel<64><<<heads, 256, 0, s>>>(static_cast<TaoState*>(state), sealed);
+  else
+    tao::memo_rebuild_kernel<128><<<heads, 256, 0, s>>>(static_cast<TaoState*>(state), sealed);
+  return check_launch("memo_rebuild_kernel");
+}
+
+int tao_window_attention(const void* q, const void* k, const void* v, void* out, float* lse,
+                         int batch, int tokens, int heads, int width, void* stream) {
+  if (!q || !k || !v || !out || batch <= 0 || tokens <= 0 || heads <= 0)
+    return fail(TAO_ERR_ARG, "bad window attention arguments");
+  if (width != 64 && width != 128) return fail(TAO_ERR_ARG, "head width must be 64 or 128");
+  for (const void* p : {q, k, v, (const void*)out})
+    if (!aligned16(p)) return fail(TAO_ERR_ARG, "tensors must be 16-byte aligned");
+  tao::WinAttnParams p{};
+  p.q = static_cast<const tao::bf16*>(q);
+  p.k = static_cast<const tao::bf16*>(k);
+  p.v = static_cast<const tao::bf16*>(v);
+  p.out = static_cast<tao::bf16*>(out);
+  p.lse = lse;
+  p.q_batch_stride = p.k_batch_stride = p.o_batch_stride = (long long)tokens * heads * width;
+  p.q_row_stride = p.k_row_stride = p.o_row_stride = (long long)heads * width;
+  p.k_head_stride = width;
+  p.heads = heads;
+  p.nq = tokens;
+  p.qpos0 = 0;
+  p.kstart = -1;
+  p.ring = 0;
+  p.states = nullptr;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  dim3 grid((tokens + 63) / 64, batch * heads);
+  if (width == 64) {
+    const size_t smem = (size_t)(64 + 4 * 64) * 64 * 2;
+    if ((rc = set_smem(tao::window_attention_kernel<64>, smem))) return rc;
+    tao::window_attention_kernel<64><<<grid, 128, smem, s>>>(p);
+  } else {
+    const size_t smem = (size_t)(64 + 4 * 64) * 128 * 2;
+    if ((rc = set_smem(tao::window_attention_kernel<128>, smem))) return rc;
+    tao::window_attention_kernel<128><<<grid, 128, smem, s>>>(p);
+  }
+  return check_launch("window_attention_kernel");
+}
+
+}  // extern "C"
