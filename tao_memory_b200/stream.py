@@ -1,0 +1,400 @@
+"""Device-resident per-request, per-layer Tao state (reference ``StreamCache``).
+
+Reference: tao_attention/tao_stream.py:790-1094 (StreamCache) and 126-527
+(LayerState).  The semantic content is the same (exact local window, sealed fine
+matrices and log-partitions, pages, selected route ids, cursor) but it lives in
+fixed-capacity device buffers described by one ``TaoState`` descriptor:
+
+* the local window is a 768-slot ring (slot = position % 768) for k, v and raw k,
+  so no per-token concatenation happens;
+* fine matrices are appended in place into a preallocated bank that doubles when
+  full, instead of the reference's ``torch.cat`` repack at every seal;
+* the page-normalisation memo (page log-partitions and their softmax over pages)
+  is refreshed by the seal kernel, on the device.
+
+``export()``/``from_export()`` use the reference's snapshot dictionary, so
+snapshots move between the two implementations.
+"""
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from .config import TaoConfig, routed_counts
+
+WINDOW, FINE, KEEP, GROUP = 768, 256, 512, 8
+ROUTE_CAP = 256
+_BF16 = torch.bfloat16
+
+
+def window_start(pos):
+    """First absolute position of the exact local window while serving ``pos``."""
+    return 0 if pos < WINDOW else FINE * ((pos - KEEP) // FINE)
+
+
+def sealed_at(pos):
+    """Sealed fines before the token at ``pos`` is processed."""
+    return (pos - WINDOW) // FINE + 1 if pos >= WINDOW else 0
+
+
+def is_refresh(pos, layer, config):
+    first_turn = WINDOW + config.layer_stagger * layer
+    return pos == WINDOW or (pos >= first_turn and (pos - first_turn) % config.route_period == 0)
+
+
+def check_config(config):
+    """The sm_100a kernels implement the index-only softmax-writer preset."""
+    if (config.fine_tokens, config.local_keep, config.coarse_group) != (FINE, KEEP, GROUP):
+        raise ValueError("kernels are specialised for fine_tokens=256, local_keep=512, coarse_group=8")
+    if config.fine_writer != "softmax":
+        raise NotImplementedError("only fine_writer='softmax' is implemented on B200")
+    if not config.coarse_index_only:
+        raise NotImplementedError("only coarse_index_only=True (index_only_page_memo) is implemented on B200")
+
+
+def policy_for(config):
+    return _lib.TaoPolicy(FINE, KEEP, GROUP, config.route_period, config.layer_stagger,
+                          config.budget_root_scale, config.budget_offset, ROUTE_CAP)
+
+
+class _Workspace:
+    """Grow-only device scratch shared by calls on one device."""
+
+    cache = {}
+
+    @classmethod
+    def get(cls, device, nbytes):
+        buf = cls.cache.get(device)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            cls.cache[device] = buf
+        return buf
+
+
+class StreamCache:
+    """One request's one-layer exact-local and hierarchical history state."""
+
+    is_tao_stream = True
+
+    def __init__(self, layer_index, route_interval=2, fusion_mode="pointwise",
+                 pending_coarse_elision=False, pending_coarse_mask=False,
+                 fused_fine=True, config=TaoConfig()):
+        check_config(config)
+        self.config = config
+        self.layer_index = layer_index
+        self.route_interval = route_interval
+        self.fusion_mode = fusion_mode
+        self.fused_fine = fused_fine
+        self.pending_coarse_elision = pending_coarse_elision
+        self.pending_coarse_mask = pending_coarse_mask
+        self.position = 0
+        self.history_path_ablation = False
+        self.history_value_ablation = False
+        self._buf = None          # dict of device tensors
+        self._desc = None         # device TaoState (uint8 tensor)
+        self._host = None         # ctypes TaoState mirror
+        self._ptrs = None         # device array holding the descriptor address
+        self.heads = self.width = None
+        self.device = None
+        self.cap_fines = 0
+        self._counters = dict(fusion_pointwise_calls=0, fusion_no_history_local_returns=0,
+                              fused_fine_calls=0, peak_local_tokens=0)
+
+    # -- reference API ---------------------------------------------------
+    def get_pos(self):
+        return self.position
+
+    def next_chunk(self, desired):
+        """Tokens the next call may take without crossing a seal (tao_stream.py:914-917)."""
+        current = self.position - window_start(self.position) if self.position else 0
+        return min(desired, FINE, WINDOW - current)
+
+    def advance(self, count):
+        self.position += count
+
+    def release_execution(self, reason="request_end"):
+        """Drop execution-only resources (graphs, cached pointer arrays)."""
+        self._ptrs = None
+
+    def reset(self):
+        """Discard this request's state without touching another request."""
+        self.release_execution("reset")
+        self.__init__(self.layer_index, self.route_interval, self.fusion_mode,
+                      self.pending_coarse_elision, self.pending_coarse_mask,
+                      self.fused_fine, self.config)
+
+    # -- device buffers --------------------------------------------------
+    def _allocate(self, heads, width, device, cap):
+        if width not in (64, 128):
+            raise ValueError("head width must be 64 or 128")
+        cap = max(GROUP, int(math.ceil(cap / GROUP)) * GROUP)
+        z = lambda *shape, dt=_BF16: torch.zeros(*shape, dtype=dt, device=device)
+        pages = cap // GROUP + 1
+        self._buf = dict(
+            k_ring=z(heads, WINDOW, width), v_ring=z(heads, WINDOW, width),
+            rk_ring=z(heads, WINDOW, width),
+            fine_c=z(heads, cap, width, width), fine_z=z(heads, cap, width),
+            page_z=z(heads, pages, width), page_w=z(heads, pages, width),
+            route_ids=z(heads, ROUTE_CAP, dt=torch.int32),
+            route_pages=z(heads, ROUTE_CAP, dt=torch.int32))
+        self.heads, self.width, self.device, self.cap_fines = heads, width, device, cap
+        h = _lib.TaoState()
+        for name in ("k_ring", "v_ring", "rk_ring", "fine_c", "fine_z", "page_z", "page_w",
+                     "route_ids", "route_pages"):
+            setattr(h, name, self._buf[name].data_ptr())
+        h.position = self.position
+        h.cap_fines, h.route_cap, h.layer_index = cap, ROUTE_CAP, self.layer_index
+        h.heads, h.width = heads, width
+        self._host = h
+        self._desc = torch.zeros(ctypes.sizeof(_lib.TaoState), dtype=torch.uint8, device=device)
+        self._upload()
+        self._ptrs = None
+
+    def _upload(self):
+        raw = bytes(self._host)
+        self._desc.copy_(torch.frombuffer(bytearray(raw), dtype=torch.uint8))
+
+    def _download(self):
+        """Read the device-updated descriptor fields (synchronising)."""
+        raw = self._desc.cpu().numpy().tobytes()
+        ctypes.memmove(ctypes.addressof(self._host), raw, len(raw))
+        return self._host
+
+    def _grow(self, need):
+        """Double the fine bank until it holds ``need`` fines (in-place append
+        afterwards; existing fines are copied once)."""
+        cap = self.cap_fines
+        while cap < need:
+            cap *= 2
+        if cap == self.cap_fines:
+            return
+        host = self._download()
+        old = self._buf
+        s = sealed_at(self.position)
+        p = s // GROUP + (s % GROUP > 0)
+        self._allocate(self.heads, self.width, self.device, cap)
+        for name in ("k_ring", "v_ring", "rk_ring", "route_ids", "route_pages"):
+            self._buf[name].copy_(old[name])
+        self._buf["fine_c"][:, :s].copy_(old["fine_c"][:, :s])
+        self._buf["fine_z"][:, :s].copy_(old["fine_z"][:, :s])
+        self._buf["page_z"][:, :p].copy_(old["page_z"][:, :p])
+        self._buf["page_w"][:, :p].copy_(old["page_w"][:, :p])
+        for f in ("n_route", "n_chosen", "route_refreshes", "seal_events"):
+            setattr(self._host, f, getattr(host, f))
+        self._host.position = self.position
+        self._upload()
+
+    def _pointer_array(self):
+        if self._ptrs is None:
+            self._ptrs = torch.tensor([self._desc.data_ptr()], dtype=torch.int64, device=self.device)
+        return self._ptrs
+
+    def _ensure(self, heads, width, device, tokens):
+        if self._buf is None:
+            end = self.position + tokens
+            self._allocate(heads, width, device, max(64, sealed_at(end) + 1))
+        elif (heads, width) != (self.heads, self.width) or device != self.device:
+            raise ValueError("a state serves one head count, width and device")
+        need = sealed_at(self.position + tokens) + 1
+        if need > self.cap_fines:
+            self._grow(need)
+
+    # -- one chunk through the kernels ------------------------------------
+    def _run(self, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
+        """Advance by q.shape[1] tokens (must not cross a seal); fused output -> out."""
+        run_batch([self], q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out)
+
+    # -- snapshots (reference dictionary format, tao_stream.py:853-912) --
+    def export(self):
+        """Owned tensors for a checkpoint or an independent request."""
+        s = sealed_at(self.position)
+        layer = {"n_route": 0, "n_chosen": 0, "route_refreshes": 0}
+        local = None
+        fine_c = None
+        pages, pending = [], []
+        route = None
+        if self._buf is not None:
+            host = self._download()
+            layer = {"n_route": host.n_route, "n_chosen": host.n_chosen,
+                     "route_refreshes": host.route_refreshes}
+            n = self.position - window_start(self.position)
+            if n:
+                local = tuple(self._gather_ring(name, window_start(self.position), n)
+                              for name in ("k_ring", "v_ring", "rk_ring"))
+            if s:
+                fine_c = self._buf["fine_c"][:, :s].unsqueeze(0).clone()
+                fz = self._buf["fine_z"]
+                pz = self._buf["page_z"]
+                for p in range(s // GROUP):
+                    pages.append((pz[:, p].unsqueeze(0).clone(), None,
+                                  fz[:, p * GROUP:(p + 1) * GROUP].unsqueeze(0).clone()))
+                for i in range((s // GROUP) * GROUP, s):
+                    pending.append(fz[:, i].unsqueeze(0).clone())
+            if host.n_route:
+                ids = self._buf["route_ids"][:, :host.n_route].to(torch.int64)
+                chosen = self._buf["route_pages"][:, :host.n_chosen].to(torch.int64)
+                route = (chosen.view(1, 1, self.heads, -1).clone(),
+                         ids.view(1, 1, self.heads, -1).clone())
+        return {
+            "layer_index": self.layer_index, "config": self.config.export(),
+            "route_interval": self.route_interval, "fusion_mode": self.fusion_mode,
+            "fused_fine": self.fused_fine, "position": self.position, "local": local,
+            "packed_fine_c": fine_c, "pages": pages, "pending_z": pending,
+            "pending_square_mass": None, "pending_mass": None, "pending_gram": None,
+            "pending_cross": None, "route_ids": route, "route_key": None,
+            "state_version": s, "route_refreshes": layer["route_refreshes"],
+            "fine_seal_events": s,
+        }
+
+    @classmethod
+    def from_export(cls, saved, device=None):
+        """Restore the same cursor with no alias to the exported tensors.  Accepts
+        dictionaries produced by this class or by the reference StreamCache."""
+        state = cls(saved["layer_index"], saved["route_interval"], saved["fusion_mode"],
+                    fused_fine=saved["fused_fine"], config=TaoConfig(**saved["config"]))
+        pos = saved["position"]
+        state.position = pos
+        local = saved["local"]
+        if local is None and not saved["pages"] and not saved["pending_z"]:
+            return state
+        sample = local[0] if local is not None else saved["packed_fine_c"]
+        heads, width = sample.shape[2], sample.shape[-1]
+        dev = torch.device(device) if device is not None else (
+            sample.device if sample.is_cuda else torch.device("cuda", torch.cuda.current_device()))
+        s = sealed_at(pos)
+        state._allocate(heads, width, dev, max(64, s + 1))
+        b = state._buf
+        if local is not None:
+            n = local[0].shape[1]
+            if n != pos - window_start(pos):
+                raise ValueError("snapshot local window does not match its position")
+            for name, t in zip(("k_ring", "v_ring", "rk_ring"), local):
+                state._scatter_ring(name, pos - n, t)
+        fz = [z.reshape(heads, -1, width) for _, _, z in saved["pages"]]
+        fz += [z.reshape(heads, 1, width) for z in saved["pending_z"]]
+        if s:
+            if sum(t.shape[1] for t in fz) != s:
+                raise ValueError("snapshot fine count does not match its position")
+            b["fine_z"][:, :s].copy_(torch.cat(fz, dim=1).to(dev, _BF16))
+            b["fine_c"][:, :s].copy_(saved["packed_fine_c"][0].to(dev, _BF16))
+        h = state._host
+        route = saved["route_ids"]
+        if route is not None:
+            chosen, ids = route
+            m, kc = ids.shape[-1], chosen.shape[-1]
+            b["route_ids"][:, :m].copy_(ids.reshape(heads, m).to(dev, torch.int32))
+            b["route_pages"][:, :kc].copy_(chosen.reshape(heads, kc).to(dev, torch.int32))
+            h.n_route, h.n_chosen = m, kc
+        h.route_refreshes = saved.get("route_refreshes", 0)
+        h.seal_events = s
+        h.position = pos
+        state._upload()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(_lib.lib().tao_state_rebuild_memo(state._desc.data_ptr(), heads, width, s, stream))
+        return state
+
+    def _gather_ring(self, name, first, count):
+        out = torch.empty(1, count, self.heads, self.width, dtype=_BF16, device=self.device)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(_lib.lib().tao_ring_gather(self._buf[name].data_ptr(), self.heads, self.width,
+                                              first, count, out.data_ptr(), stream))
+        return out
+
+    def _scatter_ring(self, name, first, t):
+        t = t.to(self.device, _BF16).contiguous()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(_lib.lib().tao_ring_scatter(self._buf[name].data_ptr(), self.heads, self.width,
+                                               first, t.shape[1], t.data_ptr(), stream))
+
+    def bytes(self):
+        """Byte accounting with the reference's key names (tao_stream.py:988-1094)."""
+        s = sealed_at(self.position)
+        heads, width = self.heads or 0, self.width or 0
+        pages, pending = s // GROUP, s % GROUP
+        history = (pages * (GROUP + 1) + pending) * (width * width + width) * heads * 2
+        history -= pages * width * width * heads * 2  # index-only pages hold no matrix
+        local = self.position - window_start(self.position)
+        logical_local = local * 2 * heads * width * 2
+        physical = 0 if self._buf is None else sum(t.numel() * t.element_size() for t in self._buf.values())
+        n_route = 0 if self._buf is None else self._download().n_route
+        route_bytes = n_route * heads * 8
+        return {"history_bytes": history, "page_normalization_memo_bytes": 0,
+                "pending_writer_bytes": 0, "fused_fine": self.fused_fine,
+                "fusion_mode": self.fusion_mode, "fine_seal_events": s,
+                "route_integer_bytes": route_bytes,
+                "logical_local_bf16_kv_bytes": logical_local,
+                "logical_retained_bytes": history + logical_local,
+                "physical_local_including_raw_key_bytes": local * 3 * heads * width * 2,
+                "unique_allocated_cache_storage_bytes": physical,
+                "local_length_tokens": local, "completed_coarse_pages": pages,
+                "pending_fine_states": pending,
+                "selected_fine_per_layer": [n_route],
+                "fine_matrix_repack_bytes": 0, **self._counters}
+
+
+def _as_bf16(t, name, device):
+    if t.device != device:
+        raise ValueError(f"{name} must be on {device}")
+    if t.dtype != _BF16:
+        raise ValueError("B200 streaming supports bfloat16 operands (the reference's documented envelope)")
+    return t.contiguous()
+
+
+def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
+    """Advance every state by q.shape[1] tokens in one set of kernel launches.
+
+    q, k, v, raw_q, raw_k, out: [len(states), tokens, H, D] bf16 on one device.
+    The chunk must not cross a seal boundary of any state.
+    """
+    r, w, heads, width = q.shape
+    dev = q.device
+    lib = _lib.lib()
+    ops = [_as_bf16(t, n, dev) for t, n in ((q, "q"), (k, "k"), (v, "v"), (raw_q, "raw_q"), (raw_k, "raw_k"))]
+    for t in ops[1:]:
+        if t.shape != q.shape:
+            raise ValueError("q, k, v, raw_q and raw_k must have the same shape")
+    fa = fusion_a.detach().to(dev, _BF16).contiguous()
+    fb = fusion_b.detach().to(dev, _BF16).contiguous()
+    if fa.shape != (heads, width, 3) or fb.shape != (heads, width, 3):
+        raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
+    for st in states:
+        st._ensure(heads, width, dev, w)
+    if len(states) == 1:
+        ptrs = states[0]._pointer_array()
+    else:
+        ptrs = torch.tensor([st._desc.data_ptr() for st in states], dtype=torch.int64, device=dev)
+    cfg = states[0].config
+    policy = policy_for(cfg)
+    pos = (ctypes.c_int64 * r)(*[st.position for st in states])
+    cap = (ctypes.c_int32 * r)(*[st.cap_fines for st in states])
+    nbytes = lib.tao_stream_workspace_bytes(r, w, heads, width, ROUTE_CAP, ctypes.byref(policy))
+    ws = _Workspace.get(dev, nbytes)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(lib.tao_stream_step(ptrs.data_ptr(), r, pos, cap, ctypes.byref(policy), w, heads, width,
+                                   *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
+                                   float(alpha), out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
+    for st in states:
+        hist = st.position >= WINDOW
+        st._counters["fusion_pointwise_calls" if hist else "fusion_no_history_local_returns"] += 1
+        st._counters["fused_fine_calls"] += int(hist)
+        st.position += w
+        st._counters["peak_local_tokens"] = max(st._counters["peak_local_tokens"],
+                                                 st.position - window_start(st.position - 1)
+                                                 if st.position else 0)
+    if ptrs is not states[0]._ptrs:
+        # keep the temporary pointer array alive until the launches have consumed it
+        _Workspace.cache[("ptrs", dev)] = ptrs
+
+
+def check_device(device=None):
+    """Raise if a kernel on ``device`` reported an error since the last check."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    ws = _Workspace.cache.get(dev)
+    if ws is None:
+        return 0
+    flags = ctypes.c_int(0)
+    _lib.check(_lib.lib().tao_stream_check(ws.data_ptr(), ctypes.byref(flags),
+                                           torch.cuda.current_stream(dev).cuda_stream))
+    return flags.value

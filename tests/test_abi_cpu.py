@@ -1,0 +1,79 @@
+"""CPU-side checks of the C ABI: the library loads, exports every symbol the
+header declares, and its host-side validation and schedule agree with the
+reference's integer policy (no kernel is launched)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from tao_memory_b200 import _lib
+from tao_memory_b200.config import TaoConfig, index_only_page_memo, routed_counts
+from tao_memory_b200.stream import sealed_at, window_start, is_refresh
+from oracle import tao_oracle as o
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "tao_b200.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(tao_\w+)\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared()
+    assert len(names) >= 9
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(_lib.exported_symbols()) <= set(names)
+
+
+def test_state_layout_matches_header():
+    assert _lib.lib().tao_state_sizeof() == ctypes.sizeof(_lib.TaoState)
+
+
+def test_host_validation_errors_without_gpu():
+    lib = _lib.lib()
+    pol = _lib.TaoPolicy(256, 512, 8, 24, 2, 2, 2, 256)
+    pos = (ctypes.c_int64 * 1)(0)
+    cap = (ctypes.c_int32 * 1)(64)
+    # width 96 is rejected before any launch
+    rc = lib.tao_stream_step(1, 1, pos, cap, ctypes.byref(pol), 1, 2, 96, *([16] * 7), 0.5, 16, 256, 1 << 20, None)
+    assert rc == _lib.TAO_ERR_ARG
+    with pytest.raises(ValueError):
+        _lib.check(rc)
+    # a chunk that crosses the 768 seal boundary
+    pos[0] = 700
+    rc = lib.tao_stream_step(1, 1, pos, cap, ctypes.byref(pol), 100, 2, 64, *([16] * 7), 0.5, 16, 256, 1 << 20, None)
+    assert rc == _lib.TAO_ERR_SEAL
+    # geometry other than the preset
+    bad = _lib.TaoPolicy(128, 512, 8, 24, 2, 2, 2, 256)
+    pos[0] = 0
+    rc = lib.tao_stream_step(1, 1, pos, cap, ctypes.byref(bad), 1, 2, 64, *([16] * 7), 0.5, 16, 256, 1 << 20, None)
+    assert rc == _lib.TAO_ERR_ARG
+    assert lib.tao_stream_workspace_bytes(8, 1, 12, 64, 256, ctypes.byref(pol)) > 0
+    assert lib.tao_stream_workspace_bytes(8, 1, 12, 96, 256, ctypes.byref(pol)) == 0
+
+
+def test_schedule_matches_reference_policy():
+    cfg = index_only_page_memo()
+    for completed in range(0, 80):
+        for pending in range(0, 8):
+            assert routed_counts(completed, pending, cfg) == o.routed_counts(completed, pending)
+    for c in range(0, 5000):
+        assert cfg.budget(c) == o.budget(c)
+    # cursor helpers follow the reference's seal/refresh schedule (tao_stream.py:196-227, 959-967)
+    assert [sealed_at(p) for p in (0, 767, 768, 1023, 1024, 1280)] == [0, 0, 1, 1, 2, 3]
+    assert [p for p in range(700, 900) if is_refresh(p, 3, cfg)] == [768, 774, 798, 822, 846, 870, 894]
+    assert window_start(767) == 0 and window_start(768) == 256 and window_start(1023) == 256
+
+
+def test_config_validation_matches_reference():
+    with pytest.raises(ValueError):
+        TaoConfig(fine_writer="nope")
+    with pytest.raises(TypeError):
+        TaoConfig(fine_tokens=256.0)
+    with pytest.raises(ValueError):
+        TaoConfig(local_keep=300)
+    assert TaoConfig(**index_only_page_memo().export()) == index_only_page_memo()

@@ -1,0 +1,178 @@
+"""Streaming prefill/decode on the GPU vs the reference goldens and the CPU oracle.
+
+Tolerance (bf16 outputs): |a-b| <= 2e-2 + 2e-2*|b| per element; routing
+selections are integers and must match exactly.  A CUDA result is compared with
+the reference's own outputs (golden fixtures) and with the oracle at other sizes.
+"""
+import os
+
+import pytest
+import torch
+
+from oracle import tao_oracle as o
+from oracle.inputs import make_inputs
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+KEYS = ("q", "k", "v", "raw_q", "raw_k")
+ATOL = RTOL = 2e-2
+
+
+def _tb():
+    import tao_memory_b200 as tb
+    from tao_memory_b200.presets import index_only_page_memo
+    from tao_memory_b200.stream import check_device
+    return tb, index_only_page_memo, check_device
+
+
+def close_frac(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    bad = (a - b).abs() > ATOL + RTOL * b.abs()
+    return bad.float().mean().item()
+
+
+def run_gpu(x, layer, splits, steps, alpha, snapshot_at=None):
+    tb, preset, check_device = _tb()
+    dev = torch.device("cuda")
+    xs = {k: t.to(dev) for k, t in x.items()}
+    st = tb.new_state(layer, preset())
+    outs, ids, pos = [], [], 0
+    snap = None
+    kw = dict(fusion_a=xs["fusion_a"], fusion_b=xs["fusion_b"], alpha=alpha)
+    for n in splits:
+        sl = slice(pos, pos + n)
+        out, st = tb.tao_attention_prefill(*(xs[k][:, sl] for k in KEYS[:3]), raw_q=xs["raw_q"][:, sl],
+                                           raw_k=xs["raw_k"][:, sl], state=st, position=pos, **kw)
+        outs.append(out)
+        pos += n
+    for i in range(steps):
+        sl = slice(pos, pos + 1)
+        out, st = tb.tao_attention_decode(*(xs[k][:, sl] for k in KEYS[:3]), raw_q=xs["raw_q"][:, sl],
+                                          raw_k=xs["raw_k"][:, sl], state=st, position=pos, **kw)
+        outs.append(out)
+        e = st.export()["route_ids"]
+        ids.append(None if e is None else e[1].cpu())
+        pos += 1
+        if snapshot_at is not None and i + 1 == snapshot_at:
+            snap = st.export()
+    torch.cuda.synchronize()
+    assert check_device() == 0
+    return torch.cat(outs, 1), ids, st, snap
+
+
+@pytest.mark.parametrize("name", ["stream_h2d64", "stream_h1d128", "stream_pages"])
+def test_stream_matches_reference_golden(name):
+    g = torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
+    heads, width, layer, splits, steps, seed = g["case"]
+    x, _ = make_inputs(1, sum(splits) + steps, heads, width, seed)
+    out, ids, st, _ = run_gpu(x, layer, splits, steps, g["alpha"])
+    stride = g.get("row_stride", 1)
+    assert close_frac(out[:, ::stride], g["output"]) <= 1e-4
+    if "decode_output" in g:
+        assert close_frac(out[:, -steps:], g["decode_output"]) == 0.0
+    mism = sum(int(not torch.equal(a, b)) for a, b in zip(ids, g["decode_route_ids"]) if b is not None)
+    assert mism == 0, f"{mism} decode steps with different routes"
+    snap = st.export()
+    ref = g["snapshot_final"]
+    assert snap["position"] == ref["position"]
+    for (pz, _, fz), (rpz, _, rfz) in zip(snap["pages"], ref["pages"]):
+        assert close_frac(pz, rpz) == 0.0 and close_frac(fz, rfz) == 0.0
+    assert close_frac(snap["packed_fine_c"], ref["packed_fine_c"]) == 0.0
+
+
+@pytest.mark.parametrize("heads,width,layer,splits,steps", [
+    (4, 64, 2, (300, 1500, 1333), 60),
+    (3, 128, 5, (2100,), 40),
+])
+def test_stream_matches_oracle(heads, width, layer, splits, steps, one_thread):
+    x, _ = make_inputs(1, sum(splits) + steps, heads, width, seed=11 + layer)
+    out, ids, _, _ = run_gpu(x, layer, splits, steps, 0.4)
+    st = o.OracleStream(layer)
+    ref, ref_ids, pos = [], [], 0
+    for n in list(splits) + [1] * steps:
+        sl = slice(pos, pos + n)
+        ref.append(st.step(*(x[k][:, sl] for k in KEYS), x["fusion_a"], x["fusion_b"], 0.4))
+        if n == 1:
+            ref_ids.append(st.route_ids[1].clone())
+        pos += n
+    ref = torch.cat(ref, 1)
+    assert close_frac(out, ref) <= 1e-4
+    assert sum(int(not torch.equal(a, b)) for a, b in zip(ids, ref_ids)) == 0
+
+
+def test_batch_decode_equals_single_requests():
+    tb, preset, check_device = _tb()
+    dev = torch.device("cuda")
+    R, H, D, P = 3, 2, 64, 1100
+    xs = [make_inputs(1, P + 30, H, D, seed=40 + r)[0] for r in range(R)]
+    xs = [{k: t.to(dev) for k, t in x.items()} for x in xs]
+    fa, fb = xs[0]["fusion_a"], xs[0]["fusion_b"]
+    singles, batch = [], []
+    for r in range(R):
+        for lst in (singles, batch):
+            st = tb.new_state(r, preset())
+            tb.tao_attention_prefill(*(xs[r][k][:, :P] for k in KEYS[:3]), raw_q=xs[r]["raw_q"][:, :P],
+                                     raw_k=xs[r]["raw_k"][:, :P], fusion_a=fa, fusion_b=fb, alpha=0.3,
+                                     state=st, position=0)
+            lst.append(st)
+    for t in range(P, P + 30):
+        sl = slice(t, t + 1)
+        one = [tb.tao_attention_decode(*(xs[r][k][:, sl] for k in KEYS[:3]), raw_q=xs[r]["raw_q"][:, sl],
+                                       raw_k=xs[r]["raw_k"][:, sl], fusion_a=fa, fusion_b=fb, alpha=0.3,
+                                       state=singles[r], position=t)[0] for r in range(R)]
+        stack = {k: torch.cat([xs[r][k][:, sl] for r in range(R)], 0) for k in KEYS}
+        many, _ = tb.tao_attention_decode_batch(*(stack[k] for k in KEYS[:3]), raw_q=stack["raw_q"],
+                                                raw_k=stack["raw_k"], fusion_a=fa, fusion_b=fb,
+                                                alpha=0.3, states=batch)
+        assert torch.equal(torch.cat(one, 0), many)
+    assert check_device() == 0
+
+
+def test_export_import_roundtrip_and_reference_snapshot(one_thread):
+    tb, preset, check_device = _tb()
+    from tao_memory_b200 import StreamCache
+    dev = torch.device("cuda")
+    g = torch.load(os.path.join(GOLDEN, "stream_h2d64.pt"), weights_only=False)
+    heads, width, layer, splits, steps, seed = g["case"]
+    total = sum(splits) + steps
+    x, _ = make_inputs(1, total + 20, heads, width, seed)
+    out, _, st, snap = run_gpu({k: t[:, :total] if t.dim() == 4 else t for k, t in x.items()},
+                               layer, splits, steps, g["alpha"], snapshot_at=steps)
+    xs = {k: t.to(dev) for k, t in x.items()}
+    kw = dict(fusion_a=xs["fusion_a"], fusion_b=xs["fusion_b"], alpha=g["alpha"])
+    a = StreamCache.from_export(st.export())
+    b = StreamCache.from_export(g["snapshot_final"], device=dev)   # produced by the reference
+    orc = o.OracleStream.from_export(g["snapshot_final"])
+    for t in range(total, total + 20):
+        sl = slice(t, t + 1)
+        args = [xs[k][:, sl] for k in KEYS[:3]]
+        o1, st = tb.tao_attention_decode(*args, raw_q=xs["raw_q"][:, sl], raw_k=xs["raw_k"][:, sl],
+                                         state=st, position=t, **kw)
+        o2, a = tb.tao_attention_decode(*args, raw_q=xs["raw_q"][:, sl], raw_k=xs["raw_k"][:, sl],
+                                        state=a, position=t, **kw)
+        o3, b = tb.tao_attention_decode(*args, raw_q=xs["raw_q"][:, sl], raw_k=xs["raw_k"][:, sl],
+                                        state=b, position=t, **kw)
+        ref = orc.step(*(x[k][:, sl] for k in KEYS), x["fusion_a"], x["fusion_b"], g["alpha"])
+        assert torch.equal(o1, o2)
+        assert close_frac(o3, ref) == 0.0
+    st.reset()
+    assert st.get_pos() == 0 and a.get_pos() == total + 20
+    assert check_device() == 0
+
+
+def test_stream_errors():
+    tb, preset, _ = _tb()
+    dev = torch.device("cuda")
+    x, _ = make_inputs(1, 4, 1, 64)
+    xs = {k: t.to(dev) for k, t in x.items()}
+    st = tb.new_state(0, preset())
+    kw = dict(fusion_a=xs["fusion_a"], fusion_b=xs["fusion_b"], alpha=0.5)
+    with pytest.raises(ValueError):
+        tb.tao_attention_prefill(*(xs[k] for k in KEYS[:3]), raw_q=xs["raw_q"], raw_k=xs["raw_k"],
+                                 state=st, position=3, **kw)
+    with pytest.raises(ValueError):
+        tb.tao_attention_decode(*(xs[k][:, :2] for k in KEYS[:3]), raw_q=xs["raw_q"][:, :2],
+                                raw_k=xs["raw_k"][:, :2], state=st, position=0, **kw)
+    with pytest.raises(ValueError):
+        tb.tao_attention_prefill(*(xs[k].float() for k in KEYS[:3]), raw_q=xs["raw_q"].float(),
+                                 raw_k=xs["raw_k"].float(), state=st, position=0, **kw)
