@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""Benchmark of the TaoMemory decode hot path on B200.
+
+Workload ("decode128k"): per GPU, 8 independent requests (one state each), H=12,
+D=64, bf16, each prefilled with 131,072 synthetic tokens ~N(0,1) through the
+public prefill API, then decoded one token per request per step.  A step is one
+decode token for every request on the rank (weak scaling: 8 requests per GPU).
+
+Reported (one JSON line on rank 0):
+* value      -- decode tokens/s over all ranks, inputs resident in HBM, steps
+                launched through the C ABI (BatchDecoder), L2 flushed between
+                timed steps (256 MiB memset outside the timed window);
+* e2e        -- the same metric through the public Python API
+                (tao_attention_decode_batch) with the step's inputs copied from
+                pinned host memory and the output copied back inside the window;
+* roofline   -- achieved HBM GB/s of the main decode kernel (local attention +
+                selected fine read) = algorithmic bytes / CUDA-event duration;
+* cpu_baseline -- the CPU oracle (reference port) on a bounded sample.
+
+``--impl reference`` times the reference's algorithm on the host CPU (the oracle
+port in oracle/tao_oracle.py) on the same config and prints the same line.
+"""
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s @128K ctx"
+UNIT = "tok/s"
+REQUESTS, HEADS, WIDTH, CONTEXT, LAYER = 8, 12, 64, 131072, 0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=248)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--requests", type=int, default=REQUESTS)
+    ap.add_argument("--context", type=int, default=CONTEXT)
+    ap.add_argument("--cpu-sample-steps", type=int, default=4)
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the main decode kernel from the committed ncu
+    summary (line 'traffic_bytes_per_launch: N'), or None."""
+    path = os.path.join(ROOT, "profiles", "decode_main_kernel_decode128k.md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed loops run."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+
+def prefill_states(tb, preset, n, context, device, seed):
+    """n fresh states, each advanced through `context` synthetic tokens with the
+    public prefill API (pieces of 16K tokens to bound input memory)."""
+    import torch
+    gen = torch.Generator(device=device)
+    states = []
+    fa = (torch.randn(HEADS, WIDTH, 3, device=device, generator=gen.manual_seed(seed)) * 0.02).to(torch.bfloat16)
+    fb = (torch.randn(HEADS, WIDTH, 3, device=device, generator=gen) * 0.02).to(torch.bfloat16)
+    piece = 16384
+    for r in range(n):
+        st = tb.new_state(LAYER, preset())
+        gen.manual_seed(seed * 1000 + r + 1)
+        pos = 0
+        while pos < context:
+            w = min(piece, context - pos)
+            x = [torch.randn(1, w, HEADS, WIDTH, device=device, generator=gen).to(torch.bfloat16)
+                 for _ in range(5)]
+            tb.tao_attention_prefill(x[0], x[1], x[2], raw_q=x[3], raw_k=x[4], fusion_a=fa,
+                                     fusion_b=fb, alpha=0.5, state=st, position=pos)
+            pos += w
+        states.append(st)
+    return states, fa, fb
+
+
+def run_b200(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    import tao_memory_b200 as tb
+    from tao_memory_b200 import _lib
+    from tao_memory_b200.presets import index_only_page_memo
+    from tao_memory_b200.stream import BatchDecoder, decode_bytes
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    R, K, W = args.requests, args.steps, args.warmup
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(device).cuda_stream
+
+    t0 = time.time()
+    states, fa, fb = prefill_states(tb, index_only_page_memo, R, args.context, device, seed=rank + 1)
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+
+    gen = torch.Generator(device=device).manual_seed(10_000 + rank)
+    total_steps = W + 2 * K
+    inputs = torch.randn(total_steps, 5, R, 1, HEADS, WIDTH, device=device, generator=gen).to(torch.bfloat16)
+    out = torch.empty(R, 1, HEADS, WIDTH, dtype=torch.bfloat16, device=device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    dec = BatchDecoder(states, fa, fb, 0.5, device)
+    dec.reserve(total_steps + 1)
+
+    def step_ptrs(i):
+        x = inputs[i]
+        return [x[j].data_ptr() for j in range(5)]
+
+    for i in range(W):
+        dec.step(*step_ptrs(i), out.data_ptr())
+    torch.cuda.synchronize()
+    dec.check()
+
+    def ev():
+        e = ctypes.c_void_p()
+        _lib.check(lib.tao_event_create(ctypes.byref(e)))
+        return e
+
+    starts, stops = [ev() for _ in range(K)], [ev() for _ in range(K)]
+    mstarts, mstops = [ev() for _ in range(K)], [ev() for _ in range(K)]
+    algo_bytes = []
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.zero_()                     # evict L2 (outside the timed window)
+        algo_bytes.append(decode_bytes(states))
+        lib.tao_event_record(starts[i], stream)
+        lib.tao_stream_profile_next(mstarts[i], mstops[i])
+        dec.step(*step_ptrs(W + i), out.data_ptr())
+        lib.tao_event_record(stops[i], stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    dec.check()
+
+    def elapsed(a, b):
+        ms = ctypes.c_float()
+        _lib.check(lib.tao_event_elapsed(a, b, ctypes.byref(ms)))
+        return ms.value
+
+    step_ms = [elapsed(a, b) for a, b in zip(starts, stops)]
+    main_ms = [elapsed(a, b) for a, b in zip(mstarts, mstops)]
+    for e in starts + stops + mstarts + mstops:
+        lib.tao_event_destroy(e)
+    total_ms = sum(step_ms)
+
+    # ---- e2e: public API, pinned host inputs in, output back to host
+    host_in = inputs[W + K:W + 2 * K].cpu().pin_memory()
+    host_out = torch.empty(R, 1, HEADS, WIDTH, dtype=torch.bfloat16).pin_memory()
+    stage = torch.empty(5, R, 1, HEADS, WIDTH, dtype=torch.bfloat16, device=device)
+    e_start = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    e_stop = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for i in range(K):
+        flush.zero_()
+        e_start[i].record()
+        stage.copy_(host_in[i], non_blocking=True)
+        y, _ = tb.tao_attention_decode_batch(stage[0], stage[1], stage[2], raw_q=stage[3], raw_k=stage[4],
+                                             fusion_a=fa, fusion_b=fb, alpha=0.5, states=states, out=out)
+        host_out.copy_(y, non_blocking=True)
+        e_stop[i].record()
+    torch.cuda.synchronize()
+    clocks.stop()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in zip(e_start, e_stop))
+
+    # ---- max over ranks
+    tot = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = tot.tolist()
+    tokens = world * R * K
+
+    peak, peak_kind = measured_peaks()
+    achieved = sum(algo_bytes) / (sum(main_ms) * 1e-3) / 1e9
+    traffic = profile_traffic()
+    result = {
+        "metric": METRIC, "value": round(tokens / (total_ms * 1e-3), 1), "unit": UNIT,
+        "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(total_ms / K, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic ~N(0,1), seeded",
+        "config": {"workload": "decode128k (BASELINE.json config 4)", "requests_per_gpu": R,
+                   "context": args.context, "heads": HEADS, "head_dim": WIDTH, "layer_index": LAYER,
+                   "preset": "index_only_page_memo", "l2": "flushed between timed steps (256 MiB memset)",
+                   "prefill_s": round(prefill_s, 2),
+                   "prefill_tok_s": round(R * args.context / prefill_s, 1)},
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": 5 * R * HEADS * WIDTH * 2,
+                "d2h_bytes_per_step": R * HEADS * WIDTH * 2},
+        "roofline": {"bound": "hbm", "kernel": "decode_main_kernel<64>",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": int(statistics.mean(algo_bytes)),
+                     "kernel_ms_mean": round(statistics.mean(main_ms), 5),
+                     "traffic": traffic},
+        "gpu_launches": 3 * K,
+        "clocks": clocks.summary(),
+    }
+    return result, states
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (reference port = oracle/tao_oracle.py)
+# ---------------------------------------------------------------------------
+
+def synthetic_oracle_state(layer, context, seed):
+    """A reference-port state at `context` tokens with seeded random contents of
+    the exact shapes a real prefill leaves (values do not change decode cost)."""
+    import torch
+    from oracle import tao_oracle as o
+    g = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    st = o.OracleStream(layer)
+    st.position = context
+    start = 0 if context < 768 else 256 * ((context - 512) // 256)
+    n = context - start
+    st.local = tuple(torch.randn(1, n, HEADS, WIDTH, generator=g).to(bf) for _ in range(3))
+    s = (context - 768) // 256 + 1 if context >= 768 else 0
+    z = (torch.randn(1, HEADS, s, WIDTH, generator=g) + 5).to(bf)
+    st.fine_c = (torch.randn(1, HEADS, s, WIDTH, WIDTH, generator=g) * 0.05).to(bf)
+    full = s // 8
+    st.pages = [(torch.logsumexp(z[:, :, 8 * p:8 * p + 8], dim=2).to(bf), z[:, :, 8 * p:8 * p + 8])
+                for p in range(full)]
+    st.pending = [z[:, :, i] for i in range(8 * full, s)]
+    st.state_version = s
+    q = torch.randn(1, 1, HEADS, WIDTH, generator=g).to(bf)
+    st._read_segment(q, refresh=True)          # populate route ids as a refresh would
+    return st
+
+
+def time_oracle_decode(states, steps, seed, budget_s=None):
+    """Decode `steps` tokens round-robin over the oracle states; return
+    (tokens, seconds)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    fa = (torch.randn(HEADS, WIDTH, 3, generator=g) * 0.02).to(bf)
+    fb = (torch.randn(HEADS, WIDTH, 3, generator=g) * 0.02).to(bf)
+    toks = [torch.randn(5, 1, 1, HEADS, WIDTH, generator=g).to(bf) for _ in range(8)]
+    done, t0 = 0, time.perf_counter()
+    for i in range(steps):
+        st = states[i % len(states)]
+        x = toks[i % len(toks)]
+        st.step(x[0], x[1], x[2], x[3], x[4], fa, fb, 0.5)
+        done += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s:
+            break
+    return done, time.perf_counter() - t0
+
+
+def cpu_baseline_from_gpu(states, sample_steps):
+    """Time the CPU oracle on a bounded sample of the same workload: the GPU
+    states are exported and continued on the host cores."""
+    import torch
+    from oracle import tao_oracle as o
+    torch.set_num_threads(os.cpu_count() or 1)
+    picked = states[:2]
+    host = [o.OracleStream.from_export(st.export()) for st in picked]
+    time_oracle_decode(host, 2, seed=7)                         # warm-up
+    n, secs = time_oracle_decode(host, sample_steps * len(host), seed=8, budget_s=30)
+    return {"value": round(n / secs, 2), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} decode tokens over {len(host)} exported 128K-context requests "
+                      f"(H{HEADS} D{WIDTH}), oracle/tao_oracle.py on the host CPU"}
+
+
+def run_reference(args):
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    t0 = time.time()
+    states = [synthetic_oracle_state(LAYER, args.context, seed=100 + r) for r in range(args.requests)]
+    setup_s = time.time() - t0
+    time_oracle_decode(states, max(args.warmup, 1), seed=1)
+    n, secs = time_oracle_decode(states, args.steps, seed=2, budget_s=240)
+    value = n / secs
+    cores = torch.get_num_threads()
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": n, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / n, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic ~N(0,1), seeded", "impl": "reference",
+        "config": {"workload": "decode128k (BASELINE.json config 4)", "requests": args.requests,
+                   "context": args.context, "heads": HEADS, "head_dim": WIDTH,
+                   "preset": "index_only_page_memo", "step": "one decode token of one request (round robin)",
+                   "setup_s": round(setup_s, 1)},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{n} decode tokens round-robin over {args.requests} synthetic "
+                                   f"128K-context states (oracle/tao_oracle.py: the reference's "
+                                   f"algorithm restated in PyTorch CPU ops)"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args)), flush=True)
+        return 0
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    try:
+        result, states = run_b200(args, world, rank, local)
+        if rank == 0 and world == 1:
+            result["cpu_baseline"] = cpu_baseline_from_gpu(states, args.cpu_sample_steps)
+        elif rank == 0:
+            result["cpu_baseline"] = None
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

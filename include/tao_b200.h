@@ -116,6 +116,17 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
  * Returns TAO_OK or TAO_ERR_DEVICE; *flags receives the raw bits. */
 int tao_stream_check(void* workspace, int* flags, void* stream);
 
+/* CUDA events for timing (thin wrappers over the runtime, so callers need no
+ * other binding).  tao_stream_profile_next(start, stop) makes the next
+ * tao_stream_step on this host thread record `start` just before and `stop` just
+ * after its main kernel(s) (the local-attention + fine-read phase), on the
+ * stream it launches on.  No reference counterpart (profiling hook). */
+int tao_event_create(void** event);
+int tao_event_destroy(void* event);
+int tao_event_record(void* event, void* stream);
+int tao_event_elapsed(void* start, void* stop, float* ms);
+int tao_stream_profile_next(void* start, void* stop);
+
 /* Copy `count` ring slots of one request into a token-ordered [count][H][D] buffer
  * (used by export).  first_position is the absolute position of the first token. */
 int tao_ring_gather(const void* ring, int heads, int width, int64_t first_position,

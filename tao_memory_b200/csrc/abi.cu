@@ -18,6 +18,9 @@
 namespace {
 
 thread_local std::string g_last_error;
+// Events recorded around the main (HBM-bound) kernel of the next tao_stream_step
+// on this host thread; cleared after use.
+thread_local cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -123,6 +126,7 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
   if ((rc = set_smem(prep_kernel<D>, prep_smem))) return rc;
   prep_kernel<D><<<dim3(a.R * a.H, L.nslot), 256, prep_smem, s>>>(a);
   if ((rc = check_launch("prep_kernel"))) return rc;
+  if (g_prof_start) cudaEventRecord(g_prof_start, s);
   if (a.w == 1) {
     using Cfg = DecodeCfg<D>;
     const size_t main_smem = (size_t)Cfg::FPC * D * D * 2 + (size_t)Cfg::FPC * D * 4;
@@ -152,6 +156,8 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
     prefill_fine_kernel<D><<<dim3(a.R * a.H, (a.w + 15) / 16), 128, pf_smem, s>>>(a);
     if ((rc = check_launch("prefill_fine_kernel"))) return rc;
   }
+  if (g_prof_stop) cudaEventRecord(g_prof_stop, s);
+  g_prof_start = g_prof_stop = nullptr;
   const size_t fin_smem = (size_t)2 * kFine * D * 2 + (size_t)2 * D * 4;
   if ((rc = set_smem(finalize_kernel<D>, fin_smem))) return rc;
   finalize_kernel<D><<<a.R * a.H, 256, fin_smem, s>>>(a);
@@ -264,6 +270,40 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
   a.pmax = pmax;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return width == 64 ? launch_step<64>(a, L, s) : launch_step<128>(a, L, s);
+}
+
+int tao_event_create(void** event) {
+  if (!event) return fail(TAO_ERR_ARG, "null event slot");
+  cudaEvent_t e;
+  cudaError_t err = cudaEventCreate(&e);
+  if (err != cudaSuccess) return fail(TAO_ERR_CUDA, "event create: %s", cudaGetErrorString(err));
+  *event = e;
+  return TAO_OK;
+}
+
+int tao_event_destroy(void* event) {
+  if (event) cudaEventDestroy(static_cast<cudaEvent_t>(event));
+  return TAO_OK;
+}
+
+int tao_event_record(void* event, void* stream) {
+  cudaError_t err = cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return fail(TAO_ERR_CUDA, "event record: %s", cudaGetErrorString(err));
+  return TAO_OK;
+}
+
+int tao_event_elapsed(void* start, void* stop, float* ms) {
+  cudaError_t err = cudaEventSynchronize(static_cast<cudaEvent_t>(stop));
+  if (err == cudaSuccess)
+    err = cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(stop));
+  if (err != cudaSuccess) return fail(TAO_ERR_CUDA, "event elapsed: %s", cudaGetErrorString(err));
+  return TAO_OK;
+}
+
+int tao_stream_profile_next(void* start, void* stop) {
+  g_prof_start = static_cast<cudaEvent_t>(start);
+  g_prof_stop = static_cast<cudaEvent_t>(stop);
+  return TAO_OK;
 }
 
 int tao_stream_check(void* workspace, int* flags, void* stream) {

@@ -127,6 +127,9 @@ class StreamCache:
 
     # -- device buffers --------------------------------------------------
     def _allocate(self, heads, width, device, cap):
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
         if width not in (64, 128):
             raise ValueError("head width must be 64 or 128")
         cap = max(GROUP, int(math.ceil(cap / GROUP)) * GROUP)
@@ -192,6 +195,8 @@ class StreamCache:
         return self._ptrs
 
     def _ensure(self, heads, width, device, tokens):
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
         if self._buf is None:
             end = self.position + tokens
             self._allocate(heads, width, device, max(64, sealed_at(end) + 1))
@@ -398,3 +403,87 @@ def check_device(device=None):
     _lib.check(_lib.lib().tao_stream_check(ws.data_ptr(), ctypes.byref(flags),
                                            torch.cuda.current_stream(dev).cuda_stream))
     return flags.value
+
+
+def route_count_at(pos, layer, config):
+    """Selected fines M held by a state serving ``pos`` (from its latest refresh)."""
+    if pos < WINDOW:
+        return 0
+    first_turn = WINDOW + config.layer_stagger * layer
+    if pos < first_turn:
+        last = WINDOW
+    else:
+        last = first_turn + ((pos - first_turn) // config.route_period) * config.route_period
+    s = sealed_at(last)
+    return routed_counts(s // GROUP, s % GROUP, config)[2]
+
+
+def decode_bytes(states):
+    """Algorithmic HBM bytes of one decode step's main phase for these states:
+    local K and V of every key in the window (current token included), the
+    selected fine matrices with their z / page z / page weight rows, q and raw_q."""
+    total = 0
+    for st in states:
+        h, d, pos = st.heads, st.width, st.position
+        keys = pos - window_start(pos) + 1
+        m = route_count_at(pos, st.layer_index, st.config)
+        total += keys * h * d * 2 * 2 + m * h * (d * d * 2 + 3 * d * 2) + 2 * h * d * 2
+    return total
+
+
+class BatchDecoder:
+    """Low-overhead decode loop over the C ABI for a fixed set of states.
+
+    ``step(q, k, v, raw_q, raw_k, out)`` takes device pointers of
+    [len(states), 1, H, D] bf16 buffers and advances every state by one token.
+    Capacity is reserved up front with ``reserve(tokens)``; the loop performs no
+    allocation and no synchronisation.
+    """
+
+    def __init__(self, states, fusion_a, fusion_b, alpha, device):
+        self.states = list(states)
+        self.dev = torch.device(device)
+        st0 = self.states[0]
+        self.heads, self.width = st0.heads, st0.width
+        self.fa = fusion_a.detach().to(self.dev, _BF16).contiguous()
+        self.fb = fusion_b.detach().to(self.dev, _BF16).contiguous()
+        self.alpha = float(alpha)
+        self.policy = policy_for(st0.config)
+        self.lib = _lib.lib()
+        self.r = len(self.states)
+        self.pos = (ctypes.c_int64 * self.r)()
+        self.cap = (ctypes.c_int32 * self.r)()
+        nbytes = self.lib.tao_stream_workspace_bytes(self.r, 1, self.heads, self.width, ROUTE_CAP,
+                                                     ctypes.byref(self.policy))
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.dev)
+        self._sync_ptrs()
+
+    def _sync_ptrs(self):
+        self.ptrs = torch.tensor([st._desc.data_ptr() for st in self.states], dtype=torch.int64,
+                                 device=self.dev)
+        for i, st in enumerate(self.states):
+            self.pos[i] = st.position
+            self.cap[i] = st.cap_fines
+
+    def reserve(self, tokens):
+        """Make every state's fine bank hold ``tokens`` more tokens of history."""
+        for st in self.states:
+            need = sealed_at(st.position + tokens) + 1
+            if need > st.cap_fines:
+                st._grow(need)
+        self._sync_ptrs()
+
+    def step(self, q, k, v, raw_q, raw_k, out, stream=None):
+        s = torch.cuda.current_stream(self.dev).cuda_stream if stream is None else stream
+        _lib.check(self.lib.tao_stream_step(
+            self.ptrs.data_ptr(), self.r, self.pos, self.cap, ctypes.byref(self.policy), 1,
+            self.heads, self.width, q, k, v, raw_q, raw_k, self.fa.data_ptr(), self.fb.data_ptr(),
+            self.alpha, out, self.ws.data_ptr(), self.ws.numel(), s))
+        for i, st in enumerate(self.states):
+            st.position += 1
+            self.pos[i] = st.position
+
+    def check(self):
+        flags = ctypes.c_int(0)
+        _lib.check(self.lib.tao_stream_check(self.ws.data_ptr(), ctypes.byref(flags),
+                                             torch.cuda.current_stream(self.dev).cuda_stream))

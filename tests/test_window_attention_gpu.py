@@ -28,7 +28,7 @@ def test_window_attention_matches_oracle(b, t, h, d):
     bad = ((got - ref).abs() > 2e-2 + 2e-2 * ref.abs()).float().mean().item()
     assert bad == 0.0, bad
     # log-sum-exp of scaled scores, checked on a few rows
-    for tq in (0, 255, 700, t - 1):
+    for tq in (tq for tq in (0, 255, 700, t - 1) if tq < t):
         start = max(0, 256 * (tq // 256) - 512)
         s = (x["q"][0, tq, 0].float() @ x["k"][0, start:tq + 1, 0].float().T) / d ** 0.5
         assert abs(torch.logsumexp(s, 0).item() - lse[0, 0, tq].item()) < 1e-2
