@@ -116,6 +116,21 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
  * Returns TAO_OK or TAO_ERR_DEVICE; *flags receives the raw bits. */
 int tao_stream_check(void* workspace, int* flags, void* stream);
 
+/* Decode step (one token for each of n_states requests) that allocates nothing:
+ * same arguments and results as tao_stream_step with tokens = 1, but its scratch
+ * lives in a static 4 MiB device array inside the library instead of a
+ * caller-provided workspace.  For callers that cannot call cudaMalloc (memory
+ * owned by another runtime's pool, or loops where an allocation could
+ * synchronise the device).  Batches whose decode scratch exceeds 4 MiB return
+ * TAO_ERR_CAPACITY.  All calls on a device share that array: calls that overlap
+ * on the GPU race, so serialise them; the first call on a device sets the array
+ * up and should come before any stream capture.  No counterpart in the reference. */
+int tao_stream_decode_noalloc(void* const* states, int n_states, const int64_t* host_pos,
+                              const int32_t* host_cap, const TaoPolicy* policy, int heads,
+                              int width, const void* q, const void* k, const void* v,
+                              const void* raw_q, const void* raw_k, const void* fusion_a,
+                              const void* fusion_b, float alpha, void* out, void* stream);
+
 /* CUDA events for timing (thin wrappers over the runtime, so callers need no
  * other binding).  tao_stream_profile_next(start, stop) makes the next
  * tao_stream_step on this host thread record `start` just before and `stop` just

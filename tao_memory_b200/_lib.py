@@ -49,6 +49,9 @@ _SIGNATURES = {
                              ctypes.POINTER(TaoPolicy), _I, _I, _I, _VP, _VP, _VP, _VP, _VP,
                              _VP, _VP, _F, _VP, _VP, _SZ, _VP]),
     "tao_stream_check": (_I, [_VP, ctypes.POINTER(_I), _VP]),
+    "tao_stream_decode_noalloc": (_I, [_VP, _I, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_int32),
+                                       ctypes.POINTER(TaoPolicy), _I, _I, _VP, _VP, _VP, _VP, _VP,
+                                       _VP, _VP, _F, _VP, _VP]),
     "tao_ring_gather": (_I, [_VP, _I, _I, _I64, _I, _VP, _VP]),
     "tao_ring_scatter": (_I, [_VP, _I, _I, _I64, _I, _VP, _VP]),
     "tao_state_rebuild_memo": (_I, [_VP, _I, _I, _I, _VP]),

@@ -106,6 +106,10 @@ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 }  // namespace
 
+// Lets other translation units of the library report a message through
+// tao_last_error() on the calling host thread.
+void tao_set_last_error(const char* msg) { g_last_error = msg; }
+
 namespace {
 
 template <typename F>
