@@ -162,6 +162,41 @@ int tao_window_attention(const void* q, const void* k, const void* v, void* out,
                          float* lse, int batch, int tokens, int heads, int width,
                          void* stream);
 
+/* ---- training (tao_attention, operator.py:42-54) -------------------------
+ * Saved buffers of one forward, allocated by the caller (sizes from
+ * tao_train_geometry; S sealed blocks, P pages, mmax selected fines per query):
+ *   local [B][T][H][D] bf16, lse fp32 [B][H][T], fine_z [B][H][S][D] bf16,
+ *   fine_c [B][H][S][D][D] bf16, page_prefix [B][H][P][8][D] bf16,
+ *   num [B][T][H][D] bf16, den fp32 [B][T][H], sel int16 [B][T][H][mmax],
+ *   err int32 (device error word). */
+typedef struct TaoTrainBuffers {
+  void* local;
+  float* lse;
+  void* fine_z;
+  void* fine_c;
+  void* page_prefix;
+  void* num;
+  float* den;
+  int16_t* sel;
+  int* err;
+  int32_t mmax;
+  int32_t reserved;
+} TaoTrainBuffers;
+
+/* S = T/256 - 1 sealed blocks (0 for T <= 768), pages = ceil(S/8), and the
+ * largest number of selected fines any query of a T-token sequence reads. */
+int tao_train_geometry(int tokens, int* sealed, int* pages, int* mmax);
+
+/* Forward of tao_attention for [B][T][H][D] bf16 operands (index-only preset):
+ * windowed local attention, softmax writer over all sealed blocks, per-query
+ * routing with fresh selection, selected fine read and pointwise fusion.
+ * gain: device fp32 [H] = bf16(2 * alpha_h).  Reference: tao_stream.py:668-787,
+ * operator.py:21-54. */
+int tao_train_forward(const void* q, const void* k, const void* v, const void* raw_q,
+                      const void* raw_k, const void* fusion_a, const void* fusion_b,
+                      const float* gain, int batch, int tokens, int heads, int width,
+                      void* out, const TaoTrainBuffers* buffers, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

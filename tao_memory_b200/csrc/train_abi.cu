@@ -1,0 +1,155 @@
+// extern "C" training entry points (tao_attention forward / backward).
+#include <cuda_runtime.h>
+
+#include <cstdio>
+
+#include "../../include/tao_b200.h"
+#include "train_kernels.cuh"
+
+void tao_set_last_error(const char* msg);
+
+namespace {
+
+int tfail(int code, const char* msg) {
+  tao_set_last_error(msg);
+  return code;
+}
+
+int t_budget(int count) {
+  if (count <= 0) return 0;
+  long long sq = 2LL * count, r = 0;
+  while ((r + 1) * (r + 1) <= sq) ++r;
+  if (r * r < sq) ++r;
+  return (int)(r + 2 < count ? r + 2 : count);
+}
+int t_selected(int completed, int pending) {
+  const int cb = t_budget(8 * completed);
+  int coarse = (2 * cb + 7) / 8;
+  if (coarse > completed) coarse = completed;
+  const int eligible = 8 * coarse + pending;
+  const int b = t_budget(8 * completed + pending);
+  return eligible < b ? eligible : b;
+}
+
+struct Geometry {
+  int tiles, S, pages, vmax, pmax, mmax;
+};
+Geometry geometry(int T) {
+  Geometry g{};
+  g.tiles = (T + 255) / 256;
+  g.S = T > 768 ? T / 256 - 1 : 0;
+  g.pages = g.S > 0 ? (g.S + 7) / 8 : 0;
+  g.vmax = g.tiles > 3 ? g.tiles - 3 : 0;
+  g.pmax = g.vmax / 8 + 1;
+  g.mmax = 1;
+  for (int v = 1; v <= g.vmax; ++v) {
+    const int m = t_selected(v / 8, v % 8);
+    if (m > g.mmax) g.mmax = m;
+  }
+  return g;
+}
+
+template <typename F>
+bool tsmem(F* fn, size_t bytes) {
+  return bytes <= 48 * 1024 ||
+         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess;
+}
+
+template <int D>
+int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, const tao::bf16* rq,
+                  const tao::bf16* rk, const tao::bf16* fa, const tao::bf16* fb, const float* gain, int B,
+                  int T, int H, tao::bf16* out, const TaoTrainBuffers& tb, cudaStream_t s) {
+  using namespace tao;
+  const Geometry g = geometry(T);
+  TrainDims dm{B, T, H, g.S, (long long)H * D};
+  // 1. exact local window attention
+  WinAttnParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.out = static_cast<bf16*>(tb.local);
+  p.lse = tb.lse;
+  p.q_batch_stride = p.k_batch_stride = p.o_batch_stride = (long long)T * H * D;
+  p.q_row_stride = p.k_row_stride = p.o_row_stride = (long long)H * D;
+  p.k_head_stride = D;
+  p.heads = H;
+  p.nq = T;
+  p.kstart = -1;
+  const size_t attn_smem = (size_t)(64 + 4 * 64) * D * 2;
+  if (!tsmem(window_attention_kernel<D>, attn_smem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+  window_attention_kernel<D><<<dim3((T + 63) / 64, B * H), 128, attn_smem, s>>>(p);
+  if (g.S > 0) {
+    // 2. writer over all sealed blocks, 3. page prefix table
+    const size_t wsmem = (size_t)2 * 256 * D * 2 + 2 * D * 4;
+    if (!tsmem(writer_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+    writer_kernel<D><<<B * H * g.S, 128, wsmem, s>>>(rk, v, static_cast<bf16*>(tb.fine_z),
+                                                      static_cast<bf16*>(tb.fine_c), dm);
+    const long long n = (long long)B * H * g.pages * D;
+    page_prefix_kernel<D><<<(int)((n + 255) / 256), 256, 0, s>>>(
+        static_cast<const bf16*>(tb.fine_z), static_cast<bf16*>(tb.page_prefix), dm, g.pages);
+  }
+  // 4. routing + selected read + fusion
+  ReadArgs a{};
+  a.raw_q = rq;
+  a.local = static_cast<const bf16*>(tb.local);
+  a.fa = fa;
+  a.fb = fb;
+  a.gain = gain;
+  a.z = static_cast<const bf16*>(tb.fine_z);
+  a.C = static_cast<const bf16*>(tb.fine_c);
+  a.pzpre = static_cast<const bf16*>(tb.page_prefix);
+  a.out = out;
+  a.num_out = static_cast<bf16*>(tb.num);
+  a.den_out = tb.den;
+  a.sel_out = tb.sel;
+  a.dm = dm;
+  a.pages = g.pages;
+  a.mmax = g.mmax;
+  a.err = tb.err;
+  const size_t rsmem = ReadSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
+  if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the training read kernel");
+  if (!tsmem(train_read_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+  train_read_kernel<D><<<dim3(g.tiles, B * H), 256, rsmem, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return tfail(TAO_ERR_CUDA, cudaGetErrorString(e));
+  return TAO_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tao_train_geometry(int tokens, int* sealed, int* pages, int* mmax) {
+  if (tokens <= 0) return tfail(TAO_ERR_ARG, "tokens must be positive");
+  const Geometry g = geometry(tokens);
+  if (sealed) *sealed = g.S;
+  if (pages) *pages = g.pages;
+  if (mmax) *mmax = g.mmax;
+  return TAO_OK;
+}
+
+int tao_train_forward(const void* q, const void* k, const void* v, const void* raw_q, const void* raw_k,
+                      const void* fusion_a, const void* fusion_b, const float* gain, int batch,
+                      int tokens, int heads, int width, void* out, const TaoTrainBuffers* buffers,
+                      void* stream) {
+  if (!q || !k || !v || !raw_q || !raw_k || !fusion_a || !fusion_b || !gain || !out || !buffers)
+    return tfail(TAO_ERR_ARG, "null pointer");
+  if (width != 64 && width != 128) return tfail(TAO_ERR_ARG, "head width must be 64 or 128");
+  if (batch <= 0 || tokens <= 0 || heads <= 0) return tfail(TAO_ERR_ARG, "bad shape");
+  const TaoTrainBuffers& tb = *buffers;
+  if (!tb.local || !tb.lse || !tb.num || !tb.den || !tb.sel || !tb.err)
+    return tfail(TAO_ERR_ARG, "null training buffer");
+  if (tokens > 768 && (!tb.fine_z || !tb.fine_c || !tb.page_prefix))
+    return tfail(TAO_ERR_ARG, "null fine buffers");
+  if (tb.mmax != geometry(tokens).mmax) return tfail(TAO_ERR_ARG, "buffers.mmax does not match tao_train_geometry");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tao::bf16;
+  auto B = [](const void* p) { return static_cast<const bf16*>(p); };
+  return width == 64
+             ? train_forward<64>(B(q), B(k), B(v), B(raw_q), B(raw_k), B(fusion_a), B(fusion_b), gain, batch,
+                                 tokens, heads, static_cast<bf16*>(out), tb, s)
+             : train_forward<128>(B(q), B(k), B(v), B(raw_q), B(raw_k), B(fusion_a), B(fusion_b), gain, batch,
+                                  tokens, heads, static_cast<bf16*>(out), tb, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,451 @@
+// Training forward kernels of tao_attention on sm_100a.
+//
+// Reference: tao_stream.py:80-123 (writer over all blocks), 530-593 (page
+// summaries), 596-665 (per-tile routing and selected read), operator.py:21-39
+// (fusion).  Every query routes (route_interval = 1): tile t of 256 queries sees
+// the first max(0, t - 2) sealed fines.
+#pragma once
+#include "common.cuh"
+#include "window_attention.cuh"
+
+namespace tao {
+
+struct TrainDims {
+  int B, T, H, S;   // S = T/256 - 1 sealed blocks (0 when T <= 768)
+  long long row;    // token stride in elements (H * D)
+};
+
+// ---------------------------------------------------------------------------
+// Writer: one CTA per (b, h, block s).  z[b][h][s][d] and C[b][h][s][d][e] with
+// the reference's rounding points; C = p^T v on the tensor cores.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(128) writer_kernel(const bf16* __restrict__ raw_k,
+                                                     const bf16* __restrict__ v, bf16* z_out,
+                                                     bf16* c_out, TrainDims dm) {
+  using namespace wa;
+  constexpr int NT = 256, CH = D / 8;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sP = smem_u32(smem);        // [256][D] raw keys, then probabilities
+  const uint32_t sV = sP + NT * D * 2;       // [256][D]
+  float* mx = reinterpret_cast<float*>(smem + 2 * NT * D * 2);
+  float* zp = mx + D;
+  bf16* pk = reinterpret_cast<bf16*>(smem);
+  const int s = blockIdx.x % dm.S, h = (blockIdx.x / dm.S) % dm.H, b = blockIdx.x / (dm.S * dm.H);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bf16* kb = raw_k + ((long long)b * dm.T + (long long)s * NT) * dm.row + (long long)h * D;
+  const bf16* vb = v + ((long long)b * dm.T + (long long)s * NT) * dm.row + (long long)h * D;
+  for (int idx = tid; idx < NT * CH; idx += 128) {
+    int r = idx / CH, c = idx % CH;
+    cp_async16(sP + swz(r, c * 8, D), kb + (long long)r * dm.row + c * 8, true);
+    cp_async16(sV + swz(r, c * 8, D), vb + (long long)r * dm.row + c * 8, true);
+  }
+  cp_commit();
+  cp_wait<0>();
+  __syncthreads();
+  auto at = [&](int r, int d) -> bf16& {
+    return *reinterpret_cast<bf16*>(smem + swz(r, d, D));
+  };
+  // per channel: max, partition = bf16(sum_t bf16(exp(bf16(k - max)))) in token order
+  for (int d = tid; d < D; d += 128) {
+    float m = -INFINITY;
+    for (int t = 0; t < NT; ++t) m = fmaxf(m, bf(at(t, d)));
+    float sum = 0.f;
+    for (int t = 0; t < NT; ++t) sum += rb(expf(rb(__fsub_rn(bf(at(t, d)), m))));
+    mx[d] = m;
+    zp[d] = rb(sum);
+  }
+  __syncthreads();
+  for (int idx = tid; idx < NT * D; idx += 128) {
+    const int t = idx / D, d = idx % D;
+    const float e = rb(expf(rb(__fsub_rn(bf(at(t, d)), mx[d]))));
+    at(t, d) = tobf(__fdiv_rn(e, zp[d]));
+  }
+  bf16* zo = z_out + (((long long)b * dm.H + h) * dm.S + s) * D;
+  for (int d = tid; d < D; d += 128) zo[d] = tobf(__fadd_rn(mx[d], rb(logf(zp[d]))));
+  __syncthreads();
+  // C[d][e] = sum_t p[t][d] v[t][e]: warp w owns rows d in [w*D/4, (w+1)*D/4)
+  constexpr int MT = D / 64;  // m-tiles of 16 rows per warp: 1 (D64) or 2 (D128)
+  constexpr int NTL = D / 8;  // n-tiles of 8 columns
+  float acc[MT][NTL][4];
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int j = 0; j < NTL; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.f;
+  for (int kt = 0; kt < NT / 16; ++kt) {
+    uint32_t a[MT][4];
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+      const int d0 = warp * (D / 4) + i * 16;
+      const int r = kt * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+      const int c = d0 + ((lane >> 3) & 1) * 8;
+      ldsm_x4_t(sP + swz(r, c, D), a[i][0], a[i][1], a[i][2], a[i][3]);
+    }
+#pragma unroll
+    for (int np = 0; np < D / 16; ++np) {
+      uint32_t b0, b1, b2, b3;
+      const int r = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int c = np * 16 + (lane >> 4) * 8;
+      ldsm_x4_t(sV + swz(r, c, D), b0, b1, b2, b3);
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        mma16816(acc[i][2 * np], a[i], b0, b1);
+        mma16816(acc[i][2 * np + 1], a[i], b2, b3);
+      }
+    }
+  }
+  bf16* co = c_out + (((long long)b * dm.H + h) * dm.S + s) * (long long)D * D;
+  const int g = lane >> 2, c4 = lane & 3;
+#pragma unroll
+  for (int i = 0; i < MT; ++i) {
+    const int d0 = warp * (D / 4) + i * 16;
+#pragma unroll
+    for (int j = 0; j < NTL; ++j) {
+      const int e = j * 8 + c4 * 2;
+      *reinterpret_cast<__nv_bfloat162*>(co + (long long)(d0 + g) * D + e) =
+          __floats2bfloat162_rn(acc[i][j][0], acc[i][j][1]);
+      *reinterpret_cast<__nv_bfloat162*>(co + (long long)(d0 + g + 8) * D + e) =
+          __floats2bfloat162_rn(acc[i][j][2], acc[i][j][3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Page prefix table: pzpre[b][h][p][n-1][d] = bf16 logsumexp composite over the
+// first n fines of page p (n = 1..8), the page log-partition a tile sees for a
+// pending page of n fines (n = 8: a completed page).  tao_stream.py:530-593.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void page_prefix_kernel(const bf16* __restrict__ z, bf16* pzpre, TrainDims dm, int pages) {
+  const long long total = (long long)dm.B * dm.H * pages * D;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(idx % D);
+    const int p = (int)((idx / D) % pages);
+    const long long bh = idx / ((long long)D * pages);
+    const bf16* zb = z + (bh * dm.S + (long long)p * kGroup) * D + d;
+    const int avail = min(kGroup, dm.S - p * kGroup);
+    for (int n = 1; n <= kGroup; ++n) {
+      float out = 0.f;
+      if (n <= avail) {
+        float mx = -INFINITY;
+        for (int i = 0; i < n; ++i) mx = fmaxf(mx, bf(zb[(long long)i * D]));
+        const float m0 = (fabsf(mx) == INFINITY) ? 0.f : mx;
+        float s = 0.f;
+        for (int i = 0; i < n; ++i) s += rb(expf(rb(__fsub_rn(bf(zb[(long long)i * D]), m0))));
+        out = rb(__fadd_rn(rb(logf(rb(s))), m0));
+      }
+      pzpre[((bh * pages + p) * kGroup + (n - 1)) * D + d] = tobf(out);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Training read: one CTA (256 threads) per (tile of 256 queries, b, h).
+//  1. page table of the tile: completed pages + the pending prefix; page weights
+//     pw = bf16(softmax over pages); segment weights sw[s] = bf16(exp(bf16(z-pz)))
+//  2. thread q routes query q: h = bf16(softmax(raw_q)), page mass top-K (stable),
+//     candidate scores bf16(sum_d bf16(bf16(h*pw)*sw)), top-M (stable) kept as an
+//     insertion list; den = bf16(sum of the selected scores)
+//  3. for every fine s selected by some query of the tile: A_s[q] = a_{q,s}
+//     (zero rows for queries that did not select s), acc += A_s . C_s on the
+//     tensor cores (C_s double-buffered through cp.async)
+//  4. epilogue: num = bf16(acc), fine = bf16(num/den), pointwise fusion -> out.
+// Tiles without history (t < 3) copy the local output.
+// ---------------------------------------------------------------------------
+struct ReadArgs {
+  const bf16 *raw_q, *local, *fa, *fb;  // [B,T,H,D] x2, [H,D,3] x2
+  const float* gain;                     // [H] bf16(2*alpha_h) as float
+  const bf16 *z, *C, *pzpre;             // [B,H,S,D], [B,H,S,D,D], [B,H,pages,8,D]
+  bf16* out;                             // [B,T,H,D]
+  bf16* num_out;                         // [B,T,H,D]   (saved for backward)
+  float* den_out;                        // [B,T,H]
+  int16_t* sel_out;                      // [B,T,H,mmax] selected fine ids (-1 pad)
+  TrainDims dm;
+  int pages, mmax, umax;
+  int* err;
+};
+
+template <int D>
+struct ReadSmem {
+  static constexpr int NBUF = (D == 64) ? 2 : 1;
+  static size_t bytes(int P, int V, int mmax) {
+    size_t s = 0;
+    s += 256 * D * 2;              // h
+    s += 256 * D * 2;              // A tile
+    s += NBUF * D * D * 2;         // C buffers
+    s += 2 * (size_t)P * D * 4;    // pw, pz
+    s += (size_t)V * D * 2 + 16;   // segment weights
+    s += 256 * (size_t)(mmax + 1) * 4;  // top scores
+    s += 256 * (size_t)(mmax + 1) * 4;  // top ids
+    s += 256 * 4 + (size_t)(V + 8) * 4 * 2 + 256;   // den, use flags + list, misc
+    return s;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
+  using namespace wa;
+  constexpr int NBUF = ReadSmem<D>::NBUF;
+  const int tile = blockIdx.x, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q0 = tile * 256;
+  const int nq = min(256, a.dm.T - q0);
+  const int V = max(0, tile - 2);
+  const long long row = a.dm.row;
+  const long long hoff = (long long)h * D;
+
+  if (V == 0) {  // no history: output = local (operator.py:39)
+    for (int idx = tid; idx < nq * (D / 8); idx += 256) {
+      const int q = idx / (D / 8), c = idx % (D / 8);
+      const long long off = ((long long)b * a.dm.T + q0 + q) * row + hoff + c * 8;
+      *reinterpret_cast<uint4*>(a.out + off) = *reinterpret_cast<const uint4*>(a.local + off);
+    }
+    return;
+  }
+  const int completed = V / kGroup, pending = V % kGroup, P = completed + (pending > 0);
+  const Policy pol{24, 2, 2, 2};
+  const Counts cnt = routed_counts(completed, pending, pol);
+  const int K = cnt.coarse, M = cnt.selected;
+  if (M > a.mmax || completed > 64) {
+    if (tid == 0) atomicOr(a.err, kErrRouteCap);
+    return;
+  }
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ptr = smem;
+  const uint32_t sH = smem_u32(ptr);   ptr += 256 * D * 2;
+  const uint32_t sA = smem_u32(ptr);   ptr += 256 * D * 2;
+  const uint32_t sC = smem_u32(ptr);   ptr += NBUF * D * D * 2;
+  bf16* hS = reinterpret_cast<bf16*>(smem);
+  bf16* aS = hS + 256 * D;
+  float* pwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
+  float* pzS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
+  bf16* swS = reinterpret_cast<bf16*>(ptr);    ptr += ((size_t)V * D * 2 + 15) / 16 * 16;
+  float* topS = reinterpret_cast<float*>(ptr); ptr += 256 * (size_t)(a.mmax + 1) * 4;
+  int* topI = reinterpret_cast<int*>(ptr);     ptr += 256 * (size_t)(a.mmax + 1) * 4;
+  float* denS = reinterpret_cast<float*>(ptr); ptr += 256 * 4;
+  int* useS = reinterpret_cast<int*>(ptr);
+  const int TS = a.mmax + 1;  // row stride of the top lists (odd-ish: fewer bank conflicts)
+
+  // ---- 1. page table, page weights, segment weights
+  const bf16* pzb = a.pzpre + ((long long)b * a.dm.H + h) * a.pages * kGroup * D;
+  for (int idx = tid; idx < P * D; idx += 256) {
+    const int p = idx / D, d = idx % D;
+    const int n = (p < completed) ? kGroup : pending;
+    pzS[idx] = bf(pzb[((long long)p * kGroup + (n - 1)) * D + d]);
+  }
+  for (int i = tid; i < V; i += 256) useS[i] = 0;
+  __syncthreads();
+  for (int d = tid; d < D; d += 256) {
+    float mx = -INFINITY;
+    for (int p = 0; p < P; ++p) mx = fmaxf(mx, pzS[p * D + d]);
+    float sum = 0.f;
+    for (int p = 0; p < P; ++p) sum += expf(pzS[p * D + d] - mx);
+    for (int p = 0; p < P; ++p) pwS[p * D + d] = rb(__fdiv_rn(expf(pzS[p * D + d] - mx), sum));
+  }
+  const bf16* zb = a.z + ((long long)b * a.dm.H + h) * a.dm.S * D;
+  for (int idx = tid; idx < V * D; idx += 256) {
+    const int s = idx / D, d = idx % D;
+    swS[idx] = tobf(expf(rb(__fsub_rn(bf(zb[(long long)s * D + d]), pzS[(s / kGroup) * D + d]))));
+  }
+  // ---- h = bf16(softmax(raw_q)) per query, stored swizzled
+  const int q = tid;
+  const bool live = q < nq;
+  const bf16* rq = a.raw_q + ((long long)b * a.dm.T + q0 + q) * row + hoff;
+  if (live) {
+    float mx = -INFINITY;
+    for (int c = 0; c < D / 8; ++c) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
+    }
+    float sum = 0.f;
+    for (int c = 0; c < D / 8; ++c) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      for (int e = 0; e < 8; ++e) sum += expf(f[e] - mx);
+    }
+    for (int c = 0; c < D / 8; ++c) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      __nv_bfloat162 o[4];
+      for (int e = 0; e < 4; ++e)
+        o[e] = __floats2bfloat162_rn(__fdiv_rn(expf(f[2 * e] - mx), sum), __fdiv_rn(expf(f[2 * e + 1] - mx), sum));
+      *reinterpret_cast<uint4*>(smem + swz(q, c * 8, D)) = *reinterpret_cast<uint4*>(o);
+    }
+  }
+  __syncthreads();
+
+  // ---- 2. routing of query q (thread q)
+  float* tS = topS + q * TS;
+  int* tI = topI + q * TS;
+  int nt = 0;
+  auto hval = [&](int d) -> float { return bf(*reinterpret_cast<const bf16*>(smem + swz(q, d, D))); };
+  if (live) {
+    uint64_t chosen = 0;
+    for (int k = 0; k < K; ++k) {
+      float best = -INFINITY;
+      int bp = 0;
+      for (int p = 0; p < completed; ++p) {
+        if ((chosen >> p) & 1ull) continue;
+        float m = 0.f;
+        for (int d = 0; d < D; ++d) m += rb(__fmul_rn(hval(d), pwS[p * D + d]));
+        m = rb(m);
+        if (m > best) { best = m; bp = p; }
+      }
+      chosen |= 1ull << bp;
+    }
+    auto consider = [&](int id, int page) {
+      float sc = 0.f;
+      for (int d = 0; d < D; ++d)
+        sc += rb(__fmul_rn(rb(__fmul_rn(hval(d), pwS[page * D + d])), bf(swS[id * D + d])));
+      sc = rb(sc);
+      int pos = 0;
+      while (pos < nt && tS[pos] >= sc) ++pos;   // stable: equal scores keep the older id first
+      if (pos >= M) return;
+      const int last = (nt < M) ? nt : M - 1;
+      for (int j = last; j > pos; --j) { tS[j] = tS[j - 1]; tI[j] = tI[j - 1]; }
+      tS[pos] = sc;
+      tI[pos] = id;
+      if (nt < M) ++nt;
+    };
+    for (int p = 0; p < completed; ++p)
+      if ((chosen >> p) & 1ull)
+        for (int j = 0; j < kGroup; ++j) consider(p * kGroup + j, p);
+    for (int j = 0; j < pending; ++j) consider(completed * kGroup + j, completed);
+    float den = 0.f;
+    for (int m = 0; m < nt; ++m) {
+      den += tS[m];
+      useS[tI[m]] = 1;
+    }
+    denS[q] = rb(den);
+    int16_t* so = a.sel_out + (((long long)b * a.dm.T + q0 + q) * a.dm.H + h) * a.mmax;
+    for (int m = 0; m < a.mmax; ++m) so[m] = (int16_t)(m < nt ? tI[m] : -1);
+    a.den_out[((long long)b * a.dm.T + q0 + q) * a.dm.H + h] = denS[q];
+  }
+  __syncthreads();
+  int* list = useS + V;  // compacted list of fines selected by some query of the tile
+  __shared__ int nused;
+  if (tid == 0) {
+    int n = 0;
+    for (int s2 = 0; s2 < V; ++s2)
+      if (useS[s2]) list[n++] = s2;
+    nused = n;
+  }
+  __syncthreads();
+
+  // ---- 3. dense per-fine GEMMs on the tensor cores
+  constexpr int NTL = D / 8;
+  float acc[2][NTL][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < NTL; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.f;
+  const bf16* cb = a.C + ((long long)b * a.dm.H + h) * a.dm.S * (long long)D * D;
+  auto load_c = [&](int s2, int buf) {
+    const bf16* src = cb + (long long)s2 * D * D;
+    for (int idx = tid; idx < D * D / 8; idx += 256) {
+      const int r = idx / (D / 8), c = idx % (D / 8);
+      cp_async16(sC + buf * D * D * 2 + swz(r, c * 8, D), src + r * D + c * 8, true);
+    }
+    cp_commit();
+  };
+  const int nu = nused;
+  if (nu > 0) load_c(list[0], 0);
+  for (int i = 0; i < nu; ++i) {
+    const int s2 = list[i];
+    const int buf = (NBUF == 2) ? (i & 1) : 0;
+    if (NBUF == 2 && i + 1 < nu) load_c(list[i + 1], buf ^ 1);
+    // A_s row q
+    if (live) {
+      bool sel = false;
+      for (int m = 0; m < nt; ++m) sel |= (tI[m] == s2);
+      const int page = s2 / kGroup;
+      for (int c = 0; c < D / 8; ++c) {
+        __nv_bfloat162 o[4];
+        if (sel) {
+          for (int e = 0; e < 4; ++e) {
+            const int d = c * 8 + 2 * e;
+            const float a0 = rb(__fmul_rn(rb(__fmul_rn(hval(d), pwS[page * D + d])), bf(swS[s2 * D + d])));
+            const float a1 = rb(__fmul_rn(rb(__fmul_rn(hval(d + 1), pwS[page * D + d + 1])), bf(swS[s2 * D + d + 1])));
+            o[e] = __floats2bfloat162_rn(a0, a1);
+          }
+        } else {
+          for (int e = 0; e < 4; ++e) o[e] = __floats2bfloat162_rn(0.f, 0.f);
+        }
+        *reinterpret_cast<uint4*>(smem + 256 * D * 2 + swz(q, c * 8, D)) = *reinterpret_cast<uint4*>(o);
+      }
+    } else {
+      for (int c = 0; c < D / 8; ++c)
+        *reinterpret_cast<uint4*>(smem + 256 * D * 2 + swz(q, c * 8, D)) = make_uint4(0, 0, 0, 0);
+    }
+    if (NBUF == 2 && i + 1 < nu) cp_wait<1>(); else cp_wait<0>();
+    __syncthreads();
+#pragma unroll
+    for (int kt = 0; kt < D / 16; ++kt) {
+      uint32_t af[2][4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const int r = warp * 32 + mi * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kt * 16 + (lane >> 4) * 8;
+        ldsm_x4(sA + swz(r, c, D), af[mi][0], af[mi][1], af[mi][2], af[mi][3]);
+      }
+#pragma unroll
+      for (int np = 0; np < D / 16; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = np * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(sC + buf * D * D * 2 + swz(r, c, D), b0, b1, b2, b3);
+#pragma unroll
+        for (int mi = 0; mi < 2; ++mi) {
+          mma16816(acc[mi][2 * np], af[mi], b0, b1);
+          mma16816(acc[mi][2 * np + 1], af[mi], b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+    if (NBUF == 1 && i + 1 < nu) load_c(list[i + 1], 0);
+  }
+
+  // ---- 4. epilogue: num, fine, fusion (operator.py:21-39, index-only preset)
+  const float gain = a.gain[h];
+  const int g = lane >> 2, c4 = lane & 3;
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi) {
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = warp * 32 + mi * 16 + g + hr * 8;
+      if (r >= nq) continue;
+      const float den = denS[r];
+      const long long base = ((long long)b * a.dm.T + q0 + r) * row + hoff;
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) {
+        const int e = j * 8 + c4 * 2;
+        float res[2], nums[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float num = rb(acc[mi][j][hr * 2 + x]);
+          nums[x] = num;
+          const float fine = rb(__fdiv_rn(num, den));
+          const float qv = bf(a.raw_q[base + e + x]);
+          const float loc = bf(a.local[base + e + x]);
+          const bf16* fa = a.fa + ((long long)h * D + e + x) * 3;
+          const bf16* fb = a.fb + ((long long)h * D + e + x) * 3;
+          const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), qv)), bf(fb[0]))), 0.f));
+          const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), qv)), bf(fb[2])));
+          const float mx = fmaxf(s0, s2);
+          const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
+          const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
+          const float lt = rb(__fmul_rn(rho0, rb(__fmul_rn(2.f, loc))));
+          const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(gain, fine))));
+          res[x] = rb(__fadd_rn(rb(__fadd_rn(lt, 0.f)), ft));
+        }
+        *reinterpret_cast<__nv_bfloat162*>(a.out + base + e) = __floats2bfloat162_rn(res[0], res[1]);
+        *reinterpret_cast<__nv_bfloat162*>(a.num_out + base + e) = __floats2bfloat162_rn(nums[0], nums[1]);
+      }
+    }
+  }
+}
+
+}  // namespace tao
