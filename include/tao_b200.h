@@ -197,6 +197,40 @@ int tao_train_forward(const void* q, const void* k, const void* v, const void* r
                       const float* gain, int batch, int tokens, int heads, int width,
                       void* out, const TaoTrainBuffers* buffers, void* stream);
 
+/* Gradient buffers of one backward (caller-allocated):
+ *   dq, dk, dv, d_raw_q, d_raw_k : bf16 [B][T][H][D]; d_raw_k zero-filled by the caller
+ *   d_fusion_a, d_fusion_b       : fp32 [H][D][3], zero-filled (accumulated)
+ *   d_local, gn, d_rq_f          : bf16 [B][T][H][D] scratch
+ *   gd                           : fp32 [B][T][H] scratch
+ *   row_dot                      : fp32 [B][H][T] scratch
+ *   dC, dz                       : fp32 [B][H][S][D][D], [B][H][S][D], zero-filled */
+typedef struct TaoTrainGrads {
+  void* dq;
+  void* dk;
+  void* dv;
+  void* d_raw_q;
+  void* d_raw_k;
+  float* d_fusion_a;
+  float* d_fusion_b;
+  void* d_local;
+  void* gn;
+  void* d_rq_f;
+  float* gd;
+  float* row_dot;
+  float* dC;
+  float* dz;
+} TaoTrainGrads;
+
+/* Backward of tao_train_forward: gradients of q, k, v, raw_q, raw_k and the
+ * fusion parameters for the upstream gradient grad_out [B][T][H][D] bf16.
+ * Reference: autograd of operator._fuse_training, SDPA, _SelectedRead.backward
+ * (selected_read.py:175-187), the writer and page summaries. */
+int tao_train_backward(const void* grad_out, const void* q, const void* k, const void* v,
+                       const void* raw_q, const void* raw_k, const void* fusion_a,
+                       const void* fusion_b, const float* gain, int batch, int tokens, int heads,
+                       int width, const void* out, const TaoTrainBuffers* saved,
+                       const TaoTrainGrads* grads, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,7 +4,7 @@
 #include <cstdio>
 
 #include "../../include/tao_b200.h"
-#include "train_kernels.cuh"
+#include "train_backward.cuh"
 
 void tao_set_last_error(const char* msg);
 
@@ -115,9 +115,67 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
   return TAO_OK;
 }
 
+template <int D>
+int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
+  using namespace tao;
+  BwdArgs a = a0;
+  const Geometry g = geometry(a.dm.T);
+  const int B = a.dm.B, H = a.dm.H, T = a.dm.T;
+  fusion_bwd_kernel<D><<<dim3(g.tiles, B * H), 256, 0, s>>>(a);
+  const size_t asmem = (size_t)(2 * 64 + 4 * 64) * D * 2 + 256 * 4;
+  if (!tsmem(attn_bwd_kv_kernel<D>, asmem) || !tsmem(attn_bwd_q_kernel<D>, asmem))
+    return tfail(TAO_ERR_CUDA, "smem attribute");
+  attn_bwd_kv_kernel<D><<<dim3((T + 63) / 64, B * H), 128, asmem, s>>>(a);
+  attn_bwd_q_kernel<D><<<dim3((T + 63) / 64, B * H), 128, asmem, s>>>(a);
+  const size_t rsmem = ReadBwdSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
+  if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the read backward kernel");
+  if (!tsmem(read_bwd_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+  read_bwd_kernel<D><<<dim3(g.tiles, B * H), 256, rsmem, s>>>(a);
+  if (g.S > 0) {
+    const size_t wsmem = (size_t)2 * 256 * D * 2 + (size_t)D * D * 2 + 6 * D * 4;
+    if (!tsmem(writer_bwd_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+    writer_bwd_kernel<D><<<B * H * g.S, 256, wsmem, s>>>(a);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return tfail(TAO_ERR_CUDA, cudaGetErrorString(e));
+  return TAO_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int tao_train_backward(const void* grad_out, const void* q, const void* k, const void* v,
+                       const void* raw_q, const void* raw_k, const void* fusion_a,
+                       const void* fusion_b, const float* gain, int batch, int tokens, int heads,
+                       int width, const void* out, const TaoTrainBuffers* saved,
+                       const TaoTrainGrads* grads, void* stream) {
+  (void)out;
+  if (!grad_out || !q || !k || !v || !raw_q || !raw_k || !fusion_a || !fusion_b || !gain || !saved || !grads)
+    return tfail(TAO_ERR_ARG, "null pointer");
+  if (width != 64 && width != 128) return tfail(TAO_ERR_ARG, "head width must be 64 or 128");
+  if (batch <= 0 || tokens <= 0 || heads <= 0) return tfail(TAO_ERR_ARG, "bad shape");
+  const Geometry g = geometry(tokens);
+  if (saved->mmax != g.mmax) return tfail(TAO_ERR_ARG, "saved.mmax does not match tao_train_geometry");
+  using tao::bf16;
+  tao::BwdArgs a{};
+  auto C = [](const void* p) { return static_cast<const bf16*>(p); };
+  auto W = [](void* p) { return static_cast<bf16*>(p); };
+  a.g = C(grad_out); a.raw_q = C(raw_q); a.local = C(saved->local); a.num = C(saved->num);
+  a.fa = C(fusion_a); a.fb = C(fusion_b); a.q = C(q); a.k = C(k); a.v = C(v); a.raw_k = C(raw_k);
+  a.den = saved->den; a.gain = gain; a.lse = saved->lse;
+  a.z = C(saved->fine_z); a.C = C(saved->fine_c); a.pzpre = C(saved->page_prefix); a.sel = saved->sel;
+  a.d_local = W(grads->d_local); a.gn = W(grads->gn); a.d_rq_f = W(grads->d_rq_f);
+  a.gd = grads->gd; a.dv_row = grads->row_dot; a.d_fa = grads->d_fusion_a; a.d_fb = grads->d_fusion_b;
+  a.dq = W(grads->dq); a.dk = W(grads->dk); a.dv = W(grads->dv); a.d_raw_q = W(grads->d_raw_q);
+  a.d_raw_k = W(grads->d_raw_k); a.dC = grads->dC; a.dz = grads->dz;
+  a.dm = tao::TrainDims{batch, tokens, heads, g.S, (long long)heads * width};
+  a.pages = g.pages;
+  a.mmax = g.mmax;
+  a.err = saved->err;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return width == 64 ? train_backward<64>(a, s) : train_backward<128>(a, s);
+}
 
 int tao_train_geometry(int tokens, int* sealed, int* pages, int* mmax) {
   if (tokens <= 0) return tfail(TAO_ERR_ARG, "tokens must be positive");

@@ -1,0 +1,983 @@
+// Training backward kernels of tao_attention on sm_100a.
+//
+// Reference: the torch autograd of operator._fuse_training (operator.py:21-39),
+// of the SDPA local attention (flash_attention.py:16-37 via tao_stream.py:760-787),
+// _SelectedRead.backward (selected_read.py:175-187) and of the writer and page
+// summaries (tao_stream.py:80-123, 530-593).  Rounding points follow those ops.
+#pragma once
+#include "common.cuh"
+#include "window_attention.cuh"
+#include "train_kernels.cuh"
+
+namespace tao {
+
+struct BwdArgs {
+  const bf16 *g, *raw_q, *local, *num, *fa, *fb, *q, *k, *v, *raw_k;
+  const float *den, *gain, *lse;
+  const bf16 *z, *C, *pzpre;
+  const int16_t* sel;
+  bf16 *d_local, *gn, *d_rq_f;   // [B,T,H,D]
+  float *gd, *dv_row;            // [B,T,H], [B,H,T] (row dot of dO and O for attention)
+  float *d_fa, *d_fb;            // fp32 [H,D,3] accumulators
+  bf16 *dq, *dk, *dv, *d_raw_q, *d_raw_k;
+  float *dC, *dz;                // fp32 [B,H,S,D,D], [B,H,S,D] accumulators
+  TrainDims dm;
+  int pages, mmax;
+  int* err;
+};
+
+// ---------------------------------------------------------------------------
+// Fusion backward: one warp per (token, head) row, lanes over channels.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
+  constexpr int PER = D / 32;
+  const int tile = blockIdx.x, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float gain = a.gain[h];
+  float acc_fa[PER][3], acc_fb[PER][3];
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+#pragma unroll
+    for (int x = 0; x < 3; ++x) acc_fa[j][x] = acc_fb[j][x] = 0.f;
+  float fa[PER][3], fb[PER][3];
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+#pragma unroll
+    for (int x = 0; x < 3; ++x) {
+      fa[j][x] = bf(a.fa[((long long)h * D + lane + 32 * j) * 3 + x]);
+      fb[j][x] = bf(a.fb[((long long)h * D + lane + 32 * j) * 3 + x]);
+    }
+  for (int rr = 0; rr < 32; ++rr) {
+    const int t = tile * 256 + warp * 32 + rr;
+    if (t >= a.dm.T) break;
+    const long long base = ((long long)b * a.dm.T + t) * a.dm.row + (long long)h * D;
+    const bool present = t >= kWindow;
+    const float den = present ? a.den[((long long)b * a.dm.T + t) * a.dm.H + h] : 1.f;
+    float rowdot = 0.f, dden = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int d = lane + 32 * j;
+      const float gv = bf(a.g[base + d]);
+      const float loc = bf(a.local[base + d]);
+      float dloc = gv, dnum = 0.f, drq = 0.f;
+      if (present) {
+        const float qv = bf(a.raw_q[base + d]);
+        const float num = bf(a.num[base + d]);
+        const float fine = rb(__fdiv_rn(num, den));
+        const float base0 = rb(__fadd_rn(rb(__fmul_rn(fa[j][0], qv)), fb[j][0]));
+        const float s0 = rb(__fadd_rn(base0, 0.f));
+        const float s2 = rb(__fadd_rn(rb(__fmul_rn(fa[j][2], qv)), fb[j][2]));
+        const float mx = fmaxf(s0, s2);
+        const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
+        const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
+        const float l2 = rb(__fmul_rn(2.f, loc)), fg = rb(__fmul_rn(gain, fine));
+        const float drho0 = rb(__fmul_rn(gv, l2)), drho2 = rb(__fmul_rn(gv, fg));
+        dloc = rb(__fmul_rn(2.f, rb(__fmul_rn(gv, rho0))));
+        const float dfine = rb(__fmul_rn(rb(__fmul_rn(gv, rho2)), gain));
+        const float dot = drho0 * rho0 + drho2 * rho2;
+        const float ds0 = rb(rho0 * (drho0 - dot)), ds2 = rb(rho2 * (drho2 - dot));
+        acc_fb[j][0] += ds0;
+        acc_fb[j][2] += ds2;
+        acc_fa[j][0] += rb(__fmul_rn(ds0, qv));
+        acc_fa[j][2] += rb(__fmul_rn(ds2, qv));
+        drq = rb(rb(__fmul_rn(ds0, fa[j][0])) + rb(__fmul_rn(ds2, fa[j][2])));
+        dnum = rb(__fdiv_rn(dfine, den));
+        const float t2 = rb(__fdiv_rn(fine, den));
+        dden += rb(-__fmul_rn(dfine, t2));
+      }
+      a.d_local[base + d] = tobf(dloc);
+      a.gn[base + d] = tobf(dnum);
+      a.d_rq_f[base + d] = tobf(drq);
+      rowdot += dloc * loc;
+    }
+    rowdot = warp_sum(rowdot);
+    dden = warp_sum(dden);
+    if (lane == 0) {
+      a.gd[((long long)b * a.dm.T + t) * a.dm.H + h] = rb(dden);
+      a.dv_row[((long long)b * a.dm.H + h) * a.dm.T + t] = rowdot;
+    }
+  }
+  // block reduction of the fusion parameter gradients, one atomic per value per CTA
+  __shared__ float red[8][D][6];
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+#pragma unroll
+    for (int x = 0; x < 3; ++x) {
+      red[warp][lane + 32 * j][x] = acc_fa[j][x];
+      red[warp][lane + 32 * j][3 + x] = acc_fb[j][x];
+    }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < D * 6; idx += 256) {
+    const int d = idx / 6, x = idx % 6;
+    float s = 0.f;
+    for (int w = 0; w < 8; ++w) s += red[w][d][x];
+    if (s != 0.f) {
+      float* dst = (x < 3) ? a.d_fa : a.d_fb;
+      atomicAdd(dst + ((long long)h * D + d) * 3 + (x % 3), s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Windowed attention backward.  Query t sees keys [ws(t), t], ws(t) =
+// max(0, 256*floor(t/256) - 512).  P = exp(s*scale - lse[t]); dS = P (dP - rowdot).
+// ---------------------------------------------------------------------------
+TAO_DEVI long long win_lo(long long t) {
+  long long s = (t / kFine) * kFine - kKeep;
+  return s < 0 ? 0 : s;
+}
+
+// dK, dV: one CTA per (64-key block, b, h); warps own 16 keys; loop over the
+// query blocks that can see the keys.
+template <int D>
+__global__ void __launch_bounds__(128) attn_bwd_kv_kernel(BwdArgs a) {
+  using namespace wa;
+  constexpr int BN = 64, CH = D / 8;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sK = smem_u32(smem), sV = sK + BN * D * 2;
+  const uint32_t sQ = sV + BN * D * 2, sO = sQ + 2 * 64 * D * 2;  // double-buffered Q, dO
+  float* lseS = reinterpret_cast<float*>(smem + 2 * BN * D * 2 + 4 * 64 * D * 2);  // [2][64]
+  float* rdS = lseS + 128;                                                          // [2][64]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  const long long k0 = (long long)blockIdx.x * BN;
+  const int T = a.dm.T;
+  const long long row = a.dm.row;
+  const bf16* qb = a.q + (long long)b * T * row + (long long)h * D;
+  const bf16* kb = a.k + (long long)b * T * row + (long long)h * D;
+  const bf16* vb = a.v + (long long)b * T * row + (long long)h * D;
+  const bf16* ob = a.d_local + (long long)b * T * row + (long long)h * D;
+  const float* lse = a.lse + ((long long)b * a.dm.H + h) * T;
+  const float* rd = a.dv_row + ((long long)b * a.dm.H + h) * T;
+  for (int idx = tid; idx < BN * CH; idx += 128) {
+    const int r = idx / CH, c = idx % CH;
+    const bool ok = k0 + r < T;
+    const long long off = (ok ? k0 + r : k0) * row + c * 8;
+    cp_async16(sK + swz(r, c * 8, D), kb + off, ok);
+    cp_async16(sV + swz(r, c * 8, D), vb + off, ok);
+  }
+  long long qend = (k0 / kFine + 3) * kFine;
+  if (qend > T) qend = T;
+  const int nqb = (int)((qend - k0 + 63) / 64);
+  auto load_q = [&](int qb_i, int buf) {
+    const long long q0 = k0 + (long long)qb_i * 64;
+    for (int idx = tid; idx < 64 * CH; idx += 128) {
+      const int r = idx / CH, c = idx % CH;
+      const bool ok = q0 + r < T;
+      const long long off = (ok ? q0 + r : q0) * row + c * 8;
+      cp_async16(sQ + buf * 64 * D * 2 + swz(r, c * 8, D), qb + off, ok);
+      cp_async16(sO + buf * 64 * D * 2 + swz(r, c * 8, D), ob + off, ok);
+    }
+    for (int r = tid; r < 64; r += 128) {
+      const bool ok = q0 + r < T;
+      lseS[buf * 64 + r] = ok ? lse[q0 + r] * 1.4426950408889634f : 0.f;
+      rdS[buf * 64 + r] = ok ? rd[q0 + r] : 0.f;
+    }
+  };
+  load_q(0, 0);
+  cp_commit();
+  const float scale = 1.f / sqrtf((float)D), sl = 1.4426950408889634f * scale;
+  const int g = lane >> 2, c4 = lane & 3;
+  float dk[D / 8][4], dvv[D / 8][4];
+#pragma unroll
+  for (int j = 0; j < D / 8; ++j)
+#pragma unroll
+    for (int x = 0; x < 4; ++x) dk[j][x] = dvv[j][x] = 0.f;
+  uint32_t kf[D / 16][4], vf[D / 16][4];
+  for (int qi = 0; qi < nqb; ++qi) {
+    const int buf = qi & 1;
+    if (qi + 1 < nqb) {
+      load_q(qi + 1, buf ^ 1);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    if (qi == 0) {
+#pragma unroll
+      for (int kt = 0; kt < D / 16; ++kt) {
+        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kt * 16 + (lane >> 4) * 8;
+        ldsm_x4(sK + swz(r, c, D), kf[kt][0], kf[kt][1], kf[kt][2], kf[kt][3]);
+        ldsm_x4(sV + swz(r, c, D), vf[kt][0], vf[kt][1], vf[kt][2], vf[kt][3]);
+      }
+    }
+    const long long q0 = k0 + (long long)qi * 64;
+    const uint32_t qbuf = sQ + buf * 64 * D * 2, obuf = sO + buf * 64 * D * 2;
+    float st[8][4], dp[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) st[j][x] = dp[j][x] = 0.f;
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+#pragma unroll
+      for (int kt = 0; kt < D / 16; ++kt) {
+        uint32_t b0, b1, b2, b3;
+        const int r = np * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kt * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(qbuf + swz(r, c, D), b0, b1, b2, b3);
+        mma16816(st[2 * np], kf[kt], b0, b1);
+        mma16816(st[2 * np + 1], kf[kt], b2, b3);
+        ldsm_x4(obuf + swz(r, c, D), b0, b1, b2, b3);
+        mma16816(dp[2 * np], vf[kt], b0, b1);
+        mma16816(dp[2 * np + 1], vf[kt], b2, b3);
+      }
+    }
+    // P^T and dS^T (rows: keys, cols: queries)
+    uint32_t pa[4][4], da[4][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float pv[4], dsv[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const long long kp = k0 + warp * 16 + g + (x >> 1) * 8;
+        const int ql = j * 8 + c4 * 2 + (x & 1);
+        const long long qp = q0 + ql;
+        const bool ok = qp < T && kp <= qp && kp >= win_lo(qp) && kp < T;
+        const float p = ok ? exp2f(st[j][x] * sl - lseS[buf * 64 + ql]) : 0.f;
+        pv[x] = p;
+        dsv[x] = p * (dp[j][x] - rdS[buf * 64 + ql]);
+      }
+      const int kt = j >> 1;
+      if ((j & 1) == 0) {
+        pa[kt][0] = pack_bf16(pv[0], pv[1]);
+        pa[kt][1] = pack_bf16(pv[2], pv[3]);
+        da[kt][0] = pack_bf16(dsv[0], dsv[1]);
+        da[kt][1] = pack_bf16(dsv[2], dsv[3]);
+      } else {
+        pa[kt][2] = pack_bf16(pv[0], pv[1]);
+        pa[kt][3] = pack_bf16(pv[2], pv[3]);
+        da[kt][2] = pack_bf16(dsv[0], dsv[1]);
+        da[kt][3] = pack_bf16(dsv[2], dsv[3]);
+      }
+    }
+    // dV += P^T dO ; dK += dS^T Q   (B operands from [query][d] tiles, transposed loads)
+#pragma unroll
+    for (int kt = 0; kt < 4; ++kt) {
+#pragma unroll
+      for (int dpi = 0; dpi < D / 16; ++dpi) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = dpi * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(obuf + swz(r, c, D), b0, b1, b2, b3);
+        mma16816(dvv[2 * dpi], pa[kt], b0, b1);
+        mma16816(dvv[2 * dpi + 1], pa[kt], b2, b3);
+        ldsm_x4_t(qbuf + swz(r, c, D), b0, b1, b2, b3);
+        mma16816(dk[2 * dpi], da[kt], b0, b1);
+        mma16816(dk[2 * dpi + 1], da[kt], b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  bf16* dkb = a.dk + (long long)b * T * row + (long long)h * D;
+  bf16* dvb = a.dv + (long long)b * T * row + (long long)h * D;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const long long kp = k0 + warp * 16 + g + hr * 8;
+    if (kp >= T) continue;
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) {
+      const int e = j * 8 + c4 * 2;
+      *reinterpret_cast<__nv_bfloat162*>(dkb + kp * row + e) =
+          __floats2bfloat162_rn(dk[j][hr * 2] * scale, dk[j][hr * 2 + 1] * scale);
+      *reinterpret_cast<__nv_bfloat162*>(dvb + kp * row + e) =
+          __floats2bfloat162_rn(dvv[j][hr * 2], dvv[j][hr * 2 + 1]);
+    }
+  }
+}
+
+// dQ: one CTA per (64-query block, b, h); loop over the key blocks in the window.
+template <int D>
+__global__ void __launch_bounds__(128) attn_bwd_q_kernel(BwdArgs a) {
+  using namespace wa;
+  constexpr int BN = 64, CH = D / 8;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sQ = smem_u32(smem), sO = sQ + 64 * D * 2;
+  const uint32_t sK = sO + 64 * D * 2, sV = sK + 2 * BN * D * 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  const int T = a.dm.T;
+  const long long row = a.dm.row;
+  const long long q0 = (long long)blockIdx.x * 64;
+  const int nq = (int)min(64LL, T - q0);
+  const bf16* qb = a.q + (long long)b * T * row + (long long)h * D;
+  const bf16* kb = a.k + (long long)b * T * row + (long long)h * D;
+  const bf16* vb = a.v + (long long)b * T * row + (long long)h * D;
+  const bf16* ob = a.d_local + (long long)b * T * row + (long long)h * D;
+  const float* lse = a.lse + ((long long)b * a.dm.H + h) * T;
+  const float* rd = a.dv_row + ((long long)b * a.dm.H + h) * T;
+  for (int idx = tid; idx < 64 * CH; idx += 128) {
+    const int r = idx / CH, c = idx % CH;
+    const bool ok = r < nq;
+    const long long off = (q0 + (ok ? r : 0)) * row + c * 8;
+    cp_async16(sQ + swz(r, c * 8, D), qb + off, ok);
+    cp_async16(sO + swz(r, c * 8, D), ob + off, ok);
+  }
+  const long long kstart = win_lo(q0), kend = q0 + nq;
+  auto load_kv = [&](long long kk, int buf) {
+    for (int idx = tid; idx < BN * CH; idx += 128) {
+      const int r = idx / CH, c = idx % CH;
+      const bool ok = kk + r < kend;
+      const long long off = (ok ? kk + r : kk) * row + c * 8;
+      cp_async16(sK + buf * BN * D * 2 + swz(r, c * 8, D), kb + off, ok);
+      cp_async16(sV + buf * BN * D * 2 + swz(r, c * 8, D), vb + off, ok);
+    }
+  };
+  load_kv(kstart, 0);
+  cp_commit();
+  const int g = lane >> 2, c4 = lane & 3;
+  const float scale = 1.f / sqrtf((float)D), sl = 1.4426950408889634f * scale;
+  float lrow[2], rrow[2];
+  long long qrow[2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int r = warp * 16 + g + hr * 8;
+    qrow[hr] = q0 + r;
+    lrow[hr] = r < nq ? lse[q0 + r] * 1.4426950408889634f : 0.f;
+    rrow[hr] = r < nq ? rd[q0 + r] : 0.f;
+  }
+  float dq[D / 8][4];
+#pragma unroll
+  for (int j = 0; j < D / 8; ++j) dq[j][0] = dq[j][1] = dq[j][2] = dq[j][3] = 0.f;
+  uint32_t qf[D / 16][4], of[D / 16][4];
+  const int nblk = (int)((kend - kstart + BN - 1) / BN);
+  for (int blk = 0; blk < nblk; ++blk) {
+    const long long kk = kstart + (long long)blk * BN;
+    if (blk + 1 < nblk) {
+      load_kv(kk + BN, (blk + 1) & 1);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    if (blk == 0) {
+#pragma unroll
+      for (int kt = 0; kt < D / 16; ++kt) {
+        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kt * 16 + (lane >> 4) * 8;
+        ldsm_x4(sQ + swz(r, c, D), qf[kt][0], qf[kt][1], qf[kt][2], qf[kt][3]);
+        ldsm_x4(sO + swz(r, c, D), of[kt][0], of[kt][1], of[kt][2], of[kt][3]);
+      }
+    }
+    const uint32_t kbuf = sK + (blk & 1) * BN * D * 2, vbuf = sV + (blk & 1) * BN * D * 2;
+    float s[8][4], dp[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) s[j][x] = dp[j][x] = 0.f;
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+#pragma unroll
+      for (int kt = 0; kt < D / 16; ++kt) {
+        uint32_t b0, b1, b2, b3;
+        const int r = np * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kt * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(kbuf + swz(r, c, D), b0, b1, b2, b3);
+        mma16816(s[2 * np], qf[kt], b0, b1);
+        mma16816(s[2 * np + 1], qf[kt], b2, b3);
+        ldsm_x4(vbuf + swz(r, c, D), b0, b1, b2, b3);
+        mma16816(dp[2 * np], of[kt], b0, b1);
+        mma16816(dp[2 * np + 1], of[kt], b2, b3);
+      }
+    }
+    uint32_t da[4][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float dsv[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const int hr = x >> 1;
+        const long long kp = kk + j * 8 + c4 * 2 + (x & 1);
+        const bool ok = kp < kend && kp <= qrow[hr] && qrow[hr] < T;
+        const float p = ok ? exp2f(s[j][x] * sl - lrow[hr]) : 0.f;
+        dsv[x] = p * (dp[j][x] - rrow[hr]);
+      }
+      const int kt = j >> 1;
+      if ((j & 1) == 0) {
+        da[kt][0] = pack_bf16(dsv[0], dsv[1]);
+        da[kt][1] = pack_bf16(dsv[2], dsv[3]);
+      } else {
+        da[kt][2] = pack_bf16(dsv[0], dsv[1]);
+        da[kt][3] = pack_bf16(dsv[2], dsv[3]);
+      }
+    }
+#pragma unroll
+    for (int kt = 0; kt < 4; ++kt) {
+#pragma unroll
+      for (int dpi = 0; dpi < D / 16; ++dpi) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = dpi * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(kbuf + swz(r, c, D), b0, b1, b2, b3);
+        mma16816(dq[2 * dpi], da[kt], b0, b1);
+        mma16816(dq[2 * dpi + 1], da[kt], b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  bf16* dqb = a.dq + (long long)b * T * row + (long long)h * D;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int r = warp * 16 + g + hr * 8;
+    if (r >= nq) continue;
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) {
+      const int e = j * 8 + c4 * 2;
+      *reinterpret_cast<__nv_bfloat162*>(dqb + (q0 + r) * row + e) =
+          __floats2bfloat162_rn(dq[j][hr * 2] * scale, dq[j][hr * 2 + 1] * scale);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Selected-read backward: one CTA (256 threads) per (tile, b, h).  Fines are
+// visited page by page; for fine s and the queries that selected it:
+//   dA   = bf16(bf16(gn . C_s^T) + gd)                  (tensor cores)
+//   dhv += bf16(dA * w_s)   -> per page: dh += bf16(dhv*pw), dpw += bf16(dhv*h)
+//   dw_s = sum_q bf16(dA * hv)                          -> dz, d page_z via exp
+//   dC_s = A_s^T . gn (bf16 per tile)                   (tensor cores, fp32 atomics)
+// then the softmax backward of h (-> d raw_q) and of the page weights, and the
+// logsumexp backward of the tile's page log-partitions (-> dz).
+// ---------------------------------------------------------------------------
+template <int D>
+struct ReadBwdSmem {
+  static size_t bytes(int P, int V, int mmax) {
+    return 3 * (size_t)256 * D * 2 + (size_t)D * D * 2 + 4 * (size_t)P * D * 4 +
+           ((size_t)V * D * 2 + 15) / 16 * 16 + (size_t)256 * mmax * 2 + 256 * 4 + 256 +
+           (size_t)D * 4 + (size_t)(V + 8) * 4 * 2 + 64;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
+  using namespace wa;
+  const int tile = blockIdx.x, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q0 = tile * 256, nq = min(256, a.dm.T - q0);
+  const int V = max(0, tile - 2);
+  const long long row = a.dm.row, hoff = (long long)h * D;
+  if (V == 0) {
+    for (int idx = tid; idx < nq * (D / 8); idx += 256) {
+      const int q = idx / (D / 8), c = idx % (D / 8);
+      const long long off = ((long long)b * a.dm.T + q0 + q) * row + hoff + c * 8;
+      *reinterpret_cast<uint4*>(a.d_raw_q + off) = *reinterpret_cast<const uint4*>(a.d_rq_f + off);
+    }
+    return;
+  }
+  const int completed = V / kGroup, pending = V % kGroup, P = completed + (pending > 0);
+  const int M = a.mmax;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ptr = smem;
+  const uint32_t sH = smem_u32(ptr);  ptr += 256 * D * 2;
+  const uint32_t sG = smem_u32(ptr);  ptr += 256 * D * 2;
+  const uint32_t sA = smem_u32(ptr);  ptr += 256 * D * 2;
+  const uint32_t sC = smem_u32(ptr);  ptr += D * D * 2;
+  uint8_t* hB = smem;
+  uint8_t* aB = smem + 2 * 256 * D * 2;
+  float* pwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
+  float* pzS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
+  float* dpwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
+  float* dpzS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
+  bf16* swS = reinterpret_cast<bf16*>(ptr);     ptr += ((size_t)V * D * 2 + 15) / 16 * 16;
+  int16_t* selS = reinterpret_cast<int16_t*>(ptr); ptr += (size_t)256 * M * 2;
+  float* gdS = reinterpret_cast<float*>(ptr);   ptr += 256 * 4;
+  uint8_t* selq = ptr;                          ptr += 256;
+  float* dwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)D * 4;
+  int* useS = reinterpret_cast<int*>(ptr);
+  int* list = useS + V;
+
+  // ---- tables (as in the forward)
+  const bf16* pzb = a.pzpre + ((long long)b * a.dm.H + h) * a.pages * kGroup * D;
+  for (int idx = tid; idx < P * D; idx += 256) {
+    const int pg = idx / D, d = idx % D;
+    const int n = (pg < completed) ? kGroup : pending;
+    pzS[idx] = bf(pzb[((long long)pg * kGroup + (n - 1)) * D + d]);
+    dpwS[idx] = 0.f;
+    dpzS[idx] = 0.f;
+  }
+  for (int i = tid; i < V; i += 256) useS[i] = 0;
+  for (int d = tid; d < D; d += 256) dwS[d] = 0.f;
+  __syncthreads();
+  for (int d = tid; d < D; d += 256) {
+    float mx = -INFINITY;
+    for (int pg = 0; pg < P; ++pg) mx = fmaxf(mx, pzS[pg * D + d]);
+    float sum = 0.f;
+    for (int pg = 0; pg < P; ++pg) sum += expf(pzS[pg * D + d] - mx);
+    for (int pg = 0; pg < P; ++pg) pwS[pg * D + d] = rb(__fdiv_rn(expf(pzS[pg * D + d] - mx), sum));
+  }
+  const bf16* zb = a.z + ((long long)b * a.dm.H + h) * a.dm.S * D;
+  for (int idx = tid; idx < V * D; idx += 256) {
+    const int sf = idx / D, d = idx % D;
+    swS[idx] = tobf(expf(rb(__fsub_rn(bf(zb[(long long)sf * D + d]), pzS[(sf / kGroup) * D + d]))));
+  }
+  // ---- per query: h (swizzled), gn (swizzled), gd, selections
+  const int q = tid;
+  const bool live = q < nq;
+  const long long qbase = ((long long)b * a.dm.T + q0 + q) * row + hoff;
+  if (live) {
+    const bf16* rq = a.raw_q + qbase;
+    float mx = -INFINITY;
+    for (int c = 0; c < D / 8; ++c) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
+    }
+    float sum = 0.f;
+    for (int c = 0; c < D / 8; ++c) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      for (int e = 0; e < 8; ++e) sum += expf(f[e] - mx);
+    }
+    for (int c = 0; c < D / 8; ++c) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      __nv_bfloat162 o[4];
+      for (int e = 0; e < 4; ++e)
+        o[e] = __floats2bfloat162_rn(__fdiv_rn(expf(f[2 * e] - mx), sum), __fdiv_rn(expf(f[2 * e + 1] - mx), sum));
+      *reinterpret_cast<uint4*>(hB + swz(q, c * 8, D)) = *reinterpret_cast<uint4*>(o);
+      *reinterpret_cast<uint4*>(hB + 256 * D * 2 + swz(q, c * 8, D)) =
+          *reinterpret_cast<const uint4*>(a.gn + qbase + c * 8);
+    }
+    gdS[q] = a.gd[((long long)b * a.dm.T + q0 + q) * a.dm.H + h];
+    const int16_t* so = a.sel + (((long long)b * a.dm.T + q0 + q) * a.dm.H + h) * a.mmax;
+    for (int m = 0; m < M; ++m) {
+      selS[q * M + m] = so[m];
+      if (so[m] >= 0) useS[so[m]] = 1;
+    }
+  } else {
+    for (int c = 0; c < D / 8; ++c) {
+      *reinterpret_cast<uint4*>(hB + swz(q, c * 8, D)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(hB + 256 * D * 2 + swz(q, c * 8, D)) = make_uint4(0, 0, 0, 0);
+    }
+    gdS[q] = 0.f;
+    for (int m = 0; m < M; ++m) selS[q * M + m] = -1;
+  }
+  __syncthreads();
+  __shared__ int nused;
+  if (tid == 0) {
+    int n = 0;
+    for (int sf = 0; sf < V; ++sf)
+      if (useS[sf]) list[n++] = sf;
+    nused = n;
+  }
+  __syncthreads();
+
+  auto hval = [&](int qq, int d) -> float { return bf(*reinterpret_cast<const bf16*>(hB + swz(qq, d, D))); };
+  constexpr int NTL = D / 8;
+  const int g = lane >> 2, c4 = lane & 3;
+  float dhv[2][NTL][4], dh[2][NTL][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < NTL; ++j)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) dhv[i][j][x] = dh[i][j][x] = 0.f;
+  const bf16* cb = a.C + ((long long)b * a.dm.H + h) * a.dm.S * (long long)D * D;
+  int cur_page = -1;
+  auto flush_page = [&](int pg) {
+    // dh += bf16(bf16(dhv)*pw[pg]) ; dpw[pg] += sum_q bf16(bf16(dhv)*h)
+    float part[NTL][2];
+#pragma unroll
+    for (int j = 0; j < NTL; ++j) part[j][0] = part[j][1] = 0.f;
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int j = 0; j < NTL; ++j)
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const int r = warp * 32 + mi * 16 + g + (x >> 1) * 8;
+          const int d = j * 8 + c4 * 2 + (x & 1);
+          const float v = rb(dhv[mi][j][x]);
+          dh[mi][j][x] += rb(__fmul_rn(v, pwS[pg * D + d]));
+          part[j][x & 1] += rb(__fmul_rn(v, hval(r, d)));
+          dhv[mi][j][x] = 0.f;
+        }
+#pragma unroll
+    for (int j = 0; j < NTL; ++j)
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        float v = part[j][x];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        if (g == 0) atomicAdd(&dpwS[pg * D + j * 8 + c4 * 2 + x], v);
+      }
+  };
+  const int nu = nused;
+  for (int i = 0; i < nu; ++i) {
+    const int sf = list[i], pg = sf / kGroup;
+    if (pg != cur_page) {
+      if (cur_page >= 0) flush_page(cur_page);
+      cur_page = pg;
+    }
+    // load C_s, build A_s and the selection flags
+    for (int idx = tid; idx < D * D / 8; idx += 256) {
+      const int r = idx / (D / 8), c = idx % (D / 8);
+      cp_async16(sC + swz(r, c * 8, D), cb + (long long)sf * D * D + r * D + c * 8, true);
+    }
+    cp_commit();
+    bool sel = false;
+    if (live)
+      for (int m = 0; m < M; ++m) sel |= (selS[q * M + m] == sf);
+    selq[q] = sel;
+    for (int c = 0; c < D / 8; ++c) {
+      __nv_bfloat162 o[4];
+      for (int e = 0; e < 4; ++e) {
+        const int d = c * 8 + 2 * e;
+        float a0 = 0.f, a1 = 0.f;
+        if (sel) {
+          a0 = rb(__fmul_rn(rb(__fmul_rn(hval(q, d), pwS[pg * D + d])), bf(swS[sf * D + d])));
+          a1 = rb(__fmul_rn(rb(__fmul_rn(hval(q, d + 1), pwS[pg * D + d + 1])), bf(swS[sf * D + d + 1])));
+        }
+        o[e] = __floats2bfloat162_rn(a0, a1);
+      }
+      *reinterpret_cast<uint4*>(aB + swz(q, c * 8, D)) = *reinterpret_cast<uint4*>(o);
+    }
+    cp_wait<0>();
+    __syncthreads();
+    // dA = gn . C_s^T  (rows: queries of this warp, cols: d)
+    float da[2][NTL][4];
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) da[mi][j][0] = da[mi][j][1] = da[mi][j][2] = da[mi][j][3] = 0.f;
+#pragma unroll
+    for (int kt = 0; kt < D / 16; ++kt) {
+      uint32_t af[2][4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const int r = warp * 32 + mi * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kt * 16 + (lane >> 4) * 8;
+        ldsm_x4(sG + swz(r, c, D), af[mi][0], af[mi][1], af[mi][2], af[mi][3]);
+      }
+#pragma unroll
+      for (int np = 0; np < D / 16; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int r = np * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kt * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(sC + swz(r, c, D), b0, b1, b2, b3);
+#pragma unroll
+        for (int mi = 0; mi < 2; ++mi) {
+          mma16816(da[mi][2 * np], af[mi], b0, b1);
+          mma16816(da[mi][2 * np + 1], af[mi], b2, b3);
+        }
+      }
+    }
+    float wpart[NTL][2];
+#pragma unroll
+    for (int j = 0; j < NTL; ++j) wpart[j][0] = wpart[j][1] = 0.f;
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const int r = warp * 32 + mi * 16 + g + (x >> 1) * 8;
+        if (!selq[r]) continue;
+        const float gdv = gdS[r];
+#pragma unroll
+        for (int j = 0; j < NTL; ++j) {
+          const int d = j * 8 + c4 * 2 + (x & 1);
+          const float dav = rb(__fadd_rn(rb(da[mi][j][x]), gdv));
+          dhv[mi][j][x] += rb(__fmul_rn(dav, bf(swS[sf * D + d])));
+          const float hv = rb(__fmul_rn(hval(r, d), pwS[pg * D + d]));
+          wpart[j][x & 1] += rb(__fmul_rn(dav, hv));
+        }
+      }
+#pragma unroll
+    for (int j = 0; j < NTL; ++j)
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        float v = wpart[j][x];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        if (g == 0 && v != 0.f) atomicAdd(&dwS[j * 8 + c4 * 2 + x], v);
+      }
+    // dC_s = A_s^T . gn : output [d][e]; warp -> (m-tile of d rows, n range)
+    {
+      constexpr int MTILES = D / 16;                  // 4 or 8
+      constexpr int WPM = 8 / MTILES;                 // warps per m-tile: 2 or 1
+      constexpr int NPW = (D / 8) / WPM;              // n-tiles per warp: 4 or 16
+      const int mt = warp / WPM, n0 = (warp % WPM) * NPW;
+      float dc[NPW][4];
+#pragma unroll
+      for (int j = 0; j < NPW; ++j) dc[j][0] = dc[j][1] = dc[j][2] = dc[j][3] = 0.f;
+      for (int kt = 0; kt < 16; ++kt) {  // 256 queries
+        uint32_t af[4];
+        const int r = kt * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+        const int c = mt * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4_t(sA + swz(r, c, D), af[0], af[1], af[2], af[3]);
+#pragma unroll
+        for (int np = 0; np < NPW / 2; ++np) {
+          uint32_t b0, b1, b2, b3;
+          const int rr = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int cc = (n0 + 2 * np) * 8 + (lane >> 4) * 8;
+          ldsm_x4_t(sG + swz(rr, cc, D), b0, b1, b2, b3);
+          mma16816(dc[2 * np], af, b0, b1);
+          mma16816(dc[2 * np + 1], af, b2, b3);
+        }
+      }
+      float* dcb = a.dC + (((long long)b * a.dm.H + h) * a.dm.S + sf) * (long long)D * D;
+#pragma unroll
+      for (int j = 0; j < NPW; ++j) {
+        const int e = (n0 + j) * 8 + c4 * 2;
+        const int d0 = mt * 16 + g;
+        atomicAdd(reinterpret_cast<float2*>(dcb + (long long)d0 * D + e),
+                  make_float2(rb(dc[j][0]), rb(dc[j][1])));
+        atomicAdd(reinterpret_cast<float2*>(dcb + (long long)(d0 + 8) * D + e),
+                  make_float2(rb(dc[j][2]), rb(dc[j][3])));
+      }
+    }
+    __syncthreads();
+    // dw_s -> d(z - pz) = bf16(bf16(dw) * w) : dz[s] += ., d page_z[pg] -= .
+    for (int d = tid; d < D; d += 256) {
+      const float ddiff = rb(__fmul_rn(rb(dwS[d]), bf(swS[sf * D + d])));
+      atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d, ddiff);
+      dpzS[pg * D + d] -= ddiff;
+      dwS[d] = 0.f;
+    }
+    __syncthreads();
+  }
+  if (cur_page >= 0) flush_page(cur_page);
+  __syncthreads();
+  // ---- softmax backward of h -> d raw_q = bf16(fusion part + this part)
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = warp * 32 + mi * 16 + g + hr * 8;
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < NTL; ++j)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) dot += hval(r, j * 8 + c4 * 2 + x) * rb(dh[mi][j][hr * 2 + x]);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      if (r >= nq) continue;
+      const long long base = ((long long)b * a.dm.T + q0 + r) * row + hoff;
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) {
+        const int d = j * 8 + c4 * 2;
+        float o2[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float hv = hval(r, d + x);
+          const float drq = rb(hv * (rb(dh[mi][j][hr * 2 + x]) - dot));
+          o2[x] = rb(__fadd_rn(bf(a.d_rq_f[base + d + x]), drq));
+        }
+        *reinterpret_cast<__nv_bfloat162*>(a.d_raw_q + base + d) = __floats2bfloat162_rn(o2[0], o2[1]);
+      }
+    }
+  // ---- page weights softmax backward, then logsumexp backward of page_z -> dz
+  for (int d = tid; d < D; d += 256) {
+    float dot = 0.f;
+    for (int pg = 0; pg < P; ++pg) dot += pwS[pg * D + d] * rb(dpwS[pg * D + d]);
+    for (int pg = 0; pg < P; ++pg)
+      dpzS[pg * D + d] += rb(pwS[pg * D + d] * (rb(dpwS[pg * D + d]) - dot));
+  }
+  __syncthreads();
+  for (int idx = tid; idx < V * D; idx += 256) {
+    const int sf = idx / D, d = idx % D, pg = sf / kGroup;
+    const float lse = pzS[pg * D + d];
+    const float w = rb(expf(rb(__fsub_rn(bf(zb[(long long)sf * D + d]), lse))));
+    atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d,
+              rb(__fmul_rn(rb(dpzS[pg * D + d]), w)));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Writer backward: one CTA (256 threads) per (b, h, block s).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
+  using namespace wa;
+  constexpr int NT = 256, CH = D / 8, NTL = D / 8;
+  const int s = blockIdx.x % a.dm.S, h = (blockIdx.x / a.dm.S) % a.dm.H, b = blockIdx.x / (a.dm.S * a.dm.H);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sK = smem_u32(smem), sV = sK + NT * D * 2, sD = sV + NT * D * 2;
+  uint8_t* kB = smem;
+  uint8_t* dB = smem + 2 * NT * D * 2;
+  float* mx = reinterpret_cast<float*>(smem + 2 * NT * D * 2 + D * D * 2);
+  float* zp = mx + D;
+  float* dzS = zp + D;
+  float* dZp = dzS + D;   // sum_t of the partition term from prob
+  float* dmS = dZp + D;   // sum_t d_x
+  float* dZ = dmS + D;
+  const long long row = a.dm.row;
+  const long long tok0 = (long long)b * a.dm.T + (long long)s * NT;
+  const bf16* kb = a.raw_k + tok0 * row + (long long)h * D;
+  const bf16* vb = a.v + tok0 * row + (long long)h * D;
+  const float* dcb = a.dC + (((long long)b * a.dm.H + h) * a.dm.S + s) * (long long)D * D;
+  for (int idx = tid; idx < NT * CH; idx += 256) {
+    const int r = idx / CH, c = idx % CH;
+    cp_async16(sK + swz(r, c * 8, D), kb + (long long)r * row + c * 8, true);
+    cp_async16(sV + swz(r, c * 8, D), vb + (long long)r * row + c * 8, true);
+  }
+  cp_commit();
+  for (int idx = tid; idx < D * D; idx += 256) {
+    const int r = idx / D, c = idx % D;
+    *reinterpret_cast<bf16*>(dB + swz(r, c, D)) = tobf(dcb[idx]);
+  }
+  for (int d = tid; d < D; d += 256) {
+    dzS[d] = rb(a.dz[(((long long)b * a.dm.H + h) * a.dm.S + s) * D + d]);
+    dZp[d] = 0.f;
+    dmS[d] = 0.f;
+  }
+  cp_wait<0>();
+  __syncthreads();
+  auto kat = [&](int t, int d) -> float { return bf(*reinterpret_cast<const bf16*>(kB + swz(t, d, D))); };
+  for (int d = tid; d < D; d += 256) {
+    float m = -INFINITY;
+    for (int t = 0; t < NT; ++t) m = fmaxf(m, kat(t, d));
+    float sum = 0.f;
+    for (int t = 0; t < NT; ++t) sum += rb(expf(rb(__fsub_rn(kat(t, d), m))));
+    mx[d] = m;
+    zp[d] = rb(sum);
+  }
+  __syncthreads();
+  // probability p[t][d] = bf16(e / Z), recomputed from the staged raw keys
+  auto pval = [&](int t, int d) -> float {
+    return rb(__fdiv_rn(rb(expf(rb(__fsub_rn(kat(t, d), mx[d])))), zp[d]));
+  };
+  const int g = lane >> 2, c4 = lane & 3;
+  // dprob = V . dC^T and dv_w = P . dC  (rows: tokens of this warp)
+  float dp[2][NTL][4], dvw[2][NTL][4];
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int j = 0; j < NTL; ++j)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) dp[mi][j][x] = dvw[mi][j][x] = 0.f;
+#pragma unroll
+  for (int kt = 0; kt < D / 16; ++kt) {
+    uint32_t av[2][4], ap[2][4];
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi) {
+      const int r = warp * 32 + mi * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int c = kt * 16 + (lane >> 4) * 8;
+      ldsm_x4(sV + swz(r, c, D), av[mi][0], av[mi][1], av[mi][2], av[mi][3]);
+      const int t0 = warp * 32 + mi * 16 + g, d0 = kt * 16 + c4 * 2;
+      ap[mi][0] = pack_bf16(pval(t0, d0), pval(t0, d0 + 1));
+      ap[mi][1] = pack_bf16(pval(t0 + 8, d0), pval(t0 + 8, d0 + 1));
+      ap[mi][2] = pack_bf16(pval(t0, d0 + 8), pval(t0, d0 + 9));
+      ap[mi][3] = pack_bf16(pval(t0 + 8, d0 + 8), pval(t0 + 8, d0 + 9));
+    }
+#pragma unroll
+    for (int np = 0; np < D / 16; ++np) {
+      uint32_t b0, b1, b2, b3;
+      {  // B = dC^T (k = e, n = d): rows of dC, non-transposed
+        const int r = np * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kt * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(sD + swz(r, c, D), b0, b1, b2, b3);
+#pragma unroll
+        for (int mi = 0; mi < 2; ++mi) {
+          mma16816(dp[mi][2 * np], av[mi], b0, b1);
+          mma16816(dp[mi][2 * np + 1], av[mi], b2, b3);
+        }
+      }
+      {  // B = dC (k = d, n = e): transposed loads
+        const int r = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = np * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(sD + swz(r, c, D), b0, b1, b2, b3);
+#pragma unroll
+        for (int mi = 0; mi < 2; ++mi) {
+          mma16816(dvw[mi][2 * np], ap[mi], b0, b1);
+          mma16816(dvw[mi][2 * np + 1], ap[mi], b2, b3);
+        }
+      }
+    }
+  }
+  bf16* dvb = a.dv + tok0 * row + (long long)h * D;
+  // dv += dv_w ; partition term of the probability gradient
+  float zpart[NTL][2];
+#pragma unroll
+  for (int j = 0; j < NTL; ++j) zpart[j][0] = zpart[j][1] = 0.f;
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int t = warp * 32 + mi * 16 + g + hr * 8;
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) {
+        const int d = j * 8 + c4 * 2;
+        __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(dvb + (long long)t * row + d);
+        const float2 old = __bfloat1622float2(*dst);
+        *dst = __floats2bfloat162_rn(rb(old.x + rb(dvw[mi][j][hr * 2])), rb(old.y + rb(dvw[mi][j][hr * 2 + 1])));
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float pr = pval(t, d + x);
+          zpart[j][x] += rb(-__fmul_rn(rb(dp[mi][j][hr * 2 + x]), rb(__fdiv_rn(pr, zp[d + x]))));
+        }
+      }
+    }
+#pragma unroll
+  for (int j = 0; j < NTL; ++j)
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      float v = zpart[j][x];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (g == 0) atomicAdd(&dZp[j * 8 + c4 * 2 + x], v);
+    }
+  __syncthreads();
+  for (int d = tid; d < D; d += 256) {
+    const float dlog = rb(__fdiv_rn(dzS[d], zp[d]));   // z = max + log(partition)
+    dZ[d] = rb(rb(dZp[d]) + dlog);
+  }
+  __syncthreads();
+  // d_e = bf16(bf16(dprob / Z) + dZ) ; d_x = bf16(d_e * e) -> d raw_k ; sum_t d_x
+  bf16* dkb = a.d_raw_k + tok0 * row + (long long)h * D;
+  float mpart[NTL][2];
+#pragma unroll
+  for (int j = 0; j < NTL; ++j) mpart[j][0] = mpart[j][1] = 0.f;
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int t = warp * 32 + mi * 16 + g + hr * 8;
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) {
+        const int d = j * 8 + c4 * 2;
+        float o2[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float e = rb(expf(rb(__fsub_rn(kat(t, d + x), mx[d + x]))));
+          const float de = rb(__fadd_rn(rb(__fdiv_rn(rb(dp[mi][j][hr * 2 + x]), zp[d + x])), dZ[d + x]));
+          const float dx = rb(__fmul_rn(de, e));
+          o2[x] = dx;
+          mpart[j][x] += dx;
+        }
+        *reinterpret_cast<__nv_bfloat162*>(dkb + (long long)t * row + d) = __floats2bfloat162_rn(o2[0], o2[1]);
+      }
+    }
+#pragma unroll
+  for (int j = 0; j < NTL; ++j)
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      float v = mpart[j][x];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (g == 0) atomicAdd(&dmS[j * 8 + c4 * 2 + x], v);
+    }
+  __syncthreads();
+  // max: dm = dz - sum_t d_x, shared evenly by the tokens that attain the max
+  for (int d = tid; d < D; d += 256) {
+    const float dm = rb(dzS[d] - rb(dmS[d]));
+    int count = 0;
+    for (int t = 0; t < NT; ++t) count += kat(t, d) == mx[d];
+    const float share = rb(dm / count);
+    for (int t = 0; t < NT; ++t)
+      if (kat(t, d) == mx[d]) {
+        bf16* p = dkb + (long long)t * row + d;
+        *p = tobf(bf(*p) + share);
+      }
+  }
+}
+
+}  // namespace tao

@@ -50,3 +50,34 @@ def test_forward_matches_oracle(b, t, h, d, alpha, one_thread):
         out, _ = run(x, alpha)
         ref = o.tao_attention(*(x[k] for k in KEYS), x["fusion_a"], x["fusion_b"], alpha)
     assert frac_bad(out, ref) <= 1e-3
+
+
+def rel_l2(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+@pytest.mark.parametrize("name", ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages"])
+def test_backward_matches_reference_golden(name):
+    g = torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
+    b, t, h, d, alpha, seed = g["case"]
+    x, gen = make_inputs(b, t, h, d, seed)
+    grad = torch.randn(b, t, h, d, generator=gen).to(torch.bfloat16)
+    out, grads = run(x, alpha, grad)
+    s = g.get("row_stride", 1)
+    assert frac_bad(out[:, ::s], g["output"]) <= 1e-3
+    for k, ref in g["grads"].items():
+        mine = grads[k][:, ::s] if k in KEYS else grads[k]
+        assert rel_l2(mine, ref) <= 2e-2, (k, rel_l2(mine, ref))
+
+
+@pytest.mark.parametrize("b,t,h,d,alpha", [(2, 4096, 2, 64, [0.2, 0.7]), (1, 1280, 2, 128, 0.4)])
+def test_backward_matches_oracle(b, t, h, d, alpha, one_thread):
+    x, gen = make_inputs(b, t, h, d, seed=23)
+    grad = torch.randn(b, t, h, d, generator=gen).to(torch.bfloat16)
+    _, grads = run(x, alpha, grad)
+    leaves = {k: v.clone().requires_grad_(True) for k, v in x.items()}
+    ref = o.tao_attention(*(leaves[k] for k in KEYS), leaves["fusion_a"], leaves["fusion_b"], alpha)
+    ref.backward(grad)
+    for k in leaves:
+        assert rel_l2(grads[k], leaves[k].grad) <= 2e-2, (k, rel_l2(grads[k], leaves[k].grad))
