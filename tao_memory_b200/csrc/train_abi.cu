@@ -130,7 +130,8 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   const size_t rsmem = ReadBwdSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the read backward kernel");
   if (!tsmem(read_bwd_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
-  read_bwd_kernel<D><<<dim3(g.tiles, B * H), 256, rsmem, s>>>(a);
+  constexpr int NQ = ReadBwdSmem<D>::NQ;
+  read_bwd_kernel<D><<<dim3(g.tiles * (256 / NQ), B * H), NQ, rsmem, s>>>(a);
   if (g.S > 0) {
     const size_t wsmem = (size_t)2 * 256 * D * 2 + (size_t)D * D * 2 + 6 * D * 4;
     if (!tsmem(writer_bwd_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");

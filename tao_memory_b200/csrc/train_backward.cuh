@@ -445,23 +445,25 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(BwdArgs a) {
 // ---------------------------------------------------------------------------
 template <int D>
 struct ReadBwdSmem {
+  static constexpr int NQ = (D == 64) ? 256 : 128;  // queries (= threads) per CTA
   static size_t bytes(int P, int V, int mmax) {
-    return 3 * (size_t)256 * D * 2 + (size_t)D * D * 2 + 4 * (size_t)P * D * 4 +
-           ((size_t)V * D * 2 + 15) / 16 * 16 + (size_t)256 * mmax * 2 + 256 * 4 + 256 +
+    return 3 * (size_t)NQ * D * 2 + (size_t)D * D * 2 + 4 * (size_t)P * D * 4 +
+           ((size_t)V * D * 2 + 15) / 16 * 16 + (size_t)NQ * mmax * 2 + NQ * 4 + NQ +
            (size_t)D * 4 + (size_t)(V + 8) * 4 * 2 + 64;
   }
 };
 
 template <int D>
-__global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
+__global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a) {
   using namespace wa;
-  const int tile = blockIdx.x, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  constexpr int NQ = ReadBwdSmem<D>::NQ, QS = 256 / NQ;
+  const int tile = blockIdx.x / QS, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q0 = tile * 256, nq = min(256, a.dm.T - q0);
+  const int q0 = tile * 256 + (blockIdx.x % QS) * NQ, nq = max(0, min(NQ, a.dm.T - q0));
   const int V = max(0, tile - 2);
   const long long row = a.dm.row, hoff = (long long)h * D;
   if (V == 0) {
-    for (int idx = tid; idx < nq * (D / 8); idx += 256) {
+    for (int idx = tid; idx < nq * (D / 8); idx += NQ) {
       const int q = idx / (D / 8), c = idx % (D / 8);
       const long long off = ((long long)b * a.dm.T + q0 + q) * row + hoff + c * 8;
       *reinterpret_cast<uint4*>(a.d_raw_q + off) = *reinterpret_cast<const uint4*>(a.d_rq_f + off);
@@ -472,37 +474,37 @@ __global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
   const int M = a.mmax;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ptr = smem;
-  const uint32_t sH = smem_u32(ptr);  ptr += 256 * D * 2;
-  const uint32_t sG = smem_u32(ptr);  ptr += 256 * D * 2;
-  const uint32_t sA = smem_u32(ptr);  ptr += 256 * D * 2;
+  const uint32_t sH = smem_u32(ptr);  ptr += NQ * D * 2;
+  const uint32_t sG = smem_u32(ptr);  ptr += NQ * D * 2;
+  const uint32_t sA = smem_u32(ptr);  ptr += NQ * D * 2;
   const uint32_t sC = smem_u32(ptr);  ptr += D * D * 2;
   uint8_t* hB = smem;
-  uint8_t* aB = smem + 2 * 256 * D * 2;
+  uint8_t* aB = smem + 2 * NQ * D * 2;
   float* pwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* pzS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* dpwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   float* dpzS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   bf16* swS = reinterpret_cast<bf16*>(ptr);     ptr += ((size_t)V * D * 2 + 15) / 16 * 16;
-  int16_t* selS = reinterpret_cast<int16_t*>(ptr); ptr += (size_t)256 * M * 2;
-  float* gdS = reinterpret_cast<float*>(ptr);   ptr += 256 * 4;
-  uint8_t* selq = ptr;                          ptr += 256;
+  int16_t* selS = reinterpret_cast<int16_t*>(ptr); ptr += (size_t)NQ * M * 2;
+  float* gdS = reinterpret_cast<float*>(ptr);   ptr += NQ * 4;
+  uint8_t* selq = ptr;                          ptr += NQ;
   float* dwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)D * 4;
   int* useS = reinterpret_cast<int*>(ptr);
   int* list = useS + V;
 
   // ---- tables (as in the forward)
   const bf16* pzb = a.pzpre + ((long long)b * a.dm.H + h) * a.pages * kGroup * D;
-  for (int idx = tid; idx < P * D; idx += 256) {
+  for (int idx = tid; idx < P * D; idx += NQ) {
     const int pg = idx / D, d = idx % D;
     const int n = (pg < completed) ? kGroup : pending;
     pzS[idx] = bf(pzb[((long long)pg * kGroup + (n - 1)) * D + d]);
     dpwS[idx] = 0.f;
     dpzS[idx] = 0.f;
   }
-  for (int i = tid; i < V; i += 256) useS[i] = 0;
-  for (int d = tid; d < D; d += 256) dwS[d] = 0.f;
+  for (int i = tid; i < V; i += NQ) useS[i] = 0;
+  for (int d = tid; d < D; d += NQ) dwS[d] = 0.f;
   __syncthreads();
-  for (int d = tid; d < D; d += 256) {
+  for (int d = tid; d < D; d += NQ) {
     float mx = -INFINITY;
     for (int pg = 0; pg < P; ++pg) mx = fmaxf(mx, pzS[pg * D + d]);
     float sum = 0.f;
@@ -510,7 +512,7 @@ __global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
     for (int pg = 0; pg < P; ++pg) pwS[pg * D + d] = rb(__fdiv_rn(expf(pzS[pg * D + d] - mx), sum));
   }
   const bf16* zb = a.z + ((long long)b * a.dm.H + h) * a.dm.S * D;
-  for (int idx = tid; idx < V * D; idx += 256) {
+  for (int idx = tid; idx < V * D; idx += NQ) {
     const int sf = idx / D, d = idx % D;
     swS[idx] = tobf(expf(rb(__fsub_rn(bf(zb[(long long)sf * D + d]), pzS[(sf / kGroup) * D + d]))));
   }
@@ -539,7 +541,7 @@ __global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
       for (int e = 0; e < 4; ++e)
         o[e] = __floats2bfloat162_rn(__fdiv_rn(expf(f[2 * e] - mx), sum), __fdiv_rn(expf(f[2 * e + 1] - mx), sum));
       *reinterpret_cast<uint4*>(hB + swz(q, c * 8, D)) = *reinterpret_cast<uint4*>(o);
-      *reinterpret_cast<uint4*>(hB + 256 * D * 2 + swz(q, c * 8, D)) =
+      *reinterpret_cast<uint4*>(hB + NQ * D * 2 + swz(q, c * 8, D)) =
           *reinterpret_cast<const uint4*>(a.gn + qbase + c * 8);
     }
     gdS[q] = a.gd[((long long)b * a.dm.T + q0 + q) * a.dm.H + h];
@@ -551,7 +553,7 @@ __global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
   } else {
     for (int c = 0; c < D / 8; ++c) {
       *reinterpret_cast<uint4*>(hB + swz(q, c * 8, D)) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(hB + 256 * D * 2 + swz(q, c * 8, D)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(hB + NQ * D * 2 + swz(q, c * 8, D)) = make_uint4(0, 0, 0, 0);
     }
     gdS[q] = 0.f;
     for (int m = 0; m < M; ++m) selS[q * M + m] = -1;
@@ -615,7 +617,7 @@ __global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
       cur_page = pg;
     }
     // load C_s, build A_s and the selection flags
-    for (int idx = tid; idx < D * D / 8; idx += 256) {
+    for (int idx = tid; idx < D * D / 8; idx += NQ) {
       const int r = idx / (D / 8), c = idx % (D / 8);
       cp_async16(sC + swz(r, c * 8, D), cb + (long long)sf * D * D + r * D + c * 8, true);
     }
@@ -696,44 +698,48 @@ __global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
         v += __shfl_xor_sync(0xffffffffu, v, 16);
         if (g == 0 && v != 0.f) atomicAdd(&dwS[j * 8 + c4 * 2 + x], v);
       }
-    // dC_s = A_s^T . gn : output [d][e]; warp -> (m-tile of d rows, n range)
+    // dC_s = A_s^T . gn : output [d][e]; warps tile (m-tiles of d rows) x (n ranges)
     {
-      constexpr int MTILES = D / 16;                  // 4 or 8
-      constexpr int WPM = 8 / MTILES;                 // warps per m-tile: 2 or 1
-      constexpr int NPW = (D / 8) / WPM;              // n-tiles per warp: 4 or 16
-      const int mt = warp / WPM, n0 = (warp % WPM) * NPW;
-      float dc[NPW][4];
-#pragma unroll
-      for (int j = 0; j < NPW; ++j) dc[j][0] = dc[j][1] = dc[j][2] = dc[j][3] = 0.f;
-      for (int kt = 0; kt < 16; ++kt) {  // 256 queries
-        uint32_t af[4];
-        const int r = kt * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
-        const int c = mt * 16 + ((lane >> 3) & 1) * 8;
-        ldsm_x4_t(sA + swz(r, c, D), af[0], af[1], af[2], af[3]);
-#pragma unroll
-        for (int np = 0; np < NPW / 2; ++np) {
-          uint32_t b0, b1, b2, b3;
-          const int rr = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int cc = (n0 + 2 * np) * 8 + (lane >> 4) * 8;
-          ldsm_x4_t(sG + swz(rr, cc, D), b0, b1, b2, b3);
-          mma16816(dc[2 * np], af, b0, b1);
-          mma16816(dc[2 * np + 1], af, b2, b3);
-        }
-      }
+      constexpr int NW = NQ / 32, MTILES = D / 16;
+      constexpr int WPM = NW >= MTILES ? NW / MTILES : 1;   // warps per m-tile
+      constexpr int MPW = NW >= MTILES ? 1 : MTILES / NW;   // m-tiles per warp
+      constexpr int NPW = (D / 8) / WPM;                    // n-tiles per warp
       float* dcb = a.dC + (((long long)b * a.dm.H + h) * a.dm.S + sf) * (long long)D * D;
+      for (int mm = 0; mm < MPW; ++mm) {
+        const int mt = (NW >= MTILES) ? warp / WPM : warp * MPW + mm;
+        const int n0 = (NW >= MTILES) ? (warp % WPM) * NPW : 0;
+        float dc[NPW][4];
 #pragma unroll
-      for (int j = 0; j < NPW; ++j) {
-        const int e = (n0 + j) * 8 + c4 * 2;
-        const int d0 = mt * 16 + g;
-        atomicAdd(reinterpret_cast<float2*>(dcb + (long long)d0 * D + e),
-                  make_float2(rb(dc[j][0]), rb(dc[j][1])));
-        atomicAdd(reinterpret_cast<float2*>(dcb + (long long)(d0 + 8) * D + e),
-                  make_float2(rb(dc[j][2]), rb(dc[j][3])));
+        for (int j = 0; j < NPW; ++j) dc[j][0] = dc[j][1] = dc[j][2] = dc[j][3] = 0.f;
+        for (int kt = 0; kt < NQ / 16; ++kt) {
+          uint32_t af[4];
+          const int r = kt * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+          const int c = mt * 16 + ((lane >> 3) & 1) * 8;
+          ldsm_x4_t(sA + swz(r, c, D), af[0], af[1], af[2], af[3]);
+#pragma unroll
+          for (int np = 0; np < NPW / 2; ++np) {
+            uint32_t b0, b1, b2, b3;
+            const int rr = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int cc = (n0 + 2 * np) * 8 + (lane >> 4) * 8;
+            ldsm_x4_t(sG + swz(rr, cc, D), b0, b1, b2, b3);
+            mma16816(dc[2 * np], af, b0, b1);
+            mma16816(dc[2 * np + 1], af, b2, b3);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < NPW; ++j) {
+          const int e = (n0 + j) * 8 + c4 * 2;
+          const int d0 = mt * 16 + g;
+          atomicAdd(reinterpret_cast<float2*>(dcb + (long long)d0 * D + e),
+                    make_float2(rb(dc[j][0]), rb(dc[j][1])));
+          atomicAdd(reinterpret_cast<float2*>(dcb + (long long)(d0 + 8) * D + e),
+                    make_float2(rb(dc[j][2]), rb(dc[j][3])));
+        }
       }
     }
     __syncthreads();
     // dw_s -> d(z - pz) = bf16(bf16(dw) * w) : dz[s] += ., d page_z[pg] -= .
-    for (int d = tid; d < D; d += 256) {
+    for (int d = tid; d < D; d += NQ) {
       const float ddiff = rb(__fmul_rn(rb(dwS[d]), bf(swS[sf * D + d])));
       atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d, ddiff);
       dpzS[pg * D + d] -= ddiff;
@@ -772,14 +778,14 @@ __global__ void __launch_bounds__(256) read_bwd_kernel(BwdArgs a) {
       }
     }
   // ---- page weights softmax backward, then logsumexp backward of page_z -> dz
-  for (int d = tid; d < D; d += 256) {
+  for (int d = tid; d < D; d += NQ) {
     float dot = 0.f;
     for (int pg = 0; pg < P; ++pg) dot += pwS[pg * D + d] * rb(dpwS[pg * D + d]);
     for (int pg = 0; pg < P; ++pg)
       dpzS[pg * D + d] += rb(pwS[pg * D + d] * (rb(dpwS[pg * D + d]) - dot));
   }
   __syncthreads();
-  for (int idx = tid; idx < V * D; idx += 256) {
+  for (int idx = tid; idx < V * D; idx += NQ) {
     const int sf = idx / D, d = idx % D, pg = sf / kGroup;
     const float lse = pzS[pg * D + d];
     const float w = rb(expf(rb(__fsub_rn(bf(zb[(long long)sf * D + d]), lse))));
