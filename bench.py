@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--requests", type=int, default=REQUESTS)
     ap.add_argument("--context", type=int, default=CONTEXT)
     ap.add_argument("--cpu-sample-steps", type=int, default=4)
+    ap.add_argument("--workload", default="decode128k", choices=["decode128k", "train8k"])
     return ap.parse_args()
 
 
@@ -381,11 +382,181 @@ def run_reference(args):
     }
 
 
+# ---------------------------------------------------------------------------
+# Training workload: tao_attention fwd+bwd, B4 T8192 H12 D64
+# ---------------------------------------------------------------------------
+TB, TT, TH, TD = 4, 8192, 12, 64
+
+
+def local_attention_flops(tokens, heads, width, batch):
+    """Exact forward FLOPs of the windowed local attention: 4*D per (query, key)."""
+    total = 0
+    for t in range(tokens):
+        lo = max(0, 256 * (t // 256) - 512)
+        total += t - lo + 1
+    return 4 * width * total * heads * batch
+
+
+def train_inputs(device, seed, batch=TB, tokens=TT):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = [torch.randn(batch, tokens, TH, TD, device=device, generator=g).to(torch.bfloat16) for _ in range(5)]
+    fa = (torch.randn(TH, TD, 3, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    fb = (torch.randn(TH, TD, 3, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    alpha = torch.rand(TH, device=device, generator=g).tolist()
+    grad = torch.randn(batch, tokens, TH, TD, device=device, generator=g).to(torch.bfloat16)
+    return x, fa, fb, alpha, grad
+
+
+def run_train_bench(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    import tao_memory_b200 as tb
+    from tao_memory_b200 import _lib
+    from tao_memory_b200.presets import index_only_page_memo
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    lib = _lib.lib()
+    cfg = index_only_page_memo()
+    x, fa, fb, alpha, grad = train_inputs(device, seed=1 + rank)
+    leaves = [t.requires_grad_(True) for t in x] + [fa.requires_grad_(True), fb.requires_grad_(True)]
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        out = tb.tao_attention(leaves[0], leaves[1], leaves[2], raw_q=leaves[3], raw_k=leaves[4],
+                               fusion_a=leaves[5], fusion_b=leaves[6], alpha=alpha, config=cfg)
+        out.backward(grad)
+        return out
+
+    K, W = args.steps, args.warmup
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+
+    def ev():
+        e = ctypes.c_void_p()
+        _lib.check(lib.tao_event_create(ctypes.byref(e)))
+        return e
+
+    stream = torch.cuda.current_stream(device).cuda_stream
+    starts, stops, a0, a1 = ([ev() for _ in range(K)] for _ in range(4))
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("timed_train")
+    for i in range(K):
+        lib.tao_event_record(starts[i], stream)
+        lib.tao_stream_profile_next(a0[i], a1[i])
+        step()
+        lib.tao_event_record(stops[i], stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+
+    def elapsed(a, b):
+        ms = ctypes.c_float()
+        _lib.check(lib.tao_event_elapsed(a, b, ctypes.byref(ms)))
+        return ms.value
+
+    step_ms = [elapsed(a, b) for a, b in zip(starts, stops)]
+    attn_ms = [elapsed(a, b) for a, b in zip(a0, a1)]
+    # e2e: operands from pinned host memory each step, loss scalar back to the host
+    host = [t.detach().cpu().pin_memory() for t in x]
+    hgrad = grad.cpu().pin_memory()
+    dev_in = [torch.empty_like(t) for t in x]
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    for i in range(K):
+        e_s[i].record()
+        for d, h in zip(dev_in, host):
+            d.copy_(h, non_blocking=True)
+        ops = [d.requires_grad_(True) for d in dev_in]
+        g_dev = hgrad.to(device, non_blocking=True)
+        out = tb.tao_attention(ops[0], ops[1], ops[2], raw_q=ops[3], raw_k=ops[4], fusion_a=leaves[5],
+                               fusion_b=leaves[6], alpha=alpha, config=cfg)
+        loss = (out.float() * g_dev.float()).sum()
+        loss.backward()
+        loss_host.copy_(loss.detach(), non_blocking=True)
+        e_e[i].record()
+        dev_in = [d.detach() for d in dev_in]
+    torch.cuda.synchronize()
+    clocks.stop()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in zip(e_s, e_e))
+    total_ms = sum(step_ms)
+    tot = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = tot.tolist()
+    tokens = world * TB * TT * K
+    flops = local_attention_flops(TT, TH, TD, TB)
+    achieved = flops / (statistics.mean(attn_ms) * 1e-3) / 1e12
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak, kind = float(peaks["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        peak, kind = 1400.0, "fallback (sustained)"
+    return {
+        "metric": "train fwd+bwd tokens/s @8K", "value": round(tokens / (total_ms * 1e-3), 1),
+        "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(total_ms / K, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic ~N(0,1), seeded",
+        "config": {"workload": "train8k (BASELINE.json config 2)", "batch": TB, "seq_len": TT,
+                   "heads": TH, "head_dim": TD, "alpha": "U(0,1) per head",
+                   "preset": "index_only_page_memo", "l2": "inputs (5 x 50 MB) larger than L2"},
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": 6 * TB * TT * TH * TD * 2, "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "tensor", "kernel": "window_attention_kernel<64> (forward)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": kind,
+                     "algorithmic_flops_per_launch": flops,
+                     "kernel_ms_mean": round(statistics.mean(attn_ms), 4), "traffic": None},
+        "gpu_launches": 10 * K,
+        "clocks": clocks.summary(),
+    }
+
+
+def cpu_train_baseline(budget_tokens=8192):
+    """Oracle fwd+bwd on one batch row and one head of the 8K workload."""
+    import torch
+    from oracle import tao_oracle as o
+    from oracle.inputs import make_inputs
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, g = make_inputs(1, budget_tokens, 1, TD, seed=3)
+    grad = torch.randn(1, budget_tokens, 1, TD, generator=g).to(torch.bfloat16)
+    leaves = {k: v.clone().requires_grad_(True) for k, v in x.items()}
+    t0 = time.perf_counter()
+    out = o.tao_attention(leaves["q"], leaves["k"], leaves["v"], leaves["raw_q"], leaves["raw_k"],
+                          leaves["fusion_a"], leaves["fusion_b"], 0.5)
+    out.backward(grad)
+    secs = time.perf_counter() - t0
+    # one head of 12 and one batch row of 4: tokens/s of the full workload
+    value = budget_tokens / (secs * TH)
+    return {"value": round(value, 2), "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"fwd+bwd of 1 row x 1 head x {budget_tokens} tokens (of {TB} x {TH} heads), "
+                      f"oracle/tao_oracle.py; value scaled to all {TH} heads"}
+
+
 def main():
     args = parse()
     world, rank, local = dist_env()
     if args.impl == "reference":
         if rank != 0:
+            return 0
+        if args.workload == "train8k":
+            cb = cpu_train_baseline()
+            print(json.dumps({"metric": "train fwd+bwd tokens/s @8K", "value": cb["value"], "unit": "tok/s",
+                              "n_gpus": args.gpus, "steps": 1, "warmup": 0, "higher_is_better": True,
+                              "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                              "data": "synthetic ~N(0,1), seeded", "impl": "reference",
+                              "config": {"workload": "train8k (BASELINE.json config 2)"},
+                              "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tok/s",
+                                                          "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+                  flush=True)
             return 0
         print(json.dumps(run_reference(args)), flush=True)
         return 0
@@ -397,11 +568,16 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     try:
-        result, states = run_b200(args, world, rank, local)
-        if rank == 0 and world == 1:
-            result["cpu_baseline"] = cpu_baseline_from_gpu(states, args.cpu_sample_steps)
-        elif rank == 0:
-            result["cpu_baseline"] = None
+        if args.workload == "train8k":
+            result = run_train_bench(args, world, rank, local)
+            if rank == 0:
+                result["cpu_baseline"] = cpu_train_baseline() if world == 1 else None
+        else:
+            result, states = run_b200(args, world, rank, local)
+            if rank == 0 and world == 1:
+                result["cpu_baseline"] = cpu_baseline_from_gpu(states, args.cpu_sample_steps)
+            elif rank == 0:
+                result["cpu_baseline"] = None
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:

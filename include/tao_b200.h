@@ -135,7 +135,8 @@ int tao_stream_decode_noalloc(void* const* states, int n_states, const int64_t* 
  * other binding).  tao_stream_profile_next(start, stop) makes the next
  * tao_stream_step on this host thread record `start` just before and `stop` just
  * after its main kernel(s) (the local-attention + fine-read phase), on the
- * stream it launches on.  No reference counterpart (profiling hook). */
+ * stream it launches on; for the next tao_train_forward instead, around its
+ * windowed local-attention kernel.  No reference counterpart (profiling hook). */
 int tao_event_create(void** event);
 int tao_event_destroy(void* event);
 int tao_event_record(void* event, void* stream);

@@ -110,6 +110,14 @@ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 // tao_last_error() on the calling host thread.
 void tao_set_last_error(const char* msg) { g_last_error = msg; }
 
+// Hands the pending profiling events (tao_stream_profile_next) to another
+// translation unit's launcher and clears them.
+void tao_take_profile_events(cudaEvent_t* start, cudaEvent_t* stop) {
+  *start = g_prof_start;
+  *stop = g_prof_stop;
+  g_prof_start = g_prof_stop = nullptr;
+}
+
 namespace {
 
 template <typename F>

@@ -7,6 +7,7 @@
 #include "train_backward.cuh"
 
 void tao_set_last_error(const char* msg);
+void tao_take_profile_events(cudaEvent_t* start, cudaEvent_t* stop);
 
 namespace {
 
@@ -77,7 +78,11 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
   p.kstart = -1;
   const size_t attn_smem = (size_t)(64 + 4 * 64) * D * 2;
   if (!tsmem(window_attention_kernel<D>, attn_smem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+  cudaEvent_t ev0, ev1;
+  tao_take_profile_events(&ev0, &ev1);
+  if (ev0) cudaEventRecord(ev0, s);
   window_attention_kernel<D><<<dim3((T + 63) / 64, B * H), 128, attn_smem, s>>>(p);
+  if (ev1) cudaEventRecord(ev1, s);
   if (g.S > 0) {
     // 2. writer over all sealed blocks, 3. page prefix table
     const size_t wsmem = (size_t)2 * 256 * D * 2 + 2 * D * 4;
