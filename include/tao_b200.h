@@ -61,6 +61,8 @@ typedef struct TaoPolicy {
  *                             softmax over pages (the page-normalisation memo)
  *   route_ids               : int32 [H][route_cap]   selected fines, rank order
  *   route_pages             : int32 [H][route_cap]   pages kept by the page top-K
+ *   counters                : int32 [H], zero-initialised; per-head arrival counters
+ *                             of the fused decode kernel (reset by their last user)
  */
 typedef struct TaoState {
   void* k_ring;
@@ -72,6 +74,7 @@ typedef struct TaoState {
   void* page_w;
   int32_t* route_ids;
   int32_t* route_pages;
+  int32_t* counters;
   int64_t position;
   int32_t n_route;
   int32_t n_chosen;
@@ -107,6 +110,19 @@ size_t tao_stream_workspace_bytes(int n_states, int tokens, int heads, int width
  * operator.py:79-99). */
 int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
                     const int32_t* host_cap, const TaoPolicy* policy, int tokens,
+                    int heads, int width, const void* q, const void* k, const void* v,
+                    const void* raw_q, const void* raw_k, const void* fusion_a,
+                    const void* fusion_b, float alpha, void* out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Fast decode step: one token for each of n_states requests in one fused kernel
+ * (plus a routing kernel on refresh tokens and a seal kernel when a window fills).
+ * Same arguments as tao_stream_step with tokens = 1, plus host_layer (the layer
+ * index of each state, used to decide on the host whether any request refreshes).
+ * Workspace: tao_stream_workspace_bytes(n_states, 1, ...).  Results are identical
+ * to tao_stream_step.  Reference: tao_attention_decode (operator.py:130-137). */
+int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
+                    const int32_t* host_layer, const int32_t* host_cap, const TaoPolicy* policy,
                     int heads, int width, const void* q, const void* k, const void* v,
                     const void* raw_q, const void* raw_k, const void* fusion_a,
                     const void* fusion_b, float alpha, void* out, void* workspace,

@@ -26,7 +26,8 @@ class TaoState(ctypes.Structure):
                 ("rk_ring", ctypes.c_void_p), ("fine_c", ctypes.c_void_p),
                 ("fine_z", ctypes.c_void_p), ("page_z", ctypes.c_void_p),
                 ("page_w", ctypes.c_void_p), ("route_ids", ctypes.c_void_p),
-                ("route_pages", ctypes.c_void_p), ("position", ctypes.c_int64),
+                ("route_pages", ctypes.c_void_p), ("counters", ctypes.c_void_p),
+                ("position", ctypes.c_int64),
                 ("n_route", ctypes.c_int32), ("n_chosen", ctypes.c_int32),
                 ("cap_fines", ctypes.c_int32), ("route_cap", ctypes.c_int32),
                 ("layer_index", ctypes.c_int32), ("heads", ctypes.c_int32),
@@ -49,6 +50,9 @@ _SIGNATURES = {
                              ctypes.POINTER(TaoPolicy), _I, _I, _I, _VP, _VP, _VP, _VP, _VP,
                              _VP, _VP, _F, _VP, _VP, _SZ, _VP]),
     "tao_stream_check": (_I, [_VP, ctypes.POINTER(_I), _VP]),
+    "tao_decode_step": (_I, [_VP, _I, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_int32),
+                             ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(TaoPolicy), _I, _I,
+                             _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F, _VP, _VP, _SZ, _VP]),
     "tao_stream_decode_noalloc": (_I, [_VP, _I, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_int32),
                                        ctypes.POINTER(TaoPolicy), _I, _I, _VP, _VP, _VP, _VP, _VP,
                                        _VP, _VP, _F, _VP, _VP]),

@@ -12,6 +12,7 @@
 #include <string>
 
 #include "../../include/tao_b200.h"
+#include "decode_fused.cuh"
 #include "stream_kernels.cuh"
 #include "window_attention.cuh"
 
@@ -176,9 +177,111 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
   return check_launch("finalize_kernel");
 }
 
+template <int D>
+int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaStream_t s) {
+  using namespace tao;
+  int rc;
+  if (refresh) {
+    const size_t smem = (size_t)D * 4 + (size_t)a.pmax * 4 + (size_t)(8 * a.pmax + 8) * 8 + (size_t)a.pmax * 8;
+    if ((rc = set_smem(decode_route_kernel<D>, smem))) return rc;
+    decode_route_kernel<D><<<a.R * a.H, 256, smem, s>>>(a);
+    if ((rc = check_launch("decode_route_kernel"))) return rc;
+  }
+  FusedArgs f{};
+  f.s = a;
+  f.ms = ms;
+  const size_t smem = FusedCfg<D>::STAGE;
+  if ((rc = set_smem(decode_fused_kernel<D>, smem))) return rc;
+  const int grid = a.R * a.H * (FusedCfg<D>::KB + ms);
+  if (g_prof_start) cudaEventRecord(g_prof_start, s);
+  decode_fused_kernel<D><<<grid, 128, smem, s>>>(f);
+  if (g_prof_stop) cudaEventRecord(g_prof_stop, s);
+  g_prof_start = g_prof_stop = nullptr;
+  if ((rc = check_launch("decode_fused_kernel"))) return rc;
+  if (seal) {
+    const size_t ss = (size_t)2 * kFine * D * 2 + (size_t)2 * D * 4;
+    if ((rc = set_smem(decode_seal_kernel<D>, ss))) return rc;
+    decode_seal_kernel<D><<<a.R * a.H, 256, ss, s>>>(a);
+    if ((rc = check_launch("decode_seal_kernel"))) return rc;
+  }
+  return TAO_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
+                    const int32_t* host_layer, const int32_t* host_cap, const TaoPolicy* policy,
+                    int heads, int width, const void* q, const void* k, const void* v,
+                    const void* raw_q, const void* raw_k, const void* fusion_a,
+                    const void* fusion_b, float alpha, void* out, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!states || n_states <= 0 || !host_pos || !host_cap || !host_layer || !policy)
+    return fail(TAO_ERR_ARG, "null state, cursor, layer, capacity or policy array");
+  if (width != 64 && width != 128) return fail(TAO_ERR_ARG, "head width must be 64 or 128, got %d", width);
+  if (heads <= 0) return fail(TAO_ERR_ARG, "heads must be positive");
+  if (policy->fine_tokens != 256 || policy->local_keep != 512 || policy->coarse_group != 8)
+    return fail(TAO_ERR_ARG, "kernels are specialised for fine_tokens=256, local_keep=512, coarse_group=8");
+  if (policy->route_period <= 0 || policy->layer_stagger < 0 || policy->budget_root_scale <= 0 ||
+      policy->budget_offset < 0 || policy->route_cap <= 0)
+    return fail(TAO_ERR_ARG, "invalid routing policy");
+  for (const void* p : {q, k, v, raw_q, raw_k, fusion_a, fusion_b, (const void*)out, (const void*)workspace})
+    if (!p) return fail(TAO_ERR_ARG, "null tensor pointer");
+  for (const void* p : {q, k, v, raw_q, raw_k, (const void*)out})
+    if (!aligned16(p)) return fail(TAO_ERR_ARG, "token tensors must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(TAO_ERR_ARG, "workspace must be 256-byte aligned");
+  int pmax = 1, mbound = 1;
+  bool refresh = false, seal = false;
+  for (int r = 0; r < n_states; ++r) {
+    const long long pos = host_pos[r];
+    if (pos < 0) return fail(TAO_ERR_POSITION, "negative position");
+    const long long start = h_window_start(pos);
+    const int S = h_sealed_at(pos);
+    const bool sl = (pos + 1 - start) == 768;
+    const int cap = host_cap[r];
+    if (cap <= 0 || cap % 8) return fail(TAO_ERR_ARG, "fine capacity must be a positive multiple of 8");
+    if (S + (sl ? 1 : 0) > cap) return fail(TAO_ERR_CAPACITY, "fine bank capacity %d too small for %d fines", cap, S + 1);
+    seal |= sl;
+    const long long first_turn = 768 + (long long)policy->layer_stagger * host_layer[r];
+    refresh |= S > 0 && (pos == 768 || (pos >= first_turn && (pos - first_turn) % policy->route_period == 0));
+    if (cap / 8 + 1 > pmax) pmax = cap / 8 + 1;
+    const int mb = h_budget(cap, *policy);
+    if (mb > mbound) mbound = mb;
+  }
+  const int route_cap = policy->route_cap;
+  if (mbound > route_cap) mbound = route_cap;
+  const int fpc = fpc_for(width);
+  const int ms = (mbound + fpc - 1) / fpc;
+  const Layout L = make_layout(n_states, 1, heads, width, route_cap, ms, policy->route_period);
+  if (workspace_bytes < L.total) return fail(TAO_ERR_ARG, "workspace too small: %zu < %zu", workspace_bytes, L.total);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  tao::StepArgs a{};
+  a.states = reinterpret_cast<TaoState* const*>(states);
+  a.R = n_states;
+  a.w = 1;
+  a.H = heads;
+  a.pol = {policy->route_period, policy->layer_stagger, policy->budget_root_scale, policy->budget_offset};
+  a.q = static_cast<const tao::bf16*>(q);
+  a.k = static_cast<const tao::bf16*>(k);
+  a.v = static_cast<const tao::bf16*>(v);
+  a.raw_q = static_cast<const tao::bf16*>(raw_q);
+  a.raw_k = static_cast<const tao::bf16*>(raw_k);
+  a.fa = static_cast<const tao::bf16*>(fusion_a);
+  a.fb = static_cast<const tao::bf16*>(fusion_b);
+  a.gain = bf16_round(2.0f * alpha);
+  a.out = static_cast<tao::bf16*>(out);
+  a.err = reinterpret_cast<int*>(ws + L.err);
+  a.nslot = L.nslot;
+  a.route_cap = route_cap;
+  a.kblocks = L.kblocks;
+  a.msplit = ms;
+  a.local_part = reinterpret_cast<float*>(ws + L.local_part);
+  a.fine_part = reinterpret_cast<float*>(ws + L.fine_part);
+  a.pmax = pmax;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return width == 64 ? launch_decode<64>(a, ms, refresh, seal, s) : launch_decode<128>(a, ms, refresh, seal, s);
+}
 
 const char* tao_last_error(void) { return g_last_error.c_str(); }
 

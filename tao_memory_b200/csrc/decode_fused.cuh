@@ -1,0 +1,430 @@
+// Fused single-kernel decode step (one token for each of R requests).
+//
+// Work items per (request r, head h): KB local-attention key blocks and MS groups
+// of selected fines (query_fresh_fine.py:8-49), one CTA per item with its bulk
+// copies issued first and the load-independent work (query scaling, h softmax,
+// channel weights) done while they are in flight.  Each item writes a partial; the CTA
+// that completes the last item of (r, h) combines the partials, applies the
+// pointwise fusion (fusion_pointwise.py:10-92) and writes the output; the CTA
+// that completes the last head of request r advances its cursor.  Arrival
+// counters are TaoState.counters[h] and TaoState.arrive, reset by their last user.
+//
+// Routing (refresh tokens) and sealing (window full) run as separate small
+// kernels that the host launches only on the steps that need them.
+#pragma once
+#include "stream_kernels.cuh"
+
+namespace tao {
+
+struct FusedArgs {
+  StepArgs s;        // states, shapes, inputs, outputs, policy, partial buffers
+  int ms;            // fine items per (r, h)
+};
+
+template <int D>
+struct FusedCfg {
+  static constexpr int SLOTS = DecodeCfg<D>::SLOTS;
+  static constexpr int FPC = DecodeCfg<D>::FPC;
+  static constexpr int KB = DecodeCfg<D>::KBLOCKS;
+  static constexpr int STAGE = 32768;  // bytes per pipeline stage
+};
+
+// Item i -> (rh, slot): slots of one (r, h) are spread over the grid.
+struct Item {
+  int r, h, slot;
+};
+TAO_DEVI Item item_of(int i, int R, int H) {
+  const int rh = i % (R * H);
+  return {rh / H, rh % H, i / (R * H)};
+}
+
+template <int D>
+TAO_DEVI bool local_block_live(long long t, long long start, int s0, int slots) {
+  const int tm = (int)(t % kWindow);
+  if (tm >= s0 && tm < s0 + slots) return true;
+  const long long count = t - start + 1;
+  const int dist = (tm - (s0 + slots - 1) + kWindow) % kWindow;  // nearest slot of the block
+  return dist < count;
+}
+
+// Issue the bulk copies of one item into `stage`; returns the bytes armed (0 = none).
+template <int D>
+TAO_DEVI uint32_t issue_item(const FusedArgs& f, const Item& it, uint8_t* stage, uint64_t* bar) {
+  using Cfg = FusedCfg<D>;
+  const StepArgs& a = f.s;
+  const TaoState& st = *a.states[it.r];
+  const long long t = st.position;
+  if (it.slot < Cfg::KB) {
+    const int s0 = it.slot * Cfg::SLOTS;
+    if (!local_block_live<D>(t, window_start(t), s0, Cfg::SLOTS)) return 0;
+    const uint32_t bytes = Cfg::SLOTS * D * 2;
+    mbar_expect_tx(bar, 2 * bytes);
+    bulk_g2s(stage, ring_head<D>(st.k_ring, it.h) + (long long)s0 * D, bytes, bar);
+    bulk_g2s(stage + bytes, ring_head<D>(st.v_ring, it.h) + (long long)s0 * D, bytes, bar);
+    return 2 * bytes;
+  }
+  if (t < kWindow) return 0;
+  const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
+  const int M = st.n_route;
+  if (m0 >= M) return 0;
+  const int nf = min(Cfg::FPC, M - m0);
+  const int32_t* ids = st.route_ids + (long long)it.h * st.route_cap + m0;
+  const bf16* fc = reinterpret_cast<const bf16*>(st.fine_c) + (long long)it.h * st.cap_fines * D * D;
+  const uint32_t bytes = D * D * 2;
+  mbar_expect_tx(bar, nf * bytes);
+  for (int i = 0; i < nf; ++i) bulk_g2s(stage + i * bytes, fc + (long long)ids[i] * D * D, bytes, bar);
+  return nf * bytes;
+}
+
+// h = bf16(softmax_d(raw_q)) of request r, head h (one warp), into hq[D].
+template <int D>
+TAO_DEVI void softmax_row(const bf16* x, float* hq, int lane) {
+  float vals[D / 32];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) {
+    vals[j] = bf(x[lane + 32 * j]);
+    mx = fmaxf(mx, vals[j]);
+  }
+  mx = warp_max(mx);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) {
+    vals[j] = expf(vals[j] - mx);
+    s += vals[j];
+  }
+  s = warp_sum(s);
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) hq[lane + 32 * j] = rb(__fdiv_rn(vals[j], s));
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
+  using Cfg = FusedCfg<D>;
+  const StepArgs& a = f.s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t armed;
+  __shared__ int flag;
+  __shared__ float qv[D];
+  __shared__ float red[128 + 8];
+  __shared__ float chs[Cfg::FPC * D];
+  __shared__ int last_rh;
+  const int per = Cfg::KB + f.ms;
+  const Item it = item_of(blockIdx.x, a.R, a.H);
+  TaoState& st = *a.states[it.r];
+  const long long t = st.position;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    armed = issue_item<D>(f, it, dsm, &bar);
+  }
+  const long long src = ((long long)it.r * a.H + it.h) * D;
+  if (it.slot < Cfg::KB) {
+    // ------------------------------------------------ local attention block
+    const int s0 = it.slot * Cfg::SLOTS;
+    const float sl = 1.4426950408889634f / sqrtf((float)D);
+    for (int d = tid; d < D; d += 128) qv[d] = bf(a.q[src + d]) * sl;
+    __syncthreads();
+    float* part = a.local_part + (((long long)it.r * a.H + it.h) * Cfg::KB + it.slot) * (D + 2);
+    if (!armed) {
+      if (tid == 0) { part[D] = -INFINITY; part[D + 1] = 0.f; }
+    } else {
+      if (!wait_uniform(&bar, 0, a.err, &flag)) return;
+      bf16* sk = reinterpret_cast<bf16*>(dsm);
+      bf16* sv = sk + Cfg::SLOTS * D;
+      const int tm = (int)(t % kWindow);
+      if (tm >= s0 && tm < s0 + Cfg::SLOTS) {
+        // this block owns the current token's slot: append to the ring, patch smem
+        for (int d = tid; d < D / 8; d += 128) {
+          const uint4 kk = reinterpret_cast<const uint4*>(a.k + src)[d];
+          const uint4 vv = reinterpret_cast<const uint4*>(a.v + src)[d];
+          const uint4 rr = reinterpret_cast<const uint4*>(a.raw_k + src)[d];
+          reinterpret_cast<uint4*>(sk + (tm - s0) * D)[d] = kk;
+          reinterpret_cast<uint4*>(sv + (tm - s0) * D)[d] = vv;
+          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.k_ring) + ((long long)it.h * kWindow + tm) * D)[d] = kk;
+          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.v_ring) + ((long long)it.h * kWindow + tm) * D)[d] = vv;
+          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.rk_ring) + ((long long)it.h * kWindow + tm) * D)[d] = rr;
+        }
+        __syncthreads();
+      }
+      constexpr int TPK = 128 / Cfg::SLOTS;
+      const int key = tid / TPK, pid = tid % TPK;
+      float sc = 0.f;
+      {
+        const bf16* kr = sk + key * D;
+        constexpr int NCH = D / 8 / TPK;
+#pragma unroll
+        for (int x = 0; x < NCH; ++x) {
+          const int c = pid * NCH + ((x + key) % NCH);
+          float fv[8];
+          unpack8(*reinterpret_cast<const uint4*>(kr + c * 8), fv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) sc += fv[e] * qv[c * 8 + e];
+        }
+        if (TPK == 2) sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+      }
+      const long long kp = t - (long long)((tm - (s0 + key) + kWindow) % kWindow);
+      if (kp < window_start(t) || kp > t) sc = -INFINITY;
+      float mx = warp_max(sc);
+      if (lane == 0) red[warp] = mx;
+      __syncthreads();
+      mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+      const float pk = (sc == -INFINITY) ? 0.f : exp2f(sc - mx);
+      const float ls = warp_sum(pid == 0 ? pk : 0.f);
+      if (pid == 0) red[8 + key] = pk;
+      __syncthreads();
+      if (lane == 0) red[4 + warp] = ls;
+      constexpr int ECH = D / 8, KG = 128 / ECH, KPG = Cfg::SLOTS / KG;
+      const int ec = tid % ECH, kg = tid / ECH;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int x = 0; x < KPG; ++x) {
+        const int kk = kg * KPG + x;
+        const float pj = red[8 + kk];
+        float fv[8];
+        unpack8(*reinterpret_cast<const uint4*>(sv + kk * D + ec * 8), fv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += pj * fv[e];
+      }
+      // reduce over key groups in the (now free) K half of the stage
+      float* rs = reinterpret_cast<float*>(dsm);
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rs[kg * D + ec * 8 + e] = acc[e];
+      __syncthreads();
+      for (int d = tid; d < D; d += 128) {
+        float sum = 0.f;
+        for (int g2 = 0; g2 < KG; ++g2) sum += rs[g2 * D + d];
+        part[d] = sum;
+      }
+      if (tid == 0) { part[D] = mx; part[D + 1] = red[4] + red[5] + red[6] + red[7]; }
+    }
+  } else if (t >= kWindow) {
+    // -------------------------------------------------- selected fine group
+    const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
+    const int nf = min(Cfg::FPC, st.n_route - m0);
+    if (nf > 0) {
+      const int32_t* ids = st.route_ids + (long long)it.h * st.route_cap + m0;
+      const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
+      const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + (long long)it.h * st.cap_fines * D;
+      const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + it.h * pstride;
+      const bf16* pw = reinterpret_cast<const bf16*>(st.page_w) + it.h * pstride;
+      // channels do not depend on the matrices in flight: compute them first
+      if (warp == 0) softmax_row<D>(a.raw_q + src, qv, lane);
+      __syncthreads();
+      for (int x = warp; x < nf; x += 4) {
+        const int id = ids[x], page = id / kGroup;
+        float sum = 0.f;
+        for (int d = lane; d < D; d += 32) {
+          const float hv = rb(__fmul_rn(qv[d], bf(pw[(long long)page * D + d])));
+          const float w = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
+          const float c = rb(__fmul_rn(hv, w));
+          chs[x * D + d] = c;
+          sum += c;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) red[x] = rb(sum);
+      }
+      if (!wait_uniform(&bar, 0, a.err, &flag)) return;
+      constexpr int ECH = D / 8, RG = 128 / ECH, RPG = D / RG;
+      const int ec = tid % ECH, rg = tid / ECH;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      const bf16* sc_ = reinterpret_cast<const bf16*>(dsm);
+      for (int x = 0; x < nf; ++x) {
+#pragma unroll
+        for (int y = 0; y < RPG; ++y) {
+          const int d = rg * RPG + y;
+          const float c = chs[x * D + d];
+          float fv[8];
+          unpack8(*reinterpret_cast<const uint4*>(sc_ + x * D * D + d * D + ec * 8), fv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += c * fv[e];
+        }
+      }
+      __syncthreads();
+      float* rs = reinterpret_cast<float*>(dsm);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rs[rg * D + ec * 8 + e] = acc[e];
+      __syncthreads();
+      float* part = a.fine_part + (((long long)it.r * a.H + it.h) * f.ms + (it.slot - Cfg::KB)) * (D + 1);
+      for (int d = tid; d < D; d += 128) {
+        float sum = 0.f;
+        for (int g2 = 0; g2 < RG; ++g2) sum += rs[g2 * D + d];
+        part[d] = sum;
+      }
+      if (tid == 0) {
+        float den = 0.f;
+        for (int x = 0; x < nf; ++x) den += red[x];
+        part[D] = den;
+      }
+    }
+  }
+  // ---- arrival: the CTA completing the last item of (r, h) finalises it
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    last_rh = (atomicAdd(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
+    if (last_rh) st.counters[it.h] = 0;
+    __threadfence();
+  }
+  __syncthreads();
+  if (!last_rh) return;
+  const bool hist = t >= kWindow;
+  const int M = st.n_route;
+  const int nparts = (M + Cfg::FPC - 1) / Cfg::FPC;
+  const float* lp = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
+  const float* fp = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
+  for (int d = tid; d < D; d += 128) {
+    float Mx = -INFINITY;
+    for (int b2 = 0; b2 < Cfg::KB; ++b2) Mx = fmaxf(Mx, __ldcg(lp + b2 * (D + 2) + D));
+    float L = 0.f, O = 0.f;
+    for (int b2 = 0; b2 < Cfg::KB; ++b2) {
+      const float mb = __ldcg(lp + b2 * (D + 2) + D);
+      if (mb == -INFINITY) continue;
+      const float scl = exp2f(mb - Mx);
+      L += scl * __ldcg(lp + b2 * (D + 2) + D + 1);
+      O += scl * __ldcg(lp + b2 * (D + 2) + d);
+    }
+    const float local = rb(O / L);
+    float outv = local;
+    if (hist) {
+      float acc = 0.f, den = 0.f;
+      for (int p2 = 0; p2 < nparts; ++p2) {
+        acc += __ldcg(fp + p2 * (D + 1) + d);
+        den += __ldcg(fp + p2 * (D + 1) + D);
+      }
+      const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
+      const float qq = bf(a.raw_q[src + d]);
+      const bf16* fa = a.fa + ((long long)it.h * D + d) * 3;
+      const bf16* fb = a.fb + ((long long)it.h * D + d) * 3;
+      const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), qq)), bf(fb[0]))), 0.f));
+      const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), qq)), bf(fb[2])));
+      const float mx = fmaxf(s0, s2);
+      const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
+      const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
+      const float lt = rb(__fmul_rn(rho0, rb(__fmul_rn(2.f, local))));
+      const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(a.gain, fine))));
+      outv = rb(__fadd_rn(rb(__fadd_rn(lt, 0.f)), ft));
+    }
+    a.out[src + d] = tobf(outv);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(&st.arrive, 1) == a.H - 1) {
+      st.arrive = 0;
+      st.position = t + 1;
+      __threadfence();
+    }
+  }
+}
+
+// Routing on refresh tokens: writes the state's route arrays directly.
+template <int D>
+__global__ void __launch_bounds__(256) decode_route_kernel(StepArgs a) {
+  const int r = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  TaoState& st = *a.states[r];
+  const long long t = st.position;
+  const int S = sealed_at(t);
+  if (S == 0 || !is_refresh(t, st.layer_index, a.pol)) return;
+  const int completed = S / kGroup, pending = S % kGroup;
+  const int P = completed + (pending > 0);
+  extern __shared__ __align__(128) uint8_t dsm[];
+  float* hq = reinterpret_cast<float*>(dsm);
+  float* pm = hq + D;
+  float* cm = pm + a.pmax;
+  int* cand_id = reinterpret_cast<int*>(cm + 8 * a.pmax + 8);
+  int* chosen = cand_id + 8 * a.pmax + 8;
+  int* sorted = chosen + a.pmax;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarp = blockDim.x >> 5;
+  const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
+  const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + h * pstride;
+  const bf16* pw = reinterpret_cast<const bf16*>(st.page_w) + h * pstride;
+  const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + (long long)h * st.cap_fines * D;
+  if (warp == 0) softmax_row<D>(a.raw_q + ((long long)r * a.H + h) * D, hq, lane);
+  __syncthreads();
+  const Counts cnt = routed_counts(completed, pending, a.pol);
+  const int K = cnt.coarse, U = cnt.eligible, M = cnt.selected;
+  if (M > st.route_cap || P > a.pmax) {
+    if (tid == 0) atomicOr(a.err, kErrRouteCap);
+    return;
+  }
+  if (K > 0) {
+    for (int p = warp; p < completed; p += nwarp) {
+      float s = 0.f;
+      for (int d = lane; d < D; d += 32) s += rb(__fmul_rn(hq[d], bf(pw[(long long)p * D + d])));
+      s = warp_sum(s);
+      if (lane == 0) pm[p] = rb(s);
+    }
+    __syncthreads();
+    for (int p = tid; p < completed; p += blockDim.x) {
+      const float v = pm[p];
+      int rank = 0;
+      for (int q = 0; q < completed; ++q) {
+        const float u = pm[q];
+        rank += (u > v) || (u == v && q < p);
+      }
+      if (rank < K) chosen[rank] = p;
+    }
+    __syncthreads();
+    for (int j = tid; j < K; j += blockDim.x) {
+      int pg = chosen[j], pos = 0;
+      for (int x = 0; x < K; ++x) pos += chosen[x] < pg;
+      sorted[pos] = pg;
+    }
+    __syncthreads();
+  }
+  for (int u = tid; u < U; u += blockDim.x)
+    cand_id[u] = (u < kGroup * K) ? sorted[u / kGroup] * kGroup + (u % kGroup)
+                                  : completed * kGroup + (u - kGroup * K);
+  __syncthreads();
+  for (int u = warp; u < U; u += nwarp) {
+    const int id = cand_id[u], page = id / kGroup;
+    float s = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const float hv = rb(__fmul_rn(hq[d], bf(pw[(long long)page * D + d])));
+      const float w = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
+      s += rb(__fmul_rn(hv, w));
+    }
+    s = warp_sum(s);
+    if (lane == 0) cm[u] = rb(s);
+  }
+  __syncthreads();
+  int32_t* ids = st.route_ids + (long long)h * st.route_cap;
+  int32_t* pgs = st.route_pages + (long long)h * st.route_cap;
+  for (int u = tid; u < U; u += blockDim.x) {
+    const float v = cm[u];
+    int rank = 0;
+    for (int q = 0; q < U; ++q) {
+      const float x = cm[q];
+      rank += (x > v) || (x == v && q < u);
+    }
+    if (rank < M) ids[rank] = cand_id[u];
+  }
+  for (int j = tid; j < K; j += blockDim.x) pgs[j] = sorted[j];
+  if (h == 0 && tid == 0) {
+    st.n_route = M;
+    st.n_chosen = K;
+    st.route_refreshes += 1;
+  }
+}
+
+// Seal after a decode step (the cursor has advanced): if the window now holds
+// 768 tokens, write the oldest block's fine and refresh the page memo.
+template <int D>
+__global__ void __launch_bounds__(256) decode_seal_kernel(StepArgs a) {
+  const int r = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  TaoState& st = *a.states[r];
+  const long long t = st.position - 1;  // the token just served
+  const long long start = window_start(t);
+  if (t + 1 - start != kWindow) return;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  const int S = sealed_at(t);
+  seal_block<D>(st, h, start, S, dsm);
+  refresh_memo<D>(st, h, S + 1, S / kGroup);
+  if (h == 0 && threadIdx.x == 0) st.seal_events += 1;
+}
+
+}  // namespace tao

@@ -30,7 +30,6 @@ __global__ void __launch_bounds__(128) writer_kernel(const bf16* __restrict__ ra
   const uint32_t sV = sP + NT * D * 2;       // [256][D]
   float* mx = reinterpret_cast<float*>(smem + 2 * NT * D * 2);
   float* zp = mx + D;
-  bf16* pk = reinterpret_cast<bf16*>(smem);
   const int s = blockIdx.x % dm.S, h = (blockIdx.x / dm.S) % dm.H, b = blockIdx.x / (dm.S * dm.H);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bf16* kb = raw_k + ((long long)b * dm.T + (long long)s * NT) * dm.row + (long long)h * D;
@@ -218,7 +217,6 @@ __global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
   const uint32_t sA = smem_u32(ptr);   ptr += 256 * D * 2;
   const uint32_t sC = smem_u32(ptr);   ptr += NBUF * D * D * 2;
   bf16* hS = reinterpret_cast<bf16*>(smem);
-  bf16* aS = hS + 256 * D;
   float* pwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   float* pzS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   bf16* swS = reinterpret_cast<bf16*>(ptr);    ptr += ((size_t)V * D * 2 + 15) / 16 * 16;

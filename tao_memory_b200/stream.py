@@ -141,11 +141,12 @@ class StreamCache:
             fine_c=z(heads, cap, width, width), fine_z=z(heads, cap, width),
             page_z=z(heads, pages, width), page_w=z(heads, pages, width),
             route_ids=z(heads, ROUTE_CAP, dt=torch.int32),
-            route_pages=z(heads, ROUTE_CAP, dt=torch.int32))
+            route_pages=z(heads, ROUTE_CAP, dt=torch.int32),
+            counters=z(heads, dt=torch.int32))
         self.heads, self.width, self.device, self.cap_fines = heads, width, device, cap
         h = _lib.TaoState()
         for name in ("k_ring", "v_ring", "rk_ring", "fine_c", "fine_z", "page_z", "page_w",
-                     "route_ids", "route_pages"):
+                     "route_ids", "route_pages", "counters"):
             setattr(h, name, self._buf[name].data_ptr())
         h.position = self.position
         h.cap_fines, h.route_cap, h.layer_index = cap, ROUTE_CAP, self.layer_index
@@ -377,9 +378,15 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
     nbytes = lib.tao_stream_workspace_bytes(r, w, heads, width, ROUTE_CAP, ctypes.byref(policy))
     ws = _Workspace.get(dev, nbytes)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    _lib.check(lib.tao_stream_step(ptrs.data_ptr(), r, pos, cap, ctypes.byref(policy), w, heads, width,
-                                   *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
-                                   float(alpha), out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
+    if w == 1:
+        layers = (ctypes.c_int32 * r)(*[st.layer_index for st in states])
+        _lib.check(lib.tao_decode_step(ptrs.data_ptr(), r, pos, layers, cap, ctypes.byref(policy), heads,
+                                       width, *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
+                                       float(alpha), out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
+    else:
+        _lib.check(lib.tao_stream_step(ptrs.data_ptr(), r, pos, cap, ctypes.byref(policy), w, heads, width,
+                                       *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
+                                       float(alpha), out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
     for st in states:
         hist = st.position >= WINDOW
         st._counters["fusion_pointwise_calls" if hist else "fusion_no_history_local_returns"] += 1
@@ -453,6 +460,7 @@ class BatchDecoder:
         self.r = len(self.states)
         self.pos = (ctypes.c_int64 * self.r)()
         self.cap = (ctypes.c_int32 * self.r)()
+        self.layers = (ctypes.c_int32 * self.r)(*[st.layer_index for st in self.states])
         nbytes = self.lib.tao_stream_workspace_bytes(self.r, 1, self.heads, self.width, ROUTE_CAP,
                                                      ctypes.byref(self.policy))
         self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.dev)
@@ -475,8 +483,8 @@ class BatchDecoder:
 
     def step(self, q, k, v, raw_q, raw_k, out, stream=None):
         s = torch.cuda.current_stream(self.dev).cuda_stream if stream is None else stream
-        _lib.check(self.lib.tao_stream_step(
-            self.ptrs.data_ptr(), self.r, self.pos, self.cap, ctypes.byref(self.policy), 1,
+        _lib.check(self.lib.tao_decode_step(
+            self.ptrs.data_ptr(), self.r, self.pos, self.layers, self.cap, ctypes.byref(self.policy),
             self.heads, self.width, q, k, v, raw_q, raw_k, self.fa.data_ptr(), self.fb.data_ptr(),
             self.alpha, out, self.ws.data_ptr(), self.ws.numel(), s))
         for i, st in enumerate(self.states):
