@@ -22,6 +22,9 @@ thread_local std::string g_last_error;
 // Events recorded around the main (HBM-bound) kernel of the next tao_stream_step
 // on this host thread; cleared after use.
 thread_local cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
+// Decode kernel choice: 2 = one warp per 8 KB item (default), 0 = warp-specialised
+// persistent, 1 = one CTA per item.
+int g_decode_variant = 2;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -94,7 +97,8 @@ Layout make_layout(int R, int w, int H, int D, int route_cap, int msplit_decode,
   L.slot_n = off;
   off = align256(off + (size_t)R * L.nslot * 2 * 4);
   L.local_part = off;
-  if (w == 1) off = align256(off + (size_t)R * H * L.kblocks * (D + 2) * 4);
+  // decode partials: room for the warp kernel's 768/(2048/D) local items per (r, h)
+  if (w == 1) off = align256(off + (size_t)R * H * (768 / (2048 / D)) * (D + 2) * 4);
   L.local_out = off;
   if (w > 1) off = align256(off + (size_t)R * w * H * D * 2);
   L.fine_part = off;
@@ -190,11 +194,27 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
   FusedArgs f{};
   f.s = a;
   f.ms = ms;
-  const size_t smem = FusedCfg<D>::STAGE;
-  if ((rc = set_smem(decode_fused_kernel<D>, smem))) return rc;
-  const int grid = a.R * a.H * (FusedCfg<D>::KB + ms);
+  const int total = a.R * a.H * (FusedCfg<D>::KB + ms);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
   if (g_prof_start) cudaEventRecord(g_prof_start, s);
-  decode_fused_kernel<D><<<grid, 128, smem, s>>>(f);
+  if (g_decode_variant == 2) {
+    const int wt = a.R * a.H * (WarpCfg<D>::LI + ms);
+    decode_warp_kernel<D><<<(wt + 7) / 8, 256, 0, s>>>(f);
+  } else if (g_decode_variant == 0) {
+    const size_t smem = (size_t)kWsStages * FusedCfg<D>::STAGE;
+    if ((rc = set_smem(decode_ws_kernel<D>, smem))) return rc;
+    decode_ws_kernel<D><<<total < sms ? total : sms, 288, smem, s>>>(f);
+  } else {
+    const size_t smem = FusedCfg<D>::STAGE;
+    if ((rc = set_smem(decode_fused_kernel<D>, smem))) return rc;
+    decode_fused_kernel<D><<<total, 128, smem, s>>>(f);
+  }
   if (g_prof_stop) cudaEventRecord(g_prof_stop, s);
   g_prof_start = g_prof_stop = nullptr;
   if ((rc = check_launch("decode_fused_kernel"))) return rc;
@@ -251,7 +271,8 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
   }
   const int route_cap = policy->route_cap;
   if (mbound > route_cap) mbound = route_cap;
-  const int fpc = fpc_for(width);
+  // fine partials per (r, h): one per selected fine (warp kernel) or per group of fpc
+  const int fpc = (g_decode_variant == 2) ? 1 : fpc_for(width);
   const int ms = (mbound + fpc - 1) / fpc;
   const Layout L = make_layout(n_states, 1, heads, width, route_cap, ms, policy->route_period);
   if (workspace_bytes < L.total) return fail(TAO_ERR_ARG, "workspace too small: %zu < %zu", workspace_bytes, L.total);
@@ -294,10 +315,8 @@ size_t tao_stream_workspace_bytes(int n_states, int tokens, int heads, int width
   if (n_states <= 0 || tokens <= 0 || heads <= 0 || (width != 64 && width != 128) ||
       route_cap <= 0 || !policy || policy->route_period <= 0)
     return 0;
-  const int fpc = fpc_for(width);
-  return make_layout(n_states, tokens, heads, width, route_cap, (route_cap + fpc - 1) / fpc,
-                     policy->route_period)
-      .total;
+  // one fine partial per selected fine covers every decode kernel variant
+  return make_layout(n_states, tokens, heads, width, route_cap, route_cap, policy->route_period).total;
 }
 
 int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
@@ -418,6 +437,12 @@ int tao_event_elapsed(void* start, void* stop, float* ms) {
 int tao_stream_profile_next(void* start, void* stop) {
   g_prof_start = static_cast<cudaEvent_t>(start);
   g_prof_stop = static_cast<cudaEvent_t>(stop);
+  return TAO_OK;
+}
+
+int tao_decode_variant(int variant) {
+  if (variant < 0 || variant > 2) return fail(TAO_ERR_ARG, "decode variant must be 0, 1 or 2");
+  g_decode_variant = variant;
   return TAO_OK;
 }
 

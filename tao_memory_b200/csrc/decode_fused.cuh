@@ -321,6 +321,560 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-specialised persistent variant: one CTA per SM, warp 8 produces (bulk
+// copies of the CTA's items into a ring of NS shared-memory stages, guarded by
+// full/empty mbarriers), warps 0-3 and 4-7 consume alternate items.  Loads of up
+// to NS items are in flight while two items are computed.  Same arithmetic and
+// arrival protocol as decode_fused_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kWsStages = 6;
+
+struct WsDesc {
+  int item, armed, nf;
+};
+
+TAO_DEVI void group_sync(int g) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(128) : "memory");
+}
+
+// Bounded wait by the group's first thread, broadcast to the group.
+TAO_DEVI bool group_wait(uint64_t* bar, uint32_t phase, int* err, int* flag, int g, int gtid) {
+  if (gtid == 0) *flag = mbar_wait(bar, phase, err) ? 1 : 0;
+  group_sync(g);
+  const bool ok = *flag != 0;
+  if (ok) {
+    while (!mbar_try_wait(bar, phase)) {
+    }
+  }
+  return ok;
+}
+
+template <int D>
+struct WsGroupScratch {
+  float qv[D];
+  float red[128 + 8];
+  float chs[FusedCfg<D>::FPC * D];
+  int flag;
+  int last;
+};
+
+template <int D>
+__global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
+  using Cfg = FusedCfg<D>;
+  constexpr int NS = kWsStages;
+  const StepArgs& a = f.s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ __align__(8) uint64_t full[NS], empty[NS];
+  __shared__ WsDesc desc[NS];
+  __shared__ WsGroupScratch<D> gs[2];
+  __shared__ int pflag;
+  const int per = Cfg::KB + f.ms;
+  const int total = a.R * a.H * per;
+  const int G = gridDim.x;
+  if (tid == 0) {
+    for (int x = 0; x < NS; ++x) {
+      mbar_init(&full[x], 1);
+      mbar_init(&empty[x], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0) return;
+    for (int j = 0;; ++j) {
+      const int i = blockIdx.x + j * G;
+      if (i >= total) break;
+      const int st_ = j % NS, use = j / NS;
+      if (use > 0 && !mbar_wait(&empty[st_], (use - 1) & 1, a.err)) return;
+      const Item it = item_of(i, a.R, a.H);
+      uint8_t* stage = dsm + (size_t)st_ * Cfg::STAGE;
+      desc[st_].item = i;
+      const uint32_t bytes = issue_item<D>(f, it, stage, &full[st_]);
+      desc[st_].armed = bytes;
+      if (bytes == 0) mbar_arrive(&full[st_]);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int g = warp >> 2, gtid = tid & 127, gwarp = warp & 3;
+  WsGroupScratch<D>& sc = gs[g];
+  for (int j = g;; j += 2) {
+    const int i = blockIdx.x + j * G;
+    if (i >= total) break;
+    const int st_ = j % NS, use = j / NS;
+    if (!group_wait(&full[st_], use & 1, a.err, &sc.flag, g, gtid)) return;
+    const bool armed = desc[st_].armed != 0;
+    uint8_t* stage = dsm + (size_t)st_ * Cfg::STAGE;
+    const Item it = item_of(i, a.R, a.H);
+    TaoState& st = *a.states[it.r];
+    const long long t = st.position;
+    const long long src = ((long long)it.r * a.H + it.h) * D;
+    if (it.slot < Cfg::KB) {
+      // ---------------------------------------------- local attention block
+      const int s0 = it.slot * Cfg::SLOTS;
+      float* part = a.local_part + (((long long)it.r * a.H + it.h) * Cfg::KB + it.slot) * (D + 2);
+      if (!armed) {
+        if (gtid == 0) { part[D] = -INFINITY; part[D + 1] = 0.f; }
+      } else {
+        const float sl = 1.4426950408889634f / sqrtf((float)D);
+        for (int d = gtid; d < D; d += 128) sc.qv[d] = bf(a.q[src + d]) * sl;
+        bf16* sk = reinterpret_cast<bf16*>(stage);
+        bf16* sv = sk + Cfg::SLOTS * D;
+        const int tm = (int)(t % kWindow);
+        if (tm >= s0 && tm < s0 + Cfg::SLOTS) {
+          for (int d = gtid; d < D / 8; d += 128) {
+            const uint4 kk = reinterpret_cast<const uint4*>(a.k + src)[d];
+            const uint4 vv = reinterpret_cast<const uint4*>(a.v + src)[d];
+            const uint4 rr = reinterpret_cast<const uint4*>(a.raw_k + src)[d];
+            reinterpret_cast<uint4*>(sk + (tm - s0) * D)[d] = kk;
+            reinterpret_cast<uint4*>(sv + (tm - s0) * D)[d] = vv;
+            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.k_ring) + ((long long)it.h * kWindow + tm) * D)[d] = kk;
+            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.v_ring) + ((long long)it.h * kWindow + tm) * D)[d] = vv;
+            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.rk_ring) + ((long long)it.h * kWindow + tm) * D)[d] = rr;
+          }
+        }
+        group_sync(g);
+        constexpr int TPK = 128 / Cfg::SLOTS;
+        const int key = gtid / TPK, pid = gtid % TPK;
+        float scv = 0.f;
+        {
+          const bf16* kr = sk + key * D;
+          constexpr int NCH = D / 8 / TPK;
+#pragma unroll
+          for (int x = 0; x < NCH; ++x) {
+            const int c = pid * NCH + ((x + key) % NCH);
+            float fv[8];
+            unpack8(*reinterpret_cast<const uint4*>(kr + c * 8), fv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) scv += fv[e] * sc.qv[c * 8 + e];
+          }
+          if (TPK == 2) scv += __shfl_xor_sync(0xffffffffu, scv, 1);
+        }
+        const long long kp = t - (long long)((tm - (s0 + key) + kWindow) % kWindow);
+        if (kp < window_start(t) || kp > t) scv = -INFINITY;
+        float mx = warp_max(scv);
+        if (lane == 0) sc.red[gwarp] = mx;
+        group_sync(g);
+        mx = fmaxf(fmaxf(sc.red[0], sc.red[1]), fmaxf(sc.red[2], sc.red[3]));
+        const float pk = (scv == -INFINITY) ? 0.f : exp2f(scv - mx);
+        const float ls = warp_sum(pid == 0 ? pk : 0.f);
+        if (pid == 0) sc.red[8 + key] = pk;
+        group_sync(g);
+        if (lane == 0) sc.red[4 + gwarp] = ls;
+        constexpr int ECH = D / 8, KG = 128 / ECH, KPG = Cfg::SLOTS / KG;
+        const int ec = gtid % ECH, kg = gtid / ECH;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int x = 0; x < KPG; ++x) {
+          const int kk = kg * KPG + x;
+          const float pj = sc.red[8 + kk];
+          float fv[8];
+          unpack8(*reinterpret_cast<const uint4*>(sv + kk * D + ec * 8), fv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += pj * fv[e];
+        }
+        float* rs = reinterpret_cast<float*>(stage);
+        group_sync(g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) rs[kg * D + ec * 8 + e] = acc[e];
+        group_sync(g);
+        for (int d = gtid; d < D; d += 128) {
+          float sum = 0.f;
+          for (int g2 = 0; g2 < KG; ++g2) sum += rs[g2 * D + d];
+          part[d] = sum;
+        }
+        if (gtid == 0) { part[D] = mx; part[D + 1] = sc.red[4] + sc.red[5] + sc.red[6] + sc.red[7]; }
+      }
+    } else if (armed) {
+      // ------------------------------------------------ selected fine group
+      const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
+      const int nf = min(Cfg::FPC, st.n_route - m0);
+      const int32_t* ids = st.route_ids + (long long)it.h * st.route_cap + m0;
+      const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
+      const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + (long long)it.h * st.cap_fines * D;
+      const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + it.h * pstride;
+      const bf16* pw = reinterpret_cast<const bf16*>(st.page_w) + it.h * pstride;
+      if (gwarp == 0) softmax_row<D>(a.raw_q + src, sc.qv, lane);
+      group_sync(g);
+      for (int x = gwarp; x < nf; x += 4) {
+        const int id = ids[x], page = id / kGroup;
+        float sum = 0.f;
+        for (int d = lane; d < D; d += 32) {
+          const float hv = rb(__fmul_rn(sc.qv[d], bf(pw[(long long)page * D + d])));
+          const float w = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
+          const float c = rb(__fmul_rn(hv, w));
+          sc.chs[x * D + d] = c;
+          sum += c;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) sc.red[x] = rb(sum);
+      }
+      group_sync(g);
+      constexpr int ECH = D / 8, RG = 128 / ECH, RPG = D / RG;
+      const int ec = gtid % ECH, rg = gtid / ECH;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      const bf16* cm = reinterpret_cast<const bf16*>(stage);
+      for (int x = 0; x < nf; ++x) {
+#pragma unroll
+        for (int y = 0; y < RPG; ++y) {
+          const int d = rg * RPG + y;
+          const float c = sc.chs[x * D + d];
+          float fv[8];
+          unpack8(*reinterpret_cast<const uint4*>(cm + x * D * D + d * D + ec * 8), fv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += c * fv[e];
+        }
+      }
+      group_sync(g);
+      float* rs = reinterpret_cast<float*>(stage);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rs[rg * D + ec * 8 + e] = acc[e];
+      group_sync(g);
+      float* part = a.fine_part + (((long long)it.r * a.H + it.h) * f.ms + (it.slot - Cfg::KB)) * (D + 1);
+      for (int d = gtid; d < D; d += 128) {
+        float sum = 0.f;
+        for (int g2 = 0; g2 < RG; ++g2) sum += rs[g2 * D + d];
+        part[d] = sum;
+      }
+      if (gtid == 0) {
+        float den = 0.f;
+        for (int x = 0; x < nf; ++x) den += sc.red[x];
+        part[D] = den;
+      }
+    }
+    // ---- release the stage, then arrival
+    group_sync(g);
+    if (gtid == 0) {
+      mbar_arrive(&empty[st_]);
+      __threadfence();
+      sc.last = (atomicAdd(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
+      if (sc.last) st.counters[it.h] = 0;
+      __threadfence();
+    }
+    group_sync(g);
+    if (!sc.last) continue;
+    const bool hist = t >= kWindow;
+    const int M = st.n_route;
+    const int nparts = (M + Cfg::FPC - 1) / Cfg::FPC;
+    const float* lp = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
+    const float* fp = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
+    for (int d = gtid; d < D; d += 128) {
+      float Mx = -INFINITY;
+      for (int b2 = 0; b2 < Cfg::KB; ++b2) Mx = fmaxf(Mx, __ldcg(lp + b2 * (D + 2) + D));
+      float L = 0.f, O = 0.f;
+      for (int b2 = 0; b2 < Cfg::KB; ++b2) {
+        const float mb = __ldcg(lp + b2 * (D + 2) + D);
+        if (mb == -INFINITY) continue;
+        const float scl = exp2f(mb - Mx);
+        L += scl * __ldcg(lp + b2 * (D + 2) + D + 1);
+        O += scl * __ldcg(lp + b2 * (D + 2) + d);
+      }
+      const float local = rb(O / L);
+      float outv = local;
+      if (hist) {
+        float acc = 0.f, den = 0.f;
+        for (int p2 = 0; p2 < nparts; ++p2) {
+          acc += __ldcg(fp + p2 * (D + 1) + d);
+          den += __ldcg(fp + p2 * (D + 1) + D);
+        }
+        const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
+        const float qq = bf(a.raw_q[src + d]);
+        const bf16* fa = a.fa + ((long long)it.h * D + d) * 3;
+        const bf16* fb = a.fb + ((long long)it.h * D + d) * 3;
+        const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), qq)), bf(fb[0]))), 0.f));
+        const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), qq)), bf(fb[2])));
+        const float mx = fmaxf(s0, s2);
+        const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
+        const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
+        const float lt = rb(__fmul_rn(rho0, rb(__fmul_rn(2.f, local))));
+        const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(a.gain, fine))));
+        outv = rb(__fadd_rn(rb(__fadd_rn(lt, 0.f)), ft));
+      }
+      a.out[src + d] = tobf(outv);
+    }
+    group_sync(g);
+    if (gtid == 0) {
+      __threadfence();
+      if (atomicAdd(&st.arrive, 1) == a.H - 1) {
+        st.arrive = 0;
+        st.position = t + 1;
+        __threadfence();
+      }
+    }
+  }
+  (void)pflag;
+}
+
+// ---------------------------------------------------------------------------
+// Warp-granular variant: one warp per 8 KB work item, no block barriers.
+//   local item  : KPW consecutive ring slots (32 keys for D64, 16 for D128): 4 KB
+//                 of K and 4 KB of V read with 16-byte vector loads into registers
+//   fine item   : one selected fine matrix in 4 KB slices, two slices in flight
+//                 (8 KB for D64, 32 KB for D128)
+// Lane l of a 512-byte warp load holds row (l / CPR) and 16-byte chunk (l % CPR)
+// of that slice (CPR = D/8 chunks per row).  Partials go to the workspace; the
+// warp completing the last item of (r, h) combines and fuses; the warp completing
+// the last head of request r advances its cursor.
+// ---------------------------------------------------------------------------
+template <int D>
+struct WarpCfg {
+  static constexpr int CPR = D / 8;              // 16-byte chunks per row
+  static constexpr int RPL = 32 / CPR;           // rows per 512-byte warp load
+  static constexpr int KPW = 4096 / (D * 2);     // rows per 4 KB slice (keys per local item)
+  static constexpr int LI = kWindow / KPW;       // local items per (r, h): 24 (D64) / 48 (D128)
+  static constexpr int LOADS = KPW / RPL;        // 512-byte warp loads per 4 KB slice (8)
+  static constexpr int FCH = D / KPW;            // 4 KB slices of a fine matrix: 2 / 8
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) decode_warp_kernel(FusedArgs f) {
+  using W = WarpCfg<D>;
+  const StepArgs& a = f.s;
+  const int lane = threadIdx.x & 31;
+  const int per = W::LI + f.ms;
+  const int total = a.R * a.H * per;
+  const int wi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (wi >= total) return;
+  const Item it = item_of(wi, a.R, a.H);
+  TaoState& st = *a.states[it.r];
+  const long long t = st.position;
+  const long long src = ((long long)it.r * a.H + it.h) * D;
+  const int row = lane / W::CPR, chunk = lane % W::CPR;
+  if (it.slot < W::LI) {
+    // ---------------------------------------------------- local attention item
+    const int s0 = it.slot * W::KPW;
+    const int tm = (int)(t % kWindow);
+    const long long start = window_start(t);
+    float* part = a.local_part + (((long long)it.r * a.H + it.h) * W::LI + it.slot) * (D + 2);
+    const bf16* kr = ring_head<D>(st.k_ring, it.h) + (long long)s0 * D;
+    const bf16* vr = ring_head<D>(st.v_ring, it.h) + (long long)s0 * D;
+    if (!local_block_live<D>(t, start, s0, W::KPW)) {
+      if (lane == 0) { part[D] = -INFINITY; part[D + 1] = 0.f; }
+    } else {
+      uint4 kv[W::LOADS], vv[W::LOADS];
+#pragma unroll
+      for (int x = 0; x < W::LOADS; ++x) {
+        kv[x] = __ldcs(reinterpret_cast<const uint4*>(kr + (x * W::RPL + row) * D) + chunk);
+        vv[x] = __ldcs(reinterpret_cast<const uint4*>(vr + (x * W::RPL + row) * D) + chunk);
+      }
+      const uint4 qc = *(reinterpret_cast<const uint4*>(a.q + src) + chunk);
+      // the current token: use (and append) the new k / v
+      const bool own = tm >= s0 && tm < s0 + W::KPW;
+      if (own) {
+        const uint4 nk = *(reinterpret_cast<const uint4*>(a.k + src) + chunk);
+        const uint4 nv = *(reinterpret_cast<const uint4*>(a.v + src) + chunk);
+        const int x0 = (tm - s0) / W::RPL, r0 = (tm - s0) % W::RPL;
+#pragma unroll
+        for (int x = 0; x < W::LOADS; ++x)
+          if (x == x0 && row == r0) { kv[x] = nk; vv[x] = nv; }
+        if (row == 0) {
+          const uint4 nr = *(reinterpret_cast<const uint4*>(a.raw_k + src) + chunk);
+          const long long off = ((long long)it.h * kWindow + tm) * D;
+          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.k_ring) + off)[chunk] = nk;
+          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.v_ring) + off)[chunk] = nv;
+          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.rk_ring) + off)[chunk] = nr;
+        }
+      }
+      float qf[8];
+      unpack8(qc, qf);
+      const float sl = 1.4426950408889634f / sqrtf((float)D);
+      float sc[W::LOADS];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int x = 0; x < W::LOADS; ++x) {
+        float kf[8];
+        unpack8(kv[x], kf);
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dot += kf[e] * qf[e];
+#pragma unroll
+        for (int o = W::CPR / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const int key = s0 + x * W::RPL + row;
+        const long long kp = t - (long long)((tm - key + kWindow) % kWindow);
+        sc[x] = (kp < start || kp > t) ? -INFINITY : dot * sl;
+        mx = fmaxf(mx, sc[x]);
+      }
+      mx = warp_max(mx);
+      float lsum = 0.f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int x = 0; x < W::LOADS; ++x) {
+        const float p = (sc[x] == -INFINITY) ? 0.f : exp2f(sc[x] - mx);
+        lsum += (chunk == 0) ? p : 0.f;
+        float vf[8];
+        unpack8(vv[x], vf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += p * vf[e];
+      }
+      lsum = warp_sum(lsum);
+#pragma unroll
+      for (int o = 16; o >= W::CPR; o >>= 1)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+      if (row == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part[chunk * 8 + e] = acc[e];
+      }
+      if (lane == 0) { part[D] = mx; part[D + 1] = lsum; }
+    }
+  } else if (t >= kWindow) {
+    // ---------------------------------------------------- selected fine item
+    const int m = it.slot - W::LI;
+    if (m < st.n_route) {
+      const int id = st.route_ids[(long long)it.h * st.route_cap + m];
+      const int page = id / kGroup;
+      const bf16* cmat = reinterpret_cast<const bf16*>(st.fine_c) + ((long long)it.h * st.cap_fines + id) * D * D;
+      constexpr int CHUNKS = W::FCH;
+      uint4 cv[2][W::LOADS];
+#pragma unroll
+      for (int x = 0; x < W::LOADS; ++x)
+        cv[0][x] = __ldcs(reinterpret_cast<const uint4*>(cmat + (x * W::RPL + row) * D) + chunk);
+      if (CHUNKS > 1) {
+#pragma unroll
+        for (int x = 0; x < W::LOADS; ++x)
+          cv[1][x] = __ldcs(reinterpret_cast<const uint4*>(cmat + (W::KPW + x * W::RPL + row) * D) + chunk);
+      }
+      // channels: ch[d] = bf16(bf16(h*pw) * bf16(exp(bf16(z - pz)))) for d = lane + 32 j
+      const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
+      const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + ((long long)it.h * st.cap_fines + id) * D;
+      const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + it.h * pstride + (long long)page * D;
+      const bf16* pw = reinterpret_cast<const bf16*>(st.page_w) + it.h * pstride + (long long)page * D;
+      float hq[D / 32];
+      {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) { hq[j] = bf(a.raw_q[src + lane + 32 * j]); mx = fmaxf(mx, hq[j]); }
+        mx = warp_max(mx);
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) { hq[j] = expf(hq[j] - mx); s += hq[j]; }
+        s = warp_sum(s);
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) hq[j] = rb(__fdiv_rn(hq[j], s));
+      }
+      float ch[D / 32], den = 0.f;
+#pragma unroll
+      for (int j = 0; j < D / 32; ++j) {
+        const int d = lane + 32 * j;
+        const float hv = rb(__fmul_rn(hq[j], bf(pw[d])));
+        const float w = rb(expf(rb(__fsub_rn(bf(fz[d]), bf(pz[d])))));
+        ch[j] = rb(__fmul_rn(hv, w));
+        den += ch[j];
+      }
+      den = warp_sum(den);
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int c = 0; c < CHUNKS; ++c) {
+        const int cb = c & 1;
+#pragma unroll
+        for (int x = 0; x < W::LOADS; ++x) {
+          // matrix row of this lane; rows of one load never cross a 32-row boundary
+          const int d = c * W::KPW + x * W::RPL + row;
+          constexpr int JJ = 0;
+          const float chd = __shfl_sync(0xffffffffu, ch[((c * W::KPW + x * W::RPL) >> 5) + JJ], d & 31);
+          float cf[8];
+          unpack8(cv[cb][x], cf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += chd * cf[e];
+        }
+        if (c + 2 < CHUNKS) {
+#pragma unroll
+          for (int x = 0; x < W::LOADS; ++x)
+            cv[cb][x] = __ldcs(reinterpret_cast<const uint4*>(cmat + ((c + 2) * W::KPW + x * W::RPL + row) * D) + chunk);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o >= W::CPR; o >>= 1)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+      float* part = a.fine_part + (((long long)it.r * a.H + it.h) * f.ms + m) * (D + 1);
+      if (row == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part[chunk * 8 + e] = acc[e];
+      }
+      if (lane == 0) part[D] = rb(den);
+    }
+  }
+  // ---- arrival; the warp completing (r, h) combines and fuses
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    __threadfence();
+    last = (atomicAdd(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
+    if (last) st.counters[it.h] = 0;
+    __threadfence();
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  const bool hist = t >= kWindow;
+  const int M = st.n_route;
+  const float* lp = a.local_part + ((long long)it.r * a.H + it.h) * W::LI * (D + 2);
+  const float* fp = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
+  float Mx = -INFINITY;
+  for (int b2 = lane; b2 < W::LI; b2 += 32) Mx = fmaxf(Mx, __ldcg(lp + b2 * (D + 2) + D));
+  Mx = warp_max(Mx);
+  float sc2[W::LI / 32 + 1];
+  float L = 0.f;
+#pragma unroll
+  for (int x = 0; x < W::LI / 32 + 1; ++x) {
+    const int b2 = lane + 32 * x;
+    float v = 0.f;
+    if (b2 < W::LI) {
+      const float mb = __ldcg(lp + b2 * (D + 2) + D);
+      v = (mb == -INFINITY) ? 0.f : exp2f(mb - Mx);
+      L += v * __ldcg(lp + b2 * (D + 2) + D + 1);
+    }
+    sc2[x] = v;
+  }
+  L = warp_sum(L);
+  float den = 0.f;
+  if (hist) {
+    for (int m2 = lane; m2 < M; m2 += 32) den += __ldcg(fp + m2 * (D + 1) + D);
+    den = warp_sum(den);
+  }
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) {
+    const int d = lane + 32 * j;
+    float O = 0.f;
+    for (int b2 = 0; b2 < W::LI; ++b2) {
+      const float w = __shfl_sync(0xffffffffu, sc2[b2 >> 5], b2 & 31);
+      if (w != 0.f) O += w * __ldcg(lp + b2 * (D + 2) + d);
+    }
+    const float local = rb(O / L);
+    float outv = local;
+    if (hist) {
+      float acc = 0.f;
+      for (int m2 = 0; m2 < M; ++m2) acc += __ldcg(fp + m2 * (D + 1) + d);
+      const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
+      const float qq = bf(a.raw_q[src + d]);
+      const bf16* fa = a.fa + ((long long)it.h * D + d) * 3;
+      const bf16* fb = a.fb + ((long long)it.h * D + d) * 3;
+      const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), qq)), bf(fb[0]))), 0.f));
+      const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), qq)), bf(fb[2])));
+      const float mx = fmaxf(s0, s2);
+      const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
+      const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
+      const float lt = rb(__fmul_rn(rho0, rb(__fmul_rn(2.f, local))));
+      const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(a.gain, fine))));
+      outv = rb(__fadd_rn(rb(__fadd_rn(lt, 0.f)), ft));
+    }
+    a.out[src + d] = tobf(outv);
+  }
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    if (atomicAdd(&st.arrive, 1) == a.H - 1) {
+      st.arrive = 0;
+      st.position = t + 1;
+      __threadfence();
+    }
+  }
+}
+
 // Routing on refresh tokens: writes the state's route arrays directly.
 template <int D>
 __global__ void __launch_bounds__(256) decode_route_kernel(StepArgs a) {
