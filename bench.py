@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--context", type=int, default=CONTEXT)
     ap.add_argument("--cpu-sample-steps", type=int, default=4)
     ap.add_argument("--workload", default="decode128k", choices=["decode128k", "train8k"])
+    ap.add_argument("--decode-variant", type=int, default=None,
+                    help="decode kernel of tao_decode_step (0 persistent, 1 CTA/item, 2 warp/item)")
     return ap.parse_args()
 
 
@@ -171,6 +173,8 @@ def run_b200(args, world, rank, local):
     torch.cuda.set_device(device)
     R, K, W = args.requests, args.steps, args.warmup
     lib = _lib.lib()
+    if args.decode_variant is not None:
+        _lib.check(lib.tao_decode_variant(args.decode_variant))
     stream = torch.cuda.current_stream(device).cuda_stream
 
     t0 = time.time()
@@ -291,7 +295,7 @@ def run_b200(args, world, rank, local):
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": 5 * R * HEADS * WIDTH * 2,
                 "d2h_bytes_per_step": R * HEADS * WIDTH * 2},
-        "roofline": {"bound": "hbm", "kernel": "decode_fused_kernel<64>",
+        "roofline": {"bound": "hbm", "kernel": "tao_decode_step main kernel (variant %s)" % (1 if args.decode_variant is None else args.decode_variant),
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": int(statistics.mean(algo_bytes)),

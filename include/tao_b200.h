@@ -128,9 +128,9 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
                     const void* fusion_b, float alpha, void* out, void* workspace,
                     size_t workspace_bytes, void* stream);
 
-/* Select the decode kernel of tao_decode_step for this process: 2 = one warp per
- * 8 KB work item (default), 0 = warp-specialised persistent kernel, 1 = one CTA
- * per work item.  Results agree to fp32 summation order. */
+/* Select the decode kernel of tao_decode_step for this process: 1 = one CTA per work
+ * item (default), 0 = warp-specialised persistent kernel, 2 = one warp per 8 KB
+ * work item.  Results agree to fp32 summation order. */
 int tao_decode_variant(int variant);
 
 /* Read and clear the device error word of a workspace (synchronises `stream`).

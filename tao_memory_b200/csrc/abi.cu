@@ -22,9 +22,9 @@ thread_local std::string g_last_error;
 // Events recorded around the main (HBM-bound) kernel of the next tao_stream_step
 // on this host thread; cleared after use.
 thread_local cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
-// Decode kernel choice: 2 = one warp per 8 KB item (default), 0 = warp-specialised
-// persistent, 1 = one CTA per item.
-int g_decode_variant = 2;
+// Decode kernel choice: 1 = one CTA per item (default), 0 = warp-specialised
+// persistent, 2 = one warp per 8 KB item.
+int g_decode_variant = 1;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -207,9 +207,13 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
     const int wt = a.R * a.H * (WarpCfg<D>::LI + ms);
     decode_warp_kernel<D><<<(wt + 7) / 8, 256, 0, s>>>(f);
   } else if (g_decode_variant == 0) {
-    const size_t smem = (size_t)kWsStages * FusedCfg<D>::STAGE;
+    if (a.R > kWsMaxReq) return fail(TAO_ERR_ARG, "decode variant 0 takes at most %d requests per call", kWsMaxReq);
+    const size_t smem = (size_t)kWsStages * WsLayout<D>::STAGE;
     if ((rc = set_smem(decode_ws_kernel<D>, smem))) return rc;
-    decode_ws_kernel<D><<<total < sms ? total : sms, 288, smem, s>>>(f);
+    int grid = total < sms ? total : sms;
+    const int need = (total + kWsMaxItems - 1) / kWsMaxItems;
+    if (grid < need) grid = need;
+    decode_ws_kernel<D><<<grid, 288, smem, s>>>(f);
   } else {
     const size_t smem = FusedCfg<D>::STAGE;
     if ((rc = set_smem(decode_fused_kernel<D>, smem))) return rc;

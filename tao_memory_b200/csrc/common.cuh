@@ -99,6 +99,15 @@ TAO_DEVI bool mbar_wait(uint64_t* bar, uint32_t phase, int* err) {
   return false;
 }
 
+// Arrival counters: a release-ordered add (the CTA's earlier writes, ordered by a
+// preceding barrier, become visible first) and an acquire fence for the winner.
+TAO_DEVI int atomic_add_release(int* p, int v) {
+  int old;
+  asm volatile("atom.add.release.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+TAO_DEVI void fence_acquire() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // Integer schedule (reference tao_stream.py:29-37, config.py:54-60,
 // tao_stream.py:196-227, 914-917, 959-967).

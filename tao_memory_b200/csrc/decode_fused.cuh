@@ -264,36 +264,50 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   // ---- arrival: the CTA completing the last item of (r, h) finalises it
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    last_rh = (atomicAdd(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
-    if (last_rh) st.counters[it.h] = 0;
-    __threadfence();
+    last_rh = (atomic_add_release(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
+    if (last_rh) {
+      st.counters[it.h] = 0;
+      fence_acquire();
+    }
   }
   __syncthreads();
   if (!last_rh) return;
   const bool hist = t >= kWindow;
   const int M = st.n_route;
-  const int nparts = (M + Cfg::FPC - 1) / Cfg::FPC;
-  const float* lp = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
-  const float* fp = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
+  const int nparts = hist ? (M + Cfg::FPC - 1) / Cfg::FPC : 0;
+  // stage all partials of (r, h) in shared memory with one round of coalesced loads
+  float* lp = reinterpret_cast<float*>(dsm);                 // [KB][D+2]
+  float* fp = lp + Cfg::KB * (D + 2);                        // [staged][D+1]
+  const float* fg = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
+  const int room = (Cfg::STAGE / 4 - Cfg::KB * (D + 2)) / (D + 1);
+  const int staged = nparts < room ? nparts : room;          // the rest is read from L2
+  {
+    const float* lg = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
+    for (int x = tid; x < Cfg::KB * (D + 2); x += 128) lp[x] = __ldcg(lg + x);
+    for (int x = tid; x < staged * (D + 1); x += 128) fp[x] = __ldcg(fg + x);
+  }
+  __syncthreads();
+  auto fpart = [&](int p2, int x) -> float {
+    return p2 < staged ? fp[p2 * (D + 1) + x] : __ldcg(fg + p2 * (D + 1) + x);
+  };
   for (int d = tid; d < D; d += 128) {
     float Mx = -INFINITY;
-    for (int b2 = 0; b2 < Cfg::KB; ++b2) Mx = fmaxf(Mx, __ldcg(lp + b2 * (D + 2) + D));
+    for (int b2 = 0; b2 < Cfg::KB; ++b2) Mx = fmaxf(Mx, lp[b2 * (D + 2) + D]);
     float L = 0.f, O = 0.f;
     for (int b2 = 0; b2 < Cfg::KB; ++b2) {
-      const float mb = __ldcg(lp + b2 * (D + 2) + D);
+      const float mb = lp[b2 * (D + 2) + D];
       if (mb == -INFINITY) continue;
       const float scl = exp2f(mb - Mx);
-      L += scl * __ldcg(lp + b2 * (D + 2) + D + 1);
-      O += scl * __ldcg(lp + b2 * (D + 2) + d);
+      L += scl * lp[b2 * (D + 2) + D + 1];
+      O += scl * lp[b2 * (D + 2) + d];
     }
     const float local = rb(O / L);
     float outv = local;
     if (hist) {
       float acc = 0.f, den = 0.f;
       for (int p2 = 0; p2 < nparts; ++p2) {
-        acc += __ldcg(fp + p2 * (D + 1) + d);
-        den += __ldcg(fp + p2 * (D + 1) + D);
+        acc += fpart(p2, d);
+        den += fpart(p2, D);
       }
       const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
       const float qq = bf(a.raw_q[src + d]);
@@ -312,33 +326,56 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   }
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(&st.arrive, 1) == a.H - 1) {
+    if (atomic_add_release(&st.arrive, 1) == a.H - 1) {
+      fence_acquire();
       st.arrive = 0;
       st.position = t + 1;
-      __threadfence();
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// Warp-specialised persistent variant: one CTA per SM, warp 8 produces (bulk
-// copies of the CTA's items into a ring of NS shared-memory stages, guarded by
-// full/empty mbarriers), warps 0-3 and 4-7 consume alternate items.  Loads of up
-// to NS items are in flight while two items are computed.  Same arithmetic and
-// arrival protocol as decode_fused_kernel.
+// Warp-specialised persistent variant: each CTA owns up to kWsMaxItems items.
+//  * start: request descriptors -> shared memory; the 32 producer lanes build
+//    every item's metadata in parallel (route ids included)
+//  * warp 8 lane 0 streams each item into a ring of NS stages: the big tile
+//    (K|V rows or selected matrices) plus the small rows the item needs (q or
+//    raw_q, fine z / page z / page weight rows, the new token's k / v / raw k),
+//    all as bulk copies on the stage's full mbarrier
+//  * warps 0-3 and 4-7 consume alternate items from shared memory only, release
+//    the stage (empty mbarrier) and follow the same arrival / combine protocol
 // ---------------------------------------------------------------------------
 constexpr int kWsStages = 6;
+constexpr int kWsMaxItems = 64;
+constexpr int kWsMaxReq = 64;
 
-struct WsDesc {
-  int item, armed, nf;
+struct ReqCache {
+  const bf16 *k, *v, *rk, *fc, *fz, *pz, *pw;
+  const int32_t* ids;
+  int32_t* counters;
+  TaoState* st;
+  long long t;
+  int n_route, cap, route_cap, pages;
+};
+
+template <int D>
+struct WsMeta {
+  int r, h, slot, nf, armed, own;
+  int ids[FusedCfg<D>::FPC];
+};
+
+template <int D>
+struct WsLayout {
+  static constexpr int MAIN = 32768;                 // K|V tile or selected matrices
+  static constexpr int ROW = D * 2;                  // one bf16 row
+  static constexpr int AUX = ROW * (1 + 3 + 3 * FusedCfg<D>::FPC);
+  static constexpr int STAGE = MAIN + ((AUX + 127) / 128) * 128;
 };
 
 TAO_DEVI void group_sync(int g) {
   asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(128) : "memory");
 }
 
-// Bounded wait by the group's first thread, broadcast to the group.
 TAO_DEVI bool group_wait(uint64_t* bar, uint32_t phase, int* err, int* flag, int g, int gtid) {
   if (gtid == 0) *flag = mbar_wait(bar, phase, err) ? 1 : 0;
   group_sync(g);
@@ -362,17 +399,19 @@ struct WsGroupScratch {
 template <int D>
 __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
   using Cfg = FusedCfg<D>;
+  using LY = WsLayout<D>;
   constexpr int NS = kWsStages;
   const StepArgs& a = f.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ __align__(8) uint64_t full[NS], empty[NS];
-  __shared__ WsDesc desc[NS];
+  __shared__ ReqCache rq[kWsMaxReq];
+  __shared__ WsMeta<D> meta[kWsMaxItems];
   __shared__ WsGroupScratch<D> gs[2];
-  __shared__ int pflag;
   const int per = Cfg::KB + f.ms;
   const int total = a.R * a.H * per;
   const int G = gridDim.x;
+  const int nitems = (total - (int)blockIdx.x + G - 1) / G;
   if (tid == 0) {
     for (int x = 0; x < NS; ++x) {
       mbar_init(&full[x], 1);
@@ -380,62 +419,129 @@ __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
     }
     fence_mbar_init();
   }
+  for (int r = tid; r < a.R; r += blockDim.x) {
+    TaoState* st = a.states[r];
+    ReqCache c;
+    c.k = reinterpret_cast<const bf16*>(st->k_ring);
+    c.v = reinterpret_cast<const bf16*>(st->v_ring);
+    c.rk = reinterpret_cast<const bf16*>(st->rk_ring);
+    c.fc = reinterpret_cast<const bf16*>(st->fine_c);
+    c.fz = reinterpret_cast<const bf16*>(st->fine_z);
+    c.pz = reinterpret_cast<const bf16*>(st->page_z);
+    c.pw = reinterpret_cast<const bf16*>(st->page_w);
+    c.ids = st->route_ids;
+    c.counters = st->counters;
+    c.st = st;
+    c.t = st->position;
+    c.n_route = st->n_route;
+    c.cap = st->cap_fines;
+    c.route_cap = st->route_cap;
+    c.pages = st->cap_fines / kGroup + 1;
+    rq[r] = c;
+  }
   __syncthreads();
 
   if (warp == 8) {
-    // ------------------------------------------------------------ producer
+    // ---------------------------------------------------------- producer
+    for (int j = lane; j < nitems; j += 32) {
+      const Item it = item_of(blockIdx.x + j * G, a.R, a.H);
+      const ReqCache& c = rq[it.r];
+      WsMeta<D> m;
+      m.r = it.r; m.h = it.h; m.slot = it.slot; m.nf = 0; m.own = 0; m.armed = 0;
+      if (it.slot < Cfg::KB) {
+        const int s0 = it.slot * Cfg::SLOTS;
+        const int tm = (int)(c.t % kWindow);
+        m.armed = local_block_live<D>(c.t, window_start(c.t), s0, Cfg::SLOTS) ? 1 : 0;
+        m.own = (tm >= s0 && tm < s0 + Cfg::SLOTS) ? 1 : 0;
+      } else if (c.t >= kWindow) {
+        const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
+        m.nf = max(0, min(Cfg::FPC, c.n_route - m0));
+        for (int x = 0; x < m.nf; ++x) m.ids[x] = c.ids[(long long)it.h * c.route_cap + m0 + x];
+        m.armed = m.nf > 0;
+      }
+      meta[j] = m;
+    }
+    __syncwarp();
     if (lane != 0) return;
-    for (int j = 0;; ++j) {
-      const int i = blockIdx.x + j * G;
-      if (i >= total) break;
-      const int st_ = j % NS, use = j / NS;
-      if (use > 0 && !mbar_wait(&empty[st_], (use - 1) & 1, a.err)) return;
-      const Item it = item_of(i, a.R, a.H);
-      uint8_t* stage = dsm + (size_t)st_ * Cfg::STAGE;
-      desc[st_].item = i;
-      const uint32_t bytes = issue_item<D>(f, it, stage, &full[st_]);
-      desc[st_].armed = bytes;
-      if (bytes == 0) mbar_arrive(&full[st_]);
+    for (int j = 0; j < nitems; ++j) {
+      const int sj = j % NS, use = j / NS;
+      if (use > 0 && !mbar_wait(&empty[sj], (use - 1) & 1, a.err)) return;
+      const WsMeta<D>& m = meta[j];
+      if (!m.armed) {
+        mbar_arrive(&full[sj]);
+        continue;
+      }
+      const ReqCache& c = rq[m.r];
+      uint8_t* stage = dsm + (size_t)sj * LY::STAGE;
+      uint8_t* aux = stage + LY::MAIN;
+      const long long src = ((long long)m.r * a.H + m.h) * D;
+      if (m.slot < Cfg::KB) {
+        const uint32_t bytes = Cfg::SLOTS * D * 2;
+        const long long hoff = (long long)m.h * kWindow * D + (long long)m.slot * Cfg::SLOTS * D;
+        mbar_expect_tx(&full[sj], 2 * bytes + LY::ROW * (m.own ? 4 : 1));
+        bulk_g2s(stage, c.k + hoff, bytes, &full[sj]);
+        bulk_g2s(stage + bytes, c.v + hoff, bytes, &full[sj]);
+        bulk_g2s(aux, a.q + src, LY::ROW, &full[sj]);
+        if (m.own) {
+          bulk_g2s(aux + LY::ROW, a.k + src, LY::ROW, &full[sj]);
+          bulk_g2s(aux + 2 * LY::ROW, a.v + src, LY::ROW, &full[sj]);
+          bulk_g2s(aux + 3 * LY::ROW, a.raw_k + src, LY::ROW, &full[sj]);
+        }
+      } else {
+        const uint32_t mbytes = D * D * 2;
+        mbar_expect_tx(&full[sj], m.nf * (mbytes + 3 * LY::ROW) + LY::ROW);
+        const long long zb = (long long)m.h * c.cap * D;
+        const long long pb = (long long)m.h * c.pages * D;
+        bulk_g2s(aux, a.raw_q + src, LY::ROW, &full[sj]);
+        for (int x = 0; x < m.nf; ++x) {
+          const int id = m.ids[x], page = id / kGroup;
+          bulk_g2s(stage + x * mbytes, c.fc + ((long long)m.h * c.cap + id) * D * D, mbytes, &full[sj]);
+          uint8_t* rows = aux + LY::ROW * (1 + 3 * x);
+          bulk_g2s(rows, c.fz + zb + (long long)id * D, LY::ROW, &full[sj]);
+          bulk_g2s(rows + LY::ROW, c.pz + pb + (long long)page * D, LY::ROW, &full[sj]);
+          bulk_g2s(rows + 2 * LY::ROW, c.pw + pb + (long long)page * D, LY::ROW, &full[sj]);
+        }
+      }
     }
     return;
   }
 
-  // -------------------------------------------------------------- consumers
+  // ------------------------------------------------------------ consumers
   const int g = warp >> 2, gtid = tid & 127, gwarp = warp & 3;
   WsGroupScratch<D>& sc = gs[g];
-  for (int j = g;; j += 2) {
-    const int i = blockIdx.x + j * G;
-    if (i >= total) break;
-    const int st_ = j % NS, use = j / NS;
-    if (!group_wait(&full[st_], use & 1, a.err, &sc.flag, g, gtid)) return;
-    const bool armed = desc[st_].armed != 0;
-    uint8_t* stage = dsm + (size_t)st_ * Cfg::STAGE;
-    const Item it = item_of(i, a.R, a.H);
-    TaoState& st = *a.states[it.r];
-    const long long t = st.position;
-    const long long src = ((long long)it.r * a.H + it.h) * D;
-    if (it.slot < Cfg::KB) {
+  for (int j = g; j < nitems; j += 2) {
+    const int sj = j % NS, use = j / NS;
+    if (!group_wait(&full[sj], use & 1, a.err, &sc.flag, g, gtid)) return;
+    const WsMeta<D>& m = meta[j];
+    const ReqCache& c = rq[m.r];
+    uint8_t* stage = dsm + (size_t)sj * LY::STAGE;
+    const bf16* aux = reinterpret_cast<const bf16*>(stage + LY::MAIN);
+    const long long t = c.t;
+    const long long src = ((long long)m.r * a.H + m.h) * D;
+    if (m.slot < Cfg::KB) {
       // ---------------------------------------------- local attention block
-      const int s0 = it.slot * Cfg::SLOTS;
-      float* part = a.local_part + (((long long)it.r * a.H + it.h) * Cfg::KB + it.slot) * (D + 2);
-      if (!armed) {
+      float* part = a.local_part + (((long long)m.r * a.H + m.h) * Cfg::KB + m.slot) * (D + 2);
+      if (!m.armed) {
         if (gtid == 0) { part[D] = -INFINITY; part[D + 1] = 0.f; }
       } else {
+        const int s0 = m.slot * Cfg::SLOTS;
         const float sl = 1.4426950408889634f / sqrtf((float)D);
-        for (int d = gtid; d < D; d += 128) sc.qv[d] = bf(a.q[src + d]) * sl;
+        for (int d = gtid; d < D; d += 128) sc.qv[d] = bf(aux[d]) * sl;
         bf16* sk = reinterpret_cast<bf16*>(stage);
         bf16* sv = sk + Cfg::SLOTS * D;
         const int tm = (int)(t % kWindow);
-        if (tm >= s0 && tm < s0 + Cfg::SLOTS) {
+        if (m.own) {
+          // append the current token to the ring and patch the staged rows
+          const long long off = ((long long)m.h * kWindow + tm) * D;
           for (int d = gtid; d < D / 8; d += 128) {
-            const uint4 kk = reinterpret_cast<const uint4*>(a.k + src)[d];
-            const uint4 vv = reinterpret_cast<const uint4*>(a.v + src)[d];
-            const uint4 rr = reinterpret_cast<const uint4*>(a.raw_k + src)[d];
+            const uint4 kk = reinterpret_cast<const uint4*>(aux + D)[d];
+            const uint4 vv = reinterpret_cast<const uint4*>(aux + 2 * D)[d];
+            const uint4 rr = reinterpret_cast<const uint4*>(aux + 3 * D)[d];
             reinterpret_cast<uint4*>(sk + (tm - s0) * D)[d] = kk;
             reinterpret_cast<uint4*>(sv + (tm - s0) * D)[d] = vv;
-            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.k_ring) + ((long long)it.h * kWindow + tm) * D)[d] = kk;
-            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.v_ring) + ((long long)it.h * kWindow + tm) * D)[d] = vv;
-            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.rk_ring) + ((long long)it.h * kWindow + tm) * D)[d] = rr;
+            reinterpret_cast<uint4*>(const_cast<bf16*>(c.k) + off)[d] = kk;
+            reinterpret_cast<uint4*>(const_cast<bf16*>(c.v) + off)[d] = vv;
+            reinterpret_cast<uint4*>(const_cast<bf16*>(c.rk) + off)[d] = rr;
           }
         }
         group_sync(g);
@@ -447,11 +553,11 @@ __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
           constexpr int NCH = D / 8 / TPK;
 #pragma unroll
           for (int x = 0; x < NCH; ++x) {
-            const int c = pid * NCH + ((x + key) % NCH);
+            const int ch = pid * NCH + ((x + key) % NCH);
             float fv[8];
-            unpack8(*reinterpret_cast<const uint4*>(kr + c * 8), fv);
+            unpack8(*reinterpret_cast<const uint4*>(kr + ch * 8), fv);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) scv += fv[e] * sc.qv[c * 8 + e];
+            for (int e = 0; e < 8; ++e) scv += fv[e] * sc.qv[ch * 8 + e];
           }
           if (TPK == 2) scv += __shfl_xor_sync(0xffffffffu, scv, 1);
         }
@@ -490,26 +596,20 @@ __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
         }
         if (gtid == 0) { part[D] = mx; part[D + 1] = sc.red[4] + sc.red[5] + sc.red[6] + sc.red[7]; }
       }
-    } else if (armed) {
+    } else if (m.armed) {
       // ------------------------------------------------ selected fine group
-      const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
-      const int nf = min(Cfg::FPC, st.n_route - m0);
-      const int32_t* ids = st.route_ids + (long long)it.h * st.route_cap + m0;
-      const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
-      const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + (long long)it.h * st.cap_fines * D;
-      const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + it.h * pstride;
-      const bf16* pw = reinterpret_cast<const bf16*>(st.page_w) + it.h * pstride;
-      if (gwarp == 0) softmax_row<D>(a.raw_q + src, sc.qv, lane);
+      const int nf = m.nf;
+      if (gwarp == 0) softmax_row<D>(aux, sc.qv, lane);
       group_sync(g);
       for (int x = gwarp; x < nf; x += 4) {
-        const int id = ids[x], page = id / kGroup;
+        const bf16* rows = aux + D * (1 + 3 * x);
         float sum = 0.f;
         for (int d = lane; d < D; d += 32) {
-          const float hv = rb(__fmul_rn(sc.qv[d], bf(pw[(long long)page * D + d])));
-          const float w = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
-          const float c = rb(__fmul_rn(hv, w));
-          sc.chs[x * D + d] = c;
-          sum += c;
+          const float hv = rb(__fmul_rn(sc.qv[d], bf(rows[2 * D + d])));
+          const float w = rb(expf(rb(__fsub_rn(bf(rows[d]), bf(rows[D + d])))));
+          const float cc = rb(__fmul_rn(hv, w));
+          sc.chs[x * D + d] = cc;
+          sum += cc;
         }
         sum = warp_sum(sum);
         if (lane == 0) sc.red[x] = rb(sum);
@@ -523,11 +623,11 @@ __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
 #pragma unroll
         for (int y = 0; y < RPG; ++y) {
           const int d = rg * RPG + y;
-          const float c = sc.chs[x * D + d];
+          const float cc = sc.chs[x * D + d];
           float fv[8];
           unpack8(*reinterpret_cast<const uint4*>(cm + x * D * D + d * D + ec * 8), fv);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] += c * fv[e];
+          for (int e = 0; e < 8; ++e) acc[e] += cc * fv[e];
         }
       }
       group_sync(g);
@@ -535,7 +635,7 @@ __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) rs[rg * D + ec * 8 + e] = acc[e];
       group_sync(g);
-      float* part = a.fine_part + (((long long)it.r * a.H + it.h) * f.ms + (it.slot - Cfg::KB)) * (D + 1);
+      float* part = a.fine_part + (((long long)m.r * a.H + m.h) * f.ms + (m.slot - Cfg::KB)) * (D + 1);
       for (int d = gtid; d < D; d += 128) {
         float sum = 0.f;
         for (int g2 = 0; g2 < RG; ++g2) sum += rs[g2 * D + d];
@@ -550,19 +650,19 @@ __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
     // ---- release the stage, then arrival
     group_sync(g);
     if (gtid == 0) {
-      mbar_arrive(&empty[st_]);
+      mbar_arrive(&empty[sj]);
       __threadfence();
-      sc.last = (atomicAdd(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
-      if (sc.last) st.counters[it.h] = 0;
+      sc.last = (atomicAdd(&c.counters[m.h], 1) == per - 1) ? 1 : 0;
+      if (sc.last) c.counters[m.h] = 0;
       __threadfence();
     }
     group_sync(g);
     if (!sc.last) continue;
     const bool hist = t >= kWindow;
-    const int M = st.n_route;
+    const int M = c.n_route;
     const int nparts = (M + Cfg::FPC - 1) / Cfg::FPC;
-    const float* lp = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
-    const float* fp = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
+    const float* lp = a.local_part + ((long long)m.r * a.H + m.h) * Cfg::KB * (D + 2);
+    const float* fp = a.fine_part + ((long long)m.r * a.H + m.h) * f.ms * (D + 1);
     for (int d = gtid; d < D; d += 128) {
       float Mx = -INFINITY;
       for (int b2 = 0; b2 < Cfg::KB; ++b2) Mx = fmaxf(Mx, __ldcg(lp + b2 * (D + 2) + D));
@@ -584,8 +684,8 @@ __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
         }
         const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
         const float qq = bf(a.raw_q[src + d]);
-        const bf16* fa = a.fa + ((long long)it.h * D + d) * 3;
-        const bf16* fb = a.fb + ((long long)it.h * D + d) * 3;
+        const bf16* fa = a.fa + ((long long)m.h * D + d) * 3;
+        const bf16* fb = a.fb + ((long long)m.h * D + d) * 3;
         const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), qq)), bf(fb[0]))), 0.f));
         const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), qq)), bf(fb[2])));
         const float mx = fmaxf(s0, s2);
@@ -600,14 +700,13 @@ __global__ void __launch_bounds__(288) decode_ws_kernel(FusedArgs f) {
     group_sync(g);
     if (gtid == 0) {
       __threadfence();
-      if (atomicAdd(&st.arrive, 1) == a.H - 1) {
-        st.arrive = 0;
-        st.position = t + 1;
+      if (atomicAdd(&c.st->arrive, 1) == a.H - 1) {
+        c.st->arrive = 0;
+        c.st->position = t + 1;
         __threadfence();
       }
     }
   }
-  (void)pflag;
 }
 
 // ---------------------------------------------------------------------------

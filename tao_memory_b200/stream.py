@@ -348,6 +348,33 @@ def _as_bf16(t, name, device):
     return t.contiguous()
 
 
+class _BatchArgs:
+    """Per-batch ctypes arguments reused across calls (pointer array, policy,
+    cursor/capacity/layer arrays, workspace size)."""
+
+    cache = {}
+
+    def __init__(self, states, w, heads, width, dev):
+        self.r = len(states)
+        self.ptrs = torch.tensor([st._desc.data_ptr() for st in states], dtype=torch.int64, device=dev)
+        self.policy = policy_for(states[0].config)
+        self.pos = (ctypes.c_int64 * self.r)()
+        self.cap = (ctypes.c_int32 * self.r)(*[st.cap_fines for st in states])
+        self.layers = (ctypes.c_int32 * self.r)(*[st.layer_index for st in states])
+        self.nbytes = _lib.lib().tao_stream_workspace_bytes(self.r, w, heads, width, ROUTE_CAP,
+                                                           ctypes.byref(self.policy))
+
+    @classmethod
+    def get(cls, states, w, heads, width, dev):
+        key = (tuple(st._desc.data_ptr() for st in states), tuple(st.cap_fines for st in states), w, heads, width)
+        args = cls.cache.get(key)
+        if args is None:
+            if len(cls.cache) > 256:
+                cls.cache.clear()
+            args = cls.cache[key] = cls(states, w, heads, width, dev)
+        return args
+
+
 def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
     """Advance every state by q.shape[1] tokens in one set of kernel launches.
 
@@ -361,43 +388,41 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
     for t in ops[1:]:
         if t.shape != q.shape:
             raise ValueError("q, k, v, raw_q and raw_k must have the same shape")
-    fa = fusion_a.detach().to(dev, _BF16).contiguous()
-    fb = fusion_b.detach().to(dev, _BF16).contiguous()
+    fa = fusion_a if (fusion_a.dtype == _BF16 and fusion_a.is_contiguous() and fusion_a.device == dev) \
+        else fusion_a.detach().to(dev, _BF16).contiguous()
+    fb = fusion_b if (fusion_b.dtype == _BF16 and fusion_b.is_contiguous() and fusion_b.device == dev) \
+        else fusion_b.detach().to(dev, _BF16).contiguous()
     if fa.shape != (heads, width, 3) or fb.shape != (heads, width, 3):
         raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
     for st in states:
         st._ensure(heads, width, dev, w)
-    if len(states) == 1:
-        ptrs = states[0]._pointer_array()
-    else:
-        ptrs = torch.tensor([st._desc.data_ptr() for st in states], dtype=torch.int64, device=dev)
-    cfg = states[0].config
-    policy = policy_for(cfg)
-    pos = (ctypes.c_int64 * r)(*[st.position for st in states])
-    cap = (ctypes.c_int32 * r)(*[st.cap_fines for st in states])
-    nbytes = lib.tao_stream_workspace_bytes(r, w, heads, width, ROUTE_CAP, ctypes.byref(policy))
-    ws = _Workspace.get(dev, nbytes)
+    args = _BatchArgs.get(states, w, heads, width, dev)
+    for i, st in enumerate(states):
+        args.pos[i] = st.position
+    ws = _Workspace.get(dev, args.nbytes)
     stream = torch.cuda.current_stream(dev).cuda_stream
     if w == 1:
-        layers = (ctypes.c_int32 * r)(*[st.layer_index for st in states])
-        _lib.check(lib.tao_decode_step(ptrs.data_ptr(), r, pos, layers, cap, ctypes.byref(policy), heads,
-                                       width, *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
-                                       float(alpha), out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
-    else:
-        _lib.check(lib.tao_stream_step(ptrs.data_ptr(), r, pos, cap, ctypes.byref(policy), w, heads, width,
+        _lib.check(lib.tao_decode_step(args.ptrs.data_ptr(), r, args.pos, args.layers, args.cap,
+                                       ctypes.byref(args.policy), heads, width,
                                        *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
                                        float(alpha), out.data_ptr(), ws.data_ptr(), ws.numel(), stream))
+    else:
+        _lib.check(lib.tao_stream_step(args.ptrs.data_ptr(), r, args.pos, args.cap, ctypes.byref(args.policy),
+                                       w, heads, width, *(t.data_ptr() for t in ops), fa.data_ptr(),
+                                       fb.data_ptr(), float(alpha), out.data_ptr(), ws.data_ptr(),
+                                       ws.numel(), stream))
     for st in states:
         hist = st.position >= WINDOW
-        st._counters["fusion_pointwise_calls" if hist else "fusion_no_history_local_returns"] += 1
-        st._counters["fused_fine_calls"] += int(hist)
+        c = st._counters
+        if hist:
+            c["fusion_pointwise_calls"] += 1
+            c["fused_fine_calls"] += 1
+        else:
+            c["fusion_no_history_local_returns"] += 1
         st.position += w
-        st._counters["peak_local_tokens"] = max(st._counters["peak_local_tokens"],
-                                                 st.position - window_start(st.position - 1)
-                                                 if st.position else 0)
-    if ptrs is not states[0]._ptrs:
-        # keep the temporary pointer array alive until the launches have consumed it
-        _Workspace.cache[("ptrs", dev)] = ptrs
+        local = st.position - window_start(st.position - 1)
+        if local > c["peak_local_tokens"]:
+            c["peak_local_tokens"] = local
 
 
 def check_device(device=None):
