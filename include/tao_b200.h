@@ -225,7 +225,9 @@ int tao_train_forward(const void* q, const void* k, const void* v, const void* r
  *   d_local, gn, d_rq_f          : bf16 [B][T][H][D] scratch
  *   gd                           : fp32 [B][T][H] scratch
  *   row_dot                      : fp32 [B][H][T] scratch
- *   dC, dz                       : fp32 [B][H][S][D][D], [B][H][S][D], zero-filled */
+ *   dC, dz                       : fp32 [B][H][S][D][D], [B][H][S][D]; dz zero-filled
+ *   dc_partial                   : bf16 [B][H][tao_train_pairs(T)][D][D], zero-filled
+ *                                  (one dC partial per (tile, visible fine) pair) */
 typedef struct TaoTrainGrads {
   void* dq;
   void* dk;
@@ -241,7 +243,11 @@ typedef struct TaoTrainGrads {
   float* row_dot;
   float* dC;
   float* dz;
+  void* dc_partial;
 } TaoTrainGrads;
+
+/* Number of (256-query tile, visible fine) pairs of a T-token sequence. */
+int tao_train_pairs(int tokens);
 
 /* Backward of tao_train_forward: gradients of q, k, v, raw_q, raw_k and the
  * fusion parameters for the upstream gradient grad_out [B][T][H][D] bf16.

@@ -126,7 +126,7 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   BwdArgs a = a0;
   const Geometry g = geometry(a.dm.T);
   const int B = a.dm.B, H = a.dm.H, T = a.dm.T;
-  fusion_bwd_kernel<D><<<dim3(g.tiles, B * H), 256, 0, s>>>(a);
+  fusion_bwd_kernel<D><<<dim3((T + 8 * kFusionRowsPerWarp - 1) / (8 * kFusionRowsPerWarp), B * H), 256, 0, s>>>(a);
   const size_t asmem = (size_t)(2 * 64 + 4 * 64) * D * 2 + 256 * 4;
   if (!tsmem(attn_bwd_kv_kernel<D>, asmem) || !tsmem(attn_bwd_q_kernel<D>, asmem))
     return tfail(TAO_ERR_CUDA, "smem attribute");
@@ -138,6 +138,7 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   constexpr int NQ = ReadBwdSmem<D>::NQ;
   read_bwd_kernel<D><<<dim3(g.tiles * (256 / NQ), B * H), NQ, rsmem, s>>>(a);
   if (g.S > 0) {
+    dc_reduce_kernel<D><<<B * H * g.S, 256, 0, s>>>(a, g.tiles);
     const size_t wsmem = (size_t)2 * 256 * D * 2 + (size_t)D * D * 2 + 6 * D * 4;
     if (!tsmem(writer_bwd_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
     writer_bwd_kernel<D><<<B * H * g.S, 256, wsmem, s>>>(a);
@@ -175,12 +176,19 @@ int tao_train_backward(const void* grad_out, const void* q, const void* k, const
   a.gd = grads->gd; a.dv_row = grads->row_dot; a.d_fa = grads->d_fusion_a; a.d_fb = grads->d_fusion_b;
   a.dq = W(grads->dq); a.dk = W(grads->dk); a.dv = W(grads->dv); a.d_raw_q = W(grads->d_raw_q);
   a.d_raw_k = W(grads->d_raw_k); a.dC = grads->dC; a.dz = grads->dz;
+  a.dcp = W(grads->dc_partial);
+  a.npairs = g.vmax * (g.vmax + 1) / 2;
   a.dm = tao::TrainDims{batch, tokens, heads, g.S, (long long)heads * width};
   a.pages = g.pages;
   a.mmax = g.mmax;
   a.err = saved->err;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return width == 64 ? train_backward<64>(a, s) : train_backward<128>(a, s);
+}
+
+int tao_train_pairs(int tokens) {
+  const Geometry g = geometry(tokens);
+  return g.vmax * (g.vmax + 1) / 2;
 }
 
 int tao_train_geometry(int tokens, int* sealed, int* pages, int* mmax) {

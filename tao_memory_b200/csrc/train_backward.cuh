@@ -20,15 +20,19 @@ struct BwdArgs {
   float *gd, *dv_row;            // [B,T,H], [B,H,T] (row dot of dO and O for attention)
   float *d_fa, *d_fb;            // fp32 [H,D,3] accumulators
   bf16 *dq, *dk, *dv, *d_raw_q, *d_raw_k;
-  float *dC, *dz;                // fp32 [B,H,S,D,D], [B,H,S,D] accumulators
+  float *dC, *dz;                // fp32 [B,H,S,D,D] (reduced), [B,H,S,D] accumulators
+  bf16* dcp;                     // per-(tile, fine) dC partials [B,H,npairs,D,D]
+  int npairs;                    // sum over tiles of visible fines
   TrainDims dm;
   int pages, mmax;
   int* err;
 };
 
 // ---------------------------------------------------------------------------
-// Fusion backward: one warp per (token, head) row, lanes over channels.
+// Fusion backward: one warp per (token, head) row, lanes over channels; each warp
+// takes kFusionRowsPerWarp consecutive tokens, a CTA 8 warps.
 // ---------------------------------------------------------------------------
+constexpr int kFusionRowsPerWarp = 4;
 template <int D>
 __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
   constexpr int PER = D / 32;
@@ -48,8 +52,8 @@ __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
       fa[j][x] = bf(a.fa[((long long)h * D + lane + 32 * j) * 3 + x]);
       fb[j][x] = bf(a.fb[((long long)h * D + lane + 32 * j) * 3 + x]);
     }
-  for (int rr = 0; rr < 32; ++rr) {
-    const int t = tile * 256 + warp * 32 + rr;
+  for (int rr = 0; rr < kFusionRowsPerWarp; ++rr) {
+    const int t = tile * 8 * kFusionRowsPerWarp + warp * kFusionRowsPerWarp + rr;
     if (t >= a.dm.T) break;
     const long long base = ((long long)b * a.dm.T + t) * a.dm.row + (long long)h * D;
     const bool present = t >= kWindow;
@@ -704,7 +708,9 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
       constexpr int WPM = NW >= MTILES ? NW / MTILES : 1;   // warps per m-tile
       constexpr int MPW = NW >= MTILES ? 1 : MTILES / NW;   // m-tiles per warp
       constexpr int NPW = (D / 8) / WPM;                    // n-tiles per warp
-      float* dcb = a.dC + (((long long)b * a.dm.H + h) * a.dm.S + sf) * (long long)D * D;
+      // this tile's bf16 partial of dC_s (the reference rounds dC per tile as well)
+      const long long pair = (long long)(tile - 3) * (tile - 2) / 2 + sf;
+      bf16* dcb = a.dcp + (((long long)b * a.dm.H + h) * a.npairs + pair) * (long long)D * D;
       for (int mm = 0; mm < MPW; ++mm) {
         const int mt = (NW >= MTILES) ? warp / WPM : warp * MPW + mm;
         const int n0 = (NW >= MTILES) ? (warp % WPM) * NPW : 0;
@@ -730,10 +736,13 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
         for (int j = 0; j < NPW; ++j) {
           const int e = (n0 + j) * 8 + c4 * 2;
           const int d0 = mt * 16 + g;
-          atomicAdd(reinterpret_cast<float2*>(dcb + (long long)d0 * D + e),
-                    make_float2(rb(dc[j][0]), rb(dc[j][1])));
-          atomicAdd(reinterpret_cast<float2*>(dcb + (long long)(d0 + 8) * D + e),
-                    make_float2(rb(dc[j][2]), rb(dc[j][3])));
+          if (QS == 1) {
+            *reinterpret_cast<__nv_bfloat162*>(dcb + (long long)d0 * D + e) = __floats2bfloat162_rn(dc[j][0], dc[j][1]);
+            *reinterpret_cast<__nv_bfloat162*>(dcb + (long long)(d0 + 8) * D + e) = __floats2bfloat162_rn(dc[j][2], dc[j][3]);
+          } else {  // half tiles: both halves add into the zero-initialised partial
+            atomicAdd(reinterpret_cast<__nv_bfloat162*>(dcb + (long long)d0 * D + e), __floats2bfloat162_rn(dc[j][0], dc[j][1]));
+            atomicAdd(reinterpret_cast<__nv_bfloat162*>(dcb + (long long)(d0 + 8) * D + e), __floats2bfloat162_rn(dc[j][2], dc[j][3]));
+          }
         }
       }
     }
@@ -795,6 +804,26 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
 }
 
 // ---------------------------------------------------------------------------
+// dC[b][h][s] = sum over the tiles t >= s + 3 of their bf16 partials (fp32 sum).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) dc_reduce_kernel(BwdArgs a, int tiles) {
+  const int s = blockIdx.x % a.dm.S, bh = blockIdx.x / a.dm.S;
+  const bf16* base = a.dcp + (long long)bh * a.npairs * D * D;
+  float* out = a.dC + ((long long)bh * a.dm.S + s) * D * D;
+  for (int x = threadIdx.x * 2; x < D * D; x += 512) {
+    float2 acc = make_float2(0.f, 0.f);
+    for (int t = s + 3; t < tiles; ++t) {
+      const long long pair = (long long)(t - 3) * (t - 2) / 2 + s;
+      const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(base + pair * D * D + x));
+      acc.x += v.x;
+      acc.y += v.y;
+    }
+    *reinterpret_cast<float2*>(out + x) = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Writer backward: one CTA (256 threads) per (b, h, block s).
 // ---------------------------------------------------------------------------
 template <int D>
@@ -836,15 +865,8 @@ __global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
   cp_wait<0>();
   __syncthreads();
   auto kat = [&](int t, int d) -> float { return bf(*reinterpret_cast<const bf16*>(kB + swz(t, d, D))); };
-  for (int d = tid; d < D; d += 256) {
-    float m = -INFINITY;
-    for (int t = 0; t < NT; ++t) m = fmaxf(m, kat(t, d));
-    float sum = 0.f;
-    for (int t = 0; t < NT; ++t) sum += rb(expf(rb(__fsub_rn(kat(t, d), m))));
-    mx[d] = m;
-    zp[d] = rb(sum);
-  }
-  __syncthreads();
+  __shared__ float stat_scratch[2 * 256];
+  channel_stats<D, 256>(kat, mx, zp, stat_scratch);
   // probability p[t][d] = bf16(e / Z), recomputed from the staged raw keys
   auto pval = [&](int t, int d) -> float {
     return rb(__fdiv_rn(rb(expf(rb(__fsub_rn(kat(t, d), mx[d])))), zp[d]));
@@ -973,12 +995,19 @@ __global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
     }
   __syncthreads();
   // max: dm = dz - sum_t d_x, shared evenly by the tokens that attain the max
-  for (int d = tid; d < D; d += 256) {
-    const float dm = rb(dzS[d] - rb(dmS[d]));
+  {
+    constexpr int G = 256 / D, TPG = NT / G;
+    const int d = tid % D, grp = tid / D;
+    int cnt = 0;
+    for (int t = grp * TPG; t < (grp + 1) * TPG; ++t) cnt += kat(t, d) == mx[d];
+    stat_scratch[grp * D + d] = (float)cnt;
+    __syncthreads();
     int count = 0;
-    for (int t = 0; t < NT; ++t) count += kat(t, d) == mx[d];
+#pragma unroll
+    for (int x = 0; x < G; ++x) count += (int)stat_scratch[x * D + d];
+    const float dm = rb(dzS[d] - rb(dmS[d]));
     const float share = rb(dm / count);
-    for (int t = 0; t < NT; ++t)
+    for (int t = grp * TPG; t < (grp + 1) * TPG; ++t)
       if (kat(t, d) == mx[d]) {
         bf16* p = dkb + (long long)t * row + d;
         *p = tobf(bf(*p) + share);

@@ -15,6 +15,34 @@ struct TrainDims {
   long long row;    // token stride in elements (H * D)
 };
 
+// Per-channel max and partition of a staged [256][D] key block, with the token
+// range split over NTHREADS / D thread groups (partials combined in `scratch`,
+// 2 * NTHREADS floats): m = max_t k, Z = bf16(sum_t bf16(exp(bf16(k - m)))).
+template <int D, int NTHREADS, typename KAt>
+TAO_DEVI void channel_stats(KAt kat, float* mx, float* zp, float* scratch) {
+  constexpr int G = NTHREADS / D, TPG = 256 / G;
+  const int tid = threadIdx.x, d = tid % D, grp = tid / D;
+  float m = -INFINITY;
+  for (int t = grp * TPG; t < (grp + 1) * TPG; ++t) m = fmaxf(m, kat(t, d));
+  scratch[grp * D + d] = m;
+  __syncthreads();
+  m = -INFINITY;
+#pragma unroll
+  for (int x = 0; x < G; ++x) m = fmaxf(m, scratch[x * D + d]);
+  float sum = 0.f;
+  for (int t = grp * TPG; t < (grp + 1) * TPG; ++t) sum += rb(expf(rb(__fsub_rn(kat(t, d), m))));
+  scratch[NTHREADS + grp * D + d] = sum;
+  __syncthreads();
+  if (grp == 0) {
+    float z = 0.f;
+#pragma unroll
+    for (int x = 0; x < G; ++x) z += scratch[NTHREADS + x * D + d];
+    mx[d] = m;
+    zp[d] = rb(z);
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // Writer: one CTA per (b, h, block s).  z[b][h][s][d] and C[b][h][s][d][e] with
 // the reference's rounding points; C = p^T v on the tensor cores.
@@ -45,16 +73,9 @@ __global__ void __launch_bounds__(128) writer_kernel(const bf16* __restrict__ ra
   auto at = [&](int r, int d) -> bf16& {
     return *reinterpret_cast<bf16*>(smem + swz(r, d, D));
   };
-  // per channel: max, partition = bf16(sum_t bf16(exp(bf16(k - max)))) in token order
-  for (int d = tid; d < D; d += 128) {
-    float m = -INFINITY;
-    for (int t = 0; t < NT; ++t) m = fmaxf(m, bf(at(t, d)));
-    float sum = 0.f;
-    for (int t = 0; t < NT; ++t) sum += rb(expf(rb(__fsub_rn(bf(at(t, d)), m))));
-    mx[d] = m;
-    zp[d] = rb(sum);
-  }
-  __syncthreads();
+  // per channel: max, partition = bf16(sum_t bf16(exp(bf16(k - max))))
+  __shared__ float stat_scratch[2 * 128];
+  channel_stats<D, 128>([&](int t, int d) { return bf(at(t, d)); }, mx, zp, stat_scratch);
   for (int idx = tid; idx < NT * D; idx += 128) {
     const int t = idx / D, d = idx % D;
     const float e = rb(expf(rb(__fsub_rn(bf(at(t, d)), mx[d]))));
