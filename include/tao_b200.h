@@ -184,6 +184,13 @@ int tao_window_attention(const void* q, const void* k, const void* v, void* out,
                          float* lse, int batch, int tokens, int heads, int width,
                          void* stream);
 
+/* Select the windowed-attention kernel for this process (tao_window_attention and
+ * the training forward): 1 = tcgen05/TMEM kernel with TMA tile loads for width 64
+ * (default; width 128 uses the mma.sync kernel), 0 = mma.sync kernel for every
+ * width.  Outputs agree to fp32 summation order.  No counterpart in the reference
+ * (it has one attention path, flash_attention.py:16-37). */
+int tao_attention_variant(int variant);
+
 /* ---- training (tao_attention, operator.py:42-54) -------------------------
  * Saved buffers of one forward, allocated by the caller (sizes from
  * tao_train_geometry; S sealed blocks, P pages, mmax selected fines per query):

@@ -16,6 +16,11 @@
 #include "stream_kernels.cuh"
 #include "window_attention.cuh"
 
+namespace tao {
+int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* out, float* lse, int B,
+                            int T, int H, int D, int* err, cudaStream_t s);
+}  // namespace tao
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -532,33 +537,10 @@ int tao_window_attention(const void* q, const void* k, const void* v, void* out,
   if (width != 64 && width != 128) return fail(TAO_ERR_ARG, "head width must be 64 or 128");
   for (const void* p : {q, k, v, (const void*)out})
     if (!aligned16(p)) return fail(TAO_ERR_ARG, "tensors must be 16-byte aligned");
-  tao::WinAttnParams p{};
-  p.q = static_cast<const tao::bf16*>(q);
-  p.k = static_cast<const tao::bf16*>(k);
-  p.v = static_cast<const tao::bf16*>(v);
-  p.out = static_cast<tao::bf16*>(out);
-  p.lse = lse;
-  p.q_batch_stride = p.k_batch_stride = p.o_batch_stride = (long long)tokens * heads * width;
-  p.q_row_stride = p.k_row_stride = p.o_row_stride = (long long)heads * width;
-  p.k_head_stride = width;
-  p.heads = heads;
-  p.nq = tokens;
-  p.qpos0 = 0;
-  p.kstart = -1;
-  p.ring = 0;
-  p.states = nullptr;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc;
-  dim3 grid((tokens + 63) / 64, batch * heads);
-  if (width == 64) {
-    const size_t smem = (size_t)(64 + 4 * 64) * 64 * 2;
-    if ((rc = set_smem(tao::window_attention_kernel<64>, smem))) return rc;
-    tao::window_attention_kernel<64><<<grid, 128, smem, s>>>(p);
-  } else {
-    const size_t smem = (size_t)(64 + 4 * 64) * 128 * 2;
-    if ((rc = set_smem(tao::window_attention_kernel<128>, smem))) return rc;
-    tao::window_attention_kernel<128><<<grid, 128, smem, s>>>(p);
-  }
+  int rc = tao::launch_window_attention(static_cast<const tao::bf16*>(q), static_cast<const tao::bf16*>(k),
+                                         static_cast<const tao::bf16*>(v), static_cast<tao::bf16*>(out), lse,
+                                         batch, tokens, heads, width, nullptr, static_cast<cudaStream_t>(stream));
+  if (rc) return rc;
   return check_launch("window_attention_kernel");
 }
 

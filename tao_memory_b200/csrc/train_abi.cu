@@ -8,6 +8,10 @@
 
 void tao_set_last_error(const char* msg);
 void tao_take_profile_events(cudaEvent_t* start, cudaEvent_t* stop);
+namespace tao {
+int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* out, float* lse, int B,
+                            int T, int H, int D, int* err, cudaStream_t s);
+}  // namespace tao
 
 namespace {
 
@@ -64,24 +68,11 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
   const Geometry g = geometry(T);
   TrainDims dm{B, T, H, g.S, (long long)H * D};
   // 1. exact local window attention
-  WinAttnParams p{};
-  p.q = q;
-  p.k = k;
-  p.v = v;
-  p.out = static_cast<bf16*>(tb.local);
-  p.lse = tb.lse;
-  p.q_batch_stride = p.k_batch_stride = p.o_batch_stride = (long long)T * H * D;
-  p.q_row_stride = p.k_row_stride = p.o_row_stride = (long long)H * D;
-  p.k_head_stride = D;
-  p.heads = H;
-  p.nq = T;
-  p.kstart = -1;
-  const size_t attn_smem = (size_t)(64 + 4 * 64) * D * 2;
-  if (!tsmem(window_attention_kernel<D>, attn_smem)) return tfail(TAO_ERR_CUDA, "smem attribute");
   cudaEvent_t ev0, ev1;
   tao_take_profile_events(&ev0, &ev1);
   if (ev0) cudaEventRecord(ev0, s);
-  window_attention_kernel<D><<<dim3((T + 63) / 64, B * H), 128, attn_smem, s>>>(p);
+  if (int rc = launch_window_attention(q, k, v, static_cast<bf16*>(tb.local), tb.lse, B, T, H, D, tb.err, s))
+    return rc;
   if (ev1) cudaEventRecord(ev1, s);
   if (g.S > 0) {
     // 2. writer over all sealed blocks, 3. page prefix table

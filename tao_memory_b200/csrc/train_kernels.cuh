@@ -237,7 +237,6 @@ __global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
   const uint32_t sH = smem_u32(ptr);   ptr += 256 * D * 2;
   const uint32_t sA = smem_u32(ptr);   ptr += 256 * D * 2;
   const uint32_t sC = smem_u32(ptr);   ptr += NBUF * D * D * 2;
-  bf16* hS = reinterpret_cast<bf16*>(smem);
   float* pwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   float* pzS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   bf16* swS = reinterpret_cast<bf16*>(ptr);    ptr += ((size_t)V * D * 2 + 15) / 16 * 16;
