@@ -70,7 +70,7 @@ int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* o
       tao_set_last_error("smem attribute");
       return TAO_ERR_CUDA;
     }
-    tc_window_attention_kernel<<<dim3((T + tc::kTcBM - 1) / tc::kTcBM, B * H), 128, tc::kTcSmem, s>>>(mq, mk, mv, out, lse,
+    tc_window_attention_kernel<<<dim3((T + tc::kTcBM - 1) / tc::kTcBM, B * H), tc::kTcThreads, tc::kTcSmem, s>>>(mq, mk, mv, out, lse,
                                                                                          T, H, err);
     return TAO_OK;
   }

@@ -6,13 +6,15 @@
 //
 // One CTA (one warpgroup, 128 threads) owns 128 queries of one (batch, head):
 //   * Q, K and V tiles arrive by TMA (cp.async.bulk.tensor, 128B swizzle) into
-//     1024-byte-aligned shared memory; K/V are double-buffered per 128-key block
+//     1024-byte-aligned shared memory; K and V have two stages each
 //   * S = Q K^T: tcgen05.mma kind::f16, M=128 N=128 K=64, fp32 accumulator in TMEM
-//   * each thread owns one query row: tcgen05.ld of its S row, scale + window mask,
+//   * each thread owns one query row: tcgen05.ld of its S row, window mask,
 //     online softmax in registers, P (bf16) written to shared memory in the
 //     K-major swizzled layout the tensor core reads
-//   * O_blk = P V: tcgen05.mma M=128 N=64 K=128 with V as an MN-major operand,
-//     read back and accumulated in registers with the softmax rescale
+//   * O += P V: tcgen05.mma M=128 N=64 K=128 with V as an MN-major operand; O
+//     stays in TMEM for the whole CTA and is rescaled there only when a row
+//     maximum grows by more than 2^8 (p = 2^(s - stale max) stays <= 256)
+//   * S of the next key block is computed while the softmax of this one runs
 // Every mbarrier wait is bounded; on a timeout the CTA records the error, frees
 // its TMEM and returns.
 #pragma once
@@ -70,6 +72,25 @@ TAO_DEVI void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+TAO_DEVI void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+      "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]),
+      "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]),
+      "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 2^x on the special-function unit (flush-to-zero; 2^-inf = +0).
+TAO_DEVI float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 TAO_DEVI void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -78,25 +99,44 @@ TAO_DEVI void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* 
       : "memory");
 }
 
-// CTA-wide bounded wait: thread 0 polls (bounded), the verdict is broadcast by
-// the barrier, and every thread then observes the completed phase itself (one
-// poll succeeds at once) so the copied bytes are visible to it.
-TAO_DEVI bool wait_all(uint64_t* bar, uint32_t phase, int* err) {
-  int got = 1;
-  if (threadIdx.x == 0) got = mbar_wait(bar, phase, err) ? 1 : 0;
-  if (!__syncthreads_and(got)) return false;
-  return mbar_wait(bar, phase, err);
-}
-
 constexpr int kTcBM = 128, kTcBN = 128, kTcD = 64;
 constexpr int kTcTile = kTcBM * kTcD * 2;  // 16 KB: 128 rows x 128 B
-// Q, K[2], V[2], P[2] tiles, then 5 mbarriers and the TMEM address slot.
-constexpr int kTcSmem = 7 * kTcTile + 64;
-constexpr int kTcTmemCols = 256;           // S: columns 0-127, O block: 128-191
+constexpr int kTcThreads = 160;            // warps 0-3: softmax rows, warp 4: TMA + MMA issue
+// Q, K[2], V[2], P[2] tiles, then 9 mbarriers, the TMEM address slot and the abort flag.
+constexpr int kTcSmem = 7 * kTcTile + 128;
+constexpr int kTcTmemCols = 256;           // S: columns 0-127, O: 128-191
+// O is rescaled only when a row maximum grows by more than this (log2 units):
+// until then scores are exponentiated against the stale maximum (p <= 2^8).
+constexpr float kTcRescale = 8.f;
+
+// Bounded wait that also gives up as soon as another thread of the CTA raised
+// the abort flag (so one timeout ends every wait of the CTA promptly).
+TAO_DEVI bool wait_or_abort(uint64_t* bar, uint32_t phase, int* err, volatile int* abort) {
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if ((i & 31u) == 31u && *abort) return false;
+  }
+  *abort = 1;
+  if (err) atomicOr(err, kErrWaitTimeout);
+  return false;
+}
+// Warp-uniform verdict of wait_or_abort (tcgen05.ld/st need the whole warp).
+TAO_DEVI bool warp_wait(uint64_t* bar, uint32_t phase, int* err, volatile int* abort) {
+  return __all_sync(0xffffffffu, wait_or_abort(bar, phase, err, abort));
+}
 
 }  // namespace tc
 
-__global__ void __launch_bounds__(128) tc_window_attention_kernel(
+
+// Roles and hand-offs of one CTA (all by mbarrier; no CTA-wide barrier in the loop):
+//   issuer (warp 4, one lane): TMA copies of Q, K(j), V(j); S(j) = Q K(j)^T into
+//     TMEM -> sfull; O += P(j) V(j) -> ofull.  K stage j&1 is refilled with K(j+2)
+//     once the softmax warps have read S(j) (sfree); V stage (j+1)&1 with V(j+1)
+//     once O(j-1) is complete.
+//   softmax (warps 0-3, one query row per thread): sfull(j) -> tcgen05.ld S row ->
+//     sfree -> mask, row max -> ofull(j-1) -> rescale the O row in TMEM if its
+//     maximum moved by more than 2^8 -> P(j) (bf16) to shared memory -> pfull.
+__global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
     const __grid_constant__ CUtensorMap tv, bf16* __restrict__ out, float* __restrict__ lse, int T,
     int H, int* err) {
@@ -108,18 +148,22 @@ __global__ void __launch_bounds__(128) tc_window_attention_kernel(
     if (threadIdx.x == 0 && err) atomicOr(err, kErrState);
     return;
   }
-  uint8_t* sQ = sm;
-  uint8_t* sK[2] = {sm + kTcTile, sm + 2 * kTcTile};
-  uint8_t* sV[2] = {sm + 3 * kTcTile, sm + 4 * kTcTile};
-  uint8_t* sP = sm + 5 * kTcTile;  // two K-major tiles: keys 0-63 and 64-127
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 7 * kTcTile);
-  uint64_t* qbar = bars;
-  uint64_t* kvbar = bars + 1;  // [2]
-  uint64_t* sbar = bars + 3;
-  uint64_t* obar = bars + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+  uint8_t* const sQ = sm;
+  uint8_t* const sK = sm + kTcTile;      // [2] stages
+  uint8_t* const sV = sm + 3 * kTcTile;  // [2] stages
+  uint8_t* const sP = sm + 5 * kTcTile;  // two K-major tiles: keys 0-63 and 64-127
+  uint64_t* const bars = reinterpret_cast<uint64_t*>(sm + 7 * kTcTile);
+  uint64_t* const qbar = bars;
+  uint64_t* const kfull = bars + 1;  // [2]
+  uint64_t* const vfull = bars + 3;  // [2]
+  uint64_t* const sfull = bars + 5;
+  uint64_t* const sfree = bars + 6;
+  uint64_t* const pfull = bars + 7;
+  uint64_t* const ofull = bars + 8;
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(bars + 10);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y / H, h = blockIdx.y % H;
   const int q0 = blockIdx.x * kTcBM;  // the 128 queries share one 256-token tile
   int kstart = (q0 / kFine) * kFine - kKeep;
@@ -135,7 +179,16 @@ __global__ void __launch_bounds__(128) tc_window_attention_kernel(
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) mbar_init(bars + i, 1);
+    mbar_init(qbar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kfull[i], 1);
+      mbar_init(&vfull[i], 1);
+    }
+    mbar_init(sfull, 1);
+    mbar_init(sfree, kTcBM);
+    mbar_init(pfull, kTcBM);
+    mbar_init(ofull, 1);
+    *abort_flag = 0;
     fence_mbar_init();
   }
   fence_before();
@@ -143,141 +196,191 @@ __global__ void __launch_bounds__(128) tc_window_attention_kernel(
   fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t tS = tbase, tO = tbase + 128;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
 
-  // Outstanding-completion bookkeeping (uniform across the CTA) for the drain.
-  int kv_armed[2] = {0, 0}, kv_done[2] = {0, 0}, s_done = 0, o_done = 0;
-  bool s_pending = false, o_pending = false;
-  if (tid == 0) {
-    mbar_expect_tx(qbar, kTcTile);
-    tma_2d(sQ, &tq, col, row0 + q0, qbar);
-  }
-  for (int j = 0; j < 2 && j < nblk; ++j) {
-    if (tid == 0) {
-      mbar_expect_tx(&kvbar[j], 2 * kTcTile);
-      tma_2d(sK[j], &tk, col, row0 + kstart + j * kTcBN, &kvbar[j]);
-      tma_2d(sV[j], &tv, col, row0 + kstart + j * kTcBN, &kvbar[j]);
-    }
-    kv_armed[j] = 1;
-  }
-  const int qpos = q0 + tid;
-  float o[kTcD];
-#pragma unroll
-  for (int d = 0; d < kTcD; ++d) o[d] = 0.f;
-  float m = -INFINITY, l = 0.f;
-  const float sl = 1.4426950408889634f * 0.125f;  // log2(e) / sqrt(64)
-  constexpr uint32_t IS = idesc_bf16(128, 128, 0, 0), IO = idesc_bf16(128, 64, 0, 1);
-  bool ok = wait_all(qbar, 0, err);
-  for (int j = 0; ok && j < nblk; ++j) {
-    const int s = j & 1;
-    ok = wait_all(&kvbar[s], kv_done[s] & 1, err);
-    if (!ok) break;
-    ++kv_done[s];
-    // ---- S = Q K^T (M=128 queries, N=128 keys, K=64 channels)
-    if (tid == 0) {
+  if (warp == 4) {
+    // ================= issuer (the whole warp walks the schedule; lane 0 issues) =====
+    constexpr uint32_t IS = idesc_bf16(128, 128, 0, 0), IO = idesc_bf16(128, 64, 0, 1);
+    const bool leader = lane == 0;
+    int k_armed[2] = {0, 0}, k_done[2] = {0, 0}, v_armed[2] = {0, 0}, v_done[2] = {0, 0};
+    int s_issued = 0, o_issued = 0;
+    auto load_k = [&](int j) {
+      const int st = j & 1;
+      if (leader) {
+        mbar_expect_tx(&kfull[st], kTcTile);
+        tma_2d(sK + st * kTcTile, &tk, col, row0 + kstart + j * kTcBN, &kfull[st]);
+      }
+      ++k_armed[st];
+    };
+    auto load_v = [&](int j) {
+      const int st = j & 1;
+      if (leader) {
+        mbar_expect_tx(&vfull[st], kTcTile);
+        tma_2d(sV + st * kTcTile, &tv, col, row0 + kstart + j * kTcBN, &vfull[st]);
+      }
+      ++v_armed[st];
+    };
+    auto issue_s = [&](int j) -> bool {
+      const int st = j & 1;
+      if (!warp_wait(&kfull[st], k_done[st] & 1, err, abort_flag)) return false;
+      ++k_done[st];
       fence_after();
+      if (leader) {
+        const uint32_t kaddr = smem_u32(sK + st * kTcTile), qaddr = smem_u32(sQ);
 #pragma unroll
-      for (int k = 0; k < kTcD / 16; ++k)
-        mma(tS, sdesc(smem_u32(sQ) + k * 32, 16, 1024), sdesc(smem_u32(sK[s]) + k * 32, 16, 1024), IS, k > 0);
-      commit(sbar);
-    }
-    s_pending = true;
-    ok = wait_all(sbar, s_done & 1, err);
-    if (!ok) break;
-    ++s_done;
-    s_pending = false;
-    fence_after();
-    // ---- this thread's score row: scale, window mask, online softmax, P -> smem
-    const int kb0 = kstart + j * kTcBN;
-    float sc[kTcBN];
-#pragma unroll
-    for (int c = 0; c < kTcBN / 32; ++c) tmem_ld32(tS + lane_off + c * 32, sc + c * 32);
-    float mx = m;
-#pragma unroll
-    for (int c = 0; c < kTcBN; ++c) {
-      const int kp = kb0 + c;
-      sc[c] = (kp <= qpos && kp < T) ? sc[c] * sl : -INFINITY;
-      mx = fmaxf(mx, sc[c]);
-    }
-    const float base = (mx == -INFINITY) ? 0.f : mx;
-    const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - base);
-    float rs = 0.f;
-#pragma unroll
-    for (int c8 = 0; c8 < kTcBN / 8; ++c8) {
-      uint32_t pk[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p0 = exp2f(sc[c8 * 8 + 2 * e] - base), p1 = exp2f(sc[c8 * 8 + 2 * e + 1] - base);
-        rs += p0 + p1;
-        __nv_bfloat162 t2 = __floats2bfloat162_rn(p0, p1);
-        pk[e] = *reinterpret_cast<uint32_t*>(&t2);
+        for (int k = 0; k < kTcD / 16; ++k)
+          mma(tS, sdesc(qaddr + k * 32, 16, 1024), sdesc(kaddr + k * 32, 16, 1024), IS, k > 0);
+        commit(sfull);
       }
-      const int sub = c8 >> 3, chunk = c8 & 7;
-      uint8_t* dst = sP + sub * kTcTile + tid * 128 + ((chunk ^ (tid & 7)) << 4);
-      *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      __syncwarp();
+      ++s_issued;
+      return true;
+    };
+    if (leader) {
+      mbar_expect_tx(qbar, kTcTile);
+      tma_2d(sQ, &tq, col, row0 + q0, qbar);
     }
-    l = l * alpha + rs;
-    m = mx;
-    fence_proxy_async();  // generic-proxy P stores -> visible to the tensor core
-    fence_before();
-    __syncthreads();
-    // ---- O_blk = P V (M=128 queries, N=64 channels, K=128 keys; V is MN-major)
-    if (tid == 0) {
+    for (int j = 0; j < 2 && j < nblk; ++j) {
+      load_k(j);
+      load_v(j);
+    }
+    bool fine = warp_wait(qbar, 0, err, abort_flag) && issue_s(0);
+    for (int j = 0; fine && j < nblk; ++j) {
+      // S(j) has been read: the S columns and K stage j&1 are free
+      if (!(fine = warp_wait(sfree, j & 1, err, abort_flag))) break;
       fence_after();
-#pragma unroll
-      for (int k = 0; k < kTcBN / 16; ++k) {
-        const uint64_t ad = sdesc(smem_u32(sP) + (k >> 2) * kTcTile + (k & 3) * 32, 16, 1024);
-        const uint64_t bd = sdesc(smem_u32(sV[s]) + k * 2048, 8192, 1024);
-        mma(tO, ad, bd, IO, k > 0);
+      if (j + 2 < nblk) load_k(j + 2);
+      if (j + 1 < nblk && !(fine = issue_s(j + 1))) break;
+      // O(j-1) complete: V stage (j+1)&1 is free
+      if (j >= 1 && j + 1 < nblk) {
+        if (!(fine = warp_wait(ofull, (j - 1) & 1, err, abort_flag))) break;
+        load_v(j + 1);
       }
-      commit(obar);
-    }
-    o_pending = true;
-    ok = wait_all(obar, o_done & 1, err);
-    if (!ok) break;
-    ++o_done;
-    o_pending = false;
-    fence_after();
-    float ob[kTcD];
+      // P(j) written (and the O rows rescaled): O += P(j) V(j)
+      if (!(fine = warp_wait(pfull, j & 1, err, abort_flag))) break;
+      const int st = j & 1;
+      if (!(fine = warp_wait(&vfull[st], v_done[st] & 1, err, abort_flag))) break;
+      ++v_done[st];
+      fence_after();
+      if (leader) {
+        const uint32_t vaddr = smem_u32(sV + st * kTcTile), paddr = smem_u32(sP);
 #pragma unroll
-    for (int c = 0; c < kTcD / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ob + c * 32);
-#pragma unroll
-    for (int d = 0; d < kTcD; ++d) o[d] = o[d] * alpha + ob[d];
-    fence_before();
-    __syncthreads();  // every thread has read S and O: TMEM and stage s are free
-    if (j + 2 < nblk) {
-      if (tid == 0) {
-        fence_after();
-        mbar_expect_tx(&kvbar[s], 2 * kTcTile);
-        tma_2d(sK[s], &tk, col, row0 + kstart + (j + 2) * kTcBN, &kvbar[s]);
-        tma_2d(sV[s], &tv, col, row0 + kstart + (j + 2) * kTcBN, &kvbar[s]);
+        for (int k = 0; k < kTcBN / 16; ++k) {
+          const uint64_t ad = sdesc(paddr + (k >> 2) * kTcTile + (k & 3) * 32, 16, 1024);
+          mma(tO, ad, sdesc(vaddr + k * 2048, 8192, 1024), IO, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        commit(ofull);
       }
-      ++kv_armed[s];
+      __syncwarp();
+      ++o_issued;
     }
-  }
-  if (!ok) {
-    // drain: wait (bounded) for this CTA's copies and MMAs still in flight
-    if (tid == 0) {
+    if (!fine) {
+      // drain (bounded): copies and MMAs of this CTA still in flight
+      *abort_flag = 1;
       mbar_wait(qbar, 0, nullptr);
-      for (int s = 0; s < 2; ++s)
-        if (kv_armed[s] > kv_done[s]) mbar_wait(&kvbar[s], kv_done[s] & 1, nullptr);
-      if (s_pending) mbar_wait(sbar, s_done & 1, nullptr);
-      if (o_pending) mbar_wait(obar, o_done & 1, nullptr);
-    }
-  } else if (qpos < T) {
-    const float inv = 1.f / l;
-    bf16* orow = out + ((long long)(row0 + qpos) * H + h) * kTcD;
-#pragma unroll
-    for (int c8 = 0; c8 < kTcD / 8; ++c8) {
-      uint32_t pk[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        __nv_bfloat162 t2 = __floats2bfloat162_rn(o[c8 * 8 + 2 * e] * inv, o[c8 * 8 + 2 * e + 1] * inv);
-        pk[e] = *reinterpret_cast<uint32_t*>(&t2);
+      for (int st = 0; st < 2; ++st) {
+        if (k_armed[st] > k_done[st]) mbar_wait(&kfull[st], k_done[st] & 1, nullptr);
+        if (v_armed[st] > v_done[st]) mbar_wait(&vfull[st], v_done[st] & 1, nullptr);
       }
-      *reinterpret_cast<uint4*>(orow + c8 * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      if (s_issued) mbar_wait(sfull, (s_issued - 1) & 1, nullptr);
+      if (o_issued) mbar_wait(ofull, (o_issued - 1) & 1, nullptr);
     }
-    if (lse) lse[((long long)b * H + h) * T + qpos] = (m + log2f(l)) * 0.6931471805599453f;
+    __syncwarp();
+  } else {
+    // ================= softmax rows =================
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int qpos = q0 + tid;
+    const float sl = 1.4426950408889634f * 0.125f;  // log2(e) / sqrt(64)
+    float mu = -INFINITY;  // exponent base of P and O (scaled log2 units)
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      if (!(ok = warp_wait(sfull, j & 1, err, abort_flag))) break;
+      fence_after();
+      float sc[kTcBN];
+#pragma unroll
+      for (int c = 0; c < kTcBN / 32; ++c) tmem_ld32(tS + lane_off + c * 32, sc + c * 32);
+      fence_before();
+      mbar_arrive(sfree);
+      const int kb0 = kstart + j * kTcBN;
+      if (kb0 + kTcBN - 1 > q0 || kb0 + kTcBN > T) {  // block reaches the diagonal or the end
+#pragma unroll
+        for (int c = 0; c < kTcBN; ++c) {
+          const int kp = kb0 + c;
+          if (kp > qpos || kp >= T) sc[c] = -INFINITY;
+        }
+      }
+      float m4[4];  // four independent chains, then a tree
+#pragma unroll
+      for (int c = 0; c < 4; ++c) m4[c] = sc[c];
+#pragma unroll
+      for (int c = 4; c < kTcBN; ++c) m4[c & 3] = fmaxf(m4[c & 3], sc[c]);
+      const float mnew = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl;
+      float alpha = 1.f;
+      const bool rescale = mnew > mu + kTcRescale;  // false for fully masked rows
+      if (rescale) {
+        alpha = ex2(mu - mnew);  // 0 when mu = -inf
+        mu = mnew;
+      }
+      const float nb = (mu == -INFINITY) ? 0.f : -mu;
+      // O(j-1) complete: the P buffer is free and the O row may be rescaled
+      if (j > 0) {
+        if (!(ok = warp_wait(ofull, (j - 1) & 1, err, abort_flag))) break;
+        fence_after();
+      }
+      float r4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c8 = 0; c8 < kTcBN / 8; ++c8) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2(fmaf(sc[c8 * 8 + 2 * e], sl, nb));
+          const float p1 = ex2(fmaf(sc[c8 * 8 + 2 * e + 1], sl, nb));
+          r4[e] += p0 + p1;
+          __nv_bfloat162 t2 = __floats2bfloat162_rn(p0, p1);
+          pk[e] = *reinterpret_cast<uint32_t*>(&t2);
+        }
+        const int sub = c8 >> 3, chunk = c8 & 7;
+        uint8_t* dst = sP + sub * kTcTile + tid * 128 + ((chunk ^ (tid & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {  // after the exponentials: sc[] is dead
+#pragma unroll
+        for (int c = 0; c < kTcD / 32; ++c) {
+          float ov[32];
+          tmem_ld32(tO + lane_off + c * 32, ov);
+#pragma unroll
+          for (int d = 0; d < 32; ++d) ov[d] *= alpha;
+          tmem_st32(tO + lane_off + c * 32, ov);
+        }
+      }
+      l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
+      fence_proxy_async();  // generic-proxy P stores -> visible to the tensor core
+      fence_before();
+      mbar_arrive(pfull);
+    }
+    // ---- epilogue: O complete -> normalise -> bf16 rows; lse in natural log
+    if (ok && warp_wait(ofull, (nblk - 1) & 1, err, abort_flag)) {
+      fence_after();
+      float ov[kTcD];
+#pragma unroll
+      for (int c = 0; c < kTcD / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ov + c * 32);
+      if (qpos < T) {
+        const float inv = 1.f / l;
+        bf16* orow = out + ((long long)(row0 + qpos) * H + h) * kTcD;
+#pragma unroll
+        for (int c8 = 0; c8 < kTcD / 8; ++c8) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 t2 =
+                __floats2bfloat162_rn(ov[c8 * 8 + 2 * e] * inv, ov[c8 * 8 + 2 * e + 1] * inv);
+            pk[e] = *reinterpret_cast<uint32_t*>(&t2);
+          }
+          *reinterpret_cast<uint4*>(orow + c8 * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+        if (lse) lse[((long long)b * H + h) * T + qpos] = (mu + log2f(l)) * 0.6931471805599453f;
+      }
+    }
   }
   fence_before();
   __syncthreads();
