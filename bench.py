@@ -527,7 +527,7 @@ def run_train_bench(args, world, rank, local):
                    "preset": "index_only_page_memo", "l2": "inputs (5 x 50 MB) larger than L2"},
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": 6 * TB * TT * TH * TD * 2, "d2h_bytes_per_step": 4},
-        "roofline": {"bound": "tensor", "kernel": "window_attention_kernel<64> (forward)",
+        "roofline": {"bound": "tensor", "kernel": "tc_window_attention_kernel (forward, tcgen05)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": kind,
                      "algorithmic_flops_per_launch": flops,

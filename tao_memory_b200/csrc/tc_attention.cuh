@@ -9,9 +9,10 @@
 //     1024-byte-aligned shared memory; K and V have two stages each
 //   * S = Q K^T: tcgen05.mma kind::f16, M=128 N=128 K=64, fp32 accumulator in TMEM
 //   * each thread owns one query row: tcgen05.ld of its S row, window mask,
-//     online softmax in registers, P (bf16) written to shared memory in the
-//     K-major swizzled layout the tensor core reads
-//   * O += P V: tcgen05.mma M=128 N=64 K=128 with V as an MN-major operand; O
+//     online softmax in registers, P (bf16 pairs) written back to TMEM with
+//     tcgen05.st (shared memory bandwidth is left to the MMA operands)
+//   * O += P V: tcgen05.mma M=128 N=64 K=128, A = P read from TMEM, V an MN-major
+//     shared-memory operand; O
 //     stays in TMEM for the whole CTA and is rescaled there only when a row
 //     maximum grows by more than 2^8 (p = 2^(s - stale max) stays <= 256)
 //   * S of the next key block is computed while the softmax of this one runs
@@ -45,6 +46,13 @@ TAO_DEVI void mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t ides
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+// A operand read from TMEM (lanes = rows, 32-bit columns = two consecutive bf16 along K).
+TAO_DEVI void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 TAO_DEVI void commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -102,9 +110,10 @@ TAO_DEVI void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* 
 constexpr int kTcBM = 128, kTcBN = 128, kTcD = 64;
 constexpr int kTcTile = kTcBM * kTcD * 2;  // 16 KB: 128 rows x 128 B
 constexpr int kTcThreads = 160;            // warps 0-3: softmax rows, warp 4: TMA + MMA issue
-// Q, K[2], V[2], P[2] tiles, then 9 mbarriers, the TMEM address slot and the abort flag.
-constexpr int kTcSmem = 7 * kTcTile + 128;
-constexpr int kTcTmemCols = 256;           // S: columns 0-127, O: 128-191
+// Q, K[2], V[2] tiles, then 9 mbarriers, the TMEM address slot and the abort flag.
+constexpr int kTcSmem = 5 * kTcTile + 128;
+// TMEM columns: S fp32 0-127, O fp32 128-191, P bf16 pairs 192-255.
+constexpr int kTcTmemCols = 256;
 // O is rescaled only when a row maximum grows by more than this (log2 units):
 // until then scores are exponentiated against the stale maximum (p <= 2^8).
 constexpr float kTcRescale = 8.f;
@@ -135,7 +144,7 @@ TAO_DEVI bool warp_wait(uint64_t* bar, uint32_t phase, int* err, volatile int* a
 //     once O(j-1) is complete.
 //   softmax (warps 0-3, one query row per thread): sfull(j) -> tcgen05.ld S row ->
 //     sfree -> mask, row max -> ofull(j-1) -> rescale the O row in TMEM if its
-//     maximum moved by more than 2^8 -> P(j) (bf16) to shared memory -> pfull.
+//     maximum moved by more than 2^8 -> P(j) (bf16 pairs) to TMEM -> pfull.
 __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
     const __grid_constant__ CUtensorMap tv, bf16* __restrict__ out, float* __restrict__ lse, int T,
@@ -151,8 +160,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
   uint8_t* const sQ = sm;
   uint8_t* const sK = sm + kTcTile;      // [2] stages
   uint8_t* const sV = sm + 3 * kTcTile;  // [2] stages
-  uint8_t* const sP = sm + 5 * kTcTile;  // two K-major tiles: keys 0-63 and 64-127
-  uint64_t* const bars = reinterpret_cast<uint64_t*>(sm + 7 * kTcTile);
+  uint64_t* const bars = reinterpret_cast<uint64_t*>(sm + 5 * kTcTile);
   uint64_t* const qbar = bars;
   uint64_t* const kfull = bars + 1;  // [2]
   uint64_t* const vfull = bars + 3;  // [2]
@@ -195,7 +203,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
   __syncthreads();
   fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t tS = tbase, tO = tbase + 128;
+  const uint32_t tS = tbase, tO = tbase + 128, tP = tbase + 192;
 
   if (warp == 4) {
     // ================= issuer (the whole warp walks the schedule; lane 0 issues) =====
@@ -262,12 +270,10 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
       ++v_done[st];
       fence_after();
       if (leader) {
-        const uint32_t vaddr = smem_u32(sV + st * kTcTile), paddr = smem_u32(sP);
+        const uint32_t vaddr = smem_u32(sV + st * kTcTile);
 #pragma unroll
-        for (int k = 0; k < kTcBN / 16; ++k) {
-          const uint64_t ad = sdesc(paddr + (k >> 2) * kTcTile + (k & 3) * 32, 16, 1024);
-          mma(tO, ad, sdesc(vaddr + k * 2048, 8192, 1024), IO, (j > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < kTcBN / 16; ++k)  // A = P(j) from TMEM, 16 keys = 8 columns per step
+          mma_ts(tO, tP + k * 8, sdesc(vaddr + k * 2048, 8192, 1024), IO, (j > 0 || k > 0) ? 1u : 0u);
         commit(ofull);
       }
       __syncwarp();
@@ -329,19 +335,17 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
       }
       float r4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c8 = 0; c8 < kTcBN / 8; ++c8) {
-        uint32_t pk[4];
+      for (int half = 0; half < 2; ++half) {
+        float pk[32];  // 64 keys as 32 bf16 pairs (bit patterns), low half = lower key
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2(fmaf(sc[c8 * 8 + 2 * e], sl, nb));
-          const float p1 = ex2(fmaf(sc[c8 * 8 + 2 * e + 1], sl, nb));
-          r4[e] += p0 + p1;
+        for (int e = 0; e < 32; ++e) {
+          const float p0 = ex2(fmaf(sc[half * 64 + 2 * e], sl, nb));
+          const float p1 = ex2(fmaf(sc[half * 64 + 2 * e + 1], sl, nb));
+          r4[e & 3] += p0 + p1;
           __nv_bfloat162 t2 = __floats2bfloat162_rn(p0, p1);
-          pk[e] = *reinterpret_cast<uint32_t*>(&t2);
+          pk[e] = __uint_as_float(*reinterpret_cast<uint32_t*>(&t2));
         }
-        const int sub = c8 >> 3, chunk = c8 & 7;
-        uint8_t* dst = sP + sub * kTcTile + tid * 128 + ((chunk ^ (tid & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tmem_st32(tP + lane_off + half * 32, pk);
       }
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {  // after the exponentials: sc[] is dead
 #pragma unroll
@@ -354,7 +358,6 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
         }
       }
       l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
-      fence_proxy_async();  // generic-proxy P stores -> visible to the tensor core
       fence_before();
       mbar_arrive(pfull);
     }
