@@ -251,6 +251,8 @@ typedef struct TaoTrainGrads {
   float* dC;
   float* dz;
   void* dc_partial;
+  float* dq_acc;  /* fp32 [B][T][H][D] scratch for the tensor-core attention backward
+                     (width 64); NULL selects the mma.sync kernels */
 } TaoTrainGrads;
 
 /* Number of (256-query tile, visible fine) pairs of a T-token sequence. */

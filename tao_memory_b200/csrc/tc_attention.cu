@@ -8,6 +8,7 @@
 
 #include "../../include/tao_b200.h"
 #include "tc_attention.cuh"
+#include "tc_attention_bwd.cuh"
 #include "window_attention.cuh"
 
 void tao_set_last_error(const char* msg);
@@ -38,6 +39,19 @@ bool row_map(CUtensorMap* map, const void* base, unsigned long long rows, unsign
   cuuint32_t box[2] = {64, 128};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// [rows][cols] fp32 row-major, boxes of 32 rows x 32 columns (128 B), 128B swizzle.
+bool f32_map(CUtensorMap* map, const void* base, unsigned long long rows, unsigned long long cols) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -103,6 +117,42 @@ int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* o
     }
     window_attention_kernel<128><<<grid, 128, smem, s>>>(p);
   }
+  return TAO_OK;
+}
+
+int attention_variant() { return g_attention_variant; }
+
+// Windowed attention backward on the tensor cores (width 64): dK, dV and dQ of
+// contiguous [B][T][H][64] operands.  dq_acc is fp32 scratch of the same shape.
+int launch_attention_backward_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* dout, const float* lse,
+                                 const float* rowdot, bf16* dq, bf16* dk, bf16* dv, float* dq_acc, int B, int T,
+                                 int H, int* err, cudaStream_t s) {
+  for (const void* p : {(const void*)q, (const void*)k, (const void*)v, (const void*)dout, (const void*)dq_acc})
+    if (!aligned(p)) {
+      tao_set_last_error("attention backward operands must be 16-byte aligned");
+      return TAO_ERR_ARG;
+    }
+  CUtensorMap mq, mk, mv, mo, mdq;
+  const unsigned long long rows = (unsigned long long)B * T, cols = (unsigned long long)H * tb::kD;
+  if (!row_map(&mq, q, rows, cols) || !row_map(&mk, k, rows, cols) || !row_map(&mv, v, rows, cols) ||
+      !row_map(&mo, dout, rows, cols) || !f32_map(&mdq, dq_acc, rows, cols)) {
+    tao_set_last_error("cuTensorMapEncodeTiled failed");
+    return TAO_ERR_CUDA;
+  }
+  if (!smem_attr(tc_attention_bwd_kernel, tb::kSmem)) {
+    tao_set_last_error("smem attribute");
+    return TAO_ERR_CUDA;
+  }
+  const long long n = (long long)B * T * H * tb::kD;
+  if (cudaMemsetAsync(dq_acc, 0, (size_t)n * sizeof(float), s) != cudaSuccess) {
+    tao_set_last_error("dq accumulator memset failed");
+    return TAO_ERR_CUDA;
+  }
+  TcBwdArgs a{lse, rowdot, dk, dv, T, H, err};
+  tc_attention_bwd_kernel<<<dim3((T + tb::kBN - 1) / tb::kBN, B * H), tb::kThreads, tb::kSmem, s>>>(mq, mk, mv, mo,
+                                                                                                    mdq, a);
+  const long long n8 = n / 8;
+  dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, dq, n8);
   return TAO_OK;
 }
 

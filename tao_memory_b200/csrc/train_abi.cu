@@ -11,6 +11,10 @@ void tao_take_profile_events(cudaEvent_t* start, cudaEvent_t* stop);
 namespace tao {
 int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* out, float* lse, int B,
                             int T, int H, int D, int* err, cudaStream_t s);
+int launch_attention_backward_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* dout, const float* lse,
+                                 const float* rowdot, bf16* dq, bf16* dk, bf16* dv, float* dq_acc, int B, int T,
+                                 int H, int* err, cudaStream_t s);
+int attention_variant();
 }  // namespace tao
 
 namespace {
@@ -118,11 +122,17 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   const Geometry g = geometry(a.dm.T);
   const int B = a.dm.B, H = a.dm.H, T = a.dm.T;
   fusion_bwd_kernel<D><<<dim3((T + 8 * kFusionRowsPerWarp - 1) / (8 * kFusionRowsPerWarp), B * H), 256, 0, s>>>(a);
-  const size_t asmem = (size_t)(2 * 64 + 4 * 64) * D * 2 + 256 * 4;
-  if (!tsmem(attn_bwd_kv_kernel<D>, asmem) || !tsmem(attn_bwd_q_kernel<D>, asmem))
-    return tfail(TAO_ERR_CUDA, "smem attribute");
-  attn_bwd_kv_kernel<D><<<dim3((T + 63) / 64, B * H), 128, asmem, s>>>(a);
-  attn_bwd_q_kernel<D><<<dim3((T + 63) / 64, B * H), 128, asmem, s>>>(a);
+  if (D == 64 && a.dq_acc && attention_variant() == 1) {
+    if (int rc = launch_attention_backward_tc(a.q, a.k, a.v, a.d_local, a.lse, a.dv_row, a.dq, a.dk, a.dv,
+                                              a.dq_acc, B, T, H, a.err, s))
+      return rc;
+  } else {
+    const size_t asmem = (size_t)(2 * 64 + 4 * 64) * D * 2 + 256 * 4;
+    if (!tsmem(attn_bwd_kv_kernel<D>, asmem) || !tsmem(attn_bwd_q_kernel<D>, asmem))
+      return tfail(TAO_ERR_CUDA, "smem attribute");
+    attn_bwd_kv_kernel<D><<<dim3((T + 63) / 64, B * H), 128, asmem, s>>>(a);
+    attn_bwd_q_kernel<D><<<dim3((T + 63) / 64, B * H), 128, asmem, s>>>(a);
+  }
   const size_t rsmem = ReadBwdSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the read backward kernel");
   if (!tsmem(read_bwd_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
@@ -168,6 +178,7 @@ int tao_train_backward(const void* grad_out, const void* q, const void* k, const
   a.dq = W(grads->dq); a.dk = W(grads->dk); a.dv = W(grads->dv); a.d_raw_q = W(grads->d_raw_q);
   a.d_raw_k = W(grads->d_raw_k); a.dC = grads->dC; a.dz = grads->dz;
   a.dcp = W(grads->dc_partial);
+  a.dq_acc = grads->dq_acc;
   a.npairs = g.vmax * (g.vmax + 1) / 2;
   a.dm = tao::TrainDims{batch, tokens, heads, g.S, (long long)heads * width};
   a.pages = g.pages;

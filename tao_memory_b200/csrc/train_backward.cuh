@@ -22,6 +22,7 @@ struct BwdArgs {
   bf16 *dq, *dk, *dv, *d_raw_q, *d_raw_k;
   float *dC, *dz;                // fp32 [B,H,S,D,D] (reduced), [B,H,S,D] accumulators
   bf16* dcp;                     // per-(tile, fine) dC partials [B,H,npairs,D,D]
+  float* dq_acc;                 // fp32 [B,T,H,D] dQ accumulator (tensor-core path) or null
   int npairs;                    // sum over tiles of visible fines
   TrainDims dm;
   int pages, mmax;

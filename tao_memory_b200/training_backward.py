@@ -12,7 +12,7 @@ _BF16 = torch.bfloat16
 class _Grads(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("dq", "dk", "dv", "d_raw_q", "d_raw_k", "d_fusion_a",
                                              "d_fusion_b", "d_local", "gn", "d_rq_f", "gd", "row_dot",
-                                             "dC", "dz", "dc_partial")]
+                                             "dC", "dz", "dc_partial", "dq_acc")]
 
 
 def backward(ctx, grad):
@@ -34,7 +34,8 @@ def backward(ctx, grad):
               dC=torch.empty(b, h, s, d, d, dtype=torch.float32, device=dev),
               dz=torch.zeros(b, h, s, d, dtype=torch.float32, device=dev),
               dc_partial=torch.zeros(b, h, max(1, _lib.lib().tao_train_pairs(t)), d, d, dtype=_BF16,
-                                     device=dev))
+                                     device=dev),
+              dq_acc=torch.empty(b, t, h, d, dtype=torch.float32, device=dev))
     gdesc = _Grads(*(gr[n].data_ptr() for n, _ in _Grads._fields_))
     sdesc = _Buffers(*(saved[n].data_ptr() for n in ("local", "lse", "fine_z", "fine_c", "page_prefix",
                                                     "num", "den", "sel", "err")),
