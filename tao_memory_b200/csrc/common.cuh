@@ -39,6 +39,16 @@ TAO_DEVI float warp_max(float v) {
   return v;
 }
 
+// Products of two bf16 pairs rounded to bf16, lane by lane.  The product of two
+// bf16 values is exact in fp32, so this equals rb(a * b) for each lane.
+TAO_DEVI uint32_t hmul2u(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+// Low / high bf16 of a pair as fp32.
+TAO_DEVI float lo_f(uint32_t x) { return __uint_as_float(x << 16); }
+TAO_DEVI float hi_f(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
+
 // Unpack 8 bf16 (one 16-byte vector) into fp32.
 TAO_DEVI void unpack8(const uint4& u, float* f) {
   const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);

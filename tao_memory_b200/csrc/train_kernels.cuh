@@ -204,7 +204,7 @@ struct ReadSmem {
 };
 
 template <int D>
-__global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
+__global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   using namespace wa;
   constexpr int NBUF = ReadSmem<D>::NBUF;
   const int tile = blockIdx.x, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
@@ -237,8 +237,9 @@ __global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
   const uint32_t sH = smem_u32(ptr);   ptr += 256 * D * 2;
   const uint32_t sA = smem_u32(ptr);   ptr += 256 * D * 2;
   const uint32_t sC = smem_u32(ptr);   ptr += NBUF * D * D * 2;
-  float* pwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   float* pzS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
+  bf16* pw2S = reinterpret_cast<bf16*>(ptr);   ptr += (size_t)P * D * 2;   // page weights (bf16 values)
+  ptr += (size_t)P * D * 2;                                                // (keeps the old footprint)
   bf16* swS = reinterpret_cast<bf16*>(ptr);    ptr += ((size_t)V * D * 2 + 15) / 16 * 16;
   float* topS = reinterpret_cast<float*>(ptr); ptr += 256 * (size_t)(a.mmax + 1) * 4;
   int* topI = reinterpret_cast<int*>(ptr);     ptr += 256 * (size_t)(a.mmax + 1) * 4;
@@ -260,7 +261,7 @@ __global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
     for (int p = 0; p < P; ++p) mx = fmaxf(mx, pzS[p * D + d]);
     float sum = 0.f;
     for (int p = 0; p < P; ++p) sum += expf(pzS[p * D + d] - mx);
-    for (int p = 0; p < P; ++p) pwS[p * D + d] = rb(__fdiv_rn(expf(pzS[p * D + d] - mx), sum));
+    for (int p = 0; p < P; ++p) pw2S[p * D + d] = tobf(__fdiv_rn(expf(pzS[p * D + d] - mx), sum));
   }
   const bf16* zb = a.z + ((long long)b * a.dm.H + h) * a.dm.S * D;
   for (int idx = tid; idx < V * D; idx += 256) {
@@ -295,30 +296,56 @@ __global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
   }
   __syncthreads();
 
-  // ---- 2. routing of query q (thread q)
+  // ---- 2. routing of query q (thread q).  Products are formed two at a time as
+  // bf16 pairs (bit-identical to rounding each fp32 product) and summed in fp32
+  // in channel order.
   float* tS = topS + q * TS;
   int* tI = topI + q * TS;
   int nt = 0;
-  auto hval = [&](int d) -> float { return bf(*reinterpret_cast<const bf16*>(smem + swz(q, d, D))); };
+  const uint32_t* pw2 = reinterpret_cast<const uint32_t*>(pw2S);  // [P][D/2]
+  const uint32_t* sw2 = reinterpret_cast<const uint32_t*>(swS);   // [V][D/2]
+  auto hchunk = [&](int c) -> uint4 { return *reinterpret_cast<const uint4*>(smem + swz(q, c * 8, D)); };
+  // hv = bf16(h * pw[page]) as D/2 pairs
+  auto page_hv = [&](int page, uint32_t* hv) {
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      const uint4 hc = hchunk(c);
+      const uint4 pc = *reinterpret_cast<const uint4*>(pw2 + page * (D / 2) + c * 4);
+      hv[c * 4 + 0] = hmul2u(hc.x, pc.x);
+      hv[c * 4 + 1] = hmul2u(hc.y, pc.y);
+      hv[c * 4 + 2] = hmul2u(hc.z, pc.z);
+      hv[c * 4 + 3] = hmul2u(hc.w, pc.w);
+    }
+  };
   if (live) {
+    // page scores once, then the K best pages (ties: lower page first)
+    float ps[64];
+    for (int p = 0; p < completed; ++p) {
+      float m = 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        const uint4 hc = hchunk(c);
+        const uint4 pc = *reinterpret_cast<const uint4*>(pw2 + p * (D / 2) + c * 4);
+        const uint32_t pr[4] = {hmul2u(hc.x, pc.x), hmul2u(hc.y, pc.y), hmul2u(hc.z, pc.z), hmul2u(hc.w, pc.w)};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          m += lo_f(pr[u]);
+          m += hi_f(pr[u]);
+        }
+      }
+      ps[p] = rb(m);
+    }
     uint64_t chosen = 0;
     for (int k = 0; k < K; ++k) {
       float best = -INFINITY;
       int bp = 0;
       for (int p = 0; p < completed; ++p) {
         if ((chosen >> p) & 1ull) continue;
-        float m = 0.f;
-        for (int d = 0; d < D; ++d) m += rb(__fmul_rn(hval(d), pwS[p * D + d]));
-        m = rb(m);
-        if (m > best) { best = m; bp = p; }
+        if (ps[p] > best) { best = ps[p]; bp = p; }
       }
       chosen |= 1ull << bp;
     }
-    auto consider = [&](int id, int page) {
-      float sc = 0.f;
-      for (int d = 0; d < D; ++d)
-        sc += rb(__fmul_rn(rb(__fmul_rn(hval(d), pwS[page * D + d])), bf(swS[id * D + d])));
-      sc = rb(sc);
+    auto consider = [&](int id, float sc) {
       int pos = 0;
       while (pos < nt && tS[pos] >= sc) ++pos;   // stable: equal scores keep the older id first
       if (pos >= M) return;
@@ -328,10 +355,30 @@ __global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
       tI[pos] = id;
       if (nt < M) ++nt;
     };
+    // candidate fines of a page: score = bf16(sum_d bf16(hv * w_fine))
+    auto page_candidates = [&](int page, int first, int count) {
+      uint32_t hv[D / 2];
+      page_hv(page, hv);
+      for (int j = 0; j < count; ++j) {
+        const int id = first + j;
+        float sc = 0.f;
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+          const uint4 wc = *reinterpret_cast<const uint4*>(sw2 + id * (D / 2) + c * 4);
+          const uint32_t pr[4] = {hmul2u(hv[c * 4], wc.x), hmul2u(hv[c * 4 + 1], wc.y), hmul2u(hv[c * 4 + 2], wc.z),
+                                  hmul2u(hv[c * 4 + 3], wc.w)};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            sc += lo_f(pr[u]);
+            sc += hi_f(pr[u]);
+          }
+        }
+        consider(id, rb(sc));
+      }
+    };
     for (int p = 0; p < completed; ++p)
-      if ((chosen >> p) & 1ull)
-        for (int j = 0; j < kGroup; ++j) consider(p * kGroup + j, p);
-    for (int j = 0; j < pending; ++j) consider(completed * kGroup + j, completed);
+      if ((chosen >> p) & 1ull) page_candidates(p, p * kGroup, kGroup);
+    if (pending > 0) page_candidates(completed, completed * kGroup, pending);
     float den = 0.f;
     for (int m = 0; m < nt; ++m) {
       den += tS[m];
@@ -375,24 +422,19 @@ __global__ void __launch_bounds__(256) train_read_kernel(ReadArgs a) {
     const int s2 = list[i];
     const int buf = (NBUF == 2) ? (i & 1) : 0;
     if (NBUF == 2 && i + 1 < nu) load_c(list[i + 1], buf ^ 1);
-    // A_s row q
-    if (live) {
-      bool sel = false;
+    // A_s row q: bf16(hv * w_s) where query q selected fine s2, else zero
+    bool sel = false;
+    if (live)
       for (int m = 0; m < nt; ++m) sel |= (tI[m] == s2);
-      const int page = s2 / kGroup;
+    if (sel) {
+      uint32_t hv[D / 2];
+      page_hv(s2 / kGroup, hv);
+#pragma unroll
       for (int c = 0; c < D / 8; ++c) {
-        __nv_bfloat162 o[4];
-        if (sel) {
-          for (int e = 0; e < 4; ++e) {
-            const int d = c * 8 + 2 * e;
-            const float a0 = rb(__fmul_rn(rb(__fmul_rn(hval(d), pwS[page * D + d])), bf(swS[s2 * D + d])));
-            const float a1 = rb(__fmul_rn(rb(__fmul_rn(hval(d + 1), pwS[page * D + d + 1])), bf(swS[s2 * D + d + 1])));
-            o[e] = __floats2bfloat162_rn(a0, a1);
-          }
-        } else {
-          for (int e = 0; e < 4; ++e) o[e] = __floats2bfloat162_rn(0.f, 0.f);
-        }
-        *reinterpret_cast<uint4*>(smem + 256 * D * 2 + swz(q, c * 8, D)) = *reinterpret_cast<uint4*>(o);
+        const uint4 wc = *reinterpret_cast<const uint4*>(sw2 + s2 * (D / 2) + c * 4);
+        const uint4 o = make_uint4(hmul2u(hv[c * 4], wc.x), hmul2u(hv[c * 4 + 1], wc.y),
+                                   hmul2u(hv[c * 4 + 2], wc.z), hmul2u(hv[c * 4 + 3], wc.w));
+        *reinterpret_cast<uint4*>(smem + 256 * D * 2 + swz(q, c * 8, D)) = o;
       }
     } else {
       for (int c = 0; c < D / 8; ++c)
