@@ -452,7 +452,7 @@ template <int D>
 struct ReadBwdSmem {
   static constexpr int NQ = (D == 64) ? 256 : 128;  // queries (= threads) per CTA
   static size_t bytes(int P, int V, int mmax) {
-    return 3 * (size_t)NQ * D * 2 + (size_t)D * D * 2 + 4 * (size_t)P * D * 4 +
+    return 4 * (size_t)NQ * D * 2 + (size_t)D * D * 2 + 4 * (size_t)P * D * 4 + (size_t)P * D * 2 +
            ((size_t)V * D * 2 + 15) / 16 * 16 + (size_t)NQ * mmax * 2 + NQ * 4 + NQ +
            (size_t)D * 4 + (size_t)(V + 8) * 4 * 2 + 64;
   }
@@ -483,12 +483,14 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
   const uint32_t sG = smem_u32(ptr);  ptr += NQ * D * 2;
   const uint32_t sA = smem_u32(ptr);  ptr += NQ * D * 2;
   const uint32_t sC = smem_u32(ptr);  ptr += D * D * 2;
+  uint8_t* hvB = ptr;                 ptr += NQ * D * 2;  // bf16(h * pw[page]) of the current page
   uint8_t* hB = smem;
   uint8_t* aB = smem + 2 * NQ * D * 2;
   float* pwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* pzS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* dpwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   float* dpzS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
+  bf16* pw2S = reinterpret_cast<bf16*>(ptr);    ptr += (size_t)P * D * 2;  // page weights as bf16
   bf16* swS = reinterpret_cast<bf16*>(ptr);     ptr += ((size_t)V * D * 2 + 15) / 16 * 16;
   int16_t* selS = reinterpret_cast<int16_t*>(ptr); ptr += (size_t)NQ * M * 2;
   float* gdS = reinterpret_cast<float*>(ptr);   ptr += NQ * 4;
@@ -514,7 +516,10 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
     for (int pg = 0; pg < P; ++pg) mx = fmaxf(mx, pzS[pg * D + d]);
     float sum = 0.f;
     for (int pg = 0; pg < P; ++pg) sum += expf(pzS[pg * D + d] - mx);
-    for (int pg = 0; pg < P; ++pg) pwS[pg * D + d] = rb(__fdiv_rn(expf(pzS[pg * D + d] - mx), sum));
+    for (int pg = 0; pg < P; ++pg) {
+      pwS[pg * D + d] = rb(__fdiv_rn(expf(pzS[pg * D + d] - mx), sum));
+      pw2S[pg * D + d] = tobf(pwS[pg * D + d]);
+    }
   }
   const bf16* zb = a.z + ((long long)b * a.dm.H + h) * a.dm.S * D;
   for (int idx = tid; idx < V * D; idx += NQ) {
@@ -585,6 +590,11 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
       for (int x = 0; x < 4; ++x) dhv[i][j][x] = dh[i][j][x] = 0.f;
   const bf16* cb = a.C + ((long long)b * a.dm.H + h) * a.dm.S * (long long)D * D;
   int cur_page = -1;
+  const uint32_t* pw2 = reinterpret_cast<const uint32_t*>(pw2S);
+  const uint32_t* sw2 = reinterpret_cast<const uint32_t*>(swS);
+  auto pair_at = [&](const uint8_t* base, int r, int d) -> uint32_t {  // bf16 pair (d even) of row r
+    return *reinterpret_cast<const uint32_t*>(base + swz(r, d, D));
+  };
   auto flush_page = [&](int pg) {
     // dh += bf16(bf16(dhv)*pw[pg]) ; dpw[pg] += sum_q bf16(bf16(dhv)*h)
     float part[NTL][2];
@@ -593,16 +603,21 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
 #pragma unroll
     for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-      for (int j = 0; j < NTL; ++j)
+      for (int xp = 0; xp < 2; ++xp) {
+        const int r = warp * 32 + mi * 16 + g + xp * 8;
 #pragma unroll
-        for (int x = 0; x < 4; ++x) {
-          const int r = warp * 32 + mi * 16 + g + (x >> 1) * 8;
-          const int d = j * 8 + c4 * 2 + (x & 1);
-          const float v = rb(dhv[mi][j][x]);
-          dh[mi][j][x] += rb(__fmul_rn(v, pwS[pg * D + d]));
-          part[j][x & 1] += rb(__fmul_rn(v, hval(r, d)));
-          dhv[mi][j][x] = 0.f;
+        for (int j = 0; j < NTL; ++j) {
+          const int d = j * 8 + c4 * 2;
+          const uint32_t v2 = wa::pack_bf16(dhv[mi][j][2 * xp], dhv[mi][j][2 * xp + 1]);
+          const uint32_t pp = hmul2u(v2, pw2[(pg * D + d) / 2]);
+          const uint32_t hh = hmul2u(v2, pair_at(hB, r, d));
+          dh[mi][j][2 * xp] += lo_f(pp);
+          dh[mi][j][2 * xp + 1] += hi_f(pp);
+          part[j][0] += lo_f(hh);
+          part[j][1] += hi_f(hh);
+          dhv[mi][j][2 * xp] = dhv[mi][j][2 * xp + 1] = 0.f;
         }
+      }
 #pragma unroll
     for (int j = 0; j < NTL; ++j)
 #pragma unroll
@@ -620,6 +635,14 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
     if (pg != cur_page) {
       if (cur_page >= 0) flush_page(cur_page);
       cur_page = pg;
+      // hv = bf16(h * pw[pg]) of this thread's query row (read by all threads after the next barrier)
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        const uint4 hc = *reinterpret_cast<const uint4*>(hB + swz(q, c * 8, D));
+        const uint4 pc = *reinterpret_cast<const uint4*>(pw2 + (pg * D + c * 8) / 2);
+        *reinterpret_cast<uint4*>(hvB + swz(q, c * 8, D)) =
+            make_uint4(hmul2u(hc.x, pc.x), hmul2u(hc.y, pc.y), hmul2u(hc.z, pc.z), hmul2u(hc.w, pc.w));
+      }
     }
     // load C_s, build A_s and the selection flags
     for (int idx = tid; idx < D * D / 8; idx += NQ) {
@@ -631,18 +654,15 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
     if (live)
       for (int m = 0; m < M; ++m) sel |= (selS[q * M + m] == sf);
     selq[q] = sel;
+#pragma unroll
     for (int c = 0; c < D / 8; ++c) {
-      __nv_bfloat162 o[4];
-      for (int e = 0; e < 4; ++e) {
-        const int d = c * 8 + 2 * e;
-        float a0 = 0.f, a1 = 0.f;
-        if (sel) {
-          a0 = rb(__fmul_rn(rb(__fmul_rn(hval(q, d), pwS[pg * D + d])), bf(swS[sf * D + d])));
-          a1 = rb(__fmul_rn(rb(__fmul_rn(hval(q, d + 1), pwS[pg * D + d + 1])), bf(swS[sf * D + d + 1])));
-        }
-        o[e] = __floats2bfloat162_rn(a0, a1);
+      uint4 o = make_uint4(0, 0, 0, 0);
+      if (sel) {
+        const uint4 hc = *reinterpret_cast<const uint4*>(hvB + swz(q, c * 8, D));
+        const uint4 wc = *reinterpret_cast<const uint4*>(sw2 + (sf * D + c * 8) / 2);
+        o = make_uint4(hmul2u(hc.x, wc.x), hmul2u(hc.y, wc.y), hmul2u(hc.z, wc.z), hmul2u(hc.w, wc.w));
       }
-      *reinterpret_cast<uint4*>(aB + swz(q, c * 8, D)) = *reinterpret_cast<uint4*>(o);
+      *reinterpret_cast<uint4*>(aB + swz(q, c * 8, D)) = o;
     }
     cp_wait<0>();
     __syncthreads();
@@ -680,17 +700,22 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
 #pragma unroll
     for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        const int r = warp * 32 + mi * 16 + g + (x >> 1) * 8;
+      for (int xp = 0; xp < 2; ++xp) {
+        const int r = warp * 32 + mi * 16 + g + xp * 8;
         if (!selq[r]) continue;
         const float gdv = gdS[r];
 #pragma unroll
         for (int j = 0; j < NTL; ++j) {
-          const int d = j * 8 + c4 * 2 + (x & 1);
-          const float dav = rb(__fadd_rn(rb(da[mi][j][x]), gdv));
-          dhv[mi][j][x] += rb(__fmul_rn(dav, bf(swS[sf * D + d])));
-          const float hv = rb(__fmul_rn(hval(r, d), pwS[pg * D + d]));
-          wpart[j][x & 1] += rb(__fmul_rn(dav, hv));
+          const int d = j * 8 + c4 * 2;
+          // dA = bf16(bf16(gn . C^T) + gd), a pair of channels
+          const uint32_t dav = wa::pack_bf16(__fadd_rn(rb(da[mi][j][2 * xp]), gdv),
+                                             __fadd_rn(rb(da[mi][j][2 * xp + 1]), gdv));
+          const uint32_t pw_ = hmul2u(dav, sw2[(sf * D + d) / 2]);
+          const uint32_t ph = hmul2u(dav, pair_at(hvB, r, d));
+          dhv[mi][j][2 * xp] += lo_f(pw_);
+          dhv[mi][j][2 * xp + 1] += hi_f(pw_);
+          wpart[j][0] += lo_f(ph);
+          wpart[j][1] += hi_f(ph);
         }
       }
 #pragma unroll
