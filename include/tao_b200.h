@@ -133,6 +133,16 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
  * work item.  Results agree to fp32 summation order. */
 int tao_decode_variant(int variant);
 
+/* Graph mode for the calling host thread (on != 0): tao_decode_step then always
+ * launches its route and seal kernels, which decide on the device from each state's
+ * cursor whether the token refreshes the routes or seals a block.  A step launched
+ * in this mode can be captured once into a CUDA graph and replayed for every later
+ * token while the fine-bank capacity (grid sizes) is unchanged; nothing is re-captured
+ * at a seal.  Reference counterpart: HistoryRegionGraph
+ * (history_region_graph.py:10-113), which captures only the history read and
+ * re-captures at every seal. */
+int tao_decode_graph_mode(int on);
+
 /* Read and clear the device error word of a workspace (synchronises `stream`).
  * Returns TAO_OK or TAO_ERR_DEVICE; *flags receives the raw bits. */
 int tao_stream_check(void* workspace, int* flags, void* stream);

@@ -186,6 +186,11 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
   return check_launch("finalize_kernel");
 }
 
+// Graph mode (tao_decode_graph_mode): every decode step launches the route and seal
+// kernels, which decide on the device from the cursor whether this token refreshes
+// or seals, so one captured launch sequence serves every token.
+thread_local int g_graph_mode = 0;
+
 template <int D>
 int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaStream_t s) {
   using namespace tao;
@@ -310,7 +315,13 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
   a.fine_part = reinterpret_cast<float*>(ws + L.fine_part);
   a.pmax = pmax;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (g_graph_mode) refresh = seal = true;
   return width == 64 ? launch_decode<64>(a, ms, refresh, seal, s) : launch_decode<128>(a, ms, refresh, seal, s);
+}
+
+int tao_decode_graph_mode(int on) {
+  g_graph_mode = on ? 1 : 0;
+  return TAO_OK;
 }
 
 const char* tao_last_error(void) { return g_last_error.c_str(); }

@@ -140,7 +140,7 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   read_bwd_kernel<D><<<dim3(g.tiles * (256 / NQ), B * H), NQ, rsmem, s>>>(a);
   if (g.S > 0) {
     dc_reduce_kernel<D><<<B * H * g.S, 256, 0, s>>>(a, g.tiles);
-    const size_t wsmem = (size_t)2 * 256 * D * 2 + (size_t)D * D * 2 + 6 * D * 4;
+    const size_t wsmem = WriterBwdSmem<D>::bytes();
     if (!tsmem(writer_bwd_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
     writer_bwd_kernel<D><<<B * H * g.S, 256, wsmem, s>>>(a);
   }

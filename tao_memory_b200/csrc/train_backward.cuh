@@ -74,7 +74,9 @@ __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
         const float s0 = rb(__fadd_rn(base0, 0.f));
         const float s2 = rb(__fadd_rn(rb(__fmul_rn(fa[j][2], qv)), fb[j][2]));
         const float mx = fmaxf(s0, s2);
-        const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
+        // the larger term is exp(0) = 1 exactly: one exponential per element
+        const float eo = expf(fminf(s0, s2) - mx);
+        const float e0 = s0 >= s2 ? 1.f : eo, e2 = s0 >= s2 ? eo : 1.f;
         const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
         const float l2 = rb(__fmul_rn(2.f, loc)), fg = rb(__fmul_rn(gain, fine));
         const float drho0 = rb(__fmul_rn(gv, l2)), drho2 = rb(__fmul_rn(gv, fg));
@@ -851,18 +853,37 @@ __global__ void __launch_bounds__(256) dc_reduce_kernel(BwdArgs a, int tiles) {
 
 // ---------------------------------------------------------------------------
 // Writer backward: one CTA (256 threads) per (b, h, block s).
+//   p = bf16(e / Z), e = bf16(exp(bf16(k - m))) are formed once into shared memory
+//   (p over the raw keys, e in its own tile for width 64), then
+//   dv += P . dC and dprob = V . dC^T run as two separate tensor-core passes so the
+//   width-64 kernel fits two CTAs per SM.
 // ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
+struct WriterBwdSmem {
+  static constexpr bool kStoreE = (D == 64);
+  static constexpr size_t bytes() {
+    return (size_t)(kStoreE ? 3 : 2) * 256 * D * 2 + (size_t)D * D * 2 + (size_t)256 * (D / 32) * 4 +
+           (size_t)6 * D * 4;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdArgs a) {
   using namespace wa;
-  constexpr int NT = 256, CH = D / 8, NTL = D / 8;
+  constexpr int NT = 256, CH = D / 8, NTL = D / 8, TW = D / 32;
+  constexpr bool kStoreE = WriterBwdSmem<D>::kStoreE;
   const int s = blockIdx.x % a.dm.S, h = (blockIdx.x / a.dm.S) % a.dm.H, b = blockIdx.x / (a.dm.S * a.dm.H);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t sK = smem_u32(smem), sV = sK + NT * D * 2, sD = sV + NT * D * 2;
-  uint8_t* kB = smem;
-  uint8_t* dB = smem + 2 * NT * D * 2;
-  float* mx = reinterpret_cast<float*>(smem + 2 * NT * D * 2 + D * D * 2);
+  uint8_t* ptr = smem;
+  const uint32_t sK = smem_u32(ptr);   // raw keys, then probabilities p
+  uint8_t* kB = ptr;                   ptr += NT * D * 2;
+  const uint32_t sV = smem_u32(ptr);   ptr += NT * D * 2;
+  uint8_t* eB = ptr;                   ptr += kStoreE ? NT * D * 2 : 0;
+  const uint32_t sD = smem_u32(ptr);
+  uint8_t* dB = ptr;                   ptr += D * D * 2;
+  uint32_t* tieS = reinterpret_cast<uint32_t*>(ptr);  ptr += NT * TW * 4;   // k == max, one bit per (t, d)
+  float* mx = reinterpret_cast<float*>(ptr);
   float* zp = mx + D;
   float* dzS = zp + D;
   float* dZp = dzS + D;   // sum_t of the partition term from prob
@@ -890,50 +911,51 @@ __global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
   }
   cp_wait<0>();
   __syncthreads();
-  auto kat = [&](int t, int d) -> float { return bf(*reinterpret_cast<const bf16*>(kB + swz(t, d, D))); };
+  auto at = [&](uint8_t* base, int t, int d) -> bf16& { return *reinterpret_cast<bf16*>(base + swz(t, d, D)); };
   __shared__ float stat_scratch[2 * 256];
-  channel_stats<D, 256>(kat, mx, zp, stat_scratch);
-  // probability p[t][d] = bf16(e / Z), recomputed from the staged raw keys
-  auto pval = [&](int t, int d) -> float {
-    return rb(__fdiv_rn(rb(expf(rb(__fsub_rn(kat(t, d), mx[d])))), zp[d]));
-  };
-  const int g = lane >> 2, c4 = lane & 3;
-  // dprob = V . dC^T and dv_w = P . dC  (rows: tokens of this warp)
-  float dp[2][NTL][4], dvw[2][NTL][4];
+  channel_stats<D, 256>([&](int t, int d) { return bf(at(kB, t, d)); }, mx, zp, stat_scratch);
+  // ties of the max (thread t: its token row)
+  {
+    const int t = tid;
 #pragma unroll
-  for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-    for (int j = 0; j < NTL; ++j)
-#pragma unroll
-      for (int x = 0; x < 4; ++x) dp[mi][j][x] = dvw[mi][j][x] = 0.f;
-#pragma unroll
-  for (int kt = 0; kt < D / 16; ++kt) {
-    uint32_t av[2][4], ap[2][4];
-#pragma unroll
-    for (int mi = 0; mi < 2; ++mi) {
-      const int r = warp * 32 + mi * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-      const int c = kt * 16 + (lane >> 4) * 8;
-      ldsm_x4(sV + swz(r, c, D), av[mi][0], av[mi][1], av[mi][2], av[mi][3]);
-      const int t0 = warp * 32 + mi * 16 + g, d0 = kt * 16 + c4 * 2;
-      ap[mi][0] = pack_bf16(pval(t0, d0), pval(t0, d0 + 1));
-      ap[mi][1] = pack_bf16(pval(t0 + 8, d0), pval(t0 + 8, d0 + 1));
-      ap[mi][2] = pack_bf16(pval(t0, d0 + 8), pval(t0, d0 + 9));
-      ap[mi][3] = pack_bf16(pval(t0 + 8, d0 + 8), pval(t0 + 8, d0 + 9));
+    for (int w = 0; w < TW; ++w) {
+      uint32_t bits = 0;
+      for (int j = 0; j < 32; ++j) bits |= (uint32_t)(bf(at(kB, t, w * 32 + j)) == mx[w * 32 + j]) << j;
+      tieS[t * TW + w] = bits;
     }
+  }
+  __syncthreads();
+  // e and p, once per element
+  for (int idx = tid; idx < NT * D; idx += 256) {
+    const int t = idx / D, d = idx % D;
+    const float e = rb(expf(rb(__fsub_rn(bf(at(kB, t, d)), mx[d]))));
+    if (kStoreE) at(eB, t, d) = tobf(e);
+    at(kB, t, d) = tobf(__fdiv_rn(e, zp[d]));
+  }
+  __syncthreads();
+  const int g = lane >> 2, c4 = lane & 3;
+  bf16* dvb = a.dv + tok0 * row + (long long)h * D;
+  // ---- pass 1: dv_w = P . dC (rows: this warp's 32 tokens) ; dv += dv_w
+  {
+    float dvw[2][NTL][4];
 #pragma unroll
-    for (int np = 0; np < D / 16; ++np) {
-      uint32_t b0, b1, b2, b3;
-      {  // B = dC^T (k = e, n = d): rows of dC, non-transposed
-        const int r = np * 16 + (lane & 7) + (lane >> 4) * 8;
-        const int c = kt * 16 + ((lane >> 3) & 1) * 8;
-        ldsm_x4(sD + swz(r, c, D), b0, b1, b2, b3);
+    for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-        for (int mi = 0; mi < 2; ++mi) {
-          mma16816(dp[mi][2 * np], av[mi], b0, b1);
-          mma16816(dp[mi][2 * np + 1], av[mi], b2, b3);
-        }
+      for (int j = 0; j < NTL; ++j)
+#pragma unroll
+        for (int x = 0; x < 4; ++x) dvw[mi][j][x] = 0.f;
+#pragma unroll
+    for (int kt = 0; kt < D / 16; ++kt) {
+      uint32_t ap[2][4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const int r = warp * 32 + mi * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kt * 16 + (lane >> 4) * 8;
+        ldsm_x4(sK + swz(r, c, D), ap[mi][0], ap[mi][1], ap[mi][2], ap[mi][3]);
       }
-      {  // B = dC (k = d, n = e): transposed loads
+#pragma unroll
+      for (int np = 0; np < D / 16; ++np) {
+        uint32_t b0, b1, b2, b3;  // B = dC (k = d, n = e): transposed loads
         const int r = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         const int c = np * 16 + (lane >> 4) * 8;
         ldsm_x4_t(sD + swz(r, c, D), b0, b1, b2, b3);
@@ -944,9 +966,51 @@ __global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
         }
       }
     }
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int t = warp * 32 + mi * 16 + g + hr * 8;
+#pragma unroll
+        for (int j = 0; j < NTL; ++j) {
+          const int d = j * 8 + c4 * 2;
+          __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(dvb + (long long)t * row + d);
+          const float2 old = __bfloat1622float2(*dst);
+          *dst = __floats2bfloat162_rn(rb(old.x + rb(dvw[mi][j][hr * 2])), rb(old.y + rb(dvw[mi][j][hr * 2 + 1])));
+        }
+      }
   }
-  bf16* dvb = a.dv + tok0 * row + (long long)h * D;
-  // dv += dv_w ; partition term of the probability gradient
+  // ---- pass 2: dprob = V . dC^T
+  float dp[2][NTL][4];
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int j = 0; j < NTL; ++j)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) dp[mi][j][x] = 0.f;
+#pragma unroll
+  for (int kt = 0; kt < D / 16; ++kt) {
+    uint32_t av[2][4];
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi) {
+      const int r = warp * 32 + mi * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int c = kt * 16 + (lane >> 4) * 8;
+      ldsm_x4(sV + swz(r, c, D), av[mi][0], av[mi][1], av[mi][2], av[mi][3]);
+    }
+#pragma unroll
+    for (int np = 0; np < D / 16; ++np) {
+      uint32_t b0, b1, b2, b3;  // B = dC^T (k = e, n = d): rows of dC, non-transposed
+      const int r = np * 16 + (lane & 7) + (lane >> 4) * 8;
+      const int c = kt * 16 + ((lane >> 3) & 1) * 8;
+      ldsm_x4(sD + swz(r, c, D), b0, b1, b2, b3);
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        mma16816(dp[mi][2 * np], av[mi], b0, b1);
+        mma16816(dp[mi][2 * np + 1], av[mi], b2, b3);
+      }
+    }
+  }
+  // partition term of the probability gradient: sum_t -bf16(dprob) * bf16(p / Z)
   float zpart[NTL][2];
 #pragma unroll
   for (int j = 0; j < NTL; ++j) zpart[j][0] = zpart[j][1] = 0.f;
@@ -958,14 +1022,11 @@ __global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {
         const int d = j * 8 + c4 * 2;
-        __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(dvb + (long long)t * row + d);
-        const float2 old = __bfloat1622float2(*dst);
-        *dst = __floats2bfloat162_rn(rb(old.x + rb(dvw[mi][j][hr * 2])), rb(old.y + rb(dvw[mi][j][hr * 2 + 1])));
+        const uint32_t p2 = *reinterpret_cast<const uint32_t*>(kB + swz(t, d, D));
+        const float pr[2] = {lo_f(p2), hi_f(p2)};
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float pr = pval(t, d + x);
-          zpart[j][x] += rb(-__fmul_rn(rb(dp[mi][j][hr * 2 + x]), rb(__fdiv_rn(pr, zp[d + x]))));
-        }
+        for (int x = 0; x < 2; ++x)
+          zpart[j][x] += rb(-__fmul_rn(rb(dp[mi][j][hr * 2 + x]), rb(__fdiv_rn(pr[x], zp[d + x]))));
       }
     }
 #pragma unroll
@@ -997,12 +1058,22 @@ __global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {
         const int d = j * 8 + c4 * 2;
+        float ev[2];
+        if (kStoreE) {
+          const uint32_t e2 = *reinterpret_cast<const uint32_t*>(eB + swz(t, d, D));
+          ev[0] = lo_f(e2);
+          ev[1] = hi_f(e2);
+        } else {
+#pragma unroll
+          for (int x = 0; x < 2; ++x)
+            ev[x] = rb(expf(rb(__fsub_rn(bf(*reinterpret_cast<const bf16*>(kb + (long long)t * row + d + x)),
+                                         mx[d + x]))));
+        }
         float o2[2];
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          const float e = rb(expf(rb(__fsub_rn(kat(t, d + x), mx[d + x]))));
           const float de = rb(__fadd_rn(rb(__fdiv_rn(rb(dp[mi][j][hr * 2 + x]), zp[d + x])), dZ[d + x]));
-          const float dx = rb(__fmul_rn(de, e));
+          const float dx = rb(__fmul_rn(de, ev[x]));
           o2[x] = dx;
           mpart[j][x] += dx;
         }
@@ -1024,8 +1095,9 @@ __global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
   {
     constexpr int G = 256 / D, TPG = NT / G;
     const int d = tid % D, grp = tid / D;
+    const uint32_t bit = 1u << (d & 31);
     int cnt = 0;
-    for (int t = grp * TPG; t < (grp + 1) * TPG; ++t) cnt += kat(t, d) == mx[d];
+    for (int t = grp * TPG; t < (grp + 1) * TPG; ++t) cnt += (tieS[t * TW + d / 32] & bit) != 0;
     stat_scratch[grp * D + d] = (float)cnt;
     __syncthreads();
     int count = 0;
@@ -1034,7 +1106,7 @@ __global__ void __launch_bounds__(256) writer_bwd_kernel(BwdArgs a) {
     const float dm = rb(dzS[d] - rb(dmS[d]));
     const float share = rb(dm / count);
     for (int t = grp * TPG; t < (grp + 1) * TPG; ++t)
-      if (kat(t, d) == mx[d]) {
+      if (tieS[t * TW + d / 32] & bit) {
         bf16* p = dkb + (long long)t * row + d;
         *p = tobf(bf(*p) + share);
       }

@@ -495,7 +495,9 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
           const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), qv)), bf(fb[0]))), 0.f));
           const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), qv)), bf(fb[2])));
           const float mx = fmaxf(s0, s2);
-          const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
+          // the larger term is exp(0) = 1 exactly: one exponential per element
+          const float eo = expf(fminf(s0, s2) - mx);
+          const float e0 = s0 >= s2 ? 1.f : eo, e2 = s0 >= s2 ? eo : 1.f;
           const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
           const float lt = rb(__fmul_rn(rho0, rb(__fmul_rn(2.f, loc))));
           const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(gain, fine))));

@@ -26,6 +26,7 @@ from .config import TaoConfig, routed_counts
 
 WINDOW, FINE, KEEP, GROUP = 768, 256, 512, 8
 ROUTE_CAP = 256
+MIN_CAP = 64          # initial fine-bank capacity (fines); doubles when full
 _BF16 = torch.bfloat16
 
 
@@ -93,6 +94,7 @@ class StreamCache:
         self.history_path_ablation = False
         self.history_value_ablation = False
         self._buf = None          # dict of device tensors
+        self._graph = None        # _DecodeGraph (config.q1_history_region_graph)
         self._desc = None         # device TaoState (uint8 tensor)
         self._host = None         # ctypes TaoState mirror
         self._ptrs = None         # device array holding the descriptor address
@@ -117,6 +119,7 @@ class StreamCache:
     def release_execution(self, reason="request_end"):
         """Drop execution-only resources (graphs, cached pointer arrays)."""
         self._ptrs = None
+        self._graph = None
 
     def reset(self):
         """Discard this request's state without touching another request."""
@@ -200,7 +203,7 @@ class StreamCache:
             device = torch.device("cuda", torch.cuda.current_device())
         if self._buf is None:
             end = self.position + tokens
-            self._allocate(heads, width, device, max(64, sealed_at(end) + 1))
+            self._allocate(heads, width, device, max(MIN_CAP, sealed_at(end) + 1))
         elif (heads, width) != (self.heads, self.width) or device != self.device:
             raise ValueError("a state serves one head count, width and device")
         need = sealed_at(self.position + tokens) + 1
@@ -210,7 +213,10 @@ class StreamCache:
     # -- one chunk through the kernels ------------------------------------
     def _run(self, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
         """Advance by q.shape[1] tokens (must not cross a seal); fused output -> out."""
-        run_batch([self], q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out)
+        if self.config.q1_history_region_graph and q.shape[1] == 1 and q.device.type == "cuda":
+            _DecodeGraph.step(self, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out)
+        else:
+            run_batch([self], q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out)
 
     # -- snapshots (reference dictionary format, tao_stream.py:853-912) --
     def export(self):
@@ -366,7 +372,11 @@ class _BatchArgs:
 
     @classmethod
     def get(cls, states, w, heads, width, dev):
-        key = (tuple(st._desc.data_ptr() for st in states), tuple(st.cap_fines for st in states), w, heads, width)
+        # everything the cached arrays hold is part of the key: a freed state's
+        # descriptor address can be reused by a new state with another layer index
+        c = states[0].config
+        key = (tuple((st._desc.data_ptr(), st.cap_fines, st.layer_index) for st in states), w, heads, width,
+               c.route_period, c.layer_stagger, c.budget_root_scale, c.budget_offset)
         args = cls.cache.get(key)
         if args is None:
             if len(cls.cache) > 256:
@@ -412,29 +422,108 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
                                        fb.data_ptr(), float(alpha), out.data_ptr(), ws.data_ptr(),
                                        ws.numel(), stream))
     for st in states:
-        hist = st.position >= WINDOW
-        c = st._counters
-        if hist:
-            c["fusion_pointwise_calls"] += 1
-            c["fused_fine_calls"] += 1
-        else:
-            c["fusion_no_history_local_returns"] += 1
-        st.position += w
-        local = st.position - window_start(st.position - 1)
-        if local > c["peak_local_tokens"]:
-            c["peak_local_tokens"] = local
+        _bookkeep(st, w)
+
+
+def _bookkeep(st, w):
+    """Host-side cursor and counters after a chunk of ``w`` tokens."""
+    c = st._counters
+    if st.position >= WINDOW:
+        c["fusion_pointwise_calls"] += 1
+        c["fused_fine_calls"] += 1
+    else:
+        c["fusion_no_history_local_returns"] += 1
+    st.position += w
+    local = st.position - window_start(st.position - 1)
+    if local > c["peak_local_tokens"]:
+        c["peak_local_tokens"] = local
+
+
+class _DecodeGraph:
+    """The whole decode step of one state as a CUDA graph over fixed buffers.
+
+    Used when ``config.q1_history_region_graph`` is set (reference
+    ``HistoryRegionGraph``, history_region_graph.py:10-113, which captures the
+    history read only and re-captures after every seal).  Here the graph holds the
+    route, fused decode and seal kernels of ``tao_decode_step`` in graph mode: the
+    route and seal kernels read the cursor from the device state and return early
+    on tokens that neither refresh nor seal, so a seal needs no re-capture.  The
+    graph is captured again only when the fine bank grows (new grid sizes and
+    buffers), or when alpha or the operand shape changes.
+    """
+
+    def __init__(self, st, heads, width, alpha):
+        dev = st.device
+        lib = _lib.lib()
+        self.key = (st.cap_fines, st._desc.data_ptr(), heads, width, float(alpha))
+        self.inp = torch.zeros(5, 1, 1, heads, width, dtype=_BF16, device=dev)   # q, k, v, raw_q, raw_k
+        self.fab = torch.zeros(2, heads, width, 3, dtype=_BF16, device=dev)      # fusion_a, fusion_b
+        self.out = torch.zeros(1, 1, heads, width, dtype=_BF16, device=dev)
+        self.ptrs = torch.tensor([st._desc.data_ptr()], dtype=torch.int64, device=dev)
+        self.policy = policy_for(st.config)
+        self.pos = (ctypes.c_int64 * 1)(st.position)
+        self.cap = (ctypes.c_int32 * 1)(st.cap_fines)
+        self.layer = (ctypes.c_int32 * 1)(st.layer_index)
+        nbytes = lib.tao_stream_workspace_bytes(1, 1, heads, width, ROUTE_CAP, ctypes.byref(self.policy))
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _GRAPH_WORKSPACES.setdefault(dev, []).append(self.ws)
+        self.graph = torch.cuda.CUDAGraph()
+        rc = 0
+        lib.tao_decode_graph_mode(1)
+        try:
+            # "relaxed": the launcher may set kernel shared-memory attributes during capture
+            with torch.cuda.graph(self.graph, capture_error_mode="relaxed"):
+                rc = lib.tao_decode_step(self.ptrs.data_ptr(), 1, self.pos, self.layer, self.cap,
+                                         ctypes.byref(self.policy), heads, width,
+                                         *(self.inp[i].data_ptr() for i in range(5)),
+                                         self.fab[0].data_ptr(), self.fab[1].data_ptr(), float(alpha),
+                                         self.out.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                                         torch.cuda.current_stream(dev).cuda_stream)
+        finally:
+            lib.tao_decode_graph_mode(0)
+        _lib.check(rc)
+
+    @staticmethod
+    def step(st, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
+        r, w, heads, width = q.shape
+        if r != 1 or w != 1:
+            raise ValueError("graph decode takes [1, 1, heads, width] operands")
+        dev = q.device
+        ops = [_as_bf16(t, n, dev) for t, n in ((q, "q"), (k, "k"), (v, "v"), (raw_q, "raw_q"), (raw_k, "raw_k"))]
+        for t in ops[1:]:
+            if t.shape != q.shape:
+                raise ValueError("q, k, v, raw_q and raw_k must have the same shape")
+        if fusion_a.shape != (heads, width, 3) or fusion_b.shape != (heads, width, 3):
+            raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
+        st._ensure(heads, width, dev, 1)   # may grow the fine bank (new buffers)
+        g = st._graph
+        key = (st.cap_fines, st._desc.data_ptr(), heads, width, float(alpha))
+        if g is None or g.key != key:
+            g = st._graph = _DecodeGraph(st, heads, width, alpha)
+        for i, t in enumerate(ops):
+            g.inp[i].copy_(t)
+        g.fab[0].copy_(fusion_a)
+        g.fab[1].copy_(fusion_b)
+        g.graph.replay()
+        out.copy_(g.out)
+        _bookkeep(st, 1)
+
+
+_GRAPH_WORKSPACES = {}
 
 
 def check_device(device=None):
     """Raise if a kernel on ``device`` reported an error since the last check."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    ws = _Workspace.cache.get(dev)
-    if ws is None:
-        return 0
+    stream = torch.cuda.current_stream(dev).cuda_stream
     flags = ctypes.c_int(0)
-    _lib.check(_lib.lib().tao_stream_check(ws.data_ptr(), ctypes.byref(flags),
-                                           torch.cuda.current_stream(dev).cuda_stream))
-    return flags.value
+    total = 0
+    for ws in [_Workspace.cache.get(dev)] + _GRAPH_WORKSPACES.get(dev, []):
+        if ws is None:
+            continue
+        _lib.check(_lib.lib().tao_stream_check(ws.data_ptr(), ctypes.byref(flags), stream))
+        total |= flags.value
+    return total
 
 
 def route_count_at(pos, layer, config):

@@ -77,3 +77,29 @@ def test_config_validation_matches_reference():
     with pytest.raises(ValueError):
         TaoConfig(local_keep=300)
     assert TaoConfig(**index_only_page_memo().export()) == index_only_page_memo()
+
+
+def test_batch_argument_cache_keys_on_layer_and_policy():
+    """A descriptor address reused by a new state with another layer index must
+    not return cached per-state arrays of the old state."""
+    import torch
+    from tao_memory_b200.stream import _BatchArgs
+    from tao_memory_b200.config import TaoConfig
+
+    class _Desc:
+        def __init__(self, p):
+            self.p = p
+
+        def data_ptr(self):
+            return self.p
+
+    class _State:
+        def __init__(self, layer, cfg=TaoConfig()):
+            self._desc, self.cap_fines, self.layer_index, self.config = _Desc(4096), 64, layer, cfg
+
+    dev = torch.device("cpu")
+    a = _BatchArgs.get([_State(0)], 1, 2, 64, dev)
+    b = _BatchArgs.get([_State(3)], 1, 2, 64, dev)
+    assert a is not b and list(a.layers) == [0] and list(b.layers) == [3]
+    c = _BatchArgs.get([_State(3, TaoConfig(route_period=12))], 1, 2, 64, dev)
+    assert c is not b and c.policy.route_period == 12

@@ -176,3 +176,46 @@ def test_stream_errors():
     with pytest.raises(ValueError):
         tb.tao_attention_prefill(*(xs[k].float() for k in KEYS[:3]), raw_q=xs["raw_q"].float(),
                                  raw_k=xs["raw_k"].float(), state=st, position=0, **kw)
+
+
+def test_graph_decode_equals_eager(monkeypatch):
+    """config.q1_history_region_graph: decode replays one captured CUDA graph per
+    fine-bank capacity.  Outputs and exported states equal eager decode bit for bit
+    across route refreshes, seals and a fine-bank growth (initial capacity lowered to
+    8 fines so the growth happens within the test)."""
+    tb, preset, check_device = _tb()
+    from tao_memory_b200 import stream
+    monkeypatch.setattr(stream, "MIN_CAP", 8)
+    dev = torch.device("cuda")
+    H, D, P, N = 2, 64, 1000, 1700
+    x = {k: t.to(dev) for k, t in make_inputs(1, P + N, H, D, seed=77)[0].items()}
+    kw = dict(fusion_a=x["fusion_a"], fusion_b=x["fusion_b"], alpha=0.45)
+    outs = {}
+    states = {}
+    for graph in (False, True):
+        st = tb.new_state(3, preset(graph=graph))
+        got = [tb.tao_attention_prefill(*(x[k][:, :P] for k in KEYS[:3]), raw_q=x["raw_q"][:, :P],
+                                        raw_k=x["raw_k"][:, :P], state=st, position=0, **kw)[0]]
+        for t in range(P, P + N):
+            sl = slice(t, t + 1)
+            got.append(tb.tao_attention_decode(*(x[k][:, sl] for k in KEYS[:3]), raw_q=x["raw_q"][:, sl],
+                                               raw_k=x["raw_k"][:, sl], state=st, position=t, **kw)[0])
+        outs[graph] = torch.cat(got, 1)
+        states[graph] = st
+    torch.cuda.synchronize()
+    assert check_device() == 0
+    assert states[True].cap_fines > 8 and states[True]._graph is not None
+    assert torch.equal(outs[False], outs[True])
+    def same(a, b):
+        if isinstance(a, torch.Tensor):
+            return torch.equal(a, b)
+        if isinstance(a, (list, tuple)):
+            return len(a) == len(b) and all(same(u, w) for u, w in zip(a, b))
+        if isinstance(a, dict):
+            return a.keys() == b.keys() and all(same(a[k], b[k]) for k in a)
+        return a == b
+    ea, eb = states[False].export(), states[True].export()
+    ca, cb = dict(ea.pop("config")), dict(eb.pop("config"))
+    assert cb.pop("q1_history_region_graph") and not ca.pop("q1_history_region_graph") and ca == cb
+    for key in ea:
+        assert same(ea[key], eb[key]), key
