@@ -456,7 +456,7 @@ struct ReadBwdSmem {
   static size_t bytes(int P, int V, int mmax) {
     return 4 * (size_t)NQ * D * 2 + (size_t)D * D * 2 + 4 * (size_t)P * D * 4 + (size_t)P * D * 2 +
            ((size_t)V * D * 2 + 15) / 16 * 16 + (size_t)NQ * mmax * 2 + NQ * 4 + NQ +
-           (size_t)D * 4 + (size_t)(V + 8) * 4 * 2 + 64;
+           (size_t)(NQ / 32) * D * 4 + (size_t)(V + 8) * 4 * 2 + 64;
   }
 };
 
@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
   int16_t* selS = reinterpret_cast<int16_t*>(ptr); ptr += (size_t)NQ * M * 2;
   float* gdS = reinterpret_cast<float*>(ptr);   ptr += NQ * 4;
   uint8_t* selq = ptr;                          ptr += NQ;
-  float* dwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)D * 4;
+  float* dwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)(NQ / 32) * D * 4;  // per-warp dw partials
   int* useS = reinterpret_cast<int*>(ptr);
   int* list = useS + V;
 
@@ -511,7 +511,6 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
     dpzS[idx] = 0.f;
   }
   for (int i = tid; i < V; i += NQ) useS[i] = 0;
-  for (int d = tid; d < D; d += NQ) dwS[d] = 0.f;
   __syncthreads();
   for (int d = tid; d < D; d += NQ) {
     float mx = -INFINITY;
@@ -728,7 +727,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
         v += __shfl_xor_sync(0xffffffffu, v, 4);
         v += __shfl_xor_sync(0xffffffffu, v, 8);
         v += __shfl_xor_sync(0xffffffffu, v, 16);
-        if (g == 0 && v != 0.f) atomicAdd(&dwS[j * 8 + c4 * 2 + x], v);
+        if (g == 0) dwS[warp * D + j * 8 + c4 * 2 + x] = v;  // summed over warps after the barrier
       }
     // dC_s = A_s^T . gn : output [d][e]; warps tile (m-tiles of d rows) x (n ranges)
     {
@@ -777,10 +776,12 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
     __syncthreads();
     // dw_s -> d(z - pz) = bf16(bf16(dw) * w) : dz[s] += ., d page_z[pg] -= .
     for (int d = tid; d < D; d += NQ) {
-      const float ddiff = rb(__fmul_rn(rb(dwS[d]), bf(swS[sf * D + d])));
+      float dw = 0.f;
+#pragma unroll
+      for (int w = 0; w < NQ / 32; ++w) dw += dwS[w * D + d];
+      const float ddiff = rb(__fmul_rn(rb(dw), bf(swS[sf * D + d])));
       atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d, ddiff);
       dpzS[pg * D + d] -= ddiff;
-      dwS[d] = 0.f;
     }
     __syncthreads();
   }
