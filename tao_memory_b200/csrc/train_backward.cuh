@@ -33,7 +33,7 @@ struct BwdArgs {
 // Fusion backward: one warp per (token, head) row, lanes over channels; each warp
 // takes kFusionRowsPerWarp consecutive tokens, a CTA 8 warps.
 // ---------------------------------------------------------------------------
-constexpr int kFusionRowsPerWarp = 4;
+constexpr int kFusionRowsPerWarp = 16;
 template <int D>
 __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
   constexpr int PER = D / 32;
@@ -913,7 +913,7 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
   cp_wait<0>();
   __syncthreads();
   auto at = [&](uint8_t* base, int t, int d) -> bf16& { return *reinterpret_cast<bf16*>(base + swz(t, d, D)); };
-  __shared__ float stat_scratch[2 * 256];
+  __shared__ float stat_scratch[(8 * D > 512) ? 8 * D : 512];  // also per-warp [8][D] partials
   channel_stats<D, 256>([&](int t, int d) { return bf(at(kB, t, d)); }, mx, zp, stat_scratch);
   // ties of the max (thread t: its token row)
   {
@@ -1038,12 +1038,16 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
       v += __shfl_xor_sync(0xffffffffu, v, 4);
       v += __shfl_xor_sync(0xffffffffu, v, 8);
       v += __shfl_xor_sync(0xffffffffu, v, 16);
-      if (g == 0) atomicAdd(&dZp[j * 8 + c4 * 2 + x], v);
+      if (g == 0) stat_scratch[warp * D + j * 8 + c4 * 2 + x] = v;  // per-warp partial
     }
   __syncthreads();
   for (int d = tid; d < D; d += 256) {
+    float zsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) zsum += stat_scratch[w * D + d];
+    dZp[d] = zsum;
     const float dlog = rb(__fdiv_rn(dzS[d], zp[d]));   // z = max + log(partition)
-    dZ[d] = rb(rb(dZp[d]) + dlog);
+    dZ[d] = rb(rb(zsum) + dlog);
   }
   __syncthreads();
   // d_e = bf16(bf16(dprob / Z) + dZ) ; d_x = bf16(d_e * e) -> d raw_k ; sum_t d_x
@@ -1089,8 +1093,15 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
       v += __shfl_xor_sync(0xffffffffu, v, 4);
       v += __shfl_xor_sync(0xffffffffu, v, 8);
       v += __shfl_xor_sync(0xffffffffu, v, 16);
-      if (g == 0) atomicAdd(&dmS[j * 8 + c4 * 2 + x], v);
+      if (g == 0) stat_scratch[warp * D + j * 8 + c4 * 2 + x] = v;  // per-warp partial
     }
+  __syncthreads();
+  for (int d = tid; d < D; d += 256) {
+    float msum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) msum += stat_scratch[w * D + d];
+    dmS[d] = msum;
+  }
   __syncthreads();
   // max: dm = dz - sum_t d_x, shared evenly by the tokens that attain the max
   {
