@@ -194,6 +194,16 @@ int tao_window_attention(const void* q, const void* k, const void* v, void* out,
                          float* lse, int batch, int tokens, int heads, int width,
                          void* stream);
 
+/* Sufficient statistics of the association fine writers for `blocks` x `heads`
+ * 256-token blocks: u = bf16(softmax over channels of k[t]) (fp32 softmax), then
+ * gram = u^T u and cross = u^T v, fp32 [blocks][heads][width][width].  Token t of
+ * (block b, head h) starts at k + b*block_stride + h*head_stride + t*token_stride
+ * (elements; rows 16-byte aligned), likewise for v.  Reference:
+ * association_statistics (association_writer.py:11-18) at a seal (tao_stream.py:72-74). */
+int tao_writer_stats(const void* k, const void* v, long long token_stride, long long head_stride,
+                     long long block_stride, int blocks, int heads, int width, float* gram,
+                     float* cross, void* stream);
+
 /* Select the windowed-attention kernel for this process (tao_window_attention and
  * the training forward): 1 = tcgen05/TMEM kernel with TMA tile loads for width 64
  * (default; width 128 uses the mma.sync kernel), 0 = mma.sync kernel for every

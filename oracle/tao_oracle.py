@@ -13,7 +13,8 @@ container where it was importable (script: ``tests/golden/make_golden.py``);
 
 Scope: the preset path ``index_only_page_memo`` (``coarse_index_only=True``,
 ``fine_writer="softmax"``), streaming prefill/decode for one request and
-training forward/backward for batch B.
+training forward/backward for batch B; for streaming also
+``fine_writer="regularized_association"`` on the same preset.
 
 Rounding conventions (probed against torch CPU 2.11):
 * ``F.softmax``, ``Tensor.sum`` and ``Tensor.exp`` on bf16 compute in fp32 and
@@ -97,6 +98,25 @@ def seal_block(raw_k, v):
     with torch.autocast(device_type="cpu", enabled=False):
         c = torch.einsum("bthd,bthe->bhde", prob, v).to(dt)
     return z, c
+
+
+def association_statistics(raw_k, v):
+    """Association-writer statistics of one block [B,256,H,D] (association_writer.py:11-18):
+    u = bf16(fp32 softmax over channels), G = u^T u and X = u^T v in fp32, [B,H,D,D]."""
+    with torch.autocast(device_type="cpu", enabled=False):
+        u = raw_k.float().softmax(dim=-1).to(BF16).transpose(1, 2).float()
+        values = v.transpose(1, 2).float()
+        return u.transpose(-1, -2) @ u, u.transpose(-1, -2) @ values
+
+
+def association_matrix(gram, cross):
+    """Regularised solve (association_writer.py:21-32): C = bf16(A^{-1} X) with
+    A = G + (trace(G)/D) I through a Cholesky factor."""
+    with torch.autocast(device_type="cpu", enabled=False):
+        width = gram.shape[-1]
+        reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / width
+        system = gram + reg[..., None, None] * torch.eye(width, dtype=F32)
+        return torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(BF16)
 
 
 def seal_all(raw_k, v, fine=256):
@@ -183,8 +203,10 @@ class OracleStream:
 
     FINE, KEEP, GROUP, PERIOD, STAGGER = 256, 512, 8, 24, 2
 
-    def __init__(self, layer_index=0):
+    def __init__(self, layer_index=0, fine_writer="softmax"):
         self.layer_index = layer_index
+        self.fine_writer = fine_writer
+        self.pending_gram = self.pending_cross = None   # fp32 writer statistics (association writers)
         self.position = 0
         self.local = None              # (k, v, raw_k) [1,L,H,D]
         self.pages = []                # (page_z [1,H,D], fine_z [1,H,8,D])
@@ -279,6 +301,13 @@ class OracleStream:
     def seal(self, raw_k, v):
         """LayerState.seal/append_fine (tao_stream.py:435-512), index-only pages."""
         z, c = seal_block(raw_k, v)
+        if self.fine_writer == "regularized_association":
+            # tao_stream.py:72-74 and 463-475: same z, C from the regularised solve;
+            # with index-only pages the statistics keep accumulating (never reset)
+            gram, cross = association_statistics(raw_k, v)
+            c = association_matrix(gram, cross)
+            self.pending_gram = gram if self.pending_gram is None else self.pending_gram + gram
+            self.pending_cross = cross if self.pending_cross is None else self.pending_cross + cross
         self.state_version += 1
         c = c.unsqueeze(2)
         self.fine_c = c if self.fine_c is None else torch.cat((self.fine_c, c), dim=2)
@@ -333,6 +362,8 @@ class OracleStream:
             "packed_fine_c": None if self.fine_c is None else clone(self.fine_c),
             "pages": [(clone(pz), None, clone(fz)) for pz, fz in self.pages],
             "pending_z": [clone(z) for z in self.pending],
+            "pending_gram": None if self.pending_gram is None else clone(self.pending_gram),
+            "pending_cross": None if self.pending_cross is None else clone(self.pending_cross),
             "route_ids": None if self.route_ids is None else tuple(map(clone, self.route_ids)),
             "state_version": self.state_version,
             "route_refreshes": self.route_refreshes,
@@ -341,13 +372,15 @@ class OracleStream:
 
     @classmethod
     def from_export(cls, saved):
-        st = cls(saved["layer_index"])
+        st = cls(saved["layer_index"], saved.get("config", {}).get("fine_writer", "softmax"))
         st.position = saved["position"]
         cpu = lambda t: t.detach().to("cpu").clone()
         st.local = None if saved["local"] is None else tuple(map(cpu, saved["local"]))
         st.fine_c = None if saved["packed_fine_c"] is None else cpu(saved["packed_fine_c"])
         st.pages = [(cpu(pz), cpu(fz)) for pz, _, fz in saved["pages"]]
         st.pending = [cpu(z) for z in saved["pending_z"]]
+        st.pending_gram = None if saved.get("pending_gram") is None else cpu(saved["pending_gram"])
+        st.pending_cross = None if saved.get("pending_cross") is None else cpu(saved["pending_cross"])
         st.route_ids = None if saved["route_ids"] is None else tuple(map(cpu, saved["route_ids"]))
         st.state_version = saved["state_version"]
         st.route_refreshes = saved.get("route_refreshes", 0)

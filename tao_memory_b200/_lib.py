@@ -53,6 +53,7 @@ _SIGNATURES = {
     "tao_decode_variant": (_I, [_I]),
     "tao_attention_variant": (_I, [_I]),
     "tao_decode_graph_mode": (_I, [_I]),
+    "tao_writer_stats": (_I, [_VP, _VP, _I64, _I64, _I64, _I, _I, _I, _VP, _VP, _VP]),
     "tao_decode_step": (_I, [_VP, _I, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_int32),
                              ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(TaoPolicy), _I, _I,
                              _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F, _VP, _VP, _SZ, _VP]),

@@ -27,6 +27,7 @@ from .config import TaoConfig, routed_counts
 WINDOW, FINE, KEEP, GROUP = 768, 256, 512, 8
 ROUTE_CAP = 256
 MIN_CAP = 64          # initial fine-bank capacity (fines); doubles when full
+WRITERS_B200 = ("softmax", "regularized_association")
 _BF16 = torch.bfloat16
 
 
@@ -49,8 +50,9 @@ def check_config(config):
     """The sm_100a kernels implement the index-only softmax-writer preset."""
     if (config.fine_tokens, config.local_keep, config.coarse_group) != (FINE, KEEP, GROUP):
         raise ValueError("kernels are specialised for fine_tokens=256, local_keep=512, coarse_group=8")
-    if config.fine_writer != "softmax":
-        raise NotImplementedError("only fine_writer='softmax' is implemented on B200")
+    if config.fine_writer not in WRITERS_B200:
+        raise NotImplementedError("fine_writer=%r is not implemented on B200 (implemented: %s)"
+                                  % (config.fine_writer, ", ".join(WRITERS_B200)))
     if not config.coarse_index_only:
         raise NotImplementedError("only coarse_index_only=True (index_only_page_memo) is implemented on B200")
 
@@ -95,6 +97,7 @@ class StreamCache:
         self.history_value_ablation = False
         self._buf = None          # dict of device tensors
         self._graph = None        # _DecodeGraph (config.q1_history_region_graph)
+        self._gram = self._cross = None  # fp32 [1,H,D,D] writer statistics (association writers)
         self._desc = None         # device TaoState (uint8 tensor)
         self._host = None         # ctypes TaoState mirror
         self._ptrs = None         # device array holding the descriptor address
@@ -213,10 +216,35 @@ class StreamCache:
     # -- one chunk through the kernels ------------------------------------
     def _run(self, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
         """Advance by q.shape[1] tokens (must not cross a seal); fused output -> out."""
-        if self.config.q1_history_region_graph and q.shape[1] == 1 and q.device.type == "cuda":
+        if (self.config.q1_history_region_graph and self.config.fine_writer == "softmax"
+                and q.shape[1] == 1 and q.device.type == "cuda"):
             _DecodeGraph.step(self, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out)
         else:
             run_batch([self], q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out)
+
+    # -- association fine writer (tao_stream.py:72-74, 463-475) -----------
+    def _seal_writer(self, s):
+        """Replace fine ``s`` (just sealed by the softmax writer kernels, whose z
+        routing keeps) by the regularised association matrix of the same block:
+        statistics on the tensor cores (``tao_writer_stats``), the Cholesky solve in
+        torch.linalg.  The block's 256 tokens are still in the ring (nothing has
+        been appended since the seal).  As in the reference with index-only pages,
+        the fp32 statistics accumulate without reset (they only feed snapshots)."""
+        heads, width = self.heads, self.width
+        slot0 = (s * FINE) % WINDOW
+        gram = torch.empty(1, heads, width, width, dtype=torch.float32, device=self.device)
+        cross = torch.empty_like(gram)
+        k = self._buf["rk_ring"][:, slot0:slot0 + FINE]
+        v = self._buf["v_ring"][:, slot0:slot0 + FINE]
+        _lib.check(_lib.lib().tao_writer_stats(k.data_ptr(), v.data_ptr(), width, WINDOW * width, 0, 1, heads,
+                                               width, gram.data_ptr(), cross.data_ptr(),
+                                               torch.cuda.current_stream(self.device).cuda_stream))
+        reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / width
+        system = gram + reg[..., None, None] * torch.eye(width, dtype=torch.float32, device=self.device)
+        c = torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(_BF16)
+        self._buf["fine_c"][:, s].copy_(c[0])
+        self._gram = gram if self._gram is None else self._gram + gram
+        self._cross = cross if self._cross is None else self._cross + cross
 
     # -- snapshots (reference dictionary format, tao_stream.py:853-912) --
     def export(self):
@@ -254,8 +282,10 @@ class StreamCache:
             "route_interval": self.route_interval, "fusion_mode": self.fusion_mode,
             "fused_fine": self.fused_fine, "position": self.position, "local": local,
             "packed_fine_c": fine_c, "pages": pages, "pending_z": pending,
-            "pending_square_mass": None, "pending_mass": None, "pending_gram": None,
-            "pending_cross": None, "route_ids": route, "route_key": None,
+            "pending_square_mass": None, "pending_mass": None,
+            "pending_gram": None if self._gram is None else self._gram.clone(),
+            "pending_cross": None if self._cross is None else self._cross.clone(),
+            "route_ids": route, "route_key": None,
             "state_version": s, "route_refreshes": layer["route_refreshes"],
             "fine_seal_events": s,
         }
@@ -278,6 +308,9 @@ class StreamCache:
         s = sealed_at(pos)
         state._allocate(heads, width, dev, max(64, s + 1))
         b = state._buf
+        for name, attr in (("pending_gram", "_gram"), ("pending_cross", "_cross")):
+            if saved.get(name) is not None:
+                setattr(state, attr, saved[name].to(dev, torch.float32).clone())
         if local is not None:
             n = local[0].shape[1]
             if n != pos - window_start(pos):
@@ -332,8 +365,11 @@ class StreamCache:
         physical = 0 if self._buf is None else sum(t.numel() * t.element_size() for t in self._buf.values())
         n_route = 0 if self._buf is None else self._download().n_route
         route_bytes = n_route * heads * 8
+        stat = lambda t: 0 if t is None else t.numel() * t.element_size()
+        writer = stat(self._gram) + stat(self._cross)
         return {"history_bytes": history, "page_normalization_memo_bytes": 0,
-                "pending_writer_bytes": 0, "fused_fine": self.fused_fine,
+                "pending_writer_bytes": writer, "pending_gram_cross_bytes": writer,
+                "pending_cross_bytes": stat(self._cross), "fused_fine": self.fused_fine,
                 "fusion_mode": self.fusion_mode, "fine_seal_events": s,
                 "route_integer_bytes": route_bytes,
                 "logical_local_bf16_kv_bytes": logical_local,
@@ -422,6 +458,10 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
                                        fb.data_ptr(), float(alpha), out.data_ptr(), ws.data_ptr(),
                                        ws.numel(), stream))
     for st in states:
+        if st.config.fine_writer != "softmax":
+            end = st.position + w
+            if end - window_start(end - 1) == WINDOW:   # this chunk sealed a block
+                st._seal_writer(sealed_at(end - 1))
         _bookkeep(st, w)
 
 

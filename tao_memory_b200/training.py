@@ -81,6 +81,9 @@ class _TaoAttention(torch.autograd.Function):
 
 def tao_attention_train(q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, config):
     check_config(config)
+    if config.fine_writer != "softmax":
+        raise NotImplementedError("tao_attention (training) implements fine_writer='softmax' on B200; "
+                                  "%r is implemented for streaming only" % config.fine_writer)
     ops = (q, k, v, raw_q, raw_k)
     if any(t.dtype != _BF16 for t in ops):
         raise ValueError("tao_attention on B200 takes bf16 operands (the reference's selected read "

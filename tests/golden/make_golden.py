@@ -134,6 +134,12 @@ STREAM_CASES = {
     "stream_pages": (1, 64, 3, (9000,), 40, 3),
 }
 
+# streaming cases with another fine writer on the index-only preset:
+# name: (case tuple as above, fine_writer)
+WRITER_CASES = {
+    "stream_regularized": ((2, 64, 1, (1000, 1900), 40, 8), "regularized_association"),
+}
+
 TRAIN_CASES = {
     # name: (batch, tokens, heads, width, alpha, seed)
     "train_t2048_h2": (1, 2048, 2, 64, 0.5, 4),
@@ -146,11 +152,18 @@ TRAIN_CASES = {
 def run_stream(name, mode):
     from tao_attention import new_state, tao_attention_prefill, tao_attention_decode, StreamCache
     from tao_attention.presets import index_only_page_memo
-    heads, width, layer, splits, steps, seed = STREAM_CASES[name]
+    from tao_attention.config import TaoConfig
+    if name in WRITER_CASES:
+        case, writer = WRITER_CASES[name]
+        base = index_only_page_memo()
+        config = TaoConfig(**{**base.export(), "fine_writer": writer})
+    else:
+        case, config = STREAM_CASES[name], index_only_page_memo()
+    heads, width, layer, splits, steps, seed = case
     total = sum(splits) + steps
     x, _ = make_inputs(1, total, heads, width, seed)
     alpha = 0.5
-    state = new_state(layer, index_only_page_memo())
+    state = new_state(layer, config)
     outs, route_ids, positions = [], [], []
     pos = 0
     kw = dict(fusion_a=x["fusion_a"], fusion_b=x["fusion_b"], alpha=alpha)
@@ -179,7 +192,7 @@ def run_stream(name, mode):
                 snapshot = state.export()
         final = state.export()
     return {
-        "kind": "stream", "mode": mode, "case": STREAM_CASES[name], "alpha": alpha,
+        "kind": "stream", "mode": mode, "case": case, "alpha": alpha, "config": config.export(),
         "input_digest": digest(*(x[k] for k in ("q", "k", "v", "raw_q", "raw_k", "fusion_a", "fusion_b"))),
         "output": torch.cat(outs, dim=1),
         "prefill_route_ids": None if prefill_ids is None else prefill_ids[1].clone(),
@@ -224,7 +237,7 @@ def compact(name, result):
         for k in ("q", "k", "v", "raw_q", "raw_k"):
             result["grads"][k] = result["grads"][k][:, ::stride].clone()
     else:
-        steps = STREAM_CASES[name][4]
+        steps = (WRITER_CASES[name][0] if name in WRITER_CASES else STREAM_CASES[name])[4]
         out = result["output"]
         result["decode_output"] = out[:, -steps:].clone()
         result["output"] = out[:, ::stride].clone()
@@ -248,7 +261,7 @@ def main():
         check_fast()
         install_fast(args.reference)
     mode = "reference+fast-inference-kernels" if args.fast else "reference (interpreted Triton, patched)"
-    cases = args.cases or [*STREAM_CASES, *TRAIN_CASES]
+    cases = args.cases or [*STREAM_CASES, *WRITER_CASES, *TRAIN_CASES]
     if args.compact_only:
         for name in cases:
             path = os.path.join(HERE, name + ".pt")
@@ -258,7 +271,7 @@ def main():
         return
     for name in cases:
         t0 = time.time()
-        result = run_stream(name, mode) if name in STREAM_CASES else run_train(name, mode)
+        result = run_stream(name, mode) if name in STREAM_CASES or name in WRITER_CASES else run_train(name, mode)
         torch.save(compact(name, result), os.path.join(HERE, name + ".pt"))
         print(f"{name}: {time.time() - t0:.1f}s ({mode})", flush=True)
 

@@ -9,7 +9,7 @@ from oracle import tao_oracle as o
 from oracle.inputs import make_inputs, digest
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-STREAM = ["stream_h2d64", "stream_h1d128", "stream_pages"]
+STREAM = ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized"]
 TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages"]
 KEYS = ("q", "k", "v", "raw_q", "raw_k")
 
@@ -24,7 +24,7 @@ def test_stream_oracle_matches_reference(name, one_thread):
     heads, width, layer, splits, steps, seed = g["case"]
     x, _ = make_inputs(1, sum(splits) + steps, heads, width, seed)
     assert digest(*(x[k] for k in (*KEYS, "fusion_a", "fusion_b"))) == g["input_digest"]
-    st = o.OracleStream(layer)
+    st = o.OracleStream(layer, g.get("config", {}).get("fine_writer", "softmax"))
     outs, ids, pos = [], [], 0
     for n in list(splits) + [1] * steps:
         sl = slice(pos, pos + n)
@@ -54,6 +54,10 @@ def test_stream_oracle_matches_reference(name, one_thread):
         assert torch.equal(pz, rpz) and torch.equal(fz, rfz)
     for z, rz in zip(mine_snap["pending_z"], snap["pending_z"]):
         assert torch.equal(z, rz)
+    for key in ("pending_gram", "pending_cross"):
+        assert (mine_snap[key] is None) == (snap[key] is None)
+        if snap[key] is not None:
+            assert torch.equal(mine_snap[key], snap[key]), key
 
 
 @pytest.mark.parametrize("name", TRAIN)
