@@ -229,8 +229,15 @@ typedef struct TaoTrainBuffers {
   int16_t* sel;
   int* err;
   int32_t mmax;
-  int32_t reserved;
+  int32_t flags;  /* TAO_TRAIN_CALLER_FINE_C: fine_c holds the caller's fine matrices */
 } TaoTrainBuffers;
+
+/* TaoTrainBuffers.flags bit for fine writers other than softmax (reference
+ * _seal_training_all, tao_stream.py:80-123): the caller fills fine_c before
+ * tao_train_forward (the writer kernel then writes fine_z only, which keeps the
+ * softmax writer's z), and tao_train_backward returns dC in grads->dC for the caller
+ * to differentiate; the library's writer backward then carries the z path only. */
+#define TAO_TRAIN_CALLER_FINE_C 1
 
 /* S = T/256 - 1 sealed blocks (0 for T <= 768), pages = ceil(S/8), and the
  * largest number of selected fines any query of a T-token sequence reads. */

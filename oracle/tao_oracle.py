@@ -119,9 +119,11 @@ def association_matrix(gram, cross):
         return torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(BF16)
 
 
-def seal_all(raw_k, v, fine=256):
+def seal_all(raw_k, v, fine=256, writer="softmax"):
     """Training writer over all complete blocks but the last (tao_stream.py:80-123):
-    returns z [B,H,S,D], C [B,H,S,D,D] with S = T//fine - 1."""
+    returns z [B,H,S,D], C [B,H,S,D,D] with S = T//fine - 1.  With
+    writer="regularized_association" z stays the softmax writer's and C is the
+    regularised association matrix of each block (tao_stream.py:113-117)."""
     b, total, heads, d = raw_k.shape
     s = total // fine - 1
     keys = raw_k[:, :s * fine].reshape(b, s, fine, heads, d)
@@ -132,6 +134,11 @@ def seal_all(raw_k, v, fine=256):
     partition = exponent.sum(dim=2, keepdim=True).to(dt)
     prob = (exponent / partition).to(dt)
     z = (maximum.squeeze(2) + partition.squeeze(2).log()).to(dt)
+    if writer == "regularized_association":
+        gram, cross = association_statistics(keys.reshape(b * s, fine, heads, d),
+                                             values.reshape(b * s, fine, heads, d))
+        c = association_matrix(gram, cross).reshape(b, s, heads, d, d).permute(0, 2, 1, 3, 4)
+        return z.permute(0, 2, 1, 3), c
     with torch.autocast(device_type="cpu", enabled=False):
         c = torch.einsum("bsihd,bsihe->bhsde", prob, values).to(dt)
     return z.permute(0, 2, 1, 3), c
@@ -505,14 +512,14 @@ def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8):
     return (num / den).to(dt), sel_id
 
 
-def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False):
+def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False, writer="softmax"):
     """read_training (tao_stream.py:668-757) with route_interval=1; returns
     (local, fine, [selected ids per tile])."""
     local = _local_training(q, k, v)
     b, total, heads, d = q.shape
     if total <= keep_plus(fine):
         return local, torch.zeros_like(local), []
-    fine_z, fine_c = seal_all(raw_k, v, fine)
+    fine_z, fine_c = seal_all(raw_k, v, fine, writer)
     fine_parts, ids = [], []
     for tile, query in enumerate(raw_q.split(fine, dim=1)):
         visible = max(0, tile - 2)
@@ -562,11 +569,11 @@ def fuse_training(local, raw_q, fine, fine_present, fa, fb, alpha):
     return torch.where(fine_present, fused, local)
 
 
-def tao_attention(q, k, v, raw_q, raw_k, fa, fb, alpha):
+def tao_attention(q, k, v, raw_q, raw_k, fa, fb, alpha, writer="softmax"):
     """operator.tao_attention (operator.py:42-54), index-only preset.  ``alpha``
     may be a float or a per-head sequence (heads are independent, so per-head
     alpha equals one reference call per head slice)."""
-    local, fine, _ = training_read(raw_q, raw_k, v, q, k)
+    local, fine, _ = training_read(raw_q, raw_k, v, q, k, writer=writer)
     positions = torch.arange(q.shape[1])[None, :, None, None]
     present = positions >= 768
     if isinstance(alpha, (int, float)):

@@ -83,7 +83,8 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
     const size_t wsmem = (size_t)2 * 256 * D * 2 + 2 * D * 4;
     if (!tsmem(writer_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
     writer_kernel<D><<<B * H * g.S, 128, wsmem, s>>>(rk, v, static_cast<bf16*>(tb.fine_z),
-                                                      static_cast<bf16*>(tb.fine_c), dm);
+                                                      static_cast<bf16*>(tb.fine_c), dm,
+                                                      (tb.flags & TAO_TRAIN_CALLER_FINE_C) ? 0 : 1);
     const long long n = (long long)B * H * g.pages * D;
     page_prefix_kernel<D><<<(int)((n + 255) / 256), 256, 0, s>>>(
         static_cast<const bf16*>(tb.fine_z), static_cast<bf16*>(tb.page_prefix), dm, g.pages);
@@ -184,6 +185,7 @@ int tao_train_backward(const void* grad_out, const void* q, const void* k, const
   a.pages = g.pages;
   a.mmax = g.mmax;
   a.err = saved->err;
+  a.caller_c = (saved->flags & TAO_TRAIN_CALLER_FINE_C) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return width == 64 ? train_backward<64>(a, s) : train_backward<128>(a, s);
 }

@@ -23,6 +23,7 @@ struct BwdArgs {
   float *dC, *dz;                // fp32 [B,H,S,D,D] (reduced), [B,H,S,D] accumulators
   bf16* dcp;                     // per-(tile, fine) dC partials [B,H,npairs,D,D]
   float* dq_acc;                 // fp32 [B,T,H,D] dQ accumulator (tensor-core path) or null
+  int caller_c;                  // 1: fine C came from the caller; writer backward: z path only
   int npairs;                    // sum over tiles of visible fines
   TrainDims dm;
   int pages, mmax;
@@ -903,7 +904,8 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
   cp_commit();
   for (int idx = tid; idx < D * D; idx += 256) {
     const int r = idx / D, c = idx % D;
-    *reinterpret_cast<bf16*>(dB + swz(r, c, D)) = tobf(dcb[idx]);
+    // a caller-supplied C (another fine writer) takes its dC elsewhere: z path only
+    *reinterpret_cast<bf16*>(dB + swz(r, c, D)) = a.caller_c ? tobf(0.f) : tobf(dcb[idx]);
   }
   for (int d = tid; d < D; d += 256) {
     dzS[d] = rb(a.dz[(((long long)b * a.dm.H + h) * a.dm.S + s) * D + d]);

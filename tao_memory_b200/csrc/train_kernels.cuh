@@ -50,7 +50,7 @@ TAO_DEVI void channel_stats(KAt kat, float* mx, float* zp, float* scratch) {
 template <int D>
 __global__ void __launch_bounds__(128) writer_kernel(const bf16* __restrict__ raw_k,
                                                      const bf16* __restrict__ v, bf16* z_out,
-                                                     bf16* c_out, TrainDims dm) {
+                                                     bf16* c_out, TrainDims dm, int write_c) {
   using namespace wa;
   constexpr int NT = 256, CH = D / 8;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -83,6 +83,7 @@ __global__ void __launch_bounds__(128) writer_kernel(const bf16* __restrict__ ra
   }
   bf16* zo = z_out + (((long long)b * dm.H + h) * dm.S + s) * D;
   for (int d = tid; d < D; d += 128) zo[d] = tobf(__fadd_rn(mx[d], rb(logf(zp[d]))));
+  if (!write_c) return;  // the caller supplies C (another fine writer)
   __syncthreads();
   // C[d][e] = sum_t p[t][d] v[t][e]: warp w owns rows d in [w*D/4, (w+1)*D/4)
   constexpr int MT = D / 64;  // m-tiles of 16 rows per warp: 1 (D64) or 2 (D128)

@@ -16,13 +16,14 @@ from . import _lib
 from .stream import check_config
 
 _BF16 = torch.bfloat16
+TAO_TRAIN_CALLER_FINE_C = 1   # TaoTrainBuffers.flags (include/tao_b200.h)
 
 
 class _Buffers(ctypes.Structure):
     _fields_ = [("local", ctypes.c_void_p), ("lse", ctypes.c_void_p), ("fine_z", ctypes.c_void_p),
                 ("fine_c", ctypes.c_void_p), ("page_prefix", ctypes.c_void_p), ("num", ctypes.c_void_p),
                 ("den", ctypes.c_void_p), ("sel", ctypes.c_void_p), ("err", ctypes.c_void_p),
-                ("mmax", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("mmax", ctypes.c_int32), ("flags", ctypes.c_int32)]
 
 
 def _geometry(tokens):
@@ -43,7 +44,26 @@ def _gains(alpha, heads, device):
     return g.to(device)
 
 
-def _forward(q, k, v, raw_q, raw_k, fa, fb, gain):
+def _regularized_matrices(raw_k, v, s):
+    """fine_writer="regularized_association": C of the S sealed blocks
+    (_seal_training_all, tao_stream.py:113-117): writer statistics on the tensor
+    cores (``tao_writer_stats``), the regularised Cholesky solve in torch.linalg
+    (association_matrix, association_writer.py:21-32).  Returns bf16 [B,H,S,D,D]."""
+    b, t, h, d = raw_k.shape
+    dev = raw_k.device
+    gram = torch.empty(b, s, h, d, d, dtype=torch.float32, device=dev)
+    cross = torch.empty_like(gram)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for i in range(b):
+        _lib.check(_lib.lib().tao_writer_stats(raw_k[i].data_ptr(), v[i].data_ptr(), h * d, d, 256 * h * d, s, h, d,
+                                               gram[i].data_ptr(), cross[i].data_ptr(), stream))
+    gram, cross = gram.permute(0, 2, 1, 3, 4), cross.permute(0, 2, 1, 3, 4)
+    reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / d
+    system = gram + reg[..., None, None] * torch.eye(d, dtype=torch.float32, device=dev)
+    return torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(_BF16)
+
+
+def _forward(q, k, v, raw_q, raw_k, fa, fb, gain, writer="softmax"):
     b, t, h, d = q.shape
     dev = q.device
     s, pages, mmax = _geometry(t)
@@ -55,8 +75,12 @@ def _forward(q, k, v, raw_q, raw_k, fa, fb, gain):
         num=torch.empty_like(q), den=torch.empty(b, t, h, dtype=torch.float32, device=dev),
         sel=torch.empty(b, t, h, mmax, dtype=torch.int16, device=dev),
         err=torch.zeros(1, dtype=torch.int32, device=dev))
+    flags = 0
+    if writer != "softmax" and s > 0:
+        bufs["fine_c"].copy_(_regularized_matrices(raw_k, v, s))
+        flags = TAO_TRAIN_CALLER_FINE_C
     desc = _Buffers(*(bufs[n].data_ptr() for n in ("local", "lse", "fine_z", "fine_c", "page_prefix",
-                                                   "num", "den", "sel", "err")), mmax, 0)
+                                                   "num", "den", "sel", "err")), mmax, flags)
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream(dev).cuda_stream
     _lib.check(_lib.lib().tao_train_forward(
@@ -67,10 +91,11 @@ def _forward(q, k, v, raw_q, raw_k, fa, fb, gain):
 
 class _TaoAttention(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, raw_q, raw_k, fa, fb, gain):
-        out, bufs = _forward(q, k, v, raw_q, raw_k, fa, fb, gain)
+    def forward(ctx, q, k, v, raw_q, raw_k, fa, fb, gain, writer="softmax"):
+        out, bufs = _forward(q, k, v, raw_q, raw_k, fa, fb, gain, writer)
         ctx.save_for_backward(q, k, v, raw_q, raw_k, fa, fb, gain, out, *bufs.values())
         ctx.names = tuple(bufs)
+        ctx.writer = writer
         return out
 
     @staticmethod
@@ -81,9 +106,6 @@ class _TaoAttention(torch.autograd.Function):
 
 def tao_attention_train(q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, config):
     check_config(config)
-    if config.fine_writer != "softmax":
-        raise NotImplementedError("tao_attention (training) implements fine_writer='softmax' on B200; "
-                                  "%r is implemented for streaming only" % config.fine_writer)
     ops = (q, k, v, raw_q, raw_k)
     if any(t.dtype != _BF16 for t in ops):
         raise ValueError("tao_attention on B200 takes bf16 operands (the reference's selected read "
@@ -100,4 +122,5 @@ def tao_attention_train(q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, config
     gain = _gains(alpha, heads, q.device)
     fa = fusion_a.to(_BF16)
     fb = fusion_b.to(_BF16)
-    return _TaoAttention.apply(*(t.contiguous() for t in ops), fa.contiguous(), fb.contiguous(), gain)
+    return _TaoAttention.apply(*(t.contiguous() for t in ops), fa.contiguous(), fb.contiguous(), gain,
+                               config.fine_writer)

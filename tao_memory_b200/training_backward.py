@@ -15,6 +15,32 @@ class _Grads(ctypes.Structure):
                                              "dC", "dz", "dc_partial", "dq_acc")]
 
 
+def _regularized_backward(saved, gr, s):
+    """C path of fine_writer="regularized_association": the library returned dC
+    (fp32 sum of the per-tile bf16 partials) and the z path; differentiate
+    C = association_matrix(association_statistics(raw_k, v)) per sealed block with
+    torch autograd, as the reference does (association_writer.py:11-32 under
+    tao_stream.py:113-117), and add the result to d raw_k and dv in bf16."""
+    raw_k, v = saved["raw_k"], saved["v"]
+    b, t, h, d = raw_k.shape
+    n = s * 256
+    with torch.enable_grad():
+        kb = raw_k[:, :n].detach().requires_grad_(True)
+        vb = v[:, :n].detach().requires_grad_(True)
+        keys = kb.reshape(b * s, 256, h, d)
+        values = vb.reshape(b * s, 256, h, d)
+        u = keys.float().softmax(dim=-1).to(_BF16).transpose(1, 2).float()
+        vals = values.transpose(1, 2).float()
+        gram, cross = u.transpose(-1, -2) @ u, u.transpose(-1, -2) @ vals
+        reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / d
+        system = gram + reg[..., None, None] * torch.eye(d, dtype=torch.float32, device=raw_k.device)
+        c = torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(_BF16)
+        c = c.reshape(b, s, h, d, d).permute(0, 2, 1, 3, 4)
+        dk, dv = torch.autograd.grad(c, (kb, vb), gr["dC"].to(_BF16))
+    gr["d_raw_k"][:, :n] += dk
+    gr["dv"][:, :n] += dv
+
+
 def backward(ctx, grad):
     from .training import _Buffers
     saved = dict(zip(("q", "k", "v", "raw_q", "raw_k", "fa", "fb", "gain", "out") + ctx.names,
@@ -37,14 +63,18 @@ def backward(ctx, grad):
                                      device=dev),
               dq_acc=torch.empty(b, t, h, d, dtype=torch.float32, device=dev))
     gdesc = _Grads(*(gr[n].data_ptr() for n, _ in _Grads._fields_))
+    caller_c = ctx.writer != "softmax" and t > 768
+    from .training import TAO_TRAIN_CALLER_FINE_C
     sdesc = _Buffers(*(saved[n].data_ptr() for n in ("local", "lse", "fine_z", "fine_c", "page_prefix",
                                                     "num", "den", "sel", "err")),
-                     saved["sel"].shape[-1], 0)
+                     saved["sel"].shape[-1], TAO_TRAIN_CALLER_FINE_C if caller_c else 0)
     stream = torch.cuda.current_stream(dev).cuda_stream
     _lib.check(_lib.lib().tao_train_backward(
         grad.data_ptr(), *(saved[n].data_ptr() for n in ("q", "k", "v", "raw_q", "raw_k", "fa", "fb", "gain")),
         b, t, h, d, saved["out"].data_ptr(), ctypes.byref(sdesc), ctypes.byref(gdesc), stream))
+    if caller_c:
+        _regularized_backward(saved, gr, s)
     # parameter gradients: the reference sums bf16 products in fp32 and rounds once
     dfa = gr["d_fusion_a"].to(_BF16)
     dfb = gr["d_fusion_b"].to(_BF16)
-    return gr["dq"], gr["dk"], gr["dv"], gr["d_raw_q"], gr["d_raw_k"], dfa, dfb, None
+    return gr["dq"], gr["dk"], gr["dv"], gr["d_raw_q"], gr["d_raw_k"], dfa, dfb, None, None

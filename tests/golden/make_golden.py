@@ -140,6 +140,11 @@ WRITER_CASES = {
     "stream_regularized": ((2, 64, 1, (1000, 1900), 40, 8), "regularized_association"),
 }
 
+# training cases with another fine writer on the index-only preset
+TRAIN_WRITER_CASES = {
+    "train_regularized": ((1, 2048, 2, 64, 0.5, 9), "regularized_association"),
+}
+
 TRAIN_CASES = {
     # name: (batch, tokens, heads, width, alpha, seed)
     "train_t2048_h2": (1, 2048, 2, 64, 0.5, 4),
@@ -205,17 +210,23 @@ def run_stream(name, mode):
 def run_train(name, mode):
     from tao_attention import tao_attention
     from tao_attention.presets import index_only_page_memo
-    batch, tokens, heads, width, alpha, seed = TRAIN_CASES[name]
+    from tao_attention.config import TaoConfig
+    if name in TRAIN_WRITER_CASES:
+        case, writer = TRAIN_WRITER_CASES[name]
+        config = TaoConfig(**{**index_only_page_memo().export(), "fine_writer": writer})
+    else:
+        case, config = TRAIN_CASES[name], index_only_page_memo()
+    batch, tokens, heads, width, alpha, seed = case
     x, g = make_inputs(batch, tokens, heads, width, seed)
     grad = torch.randn(batch, tokens, heads, width, generator=g).to(torch.bfloat16)
     leaves = {k: x[k].clone().requires_grad_(True) for k in x}
     out = tao_attention(leaves["q"], leaves["k"], leaves["v"], raw_q=leaves["raw_q"],
                         raw_k=leaves["raw_k"], fusion_a=leaves["fusion_a"],
                         fusion_b=leaves["fusion_b"], alpha=alpha,
-                        config=index_only_page_memo())
+                        config=config)
     out.backward(grad)
     return {
-        "kind": "train", "mode": mode, "case": TRAIN_CASES[name], "alpha": alpha,
+        "kind": "train", "mode": mode, "case": case, "alpha": alpha, "config": config.export(),
         "input_digest": digest(*(x[k] for k in ("q", "k", "v", "raw_q", "raw_k", "fusion_a", "fusion_b")), grad),
         "output": out.detach(),
         "grads": {k: leaves[k].grad.detach().clone() for k in leaves},
@@ -261,7 +272,7 @@ def main():
         check_fast()
         install_fast(args.reference)
     mode = "reference+fast-inference-kernels" if args.fast else "reference (interpreted Triton, patched)"
-    cases = args.cases or [*STREAM_CASES, *WRITER_CASES, *TRAIN_CASES]
+    cases = args.cases or [*STREAM_CASES, *WRITER_CASES, *TRAIN_CASES, *TRAIN_WRITER_CASES]
     if args.compact_only:
         for name in cases:
             path = os.path.join(HERE, name + ".pt")

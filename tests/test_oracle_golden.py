@@ -10,7 +10,7 @@ from oracle.inputs import make_inputs, digest
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 STREAM = ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized"]
-TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages"]
+TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages", "train_regularized"]
 KEYS = ("q", "k", "v", "raw_q", "raw_k")
 
 
@@ -68,7 +68,8 @@ def test_training_oracle_matches_reference(name, one_thread):
     grad = torch.randn(b, t, h, d, generator=gen).to(torch.bfloat16)
     assert digest(*(x[k] for k in (*KEYS, "fusion_a", "fusion_b")), grad) == g["input_digest"]
     leaves = {k: x[k].clone().requires_grad_(True) for k in x}
-    out = o.tao_attention(*(leaves[k] for k in KEYS), leaves["fusion_a"], leaves["fusion_b"], alpha)
+    writer = g.get("config", {}).get("fine_writer", "softmax")
+    out = o.tao_attention(*(leaves[k] for k in KEYS), leaves["fusion_a"], leaves["fusion_b"], alpha, writer)
     out.backward(grad)
     s = g.get("row_stride", 1)
     ref = g["output"]

@@ -19,26 +19,34 @@ def frac_bad(a, b):
     return ((a - b).abs() > 2e-2 + 2e-2 * b.abs()).float().mean().item()
 
 
-def run(x, alpha, grad=None):
+def run(x, alpha, grad=None, config=None):
     import tao_memory_b200 as tb
     from tao_memory_b200.presets import index_only_page_memo
     leaves = {k: t.cuda().requires_grad_(grad is not None) for k, t in x.items()}
     out = tb.tao_attention(*(leaves[k] for k in KEYS[:3]), raw_q=leaves["raw_q"], raw_k=leaves["raw_k"],
                            fusion_a=leaves["fusion_a"], fusion_b=leaves["fusion_b"], alpha=alpha,
-                           config=index_only_page_memo())
+                           config=index_only_page_memo() if config is None else config)
     if grad is not None:
         out.backward(grad.cuda())
         return out.detach(), {k: leaves[k].grad for k in leaves}
     return out.detach(), None
 
 
-@pytest.mark.parametrize("name", ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages"])
+GOLDEN_TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages", "train_regularized"]
+
+
+def _config(g):
+    from tao_memory_b200 import TaoConfig
+    return TaoConfig(**g["config"]) if "config" in g else None
+
+
+@pytest.mark.parametrize("name", GOLDEN_TRAIN)
 def test_forward_matches_reference_golden(name):
     g = torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
     b, t, h, d, alpha, seed = g["case"]
     x, _ = make_inputs(b, t, h, d, seed)
     with torch.no_grad():
-        out, _ = run(x, alpha)
+        out, _ = run(x, alpha, config=_config(g))
     s = g.get("row_stride", 1)
     assert frac_bad(out[:, ::s], g["output"]) <= 1e-3
 
@@ -57,13 +65,13 @@ def rel_l2(a, b):
     return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
 
 
-@pytest.mark.parametrize("name", ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages"])
+@pytest.mark.parametrize("name", GOLDEN_TRAIN)
 def test_backward_matches_reference_golden(name):
     g = torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
     b, t, h, d, alpha, seed = g["case"]
     x, gen = make_inputs(b, t, h, d, seed)
     grad = torch.randn(b, t, h, d, generator=gen).to(torch.bfloat16)
-    out, grads = run(x, alpha, grad)
+    out, grads = run(x, alpha, grad, config=_config(g))
     s = g.get("row_stride", 1)
     assert frac_bad(out[:, ::s], g["output"]) <= 1e-3
     for k, ref in g["grads"].items():
@@ -100,3 +108,23 @@ def test_tcgen05_attention_backward_matches_mma_sync(b, t, h):
     assert frac_bad(out1, out0) == 0.0
     for k in ("q", "k", "v", "raw_q", "raw_k"):
         assert rel_l2(g1[k], g0[k]) <= 1e-2, (k, rel_l2(g1[k], g0[k]))
+
+
+def test_regularized_writer_training_matches_oracle(one_thread):
+    """fine_writer="regularized_association" through tao_attention: outputs and
+    gradients against the oracle on a larger case than the reference golden
+    (two batches, three heads, two completed pages)."""
+    from tao_memory_b200 import TaoConfig
+    from tao_memory_b200.presets import index_only_page_memo
+    config = TaoConfig(**{**index_only_page_memo().export(), "fine_writer": "regularized_association"})
+    b, t, h, d, alpha = 2, 5120, 3, 64, 0.6
+    x, gen = make_inputs(b, t, h, d, seed=41)
+    grad = torch.randn(b, t, h, d, generator=gen).to(torch.bfloat16)
+    out, grads = run(x, alpha, grad, config=config)
+    leaves = {k: x[k].clone().requires_grad_(True) for k in x}
+    ref = o.tao_attention(*(leaves[k] for k in KEYS), leaves["fusion_a"], leaves["fusion_b"], alpha,
+                          "regularized_association")
+    ref.backward(grad)
+    assert frac_bad(out, ref.detach()) <= 1e-3
+    for k in leaves:
+        assert rel_l2(grads[k], leaves[k].grad) <= 2e-2, (k, rel_l2(grads[k], leaves[k].grad))
