@@ -274,21 +274,31 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   const bool live = q < nq;
   const bf16* rq = a.raw_q + ((long long)b * a.dm.T + q0 + q) * row + hoff;
   if (live) {
+    // the query row, read once into registers (width 64; width 128 re-reads it)
+    uint4 rqv[D == 64 ? D / 8 : 1];
+    if constexpr (D == 64) {
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) rqv[c] = *reinterpret_cast<const uint4*>(rq + c * 8);
+    }
+    auto rq_chunk = [&](int c) -> uint4 {
+      if constexpr (D == 64) return rqv[c];
+      else return *reinterpret_cast<const uint4*>(rq + c * 8);
+    };
     float mx = -INFINITY;
     for (int c = 0; c < D / 8; ++c) {
       float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      unpack8(rq_chunk(c), f);
       for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
     }
     float sum = 0.f;
     for (int c = 0; c < D / 8; ++c) {
       float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      unpack8(rq_chunk(c), f);
       for (int e = 0; e < 8; ++e) sum += expf(f[e] - mx);
     }
     for (int c = 0; c < D / 8; ++c) {
       float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
+      unpack8(rq_chunk(c), f);
       __nv_bfloat162 o[4];
       for (int e = 0; e < 4; ++e)
         o[e] = __floats2bfloat162_rn(__fdiv_rn(expf(f[2 * e] - mx), sum), __fdiv_rn(expf(f[2 * e + 1] - mx), sum));
@@ -469,7 +479,23 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
     if (NBUF == 1 && i + 1 < nu) load_c(list[i + 1], 0);
   }
 
-  // ---- 4. epilogue: num, fine, fusion (operator.py:21-39, index-only preset)
+  // ---- 4. epilogue: num, fine, fusion (operator.py:21-39, index-only preset).
+  // The tile's raw_q and local rows are staged (coalesced) into the h and A
+  // buffers, free now, and the fusion parameters of this head into shared memory.
+  __shared__ float fabS[2][D * 3];
+  for (int idx = tid; idx < nq * (D / 8); idx += 256) {
+    const int r = idx / (D / 8), c = idx % (D / 8);
+    const long long off = ((long long)b * a.dm.T + q0 + r) * row + hoff + c * 8;
+    cp_async16(sH + swz(r, c * 8, D), a.raw_q + off, true);
+    cp_async16(sA + swz(r, c * 8, D), a.local + off, true);
+  }
+  cp_commit();
+  for (int idx = tid; idx < D * 3; idx += 256) {
+    fabS[0][idx] = bf(a.fa[(long long)h * D * 3 + idx]);
+    fabS[1][idx] = bf(a.fb[(long long)h * D * 3 + idx]);
+  }
+  cp_wait<0>();
+  __syncthreads();
   const float gain = a.gain[h];
   const int g = lane >> 2, c4 = lane & 3;
 #pragma unroll
@@ -483,18 +509,20 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {
         const int e = j * 8 + c4 * 2;
+        const uint32_t q2 = *reinterpret_cast<const uint32_t*>(smem + swz(r, e, D));
+        const uint32_t l2 = *reinterpret_cast<const uint32_t*>(smem + 256 * D * 2 + swz(r, e, D));
         float res[2], nums[2];
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const float num = rb(acc[mi][j][hr * 2 + x]);
           nums[x] = num;
           const float fine = rb(__fdiv_rn(num, den));
-          const float qv = bf(a.raw_q[base + e + x]);
-          const float loc = bf(a.local[base + e + x]);
-          const bf16* fa = a.fa + ((long long)h * D + e + x) * 3;
-          const bf16* fb = a.fb + ((long long)h * D + e + x) * 3;
-          const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), qv)), bf(fb[0]))), 0.f));
-          const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), qv)), bf(fb[2])));
+          const float qv = x ? hi_f(q2) : lo_f(q2);
+          const float loc = x ? hi_f(l2) : lo_f(l2);
+          const float* fa = fabS[0] + (e + x) * 3;
+          const float* fb = fabS[1] + (e + x) * 3;
+          const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(fa[0], qv)), fb[0])), 0.f));
+          const float s2 = rb(__fadd_rn(rb(__fmul_rn(fa[2], qv)), fb[2]));
           const float mx = fmaxf(s0, s2);
           // the larger term is exp(0) = 1 exactly: one exponential per element
           const float eo = expf(fminf(s0, s2) - mx);
