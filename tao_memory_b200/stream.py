@@ -442,6 +442,12 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
         raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
     for st in states:
         st._ensure(heads, width, dev, w)
+    if (w == 1 and dev.type == "cuda" and all(st.config.q1_history_region_graph and st.config.fine_writer == "softmax"
+                                              for st in states)
+            and _BatchGraph.run(states, ops, fa, fb, alpha, out, heads, width)):
+        for st in states:
+            _bookkeep(st, 1)
+        return
     args = _BatchArgs.get(states, w, heads, width, dev)
     for i, st in enumerate(states):
         args.pos[i] = st.position
@@ -550,6 +556,60 @@ class _DecodeGraph:
 
 
 _GRAPH_WORKSPACES = {}
+
+
+class _BatchGraph:
+    """Graph mode for ``tao_attention_decode_batch`` (states configured with
+    ``q1_history_region_graph``): the decode step of the whole batch, captured over
+    the caller's own operand buffers.  A step is captured the second time the same
+    states, capacities, alpha and operand addresses are seen in a row (callers that
+    reuse their buffers, as graph users do) and replayed from then on; other calls
+    run eagerly.  Like ``_DecodeGraph``, nothing is re-captured at a seal."""
+
+    cache = {}      # key -> _BatchGraph
+    last = None     # key of the previous eager call
+
+    def __init__(self, states, ops, fa, fb, alpha, out, heads, width):
+        dev = ops[0].device
+        lib = _lib.lib()
+        r = len(states)
+        self.ptrs = torch.tensor([st._desc.data_ptr() for st in states], dtype=torch.int64, device=dev)
+        self.policy = policy_for(states[0].config)
+        self.pos = (ctypes.c_int64 * r)(*[st.position for st in states])
+        self.cap = (ctypes.c_int32 * r)(*[st.cap_fines for st in states])
+        self.layers = (ctypes.c_int32 * r)(*[st.layer_index for st in states])
+        nbytes = lib.tao_stream_workspace_bytes(r, 1, heads, width, ROUTE_CAP, ctypes.byref(self.policy))
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _GRAPH_WORKSPACES.setdefault(dev, []).append(self.ws)
+        self.graph = torch.cuda.CUDAGraph()
+        rc = 0
+        lib.tao_decode_graph_mode(1)
+        try:
+            with torch.cuda.graph(self.graph, capture_error_mode="relaxed"):
+                rc = lib.tao_decode_step(self.ptrs.data_ptr(), r, self.pos, self.layers, self.cap,
+                                         ctypes.byref(self.policy), heads, width,
+                                         *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
+                                         float(alpha), out.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                                         torch.cuda.current_stream(dev).cuda_stream)
+        finally:
+            lib.tao_decode_graph_mode(0)
+        _lib.check(rc)
+
+    @classmethod
+    def run(cls, states, ops, fa, fb, alpha, out, heads, width):
+        """Replay (or capture and replay) the batch step; False = run it eagerly."""
+        key = (tuple((st._desc.data_ptr(), st.cap_fines, st.layer_index) for st in states), heads, width,
+               float(alpha), tuple(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(), out.data_ptr())
+        g = cls.cache.get(key)
+        if g is None:
+            if cls.last != key:
+                cls.last = key
+                return False
+            if len(cls.cache) >= 8:
+                cls.cache.clear()
+            g = cls.cache[key] = cls(states, ops, fa, fb, alpha, out, heads, width)
+        g.graph.replay()
+        return True
 
 
 def check_device(device=None):
