@@ -138,7 +138,7 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the read backward kernel");
   if (!tsmem(read_bwd_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
   constexpr int NQ = ReadBwdSmem<D>::NQ;
-  read_bwd_kernel<D><<<dim3(g.tiles * (256 / NQ), B * H), NQ, rsmem, s>>>(a);
+  read_bwd_kernel<D><<<dim3(g.tiles * (256 / NQ), B * H), ReadBwdSmem<D>::NT, rsmem, s>>>(a);
   if (g.S > 0) {
     dc_reduce_kernel<D><<<B * H * g.S, 256, 0, s>>>(a, g.tiles);
     const size_t wsmem = WriterBwdSmem<D>::bytes();

@@ -442,36 +442,53 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(BwdArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Selected-read backward: one CTA (256 threads) per (tile, b, h).  Fines are
-// visited page by page; for fine s and the queries that selected it:
+// Selected-read backward: one CTA (NT threads, 16 * MI query rows per warp) per
+// (tile part, b, h).
+// Fines are visited page by page; for fine s only the queries that selected it
+// take part: they are compacted into a row list (ldmatrix gathers their rows by
+// address, so nothing is copied) and
 //   dA   = bf16(bf16(gn . C_s^T) + gd)                  (tensor cores)
 //   dhv += bf16(dA * w_s)   -> per page: dh += bf16(dhv*pw), dpw += bf16(dhv*h)
 //   dw_s = sum_q bf16(dA * hv)                          -> dz, d page_z via exp
-//   dC_s = A_s^T . gn (bf16 per tile)                   (tensor cores, fp32 atomics)
-// then the softmax backward of h (-> d raw_q) and of the page weights, and the
-// logsumexp backward of the tile's page log-partitions (-> dz).
+//   dC_s = A_s^T . gn (bf16 per tile)                   (tensor cores)
+// run over ceil(selected/16) row blocks instead of all NQ rows.  dhv lives in
+// shared memory (fp32, rows XOR-swizzled by 16-byte chunk); C_{s+1} is fetched
+// while fine s is processed (D = 64).  Then the softmax backward of h (-> d raw_q)
+// and of the page weights, and the logsumexp backward of the tile's page
+// log-partitions (-> dz).
 // ---------------------------------------------------------------------------
 template <int D>
 struct ReadBwdSmem {
-  static constexpr int NQ = (D == 64) ? 256 : 128;  // queries (= threads) per CTA
-  static size_t bytes(int P, int V, int mmax) {
-    return 4 * (size_t)NQ * D * 2 + (size_t)D * D * 2 + 4 * (size_t)P * D * 4 + (size_t)P * D * 2 +
-           ((size_t)V * D * 2 + 15) / 16 * 16 + (size_t)NQ * mmax * 2 + NQ * 4 + NQ +
-           (size_t)(NQ / 32) * D * 4 + (size_t)(V + 8) * 4 * 2 + 64;
+  static constexpr int NQ = (D == 64) ? 256 : 128;  // queries per CTA
+  static constexpr int NT = (D == 64) ? NQ : 2 * NQ;  // threads per CTA (2 * NQ: fewer registers per thread)
+  static constexpr int CB = (D == 64) ? 2 : 1;      // C_s buffers (2: next fine prefetched)
+  static size_t bytes(int P, int V, int /*mmax*/) {
+    const size_t words = (size_t)(V + 31) / 32;
+    return 3 * (size_t)NQ * D * 2 + (size_t)CB * D * D * 2 + (size_t)NQ * D * 4 + 4 * (size_t)P * D * 4 +
+           (size_t)P * D * 2 + (size_t)D * 2 + words * NQ * 4 + NQ * 4 + NQ + (size_t)(NT / 32) * D * 4 +
+           (size_t)(V + 8) * 4 * 2 + 64;
   }
 };
 
+// float offset of the channel pair (r, d..d+1) in a [rows][D] fp32 tile whose
+// 16-byte chunks are XOR-swizzled by r % 8
 template <int D>
-__global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a) {
+TAO_DEVI int dhv_off(int r, int d) {
+  return r * D + ((((d >> 2) ^ (r & 7))) << 2) + (d & 3);
+}
+
+template <int D>
+__global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs a) {
   using namespace wa;
-  constexpr int NQ = ReadBwdSmem<D>::NQ, QS = 256 / NQ;
+  constexpr int NQ = ReadBwdSmem<D>::NQ, NT = ReadBwdSmem<D>::NT, CB = ReadBwdSmem<D>::CB, QS = 256 / NQ;
+  constexpr int NW = NT / 32, MI = NQ / (16 * NW);  // warp w owns query rows 16*MI*w .. + 16*MI - 1
   const int tile = blockIdx.x / QS, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = tile * 256 + (blockIdx.x % QS) * NQ, nq = max(0, min(NQ, a.dm.T - q0));
   const int V = max(0, tile - 2);
   const long long row = a.dm.row, hoff = (long long)h * D;
   if (V == 0) {
-    for (int idx = tid; idx < nq * (D / 8); idx += NQ) {
+    for (int idx = tid; idx < nq * (D / 8); idx += NT) {
       const int q = idx / (D / 8), c = idx % (D / 8);
       const long long off = ((long long)b * a.dm.T + q0 + q) * row + hoff + c * 8;
       *reinterpret_cast<uint4*>(a.d_raw_q + off) = *reinterpret_cast<const uint4*>(a.d_rq_f + off);
@@ -479,41 +496,43 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
     return;
   }
   const int completed = V / kGroup, pending = V % kGroup, P = completed + (pending > 0);
-  const int M = a.mmax;
+  const int M = a.mmax, VW = (V + 31) / 32;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ptr = smem;
   const uint32_t sH = smem_u32(ptr);  ptr += NQ * D * 2;
   const uint32_t sG = smem_u32(ptr);  ptr += NQ * D * 2;
-  const uint32_t sA = smem_u32(ptr);  ptr += NQ * D * 2;
-  const uint32_t sC = smem_u32(ptr);  ptr += D * D * 2;
-  uint8_t* hvB = ptr;                 ptr += NQ * D * 2;  // bf16(h * pw[page]) of the current page
+  const uint32_t sA = smem_u32(ptr);  ptr += NQ * D * 2;   // A_s rows of the selecting queries, compacted
+  const uint32_t sC = smem_u32(ptr);  ptr += CB * D * D * 2;
   uint8_t* hB = smem;
   uint8_t* aB = smem + 2 * NQ * D * 2;
+  float* dhvS = reinterpret_cast<float*>(ptr);  ptr += (size_t)NQ * D * 4;  // dhv of the current page
   float* pwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* pzS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* dpwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   float* dpzS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
   bf16* pw2S = reinterpret_cast<bf16*>(ptr);    ptr += (size_t)P * D * 2;  // page weights as bf16
-  bf16* swS = reinterpret_cast<bf16*>(ptr);     ptr += ((size_t)V * D * 2 + 15) / 16 * 16;
-  int16_t* selS = reinterpret_cast<int16_t*>(ptr); ptr += (size_t)NQ * M * 2;
+  bf16* wS = reinterpret_cast<bf16*>(ptr);      ptr += D * 2;              // w_s of the current fine
+  uint32_t* selB = reinterpret_cast<uint32_t*>(ptr); ptr += (size_t)VW * NQ * 4;  // [word][query] bits
   float* gdS = reinterpret_cast<float*>(ptr);   ptr += NQ * 4;
-  uint8_t* selq = ptr;                          ptr += NQ;
-  float* dwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)(NQ / 32) * D * 4;  // per-warp dw partials
+  uint8_t* rowS = ptr;                          ptr += NQ;   // compacted row -> query
+  float* dwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)NW * D * 4;  // per-warp dw partials
   int* useS = reinterpret_cast<int*>(ptr);
   int* list = useS + V;
+  __shared__ int cntS[NW];
 
   // ---- tables (as in the forward)
   const bf16* pzb = a.pzpre + ((long long)b * a.dm.H + h) * a.pages * kGroup * D;
-  for (int idx = tid; idx < P * D; idx += NQ) {
+  for (int idx = tid; idx < P * D; idx += NT) {
     const int pg = idx / D, d = idx % D;
     const int n = (pg < completed) ? kGroup : pending;
-    pzS[idx] = bf(pzb[((long long)pg * kGroup + (n - 1)) * D + d]);
+    pzS[idx] = bf(__ldg(pzb + ((long long)pg * kGroup + (n - 1)) * D + d));
     dpwS[idx] = 0.f;
     dpzS[idx] = 0.f;
   }
-  for (int i = tid; i < V; i += NQ) useS[i] = 0;
+  for (int i = tid; i < V; i += NT) useS[i] = 0;
+  for (int i = tid; i < NQ * D; i += NT) dhvS[i] = 0.f;
   __syncthreads();
-  for (int d = tid; d < D; d += NQ) {
+  for (int d = tid; d < D; d += NT) {
     float mx = -INFINITY;
     for (int pg = 0; pg < P; ++pg) mx = fmaxf(mx, pzS[pg * D + d]);
     float sum = 0.f;
@@ -524,51 +543,85 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
     }
   }
   const bf16* zb = a.z + ((long long)b * a.dm.H + h) * a.dm.S * D;
-  for (int idx = tid; idx < V * D; idx += NQ) {
-    const int sf = idx / D, d = idx % D;
-    swS[idx] = tobf(expf(rb(__fsub_rn(bf(zb[(long long)sf * D + d]), pzS[(sf / kGroup) * D + d]))));
-  }
-  // ---- per query: h (swizzled), gn (swizzled), gd, selections
-  const int q = tid;
+  // ---- per query: h (swizzled); gn (swizzled), gd and the selection bits (with
+  // 2 * NQ threads the second NQ load these while the first NQ compute h)
+  const int q = tid % NQ;
+  const bool first = tid < NQ;
   const bool live = q < nq;
   const long long qbase = ((long long)b * a.dm.T + q0 + q) * row + hoff;
-  if (live) {
-    const bf16* rq = a.raw_q + qbase;
-    float mx = -INFINITY;
-    for (int c = 0; c < D / 8; ++c) {
-      float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
-      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
+  // every global read of this kernel is of data it does not write: read-only
+  // loads (ld.global.nc), issued before the shared-memory stores that use them
+  if (first) {
+    uint4 rv[D / 8];
+    if (live) {
+      const uint4* rq = reinterpret_cast<const uint4*>(a.raw_q + qbase);
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) rv[c] = __ldg(rq + c);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        float f[8];
+        unpack8(rv[c], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        float f[8];
+        unpack8(rv[c], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sum += expf(f[e] - mx);
+      }
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) {
+        float f[8];
+        unpack8(rv[c], f);
+        __nv_bfloat162 o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          o[e] = __floats2bfloat162_rn(__fdiv_rn(expf(f[2 * e] - mx), sum), __fdiv_rn(expf(f[2 * e + 1] - mx), sum));
+        rv[c] = *reinterpret_cast<uint4*>(o);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) rv[c] = make_uint4(0, 0, 0, 0);
     }
-    float sum = 0.f;
-    for (int c = 0; c < D / 8; ++c) {
-      float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
-      for (int e = 0; e < 8; ++e) sum += expf(f[e] - mx);
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(hB + swz(q, c * 8, D)) = rv[c];
+  }
+  if (NT == NQ || !first) {
+    for (int w = 0; w < VW; ++w) selB[w * NQ + q] = 0u;
+    uint4 gv[D / 8];
+    float gdv = 0.f;
+    if (live) {
+      const uint4* gq = reinterpret_cast<const uint4*>(a.gn + qbase);
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) gv[c] = __ldg(gq + c);
+      gdv = __ldg(a.gd + ((long long)b * a.dm.T + q0 + q) * a.dm.H + h);
+    } else {
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) gv[c] = make_uint4(0, 0, 0, 0);
     }
-    for (int c = 0; c < D / 8; ++c) {
-      float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(rq + c * 8), f);
-      __nv_bfloat162 o[4];
-      for (int e = 0; e < 4; ++e)
-        o[e] = __floats2bfloat162_rn(__fdiv_rn(expf(f[2 * e] - mx), sum), __fdiv_rn(expf(f[2 * e + 1] - mx), sum));
-      *reinterpret_cast<uint4*>(hB + swz(q, c * 8, D)) = *reinterpret_cast<uint4*>(o);
-      *reinterpret_cast<uint4*>(hB + NQ * D * 2 + swz(q, c * 8, D)) =
-          *reinterpret_cast<const uint4*>(a.gn + qbase + c * 8);
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(hB + NQ * D * 2 + swz(q, c * 8, D)) = gv[c];
+    gdS[q] = gdv;
+    if (live) {
+      const short* so = reinterpret_cast<const short*>(a.sel) + (((long long)b * a.dm.T + q0 + q) * a.dm.H + h) * a.mmax;
+      for (int m0 = 0; m0 < M; m0 += 8) {
+        int sv[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) sv[m] = (m0 + m < M) ? (int)__ldg(so + m0 + m) : -1;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int s = sv[m];
+          if (s >= 0 && s < V) {
+            selB[(s >> 5) * NQ + q] |= 1u << (s & 31);
+            useS[s] = 1;
+          }
+        }
+      }
     }
-    gdS[q] = a.gd[((long long)b * a.dm.T + q0 + q) * a.dm.H + h];
-    const int16_t* so = a.sel + (((long long)b * a.dm.T + q0 + q) * a.dm.H + h) * a.mmax;
-    for (int m = 0; m < M; ++m) {
-      selS[q * M + m] = so[m];
-      if (so[m] >= 0) useS[so[m]] = 1;
-    }
-  } else {
-    for (int c = 0; c < D / 8; ++c) {
-      *reinterpret_cast<uint4*>(hB + swz(q, c * 8, D)) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(hB + NQ * D * 2 + swz(q, c * 8, D)) = make_uint4(0, 0, 0, 0);
-    }
-    gdS[q] = 0.f;
-    for (int m = 0; m < M; ++m) selS[q * M + m] = -1;
   }
   __syncthreads();
   __shared__ int nused;
@@ -583,43 +636,58 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
   auto hval = [&](int qq, int d) -> float { return bf(*reinterpret_cast<const bf16*>(hB + swz(qq, d, D))); };
   constexpr int NTL = D / 8;
   const int g = lane >> 2, c4 = lane & 3;
-  float dhv[2][NTL][4], dh[2][NTL][4];
+  float dh[MI][NTL][4];  // rows 16 * (MI * warp + mi) + g (+ 8)
 #pragma unroll
-  for (int i = 0; i < 2; ++i)
+  for (int mi = 0; mi < MI; ++mi)
 #pragma unroll
     for (int j = 0; j < NTL; ++j)
 #pragma unroll
-      for (int x = 0; x < 4; ++x) dhv[i][j][x] = dh[i][j][x] = 0.f;
+      for (int x = 0; x < 4; ++x) dh[mi][j][x] = 0.f;
   const bf16* cb = a.C + ((long long)b * a.dm.H + h) * a.dm.S * (long long)D * D;
   int cur_page = -1;
   const uint32_t* pw2 = reinterpret_cast<const uint32_t*>(pw2S);
-  const uint32_t* sw2 = reinterpret_cast<const uint32_t*>(swS);
+  const uint32_t* w2 = reinterpret_cast<const uint32_t*>(wS);
   auto pair_at = [&](const uint8_t* base, int r, int d) -> uint32_t {  // bf16 pair (d even) of row r
     return *reinterpret_cast<const uint32_t*>(base + swz(r, d, D));
   };
+  auto fetch_c = [&](int sf, int buf) {
+    for (int idx = tid; idx < D * D / 8; idx += NT) {
+      const int r = idx / (D / 8), c = idx % (D / 8);
+      cp_async16(sC + buf * D * D * 2 + swz(r, c * 8, D), cb + (long long)sf * D * D + r * D + c * 8, true);
+    }
+  };
   auto flush_page = [&](int pg) {
-    // dh += bf16(bf16(dhv)*pw[pg]) ; dpw[pg] += sum_q bf16(bf16(dhv)*h)
+    // dh += bf16(bf16(dhv)*pw[pg]) ; dpw[pg] += sum_q bf16(bf16(dhv)*h) ; dhv = 0
     float part[NTL][2];
 #pragma unroll
     for (int j = 0; j < NTL; ++j) part[j][0] = part[j][1] = 0.f;
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int rr = 0; rr < 2 * MI; ++rr) {
+      const int mi = rr >> 1, xp = rr & 1;
+      const int r = (warp * MI + mi) * 16 + g + xp * 8;
+      float2 acc[NTL];
+      uint32_t hp[NTL];
 #pragma unroll
-      for (int xp = 0; xp < 2; ++xp) {
-        const int r = warp * 32 + mi * 16 + g + xp * 8;
-#pragma unroll
-        for (int j = 0; j < NTL; ++j) {
-          const int d = j * 8 + c4 * 2;
-          const uint32_t v2 = wa::pack_bf16(dhv[mi][j][2 * xp], dhv[mi][j][2 * xp + 1]);
-          const uint32_t pp = hmul2u(v2, pw2[(pg * D + d) / 2]);
-          const uint32_t hh = hmul2u(v2, pair_at(hB, r, d));
-          dh[mi][j][2 * xp] += lo_f(pp);
-          dh[mi][j][2 * xp + 1] += hi_f(pp);
-          part[j][0] += lo_f(hh);
-          part[j][1] += hi_f(hh);
-          dhv[mi][j][2 * xp] = dhv[mi][j][2 * xp + 1] = 0.f;
-        }
+      for (int j = 0; j < NTL; ++j) {  // all loads before the stores that clear the cells
+        const int d = j * 8 + c4 * 2;
+        acc[j] = *reinterpret_cast<const float2*>(dhvS + dhv_off<D>(r, d));
+        hp[j] = pair_at(hB, r, d);
       }
+#pragma unroll
+      for (int j = 0; j < NTL; ++j)
+        *reinterpret_cast<float2*>(dhvS + dhv_off<D>(r, j * 8 + c4 * 2)) = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) {
+        const int d = j * 8 + c4 * 2;
+        const uint32_t v2 = wa::pack_bf16(acc[j].x, acc[j].y);
+        const uint32_t pp = hmul2u(v2, pw2[(pg * D + d) / 2]);
+        const uint32_t hh = hmul2u(v2, hp[j]);
+        dh[mi][j][2 * xp] += lo_f(pp);
+        dh[mi][j][2 * xp + 1] += hi_f(pp);
+        part[j][0] += lo_f(hh);
+        part[j][1] += hi_f(hh);
+      }
+    }
 #pragma unroll
     for (int j = 0; j < NTL; ++j)
 #pragma unroll
@@ -632,94 +700,123 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
       }
   };
   const int nu = nused;
+  float znext = (nu > 0 && tid < D) ? bf(__ldg(zb + (long long)list[0] * D + tid)) : 0.f;  // z of the next fine
+  if (CB == 2 && nu > 0) {
+    fetch_c(list[0], 0);
+    cp_commit();
+  }
   for (int i = 0; i < nu; ++i) {
     const int sf = list[i], pg = sf / kGroup;
+    const int buf = (CB == 2) ? (i & 1) : 0;
+    // ---- phase 1: page change, w_s, C prefetch, selection ballot
     if (pg != cur_page) {
       if (cur_page >= 0) flush_page(cur_page);
       cur_page = pg;
-      // hv = bf16(h * pw[pg]) of this thread's query row (read by all threads after the next barrier)
+    }
+    if (tid < D) {  // D <= NT: one channel per thread
+      const float zc = znext;
+      if (i + 1 < nu) znext = bf(__ldg(zb + (long long)list[i + 1] * D + tid));
+      wS[tid] = tobf(expf(rb(__fsub_rn(zc, pzS[pg * D + tid]))));
+    }
+    if (CB == 2) {
+      if (i + 1 < nu) fetch_c(list[i + 1], buf ^ 1);
+    } else {
+      fetch_c(sf, 0);
+    }
+    cp_commit();
+    const bool sel = first && ((selB[(sf >> 5) * NQ + q] >> (sf & 31)) & 1u);
+    const unsigned ballot = __ballot_sync(0xffffffffu, sel);
+    if (lane == 0) cntS[warp] = __popc(ballot);
+    __syncthreads();
+    // ---- phase 2: compacted row list and A_s = bf16(bf16(h * pw) * w_s) of the selecting queries
+    int before = 0, ns = 0;
+#pragma unroll
+    for (int w = 0; w < NQ / 32; ++w) {  // only the first NQ threads vote
+      const int c = cntS[w];
+      before += (w < warp) ? c : 0;
+      ns += c;
+    }
+    const int npad = (ns + 15) & ~15;
+    if (sel) {
+      const int pos = before + __popc(ballot & ((1u << lane) - 1u));
+      rowS[pos] = (uint8_t)q;
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
         const uint4 hc = *reinterpret_cast<const uint4*>(hB + swz(q, c * 8, D));
         const uint4 pc = *reinterpret_cast<const uint4*>(pw2 + (pg * D + c * 8) / 2);
-        *reinterpret_cast<uint4*>(hvB + swz(q, c * 8, D)) =
-            make_uint4(hmul2u(hc.x, pc.x), hmul2u(hc.y, pc.y), hmul2u(hc.z, pc.z), hmul2u(hc.w, pc.w));
+        const uint4 wc = *reinterpret_cast<const uint4*>(w2 + c * 4);
+        *reinterpret_cast<uint4*>(aB + swz(pos, c * 8, D)) =
+            make_uint4(hmul2u(hmul2u(hc.x, pc.x), wc.x), hmul2u(hmul2u(hc.y, pc.y), wc.y),
+                       hmul2u(hmul2u(hc.z, pc.z), wc.z), hmul2u(hmul2u(hc.w, pc.w), wc.w));
       }
     }
-    // load C_s, build A_s and the selection flags
-    for (int idx = tid; idx < D * D / 8; idx += NQ) {
-      const int r = idx / (D / 8), c = idx % (D / 8);
-      cp_async16(sC + swz(r, c * 8, D), cb + (long long)sf * D * D + r * D + c * 8, true);
-    }
-    cp_commit();
-    bool sel = false;
-    if (live)
-      for (int m = 0; m < M; ++m) sel |= (selS[q * M + m] == sf);
-    selq[q] = sel;
+    if (tid >= ns && tid < npad) {  // padding rows: A = 0, any valid query row for gn
+      rowS[tid] = 0;
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      uint4 o = make_uint4(0, 0, 0, 0);
-      if (sel) {
-        const uint4 hc = *reinterpret_cast<const uint4*>(hvB + swz(q, c * 8, D));
-        const uint4 wc = *reinterpret_cast<const uint4*>(sw2 + (sf * D + c * 8) / 2);
-        o = make_uint4(hmul2u(hc.x, wc.x), hmul2u(hc.y, wc.y), hmul2u(hc.z, wc.z), hmul2u(hc.w, wc.w));
-      }
-      *reinterpret_cast<uint4*>(aB + swz(q, c * 8, D)) = o;
+      for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(aB + swz(tid, c * 8, D)) = make_uint4(0, 0, 0, 0);
     }
-    cp_wait<0>();
+    if (CB == 2) cp_wait<1>();
+    else cp_wait<0>();
     __syncthreads();
-    // dA = gn . C_s^T  (rows: queries of this warp, cols: d)
-    float da[2][NTL][4];
+    // ---- phase 3a: dA = gn . C_s^T over the compacted rows, 16 per block; elementwise
+    const uint32_t cbuf = sC + buf * D * D * 2;
+    uint32_t wv[NTL], pv[NTL];  // w_s and pw[pg] pairs of this lane's channels
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-      for (int j = 0; j < NTL; ++j) da[mi][j][0] = da[mi][j][1] = da[mi][j][2] = da[mi][j][3] = 0.f;
-#pragma unroll
-    for (int kt = 0; kt < D / 16; ++kt) {
-      uint32_t af[2][4];
-#pragma unroll
-      for (int mi = 0; mi < 2; ++mi) {
-        const int r = warp * 32 + mi * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = kt * 16 + (lane >> 4) * 8;
-        ldsm_x4(sG + swz(r, c, D), af[mi][0], af[mi][1], af[mi][2], af[mi][3]);
-      }
-#pragma unroll
-      for (int np = 0; np < D / 16; ++np) {
-        uint32_t b0, b1, b2, b3;
-        const int r = np * 16 + (lane & 7) + (lane >> 4) * 8;
-        const int c = kt * 16 + ((lane >> 3) & 1) * 8;
-        ldsm_x4(sC + swz(r, c, D), b0, b1, b2, b3);
-#pragma unroll
-        for (int mi = 0; mi < 2; ++mi) {
-          mma16816(da[mi][2 * np], af[mi], b0, b1);
-          mma16816(da[mi][2 * np + 1], af[mi], b2, b3);
-        }
-      }
+    for (int j = 0; j < NTL; ++j) {
+      wv[j] = w2[(j * 8 + c4 * 2) / 2];
+      pv[j] = pw2[(pg * D + j * 8 + c4 * 2) / 2];
     }
     float wpart[NTL][2];
 #pragma unroll
     for (int j = 0; j < NTL; ++j) wpart[j][0] = wpart[j][1] = 0.f;
+    for (int mt = warp; mt < npad / 16; mt += NW) {
+      float da[NTL][4];
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+      for (int j = 0; j < NTL; ++j) da[j][0] = da[j][1] = da[j][2] = da[j][3] = 0.f;
+      const int arow = rowS[mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8];
 #pragma unroll
-      for (int xp = 0; xp < 2; ++xp) {
-        const int r = warp * 32 + mi * 16 + g + xp * 8;
-        if (!selq[r]) continue;
+      for (int kt = 0; kt < D / 16; ++kt) {
+        uint32_t af[4];
+        ldsm_x4(sG + swz(arow, kt * 16 + (lane >> 4) * 8, D), af[0], af[1], af[2], af[3]);
+#pragma unroll
+        for (int np = 0; np < D / 16; ++np) {
+          uint32_t b0, b1, b2, b3;
+          const int r = np * 16 + (lane & 7) + (lane >> 4) * 8;
+          const int c = kt * 16 + ((lane >> 3) & 1) * 8;
+          ldsm_x4(cbuf + swz(r, c, D), b0, b1, b2, b3);
+          mma16816(da[2 * np], af, b0, b1);
+          mma16816(da[2 * np + 1], af, b2, b3);
+        }
+      }
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int ci = mt * 16 + g + hr * 8;
+        if (ci >= ns) continue;
+        const int r = rowS[ci];
         const float gdv = gdS[r];
+        float2 acc[NTL];
+        uint32_t hp[NTL];
+#pragma unroll
+        for (int j = 0; j < NTL; ++j) {  // all loads before the stores
+          const int d = j * 8 + c4 * 2;
+          acc[j] = *reinterpret_cast<const float2*>(dhvS + dhv_off<D>(r, d));
+          hp[j] = pair_at(hB, r, d);
+        }
 #pragma unroll
         for (int j = 0; j < NTL; ++j) {
-          const int d = j * 8 + c4 * 2;
           // dA = bf16(bf16(gn . C^T) + gd), a pair of channels
-          const uint32_t dav = wa::pack_bf16(__fadd_rn(rb(da[mi][j][2 * xp]), gdv),
-                                             __fadd_rn(rb(da[mi][j][2 * xp + 1]), gdv));
-          const uint32_t pw_ = hmul2u(dav, sw2[(sf * D + d) / 2]);
-          const uint32_t ph = hmul2u(dav, pair_at(hvB, r, d));
-          dhv[mi][j][2 * xp] += lo_f(pw_);
-          dhv[mi][j][2 * xp + 1] += hi_f(pw_);
+          const uint32_t dav = wa::pack_bf16(__fadd_rn(rb(da[j][2 * hr]), gdv), __fadd_rn(rb(da[j][2 * hr + 1]), gdv));
+          const uint32_t pw_ = hmul2u(dav, wv[j]);
+          const uint32_t ph = hmul2u(dav, hmul2u(hp[j], pv[j]));  // hv = bf16(h * pw)
+          acc[j].x += lo_f(pw_);
+          acc[j].y += hi_f(pw_);
           wpart[j][0] += lo_f(ph);
           wpart[j][1] += hi_f(ph);
         }
+#pragma unroll
+        for (int j = 0; j < NTL; ++j) *reinterpret_cast<float2*>(dhvS + dhv_off<D>(r, j * 8 + c4 * 2)) = acc[j];
       }
+    }
 #pragma unroll
     for (int j = 0; j < NTL; ++j)
 #pragma unroll
@@ -730,9 +827,10 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
         v += __shfl_xor_sync(0xffffffffu, v, 16);
         if (g == 0) dwS[warp * D + j * 8 + c4 * 2 + x] = v;  // summed over warps after the barrier
       }
-    // dC_s = A_s^T . gn : output [d][e]; warps tile (m-tiles of d rows) x (n ranges)
+    // ---- phase 3b: dC_s = A_s^T . gn over the compacted rows : output [d][e];
+    // warps tile (m-tiles of d rows) x (n ranges)
     {
-      constexpr int NW = NQ / 32, MTILES = D / 16;
+      constexpr int MTILES = D / 16;
       constexpr int WPM = NW >= MTILES ? NW / MTILES : 1;   // warps per m-tile
       constexpr int MPW = NW >= MTILES ? 1 : MTILES / NW;   // m-tiles per warp
       constexpr int NPW = (D / 8) / WPM;                    // n-tiles per warp
@@ -745,17 +843,17 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
         float dc[NPW][4];
 #pragma unroll
         for (int j = 0; j < NPW; ++j) dc[j][0] = dc[j][1] = dc[j][2] = dc[j][3] = 0.f;
-        for (int kt = 0; kt < NQ / 16; ++kt) {
+        for (int kt = 0; kt < npad / 16; ++kt) {
           uint32_t af[4];
           const int r = kt * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
           const int c = mt * 16 + ((lane >> 3) & 1) * 8;
           ldsm_x4_t(sA + swz(r, c, D), af[0], af[1], af[2], af[3]);
+          const int grow = rowS[kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8];
 #pragma unroll
           for (int np = 0; np < NPW / 2; ++np) {
             uint32_t b0, b1, b2, b3;
-            const int rr = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
             const int cc = (n0 + 2 * np) * 8 + (lane >> 4) * 8;
-            ldsm_x4_t(sG + swz(rr, cc, D), b0, b1, b2, b3);
+            ldsm_x4_t(sG + swz(grow, cc, D), b0, b1, b2, b3);
             mma16816(dc[2 * np], af, b0, b1);
             mma16816(dc[2 * np + 1], af, b2, b3);
           }
@@ -775,59 +873,63 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NQ) read_bwd_kernel(BwdArgs a)
       }
     }
     __syncthreads();
-    // dw_s -> d(z - pz) = bf16(bf16(dw) * w) : dz[s] += ., d page_z[pg] -= .
-    for (int d = tid; d < D; d += NQ) {
+    // ---- phase 4: dw_s -> d(z - pz) = bf16(bf16(dw) * w) : dz[s] += ., d page_z[pg] -= .
+    for (int d = tid; d < D; d += NT) {
       float dw = 0.f;
 #pragma unroll
-      for (int w = 0; w < NQ / 32; ++w) dw += dwS[w * D + d];
-      const float ddiff = rb(__fmul_rn(rb(dw), bf(swS[sf * D + d])));
+      for (int w = 0; w < NW; ++w) dw += dwS[w * D + d];
+      const float ddiff = rb(__fmul_rn(rb(dw), bf(wS[d])));
       atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d, ddiff);
       dpzS[pg * D + d] -= ddiff;
     }
-    __syncthreads();
   }
   if (cur_page >= 0) flush_page(cur_page);
   __syncthreads();
   // ---- softmax backward of h -> d raw_q = bf16(fusion part + this part)
 #pragma unroll
-  for (int mi = 0; mi < 2; ++mi)
+  for (int rr = 0; rr < 2 * MI; ++rr) {
+    const int mi = rr >> 1, hr = rr & 1;
+    const int r = (warp * MI + mi) * 16 + g + hr * 8;
+    float dot = 0.f;
 #pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      const int r = warp * 32 + mi * 16 + g + hr * 8;
-      float dot = 0.f;
+    for (int j = 0; j < NTL; ++j)
 #pragma unroll
-      for (int j = 0; j < NTL; ++j)
+      for (int x = 0; x < 2; ++x) dot += hval(r, j * 8 + c4 * 2 + x) * rb(dh[mi][j][hr * 2 + x]);
+    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+    dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+    if (r >= nq) continue;
+    const long long base = ((long long)b * a.dm.T + q0 + r) * row + hoff;
+    __nv_bfloat162 fpart[NTL];
 #pragma unroll
-        for (int x = 0; x < 2; ++x) dot += hval(r, j * 8 + c4 * 2 + x) * rb(dh[mi][j][hr * 2 + x]);
-      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
-      if (r >= nq) continue;
-      const long long base = ((long long)b * a.dm.T + q0 + r) * row + hoff;
+    for (int j = 0; j < NTL; ++j)
+      fpart[j] = __ldg(reinterpret_cast<const __nv_bfloat162*>(a.d_rq_f + base + j * 8 + c4 * 2));
 #pragma unroll
-      for (int j = 0; j < NTL; ++j) {
-        const int d = j * 8 + c4 * 2;
-        float o2[2];
+    for (int j = 0; j < NTL; ++j) {
+      const int d = j * 8 + c4 * 2;
+      const float2 fp = __bfloat1622float2(fpart[j]);
+      float o2[2];
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float hv = hval(r, d + x);
-          const float drq = rb(hv * (rb(dh[mi][j][hr * 2 + x]) - dot));
-          o2[x] = rb(__fadd_rn(bf(a.d_rq_f[base + d + x]), drq));
-        }
-        *reinterpret_cast<__nv_bfloat162*>(a.d_raw_q + base + d) = __floats2bfloat162_rn(o2[0], o2[1]);
+      for (int x = 0; x < 2; ++x) {
+        const float hv = hval(r, d + x);
+        const float drq = rb(hv * (rb(dh[mi][j][hr * 2 + x]) - dot));
+        o2[x] = rb(__fadd_rn(x ? fp.y : fp.x, drq));
       }
+      *reinterpret_cast<__nv_bfloat162*>(a.d_raw_q + base + d) = __floats2bfloat162_rn(o2[0], o2[1]);
     }
+  }
   // ---- page weights softmax backward, then logsumexp backward of page_z -> dz
-  for (int d = tid; d < D; d += NQ) {
+  for (int d = tid; d < D; d += NT) {
     float dot = 0.f;
     for (int pg = 0; pg < P; ++pg) dot += pwS[pg * D + d] * rb(dpwS[pg * D + d]);
     for (int pg = 0; pg < P; ++pg)
       dpzS[pg * D + d] += rb(pwS[pg * D + d] * (rb(dpwS[pg * D + d]) - dot));
   }
   __syncthreads();
-  for (int idx = tid; idx < V * D; idx += NQ) {
+#pragma unroll 4
+  for (int idx = tid; idx < V * D; idx += NT) {
     const int sf = idx / D, d = idx % D, pg = sf / kGroup;
     const float lse = pzS[pg * D + d];
-    const float w = rb(expf(rb(__fsub_rn(bf(zb[(long long)sf * D + d]), lse))));
+    const float w = rb(expf(rb(__fsub_rn(bf(__ldg(zb + (long long)sf * D + d)), lse))));
     atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d,
               rb(__fmul_rn(rb(dpzS[pg * D + d]), w)));
   }
