@@ -31,73 +31,166 @@ struct BwdArgs {
 };
 
 // ---------------------------------------------------------------------------
-// Fusion backward: one warp per (token, head) row, lanes over channels; each warp
-// takes kFusionRowsPerWarp consecutive tokens, a CTA 8 warps.
+// Fusion backward: one warp per (token, head) row, each lane a pair of adjacent
+// channels (64p + 2*lane, +1), so every bf16 rounding point rounds both with one
+// packed conversion; each warp takes kFusionRowsPerWarp consecutive tokens (the
+// next row's inputs are loaded while the current one is processed), a CTA 8 warps.
 // ---------------------------------------------------------------------------
 constexpr int kFusionRowsPerWarp = 16;
+
+// both values rounded to bf16 (one cvt.rn.bf16x2.f32)
+TAO_DEVI void rb2(float& x, float& y) {
+  const uint32_t u = wa::pack_bf16(x, y);
+  x = lo_f(u);
+  y = hi_f(u);
+}
+// bf16 pair of two values that are already bf16-representable (no rounding)
+TAO_DEVI uint32_t pack_exact(float x, float y) {
+  return (__float_as_uint(x) >> 16) | (__float_as_uint(y) & 0xffff0000u);
+}
+
 template <int D>
 __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
-  constexpr int PER = D / 32;
+  constexpr int NP = D / 64;
   const int tile = blockIdx.x, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float gain = a.gain[h];
-  float acc_fa[PER][3], acc_fb[PER][3];
+  float acc_fa[NP][2][3], acc_fb[NP][2][3], fa[NP][2][3], fb[NP][2][3];
 #pragma unroll
-  for (int j = 0; j < PER; ++j)
+  for (int p = 0; p < NP; ++p)
 #pragma unroll
-    for (int x = 0; x < 3; ++x) acc_fa[j][x] = acc_fb[j][x] = 0.f;
-  float fa[PER][3], fb[PER][3];
+    for (int k = 0; k < 2; ++k)
 #pragma unroll
-  for (int j = 0; j < PER; ++j)
-#pragma unroll
-    for (int x = 0; x < 3; ++x) {
-      fa[j][x] = bf(a.fa[((long long)h * D + lane + 32 * j) * 3 + x]);
-      fb[j][x] = bf(a.fb[((long long)h * D + lane + 32 * j) * 3 + x]);
-    }
-  for (int rr = 0; rr < kFusionRowsPerWarp; ++rr) {
-    const int t = tile * 8 * kFusionRowsPerWarp + warp * kFusionRowsPerWarp + rr;
-    if (t >= a.dm.T) break;
-    const long long base = ((long long)b * a.dm.T + t) * a.dm.row + (long long)h * D;
+      for (int x = 0; x < 3; ++x) {
+        const long long i = ((long long)h * D + 64 * p + 2 * lane + k) * 3 + x;
+        acc_fa[p][k][x] = acc_fb[p][k][x] = 0.f;
+        fa[p][k][x] = bf(a.fa[i]);
+        fb[p][k][x] = bf(a.fb[i]);
+      }
+  const int t0 = tile * 8 * kFusionRowsPerWarp + warp * kFusionRowsPerWarp;
+  const int rows = min(kFusionRowsPerWarp, a.dm.T - t0);
+  // row inputs (read-only in this kernel): g, local, raw_q, num pairs and den
+  uint32_t cg[NP], cl[NP], cq[NP], cn[NP];
+  float cden = 1.f;
+  auto load_row = [&](int t, uint32_t (&g2)[NP], uint32_t (&l2)[NP], uint32_t (&q2)[NP], uint32_t (&n2)[NP],
+                      float& den) {
+    const long long base = ((long long)b * a.dm.T + t) * a.dm.row + (long long)h * D + 2 * lane;
     const bool present = t >= kWindow;
-    const float den = present ? a.den[((long long)b * a.dm.T + t) * a.dm.H + h] : 1.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      g2[p] = __ldg(reinterpret_cast<const unsigned int*>(a.g + base + 64 * p));
+      l2[p] = __ldg(reinterpret_cast<const unsigned int*>(a.local + base + 64 * p));
+      q2[p] = present ? __ldg(reinterpret_cast<const unsigned int*>(a.raw_q + base + 64 * p)) : 0u;
+      n2[p] = present ? __ldg(reinterpret_cast<const unsigned int*>(a.num + base + 64 * p)) : 0u;
+    }
+    den = present ? __ldg(a.den + ((long long)b * a.dm.T + t) * a.dm.H + h) : 1.f;
+  };
+  if (rows > 0) load_row(t0, cg, cl, cq, cn, cden);
+  for (int rr = 0; rr < rows; ++rr) {
+    const int t = t0 + rr;
+    uint32_t ng[NP], nl[NP], nq[NP], nn[NP];
+    float nden = 1.f;
+    if (rr + 1 < rows) load_row(t + 1, ng, nl, nq, nn, nden);
+    const long long base = ((long long)b * a.dm.T + t) * a.dm.row + (long long)h * D + 2 * lane;
+    const bool present = t >= kWindow;
+    const float den = cden;
     float rowdot = 0.f, dden = 0.f;
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      const int d = lane + 32 * j;
-      const float gv = bf(a.g[base + d]);
-      const float loc = bf(a.local[base + d]);
-      float dloc = gv, dnum = 0.f, drq = 0.f;
+    for (int p = 0; p < NP; ++p) {
+      const float gv[2] = {lo_f(cg[p]), hi_f(cg[p])}, loc[2] = {lo_f(cl[p]), hi_f(cl[p])};
+      float dloc[2] = {gv[0], gv[1]}, dnum[2] = {0.f, 0.f}, drq[2] = {0.f, 0.f};
       if (present) {
-        const float qv = bf(a.raw_q[base + d]);
-        const float num = bf(a.num[base + d]);
-        const float fine = rb(__fdiv_rn(num, den));
-        const float base0 = rb(__fadd_rn(rb(__fmul_rn(fa[j][0], qv)), fb[j][0]));
-        const float s0 = rb(__fadd_rn(base0, 0.f));
-        const float s2 = rb(__fadd_rn(rb(__fmul_rn(fa[j][2], qv)), fb[j][2]));
-        const float mx = fmaxf(s0, s2);
-        // the larger term is exp(0) = 1 exactly: one exponential per element
-        const float eo = expf(fminf(s0, s2) - mx);
-        const float e0 = s0 >= s2 ? 1.f : eo, e2 = s0 >= s2 ? eo : 1.f;
-        const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
-        const float l2 = rb(__fmul_rn(2.f, loc)), fg = rb(__fmul_rn(gain, fine));
-        const float drho0 = rb(__fmul_rn(gv, l2)), drho2 = rb(__fmul_rn(gv, fg));
-        dloc = rb(__fmul_rn(2.f, rb(__fmul_rn(gv, rho0))));
-        const float dfine = rb(__fmul_rn(rb(__fmul_rn(gv, rho2)), gain));
-        const float dot = drho0 * rho0 + drho2 * rho2;
-        const float ds0 = rb(rho0 * (drho0 - dot)), ds2 = rb(rho2 * (drho2 - dot));
-        acc_fb[j][0] += ds0;
-        acc_fb[j][2] += ds2;
-        acc_fa[j][0] += rb(__fmul_rn(ds0, qv));
-        acc_fa[j][2] += rb(__fmul_rn(ds2, qv));
-        drq = rb(rb(__fmul_rn(ds0, fa[j][0])) + rb(__fmul_rn(ds2, fa[j][2])));
-        dnum = rb(__fdiv_rn(dfine, den));
-        const float t2 = rb(__fdiv_rn(fine, den));
-        dden += rb(-__fmul_rn(dfine, t2));
+        const float qv[2] = {lo_f(cq[p]), hi_f(cq[p])};
+        float fine[2], s0[2], s2[2], rho0[2], rho2[2], fg[2], drho0[2], drho2[2], t1[2], dfine[2];
+        float ds0[2], ds2[2], fa0[2], fa2[2], x0[2], x1[2], dn[2], t2[2], dd[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) fine[k] = __fdiv_rn(k ? hi_f(cn[p]) : lo_f(cn[p]), den);
+        rb2(fine[0], fine[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          s0[k] = __fmul_rn(fa[p][k][0], qv[k]);
+          s2[k] = __fmul_rn(fa[p][k][2], qv[k]);
+        }
+        rb2(s0[0], s0[1]);
+        rb2(s2[0], s2[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          s0[k] = __fadd_rn(s0[k], fb[p][k][0]);  // base0; + 0 (the absent middle term) is exact
+          s2[k] = __fadd_rn(s2[k], fb[p][k][2]);
+        }
+        rb2(s0[0], s0[1]);
+        rb2(s2[0], s2[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const float mx = fmaxf(s0[k], s2[k]);
+          // the larger term is exp(0) = 1 exactly: one exponential per element
+          const float eo = expf(fminf(s0[k], s2[k]) - mx);
+          const float e0 = s0[k] >= s2[k] ? 1.f : eo, e2 = s0[k] >= s2[k] ? eo : 1.f;
+          rho0[k] = __fdiv_rn(e0, e0 + e2);
+          rho2[k] = __fdiv_rn(e2, e0 + e2);
+        }
+        rb2(rho0[0], rho0[1]);
+        rb2(rho2[0], rho2[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          fg[k] = __fmul_rn(gain, fine[k]);
+          drho0[k] = __fmul_rn(gv[k], __fmul_rn(2.f, loc[k]));  // bf16(2 * local) = 2 * local
+          t1[k] = __fmul_rn(gv[k], rho0[k]);
+          dfine[k] = __fmul_rn(gv[k], rho2[k]);
+        }
+        rb2(fg[0], fg[1]);
+        rb2(drho0[0], drho0[1]);
+        rb2(t1[0], t1[1]);
+        rb2(dfine[0], dfine[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          drho2[k] = __fmul_rn(gv[k], fg[k]);
+          dloc[k] = __fmul_rn(2.f, t1[k]);  // exact
+          dfine[k] = __fmul_rn(dfine[k], gain);
+        }
+        rb2(drho2[0], drho2[1]);
+        rb2(dfine[0], dfine[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const float dot = drho0[k] * rho0[k] + drho2[k] * rho2[k];
+          ds0[k] = rho0[k] * (drho0[k] - dot);
+          ds2[k] = rho2[k] * (drho2[k] - dot);
+        }
+        rb2(ds0[0], ds0[1]);
+        rb2(ds2[0], ds2[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          acc_fb[p][k][0] += ds0[k];
+          acc_fb[p][k][2] += ds2[k];
+          fa0[k] = __fmul_rn(ds0[k], qv[k]);
+          fa2[k] = __fmul_rn(ds2[k], qv[k]);
+          x0[k] = __fmul_rn(ds0[k], fa[p][k][0]);
+          x1[k] = __fmul_rn(ds2[k], fa[p][k][2]);
+          dn[k] = __fdiv_rn(dfine[k], den);
+          t2[k] = __fdiv_rn(fine[k], den);
+        }
+        rb2(fa0[0], fa0[1]);
+        rb2(fa2[0], fa2[1]);
+        rb2(x0[0], x0[1]);
+        rb2(x1[0], x1[1]);
+        rb2(dn[0], dn[1]);
+        rb2(t2[0], t2[1]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          acc_fa[p][k][0] += fa0[k];
+          acc_fa[p][k][2] += fa2[k];
+          drq[k] = x0[k] + x1[k];
+          dnum[k] = dn[k];
+          dd[k] = -__fmul_rn(dfine[k], t2[k]);
+        }
+        rb2(drq[0], drq[1]);
+        rb2(dd[0], dd[1]);
+        dden += dd[0] + dd[1];
       }
-      a.d_local[base + d] = tobf(dloc);
-      a.gn[base + d] = tobf(dnum);
-      a.d_rq_f[base + d] = tobf(drq);
-      rowdot += dloc * loc;
+      *reinterpret_cast<uint32_t*>(a.d_local + base + 64 * p) = pack_exact(dloc[0], dloc[1]);
+      *reinterpret_cast<uint32_t*>(a.gn + base + 64 * p) = pack_exact(dnum[0], dnum[1]);
+      *reinterpret_cast<uint32_t*>(a.d_rq_f + base + 64 * p) = pack_exact(drq[0], drq[1]);
+      rowdot += dloc[0] * loc[0] + dloc[1] * loc[1];
     }
     rowdot = warp_sum(rowdot);
     dden = warp_sum(dden);
@@ -105,16 +198,26 @@ __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
       a.gd[((long long)b * a.dm.T + t) * a.dm.H + h] = rb(dden);
       a.dv_row[((long long)b * a.dm.H + h) * a.dm.T + t] = rowdot;
     }
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      cg[p] = ng[p];
+      cl[p] = nl[p];
+      cq[p] = nq[p];
+      cn[p] = nn[p];
+    }
+    cden = nden;
   }
   // block reduction of the fusion parameter gradients, one atomic per value per CTA
   __shared__ float red[8][D][6];
 #pragma unroll
-  for (int j = 0; j < PER; ++j)
+  for (int p = 0; p < NP; ++p)
 #pragma unroll
-    for (int x = 0; x < 3; ++x) {
-      red[warp][lane + 32 * j][x] = acc_fa[j][x];
-      red[warp][lane + 32 * j][3 + x] = acc_fb[j][x];
-    }
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+      for (int x = 0; x < 3; ++x) {
+        red[warp][64 * p + 2 * lane + k][x] = acc_fa[p][k][x];
+        red[warp][64 * p + 2 * lane + k][3 + x] = acc_fb[p][k][x];
+      }
   __syncthreads();
   for (int idx = threadIdx.x; idx < D * 6; idx += 256) {
     const int d = idx / 6, x = idx % 6;
@@ -1004,13 +1107,24 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
     cp_async16(sV + swz(r, c * 8, D), vb + (long long)r * row + c * 8, true);
   }
   cp_commit();
-  for (int idx = tid; idx < D * D; idx += 256) {
-    const int r = idx / D, c = idx % D;
-    // a caller-supplied C (another fine writer) takes its dC elsewhere: z path only
-    *reinterpret_cast<bf16*>(dB + swz(r, c, D)) = a.caller_c ? tobf(0.f) : tobf(dcb[idx]);
+  {
+    // dC (fp32) -> bf16 tile; all read-only loads issued before the stores.  A
+    // caller-supplied C (another fine writer) takes its dC elsewhere: z path only.
+    constexpr int NV = D * D / 4 / 256;
+    float4 cv[NV];
+#pragma unroll
+    for (int it = 0; it < NV; ++it)
+      cv[it] = a.caller_c ? make_float4(0.f, 0.f, 0.f, 0.f)
+                          : __ldg(reinterpret_cast<const float4*>(dcb) + tid + it * 256);
+#pragma unroll
+    for (int it = 0; it < NV; ++it) {
+      const int e0 = (tid + it * 256) * 4, r = e0 / D, c = e0 % D;
+      *reinterpret_cast<uint2*>(dB + swz(r, c, D)) =
+          make_uint2(wa::pack_bf16(cv[it].x, cv[it].y), wa::pack_bf16(cv[it].z, cv[it].w));
+    }
   }
   for (int d = tid; d < D; d += 256) {
-    dzS[d] = rb(a.dz[(((long long)b * a.dm.H + h) * a.dm.S + s) * D + d]);
+    dzS[d] = rb(__ldg(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + s) * D + d));
     dZp[d] = 0.f;
     dmS[d] = 0.f;
   }
@@ -1072,18 +1186,26 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
       }
     }
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int mi = 0; mi < 2; ++mi) {
+      // dv += dv_w: this CTA's own rows; the 2 x NTL loads go out before the stores
+      __nv_bfloat162 old[2][NTL];
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr)
+#pragma unroll
+        for (int j = 0; j < NTL; ++j)
+          old[hr][j] = *reinterpret_cast<const __nv_bfloat162*>(
+              dvb + (long long)(warp * 32 + mi * 16 + g + hr * 8) * row + j * 8 + c4 * 2);
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
         const int t = warp * 32 + mi * 16 + g + hr * 8;
 #pragma unroll
         for (int j = 0; j < NTL; ++j) {
-          const int d = j * 8 + c4 * 2;
-          __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(dvb + (long long)t * row + d);
-          const float2 old = __bfloat1622float2(*dst);
-          *dst = __floats2bfloat162_rn(rb(old.x + rb(dvw[mi][j][hr * 2])), rb(old.y + rb(dvw[mi][j][hr * 2 + 1])));
+          const float2 o = __bfloat1622float2(old[hr][j]);
+          *reinterpret_cast<__nv_bfloat162*>(dvb + (long long)t * row + j * 8 + c4 * 2) =
+              __floats2bfloat162_rn(rb(o.x + rb(dvw[mi][j][hr * 2])), rb(o.y + rb(dvw[mi][j][hr * 2 + 1])));
         }
       }
+    }
   }
   // ---- pass 2: dprob = V . dC^T
   float dp[2][NTL][4];
@@ -1164,19 +1286,21 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
       const int t = warp * 32 + mi * 16 + g + hr * 8;
+      uint32_t kp[NTL];  // e pairs (width 64) or raw key pairs, loaded before the stores below
+#pragma unroll
+      for (int j = 0; j < NTL; ++j)
+        kp[j] = kStoreE ? *reinterpret_cast<const uint32_t*>(eB + swz(t, j * 8 + c4 * 2, D))
+                        : __ldg(reinterpret_cast<const unsigned int*>(kb + (long long)t * row + j * 8 + c4 * 2));
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {
         const int d = j * 8 + c4 * 2;
         float ev[2];
         if (kStoreE) {
-          const uint32_t e2 = *reinterpret_cast<const uint32_t*>(eB + swz(t, d, D));
-          ev[0] = lo_f(e2);
-          ev[1] = hi_f(e2);
+          ev[0] = lo_f(kp[j]);
+          ev[1] = hi_f(kp[j]);
         } else {
-#pragma unroll
-          for (int x = 0; x < 2; ++x)
-            ev[x] = rb(expf(rb(__fsub_rn(bf(*reinterpret_cast<const bf16*>(kb + (long long)t * row + d + x)),
-                                         mx[d + x]))));
+          ev[0] = rb(expf(rb(__fsub_rn(lo_f(kp[j]), mx[d]))));
+          ev[1] = rb(expf(rb(__fsub_rn(hi_f(kp[j]), mx[d + 1]))));
         }
         float o2[2];
 #pragma unroll
