@@ -38,17 +38,6 @@ struct BwdArgs {
 // ---------------------------------------------------------------------------
 constexpr int kFusionRowsPerWarp = 16;
 
-// both values rounded to bf16 (one cvt.rn.bf16x2.f32)
-TAO_DEVI void rb2(float& x, float& y) {
-  const uint32_t u = wa::pack_bf16(x, y);
-  x = lo_f(u);
-  y = hi_f(u);
-}
-// bf16 pair of two values that are already bf16-representable (no rounding)
-TAO_DEVI uint32_t pack_exact(float x, float y) {
-  return (__float_as_uint(x) >> 16) | (__float_as_uint(y) & 0xffff0000u);
-}
-
 template <int D>
 __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
   constexpr int NP = D / 64;

@@ -174,6 +174,17 @@ __global__ void page_prefix_kernel(const bf16* __restrict__ z, bf16* pzpre, Trai
 //  4. epilogue: num = bf16(acc), fine = bf16(num/den), pointwise fusion -> out.
 // Tiles without history (t < 3) copy the local output.
 // ---------------------------------------------------------------------------
+// both values rounded to bf16 (one cvt.rn.bf16x2.f32)
+TAO_DEVI void rb2(float& x, float& y) {
+  const uint32_t u = wa::pack_bf16(x, y);
+  x = lo_f(u);
+  y = hi_f(u);
+}
+// bf16 pair of two values that are already bf16-representable (no rounding)
+TAO_DEVI uint32_t pack_exact(float x, float y) {
+  return (__float_as_uint(x) >> 16) | (__float_as_uint(y) & 0xffff0000u);
+}
+
 struct ReadArgs {
   const bf16 *raw_q, *local, *fa, *fb;  // [B,T,H,D] x2, [H,D,3] x2
   const float* gain;                     // [H] bf16(2*alpha_h) as float
@@ -200,6 +211,7 @@ struct ReadSmem {
     s += 256 * (size_t)(mmax + 1) * 4;  // top scores
     s += 256 * (size_t)(mmax + 1) * 4;  // top ids
     s += 256 * 4 + (size_t)(V + 8) * 4 * 2 + 256;   // den, use flags + list, misc
+    s += (size_t)(V + 31) / 32 * 256 * 4;          // selection bits [word][query]
     return s;
   }
 };
@@ -245,6 +257,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   float* topS = reinterpret_cast<float*>(ptr); ptr += 256 * (size_t)(a.mmax + 1) * 4;
   int* topI = reinterpret_cast<int*>(ptr);     ptr += 256 * (size_t)(a.mmax + 1) * 4;
   float* denS = reinterpret_cast<float*>(ptr); ptr += 256 * 4;
+  uint32_t* selB = reinterpret_cast<uint32_t*>(ptr); ptr += (size_t)(V + 31) / 32 * 256 * 4;
   int* useS = reinterpret_cast<int*>(ptr);
   const int TS = a.mmax + 1;  // row stride of the top lists (odd-ish: fewer bank conflicts)
 
@@ -253,7 +266,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   for (int idx = tid; idx < P * D; idx += 256) {
     const int p = idx / D, d = idx % D;
     const int n = (p < completed) ? kGroup : pending;
-    pzS[idx] = bf(pzb[((long long)p * kGroup + (n - 1)) * D + d]);
+    pzS[idx] = bf(__ldg(pzb + ((long long)p * kGroup + (n - 1)) * D + d));
   }
   for (int i = tid; i < V; i += 256) useS[i] = 0;
   __syncthreads();
@@ -265,9 +278,10 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
     for (int p = 0; p < P; ++p) pw2S[p * D + d] = tobf(__fdiv_rn(expf(pzS[p * D + d] - mx), sum));
   }
   const bf16* zb = a.z + ((long long)b * a.dm.H + h) * a.dm.S * D;
+#pragma unroll 4
   for (int idx = tid; idx < V * D; idx += 256) {
     const int s = idx / D, d = idx % D;
-    swS[idx] = tobf(expf(rb(__fsub_rn(bf(zb[(long long)s * D + d]), pzS[(s / kGroup) * D + d]))));
+    swS[idx] = tobf(expf(rb(__fsub_rn(bf(__ldg(zb + (long long)s * D + d)), pzS[(s / kGroup) * D + d]))));
   }
   // ---- h = bf16(softmax(raw_q)) per query, stored swizzled
   const int q = tid;
@@ -356,7 +370,9 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
       }
       chosen |= 1ull << bp;
     }
+    float thr = -INFINITY;  // score of the M-th entry once the list is full
     auto consider = [&](int id, float sc) {
+      if (nt == M && sc <= thr) return;   // equal scores keep the older id: rejected
       int pos = 0;
       while (pos < nt && tS[pos] >= sc) ++pos;   // stable: equal scores keep the older id first
       if (pos >= M) return;
@@ -365,6 +381,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
       tS[pos] = sc;
       tI[pos] = id;
       if (nt < M) ++nt;
+      if (nt == M) thr = tS[M - 1];
     };
     // candidate fines of a page: score = bf16(sum_d bf16(hv * w_fine))
     auto page_candidates = [&](int page, int first, int count) {
@@ -396,6 +413,8 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
       useS[tI[m]] = 1;
     }
     denS[q] = rb(den);
+    for (int w = 0; w < (V + 31) / 32; ++w) selB[w * 256 + q] = 0u;
+    for (int m = 0; m < nt; ++m) selB[(tI[m] >> 5) * 256 + q] |= 1u << (tI[m] & 31);
     int16_t* so = a.sel_out + (((long long)b * a.dm.T + q0 + q) * a.dm.H + h) * a.mmax;
     for (int m = 0; m < a.mmax; ++m) so[m] = (int16_t)(m < nt ? tI[m] : -1);
     a.den_out[((long long)b * a.dm.T + q0 + q) * a.dm.H + h] = denS[q];
@@ -434,9 +453,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
     const int buf = (NBUF == 2) ? (i & 1) : 0;
     if (NBUF == 2 && i + 1 < nu) load_c(list[i + 1], buf ^ 1);
     // A_s row q: bf16(hv * w_s) where query q selected fine s2, else zero
-    bool sel = false;
-    if (live)
-      for (int m = 0; m < nt; ++m) sel |= (tI[m] == s2);
+    const bool sel = live && ((selB[(s2 >> 5) * 256 + q] >> (s2 & 31)) & 1u);
     if (sel) {
       uint32_t hv[D / 2];
       page_hv(s2 / kGroup, hv);
@@ -508,32 +525,58 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
       const long long base = ((long long)b * a.dm.T + q0 + r) * row + hoff;
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {
+        // channels e, e + 1: every rounding point rounds the pair with one conversion;
+        // bf16(x + 0) and bf16(2 * local) are exact and not re-rounded
         const int e = j * 8 + c4 * 2;
         const uint32_t q2 = *reinterpret_cast<const uint32_t*>(smem + swz(r, e, D));
         const uint32_t l2 = *reinterpret_cast<const uint32_t*>(smem + 256 * D * 2 + swz(r, e, D));
-        float res[2], nums[2];
+        const float qv[2] = {lo_f(q2), hi_f(q2)}, loc[2] = {lo_f(l2), hi_f(l2)};
+        float nums[2] = {acc[mi][j][hr * 2], acc[mi][j][hr * 2 + 1]};
+        rb2(nums[0], nums[1]);
+        float fine[2], s0[2], s2[2], rho0[2], rho2[2], lt[2], fg[2], res[2];
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          const float num = rb(acc[mi][j][hr * 2 + x]);
-          nums[x] = num;
-          const float fine = rb(__fdiv_rn(num, den));
-          const float qv = x ? hi_f(q2) : lo_f(q2);
-          const float loc = x ? hi_f(l2) : lo_f(l2);
           const float* fa = fabS[0] + (e + x) * 3;
-          const float* fb = fabS[1] + (e + x) * 3;
-          const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(fa[0], qv)), fb[0])), 0.f));
-          const float s2 = rb(__fadd_rn(rb(__fmul_rn(fa[2], qv)), fb[2]));
-          const float mx = fmaxf(s0, s2);
-          // the larger term is exp(0) = 1 exactly: one exponential per element
-          const float eo = expf(fminf(s0, s2) - mx);
-          const float e0 = s0 >= s2 ? 1.f : eo, e2 = s0 >= s2 ? eo : 1.f;
-          const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
-          const float lt = rb(__fmul_rn(rho0, rb(__fmul_rn(2.f, loc))));
-          const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(gain, fine))));
-          res[x] = rb(__fadd_rn(rb(__fadd_rn(lt, 0.f)), ft));
+          fine[x] = __fdiv_rn(nums[x], den);
+          s0[x] = __fmul_rn(fa[0], qv[x]);
+          s2[x] = __fmul_rn(fa[2], qv[x]);
         }
-        *reinterpret_cast<__nv_bfloat162*>(a.out + base + e) = __floats2bfloat162_rn(res[0], res[1]);
-        *reinterpret_cast<__nv_bfloat162*>(a.num_out + base + e) = __floats2bfloat162_rn(nums[0], nums[1]);
+        rb2(fine[0], fine[1]);
+        rb2(s0[0], s0[1]);
+        rb2(s2[0], s2[1]);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float* fb = fabS[1] + (e + x) * 3;
+          s0[x] = __fadd_rn(s0[x], fb[0]);
+          s2[x] = __fadd_rn(s2[x], fb[2]);
+          fg[x] = __fmul_rn(gain, fine[x]);
+        }
+        rb2(s0[0], s0[1]);
+        rb2(s2[0], s2[1]);
+        rb2(fg[0], fg[1]);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float mx = fmaxf(s0[x], s2[x]);
+          // the larger term is exp(0) = 1 exactly: one exponential per element
+          const float eo = expf(fminf(s0[x], s2[x]) - mx);
+          const float e0 = s0[x] >= s2[x] ? 1.f : eo, e2 = s0[x] >= s2[x] ? eo : 1.f;
+          rho0[x] = __fdiv_rn(e0, e0 + e2);
+          rho2[x] = __fdiv_rn(e2, e0 + e2);
+        }
+        rb2(rho0[0], rho0[1]);
+        rb2(rho2[0], rho2[1]);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          lt[x] = __fmul_rn(rho0[x], __fmul_rn(2.f, loc[x]));
+          res[x] = __fmul_rn(rho2[x], fg[x]);
+        }
+        rb2(lt[0], lt[1]);
+        rb2(res[0], res[1]);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) res[x] = __fadd_rn(lt[x], res[x]);
+        rb2(res[0], res[1]);
+        *reinterpret_cast<uint32_t*>(a.out + base + e) = pack_exact(res[0], res[1]);
+        *reinterpret_cast<uint32_t*>(a.num_out + base + e) = pack_exact(nums[0], nums[1]);
       }
     }
   }
