@@ -225,9 +225,18 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
     if (grid < need) grid = need;
     decode_ws_kernel<D><<<grid, 288, smem, s>>>(f);
   } else {
+    // persistent: as many CTAs as are resident at once, each walking items by the grid stride
     const size_t smem = FusedCfg<D>::STAGE;
     if ((rc = set_smem(decode_fused_kernel<D>, smem))) return rc;
-    decode_fused_kernel<D><<<total, 128, smem, s>>>(f);
+    static int resident = 0;
+    if (!resident) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel<D>, 128, smem) != cudaSuccess ||
+          per_sm <= 0)
+        per_sm = 1;
+      resident = per_sm * sms;
+    }
+    decode_fused_kernel<D><<<total < resident ? total : resident, 128, smem, s>>>(f);
   }
   if (g_prof_stop) cudaEventRecord(g_prof_stop, s);
   g_prof_start = g_prof_stop = nullptr;

@@ -47,33 +47,59 @@ TAO_DEVI bool local_block_live(long long t, long long start, int s0, int slots) 
   return dist < count;
 }
 
-// Issue the bulk copies of one item into `stage`; returns the bytes armed (0 = none).
+// Source addresses of one item's bulk copies (resolved ahead of the copy so a CTA
+// can issue its next item the moment its stage is free).
 template <int D>
-TAO_DEVI uint32_t issue_item(const FusedArgs& f, const Item& it, uint8_t* stage, uint64_t* bar) {
+struct ItemCopy {
+  static constexpr int N = FusedCfg<D>::FPC > 2 ? FusedCfg<D>::FPC : 2;
+  const void* src[N];
+  uint32_t bytes;  // per copy
+  int n;           // copies (0: nothing to load)
+};
+
+template <int D>
+TAO_DEVI ItemCopy<D> resolve_item(const FusedArgs& f, const Item& it) {
   using Cfg = FusedCfg<D>;
-  const StepArgs& a = f.s;
-  const TaoState& st = *a.states[it.r];
+  ItemCopy<D> c;
+  c.n = 0;
+  c.bytes = 0;
+  const TaoState& st = *f.s.states[it.r];
   const long long t = st.position;
   if (it.slot < Cfg::KB) {
     const int s0 = it.slot * Cfg::SLOTS;
-    if (!local_block_live<D>(t, window_start(t), s0, Cfg::SLOTS)) return 0;
-    const uint32_t bytes = Cfg::SLOTS * D * 2;
-    mbar_expect_tx(bar, 2 * bytes);
-    bulk_g2s(stage, ring_head<D>(st.k_ring, it.h) + (long long)s0 * D, bytes, bar);
-    bulk_g2s(stage + bytes, ring_head<D>(st.v_ring, it.h) + (long long)s0 * D, bytes, bar);
-    return 2 * bytes;
+    if (!local_block_live<D>(t, window_start(t), s0, Cfg::SLOTS)) return c;
+    c.bytes = Cfg::SLOTS * D * 2;
+    c.n = 2;
+    c.src[0] = ring_head<D>(st.k_ring, it.h) + (long long)s0 * D;
+    c.src[1] = ring_head<D>(st.v_ring, it.h) + (long long)s0 * D;
+    return c;
   }
-  if (t < kWindow) return 0;
+  if (t < kWindow) return c;
   const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
   const int M = st.n_route;
-  if (m0 >= M) return 0;
+  if (m0 >= M) return c;
   const int nf = min(Cfg::FPC, M - m0);
   const int32_t* ids = st.route_ids + (long long)it.h * st.route_cap + m0;
   const bf16* fc = reinterpret_cast<const bf16*>(st.fine_c) + (long long)it.h * st.cap_fines * D * D;
-  const uint32_t bytes = D * D * 2;
-  mbar_expect_tx(bar, nf * bytes);
-  for (int i = 0; i < nf; ++i) bulk_g2s(stage + i * bytes, fc + (long long)ids[i] * D * D, bytes, bar);
-  return nf * bytes;
+  int id[Cfg::FPC];  // all ids first
+#pragma unroll
+  for (int i = 0; i < Cfg::FPC; ++i) id[i] = i < nf ? ids[i] : 0;
+#pragma unroll
+  for (int i = 0; i < Cfg::FPC; ++i) c.src[i] = fc + (long long)id[i] * D * D;
+  c.bytes = D * D * 2;
+  c.n = nf;
+  return c;
+}
+
+// Issue the bulk copies of a resolved item into `stage`; returns the bytes armed.
+template <int D>
+TAO_DEVI uint32_t issue_copy(const ItemCopy<D>& c, uint8_t* stage, uint64_t* bar) {
+  if (c.n == 0) return 0;
+  mbar_expect_tx(bar, c.n * c.bytes);
+#pragma unroll
+  for (int i = 0; i < ItemCopy<D>::N; ++i)
+    if (i < c.n) bulk_g2s(stage + i * c.bytes, c.src[i], c.bytes, bar);
+  return c.n * c.bytes;
 }
 
 // h = bf16(softmax_d(raw_q)) of request r, head h (one warp), into hq[D].
@@ -98,6 +124,12 @@ TAO_DEVI void softmax_row(const bf16* x, float* hq, int lane) {
   for (int j = 0; j < D / 32; ++j) hq[lane + 32 * j] = rb(__fdiv_rn(vals[j], s));
 }
 
+// Persistent form: the grid holds as many CTAs as fit on the GPU at once and each
+// walks the items i = blockIdx.x, + gridDim.x, ...  While an item's copy is in
+// flight, thread 0 resolves the next item's sources; the next copy is issued as
+// soon as the item's compute has released the stage (before its arrival atomic),
+// so a CTA's next load overlaps its own arrival and combine.  The combine reads
+// the partials from L2 and leaves the stage to the copy in flight.
 template <int D>
 __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   using Cfg = FusedCfg<D>;
@@ -105,228 +137,250 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t armed;
+  __shared__ uint32_t armed_s;
   __shared__ int flag;
   __shared__ float qv[D];
   __shared__ float red[128 + 8];
   __shared__ float chs[Cfg::FPC * D];
   __shared__ int last_rh;
   const int per = Cfg::KB + f.ms;
-  const Item it = item_of(blockIdx.x, a.R, a.H);
-  TaoState& st = *a.states[it.r];
-  const long long t = st.position;
+  const int total = a.R * a.H * per;
+  constexpr int kArriver = (D < 128) ? D : 0;  // a thread with no channel in the combine (D = 64)
+  ItemCopy<D> next_copy;
+  next_copy.n = 0;
   if (tid == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
-    armed = issue_item<D>(f, it, dsm, &bar);
+    armed_s = (blockIdx.x < total) ? issue_copy<D>(resolve_item<D>(f, item_of(blockIdx.x, a.R, a.H)), dsm, &bar) : 0u;
   }
-  const long long src = ((long long)it.r * a.H + it.h) * D;
-  if (it.slot < Cfg::KB) {
-    // ------------------------------------------------ local attention block
-    const int s0 = it.slot * Cfg::SLOTS;
-    const float sl = 1.4426950408889634f / sqrtf((float)D);
-    for (int d = tid; d < D; d += 128) qv[d] = bf(a.q[src + d]) * sl;
+  uint32_t phase = 0;
+  for (int i = blockIdx.x; i < total; i += gridDim.x) {
+    const Item it = item_of(i, a.R, a.H);
+    TaoState& st = *a.states[it.r];
+    const long long t = st.position;
+    const int n_route = st.n_route;
+    const int nxt = i + gridDim.x;
     __syncthreads();
-    float* part = a.local_part + (((long long)it.r * a.H + it.h) * Cfg::KB + it.slot) * (D + 2);
-    if (!armed) {
-      if (tid == 0) { part[D] = -INFINITY; part[D + 1] = 0.f; }
-    } else {
-      if (!wait_uniform(&bar, 0, a.err, &flag)) return;
-      bf16* sk = reinterpret_cast<bf16*>(dsm);
-      bf16* sv = sk + Cfg::SLOTS * D;
-      const int tm = (int)(t % kWindow);
-      if (tm >= s0 && tm < s0 + Cfg::SLOTS) {
-        // this block owns the current token's slot: append to the ring, patch smem
-        for (int d = tid; d < D / 8; d += 128) {
-          const uint4 kk = reinterpret_cast<const uint4*>(a.k + src)[d];
-          const uint4 vv = reinterpret_cast<const uint4*>(a.v + src)[d];
-          const uint4 rr = reinterpret_cast<const uint4*>(a.raw_k + src)[d];
-          reinterpret_cast<uint4*>(sk + (tm - s0) * D)[d] = kk;
-          reinterpret_cast<uint4*>(sv + (tm - s0) * D)[d] = vv;
-          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.k_ring) + ((long long)it.h * kWindow + tm) * D)[d] = kk;
-          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.v_ring) + ((long long)it.h * kWindow + tm) * D)[d] = vv;
-          reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.rk_ring) + ((long long)it.h * kWindow + tm) * D)[d] = rr;
+    const uint32_t armed = armed_s;
+    if (tid == 0 && nxt < total) next_copy = resolve_item<D>(f, item_of(nxt, a.R, a.H));  // overlaps the copy
+    const long long src = ((long long)it.r * a.H + it.h) * D;
+    if (it.slot < Cfg::KB) {
+      // ------------------------------------------------ local attention block
+      const int s0 = it.slot * Cfg::SLOTS;
+      const float sl = 1.4426950408889634f / sqrtf((float)D);
+      for (int d = tid; d < D; d += 128) qv[d] = bf(a.q[src + d]) * sl;
+      __syncthreads();
+      float* part = a.local_part + (((long long)it.r * a.H + it.h) * Cfg::KB + it.slot) * (D + 2);
+      if (!armed) {
+        if (tid == 0) { part[D] = -INFINITY; part[D + 1] = 0.f; }
+      } else {
+        if (!wait_uniform(&bar, phase, a.err, &flag)) return;
+        bf16* sk = reinterpret_cast<bf16*>(dsm);
+        bf16* sv = sk + Cfg::SLOTS * D;
+        const int tm = (int)(t % kWindow);
+        if (tm >= s0 && tm < s0 + Cfg::SLOTS) {
+          // this block owns the current token's slot: append to the ring, patch smem
+          for (int d = tid; d < D / 8; d += 128) {
+            const uint4 kk = reinterpret_cast<const uint4*>(a.k + src)[d];
+            const uint4 vv = reinterpret_cast<const uint4*>(a.v + src)[d];
+            const uint4 rr = reinterpret_cast<const uint4*>(a.raw_k + src)[d];
+            reinterpret_cast<uint4*>(sk + (tm - s0) * D)[d] = kk;
+            reinterpret_cast<uint4*>(sv + (tm - s0) * D)[d] = vv;
+            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.k_ring) + ((long long)it.h * kWindow + tm) * D)[d] = kk;
+            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.v_ring) + ((long long)it.h * kWindow + tm) * D)[d] = vv;
+            reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(st.rk_ring) + ((long long)it.h * kWindow + tm) * D)[d] = rr;
+          }
+          __syncthreads();
+        }
+        constexpr int TPK = 128 / Cfg::SLOTS;
+        const int key = tid / TPK, pid = tid % TPK;
+        float sc = 0.f;
+        {
+          const bf16* kr = sk + key * D;
+          constexpr int NCH = D / 8 / TPK;
+#pragma unroll
+          for (int x = 0; x < NCH; ++x) {
+            const int c = pid * NCH + ((x + key) % NCH);
+            float fv[8];
+            unpack8(*reinterpret_cast<const uint4*>(kr + c * 8), fv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sc += fv[e] * qv[c * 8 + e];
+          }
+          if (TPK == 2) sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+        }
+        const long long kp = t - (long long)((tm - (s0 + key) + kWindow) % kWindow);
+        if (kp < window_start(t) || kp > t) sc = -INFINITY;
+        float mx = warp_max(sc);
+        if (lane == 0) red[warp] = mx;
+        __syncthreads();
+        mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+        const float pk = (sc == -INFINITY) ? 0.f : exp2f(sc - mx);
+        const float ls = warp_sum(pid == 0 ? pk : 0.f);
+        if (pid == 0) red[8 + key] = pk;
+        __syncthreads();
+        if (lane == 0) red[4 + warp] = ls;
+        constexpr int ECH = D / 8, KG = 128 / ECH, KPG = Cfg::SLOTS / KG;
+        const int ec = tid % ECH, kg = tid / ECH;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int x = 0; x < KPG; ++x) {
+          const int kk = kg * KPG + x;
+          const float pj = red[8 + kk];
+          float fv[8];
+          unpack8(*reinterpret_cast<const uint4*>(sv + kk * D + ec * 8), fv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += pj * fv[e];
+        }
+        // reduce over key groups in the (now free) K half of the stage
+        float* rs = reinterpret_cast<float*>(dsm);
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < 8; ++e) rs[kg * D + ec * 8 + e] = acc[e];
+        __syncthreads();
+        for (int d = tid; d < D; d += 128) {
+          float sum = 0.f;
+          for (int g2 = 0; g2 < KG; ++g2) sum += rs[g2 * D + d];
+          part[d] = sum;
+        }
+        if (tid == 0) { part[D] = mx; part[D + 1] = red[4] + red[5] + red[6] + red[7]; }
+      }
+    } else if (t >= kWindow) {
+      // -------------------------------------------------- selected fine group
+      const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
+      const int nf = min(Cfg::FPC, st.n_route - m0);
+      if (nf > 0) {
+        const int32_t* ids = st.route_ids + (long long)it.h * st.route_cap + m0;
+        const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
+        const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + (long long)it.h * st.cap_fines * D;
+        const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + it.h * pstride;
+        const bf16* pw = reinterpret_cast<const bf16*>(st.page_w) + it.h * pstride;
+        // channels do not depend on the matrices in flight: compute them first
+        if (warp == 0) softmax_row<D>(a.raw_q + src, qv, lane);
+        __syncthreads();
+        for (int x = warp; x < nf; x += 4) {
+          const int id = ids[x], page = id / kGroup;
+          float sum = 0.f;
+          for (int d = lane; d < D; d += 32) {
+            const float hv = rb(__fmul_rn(qv[d], bf(pw[(long long)page * D + d])));
+            const float w = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
+            const float c = rb(__fmul_rn(hv, w));
+            chs[x * D + d] = c;
+            sum += c;
+          }
+          sum = warp_sum(sum);
+          if (lane == 0) red[x] = rb(sum);
+        }
+        if (!wait_uniform(&bar, phase, a.err, &flag)) return;
+        constexpr int ECH = D / 8, RG = 128 / ECH, RPG = D / RG;
+        const int ec = tid % ECH, rg = tid / ECH;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        const bf16* sc_ = reinterpret_cast<const bf16*>(dsm);
+        for (int x = 0; x < nf; ++x) {
+#pragma unroll
+          for (int y = 0; y < RPG; ++y) {
+            const int d = rg * RPG + y;
+            const float c = chs[x * D + d];
+            float fv[8];
+            unpack8(*reinterpret_cast<const uint4*>(sc_ + x * D * D + d * D + ec * 8), fv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] += c * fv[e];
+          }
         }
         __syncthreads();
-      }
-      constexpr int TPK = 128 / Cfg::SLOTS;
-      const int key = tid / TPK, pid = tid % TPK;
-      float sc = 0.f;
-      {
-        const bf16* kr = sk + key * D;
-        constexpr int NCH = D / 8 / TPK;
+        float* rs = reinterpret_cast<float*>(dsm);
 #pragma unroll
-        for (int x = 0; x < NCH; ++x) {
-          const int c = pid * NCH + ((x + key) % NCH);
-          float fv[8];
-          unpack8(*reinterpret_cast<const uint4*>(kr + c * 8), fv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) sc += fv[e] * qv[c * 8 + e];
+        for (int e = 0; e < 8; ++e) rs[rg * D + ec * 8 + e] = acc[e];
+        __syncthreads();
+        float* part = a.fine_part + (((long long)it.r * a.H + it.h) * f.ms + (it.slot - Cfg::KB)) * (D + 1);
+        for (int d = tid; d < D; d += 128) {
+          float sum = 0.f;
+          for (int g2 = 0; g2 < RG; ++g2) sum += rs[g2 * D + d];
+          part[d] = sum;
         }
-        if (TPK == 2) sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-      }
-      const long long kp = t - (long long)((tm - (s0 + key) + kWindow) % kWindow);
-      if (kp < window_start(t) || kp > t) sc = -INFINITY;
-      float mx = warp_max(sc);
-      if (lane == 0) red[warp] = mx;
-      __syncthreads();
-      mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-      const float pk = (sc == -INFINITY) ? 0.f : exp2f(sc - mx);
-      const float ls = warp_sum(pid == 0 ? pk : 0.f);
-      if (pid == 0) red[8 + key] = pk;
-      __syncthreads();
-      if (lane == 0) red[4 + warp] = ls;
-      constexpr int ECH = D / 8, KG = 128 / ECH, KPG = Cfg::SLOTS / KG;
-      const int ec = tid % ECH, kg = tid / ECH;
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-      for (int x = 0; x < KPG; ++x) {
-        const int kk = kg * KPG + x;
-        const float pj = red[8 + kk];
-        float fv[8];
-        unpack8(*reinterpret_cast<const uint4*>(sv + kk * D + ec * 8), fv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += pj * fv[e];
-      }
-      // reduce over key groups in the (now free) K half of the stage
-      float* rs = reinterpret_cast<float*>(dsm);
-      __syncthreads();
-#pragma unroll
-      for (int e = 0; e < 8; ++e) rs[kg * D + ec * 8 + e] = acc[e];
-      __syncthreads();
-      for (int d = tid; d < D; d += 128) {
-        float sum = 0.f;
-        for (int g2 = 0; g2 < KG; ++g2) sum += rs[g2 * D + d];
-        part[d] = sum;
-      }
-      if (tid == 0) { part[D] = mx; part[D + 1] = red[4] + red[5] + red[6] + red[7]; }
-    }
-  } else if (t >= kWindow) {
-    // -------------------------------------------------- selected fine group
-    const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
-    const int nf = min(Cfg::FPC, st.n_route - m0);
-    if (nf > 0) {
-      const int32_t* ids = st.route_ids + (long long)it.h * st.route_cap + m0;
-      const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
-      const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + (long long)it.h * st.cap_fines * D;
-      const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + it.h * pstride;
-      const bf16* pw = reinterpret_cast<const bf16*>(st.page_w) + it.h * pstride;
-      // channels do not depend on the matrices in flight: compute them first
-      if (warp == 0) softmax_row<D>(a.raw_q + src, qv, lane);
-      __syncthreads();
-      for (int x = warp; x < nf; x += 4) {
-        const int id = ids[x], page = id / kGroup;
-        float sum = 0.f;
-        for (int d = lane; d < D; d += 32) {
-          const float hv = rb(__fmul_rn(qv[d], bf(pw[(long long)page * D + d])));
-          const float w = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
-          const float c = rb(__fmul_rn(hv, w));
-          chs[x * D + d] = c;
-          sum += c;
-        }
-        sum = warp_sum(sum);
-        if (lane == 0) red[x] = rb(sum);
-      }
-      if (!wait_uniform(&bar, 0, a.err, &flag)) return;
-      constexpr int ECH = D / 8, RG = 128 / ECH, RPG = D / RG;
-      const int ec = tid % ECH, rg = tid / ECH;
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      const bf16* sc_ = reinterpret_cast<const bf16*>(dsm);
-      for (int x = 0; x < nf; ++x) {
-#pragma unroll
-        for (int y = 0; y < RPG; ++y) {
-          const int d = rg * RPG + y;
-          const float c = chs[x * D + d];
-          float fv[8];
-          unpack8(*reinterpret_cast<const uint4*>(sc_ + x * D * D + d * D + ec * 8), fv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] += c * fv[e];
+        if (tid == 0) {
+          float den = 0.f;
+          for (int x = 0; x < nf; ++x) den += red[x];
+          part[D] = den;
         }
       }
-      __syncthreads();
-      float* rs = reinterpret_cast<float*>(dsm);
+    }
+    if (armed) phase ^= 1u;
+    // ---- the stage is free: issue the next item, then arrive; the CTA completing
+    // the last item of (r, h) finalises it.  Every thread orders its shared-memory
+    // writes of this item (generic proxy) before the next bulk copy (async proxy).
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) {
+      armed_s = (nxt < total) ? issue_copy<D>(next_copy, dsm, &bar) : 0u;
+      last_rh = (atomic_add_release(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
+      if (last_rh) {
+        st.counters[it.h] = 0;
+        fence_acquire();
+      }
+    }
+    __syncthreads();
+    if (!last_rh) continue;
+    // Every item of (r, h) is complete, so every item of this head has read the
+    // cursor: arrive for the request now (its last head moves the cursor at the end);
+    // with D = 64 the arriving thread has no channel, so its round trip overlaps
+    // the combine.
+    int arrived = 0;
+    if (tid == kArriver) arrived = atomic_add_release(&st.arrive, 1);
+    const bool hist = t >= kWindow;
+    const int nparts = hist ? (n_route + Cfg::FPC - 1) / Cfg::FPC : 0;
+    if (tid < D) {  // D <= 128: one channel per thread; partials straight from L2
+      const int d = tid;
+      const float* lg = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
+      const float* fg = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
+      uint32_t fin[3] = {0u, 0u, 0u};  // raw_q, fusion_a (terms 0, 2), fusion_b (terms 0, 2) of channel d
+      if (hist) {
+        const bf16* fa = a.fa + ((long long)it.h * D + d) * 3;
+        const bf16* fb = a.fb + ((long long)it.h * D + d) * 3;
+        fin[0] = *reinterpret_cast<const uint16_t*>(a.raw_q + src + d);
+        fin[1] = *reinterpret_cast<const uint16_t*>(fa) | ((uint32_t)*reinterpret_cast<const uint16_t*>(fa + 2) << 16);
+        fin[2] = *reinterpret_cast<const uint16_t*>(fb) | ((uint32_t)*reinterpret_cast<const uint16_t*>(fb + 2) << 16);
+      }
+      float lm[Cfg::KB], ll[Cfg::KB], lo[Cfg::KB];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) rs[rg * D + ec * 8 + e] = acc[e];
-      __syncthreads();
-      float* part = a.fine_part + (((long long)it.r * a.H + it.h) * f.ms + (it.slot - Cfg::KB)) * (D + 1);
-      for (int d = tid; d < D; d += 128) {
-        float sum = 0.f;
-        for (int g2 = 0; g2 < RG; ++g2) sum += rs[g2 * D + d];
-        part[d] = sum;
+      for (int b2 = 0; b2 < Cfg::KB; ++b2) {
+        lm[b2] = __ldcg(lg + b2 * (D + 2) + D);
+        ll[b2] = __ldcg(lg + b2 * (D + 2) + D + 1);
+        lo[b2] = __ldcg(lg + b2 * (D + 2) + d);
       }
-      if (tid == 0) {
-        float den = 0.f;
-        for (int x = 0; x < nf; ++x) den += red[x];
-        part[D] = den;
+      float Mx = -INFINITY;
+#pragma unroll
+      for (int b2 = 0; b2 < Cfg::KB; ++b2) Mx = fmaxf(Mx, lm[b2]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int b2 = 0; b2 < Cfg::KB; ++b2) {
+        if (lm[b2] == -INFINITY) continue;
+        const float scl = exp2f(lm[b2] - Mx);
+        L += scl * ll[b2];
+        O += scl * lo[b2];
       }
-    }
-  }
-  // ---- arrival: the CTA completing the last item of (r, h) finalises it
-  __syncthreads();
-  if (tid == 0) {
-    last_rh = (atomic_add_release(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
-    if (last_rh) {
-      st.counters[it.h] = 0;
-      fence_acquire();
-    }
-  }
-  __syncthreads();
-  if (!last_rh) return;
-  const bool hist = t >= kWindow;
-  const int M = st.n_route;
-  const int nparts = hist ? (M + Cfg::FPC - 1) / Cfg::FPC : 0;
-  // stage all partials of (r, h) in shared memory with one round of coalesced loads
-  float* lp = reinterpret_cast<float*>(dsm);                 // [KB][D+2]
-  float* fp = lp + Cfg::KB * (D + 2);                        // [staged][D+1]
-  const float* fg = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
-  const int room = (Cfg::STAGE / 4 - Cfg::KB * (D + 2)) / (D + 1);
-  const int staged = nparts < room ? nparts : room;          // the rest is read from L2
-  {
-    const float* lg = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
-    for (int x = tid; x < Cfg::KB * (D + 2); x += 128) lp[x] = __ldcg(lg + x);
-    for (int x = tid; x < staged * (D + 1); x += 128) fp[x] = __ldcg(fg + x);
-  }
-  __syncthreads();
-  auto fpart = [&](int p2, int x) -> float {
-    return p2 < staged ? fp[p2 * (D + 1) + x] : __ldcg(fg + p2 * (D + 1) + x);
-  };
-  for (int d = tid; d < D; d += 128) {
-    float Mx = -INFINITY;
-    for (int b2 = 0; b2 < Cfg::KB; ++b2) Mx = fmaxf(Mx, lp[b2 * (D + 2) + D]);
-    float L = 0.f, O = 0.f;
-    for (int b2 = 0; b2 < Cfg::KB; ++b2) {
-      const float mb = lp[b2 * (D + 2) + D];
-      if (mb == -INFINITY) continue;
-      const float scl = exp2f(mb - Mx);
-      L += scl * lp[b2 * (D + 2) + D + 1];
-      O += scl * lp[b2 * (D + 2) + d];
-    }
-    const float local = rb(O / L);
-    float outv = local;
-    if (hist) {
-      float acc = 0.f, den = 0.f;
-      for (int p2 = 0; p2 < nparts; ++p2) {
-        acc += fpart(p2, d);
-        den += fpart(p2, D);
+      const float local = rb(O / L);
+      float outv = local;
+      if (hist) {
+        float acc = 0.f, den = 0.f;
+#pragma unroll 4
+        for (int p2 = 0; p2 < nparts; ++p2) {
+          acc += __ldcg(fg + p2 * (D + 1) + d);
+          den += __ldcg(fg + p2 * (D + 1) + D);
+        }
+        const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
+        const float qq = lo_f(fin[0]);
+        const float s0 = rb(__fadd_rn(rb(__fmul_rn(lo_f(fin[1]), qq)), lo_f(fin[2])));  // + 0 (middle term) is exact
+        const float s2 = rb(__fadd_rn(rb(__fmul_rn(hi_f(fin[1]), qq)), hi_f(fin[2])));
+        const float mx = fmaxf(s0, s2);
+        const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
+        const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
+        const float lt = rb(__fmul_rn(rho0, __fmul_rn(2.f, local)));  // bf16(2 * local) = 2 * local
+        const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(a.gain, fine))));
+        outv = rb(__fadd_rn(__fadd_rn(lt, 0.f), ft));  // lt + 0 (middle term) is exact: no rounding
       }
-      const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
-      const float qq = bf(a.raw_q[src + d]);
-      const bf16* fa = a.fa + ((long long)it.h * D + d) * 3;
-      const bf16* fb = a.fb + ((long long)it.h * D + d) * 3;
-      const float s0 = rb(__fadd_rn(rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), qq)), bf(fb[0]))), 0.f));
-      const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), qq)), bf(fb[2])));
-      const float mx = fmaxf(s0, s2);
-      const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
-      const float rho0 = rb(__fdiv_rn(e0, e0 + e2)), rho2 = rb(__fdiv_rn(e2, e0 + e2));
-      const float lt = rb(__fmul_rn(rho0, rb(__fmul_rn(2.f, local))));
-      const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(a.gain, fine))));
-      outv = rb(__fadd_rn(rb(__fadd_rn(lt, 0.f)), ft));
+      a.out[src + d] = tobf(outv);
     }
-    a.out[src + d] = tobf(outv);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    if (atomic_add_release(&st.arrive, 1) == a.H - 1) {
+    if (tid == kArriver && arrived == a.H - 1) {  // the request's last head: advance its cursor
       fence_acquire();
       st.arrive = 0;
       st.position = t + 1;
