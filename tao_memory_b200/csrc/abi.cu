@@ -236,7 +236,9 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
         per_sm = 1;
       resident = per_sm * sms;
     }
-    decode_fused_kernel<D><<<total < resident ? total : resident, 128, smem, s>>>(f);
+    // balanced: every CTA walks the same number of items (give or take one)
+    const int rounds = (total + resident - 1) / resident;
+    decode_fused_kernel<D><<<(total + rounds - 1) / rounds, 128, smem, s>>>(f);
   }
   if (g_prof_stop) cudaEventRecord(g_prof_stop, s);
   g_prof_start = g_prof_stop = nullptr;

@@ -362,10 +362,20 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
       float outv = local;
       if (hist) {
         float acc = 0.f, den = 0.f;
-#pragma unroll 4
-        for (int p2 = 0; p2 < nparts; ++p2) {
-          acc += __ldcg(fg + p2 * (D + 1) + d);
-          den += __ldcg(fg + p2 * (D + 1) + D);
+        for (int p0 = 0; p0 < nparts; p0 += 16) {  // 16 partials' loads in flight, then summed in order
+          float va[16], vd[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int p2 = p0 + u;
+            va[u] = p2 < nparts ? __ldcg(fg + p2 * (D + 1) + d) : 0.f;
+            vd[u] = p2 < nparts ? __ldcg(fg + p2 * (D + 1) + D) : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 16; ++u)
+            if (p0 + u < nparts) {
+              acc += va[u];
+              den += vd[u];
+            }
         }
         const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
         const float qq = lo_f(fin[0]);

@@ -526,7 +526,8 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {
         // channels e, e + 1: every rounding point rounds the pair with one conversion;
-        // bf16(x + 0) and bf16(2 * local) are exact and not re-rounded
+        // bf16(x + 0) and bf16(2 * local) are exact and not re-rounded (x + 0 is kept:
+        // it turns -0 into +0)
         const int e = j * 8 + c4 * 2;
         const uint32_t q2 = *reinterpret_cast<const uint32_t*>(smem + swz(r, e, D));
         const uint32_t l2 = *reinterpret_cast<const uint32_t*>(smem + 256 * D * 2 + swz(r, e, D));
@@ -573,7 +574,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
         rb2(lt[0], lt[1]);
         rb2(res[0], res[1]);
 #pragma unroll
-        for (int x = 0; x < 2; ++x) res[x] = __fadd_rn(lt[x], res[x]);
+        for (int x = 0; x < 2; ++x) res[x] = __fadd_rn(__fadd_rn(lt[x], 0.f), res[x]);
         rb2(res[0], res[1]);
         *reinterpret_cast<uint32_t*>(a.out + base + e) = pack_exact(res[0], res[1]);
         *reinterpret_cast<uint32_t*>(a.num_out + base + e) = pack_exact(nums[0], nums[1]);
