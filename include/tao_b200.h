@@ -254,14 +254,15 @@ int tao_train_forward(const void* q, const void* k, const void* v, const void* r
                       void* out, const TaoTrainBuffers* buffers, void* stream);
 
 /* Gradient buffers of one backward (caller-allocated):
- *   dq, dk, dv, d_raw_q, d_raw_k : bf16 [B][T][H][D]; d_raw_k zero-filled by the caller
+ *   dq, dk, dv, d_raw_q, d_raw_k : bf16 [B][T][H][D] (written completely)
  *   d_fusion_a, d_fusion_b       : fp32 [H][D][3], zero-filled (accumulated)
  *   d_local, gn, d_rq_f          : bf16 [B][T][H][D] scratch
  *   gd                           : fp32 [B][T][H] scratch
  *   row_dot                      : fp32 [B][H][T] scratch
  *   dC, dz                       : fp32 [B][H][S][D][D], [B][H][S][D]; dz zero-filled
- *   dc_partial                   : bf16 [B][H][tao_train_pairs(T)][D][D], zero-filled
- *                                  (one dC partial per (tile, visible fine) pair) */
+ *   dc_partial                   : bf16 [B][H][tao_train_pairs(T)][D][D] scratch (one dC
+ *                                  partial per (tile, visible fine) pair; the library
+ *                                  clears what it accumulates into) */
 typedef struct TaoTrainGrads {
   void* dq;
   void* dk;

@@ -122,6 +122,19 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   BwdArgs a = a0;
   const Geometry g = geometry(a.dm.T);
   const int B = a.dm.B, H = a.dm.H, T = a.dm.T;
+  // d raw_k of the tokens past the last sealed block gets no writer gradient: zero
+  // those rows here (the writer backward writes all the others)
+  const long long tail0 = (long long)g.S * kFine;
+  if (tail0 < T) {
+    const size_t row_bytes = (size_t)H * D * 2;
+    if (cudaMemset2DAsync(a.d_raw_k + tail0 * H * D, (size_t)T * row_bytes, 0, (size_t)(T - tail0) * row_bytes, B,
+                          s) != cudaSuccess)
+      return tfail(TAO_ERR_CUDA, "d_raw_k tail memset");
+  }
+  // width 128 splits a tile's queries over two CTAs that add into the same dC partial
+  if (ReadBwdSmem<D>::NQ < 256 && a.npairs > 0 &&
+      cudaMemsetAsync(a.dcp, 0, (size_t)B * H * a.npairs * D * D * 2, s) != cudaSuccess)
+    return tfail(TAO_ERR_CUDA, "dc_partial memset");
   fusion_bwd_kernel<D><<<dim3((T + 8 * kFusionRowsPerWarp - 1) / (8 * kFusionRowsPerWarp), B * H), 256, 0, s>>>(a);
   if (D == 64 && a.dq_acc && attention_variant() == 1) {
     if (int rc = launch_attention_backward_tc(a.q, a.k, a.v, a.d_local, a.lse, a.dv_row, a.dq, a.dk, a.dv,

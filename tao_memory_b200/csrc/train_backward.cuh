@@ -724,6 +724,16 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
     nused = n;
   }
   __syncthreads();
+  if (QS == 1 && nused < V) {
+    // dC partials of fines no query of this tile selected are zero (the reduction
+    // reads every pair; the buffer is not cleared beforehand)
+    for (int sf = 0; sf < V; ++sf) {
+      if (useS[sf]) continue;
+      const long long pair = (long long)(tile - 3) * (tile - 2) / 2 + sf;
+      bf16* dcb = a.dcp + (((long long)b * a.dm.H + h) * a.npairs + pair) * (long long)D * D;
+      for (int idx = tid * 8; idx < D * D; idx += NT * 8) *reinterpret_cast<uint4*>(dcb + idx) = make_uint4(0, 0, 0, 0);
+    }
+  }
 
   auto hval = [&](int qq, int d) -> float { return bf(*reinterpret_cast<const bf16*>(hB + swz(qq, d, D))); };
   constexpr int NTL = D / 8;
@@ -1133,12 +1143,18 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
     }
   }
   __syncthreads();
-  // e and p, once per element
-  for (int idx = tid; idx < NT * D; idx += 256) {
-    const int t = idx / D, d = idx % D;
-    const float e = rb(expf(rb(__fsub_rn(bf(at(kB, t, d)), mx[d]))));
-    if (kStoreE) at(eB, t, d) = tobf(e);
-    at(kB, t, d) = tobf(__fdiv_rn(e, zp[d]));
+  // e and p, once per element, two adjacent channels at a time (one packed
+  // conversion per rounding point)
+  for (int idx = tid; idx < NT * D / 2; idx += 256) {
+    const int t = idx / (D / 2), d = (idx % (D / 2)) * 2;
+    const uint32_t k2 = *reinterpret_cast<const uint32_t*>(kB + swz(t, d, D));
+    float e0 = __fsub_rn(lo_f(k2), mx[d]), e1 = __fsub_rn(hi_f(k2), mx[d + 1]);
+    rb2(e0, e1);
+    e0 = expf(e0);
+    e1 = expf(e1);
+    rb2(e0, e1);
+    if (kStoreE) *reinterpret_cast<uint32_t*>(eB + swz(t, d, D)) = pack_exact(e0, e1);
+    *reinterpret_cast<uint32_t*>(kB + swz(t, d, D)) = wa::pack_bf16(__fdiv_rn(e0, zp[d]), __fdiv_rn(e1, zp[d + 1]));
   }
   __syncthreads();
   const int g = lane >> 2, c4 = lane & 3;
@@ -1190,8 +1206,9 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
 #pragma unroll
         for (int j = 0; j < NTL; ++j) {
           const float2 o = __bfloat1622float2(old[hr][j]);
-          *reinterpret_cast<__nv_bfloat162*>(dvb + (long long)t * row + j * 8 + c4 * 2) =
-              __floats2bfloat162_rn(rb(o.x + rb(dvw[mi][j][hr * 2])), rb(o.y + rb(dvw[mi][j][hr * 2 + 1])));
+          float w0 = dvw[mi][j][hr * 2], w1 = dvw[mi][j][hr * 2 + 1];
+          rb2(w0, w1);
+          *reinterpret_cast<uint32_t*>(dvb + (long long)t * row + j * 8 + c4 * 2) = wa::pack_bf16(o.x + w0, o.y + w1);
         }
       }
     }
@@ -1239,10 +1256,14 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
       for (int j = 0; j < NTL; ++j) {
         const int d = j * 8 + c4 * 2;
         const uint32_t p2 = *reinterpret_cast<const uint32_t*>(kB + swz(t, d, D));
-        const float pr[2] = {lo_f(p2), hi_f(p2)};
-#pragma unroll
-        for (int x = 0; x < 2; ++x)
-          zpart[j][x] += rb(-__fmul_rn(rb(dp[mi][j][hr * 2 + x]), rb(__fdiv_rn(pr[x], zp[d + x]))));
+        float a0 = dp[mi][j][hr * 2], a1 = dp[mi][j][hr * 2 + 1];
+        float q0 = __fdiv_rn(lo_f(p2), zp[d]), q1 = __fdiv_rn(hi_f(p2), zp[d + 1]);
+        rb2(a0, a1);
+        rb2(q0, q1);
+        float m0 = -__fmul_rn(a0, q0), m1 = -__fmul_rn(a1, q1);
+        rb2(m0, m1);
+        zpart[j][0] += m0;
+        zpart[j][1] += m1;
       }
     }
 #pragma unroll
@@ -1288,18 +1309,24 @@ __global__ void __launch_bounds__(256, (D == 64) ? 2 : 1) writer_bwd_kernel(BwdA
           ev[0] = lo_f(kp[j]);
           ev[1] = hi_f(kp[j]);
         } else {
-          ev[0] = rb(expf(rb(__fsub_rn(lo_f(kp[j]), mx[d]))));
-          ev[1] = rb(expf(rb(__fsub_rn(hi_f(kp[j]), mx[d + 1]))));
+          ev[0] = __fsub_rn(lo_f(kp[j]), mx[d]);
+          ev[1] = __fsub_rn(hi_f(kp[j]), mx[d + 1]);
+          rb2(ev[0], ev[1]);
+          ev[0] = expf(ev[0]);
+          ev[1] = expf(ev[1]);
+          rb2(ev[0], ev[1]);
         }
-        float o2[2];
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float de = rb(__fadd_rn(rb(__fdiv_rn(rb(dp[mi][j][hr * 2 + x]), zp[d + x])), dZ[d + x]));
-          const float dx = rb(__fmul_rn(de, ev[x]));
-          o2[x] = dx;
-          mpart[j][x] += dx;
-        }
-        *reinterpret_cast<__nv_bfloat162*>(dkb + (long long)t * row + d) = __floats2bfloat162_rn(o2[0], o2[1]);
+        float a0 = dp[mi][j][hr * 2], a1 = dp[mi][j][hr * 2 + 1];
+        rb2(a0, a1);
+        float q0 = __fdiv_rn(a0, zp[d]), q1 = __fdiv_rn(a1, zp[d + 1]);
+        rb2(q0, q1);
+        float de0 = __fadd_rn(q0, dZ[d]), de1 = __fadd_rn(q1, dZ[d + 1]);
+        rb2(de0, de1);
+        float dx0 = __fmul_rn(de0, ev[0]), dx1 = __fmul_rn(de1, ev[1]);
+        rb2(dx0, dx1);
+        mpart[j][0] += dx0;
+        mpart[j][1] += dx1;
+        *reinterpret_cast<uint32_t*>(dkb + (long long)t * row + d) = pack_exact(dx0, dx1);
       }
     }
 #pragma unroll

@@ -51,7 +51,7 @@ def backward(ctx, grad):
     grad = grad.to(_BF16).contiguous()
     s = saved["fine_c"].shape[2] if t > 768 else 1
     e = lambda: torch.empty_like(q)
-    gr = dict(dq=e(), dk=e(), dv=e(), d_raw_q=e(), d_raw_k=torch.zeros_like(q),
+    gr = dict(dq=e(), dk=e(), dv=e(), d_raw_q=e(), d_raw_k=e(),
               d_fusion_a=torch.zeros(h, d, 3, dtype=torch.float32, device=dev),
               d_fusion_b=torch.zeros(h, d, 3, dtype=torch.float32, device=dev),
               d_local=e(), gn=e(), d_rq_f=e(),
@@ -59,7 +59,7 @@ def backward(ctx, grad):
               row_dot=torch.empty(b, h, t, dtype=torch.float32, device=dev),
               dC=torch.empty(b, h, s, d, d, dtype=torch.float32, device=dev),
               dz=torch.zeros(b, h, s, d, dtype=torch.float32, device=dev),
-              dc_partial=torch.zeros(b, h, max(1, _lib.lib().tao_train_pairs(t)), d, d, dtype=_BF16,
+              dc_partial=torch.empty(b, h, max(1, _lib.lib().tao_train_pairs(t)), d, d, dtype=_BF16,
                                      device=dev),
               dq_acc=torch.empty(b, t, h, d, dtype=torch.float32, device=dev))
     gdesc = _Grads(*(gr[n].data_ptr() for n, _ in _Grads._fields_))
