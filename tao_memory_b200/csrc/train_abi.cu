@@ -110,7 +110,7 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
   const size_t rsmem = ReadSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the training read kernel");
   if (!tsmem(train_read_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
-  train_read_kernel<D><<<dim3(g.tiles, B * H), 256, rsmem, s>>>(a);
+  train_read_kernel<D><<<dim3(B * H, g.tiles), 256, rsmem, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return tfail(TAO_ERR_CUDA, cudaGetErrorString(e));
   return TAO_OK;
@@ -151,7 +151,7 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the read backward kernel");
   if (!tsmem(read_bwd_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
   constexpr int NQ = ReadBwdSmem<D>::NQ;
-  read_bwd_kernel<D><<<dim3(g.tiles * (256 / NQ), B * H), ReadBwdSmem<D>::NT, rsmem, s>>>(a);
+  read_bwd_kernel<D><<<dim3(B * H * (256 / NQ), g.tiles), ReadBwdSmem<D>::NT, rsmem, s>>>(a);
   if (g.S > 0) {
     dc_reduce_kernel<D><<<B * H * g.S, 256, 0, s>>>(a, g.tiles);
     const size_t wsmem = WriterBwdSmem<D>::bytes();

@@ -574,7 +574,8 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
   using namespace wa;
   constexpr int NQ = ReadBwdSmem<D>::NQ, NT = ReadBwdSmem<D>::NT, CB = ReadBwdSmem<D>::CB, QS = 256 / NQ;
   constexpr int NW = NT / 32, MI = NQ / (16 * NW);  // warp w owns query rows 16*MI*w .. + 16*MI - 1
-  const int tile = blockIdx.x / QS, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  // grid (B*H*QS, tiles), tiles heaviest first: the longest CTAs are dispatched first
+  const int tile = gridDim.y - 1 - blockIdx.y, bh = blockIdx.x / QS, b = bh / a.dm.H, h = bh % a.dm.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = tile * 256 + (blockIdx.x % QS) * NQ, nq = max(0, min(NQ, a.dm.T - q0));
   const int V = max(0, tile - 2);

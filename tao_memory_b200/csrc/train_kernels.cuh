@@ -220,7 +220,8 @@ template <int D>
 __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   using namespace wa;
   constexpr int NBUF = ReadSmem<D>::NBUF;
-  const int tile = blockIdx.x, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  // grid (B*H, tiles), tiles heaviest first: the longest CTAs are dispatched first
+  const int tile = gridDim.y - 1 - blockIdx.y, b = blockIdx.x / a.dm.H, h = blockIdx.x % a.dm.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = tile * 256;
   const int nq = min(256, a.dm.T - q0);
