@@ -1046,15 +1046,18 @@ __global__ void __launch_bounds__(256) dc_reduce_kernel(BwdArgs a, int tiles) {
   const int s = blockIdx.x % a.dm.S, bh = blockIdx.x / a.dm.S;
   const bf16* base = a.dcp + (long long)bh * a.npairs * D * D;
   float* out = a.dC + ((long long)bh * a.dm.S + s) * D * D;
-  for (int x = threadIdx.x * 2; x < D * D; x += 512) {
-    float2 acc = make_float2(0.f, 0.f);
+  for (int x = threadIdx.x * 8; x < D * D; x += 256 * 8) {  // 8 elements (16 bytes) per load
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
     for (int t = s + 3; t < tiles; ++t) {
       const long long pair = (long long)(t - 3) * (t - 2) / 2 + s;
-      const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(base + pair * D * D + x));
-      acc.x += v.x;
-      acc.y += v.y;
+      float v[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(base + pair * D * D + x)), v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += v[e];
     }
-    *reinterpret_cast<float2*>(out + x) = acc;
+    *reinterpret_cast<float4*>(out + x) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(out + x + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
 }
 

@@ -15,11 +15,24 @@ struct TrainDims {
   long long row;    // token stride in elements (H * D)
 };
 
+// both values rounded to bf16 (one cvt.rn.bf16x2.f32)
+TAO_DEVI void rb2(float& x, float& y) {
+  const uint32_t u = wa::pack_bf16(x, y);
+  x = lo_f(u);
+  y = hi_f(u);
+}
+// bf16 pair of two values that are already bf16-representable (no rounding)
+TAO_DEVI uint32_t pack_exact(float x, float y) {
+  return (__float_as_uint(x) >> 16) | (__float_as_uint(y) & 0xffff0000u);
+}
+
 // Per-channel max and partition of a staged [256][D] key block, with the token
 // range split over NTHREADS / D thread groups (partials combined in `scratch`,
 // 2 * NTHREADS floats): m = max_t k, Z = bf16(sum_t bf16(exp(bf16(k - m)))).
-template <int D, int NTHREADS, typename KAt>
-TAO_DEVI void channel_stats(KAt kat, float* mx, float* zp, float* scratch) {
+// Tokens go two at a time (one packed conversion per rounding point, the sum
+// still in token order); eset(t, d, e) receives every e = bf16(exp(bf16(k - m))).
+template <int D, int NTHREADS, typename KAt, typename ESet>
+TAO_DEVI void channel_stats(KAt kat, float* mx, float* zp, float* scratch, ESet eset) {
   constexpr int G = NTHREADS / D, TPG = 256 / G;
   const int tid = threadIdx.x, d = tid % D, grp = tid / D;
   float m = -INFINITY;
@@ -30,7 +43,17 @@ TAO_DEVI void channel_stats(KAt kat, float* mx, float* zp, float* scratch) {
 #pragma unroll
   for (int x = 0; x < G; ++x) m = fmaxf(m, scratch[x * D + d]);
   float sum = 0.f;
-  for (int t = grp * TPG; t < (grp + 1) * TPG; ++t) sum += rb(expf(rb(__fsub_rn(kat(t, d), m))));
+  for (int t = grp * TPG; t < (grp + 1) * TPG; t += 2) {
+    float e0 = __fsub_rn(kat(t, d), m), e1 = __fsub_rn(kat(t + 1, d), m);
+    rb2(e0, e1);
+    e0 = expf(e0);
+    e1 = expf(e1);
+    rb2(e0, e1);
+    eset(t, d, e0);
+    eset(t + 1, d, e1);
+    sum += e0;
+    sum += e1;
+  }
   scratch[NTHREADS + grp * D + d] = sum;
   __syncthreads();
   if (grp == 0) {
@@ -41,6 +64,10 @@ TAO_DEVI void channel_stats(KAt kat, float* mx, float* zp, float* scratch) {
     zp[d] = rb(z);
   }
   __syncthreads();
+}
+template <int D, int NTHREADS, typename KAt>
+TAO_DEVI void channel_stats(KAt kat, float* mx, float* zp, float* scratch) {
+  channel_stats<D, NTHREADS>(kat, mx, zp, scratch, [](int, int, float) {});
 }
 
 // ---------------------------------------------------------------------------
@@ -75,11 +102,14 @@ __global__ void __launch_bounds__(128) writer_kernel(const bf16* __restrict__ ra
   };
   // per channel: max, partition = bf16(sum_t bf16(exp(bf16(k - max))))
   __shared__ float stat_scratch[2 * 128];
-  channel_stats<D, 128>([&](int t, int d) { return bf(at(t, d)); }, mx, zp, stat_scratch);
-  for (int idx = tid; idx < NT * D; idx += 128) {
-    const int t = idx / D, d = idx % D;
-    const float e = rb(expf(rb(__fsub_rn(bf(at(t, d)), mx[d]))));
-    at(t, d) = tobf(__fdiv_rn(e, zp[d]));
+  // e replaces the key in shared memory (it is exact in bf16); p = bf16(e / Z)
+  channel_stats<D, 128>([&](int t, int d) { return bf(at(t, d)); }, mx, zp, stat_scratch,
+                        [&](int t, int d, float e) { at(t, d) = tobf(e); });
+  for (int idx = tid; idx < NT * D / 2; idx += 128) {  // two channels at a time
+    const int t = idx / (D / 2), d = (idx % (D / 2)) * 2;
+    uint32_t* cell = reinterpret_cast<uint32_t*>(smem + swz(t, d, D));
+    const uint32_t e2 = *cell;
+    *cell = wa::pack_bf16(__fdiv_rn(lo_f(e2), zp[d]), __fdiv_rn(hi_f(e2), zp[d + 1]));
   }
   bf16* zo = z_out + (((long long)b * dm.H + h) * dm.S + s) * D;
   for (int d = tid; d < D; d += 128) zo[d] = tobf(__fadd_rn(mx[d], rb(logf(zp[d]))));
@@ -174,17 +204,6 @@ __global__ void page_prefix_kernel(const bf16* __restrict__ z, bf16* pzpre, Trai
 //  4. epilogue: num = bf16(acc), fine = bf16(num/den), pointwise fusion -> out.
 // Tiles without history (t < 3) copy the local output.
 // ---------------------------------------------------------------------------
-// both values rounded to bf16 (one cvt.rn.bf16x2.f32)
-TAO_DEVI void rb2(float& x, float& y) {
-  const uint32_t u = wa::pack_bf16(x, y);
-  x = lo_f(u);
-  y = hi_f(u);
-}
-// bf16 pair of two values that are already bf16-representable (no rounding)
-TAO_DEVI uint32_t pack_exact(float x, float y) {
-  return (__float_as_uint(x) >> 16) | (__float_as_uint(y) & 0xffff0000u);
-}
-
 struct ReadArgs {
   const bf16 *raw_q, *local, *fa, *fb;  // [B,T,H,D] x2, [H,D,3] x2
   const float* gain;                     // [H] bf16(2*alpha_h) as float
