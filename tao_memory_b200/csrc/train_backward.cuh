@@ -89,92 +89,82 @@ __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {
       const float gv[2] = {lo_f(cg[p]), hi_f(cg[p])}, loc[2] = {lo_f(cl[p]), hi_f(cl[p])};
       float dloc[2] = {gv[0], gv[1]}, dnum[2] = {0.f, 0.f}, drq[2] = {0.f, 0.f};
       if (present) {
-        const float qv[2] = {lo_f(cq[p]), hi_f(cq[p])};
-        float fine[2], s0[2], s2[2], rho0[2], rho2[2], fg[2], drho0[2], drho2[2], t1[2], dfine[2];
-        float ds0[2], ds2[2], fa0[2], fa2[2], x0[2], x1[2], dn[2], t2[2], dd[2];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) fine[k] = __fdiv_rn(k ? hi_f(cn[p]) : lo_f(cn[p]), den);
-        rb2(fine[0], fine[1]);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          s0[k] = __fmul_rn(fa[p][k][0], qv[k]);
-          s2[k] = __fmul_rn(fa[p][k][2], qv[k]);
-        }
-        rb2(s0[0], s0[1]);
-        rb2(s2[0], s2[1]);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          s0[k] = __fadd_rn(s0[k], fb[p][k][0]);  // base0; + 0 (the absent middle term) is exact
-          s2[k] = __fadd_rn(s2[k], fb[p][k][2]);
-        }
-        rb2(s0[0], s0[1]);
-        rb2(s2[0], s2[1]);
+        // the channel pair as float2: every rounded product / sum is a packed
+        // fp32x2 instruction (each lane IEEE round-to-nearest), divisions stay scalar
+        const float2 qv = make_float2(lo_f(cq[p]), hi_f(cq[p]));
+        const float2 gv2 = make_float2(gv[0], gv[1]), lc2 = make_float2(loc[0], loc[1]);
+        const float2 fa0w = make_float2(fa[p][0][0], fa[p][1][0]), fa2w = make_float2(fa[p][0][2], fa[p][1][2]);
+        const float2 fb0w = make_float2(fb[p][0][0], fb[p][1][0]), fb2w = make_float2(fb[p][0][2], fb[p][1][2]);
+        const float2 gain2 = make_float2(gain, gain), two = make_float2(2.f, 2.f);
+        float2 fine = make_float2(__fdiv_rn(lo_f(cn[p]), den), __fdiv_rn(hi_f(cn[p]), den));
+        rb2(fine.x, fine.y);
+        float2 s0 = __fmul2_rn(fa0w, qv), s2 = __fmul2_rn(fa2w, qv);
+        rb2(s0.x, s0.y);
+        rb2(s2.x, s2.y);
+        s0 = __fadd2_rn(s0, fb0w);  // base0; + 0 (the absent middle term) is exact
+        s2 = __fadd2_rn(s2, fb2w);
+        rb2(s0.x, s0.y);
+        rb2(s2.x, s2.y);
+        float2 rho0, rho2;
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
-          const float mx = fmaxf(s0[k], s2[k]);
+          const float a0 = k ? s0.y : s0.x, a2 = k ? s2.y : s2.x;
+          const float mx = fmaxf(a0, a2);
           // the larger term is exp(0) = 1 exactly: one exponential per element
-          const float eo = expf(fminf(s0[k], s2[k]) - mx);
-          const float e0 = s0[k] >= s2[k] ? 1.f : eo, e2 = s0[k] >= s2[k] ? eo : 1.f;
-          rho0[k] = __fdiv_rn(e0, e0 + e2);
-          rho2[k] = __fdiv_rn(e2, e0 + e2);
+          const float eo = expf(fminf(a0, a2) - mx);
+          const float e0 = a0 >= a2 ? 1.f : eo, e2 = a0 >= a2 ? eo : 1.f;
+          (k ? rho0.y : rho0.x) = __fdiv_rn(e0, e0 + e2);
+          (k ? rho2.y : rho2.x) = __fdiv_rn(e2, e0 + e2);
         }
-        rb2(rho0[0], rho0[1]);
-        rb2(rho2[0], rho2[1]);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          fg[k] = __fmul_rn(gain, fine[k]);
-          drho0[k] = __fmul_rn(gv[k], __fmul_rn(2.f, loc[k]));  // bf16(2 * local) = 2 * local
-          t1[k] = __fmul_rn(gv[k], rho0[k]);
-          dfine[k] = __fmul_rn(gv[k], rho2[k]);
-        }
-        rb2(fg[0], fg[1]);
-        rb2(drho0[0], drho0[1]);
-        rb2(t1[0], t1[1]);
-        rb2(dfine[0], dfine[1]);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          drho2[k] = __fmul_rn(gv[k], fg[k]);
-          dloc[k] = __fmul_rn(2.f, t1[k]);  // exact
-          dfine[k] = __fmul_rn(dfine[k], gain);
-        }
-        rb2(drho2[0], drho2[1]);
-        rb2(dfine[0], dfine[1]);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const float dot = drho0[k] * rho0[k] + drho2[k] * rho2[k];
-          ds0[k] = rho0[k] * (drho0[k] - dot);
-          ds2[k] = rho2[k] * (drho2[k] - dot);
-        }
-        rb2(ds0[0], ds0[1]);
-        rb2(ds2[0], ds2[1]);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          acc_fb[p][k][0] += ds0[k];
-          acc_fb[p][k][2] += ds2[k];
-          fa0[k] = __fmul_rn(ds0[k], qv[k]);
-          fa2[k] = __fmul_rn(ds2[k], qv[k]);
-          x0[k] = __fmul_rn(ds0[k], fa[p][k][0]);
-          x1[k] = __fmul_rn(ds2[k], fa[p][k][2]);
-          dn[k] = __fdiv_rn(dfine[k], den);
-          t2[k] = __fdiv_rn(fine[k], den);
-        }
-        rb2(fa0[0], fa0[1]);
-        rb2(fa2[0], fa2[1]);
-        rb2(x0[0], x0[1]);
-        rb2(x1[0], x1[1]);
-        rb2(dn[0], dn[1]);
-        rb2(t2[0], t2[1]);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          acc_fa[p][k][0] += fa0[k];
-          acc_fa[p][k][2] += fa2[k];
-          drq[k] = x0[k] + x1[k];
-          dnum[k] = dn[k];
-          dd[k] = -__fmul_rn(dfine[k], t2[k]);
-        }
-        rb2(drq[0], drq[1]);
-        rb2(dd[0], dd[1]);
-        dden += dd[0] + dd[1];
+        rb2(rho0.x, rho0.y);
+        rb2(rho2.x, rho2.y);
+        float2 fg = __fmul2_rn(gain2, fine);
+        float2 drho0 = __fmul2_rn(gv2, __fmul2_rn(two, lc2));  // bf16(2 * local) = 2 * local
+        float2 t1 = __fmul2_rn(gv2, rho0);
+        float2 dfine = __fmul2_rn(gv2, rho2);
+        rb2(fg.x, fg.y);
+        rb2(drho0.x, drho0.y);
+        rb2(t1.x, t1.y);
+        rb2(dfine.x, dfine.y);
+        float2 drho2 = __fmul2_rn(gv2, fg);
+        const float2 dl = __fmul2_rn(two, t1);  // exact
+        dloc[0] = dl.x;
+        dloc[1] = dl.y;
+        dfine = __fmul2_rn(dfine, gain2);
+        rb2(drho2.x, drho2.y);
+        rb2(dfine.x, dfine.y);
+        const float2 dot = __ffma2_rn(drho0, rho0, __fmul2_rn(drho2, rho2));
+        float2 ds0 = __fmul2_rn(rho0, __fadd2_rn(drho0, make_float2(-dot.x, -dot.y)));
+        float2 ds2 = __fmul2_rn(rho2, __fadd2_rn(drho2, make_float2(-dot.x, -dot.y)));
+        rb2(ds0.x, ds0.y);
+        rb2(ds2.x, ds2.y);
+        acc_fb[p][0][0] += ds0.x;
+        acc_fb[p][1][0] += ds0.y;
+        acc_fb[p][0][2] += ds2.x;
+        acc_fb[p][1][2] += ds2.y;
+        float2 fa0 = __fmul2_rn(ds0, qv), fa2 = __fmul2_rn(ds2, qv);
+        float2 x0 = __fmul2_rn(ds0, fa0w), x1 = __fmul2_rn(ds2, fa2w);
+        float2 dn = make_float2(__fdiv_rn(dfine.x, den), __fdiv_rn(dfine.y, den));
+        float2 t2 = make_float2(__fdiv_rn(fine.x, den), __fdiv_rn(fine.y, den));
+        rb2(fa0.x, fa0.y);
+        rb2(fa2.x, fa2.y);
+        rb2(x0.x, x0.y);
+        rb2(x1.x, x1.y);
+        rb2(dn.x, dn.y);
+        rb2(t2.x, t2.y);
+        acc_fa[p][0][0] += fa0.x;
+        acc_fa[p][1][0] += fa0.y;
+        acc_fa[p][0][2] += fa2.x;
+        acc_fa[p][1][2] += fa2.y;
+        float2 rq = __fadd2_rn(x0, x1);
+        float2 dd = __fmul2_rn(dfine, t2);
+        rb2(rq.x, rq.y);
+        rb2(dd.x, dd.y);
+        drq[0] = rq.x;
+        drq[1] = rq.y;
+        dnum[0] = dn.x;
+        dnum[1] = dn.y;
+        dden += -dd.x + -dd.y;
       }
       *reinterpret_cast<uint32_t*>(a.d_local + base + 64 * p) = pack_exact(dloc[0], dloc[1]);
       *reinterpret_cast<uint32_t*>(a.gn + base + 64 * p) = pack_exact(dnum[0], dnum[1]);
