@@ -471,7 +471,7 @@ def run_train_bench(args, world, rank, local):
         return e
 
     stream = torch.cuda.current_stream(device).cuda_stream
-    starts, stops, a0, a1 = ([ev() for _ in range(K)] for _ in range(4))
+    starts, stops, a0, a1, r0, r1 = ([ev() for _ in range(K)] for _ in range(6))
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
@@ -481,8 +481,13 @@ def run_train_bench(args, world, rank, local):
     torch.cuda.nvtx.range_push("timed_train")
     for i in range(K):
         lib.tao_event_record(starts[i], stream)
-        lib.tao_stream_profile_next(a0[i], a1[i])
-        step()
+        lib.tao_stream_profile_next(a0[i], a1[i])        # forward: local attention kernel
+        for t in leaves:
+            t.grad = None
+        out = tb.tao_attention(leaves[0], leaves[1], leaves[2], raw_q=leaves[3], raw_k=leaves[4],
+                               fusion_a=leaves[5], fusion_b=leaves[6], alpha=alpha, config=cfg)
+        lib.tao_stream_profile_next(r0[i], r1[i])        # backward: selected-read backward kernel
+        out.backward(grad)
         lib.tao_event_record(stops[i], stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -494,6 +499,7 @@ def run_train_bench(args, world, rank, local):
 
     step_ms = [elapsed(a, b) for a, b in zip(starts, stops)]
     attn_ms = [elapsed(a, b) for a, b in zip(a0, a1)]
+    rbwd_ms = [elapsed(a, b) for a, b in zip(r0, r1)]
     # e2e: operands from pinned host memory each step, loss scalar back to the host.
     # The next step's host->device copies run on a copy stream into the other half of
     # a double buffer while this step computes (an input pipeline); every step's
@@ -541,6 +547,10 @@ def run_train_bench(args, world, rank, local):
     tokens = world * TB * TT * K
     flops = local_attention_flops(TT, TH, TD, TB)
     achieved = flops / (statistics.mean(attn_ms) * 1e-3) / 1e12
+    rb_flops = read_backward_flops(TT, TH, TD, TB, cfg)
+    rb_achieved = rb_flops / (statistics.mean(rbwd_ms) * 1e-3) / 1e12
+    step_flops = 260.9e9  # per step, fwd + bwd = 3 x the forward's 86.96 GFLOP (config 2 work count)
+    step_achieved = step_flops / (total_ms / K * 1e-3) / 1e12
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
         peak, kind = float(peaks["bf16_tflops_sustained"]), "measured (sustained)"
@@ -557,14 +567,50 @@ def run_train_bench(args, world, rank, local):
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": 6 * TB * TT * TH * TD * 2, "d2h_bytes_per_step": 4,
                 "pipeline": "next step's inputs copied on a second stream during this step"},
-        "roofline": {"bound": "tensor", "kernel": "tc_window_attention_kernel (forward, tcgen05)",
-                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": kind,
-                     "algorithmic_flops_per_launch": flops,
-                     "kernel_ms_mean": round(statistics.mean(attn_ms), 4), "traffic": None},
+        # the step's dominant kernel (about a third of the step): selected-read backward
+        "roofline": {"bound": "tensor", "kernel": "read_bwd_kernel (selected-read backward)",
+                     "achieved": round(rb_achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(rb_achieved / peak, 4), "peak_kind": kind,
+                     "algorithmic_flops_per_launch": rb_flops,
+                     "kernel_ms_mean": round(statistics.mean(rbwd_ms), 4), "traffic": read_bwd_traffic()},
+        "roofline_step": {"bound": "tensor", "achieved": round(step_achieved, 1), "peak": peak,
+                          "unit": "TFLOP/s", "frac": round(step_achieved / peak, 4),
+                          "algorithmic_flops_per_step": step_flops},
+        "roofline_local_attention": {"bound": "tensor", "kernel": "tc_window_attention_kernel (forward, tcgen05)",
+                                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                                     "frac": round(achieved / peak, 4), "algorithmic_flops_per_launch": flops,
+                                     "kernel_ms_mean": round(statistics.mean(attn_ms), 4)},
         "gpu_launches": 10 * K,
         "clocks": clocks.summary(),
     }
+
+
+def read_backward_flops(tokens, heads, width, batch, cfg):
+    """Algorithmic FLOPs of the selected-read backward: every query of 256-query tile t
+    selects exactly M(t) fines, and each (query, fine) pair costs dA = gn.C^T and its
+    share of dC = A^T.gn, 2 x 2 x width^2 FLOPs."""
+    from tao_memory_b200.config import routed_counts
+    pairs = 0
+    for tile in range((tokens + 255) // 256):
+        visible = max(0, tile - 2)
+        if visible == 0:
+            continue
+        m = routed_counts(visible // 8, visible % 8, cfg)[2]
+        pairs += min(256, tokens - tile * 256) * m
+    return 4 * width * width * pairs * heads * batch
+
+
+def read_bwd_traffic():
+    """Per-launch DRAM bytes of read_bwd_kernel from the committed ncu summary
+    (line 'traffic_bytes_per_launch: N'), or None."""
+    path = os.path.join(ROOT, "profiles", "read_bwd_kernel_train8k.md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
 
 
 def cpu_train_baseline(budget_tokens=8192):

@@ -163,11 +163,13 @@ int tao_stream_decode_noalloc(void* const* states, int n_states, const int64_t* 
                               const void* fusion_b, float alpha, void* out, void* stream);
 
 /* CUDA events for timing (thin wrappers over the runtime, so callers need no
- * other binding).  tao_stream_profile_next(start, stop) makes the next
- * tao_stream_step on this host thread record `start` just before and `stop` just
- * after its main kernel(s) (the local-attention + fine-read phase), on the
- * stream it launches on; for the next tao_train_forward instead, around its
- * windowed local-attention kernel.  No reference counterpart (profiling hook). */
+ * other binding).  tao_stream_profile_next(start, stop) makes the next library
+ * call that launches one of these (from any host thread) record `start` just
+ * before and `stop` just after it, on the stream it launches on: the main
+ * kernel(s) of a stream / decode step (the local-attention + fine-read phase),
+ * the windowed local-attention kernel of tao_train_forward, or the selected-read
+ * backward kernel of tao_train_backward.  No reference counterpart (profiling
+ * hook). */
 int tao_event_create(void** event);
 int tao_event_destroy(void* event);
 int tao_event_record(void* event, void* stream);

@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/tao_b200.h"
@@ -24,9 +25,11 @@ int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* o
 namespace {
 
 thread_local std::string g_last_error;
-// Events recorded around the main (HBM-bound) kernel of the next tao_stream_step
-// on this host thread; cleared after use.
-thread_local cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
+// Events recorded around the main kernel of the next step, training forward or
+// training backward (whichever takes them first, from any host thread: torch runs
+// the backward on its own thread); cleared when taken.
+std::mutex g_prof_mutex;
+cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
 // Decode kernel choice: 1 = one CTA per item (default), 0 = warp-specialised
 // persistent, 2 = one warp per 8 KB item.
 int g_decode_variant = 1;
@@ -123,6 +126,7 @@ void tao_set_last_error(const char* msg) { g_last_error = msg; }
 // Hands the pending profiling events (tao_stream_profile_next) to another
 // translation unit's launcher and clears them.
 void tao_take_profile_events(cudaEvent_t* start, cudaEvent_t* stop) {
+  std::lock_guard<std::mutex> lock(g_prof_mutex);
   *start = g_prof_start;
   *stop = g_prof_stop;
   g_prof_start = g_prof_stop = nullptr;
@@ -148,7 +152,9 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
   if ((rc = set_smem(prep_kernel<D>, prep_smem))) return rc;
   prep_kernel<D><<<dim3(a.R * a.H, L.nslot), 256, prep_smem, s>>>(a);
   if ((rc = check_launch("prep_kernel"))) return rc;
-  if (g_prof_start) cudaEventRecord(g_prof_start, s);
+  cudaEvent_t prof0, prof1;
+  tao_take_profile_events(&prof0, &prof1);
+  if (prof0) cudaEventRecord(prof0, s);
   if (a.w == 1) {
     using Cfg = DecodeCfg<D>;
     const size_t main_smem = (size_t)Cfg::FPC * D * D * 2 + (size_t)Cfg::FPC * D * 4;
@@ -178,8 +184,7 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
     prefill_fine_kernel<D><<<dim3(a.R * a.H, (a.w + 15) / 16), 128, pf_smem, s>>>(a);
     if ((rc = check_launch("prefill_fine_kernel"))) return rc;
   }
-  if (g_prof_stop) cudaEventRecord(g_prof_stop, s);
-  g_prof_start = g_prof_stop = nullptr;
+  if (prof1) cudaEventRecord(prof1, s);
   const size_t fin_smem = (size_t)2 * kFine * D * 2 + (size_t)2 * D * 4;
   if ((rc = set_smem(finalize_kernel<D>, fin_smem))) return rc;
   finalize_kernel<D><<<a.R * a.H, 256, fin_smem, s>>>(a);
@@ -212,7 +217,9 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  if (g_prof_start) cudaEventRecord(g_prof_start, s);
+  cudaEvent_t prof0, prof1;
+  tao_take_profile_events(&prof0, &prof1);
+  if (prof0) cudaEventRecord(prof0, s);
   if (g_decode_variant == 2) {
     const int wt = a.R * a.H * (WarpCfg<D>::LI + ms);
     decode_warp_kernel<D><<<(wt + 7) / 8, 256, 0, s>>>(f);
@@ -240,8 +247,7 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
     const int rounds = (total + resident - 1) / resident;
     decode_fused_kernel<D><<<(total + rounds - 1) / rounds, 128, smem, s>>>(f);
   }
-  if (g_prof_stop) cudaEventRecord(g_prof_stop, s);
-  g_prof_start = g_prof_stop = nullptr;
+  if (prof1) cudaEventRecord(prof1, s);
   if ((rc = check_launch("decode_fused_kernel"))) return rc;
   if (seal) {
     const size_t ss = (size_t)2 * kFine * D * 2 + (size_t)2 * D * 4;
@@ -466,6 +472,7 @@ int tao_event_elapsed(void* start, void* stop, float* ms) {
 }
 
 int tao_stream_profile_next(void* start, void* stop) {
+  std::lock_guard<std::mutex> lock(g_prof_mutex);
   g_prof_start = static_cast<cudaEvent_t>(start);
   g_prof_stop = static_cast<cudaEvent_t>(stop);
   return TAO_OK;

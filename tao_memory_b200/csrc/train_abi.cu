@@ -122,6 +122,8 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   BwdArgs a = a0;
   const Geometry g = geometry(a.dm.T);
   const int B = a.dm.B, H = a.dm.H, T = a.dm.T;
+  cudaEvent_t ev0, ev1;  // profiling hook: around the selected-read backward
+  tao_take_profile_events(&ev0, &ev1);
   // d raw_k of the tokens past the last sealed block gets no writer gradient: zero
   // those rows here (the writer backward writes all the others)
   const long long tail0 = (long long)g.S * kFine;
@@ -151,7 +153,9 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the read backward kernel");
   if (!tsmem(read_bwd_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
   constexpr int NQ = ReadBwdSmem<D>::NQ;
+  if (ev0) cudaEventRecord(ev0, s);
   read_bwd_kernel<D><<<dim3(B * H * (256 / NQ), g.tiles), ReadBwdSmem<D>::NT, rsmem, s>>>(a);
+  if (ev1) cudaEventRecord(ev1, s);
   if (g.S > 0) {
     dc_reduce_kernel<D><<<B * H * g.S, 256, 0, s>>>(a, g.tiles);
     const size_t wsmem = WriterBwdSmem<D>::bytes();
