@@ -11,16 +11,19 @@
 //   warps 0-7  elementwise: warp w owns key rows 32(w%4).. (its TMEM lane
 //              quadrant) and query columns 64(w/4)..+63 of each query block
 //   warp 8     TMA copies and MMA issue (one lane issues, the warp walks)
-// TMEM (512 columns): S^T 0-127 and dP^T 128-255 (fp32, lanes = keys; P^T and
-// dS^T are written back over them as bf16 pairs), dV 256-319, dK 320-383 (fp32,
-// accumulated over the query blocks), dQ 384-447 (fp32, lanes = queries).
+// TMEM (512 columns): S^T 0-127 and dP^T 128-255 (fp32, lanes = keys), dV 256-319,
+// dK 320-383 (fp32, accumulated over the query blocks), dQ 384-447 (fp32, lanes =
+// queries).  P^T and dS^T (bf16) go to shared memory, so the S^T / dP^T columns are
+// free as soon as the elementwise warps have loaded them.
 // Per query block i (128 queries):
 //   S^T = K Q_i^T, dP^T = V dO_i^T                          (SS, N=128)   -> sfull
-//   elementwise: P^T, dS^T -> TMEM; dS^T -> shared memory     -> pfull
-//   dV += P^T dO_i, dK += dS^T Q_i (A from TMEM), dQ_i = dS K (A = dS^T staged in
-//   shared memory, read MN-major)                            -> ofull
-//   elementwise: dQ_i rows -> dqfree; each warp stages its 32x32 fp32 dQ box in
-//   shared memory and adds it to an fp32 accumulator with one TMA reduce-add
+//   elementwise: load S^T, dP^T -> sfree (the issuer starts block i+1's S^T, dP^T);
+//   P^T, dS^T in registers; then (block i-1's products done: ofull) read out dQ_{i-1}
+//   -> dqfree, and write P^T, dS^T to shared memory          -> pfull
+//   dV += P^T dO_i, dK += dS^T Q_i (A K-major from shared memory), dQ_i = dS K (A =
+//   dS^T read MN-major)                                      -> ofull
+//   dQ rows: each warp stages its 32x32 fp32 dQ box in shared memory and adds it to
+//   an fp32 accumulator with one TMA reduce-add
 // dQ of a query block collects the contributions of up to six key blocks; the
 // accumulator is zeroed before the launch and converted to bf16 afterwards.
 #pragma once
@@ -38,7 +41,8 @@ constexpr int kThreads = 288;
 // warp), lse/rowdot [2][2][128] fp32, barriers
 constexpr int kOffK = 0, kOffV = kTile, kOffQ = 2 * kTile, kOffO = 4 * kTile, kOffDS = 6 * kTile;
 constexpr int kOffDQ = 8 * kTile;
-constexpr int kOffStat = kOffDQ + 8 * 4096;
+constexpr int kOffPT = kOffDQ + 8 * 4096;  // P^T: two 64-query tiles like dS^T
+constexpr int kOffStat = kOffPT + 2 * kTile;
 constexpr int kOffBar = kOffStat + 2 * 2 * 128 * 4;
 constexpr int kSmem = kOffBar + 128;
 constexpr int kTmemCols = 512;
@@ -103,8 +107,9 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
   uint64_t* const pfull = bars + 6;
   uint64_t* const ofull = bars + 7;
   uint64_t* const dqfree = bars + 8;
-  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
-  volatile int* const abort_flag = reinterpret_cast<volatile int*>(bars + 10);
+  uint64_t* const sfree = bars + 9;
+  uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(bars + 11);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = a.T, H = a.H;
@@ -130,6 +135,7 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
     mbar_init(pfull, 256);
     mbar_init(ofull, 1);
     mbar_init(dqfree, 256);
+    mbar_init(sfree, 256);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -145,7 +151,7 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
     // ================= issuer =================
     const bool leader = lane == 0;
     constexpr uint32_t I_S = idesc_bf16(128, 128, 0, 0);   // K-major A and B
-    constexpr uint32_t I_KV = idesc_bf16(128, 64, 0, 1);   // A from TMEM, B MN-major
+    constexpr uint32_t I_KV = idesc_bf16(128, 64, 0, 1);   // A K-major, B MN-major
     constexpr uint32_t I_Q = idesc_bf16(128, 64, 1, 1);    // A and B MN-major
     int q_armed[2] = {0, 0}, q_done[2] = {0, 0};
     int s_issued = 0, o_issued = 0;
@@ -184,18 +190,15 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
     for (int i = 0; i < 2 && i < nq; ++i) load_q(i);
     fetch_stats(0);
     publish_stats(0);
+    if (nq > 1) fetch_stats(1);
     bool fine = warp_wait(kvbar, 0, a.err, abort_flag);
     if (fine) kv_pending = false;
     const uint32_t aK = smem_u32(sm + kOffK), aV = smem_u32(sm + kOffV), aDS = smem_u32(sm + kOffDS);
-    for (int i = 0; fine && i < nq; ++i) {
+    const uint32_t aPT = smem_u32(sm + kOffPT);
+    // S^T, dP^T of block i (its Q and dO stage must have landed)
+    auto issue_s = [&](int i) -> bool {
       const int st = i & 1;
-      if (i + 1 < nq) fetch_stats(i + 1);
-      if (i > 0) {
-        // every MMA of block i-1 is complete: S^T/dP^T columns and stage (i-1)&1 are free
-        if (!(fine = warp_wait(ofull, (i - 1) & 1, a.err, abort_flag))) break;
-        if (i + 1 < nq) load_q(i + 1);
-      }
-      if (!(fine = warp_wait(&qbar[st], q_done[st] & 1, a.err, abort_flag))) break;
+      if (!warp_wait(&qbar[st], q_done[st] & 1, a.err, abort_flag)) return false;
       ++q_done[st];
       fence_after();
       const uint32_t aQ = smem_u32(sm + kOffQ + st * kTile), aO = smem_u32(sm + kOffO + st * kTile);
@@ -210,22 +213,32 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
       }
       __syncwarp();
       ++s_issued;
-      // P^T, dS^T written (TMEM and shared memory)
+      return true;
+    };
+    if (fine) fine = issue_s(0);
+    for (int i = 0; fine && i < nq; ++i) {
+      const int st = i & 1;
+      // S^T(i), dP^T(i) loaded by the elementwise warps: their columns are free
+      if (!(fine = warp_wait(sfree, i & 1, a.err, abort_flag))) break;
+      if (i + 1 < nq) {
+        publish_stats(i + 1);  // stat buffer (i+1)&1 was last read by block i-1
+        if (i + 2 < nq) fetch_stats(i + 2);
+        if (!(fine = issue_s(i + 1))) break;
+      }
+      // P^T(i), dS^T(i) in shared memory; dQ columns read out (block i-1)
       if (!(fine = warp_wait(pfull, i & 1, a.err, abort_flag))) break;
-      if (i + 1 < nq) publish_stats(i + 1);  // block i-1's stat buffer is no longer read
       if (i > 0 && !(fine = warp_wait(dqfree, (i - 1) & 1, a.err, abort_flag))) break;
       fence_after();
+      const uint32_t aQ = smem_u32(sm + kOffQ + st * kTile), aO = smem_u32(sm + kOffO + st * kTile);
       if (leader) {
 #pragma unroll
-        for (int k = 0; k < kBQ / 16; ++k) {
-          const uint32_t pc = tb::pair_col(k * 16);
-          mma_ts(tDV, tS + pc, sdesc(aO + k * 2048, 8192, 1024), I_KV, (i > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < kBQ / 16; ++k)  // A = P^T (keys x queries), K-major, 16 queries per step
+          mma(tDV, sdesc(aPT + (k >> 2) * kTile + (k & 3) * 32, 16, 1024), sdesc(aO + k * 2048, 8192, 1024),
+              I_KV, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < kBQ / 16; ++k) {
-          const uint32_t pc = tb::pair_col(k * 16);
-          mma_ts(tDK, tDP + pc, sdesc(aQ + k * 2048, 8192, 1024), I_KV, (i > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < kBQ / 16; ++k)
+          mma(tDK, sdesc(aDS + (k >> 2) * kTile + (k & 3) * 32, 16, 1024), sdesc(aQ + k * 2048, 8192, 1024),
+              I_KV, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < kBN / 16; ++k)
           mma(tDQ, sdesc(aDS + k * 2048, kTile, 1024), sdesc(aK + k * 2048, 8192, 1024), I_Q, k > 0);
@@ -233,6 +246,11 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
       }
       __syncwarp();
       ++o_issued;
+      // stage i&1 is free once block i's products are done: refill it with block i+2
+      if (i + 2 < nq) {
+        if (!(fine = warp_wait(ofull, i & 1, a.err, abort_flag))) break;
+        load_q(i + 2);
+      }
     }
     if (!fine) {
       // drain (bounded): copies and MMAs of this CTA still in flight
@@ -252,7 +270,30 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
     const int key = k0 + kr;
     const float sl = 1.4426950408889634f * 0.125f;  // log2(e) / sqrt(64)
     uint8_t* const dsrow = sm + kOffDS + ch * kTile + kr * 128;
+    uint8_t* const ptrow = sm + kOffPT + ch * kTile + kr * 128;
     uint8_t* const stage = sm + kOffDQ + warp * 4096;
+    // dQ rows of block j (its products complete) -> fp32 accumulator
+    auto dq_out = [&](int j) {
+      const int qj = k0 + j * kBQ;
+      float v[32];
+      tmem_ld32(tDQ + lane_off + ch * 32, v);
+      fence_before();
+      mbar_arrive(dqfree);  // the dQ columns are free once read
+      // stage rows (query qj + 32qd + lane, channels 32ch..+31) as a 128B-swizzled
+      // 32x32 fp32 box; rows past T hold exact zeros (their P and dS are zero)
+      if (lane == 0) bulk_wait_read0();  // the previous box has been read out
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<float4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_2d(&tdq, stage, col + ch * 32, row0 + qj + qd * 32);
+        bulk_commit();
+      }
+    };
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
       const int q0 = k0 + i * kBQ;
@@ -260,14 +301,19 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
       if (!(ok = warp_wait(&statbar[sb], (i >> 1) & 1, a.err, abort_flag))) break;
       if (!(ok = warp_wait(sfull, i & 1, a.err, abort_flag))) break;
       fence_after();
+      // this thread's 64 columns of S^T and dP^T, then the columns are released
+      float s[64], dp[64];
+      tmem_ld32(tS + lane_off + ch * 64, s);
+      tmem_ld32(tS + lane_off + ch * 64 + 32, s + 32);
+      tmem_ld32(tDP + lane_off + ch * 64, dp);
+      tmem_ld32(tDP + lane_off + ch * 64 + 32, dp + 32);
+      fence_before();
+      mbar_arrive(sfree);
       const bool masked = (i == 0) || (q0 + kBQ > T);
+      uint32_t pp[32], dd[32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int c0 = ch * 64 + c * 32;  // first query column of this chunk
-        float s[32], dp[32];
-        tmem_ld32(tS + lane_off + c0, s);
-        tmem_ld32(tDP + lane_off + c0, dp);
-        uint32_t pp[16], dd[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
           // lse / rowdot of four query columns: one broadcast vector load each
@@ -277,54 +323,45 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
           float pv[4], dv[4];
 #pragma unroll
           for (int x = 0; x < 4; ++x) {
-            float p = ex2(fmaf(s[e + x], sl, -lv[x]));
+            float p = ex2(fmaf(s[c * 32 + e + x], sl, -lv[x]));
             if (masked) {
               const int q = q0 + c0 + e + x;
               if (key > q || q >= T) p = 0.f;
             }
             pv[x] = p;
-            dv[x] = p * (dp[e + x] - rv[x]);
+            dv[x] = p * (dp[c * 32 + e + x] - rv[x]);
           }
-          pp[e / 2] = pack2(pv[0], pv[1]);
-          pp[e / 2 + 1] = pack2(pv[2], pv[3]);
-          dd[e / 2] = pack2(dv[0], dv[1]);
-          dd[e / 2 + 1] = pack2(dv[2], dv[3]);
+          pp[c * 16 + e / 2] = pack2(pv[0], pv[1]);
+          pp[c * 16 + e / 2 + 1] = pack2(pv[2], pv[3]);
+          dd[c * 16 + e / 2] = pack2(dv[0], dv[1]);
+          dd[c * 16 + e / 2 + 1] = pack2(dv[2], dv[3]);
         }
-        tmem_st16(tS + lane_off + tb::pair_col(c0), pp);
-        tmem_st16(tDP + lane_off + tb::pair_col(c0), dd);
-        // dS^T row for the dQ product: queries contiguous, 128B swizzle by key row
+      }
+      // block i-1's products are done: its dQ is read out and the P^T / dS^T
+      // buffers may be overwritten
+      if (i > 0) {
+        if (!(ok = warp_wait(ofull, (i - 1) & 1, a.err, abort_flag))) break;
+        fence_after();
+        dq_out(i - 1);
+      }
+      // P^T and dS^T rows (queries contiguous, 128B swizzle by key row), for the
+      // dV / dK products (K-major A) and the dQ product (dS^T read MN-major)
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int chunk = (c * 4 + u) ^ (kr & 7);
-          *reinterpret_cast<uint4*>(dsrow + chunk * 16) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+          const int o = c * 16 + 4 * u;
+          *reinterpret_cast<uint4*>(dsrow + chunk * 16) = make_uint4(dd[o], dd[o + 1], dd[o + 2], dd[o + 3]);
+          *reinterpret_cast<uint4*>(ptrow + chunk * 16) = make_uint4(pp[o], pp[o + 1], pp[o + 2], pp[o + 3]);
         }
-      }
-      tmem_wait_st();
       fence_proxy_async();
-      fence_before();
       mbar_arrive(pfull);
-      // dQ_i rows (lanes = queries) -> fp32 accumulator
-      if (!(ok = warp_wait(ofull, i & 1, a.err, abort_flag))) break;
-      fence_after();
-      {
-        float v[32];
-        tmem_ld32(tDQ + lane_off + ch * 32, v);
-        fence_before();
-        mbar_arrive(dqfree);  // the dQ columns are free once read
-        // stage rows (query q0 + 32qd + lane, channels 32ch..+31) as a 128B-swizzled
-        // 32x32 fp32 box; rows past T hold exact zeros (their P and dS are zero)
-        if (lane == 0) bulk_wait_read0();  // the previous box has been read out
-        __syncwarp();
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<float4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-              make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) {
-          tma_reduce_add_2d(&tdq, stage, col + ch * 32, row0 + q0 + qd * 32);
-          bulk_commit();
-        }
+    }
+    if (ok && nq > 0) {  // the last block's dQ
+      if ((ok = warp_wait(ofull, (nq - 1) & 1, a.err, abort_flag))) {
+        fence_after();
+        dq_out(nq - 1);
       }
     }
     if (lane == 0) bulk_wait0();  // dQ reductions complete before the CTA ends
