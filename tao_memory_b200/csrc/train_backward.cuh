@@ -648,13 +648,20 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
       }
+      // exponentials kept from the sum for the output when they fit in registers (width 64)
+      constexpr int KEEP = (D == 64) ? D : 1;
+      float ex[KEEP];
       float sum = 0.f;
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
         float f[8];
         unpack8(rv[c], f);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) sum += expf(f[e] - mx);
+        for (int e = 0; e < 8; ++e) {
+          const float x = expf(f[e] - mx);
+          if (D == 64) ex[(c * 8 + e) % KEEP] = x;
+          sum += x;
+        }
       }
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
@@ -662,8 +669,11 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
         unpack8(rv[c], f);
         __nv_bfloat162 o[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          o[e] = __floats2bfloat162_rn(__fdiv_rn(expf(f[2 * e] - mx), sum), __fdiv_rn(expf(f[2 * e + 1] - mx), sum));
+        for (int e = 0; e < 4; ++e) {
+          const float x0 = (D == 64) ? ex[(c * 8 + 2 * e) % KEEP] : expf(f[2 * e] - mx);
+          const float x1 = (D == 64) ? ex[(c * 8 + 2 * e + 1) % KEEP] : expf(f[2 * e + 1] - mx);
+          o[e] = __floats2bfloat162_rn(__fdiv_rn(x0, sum), __fdiv_rn(x1, sum));
+        }
         rv[c] = *reinterpret_cast<uint4*>(o);
       }
     } else {
@@ -983,11 +993,22 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
   for (int rr = 0; rr < 2 * MI; ++rr) {
     const int mi = rr >> 1, hr = rr & 1;
     const int r = (warp * MI + mi) * 16 + g + hr * 8;
+    // h of this row as channel pairs, bf16(dh) with one packed conversion per pair
+    uint32_t hp[NTL];
+    float dr[NTL][2];
+#pragma unroll
+    for (int j = 0; j < NTL; ++j) {
+      hp[j] = pair_at(hB, r, j * 8 + c4 * 2);
+      dr[j][0] = dh[mi][j][hr * 2];
+      dr[j][1] = dh[mi][j][hr * 2 + 1];
+      rb2(dr[j][0], dr[j][1]);
+    }
     float dot = 0.f;
 #pragma unroll
-    for (int j = 0; j < NTL; ++j)
-#pragma unroll
-      for (int x = 0; x < 2; ++x) dot += hval(r, j * 8 + c4 * 2 + x) * rb(dh[mi][j][hr * 2 + x]);
+    for (int j = 0; j < NTL; ++j) {
+      dot += lo_f(hp[j]) * dr[j][0];
+      dot += hi_f(hp[j]) * dr[j][1];
+    }
     dot += __shfl_xor_sync(0xffffffffu, dot, 1);
     dot += __shfl_xor_sync(0xffffffffu, dot, 2);
     if (r >= nq) continue;
@@ -998,16 +1019,10 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
       fpart[j] = __ldg(reinterpret_cast<const __nv_bfloat162*>(a.d_rq_f + base + j * 8 + c4 * 2));
 #pragma unroll
     for (int j = 0; j < NTL; ++j) {
-      const int d = j * 8 + c4 * 2;
       const float2 fp = __bfloat1622float2(fpart[j]);
-      float o2[2];
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        const float hv = hval(r, d + x);
-        const float drq = rb(hv * (rb(dh[mi][j][hr * 2 + x]) - dot));
-        o2[x] = rb(__fadd_rn(x ? fp.y : fp.x, drq));
-      }
-      *reinterpret_cast<__nv_bfloat162*>(a.d_raw_q + base + d) = __floats2bfloat162_rn(o2[0], o2[1]);
+      float x0 = lo_f(hp[j]) * (dr[j][0] - dot), x1 = hi_f(hp[j]) * (dr[j][1] - dot);
+      rb2(x0, x1);  // d raw_q of this part, then bf16(fusion part + this part)
+      *reinterpret_cast<uint32_t*>(a.d_raw_q + base + j * 8 + c4 * 2) = wa::pack_bf16(fp.x + x0, fp.y + x1);
     }
   }
   // ---- page weights softmax backward, then logsumexp backward of page_z -> dz
@@ -1019,12 +1034,21 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
   }
   __syncthreads();
 #pragma unroll 4
-  for (int idx = tid; idx < V * D; idx += NT) {
-    const int sf = idx / D, d = idx % D, pg = sf / kGroup;
-    const float lse = pzS[pg * D + d];
-    const float w = rb(expf(rb(__fsub_rn(bf(__ldg(zb + (long long)sf * D + d)), lse))));
-    atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d,
-              rb(__fmul_rn(rb(dpzS[pg * D + d]), w)));
+  for (int idx = tid; idx < V * D / 2; idx += NT) {  // channel pairs: packed rounding, one 8-byte atomic
+    const int sf = idx / (D / 2), d = (idx % (D / 2)) * 2, pg = sf / kGroup;
+    const float2 zz = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162*>(zb + (long long)sf * D + d)));
+    float w0 = __fsub_rn(zz.x, pzS[pg * D + d]), w1 = __fsub_rn(zz.y, pzS[pg * D + d + 1]);
+    rb2(w0, w1);
+    w0 = expf(w0);
+    w1 = expf(w1);
+    rb2(w0, w1);
+    float g0 = dpzS[pg * D + d], g1 = dpzS[pg * D + d + 1];
+    rb2(g0, g1);
+    g0 = __fmul_rn(g0, w0);
+    g1 = __fmul_rn(g1, w1);
+    rb2(g0, g1);
+    atomicAdd(reinterpret_cast<float2*>(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d),
+              make_float2(g0, g1));
   }
 }
 
