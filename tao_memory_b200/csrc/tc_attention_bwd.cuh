@@ -38,7 +38,7 @@ constexpr int kD = 64;
 constexpr int kTile = 128 * kD * 2;      // 16 KB
 constexpr int kThreads = 288;
 // K, V, Q[2], dO[2], dS^T (two 16 KB atoms), dQ staging (4 KB per elementwise
-// warp), lse/rowdot [2][2][128] fp32, barriers
+// warp), P^T (two 16 KB atoms), lse/rowdot [2][2][128] fp32, barriers
 constexpr int kOffK = 0, kOffV = kTile, kOffQ = 2 * kTile, kOffO = 4 * kTile, kOffDS = 6 * kTile;
 constexpr int kOffDQ = 8 * kTile;
 constexpr int kOffPT = kOffDQ + 8 * 4096;  // P^T: two 64-query tiles like dS^T
@@ -47,15 +47,6 @@ constexpr int kOffBar = kOffStat + 2 * 2 * 128 * 4;
 constexpr int kSmem = kOffBar + 128;
 constexpr int kTmemCols = 512;
 
-TAO_DEVI void tmem_st16(uint32_t taddr, const uint32_t* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-TAO_DEVI void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Bulk tensor reduce-add of a shared-memory box into global memory (TMA).
 TAO_DEVI void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
   asm volatile(

@@ -736,7 +736,6 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
     }
   }
 
-  auto hval = [&](int qq, int d) -> float { return bf(*reinterpret_cast<const bf16*>(hB + swz(qq, d, D))); };
   constexpr int NTL = D / 8;
   const int g = lane >> 2, c4 = lane & 3;
   float dh[MI][NTL][4];  // rows 16 * (MI * warp + mi) + g (+ 8)
