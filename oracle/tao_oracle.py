@@ -14,7 +14,8 @@ container where it was importable (script: ``tests/golden/make_golden.py``);
 Scope: the preset path ``index_only_page_memo`` (``coarse_index_only=True``,
 ``fine_writer="softmax"``), streaming prefill/decode for one request and
 training forward/backward for batch B; for streaming also
-``fine_writer="regularized_association"`` on the same preset.
+``fine_writer="regularized_association"`` and ``"feature_mass_association"`` on the
+same preset.
 
 Rounding conventions (probed against torch CPU 2.11):
 * ``F.softmax``, ``Tensor.sum`` and ``Tensor.exp`` on bf16 compute in fp32 and
@@ -100,23 +101,51 @@ def seal_block(raw_k, v):
     return z, c
 
 
-def association_statistics(raw_k, v):
+def association_statistics(raw_k, v, with_mass=False):
     """Association-writer statistics of one block [B,256,H,D] (association_writer.py:11-18):
-    u = bf16(fp32 softmax over channels), G = u^T u and X = u^T v in fp32, [B,H,D,D]."""
+    u = bf16(fp32 softmax over channels), G = u^T u and X = u^T v in fp32, [B,H,D,D];
+    with_mass adds the fp32 feature mass sum_t u [B,H,D]."""
     with torch.autocast(device_type="cpu", enabled=False):
         u = raw_k.float().softmax(dim=-1).to(BF16).transpose(1, 2).float()
         values = v.transpose(1, 2).float()
-        return u.transpose(-1, -2) @ u, u.transpose(-1, -2) @ values
+        gram, cross = u.transpose(-1, -2) @ u, u.transpose(-1, -2) @ values
+        return (gram, cross, u.sum(dim=-2)) if with_mass else (gram, cross)
 
 
-def association_matrix(gram, cross):
+def association_matrix(gram, cross, unchecked=False):
     """Regularised solve (association_writer.py:21-32): C = bf16(A^{-1} X) with
-    A = G + (trace(G)/D) I through a Cholesky factor."""
+    A = G + (trace(G)/D) I through a Cholesky factor (unchecked: no error raised
+    for a failed factorisation, as the feature-mass writer asks)."""
     with torch.autocast(device_type="cpu", enabled=False):
         width = gram.shape[-1]
         reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / width
         system = gram + reg[..., None, None] * torch.eye(width, dtype=F32)
-        return torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(BF16)
+        if unchecked:
+            factor, _ = torch.linalg.cholesky_ex(system, upper=False, check_errors=False)
+        else:
+            factor = torch.linalg.cholesky(system)
+        return torch.cholesky_solve(cross, factor).to(BF16)
+
+
+FEATURE_WRITERS = ("feature_mass_association", "structured_gram_association")
+
+
+def feature_read(h, selected_z, selected_id, fine_c):
+    """Feature-mass read (association_writer.py:43-53, indirect_fine.py:13-33):
+    mass_m = sum_d h_d exp(z_m,d) in fp32, channel_m = bf16(h * mass_m / sum_m mass),
+    fine = bf16(sum_m sum_d channel_m,d C_m[d, :]) accumulated in fp32, no denominator.
+    h [B,Q,H,D] bf16, selected_z [B,Q,H,M,D], selected_id [B,Q,H,M], fine_c [B,H,S,D,D]."""
+    with torch.autocast(device_type="cpu", enabled=False):
+        query = h.float().unsqueeze(-2)
+        mass = (query * selected_z.float().exp()).sum(-1)
+        mixture = mass / mass.sum(-1, keepdim=True)
+        channel = (mixture.unsqueeze(-1) * query).to(h.dtype)
+        b, q, hh, m = selected_id.shape
+        bi = torch.arange(b)[:, None, None, None]
+        hi = torch.arange(hh)[None, None, :, None]
+        csel = fine_c[bi, hi, selected_id].float()
+        acc = torch.einsum("bqhmd,bqhmde->bqhe", channel.float(), csel)
+        return acc.to(h.dtype)
 
 
 def seal_all(raw_k, v, fine=256, writer="softmax"):
@@ -214,6 +243,7 @@ class OracleStream:
         self.layer_index = layer_index
         self.fine_writer = fine_writer
         self.pending_gram = self.pending_cross = None   # fp32 writer statistics (association writers)
+        self.pending_mass = None                        # fp32 feature mass (feature-mass writers)
         self.position = 0
         self.local = None              # (k, v, raw_k) [1,L,H,D]
         self.pages = []                # (page_z [1,H,D], fine_z [1,H,8,D])
@@ -238,7 +268,8 @@ class OracleStream:
         fine_z = [fz for _, fz in self.pages]
         if self.pending:
             pending_z = torch.stack(self.pending, dim=2)
-            page_z.append(torch.logsumexp(pending_z, dim=2).to(dtype))
+            page_z.append(self.pending_mass.log().to(dtype) if self.fine_writer in FEATURE_WRITERS
+                          else torch.logsumexp(pending_z, dim=2).to(dtype))
             fine_z.append(pending_z)
         page_z = torch.stack(page_z, dim=2)
         return page_z, torch.cat(fine_z, dim=2)
@@ -275,13 +306,19 @@ class OracleStream:
 
     def _read_segment(self, raw_q, refresh):
         dtype = raw_q.dtype
-        h = F.softmax(raw_q, dim=-1).to(dtype)
+        feature = self.fine_writer in FEATURE_WRITERS
+        h = F.softmax(raw_q.float() if feature else raw_q, dim=-1).to(dtype)
         page_z, fine_z = self._page_tables(dtype)
         page_weight = F.softmax(page_z, dim=2).to(dtype)
         hv = (h.unsqueeze(3) * page_weight[:, None]).to(dtype)
         if refresh:
             self._route(hv[:, :1], page_z, fine_z)
         ids = self.route_ids[1].expand(-1, raw_q.shape[1], -1, -1)
+        if feature:  # tao_stream.py:362-367
+            d = raw_q.shape[-1]
+            sel_z = fine_z[:, None].expand(-1, raw_q.shape[1], -1, -1, -1).gather(
+                3, ids[..., None].expand(-1, -1, -1, -1, d))
+            return feature_read(h, sel_z, ids, self.fine_c)
         return fine_read(hv, page_z, fine_z, ids, self.fine_c, self.GROUP)[-1]
 
     def read(self, raw_q, position):
@@ -308,7 +345,16 @@ class OracleStream:
     def seal(self, raw_k, v):
         """LayerState.seal/append_fine (tao_stream.py:435-512), index-only pages."""
         z, c = seal_block(raw_k, v)
-        if self.fine_writer == "regularized_association":
+        if self.fine_writer == "feature_mass_association":
+            # tao_stream.py:62-65 and 463-500: z = bf16(log feature mass), C from the
+            # unchecked regularised solve; mass and statistics accumulate without reset
+            gram, cross, mass = association_statistics(raw_k, v, with_mass=True)
+            c = association_matrix(gram, cross, unchecked=True)
+            z = mass.log().to(raw_k.dtype)
+            self.pending_mass = mass if self.pending_mass is None else self.pending_mass + mass
+            self.pending_gram = gram if self.pending_gram is None else self.pending_gram + gram
+            self.pending_cross = cross if self.pending_cross is None else self.pending_cross + cross
+        elif self.fine_writer == "regularized_association":
             # tao_stream.py:72-74 and 463-475: same z, C from the regularised solve;
             # with index-only pages the statistics keep accumulating (never reset)
             gram, cross = association_statistics(raw_k, v)
@@ -321,7 +367,9 @@ class OracleStream:
         self.pending.append(z)
         if len(self.pending) == self.GROUP:
             zs = torch.stack(self.pending, dim=2)
-            self.pages.append((torch.logsumexp(zs, dim=2).to(zs.dtype), zs))
+            pz = (self.pending_mass.log().to(zs.dtype) if self.fine_writer in FEATURE_WRITERS
+                  else torch.logsumexp(zs, dim=2).to(zs.dtype))
+            self.pages.append((pz, zs))
             self.pending = []
 
     # -- one chunk (StreamCache.process, tao_stream.py:919-979) ----------
@@ -371,6 +419,7 @@ class OracleStream:
             "pending_z": [clone(z) for z in self.pending],
             "pending_gram": None if self.pending_gram is None else clone(self.pending_gram),
             "pending_cross": None if self.pending_cross is None else clone(self.pending_cross),
+            "pending_mass": None if self.pending_mass is None else clone(self.pending_mass),
             "route_ids": None if self.route_ids is None else tuple(map(clone, self.route_ids)),
             "state_version": self.state_version,
             "route_refreshes": self.route_refreshes,
@@ -388,6 +437,7 @@ class OracleStream:
         st.pending = [cpu(z) for z in saved["pending_z"]]
         st.pending_gram = None if saved.get("pending_gram") is None else cpu(saved["pending_gram"])
         st.pending_cross = None if saved.get("pending_cross") is None else cpu(saved["pending_cross"])
+        st.pending_mass = None if saved.get("pending_mass") is None else cpu(saved["pending_mass"])
         st.route_ids = None if saved["route_ids"] is None else tuple(map(cpu, saved["route_ids"]))
         st.state_version = saved["state_version"]
         st.route_refreshes = saved.get("route_refreshes", 0)

@@ -138,6 +138,7 @@ STREAM_CASES = {
 # name: (case tuple as above, fine_writer)
 WRITER_CASES = {
     "stream_regularized": ((2, 64, 1, (1000, 1900), 40, 8), "regularized_association"),
+    "stream_feature_mass": ((2, 64, 1, (1000, 1900), 40, 11), "feature_mass_association"),
 }
 
 # training cases with another fine writer on the index-only preset
