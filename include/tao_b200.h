@@ -37,7 +37,11 @@ extern "C" {
 
 /* Geometry of the preset (TaoConfig, config.py:7-19).  fine_tokens, local_keep and
  * coarse_group must be 256, 512 and 8; the schedule fields are free.  route_cap is
- * the length of the route-id arrays of every state passed to one call. */
+ * the length of the route-id arrays of every state passed to one call.  fine_read
+ * selects the read of the selected fines: 0 = normalised association read
+ * (softmax and regularised-association writers, query_fresh_fine.py:8-49),
+ * 1 = feature-mass read (feature-mass writer, association_writer.py:43-53 via
+ * tao_stream.py:362-367); fine_read 1 is served by tao_stream_step only. */
 typedef struct TaoPolicy {
   int32_t fine_tokens;
   int32_t local_keep;
@@ -47,6 +51,7 @@ typedef struct TaoPolicy {
   int32_t budget_root_scale;
   int32_t budget_offset;
   int32_t route_cap;
+  int32_t fine_read;
 } TaoPolicy;
 
 /* Device-resident descriptor of one request's one-layer state.  The host writes
@@ -189,6 +194,13 @@ int tao_ring_scatter(void* ring, int heads, int width, int64_t first_position, i
  * LayerState._prepare_q1_page_memo (tao_stream.py:399-416). */
 int tao_state_rebuild_memo(void* state, int heads, int width, int sealed, void* stream);
 
+/* Recompute only the page weights page_w = bf16(softmax over pages of page_z) per
+ * channel, keeping page_z as the caller wrote it.  The feature-mass writer sets
+ * page_z itself (bf16(log of the accumulated feature mass), tao_stream.py:62-65 and
+ * 463-500) after each seal and after import.  Reference: the memo refresh of
+ * LayerState._prepare_q1_page_memo (tao_stream.py:399-416). */
+int tao_state_refresh_page_weights(void* state, int heads, int width, int sealed, void* stream);
+
 /* Windowed causal attention used by training (tao_stream.py:760-787 semantics):
  * query t sees keys [max(0, 256*floor(t/256) - 512), t].  q,k,v,out [B][T][H][D];
  * lse: fp32 [B][H][T] (log-sum-exp of the scaled scores, saved for backward). */
@@ -198,13 +210,15 @@ int tao_window_attention(const void* q, const void* k, const void* v, void* out,
 
 /* Sufficient statistics of the association fine writers for `blocks` x `heads`
  * 256-token blocks: u = bf16(softmax over channels of k[t]) (fp32 softmax), then
- * gram = u^T u and cross = u^T v, fp32 [blocks][heads][width][width].  Token t of
- * (block b, head h) starts at k + b*block_stride + h*head_stride + t*token_stride
- * (elements; rows 16-byte aligned), likewise for v.  Reference:
- * association_statistics (association_writer.py:11-18) at a seal (tao_stream.py:72-74). */
+ * gram = u^T u and cross = u^T v, fp32 [blocks][heads][width][width], and when
+ * `mass` is not null the feature mass sum_t u[t], fp32 [blocks][heads][width].
+ * Token t of (block b, head h) starts at k + b*block_stride + h*head_stride +
+ * t*token_stride (elements; rows 16-byte aligned), likewise for v.  Reference:
+ * association_statistics (association_writer.py:11-18) at a seal
+ * (tao_stream.py:62-65, 72-74). */
 int tao_writer_stats(const void* k, const void* v, long long token_stride, long long head_stride,
                      long long block_stride, int blocks, int heads, int width, float* gram,
-                     float* cross, void* stream);
+                     float* cross, float* mass, void* stream);
 
 /* Select the windowed-attention kernel for this process (tao_window_attention and
  * the training forward): 1 = tcgen05/TMEM kernel with TMA tile loads for width 64

@@ -18,7 +18,8 @@ class TaoPolicy(ctypes.Structure):
     _fields_ = [("fine_tokens", ctypes.c_int32), ("local_keep", ctypes.c_int32),
                 ("coarse_group", ctypes.c_int32), ("route_period", ctypes.c_int32),
                 ("layer_stagger", ctypes.c_int32), ("budget_root_scale", ctypes.c_int32),
-                ("budget_offset", ctypes.c_int32), ("route_cap", ctypes.c_int32)]
+                ("budget_offset", ctypes.c_int32), ("route_cap", ctypes.c_int32),
+                ("fine_read", ctypes.c_int32)]
 
 
 class TaoState(ctypes.Structure):
@@ -53,7 +54,7 @@ _SIGNATURES = {
     "tao_decode_variant": (_I, [_I]),
     "tao_attention_variant": (_I, [_I]),
     "tao_decode_graph_mode": (_I, [_I]),
-    "tao_writer_stats": (_I, [_VP, _VP, _I64, _I64, _I64, _I, _I, _I, _VP, _VP, _VP]),
+    "tao_writer_stats": (_I, [_VP, _VP, _I64, _I64, _I64, _I, _I, _I, _VP, _VP, _VP, _VP]),
     "tao_decode_step": (_I, [_VP, _I, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_int32),
                              ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(TaoPolicy), _I, _I,
                              _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F, _VP, _VP, _SZ, _VP]),
@@ -63,6 +64,7 @@ _SIGNATURES = {
     "tao_ring_gather": (_I, [_VP, _I, _I, _I64, _I, _VP, _VP]),
     "tao_ring_scatter": (_I, [_VP, _I, _I, _I64, _I, _VP, _VP]),
     "tao_state_rebuild_memo": (_I, [_VP, _I, _I, _I, _VP]),
+    "tao_state_refresh_page_weights": (_I, [_VP, _I, _I, _I, _VP]),
     "tao_window_attention": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP]),
     "tao_train_geometry": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "tao_train_forward": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP, _VP, _VP]),

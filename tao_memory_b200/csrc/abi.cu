@@ -90,11 +90,14 @@ int nslot_for(int w, int period) {
   return n < 1 + w ? n : 1 + w;
 }
 
-Layout make_layout(int R, int w, int H, int D, int route_cap, int msplit_decode, int period) {
+// feature: the feature-mass read, which serves w == 1 through the prefill kernels
+// (window attention output + one fine partial per query).
+Layout make_layout(int R, int w, int H, int D, int route_cap, int msplit_decode, int period,
+                   bool feature = false) {
   Layout L{};
   L.nslot = nslot_for(w, period);
   L.kblocks = kblocks_for(D);
-  L.msplit = (w == 1) ? msplit_decode : 1;
+  L.msplit = (w == 1 && !feature) ? msplit_decode : 1;
   size_t off = 0;
   L.err = off;
   off = align256(off + 256);
@@ -108,7 +111,7 @@ Layout make_layout(int R, int w, int H, int D, int route_cap, int msplit_decode,
   // decode partials: room for the warp kernel's 768/(2048/D) local items per (r, h)
   if (w == 1) off = align256(off + (size_t)R * H * (768 / (2048 / D)) * (D + 2) * 4);
   L.local_out = off;
-  if (w > 1) off = align256(off + (size_t)R * w * H * D * 2);
+  if (w > 1 || feature) off = align256(off + (size_t)R * w * H * D * 2);
   L.fine_part = off;
   off = align256(off + (size_t)R * w * H * L.msplit * (D + 1) * 4);
   L.total = off;
@@ -155,7 +158,7 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
   cudaEvent_t prof0, prof1;
   tao_take_profile_events(&prof0, &prof1);
   if (prof0) cudaEventRecord(prof0, s);
-  if (a.w == 1) {
+  if (a.w == 1 && !a.feature) {
     using Cfg = DecodeCfg<D>;
     const size_t main_smem = (size_t)Cfg::FPC * D * D * 2 + (size_t)Cfg::FPC * D * 4;
     if ((rc = set_smem(decode_main_kernel<D>, main_smem))) return rc;
@@ -277,6 +280,8 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
   if (policy->route_period <= 0 || policy->layer_stagger < 0 || policy->budget_root_scale <= 0 ||
       policy->budget_offset < 0 || policy->route_cap <= 0)
     return fail(TAO_ERR_ARG, "invalid routing policy");
+  if (policy->fine_read != 0)
+    return fail(TAO_ERR_ARG, "the feature-mass read (policy.fine_read = 1) is served by tao_stream_step");
   for (const void* p : {q, k, v, raw_q, raw_k, fusion_a, fusion_b, (const void*)out, (const void*)workspace})
     if (!p) return fail(TAO_ERR_ARG, "null tensor pointer");
   for (const void* p : {q, k, v, raw_q, raw_k, (const void*)out})
@@ -353,7 +358,8 @@ size_t tao_stream_workspace_bytes(int n_states, int tokens, int heads, int width
       route_cap <= 0 || !policy || policy->route_period <= 0)
     return 0;
   // one fine partial per selected fine covers every decode kernel variant
-  return make_layout(n_states, tokens, heads, width, route_cap, route_cap, policy->route_period).total;
+  return make_layout(n_states, tokens, heads, width, route_cap, route_cap, policy->route_period,
+                     policy->fine_read != 0).total;
 }
 
 int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
@@ -373,6 +379,8 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
   if (policy->route_period <= 0 || policy->layer_stagger < 0 || policy->budget_root_scale <= 0 ||
       policy->budget_offset < 0)
     return fail(TAO_ERR_ARG, "invalid routing policy");
+  if (policy->fine_read != 0 && policy->fine_read != 1)
+    return fail(TAO_ERR_ARG, "policy.fine_read must be 0 or 1, got %d", policy->fine_read);
   const void* ptrs[] = {q, k, v, raw_q, raw_k, fusion_a, fusion_b, out, workspace};
   for (const void* p : ptrs)
     if (!p) return fail(TAO_ERR_ARG, "null tensor pointer");
@@ -407,7 +415,7 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
 
   const int fpc = fpc_for(width);
   const Layout L = make_layout(n_states, tokens, heads, width, route_cap, (mbound + fpc - 1) / fpc,
-                               policy->route_period);
+                               policy->route_period, policy->fine_read != 0);
   if (workspace_bytes < L.total)
     return fail(TAO_ERR_ARG, "workspace too small: %zu < %zu", workspace_bytes, L.total);
 
@@ -439,6 +447,7 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
   a.local_out = reinterpret_cast<tao::bf16*>(ws + L.local_out);
   a.fine_part = reinterpret_cast<float*>(ws + L.fine_part);
   a.pmax = pmax;
+  a.feature = policy->fine_read;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return width == 64 ? launch_step<64>(a, L, s) : launch_step<128>(a, L, s);
 }
@@ -547,16 +556,26 @@ int tao_ring_scatter(void* ring, int heads, int width, int64_t first_position, i
   return ring_copy(ring, const_cast<void*>(in), heads, width, first_position, count, 0, stream);
 }
 
-int tao_state_rebuild_memo(void* state, int heads, int width, int sealed, void* stream) {
+namespace {
+int memo_rebuild(void* state, int heads, int width, int sealed, int weights_only, void* stream) {
   if (!state || heads <= 0 || sealed < 0) return fail(TAO_ERR_ARG, "bad memo rebuild arguments");
   if (width != 64 && width != 128) return fail(TAO_ERR_ARG, "head width must be 64 or 128");
   if (sealed == 0) return TAO_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (width == 64)
-    tao::memo_rebuild_kernel<64><<<heads, 256, 0, s>>>(static_cast<TaoState*>(state), sealed);
+    tao::memo_rebuild_kernel<64><<<heads, 256, 0, s>>>(static_cast<TaoState*>(state), sealed, weights_only);
   else
-    tao::memo_rebuild_kernel<128><<<heads, 256, 0, s>>>(static_cast<TaoState*>(state), sealed);
+    tao::memo_rebuild_kernel<128><<<heads, 256, 0, s>>>(static_cast<TaoState*>(state), sealed, weights_only);
   return check_launch("memo_rebuild_kernel");
+}
+}  // namespace
+
+int tao_state_rebuild_memo(void* state, int heads, int width, int sealed, void* stream) {
+  return memo_rebuild(state, heads, width, sealed, 0, stream);
+}
+
+int tao_state_refresh_page_weights(void* state, int heads, int width, int sealed, void* stream) {
+  return memo_rebuild(state, heads, width, sealed, 1, stream);
 }
 
 int tao_window_attention(const void* q, const void* k, const void* v, void* out, float* lse,

@@ -41,6 +41,7 @@ struct StepArgs {
   bf16* local_out;      // prefill: [R][w][H][D]
   float* fine_part;     // [R][w][H][msplit][D+1]
   int pmax;             // max pages over the batch (smem sizing)
+  int feature;          // 1: feature-mass read of the selected fines (TaoPolicy.fine_read)
 };
 
 // Position-derived plan of one chunk (constant history inside a chunk).
@@ -482,7 +483,14 @@ __global__ void __launch_bounds__(128) decode_main_kernel(StepArgs a) {
 
 // ---------------------------------------------------------------------------
 // prefill fine read: one CTA per (r,h, 16-query tile); C streamed through a
-// double-buffered shared-memory pipeline (bulk copies)
+// double-buffered shared-memory pipeline (bulk copies).
+// a.feature == 0: normalised association read (query_fresh_fine.py:8-49),
+//   channel = bf16(bf16(h*page_w) * bf16(exp(bf16(z - page_z)))), partial numerator
+//   and denominator per query.
+// a.feature == 1: feature-mass read (association_writer.py:43-53 through
+//   tao_stream.py:362-367): mass_m = sum_d h_d exp(z_m,d) (fp32), channel =
+//   bf16(h * mass_m / sum_m mass_m), numerator only (no denominator).  Also serves
+//   w == 1 for that writer.
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(128) prefill_fine_kernel(StepArgs a) {
@@ -504,6 +512,7 @@ __global__ void __launch_bounds__(128) prefill_fine_kernel(StepArgs a) {
   float* wv = ch + QT * D;                                         // [D]
   float* pwv = wv + D;                                             // [D]
   __shared__ float den_s[QT];
+  __shared__ float tot_s[QT];  // feature read: total feature mass of each query
   __shared__ int seg_s[QT];
 
   const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
@@ -560,6 +569,22 @@ __global__ void __launch_bounds__(128) prefill_fine_kernel(StepArgs a) {
       mbar_expect_tx(&bars[0], D * D * 2);
       bulk_g2s(cbuf, fc + (long long)ids[0] * D * D, D * D * 2, &bars[0]);
     }
+    if (a.feature) {
+      // total feature mass over the segment's selected fines, while C_0 is in flight
+      for (int qi = warp; qi < nq; qi += 4) {
+        if (seg_s[qi] != seg) continue;
+        float tot = 0.f;
+        for (int m = 0; m < M; ++m) {
+          const bf16* zr = fz + (long long)ids[m] * D;
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j)
+            s += __fmul_rn(hq[qi * D + lane + 32 * j], expf(bf(zr[lane + 32 * j])));
+          tot += warp_sum(s);
+        }
+        if (lane == 0) tot_s[qi] = tot;
+      }
+    }
     for (int m = 0; m < M; ++m) {
       const int buf = m & 1;
       if (tid == 0 && m + 1 < M) {
@@ -567,14 +592,29 @@ __global__ void __launch_bounds__(128) prefill_fine_kernel(StepArgs a) {
         bulk_g2s(cbuf + (buf ^ 1) * D * D, fc + (long long)ids[m + 1] * D * D, D * D * 2, &bars[buf ^ 1]);
       }
       const int id = ids[m], page = id / kGroup;
-      for (int d = tid; d < D; d += 128) {
-        wv[d] = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
-        pwv[d] = bf(pw[(long long)page * D + d]);
+      if (!a.feature) {
+        for (int d = tid; d < D; d += 128) {
+          wv[d] = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
+          pwv[d] = bf(pw[(long long)page * D + d]);
+        }
       }
       __syncthreads();
       // channels for the tile's queries in this segment
       for (int qi = warp; qi < nq; qi += 4) {
         if (seg_s[qi] != seg) continue;
+        if (a.feature) {
+          // same per-fine mass as above (same order), then bf16(h * mass / total)
+          const bf16* zr = fz + (long long)id * D;
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j)
+            s += __fmul_rn(hq[qi * D + lane + 32 * j], expf(bf(zr[lane + 32 * j])));
+          const float mix = __fdiv_rn(warp_sum(s), tot_s[qi]);
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j)
+            ch[qi * D + lane + 32 * j] = rb(__fmul_rn(mix, hq[qi * D + lane + 32 * j]));
+          continue;
+        }
         float s = 0.f;
         for (int d = lane; d < D; d += 32) {
           float hv = rb(__fmul_rn(hq[qi * D + d], pwv[d]));
@@ -734,7 +774,7 @@ __global__ void __launch_bounds__(256) finalize_kernel(StepArgs a) {
     const int i = idx / D, d = idx % D;
     const long long row = ((long long)r * a.w + i) * a.H + h;
     float local;
-    if (a.w == 1) {
+    if (a.w == 1 && !a.feature) {
       const float* part = a.local_part + ((long long)r * a.H + h) * a.kblocks * (D + 2);
       float M = -INFINITY;
       for (int b = 0; b < a.kblocks; ++b) M = fmaxf(M, part[b * (D + 2) + D]);
@@ -754,14 +794,15 @@ __global__ void __launch_bounds__(256) finalize_kernel(StepArgs a) {
     if (hist) {
       const int seg = seg_s[i];
       const int M = a.slot_n[((long long)r * a.nslot + seg) * 2];
-      const int nparts = (a.w == 1) ? (M + Cfg::FPC - 1) / Cfg::FPC : 1;
+      const int nparts = (a.w == 1 && !a.feature) ? (M + Cfg::FPC - 1) / Cfg::FPC : 1;
       const float* part = a.fine_part + row * a.msplit * (D + 1);
       float acc = 0.f, den = 0.f;
       for (int s = 0; s < nparts; ++s) {
         acc += part[s * (D + 1) + d];
         den += part[s * (D + 1) + D];
       }
-      const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
+      // feature-mass read: bf16 of the fp32 sum, no denominator (association_writer.py:53)
+      const float fine = a.feature ? rb(acc) : rb(__fdiv_rn(rb(acc), rb(den)));
       // pointwise fusion, reference cast chain (fusion_pointwise.py:19-92)
       const float q = bf(a.raw_q[row * D + d]);
       const bf16* fa = a.fa + ((long long)h * D + d) * 3;
@@ -823,10 +864,11 @@ __global__ void __launch_bounds__(256) finalize_kernel(StepArgs a) {
   }
 }
 
-// Rebuild page_z / page_w of a state from its fine_z (after import).
+// Rebuild page_z / page_w of a state from its fine_z (after import); with
+// weights_only, page_z stays as written and only page_w is recomputed.
 template <int D>
-__global__ void __launch_bounds__(256) memo_rebuild_kernel(TaoState* st, int S) {
-  refresh_memo<D>(*st, blockIdx.x, S, 0);
+__global__ void __launch_bounds__(256) memo_rebuild_kernel(TaoState* st, int S, int weights_only) {
+  refresh_memo<D>(*st, blockIdx.x, S, weights_only ? S / kGroup + (S % kGroup > 0) : 0);
 }
 
 }  // namespace tao

@@ -8,7 +8,7 @@ void tao_set_last_error(const char* msg);
 
 extern "C" int tao_writer_stats(const void* k, const void* v, long long token_stride, long long head_stride,
                                 long long block_stride, int blocks, int heads, int width, float* gram,
-                                float* cross, void* stream) {
+                                float* cross, float* mass, void* stream) {
   if (!k || !v || !gram || !cross || blocks <= 0 || heads <= 0 || token_stride <= 0) {
     tao_set_last_error("bad writer statistics arguments");
     return TAO_ERR_ARG;
@@ -19,7 +19,8 @@ extern "C" int tao_writer_stats(const void* k, const void* v, long long token_st
   }
   if (((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) || (token_stride * 2) % 16 ||
       (head_stride * 2) % 16 || (block_stride * 2) % 16 || ((reinterpret_cast<uintptr_t>(gram) |
-                                                              reinterpret_cast<uintptr_t>(cross)) & 7)) {
+                                                              reinterpret_cast<uintptr_t>(cross) |
+                                                              reinterpret_cast<uintptr_t>(mass)) & 7)) {
     tao_set_last_error("writer statistics operands must be 16-byte aligned rows");
     return TAO_ERR_ARG;
   }
@@ -31,13 +32,13 @@ extern "C" int tao_writer_stats(const void* k, const void* v, long long token_st
     if (e == cudaSuccess)
       tao::writer_stats_kernel<64><<<blocks * heads, 128, smem, s>>>(
           static_cast<const tao::bf16*>(k), static_cast<const tao::bf16*>(v), token_stride, head_stride,
-          block_stride, heads, gram, cross);
+          block_stride, heads, gram, cross, mass);
   } else {
     e = cudaFuncSetAttribute(tao::writer_stats_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       tao::writer_stats_kernel<128><<<blocks * heads, 128, smem, s>>>(
           static_cast<const tao::bf16*>(k), static_cast<const tao::bf16*>(v), token_stride, head_stride,
-          block_stride, heads, gram, cross);
+          block_stride, heads, gram, cross, mass);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {

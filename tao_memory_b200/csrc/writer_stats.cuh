@@ -2,9 +2,10 @@
 //
 // Reference: association_statistics (association_writer.py:11-18), called by the
 // seal of a 256-token block when TaoConfig.fine_writer is "regularized_association"
-// (tao_stream.py:72-74):
+// or "feature_mass_association" (tao_stream.py:62-65, 72-74):
 //   u = bf16(softmax over channels of k[t])   (fp32 softmax, one rounding)
 //   G = u^T u,  X = u^T v                       (fp32 products and sums)
+//   mass = sum_t u[t]                           (fp32, feature-mass writer only)
 // u and v are bf16 values, so every product is exact in fp32 and the bf16 tensor-
 // core MMA with fp32 accumulation computes the same sums as the reference's fp32
 // matmul, up to summation order.
@@ -22,7 +23,7 @@ template <int D>
 __global__ void __launch_bounds__(128) writer_stats_kernel(const bf16* __restrict__ k, const bf16* __restrict__ v,
                                                            long long token_stride, long long head_stride,
                                                            long long block_stride, int heads, float* gram,
-                                                           float* cross) {
+                                                           float* cross, float* mass) {
   using namespace wa;
   constexpr int NT = 256, CH = D / 8;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -65,6 +66,14 @@ __global__ void __launch_bounds__(128) writer_stats_kernel(const bf16* __restric
     }
   }
   __syncthreads();
+  // feature mass (feature-mass writer, tao_stream.py:62-65): sum_t u[t][d] in fp32
+  if (mass != nullptr) {
+    for (int d = tid; d < D; d += 128) {
+      float m = 0.f;
+      for (int t = 0; t < NT; ++t) m += bf(*reinterpret_cast<const bf16*>(smem + swz(t, d, D)));
+      mass[((long long)blk * heads + h) * D + d] = m;
+    }
+  }
   // G[d][e] = sum_t u[t][d] u[t][e], X[d][e] = sum_t u[t][d] v[t][e]
   constexpr int MT = D / 64;  // m-tiles of 16 rows per warp
   constexpr int NTL = D / 8;

@@ -27,7 +27,8 @@ from .config import TaoConfig, routed_counts
 WINDOW, FINE, KEEP, GROUP = 768, 256, 512, 8
 ROUTE_CAP = 256
 MIN_CAP = 64          # initial fine-bank capacity (fines); doubles when full
-WRITERS_B200 = ("softmax", "regularized_association")
+WRITERS_B200 = ("softmax", "regularized_association", "feature_mass_association")
+FEATURE_WRITER = "feature_mass_association"   # feature-mass read of the selected fines
 _BF16 = torch.bfloat16
 
 
@@ -46,20 +47,23 @@ def is_refresh(pos, layer, config):
     return pos == WINDOW or (pos >= first_turn and (pos - first_turn) % config.route_period == 0)
 
 
-def check_config(config):
-    """The sm_100a kernels implement the index-only softmax-writer preset."""
+def check_config(config, training=False):
+    """The sm_100a kernels implement the index-only preset with the softmax and
+    regularised-association writers, and for streaming the feature-mass writer."""
     if (config.fine_tokens, config.local_keep, config.coarse_group) != (FINE, KEEP, GROUP):
         raise ValueError("kernels are specialised for fine_tokens=256, local_keep=512, coarse_group=8")
-    if config.fine_writer not in WRITERS_B200:
-        raise NotImplementedError("fine_writer=%r is not implemented on B200 (implemented: %s)"
-                                  % (config.fine_writer, ", ".join(WRITERS_B200)))
+    writers = WRITERS_B200[:2] if training else WRITERS_B200
+    if config.fine_writer not in writers:
+        raise NotImplementedError("fine_writer=%r is not implemented on B200 %s(implemented: %s)"
+                                  % (config.fine_writer, "training " if training else "", ", ".join(writers)))
     if not config.coarse_index_only:
         raise NotImplementedError("only coarse_index_only=True (index_only_page_memo) is implemented on B200")
 
 
 def policy_for(config):
     return _lib.TaoPolicy(FINE, KEEP, GROUP, config.route_period, config.layer_stagger,
-                          config.budget_root_scale, config.budget_offset, ROUTE_CAP)
+                          config.budget_root_scale, config.budget_offset, ROUTE_CAP,
+                          int(config.fine_writer == FEATURE_WRITER))
 
 
 class _Workspace:
@@ -98,6 +102,7 @@ class StreamCache:
         self._buf = None          # dict of device tensors
         self._graph = None        # _DecodeGraph (config.q1_history_region_graph)
         self._gram = self._cross = None  # fp32 [1,H,D,D] writer statistics (association writers)
+        self._mass = None         # fp32 [1,H,D] accumulated feature mass (feature-mass writer)
         self._desc = None         # device TaoState (uint8 tensor)
         self._host = None         # ctypes TaoState mirror
         self._ptrs = None         # device array holding the descriptor address
@@ -222,29 +227,48 @@ class StreamCache:
         else:
             run_batch([self], q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out)
 
-    # -- association fine writer (tao_stream.py:72-74, 463-475) -----------
+    # -- association fine writers (tao_stream.py:62-65, 72-74, 463-500) ---
     def _seal_writer(self, s):
-        """Replace fine ``s`` (just sealed by the softmax writer kernels, whose z
-        routing keeps) by the regularised association matrix of the same block:
-        statistics on the tensor cores (``tao_writer_stats``), the Cholesky solve in
-        torch.linalg.  The block's 256 tokens are still in the ring (nothing has
-        been appended since the seal).  As in the reference with index-only pages,
-        the fp32 statistics accumulate without reset (they only feed snapshots)."""
+        """Replace fine ``s`` (just sealed by the softmax writer kernels) by the
+        regularised association matrix of the same block: statistics on the tensor
+        cores (``tao_writer_stats``), the Cholesky solve in torch.linalg.  The
+        block's 256 tokens are still in the ring (nothing has been appended since
+        the seal).  As in the reference with index-only pages, the fp32 statistics
+        accumulate without reset.
+
+        Regularised writer: z stays the softmax writer's log-partition.  Feature-mass
+        writer: z = bf16(log mass) of the block, the solve does not check the
+        factorisation (association_writer.py:21-32 called unchecked), and the page
+        receiving the fine gets page_z = bf16(log accumulated mass); the page weights
+        are then recomputed on the device."""
         heads, width = self.heads, self.width
+        feature = self.config.fine_writer == FEATURE_WRITER
         slot0 = (s * FINE) % WINDOW
         gram = torch.empty(1, heads, width, width, dtype=torch.float32, device=self.device)
         cross = torch.empty_like(gram)
+        mass = torch.empty(1, heads, width, dtype=torch.float32, device=self.device) if feature else None
         k = self._buf["rk_ring"][:, slot0:slot0 + FINE]
         v = self._buf["v_ring"][:, slot0:slot0 + FINE]
+        stream = torch.cuda.current_stream(self.device).cuda_stream
         _lib.check(_lib.lib().tao_writer_stats(k.data_ptr(), v.data_ptr(), width, WINDOW * width, 0, 1, heads,
                                                width, gram.data_ptr(), cross.data_ptr(),
-                                               torch.cuda.current_stream(self.device).cuda_stream))
+                                               None if mass is None else mass.data_ptr(), stream))
         reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / width
         system = gram + reg[..., None, None] * torch.eye(width, dtype=torch.float32, device=self.device)
-        c = torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(_BF16)
+        if feature:
+            factor, _ = torch.linalg.cholesky_ex(system, check_errors=False)
+        else:
+            factor = torch.linalg.cholesky(system)
+        c = torch.cholesky_solve(cross, factor).to(_BF16)
         self._buf["fine_c"][:, s].copy_(c[0])
         self._gram = gram if self._gram is None else self._gram + gram
         self._cross = cross if self._cross is None else self._cross + cross
+        if feature:
+            self._mass = mass if self._mass is None else self._mass + mass
+            self._buf["fine_z"][:, s].copy_(mass[0].log().to(_BF16))
+            self._buf["page_z"][:, s // GROUP].copy_(self._mass[0].log().to(_BF16))
+            _lib.check(_lib.lib().tao_state_refresh_page_weights(self._desc.data_ptr(), heads, width, s + 1,
+                                                                 stream))
 
     # -- snapshots (reference dictionary format, tao_stream.py:853-912) --
     def export(self):
@@ -282,7 +306,8 @@ class StreamCache:
             "route_interval": self.route_interval, "fusion_mode": self.fusion_mode,
             "fused_fine": self.fused_fine, "position": self.position, "local": local,
             "packed_fine_c": fine_c, "pages": pages, "pending_z": pending,
-            "pending_square_mass": None, "pending_mass": None,
+            "pending_square_mass": None,
+            "pending_mass": None if self._mass is None else self._mass.clone(),
             "pending_gram": None if self._gram is None else self._gram.clone(),
             "pending_cross": None if self._cross is None else self._cross.clone(),
             "route_ids": route, "route_key": None,
@@ -308,7 +333,7 @@ class StreamCache:
         s = sealed_at(pos)
         state._allocate(heads, width, dev, max(64, s + 1))
         b = state._buf
-        for name, attr in (("pending_gram", "_gram"), ("pending_cross", "_cross")):
+        for name, attr in (("pending_gram", "_gram"), ("pending_cross", "_cross"), ("pending_mass", "_mass")):
             if saved.get(name) is not None:
                 setattr(state, attr, saved[name].to(dev, torch.float32).clone())
         if local is not None:
@@ -337,7 +362,18 @@ class StreamCache:
         h.position = pos
         state._upload()
         stream = torch.cuda.current_stream(dev).cuda_stream
-        _lib.check(_lib.lib().tao_state_rebuild_memo(state._desc.data_ptr(), heads, width, s, stream))
+        if state.config.fine_writer == FEATURE_WRITER and s:
+            # page_z is not a function of fine_z for this writer: completed pages keep
+            # the snapshot's values, the pending page is bf16(log accumulated mass)
+            for p, (pz, _, _) in enumerate(saved["pages"]):
+                b["page_z"][:, p].copy_(pz.reshape(heads, width).to(dev, _BF16))
+            if s % GROUP:
+                if state._mass is None:
+                    raise ValueError("feature-mass snapshot with pending fines has no pending_mass")
+                b["page_z"][:, s // GROUP].copy_(state._mass[0].log().to(_BF16))
+            _lib.check(_lib.lib().tao_state_refresh_page_weights(state._desc.data_ptr(), heads, width, s, stream))
+        else:
+            _lib.check(_lib.lib().tao_state_rebuild_memo(state._desc.data_ptr(), heads, width, s, stream))
         return state
 
     def _gather_ring(self, name, first, count):
@@ -366,10 +402,11 @@ class StreamCache:
         n_route = 0 if self._buf is None else self._download().n_route
         route_bytes = n_route * heads * 8
         stat = lambda t: 0 if t is None else t.numel() * t.element_size()
-        writer = stat(self._gram) + stat(self._cross)
+        gram_cross = stat(self._gram) + stat(self._cross)
         return {"history_bytes": history, "page_normalization_memo_bytes": 0,
-                "pending_writer_bytes": writer, "pending_gram_cross_bytes": writer,
-                "pending_cross_bytes": stat(self._cross), "fused_fine": self.fused_fine,
+                "pending_writer_bytes": gram_cross + stat(self._mass), "pending_gram_cross_bytes": gram_cross,
+                "pending_cross_bytes": stat(self._cross), "pending_square_mass_bytes": 0,
+                "pending_feature_mass_bytes": stat(self._mass), "fused_fine": self.fused_fine,
                 "fusion_mode": self.fusion_mode, "fine_seal_events": s,
                 "route_integer_bytes": route_bytes,
                 "logical_local_bf16_kv_bytes": logical_local,
@@ -412,7 +449,8 @@ class _BatchArgs:
         # descriptor address can be reused by a new state with another layer index
         c = states[0].config
         key = (tuple((st._desc.data_ptr(), st.cap_fines, st.layer_index) for st in states), w, heads, width,
-               c.route_period, c.layer_stagger, c.budget_root_scale, c.budget_offset)
+               c.route_period, c.layer_stagger, c.budget_root_scale, c.budget_offset,
+               c.fine_writer == FEATURE_WRITER)
         args = cls.cache.get(key)
         if args is None:
             if len(cls.cache) > 256:
@@ -440,6 +478,9 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
         else fusion_b.detach().to(dev, _BF16).contiguous()
     if fa.shape != (heads, width, 3) or fb.shape != (heads, width, 3):
         raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
+    feature = states[0].config.fine_writer == FEATURE_WRITER
+    if any((st.config.fine_writer == FEATURE_WRITER) != feature for st in states):
+        raise ValueError("a batch mixes the feature-mass writer with other fine writers")
     for st in states:
         st._ensure(heads, width, dev, w)
     if (w == 1 and dev.type == "cuda" and all(st.config.q1_history_region_graph and st.config.fine_writer == "softmax"
@@ -453,7 +494,7 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
         args.pos[i] = st.position
     ws = _Workspace.get(dev, args.nbytes)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    if w == 1:
+    if w == 1 and not feature:   # the feature-mass read serves w == 1 through tao_stream_step
         _lib.check(lib.tao_decode_step(args.ptrs.data_ptr(), r, args.pos, args.layers, args.cap,
                                        ctypes.byref(args.policy), heads, width,
                                        *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
@@ -476,7 +517,8 @@ def _bookkeep(st, w):
     c = st._counters
     if st.position >= WINDOW:
         c["fusion_pointwise_calls"] += 1
-        c["fused_fine_calls"] += 1
+        if st.config.fine_writer != FEATURE_WRITER:   # the feature read is not the fused fine path
+            c["fused_fine_calls"] += 1
     else:
         c["fusion_no_history_local_returns"] += 1
     st.position += w

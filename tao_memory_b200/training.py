@@ -56,7 +56,7 @@ def _regularized_matrices(raw_k, v, s):
     stream = torch.cuda.current_stream(dev).cuda_stream
     for i in range(b):
         _lib.check(_lib.lib().tao_writer_stats(raw_k[i].data_ptr(), v[i].data_ptr(), h * d, d, 256 * h * d, s, h, d,
-                                               gram[i].data_ptr(), cross[i].data_ptr(), stream))
+                                               gram[i].data_ptr(), cross[i].data_ptr(), None, stream))
     gram, cross = gram.permute(0, 2, 1, 3, 4), cross.permute(0, 2, 1, 3, 4)
     reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / d
     system = gram + reg[..., None, None] * torch.eye(d, dtype=torch.float32, device=dev)
@@ -105,7 +105,7 @@ class _TaoAttention(torch.autograd.Function):
 
 
 def tao_attention_train(q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, config):
-    check_config(config)
+    check_config(config, training=True)
     ops = (q, k, v, raw_q, raw_k)
     if any(t.dtype != _BF16 for t in ops):
         raise ValueError("tao_attention on B200 takes bf16 operands (the reference's selected read "

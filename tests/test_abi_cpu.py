@@ -54,6 +54,20 @@ def test_host_validation_errors_without_gpu():
     assert rc == _lib.TAO_ERR_ARG
     assert lib.tao_stream_workspace_bytes(8, 1, 12, 64, 256, ctypes.byref(pol)) > 0
     assert lib.tao_stream_workspace_bytes(8, 1, 12, 96, 256, ctypes.byref(pol)) == 0
+    # the feature-mass read (fine_read = 1) is served by tao_stream_step; the decode
+    # entry points refuse it, and the stream entry refuses other read modes
+    feat = _lib.TaoPolicy(256, 512, 8, 24, 2, 2, 2, 256, 1)
+    layer = (ctypes.c_int32 * 1)(0)
+    rc = lib.tao_decode_step(16, 1, pos, layer, cap, ctypes.byref(feat), 2, 64, *([16] * 7), 0.5, 16, 256,
+                             1 << 20, None)
+    assert rc == _lib.TAO_ERR_ARG and b"tao_stream_step" in lib.tao_last_error()
+    rc = lib.tao_stream_decode_noalloc(16, 1, pos, cap, ctypes.byref(feat), 2, 64, *([16] * 7), 0.5, 16, None)
+    assert rc == _lib.TAO_ERR_ARG
+    odd = _lib.TaoPolicy(256, 512, 8, 24, 2, 2, 2, 256, 2)
+    rc = lib.tao_stream_step(1, 1, pos, cap, ctypes.byref(odd), 1, 2, 64, *([16] * 7), 0.5, 16, 256, 1 << 20, None)
+    assert rc == _lib.TAO_ERR_ARG
+    # w == 1 under the feature read: a window-attention output and one fine partial per query
+    assert lib.tao_stream_workspace_bytes(8, 1, 12, 64, 256, ctypes.byref(feat)) > 0
 
 
 def test_schedule_matches_reference_policy():
@@ -77,6 +91,20 @@ def test_config_validation_matches_reference():
     with pytest.raises(ValueError):
         TaoConfig(local_keep=300)
     assert TaoConfig(**index_only_page_memo().export()) == index_only_page_memo()
+
+
+def test_feature_mass_writer_is_streaming_only():
+    """The feature-mass writer runs in streaming (prefill/decode) on B200; training
+    with it is refused loudly rather than computed with another read."""
+    from tao_memory_b200.stream import check_config, policy_for
+    cfg = TaoConfig(**{**index_only_page_memo().export(), "fine_writer": "feature_mass_association"})
+    check_config(cfg)
+    assert policy_for(cfg).fine_read == 1 and policy_for(index_only_page_memo()).fine_read == 0
+    with pytest.raises(NotImplementedError):
+        check_config(cfg, training=True)
+    with pytest.raises(NotImplementedError):
+        check_config(TaoConfig(**{**index_only_page_memo().export(),
+                                  "fine_writer": "structured_gram_association"}))
 
 
 def test_batch_argument_cache_keys_on_layer_and_policy():

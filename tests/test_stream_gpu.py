@@ -60,7 +60,8 @@ def run_gpu(x, layer, splits, steps, alpha, snapshot_at=None, config=None):
     return torch.cat(outs, 1), ids, st, snap
 
 
-@pytest.mark.parametrize("name", ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized"])
+@pytest.mark.parametrize("name", ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized",
+                                  "stream_feature_mass"])
 def test_stream_matches_reference_golden(name):
     from tao_memory_b200 import TaoConfig
     g = torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
@@ -80,10 +81,10 @@ def test_stream_matches_reference_golden(name):
     for (pz, _, fz), (rpz, _, rfz) in zip(snap["pages"], ref["pages"]):
         assert close_frac(pz, rpz) == 0.0 and close_frac(fz, rfz) == 0.0
     assert close_frac(snap["packed_fine_c"], ref["packed_fine_c"]) == 0.0
-    # fp32 writer statistics (regularised writer): u = bf16(softmax) can land on the
+    # fp32 writer statistics (association writers): u = bf16(softmax) can land on the
     # other side of a bf16 rounding boundary between torch's CPU softmax and the
     # kernel's (a few values per block), so the sums agree to 1e-3 in relative norm
-    for key in ("pending_gram", "pending_cross"):
+    for key in ("pending_gram", "pending_cross", "pending_mass"):
         assert (snap[key] is None) == (ref[key] is None), key
         if ref[key] is not None:
             err = (snap[key].cpu() - ref[key]).norm() / ref[key].norm()
@@ -246,12 +247,14 @@ def test_writer_stats_match_oracle():
         kd, vd = k.cuda(), v.cuda()
         gram = torch.empty(1, heads, width, width, dtype=torch.float32, device="cuda")
         cross = torch.empty_like(gram)
+        mass = torch.empty(1, heads, width, dtype=torch.float32, device="cuda")
         _lib.check(_lib.lib().tao_writer_stats(kd.data_ptr(), vd.data_ptr(), heads * width, width, 0, 1, heads,
-                                               width, gram.data_ptr(), cross.data_ptr(),
+                                               width, gram.data_ptr(), cross.data_ptr(), mass.data_ptr(),
                                                torch.cuda.current_stream().cuda_stream))
-        rg, rx = o.association_statistics(k, v)
+        rg, rx, rm = o.association_statistics(k, v, with_mass=True)
         assert ((gram.cpu() - rg).norm() / rg.norm()).item() <= 1e-4
         assert ((cross.cpu() - rx).norm() / rx.norm()).item() <= 1e-3
+        assert ((mass.cpu() - rm).norm() / rm.norm()).item() <= 1e-4
         c = o.association_matrix(gram.cpu(), cross.cpu()).float()
         rc = o.association_matrix(rg, rx).float()
         assert ((c - rc).abs() <= 1e-2 + 1e-2 * rc.abs()).all()
