@@ -14,8 +14,8 @@ container where it was importable (script: ``tests/golden/make_golden.py``);
 Scope: the preset path ``index_only_page_memo`` (``coarse_index_only=True``,
 ``fine_writer="softmax"``), streaming prefill/decode for one request and
 training forward/backward for batch B; for streaming also
-``fine_writer="regularized_association"`` and ``"feature_mass_association"`` on the
-same preset.
+``fine_writer="regularized_association"``, ``"feature_mass_association"`` and
+``"structured_gram_association"`` on the same preset.
 
 Rounding conventions (probed against torch CPU 2.11):
 * ``F.softmax``, ``Tensor.sum`` and ``Tensor.exp`` on bf16 compute in fp32 and
@@ -128,6 +128,38 @@ def association_matrix(gram, cross, unchecked=False):
 
 
 FEATURE_WRITERS = ("feature_mass_association", "structured_gram_association")
+
+
+def structured_statistics(raw_k, v):
+    """Structured-Gram writer statistics (structured_writer.py:5-14), no dense Gram:
+    with u as in association_statistics, the fp32 square mass sum_t u*u and mass
+    sum_t u per channel [B,H,D] and X = u^T v [B,H,D,D].  Returns (square, X, mass)."""
+    with torch.autocast(device_type="cpu", enabled=False):
+        u = raw_k.float().softmax(dim=-1).to(BF16).transpose(1, 2).float()
+        values = v.transpose(1, 2).float()
+        return (u * u).sum(-2), u.transpose(-1, -2) @ values, u.sum(-2)
+
+
+def structured_matrix(square, cross, mass, count):
+    """Closed-form structured inverse applied to X (structured_writer.py:17-34), fp32
+    throughout, C = bf16 at the end.  The Gram is modelled per channel as the
+    clamped variance var = square - mass^2/count plus a ridge (mean square mass)
+    on the diagonal, a rank-one term along t = var/diag (dropped when every var is
+    zero) and the rank-one mass term, removed by Sherman-Morrison with denominator
+    count + mass . hm.  The fp32 operations run in the reference's order."""
+    with torch.autocast(device_type="cpu", enabled=False):
+        var = (square - mass * mass / count).clamp_min(0)
+        flat = var.sum(-1, keepdim=True) == 0
+        ridge = square.sum(-1, keepdim=True) / mass.shape[-1]
+        diag = var + ridge
+        t = torch.where(flat, torch.zeros_like(var), var / diag)
+        norm = torch.where(flat, torch.ones_like(ridge), (var * ridge / diag).sum(-1, keepdim=True))
+        tx = (t.unsqueeze(-1) * cross).sum(-2)
+        hx = cross / diag.unsqueeze(-1) + t.unsqueeze(-1) * tx.unsqueeze(-2) / norm.unsqueeze(-1)
+        hm = mass / diag + t * (t * mass).sum(-1, keepdim=True) / norm
+        mhx = (mass.unsqueeze(-1) * hx).sum(-2)
+        den = count + (mass * hm).sum(-1, keepdim=True)
+        return (hx - hm.unsqueeze(-1) * mhx.unsqueeze(-2) / den.unsqueeze(-1)).to(BF16)
 
 
 def feature_read(h, selected_z, selected_id, fine_c):
@@ -244,6 +276,7 @@ class OracleStream:
         self.fine_writer = fine_writer
         self.pending_gram = self.pending_cross = None   # fp32 writer statistics (association writers)
         self.pending_mass = None                        # fp32 feature mass (feature-mass writers)
+        self.pending_square_mass = None                 # fp32 sum u*u (structured-Gram writer)
         self.position = 0
         self.local = None              # (k, v, raw_k) [1,L,H,D]
         self.pages = []                # (page_z [1,H,D], fine_z [1,H,8,D])
@@ -345,7 +378,17 @@ class OracleStream:
     def seal(self, raw_k, v):
         """LayerState.seal/append_fine (tao_stream.py:435-512), index-only pages."""
         z, c = seal_block(raw_k, v)
-        if self.fine_writer == "feature_mass_association":
+        if self.fine_writer == "structured_gram_association":
+            # tao_stream.py:58-61 and 463-472: z = bf16(log feature mass), C from the
+            # structured inverse; square mass, cross and mass accumulate without reset
+            square, cross, mass = structured_statistics(raw_k, v)
+            c = structured_matrix(square, cross, mass, self.FINE)
+            z = mass.log().to(raw_k.dtype)
+            self.pending_mass = mass if self.pending_mass is None else self.pending_mass + mass
+            self.pending_square_mass = (square if self.pending_square_mass is None
+                                        else self.pending_square_mass + square)
+            self.pending_cross = cross if self.pending_cross is None else self.pending_cross + cross
+        elif self.fine_writer == "feature_mass_association":
             # tao_stream.py:62-65 and 463-500: z = bf16(log feature mass), C from the
             # unchecked regularised solve; mass and statistics accumulate without reset
             gram, cross, mass = association_statistics(raw_k, v, with_mass=True)
@@ -420,6 +463,7 @@ class OracleStream:
             "pending_gram": None if self.pending_gram is None else clone(self.pending_gram),
             "pending_cross": None if self.pending_cross is None else clone(self.pending_cross),
             "pending_mass": None if self.pending_mass is None else clone(self.pending_mass),
+            "pending_square_mass": None if self.pending_square_mass is None else clone(self.pending_square_mass),
             "route_ids": None if self.route_ids is None else tuple(map(clone, self.route_ids)),
             "state_version": self.state_version,
             "route_refreshes": self.route_refreshes,
@@ -438,6 +482,8 @@ class OracleStream:
         st.pending_gram = None if saved.get("pending_gram") is None else cpu(saved["pending_gram"])
         st.pending_cross = None if saved.get("pending_cross") is None else cpu(saved["pending_cross"])
         st.pending_mass = None if saved.get("pending_mass") is None else cpu(saved["pending_mass"])
+        st.pending_square_mass = (None if saved.get("pending_square_mass") is None
+                                  else cpu(saved["pending_square_mass"]))
         st.route_ids = None if saved["route_ids"] is None else tuple(map(cpu, saved["route_ids"]))
         st.state_version = saved["state_version"]
         st.route_refreshes = saved.get("route_refreshes", 0)

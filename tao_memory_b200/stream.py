@@ -27,8 +27,9 @@ from .config import TaoConfig, routed_counts
 WINDOW, FINE, KEEP, GROUP = 768, 256, 512, 8
 ROUTE_CAP = 256
 MIN_CAP = 64          # initial fine-bank capacity (fines); doubles when full
-WRITERS_B200 = ("softmax", "regularized_association", "feature_mass_association")
-FEATURE_WRITER = "feature_mass_association"   # feature-mass read of the selected fines
+WRITERS_B200 = ("softmax", "regularized_association", "feature_mass_association", "structured_gram_association")
+# writers whose fines are read with the feature-mass mixture (tao_stream.py:362-367)
+FEATURE_WRITERS = ("feature_mass_association", "structured_gram_association")
 _BF16 = torch.bfloat16
 
 
@@ -49,7 +50,8 @@ def is_refresh(pos, layer, config):
 
 def check_config(config, training=False):
     """The sm_100a kernels implement the index-only preset with the softmax and
-    regularised-association writers, and for streaming the feature-mass writer."""
+    regularised-association writers, and for streaming the feature-mass and
+    structured-Gram writers."""
     if (config.fine_tokens, config.local_keep, config.coarse_group) != (FINE, KEEP, GROUP):
         raise ValueError("kernels are specialised for fine_tokens=256, local_keep=512, coarse_group=8")
     writers = WRITERS_B200[:2] if training else WRITERS_B200
@@ -60,10 +62,32 @@ def check_config(config, training=False):
         raise NotImplementedError("only coarse_index_only=True (index_only_page_memo) is implemented on B200")
 
 
+def _structured_matrix(square, cross, mass, count):
+    """C of the structured-Gram writer (structured_writer.py:17-34) on the device in
+    fp32, bf16 at the end: per channel the clamped variance var = square -
+    mass^2/count plus a ridge (the mean square mass) forms the diagonal; a rank-one
+    term along t = var/diag (dropped when every var is zero) and the rank-one mass
+    term are inverted in closed form (Sherman-Morrison, denominator count +
+    mass . hm).  square, mass [1,H,D], cross [1,H,D,D]; the fp32 operations run in
+    the reference's order."""
+    var = (square - mass * mass / count).clamp_min(0)
+    flat = var.sum(-1, keepdim=True) == 0
+    ridge = square.sum(-1, keepdim=True) / mass.shape[-1]
+    diag = var + ridge
+    t = torch.where(flat, torch.zeros_like(var), var / diag)
+    norm = torch.where(flat, torch.ones_like(ridge), (var * ridge / diag).sum(-1, keepdim=True))
+    tx = (t.unsqueeze(-1) * cross).sum(-2)
+    hx = cross / diag.unsqueeze(-1) + t.unsqueeze(-1) * tx.unsqueeze(-2) / norm.unsqueeze(-1)
+    hm = mass / diag + t * (t * mass).sum(-1, keepdim=True) / norm
+    mhx = (mass.unsqueeze(-1) * hx).sum(-2)
+    den = count + (mass * hm).sum(-1, keepdim=True)
+    return (hx - hm.unsqueeze(-1) * mhx.unsqueeze(-2) / den.unsqueeze(-1)).to(_BF16)
+
+
 def policy_for(config):
     return _lib.TaoPolicy(FINE, KEEP, GROUP, config.route_period, config.layer_stagger,
                           config.budget_root_scale, config.budget_offset, ROUTE_CAP,
-                          int(config.fine_writer == FEATURE_WRITER))
+                          int(config.fine_writer in FEATURE_WRITERS))
 
 
 class _Workspace:
@@ -102,7 +126,8 @@ class StreamCache:
         self._buf = None          # dict of device tensors
         self._graph = None        # _DecodeGraph (config.q1_history_region_graph)
         self._gram = self._cross = None  # fp32 [1,H,D,D] writer statistics (association writers)
-        self._mass = None         # fp32 [1,H,D] accumulated feature mass (feature-mass writer)
+        self._mass = None         # fp32 [1,H,D] accumulated feature mass (feature-read writers)
+        self._square = None       # fp32 [1,H,D] accumulated sum u*u (structured-Gram writer)
         self._desc = None         # device TaoState (uint8 tensor)
         self._host = None         # ctypes TaoState mirror
         self._ptrs = None         # device array holding the descriptor address
@@ -240,9 +265,13 @@ class StreamCache:
         writer: z = bf16(log mass) of the block, the solve does not check the
         factorisation (association_writer.py:21-32 called unchecked), and the page
         receiving the fine gets page_z = bf16(log accumulated mass); the page weights
-        are then recomputed on the device."""
+        are then recomputed on the device.  Structured-Gram writer: the same z and
+        page z, C from the closed-form structured inverse (``_structured_matrix``)
+        of the square mass (the Gram's diagonal), X and the mass; no dense Gram is
+        kept."""
         heads, width = self.heads, self.width
-        feature = self.config.fine_writer == FEATURE_WRITER
+        writer = self.config.fine_writer
+        feature = writer in FEATURE_WRITERS
         slot0 = (s * FINE) % WINDOW
         gram = torch.empty(1, heads, width, width, dtype=torch.float32, device=self.device)
         cross = torch.empty_like(gram)
@@ -253,15 +282,20 @@ class StreamCache:
         _lib.check(_lib.lib().tao_writer_stats(k.data_ptr(), v.data_ptr(), width, WINDOW * width, 0, 1, heads,
                                                width, gram.data_ptr(), cross.data_ptr(),
                                                None if mass is None else mass.data_ptr(), stream))
-        reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / width
-        system = gram + reg[..., None, None] * torch.eye(width, dtype=torch.float32, device=self.device)
-        if feature:
-            factor, _ = torch.linalg.cholesky_ex(system, check_errors=False)
+        if writer == "structured_gram_association":
+            square = gram.diagonal(dim1=-2, dim2=-1).contiguous()
+            c = _structured_matrix(square, cross, mass, FINE)
+            self._square = square if self._square is None else self._square + square
         else:
-            factor = torch.linalg.cholesky(system)
-        c = torch.cholesky_solve(cross, factor).to(_BF16)
+            reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / width
+            system = gram + reg[..., None, None] * torch.eye(width, dtype=torch.float32, device=self.device)
+            if feature:
+                factor, _ = torch.linalg.cholesky_ex(system, check_errors=False)
+            else:
+                factor = torch.linalg.cholesky(system)
+            c = torch.cholesky_solve(cross, factor).to(_BF16)
+            self._gram = gram if self._gram is None else self._gram + gram
         self._buf["fine_c"][:, s].copy_(c[0])
-        self._gram = gram if self._gram is None else self._gram + gram
         self._cross = cross if self._cross is None else self._cross + cross
         if feature:
             self._mass = mass if self._mass is None else self._mass + mass
@@ -306,7 +340,7 @@ class StreamCache:
             "route_interval": self.route_interval, "fusion_mode": self.fusion_mode,
             "fused_fine": self.fused_fine, "position": self.position, "local": local,
             "packed_fine_c": fine_c, "pages": pages, "pending_z": pending,
-            "pending_square_mass": None,
+            "pending_square_mass": None if self._square is None else self._square.clone(),
             "pending_mass": None if self._mass is None else self._mass.clone(),
             "pending_gram": None if self._gram is None else self._gram.clone(),
             "pending_cross": None if self._cross is None else self._cross.clone(),
@@ -333,7 +367,8 @@ class StreamCache:
         s = sealed_at(pos)
         state._allocate(heads, width, dev, max(64, s + 1))
         b = state._buf
-        for name, attr in (("pending_gram", "_gram"), ("pending_cross", "_cross"), ("pending_mass", "_mass")):
+        for name, attr in (("pending_gram", "_gram"), ("pending_cross", "_cross"), ("pending_mass", "_mass"),
+                           ("pending_square_mass", "_square")):
             if saved.get(name) is not None:
                 setattr(state, attr, saved[name].to(dev, torch.float32).clone())
         if local is not None:
@@ -362,7 +397,7 @@ class StreamCache:
         h.position = pos
         state._upload()
         stream = torch.cuda.current_stream(dev).cuda_stream
-        if state.config.fine_writer == FEATURE_WRITER and s:
+        if state.config.fine_writer in FEATURE_WRITERS and s:
             # page_z is not a function of fine_z for this writer: completed pages keep
             # the snapshot's values, the pending page is bf16(log accumulated mass)
             for p, (pz, _, _) in enumerate(saved["pages"]):
@@ -404,8 +439,9 @@ class StreamCache:
         stat = lambda t: 0 if t is None else t.numel() * t.element_size()
         gram_cross = stat(self._gram) + stat(self._cross)
         return {"history_bytes": history, "page_normalization_memo_bytes": 0,
-                "pending_writer_bytes": gram_cross + stat(self._mass), "pending_gram_cross_bytes": gram_cross,
-                "pending_cross_bytes": stat(self._cross), "pending_square_mass_bytes": 0,
+                "pending_writer_bytes": gram_cross + stat(self._mass) + stat(self._square),
+                "pending_gram_cross_bytes": gram_cross,
+                "pending_cross_bytes": stat(self._cross), "pending_square_mass_bytes": stat(self._square),
                 "pending_feature_mass_bytes": stat(self._mass), "fused_fine": self.fused_fine,
                 "fusion_mode": self.fusion_mode, "fine_seal_events": s,
                 "route_integer_bytes": route_bytes,
@@ -450,7 +486,7 @@ class _BatchArgs:
         c = states[0].config
         key = (tuple((st._desc.data_ptr(), st.cap_fines, st.layer_index) for st in states), w, heads, width,
                c.route_period, c.layer_stagger, c.budget_root_scale, c.budget_offset,
-               c.fine_writer == FEATURE_WRITER)
+               c.fine_writer in FEATURE_WRITERS)
         args = cls.cache.get(key)
         if args is None:
             if len(cls.cache) > 256:
@@ -478,9 +514,9 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
         else fusion_b.detach().to(dev, _BF16).contiguous()
     if fa.shape != (heads, width, 3) or fb.shape != (heads, width, 3):
         raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
-    feature = states[0].config.fine_writer == FEATURE_WRITER
-    if any((st.config.fine_writer == FEATURE_WRITER) != feature for st in states):
-        raise ValueError("a batch mixes the feature-mass writer with other fine writers")
+    feature = states[0].config.fine_writer in FEATURE_WRITERS
+    if any((st.config.fine_writer in FEATURE_WRITERS) != feature for st in states):
+        raise ValueError("a batch mixes feature-read writers with other fine writers")
     for st in states:
         st._ensure(heads, width, dev, w)
     if (w == 1 and dev.type == "cuda" and all(st.config.q1_history_region_graph and st.config.fine_writer == "softmax"
@@ -517,7 +553,7 @@ def _bookkeep(st, w):
     c = st._counters
     if st.position >= WINDOW:
         c["fusion_pointwise_calls"] += 1
-        if st.config.fine_writer != FEATURE_WRITER:   # the feature read is not the fused fine path
+        if st.config.fine_writer not in FEATURE_WRITERS:   # the feature read is not the fused fine path
             c["fused_fine_calls"] += 1
     else:
         c["fusion_no_history_local_returns"] += 1

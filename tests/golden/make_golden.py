@@ -139,6 +139,7 @@ STREAM_CASES = {
 WRITER_CASES = {
     "stream_regularized": ((2, 64, 1, (1000, 1900), 40, 8), "regularized_association"),
     "stream_feature_mass": ((2, 64, 1, (1000, 1900), 40, 11), "feature_mass_association"),
+    "stream_structured_gram": ((2, 64, 1, (1000, 1900), 40, 13), "structured_gram_association"),
 }
 
 # training cases with another fine writer on the index-only preset

@@ -93,18 +93,17 @@ def test_config_validation_matches_reference():
     assert TaoConfig(**index_only_page_memo().export()) == index_only_page_memo()
 
 
-def test_feature_mass_writer_is_streaming_only():
-    """The feature-mass writer runs in streaming (prefill/decode) on B200; training
-    with it is refused loudly rather than computed with another read."""
+@pytest.mark.parametrize("writer", ["feature_mass_association", "structured_gram_association"])
+def test_feature_read_writers_are_streaming_only(writer):
+    """The feature-mass and structured-Gram writers run in streaming (prefill/decode)
+    on B200 with the feature-mass read; training with them is refused loudly rather
+    than computed with another read."""
     from tao_memory_b200.stream import check_config, policy_for
-    cfg = TaoConfig(**{**index_only_page_memo().export(), "fine_writer": "feature_mass_association"})
+    cfg = TaoConfig(**{**index_only_page_memo().export(), "fine_writer": writer})
     check_config(cfg)
     assert policy_for(cfg).fine_read == 1 and policy_for(index_only_page_memo()).fine_read == 0
     with pytest.raises(NotImplementedError):
         check_config(cfg, training=True)
-    with pytest.raises(NotImplementedError):
-        check_config(TaoConfig(**{**index_only_page_memo().export(),
-                                  "fine_writer": "structured_gram_association"}))
 
 
 def test_batch_argument_cache_keys_on_layer_and_policy():

@@ -9,7 +9,8 @@ from oracle import tao_oracle as o
 from oracle.inputs import make_inputs, digest
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-STREAM = ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized", "stream_feature_mass"]
+STREAM = ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized", "stream_feature_mass",
+          "stream_structured_gram"]
 TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages", "train_regularized"]
 KEYS = ("q", "k", "v", "raw_q", "raw_k")
 
@@ -54,7 +55,7 @@ def test_stream_oracle_matches_reference(name, one_thread):
         assert torch.equal(pz, rpz) and torch.equal(fz, rfz)
     for z, rz in zip(mine_snap["pending_z"], snap["pending_z"]):
         assert torch.equal(z, rz)
-    for key in ("pending_gram", "pending_cross", "pending_mass"):
+    for key in ("pending_gram", "pending_cross", "pending_mass", "pending_square_mass"):
         assert (mine_snap[key] is None) == (snap.get(key) is None)
         if snap[key] is not None:
             assert torch.equal(mine_snap[key], snap[key]), key

@@ -61,7 +61,7 @@ def run_gpu(x, layer, splits, steps, alpha, snapshot_at=None, config=None):
 
 
 @pytest.mark.parametrize("name", ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized",
-                                  "stream_feature_mass"])
+                                  "stream_feature_mass", "stream_structured_gram"])
 def test_stream_matches_reference_golden(name):
     from tao_memory_b200 import TaoConfig
     g = torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
@@ -84,7 +84,7 @@ def test_stream_matches_reference_golden(name):
     # fp32 writer statistics (association writers): u = bf16(softmax) can land on the
     # other side of a bf16 rounding boundary between torch's CPU softmax and the
     # kernel's (a few values per block), so the sums agree to 1e-3 in relative norm
-    for key in ("pending_gram", "pending_cross", "pending_mass"):
+    for key in ("pending_gram", "pending_cross", "pending_mass", "pending_square_mass"):
         assert (snap[key] is None) == (ref[key] is None), key
         if ref[key] is not None:
             err = (snap[key].cpu() - ref[key]).norm() / ref[key].norm()
