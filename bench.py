@@ -267,10 +267,10 @@ def run_b200(args, world, rank, local):
     e_start = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     e_stop = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     def e2e_step(i):
-        stage.copy_(host_in[i], non_blocking=True)
+        tb.copy_to_device(stage, host_in[i])
         y, _ = tb.tao_attention_decode_batch(stage[0], stage[1], stage[2], raw_q=stage[3], raw_k=stage[4],
                                              fusion_a=fa, fusion_b=fb, alpha=0.5, states=states, out=out)
-        host_out.copy_(y, non_blocking=True)
+        tb.copy_to_host(host_out, y)
 
     for i in range(E2E_WARM):
         e2e_step(i)

@@ -152,6 +152,17 @@ int tao_decode_graph_mode(int on);
  * Returns TAO_OK or TAO_ERR_DEVICE; *flags receives the raw bits. */
 int tao_stream_check(void* workspace, int* flags, void* stream);
 
+/* Host<->device transfer of a decode step's operands by the SMs: a kernel reads
+ * (or writes) page-locked, device-mapped host memory directly, 16 bytes per thread,
+ * on `stream`.  For the tens of kilobytes of one decode step this costs about one
+ * round trip over the host link instead of a copy engine's setup latency.  The host
+ * buffer must be page-locked with a device mapping (checked with
+ * cudaPointerGetAttributes; otherwise TAO_ERR_ARG and nothing is accessed), the
+ * other must be device memory, both 16-byte aligned and `bytes` a multiple of 16.
+ * No counterpart in the reference (its operands are already on the device). */
+int tao_copy_host_to_device(void* dst, const void* host_src, size_t bytes, void* stream);
+int tao_copy_device_to_host(void* host_dst, const void* src, size_t bytes, void* stream);
+
 /* Decode step (one token for each of n_states requests) that allocates nothing:
  * same arguments and results as tao_stream_step with tokens = 1, but its scratch
  * lives in a static 4 MiB device array inside the library instead of a

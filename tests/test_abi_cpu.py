@@ -70,6 +70,15 @@ def test_host_validation_errors_without_gpu():
     assert lib.tao_stream_workspace_bytes(8, 1, 12, 64, 256, ctypes.byref(feat)) > 0
 
 
+def test_host_transfer_argument_checks_without_gpu():
+    """Misaligned or ragged host transfers are refused before any CUDA call."""
+    lib = _lib.lib()
+    assert lib.tao_copy_host_to_device(16, 24, 64, None) == _lib.TAO_ERR_ARG
+    assert lib.tao_copy_device_to_host(16, 32, 40, None) == _lib.TAO_ERR_ARG
+    assert lib.tao_copy_host_to_device(None, 32, 64, None) == _lib.TAO_ERR_ARG
+    assert b"16-byte" in lib.tao_last_error() or b"null" in lib.tao_last_error()
+
+
 def test_schedule_matches_reference_policy():
     cfg = index_only_page_memo()
     for completed in range(0, 80):

@@ -293,3 +293,55 @@ def test_batch_graph_decode_equals_eager():
     assert check_device() == 0
     assert len(stream._BatchGraph.cache) >= 1
     assert torch.equal(outs[False], outs[True])
+
+
+def test_host_transfers_by_the_sms():
+    """copy_to_device / copy_to_host move page-locked host bytes exactly; pageable
+    host memory is refused before anything is accessed; a decode step fed and read
+    back this way equals the one fed from device memory."""
+    import tao_memory_b200 as tb
+    from tao_memory_b200.presets import index_only_page_memo
+    from tao_memory_b200.stream import check_device
+    dev = torch.device("cuda")
+    host = torch.randint(0, 1 << 15, (5, 8, 1, 12, 64), dtype=torch.int16).view(torch.bfloat16).pin_memory()
+    d = torch.empty(host.shape, dtype=host.dtype, device=dev)
+    tb.copy_to_device(d, host)
+    back = torch.empty_like(host).pin_memory()
+    tb.copy_to_host(back, d)
+    torch.cuda.synchronize()
+    assert torch.equal(d.cpu().view(torch.int16), host.view(torch.int16))
+    assert torch.equal(back.view(torch.int16), host.view(torch.int16))
+    with pytest.raises(ValueError):
+        tb.copy_to_device(d, torch.from_numpy(host.view(torch.int16).numpy().copy()).view(torch.bfloat16))
+    from tao_memory_b200 import _lib
+    rc = _lib.lib().tao_copy_host_to_device(d.data_ptr(), torch.empty(64, dtype=torch.uint8).data_ptr(), 64,
+                                            torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.TAO_ERR_ARG                    # the C entry checks the pointer kind itself
+    # one decode step both ways
+    R, H, D, P = 2, 3, 64, 900
+    xs = [{k: t.to(dev) for k, t in make_inputs(1, P + 1, H, D, seed=90 + r)[0].items()} for r in range(R)]
+    fa, fb = xs[0]["fusion_a"], xs[0]["fusion_b"]
+    outs = []
+    for via_host in (False, True):
+        states = []
+        for r in range(R):
+            st = tb.new_state(r, index_only_page_memo())
+            tb.tao_attention_prefill(*(xs[r][k][:, :P] for k in KEYS[:3]), raw_q=xs[r]["raw_q"][:, :P],
+                                     raw_k=xs[r]["raw_k"][:, :P], fusion_a=fa, fusion_b=fb, alpha=0.3,
+                                     state=st, position=0)
+            states.append(st)
+        stack = torch.stack([torch.cat([xs[r][k][:, P:P + 1] for r in range(R)], 0) for k in KEYS])
+        if via_host:
+            pinned = stack.cpu().pin_memory()
+            stack = torch.empty_like(stack)
+            tb.copy_to_device(stack, pinned)
+        y, _ = tb.tao_attention_decode_batch(*stack[:3], raw_q=stack[3], raw_k=stack[4], fusion_a=fa,
+                                             fusion_b=fb, alpha=0.3, states=states)
+        if via_host:
+            res = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+            tb.copy_to_host(res, y)
+            torch.cuda.synchronize()
+            y = res
+        outs.append(y.cpu())
+    assert torch.equal(outs[0], outs[1])
+    assert check_device() == 0
