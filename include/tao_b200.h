@@ -41,7 +41,9 @@ extern "C" {
  * selects the read of the selected fines: 0 = normalised association read
  * (softmax and regularised-association writers, query_fresh_fine.py:8-49),
  * 1 = feature-mass read (feature-mass writer, association_writer.py:43-53 via
- * tao_stream.py:362-367); fine_read 1 is served by tao_stream_step only. */
+ * tao_stream.py:362-367); tao_decode_step serves fine_read 1 with its default
+ * decode kernel (variant 1) for up to 256 selected fines, tao_stream_decode_noalloc
+ * refuses it. */
 typedef struct TaoPolicy {
   int32_t fine_tokens;
   int32_t local_keep;

@@ -280,8 +280,10 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
   if (policy->route_period <= 0 || policy->layer_stagger < 0 || policy->budget_root_scale <= 0 ||
       policy->budget_offset < 0 || policy->route_cap <= 0)
     return fail(TAO_ERR_ARG, "invalid routing policy");
-  if (policy->fine_read != 0)
-    return fail(TAO_ERR_ARG, "the feature-mass read (policy.fine_read = 1) is served by tao_stream_step");
+  if (policy->fine_read != 0 && policy->fine_read != 1)
+    return fail(TAO_ERR_ARG, "policy.fine_read must be 0 or 1, got %d", policy->fine_read);
+  if (policy->fine_read == 1 && g_decode_variant != 1)
+    return fail(TAO_ERR_ARG, "the feature-mass read runs in the default decode kernel (variant 1)");
   for (const void* p : {q, k, v, raw_q, raw_k, fusion_a, fusion_b, (const void*)out, (const void*)workspace})
     if (!p) return fail(TAO_ERR_ARG, "null tensor pointer");
   for (const void* p : {q, k, v, raw_q, raw_k, (const void*)out})
@@ -307,6 +309,8 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
   }
   const int route_cap = policy->route_cap;
   if (mbound > route_cap) mbound = route_cap;
+  if (policy->fine_read == 1 && mbound > tao::kRouteCapMax)
+    return fail(TAO_ERR_CAPACITY, "feature-mass decode holds at most %d selected fines", tao::kRouteCapMax);
   // fine partials per (r, h): one per selected fine (warp kernel) or per group of fpc
   const int fpc = (g_decode_variant == 2) ? 1 : fpc_for(width);
   const int ms = (mbound + fpc - 1) / fpc;
@@ -336,6 +340,7 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
   a.local_part = reinterpret_cast<float*>(ws + L.local_part);
   a.fine_part = reinterpret_cast<float*>(ws + L.fine_part);
   a.pmax = pmax;
+  a.feature = policy->fine_read;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (g_graph_mode) refresh = seal = true;
   return width == 64 ? launch_decode<64>(a, ms, refresh, seal, s) : launch_decode<128>(a, ms, refresh, seal, s);

@@ -11,10 +11,19 @@
 //
 // Routing (refresh tokens) and sealing (window full) run as separate small
 // kernels that the host launches only on the steps that need them.
+//
+// Feature-mass read (StepArgs.feature, the feature-read writers): a fine item first
+// forms every selected fine's mass sum_d h_d exp(z_m,d) of its (r, h) (the z rows are
+// a few KB, L2-resident) and their total, then its own fines' channels
+// bf16(h * mass_m / total); its partial has no denominator and the combine rounds
+// the sum (association_writer.py:43-53).
 #pragma once
 #include "stream_kernels.cuh"
 
 namespace tao {
+
+// Feature-mass read: the host refuses batches whose route budget could exceed this.
+constexpr int kRouteCapMax = 256;
 
 struct FusedArgs {
   StepArgs s;        // states, shapes, inputs, outputs, policy, partial buffers
@@ -142,6 +151,7 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   __shared__ float qv[D];
   __shared__ float red[128 + 8];
   __shared__ float chs[Cfg::FPC * D];
+  __shared__ float mass_s[kRouteCapMax];  // feature read: mass of every selected fine
   __shared__ int last_rh;
   const int per = Cfg::KB + f.ms;
   const int total = a.R * a.H * per;
@@ -257,7 +267,28 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
         // channels do not depend on the matrices in flight: compute them first
         if (warp == 0) softmax_row<D>(a.raw_q + src, qv, lane);
         __syncthreads();
-        for (int x = warp; x < nf; x += 4) {
+        if (a.feature) {
+          // masses of all n_route selected fines (each item forms the same total)
+          const int32_t* all = st.route_ids + (long long)it.h * st.route_cap;
+          const int nm = min(n_route, kRouteCapMax);
+          for (int m = warp; m < nm; m += 4) {
+            const bf16* zr = fz + (long long)all[m] * D;
+            float sm = 0.f;
+#pragma unroll
+            for (int j = 0; j < D / 32; ++j) sm += __fmul_rn(qv[lane + 32 * j], expf(bf(zr[lane + 32 * j])));
+            sm = warp_sum(sm);
+            if (lane == 0) mass_s[m] = sm;
+          }
+          __syncthreads();
+          float tot = 0.f;
+          for (int m = 0; m < nm; ++m) tot += mass_s[m];
+          for (int idx = tid; idx < nf * D; idx += 128) {
+            const int x = idx / D, d = idx % D;
+            chs[x * D + d] = rb(__fmul_rn(__fdiv_rn(mass_s[m0 + x], tot), qv[d]));
+          }
+          if (tid < nf) red[tid] = 0.f;
+        }
+        for (int x = warp; x < nf && !a.feature; x += 4) {
           const int id = ids[x], page = id / kGroup;
           float sum = 0.f;
           for (int d = lane; d < D; d += 32) {
@@ -377,7 +408,7 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
               den += vd[u];
             }
         }
-        const float fine = rb(__fdiv_rn(rb(acc), rb(den)));
+        const float fine = a.feature ? rb(acc) : rb(__fdiv_rn(rb(acc), rb(den)));
         const float qq = lo_f(fin[0]);
         const float s0 = rb(__fadd_rn(rb(__fmul_rn(lo_f(fin[1]), qq)), lo_f(fin[2])));  // + 0 (middle term) is exact
         const float s2 = rb(__fadd_rn(rb(__fmul_rn(hi_f(fin[1]), qq)), hi_f(fin[2])));

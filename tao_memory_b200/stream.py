@@ -530,7 +530,7 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
         args.pos[i] = st.position
     ws = _Workspace.get(dev, args.nbytes)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    if w == 1 and not feature:   # the feature-mass read serves w == 1 through tao_stream_step
+    if w == 1:
         _lib.check(lib.tao_decode_step(args.ptrs.data_ptr(), r, args.pos, args.layers, args.cap,
                                        ctypes.byref(args.policy), heads, width,
                                        *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),

@@ -54,15 +54,19 @@ def test_host_validation_errors_without_gpu():
     assert rc == _lib.TAO_ERR_ARG
     assert lib.tao_stream_workspace_bytes(8, 1, 12, 64, 256, ctypes.byref(pol)) > 0
     assert lib.tao_stream_workspace_bytes(8, 1, 12, 96, 256, ctypes.byref(pol)) == 0
-    # the feature-mass read (fine_read = 1) is served by tao_stream_step; the decode
-    # entry points refuse it, and the stream entry refuses other read modes
+    # the feature-mass read (fine_read = 1): the no-alloc decode refuses it, the
+    # other decode kernel variants refuse it, and unknown read modes are refused
     feat = _lib.TaoPolicy(256, 512, 8, 24, 2, 2, 2, 256, 1)
     layer = (ctypes.c_int32 * 1)(0)
-    rc = lib.tao_decode_step(16, 1, pos, layer, cap, ctypes.byref(feat), 2, 64, *([16] * 7), 0.5, 16, 256,
-                             1 << 20, None)
-    assert rc == _lib.TAO_ERR_ARG and b"tao_stream_step" in lib.tao_last_error()
     rc = lib.tao_stream_decode_noalloc(16, 1, pos, cap, ctypes.byref(feat), 2, 64, *([16] * 7), 0.5, 16, None)
     assert rc == _lib.TAO_ERR_ARG
+    lib.tao_decode_variant(2)
+    try:
+        rc = lib.tao_decode_step(16, 1, pos, layer, cap, ctypes.byref(feat), 2, 64, *([16] * 7), 0.5, 16, 256,
+                                 1 << 20, None)
+    finally:
+        lib.tao_decode_variant(1)
+    assert rc == _lib.TAO_ERR_ARG and b"variant 1" in lib.tao_last_error()
     odd = _lib.TaoPolicy(256, 512, 8, 24, 2, 2, 2, 256, 2)
     rc = lib.tao_stream_step(1, 1, pos, cap, ctypes.byref(odd), 1, 2, 64, *([16] * 7), 0.5, 16, 256, 1 << 20, None)
     assert rc == _lib.TAO_ERR_ARG
