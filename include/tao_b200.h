@@ -160,7 +160,8 @@ int tao_stream_check(void* workspace, int* flags, void* stream);
  * round trip over the host link instead of a copy engine's setup latency.  The host
  * buffer must be page-locked with a device mapping (checked with
  * cudaPointerGetAttributes; otherwise TAO_ERR_ARG and nothing is accessed), the
- * other must be device memory, both 16-byte aligned and `bytes` a multiple of 16.
+ * other must be device memory of the calling thread's current device (where the
+ * kernel runs), both 16-byte aligned and `bytes` a multiple of 16.
  * No counterpart in the reference (its operands are already on the device). */
 int tao_copy_host_to_device(void* dst, const void* host_src, size_t bytes, void* stream);
 int tao_copy_device_to_host(void* host_dst, const void* src, size_t bytes, void* stream);

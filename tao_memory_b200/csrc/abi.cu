@@ -206,7 +206,7 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
   if (refresh) {
     const size_t smem = (size_t)D * 4 + (size_t)a.pmax * 4 + (size_t)(8 * a.pmax + 8) * 8 + (size_t)a.pmax * 8;
     if ((rc = set_smem(decode_route_kernel<D>, smem))) return rc;
-    decode_route_kernel<D><<<a.R * a.H, 256, smem, s>>>(a);
+    decode_route_kernel<D><<<a.R * a.H, 1024, smem, s>>>(a);
     if ((rc = check_launch("decode_route_kernel"))) return rc;
   }
   FusedArgs f{};

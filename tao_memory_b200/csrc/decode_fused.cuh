@@ -1071,7 +1071,9 @@ __global__ void __launch_bounds__(256) decode_warp_kernel(FusedArgs f) {
 
 // Routing on refresh tokens: writes the state's route arrays directly.
 template <int D>
-__global__ void __launch_bounds__(256) decode_route_kernel(StepArgs a) {
+// 1024 threads: the page and candidate loops are latency chains of row loads (cold
+// after other work evicted them), so more warps cut the serial iterations per warp.
+__global__ void __launch_bounds__(1024) decode_route_kernel(StepArgs a) {
   const int r = blockIdx.x / a.H, h = blockIdx.x % a.H;
   TaoState& st = *a.states[r];
   const long long t = st.position;

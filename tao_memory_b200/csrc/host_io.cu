@@ -57,6 +57,12 @@ int checked_device(const void* p, const char** why) {
     *why = "device buffer must be device memory";
     return 0;
   }
+  int current = -1;
+  if (cudaGetDevice(&current) != cudaSuccess || attr.device != current) {
+    cudaGetLastError();
+    *why = "device buffer is not on the calling thread's current device";
+    return 0;
+  }
   return 1;
 }
 

@@ -30,12 +30,14 @@ def _check(host, dev):
 def copy_to_device(dev, host):
     """dev <- host (page-locked); returns dev."""
     nbytes, stream = _check(host, dev)
-    _lib.check(_lib.lib().tao_copy_host_to_device(dev.data_ptr(), host.data_ptr(), nbytes, stream))
+    with torch.cuda.device(dev.device):
+        _lib.check(_lib.lib().tao_copy_host_to_device(dev.data_ptr(), host.data_ptr(), nbytes, stream))
     return dev
 
 
 def copy_to_host(host, dev):
     """host (page-locked) <- dev; returns host (valid once the stream has reached the copy)."""
     nbytes, stream = _check(host, dev)
-    _lib.check(_lib.lib().tao_copy_device_to_host(host.data_ptr(), dev.data_ptr(), nbytes, stream))
+    with torch.cuda.device(dev.device):
+        _lib.check(_lib.lib().tao_copy_device_to_host(host.data_ptr(), dev.data_ptr(), nbytes, stream))
     return host
