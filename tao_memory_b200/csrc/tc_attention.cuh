@@ -129,7 +129,7 @@ TAO_DEVI bool wait_or_abort(uint64_t* bar, uint32_t phase, int* err, volatile in
   if (err) atomicOr(err, kErrWaitTimeout);
   return false;
 }
-// Warp-uniform verdict of wait_or_abort (tcgen05.ld/st need the whole warp).
+// Warp-uniform outcome of wait_or_abort (tcgen05.ld/st need the whole warp).
 TAO_DEVI bool warp_wait(uint64_t* bar, uint32_t phase, int* err, volatile int* abort) {
   return __all_sync(0xffffffffu, wait_or_abort(bar, phase, err, abort));
 }
