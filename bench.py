@@ -1,24 +1,38 @@
 #!/usr/bin/env python
-"""Benchmark of the TaoMemory decode hot path on B200.
+"""Benchmark of the TaoMemory attention hot path on B200.
 
-Workload ("decode128k"): per GPU, 8 independent requests (one state each), H=12,
-D=64, bf16, each prefilled with 131,072 synthetic tokens ~N(0,1) through the
-public prefill API, then decoded one token per request per step.  A step is one
-decode token for every request on the rank (weak scaling: 8 requests per GPU).
+Headline workload ("decode128k"): per GPU, 8 independent
+requests (one state each), H=12, D=64, bf16, each prefilled with 131,072
+synthetic tokens ~N(0,1) through the public prefill API, then decoded one token
+per request per step for the config's 256 decode steps.  A step is one decode
+token for every request on the rank (weak scaling: 8 requests per GPU); the
+timed window is the last K of the 256 steps, so it holds the seal at position
+131,327 and the route refreshes before it.
 
 Reported (one JSON line on rank 0):
 * value      -- decode tokens/s over all ranks, inputs resident in HBM, steps
                 launched through the C ABI (BatchDecoder), L2 flushed between
                 timed steps (1 GiB memset outside the timed window);
 * e2e        -- the same metric through the public Python API
-                (tao_attention_decode_batch) with the step's inputs copied from
-                pinned host memory and the output copied back inside the window;
-* roofline   -- achieved HBM GB/s of the main decode kernel (local attention +
-                selected fine read) = algorithmic bytes / CUDA-event duration;
-* cpu_baseline -- the CPU oracle (reference port) on a bounded sample.
+                (tao_attention_decode_batch) with the step's inputs handed over in
+                page-locked host memory and the output read back to host memory;
+                host clock per step, the device synchronised at the end of every
+                step (a caller that needs each token's output before the next);
+* parity     -- the timed steps' outputs and route ids against the CPU oracle
+                continuing the same states (exported before the window) on the
+                same inputs: every element, every request, every head;
+* roofline   -- achieved HBM GB/s of the main decode kernel = algorithmic bytes /
+                CUDA-event duration, against the measured copy bandwidth;
+* cpu_baseline -- the CPU oracle (reference port) on a bounded sample;
+* train8k    -- BASELINE.json config 2 (tao_attention forward + backward, B4 T8192
+                H12 D64 bf16) with its own value / e2e / roofline / cpu_baseline.
+With N > 1 ranks every rank decodes its own 8 requests and the step's outputs are
+gathered to rank 0 over NCCL on a side stream (tao_memory_b200.shard).
 
 ``--impl reference`` times the reference's algorithm on the host CPU (the oracle
-port in oracle/tao_oracle.py) on the same config and prints the same line.
+port in oracle/tao_oracle.py) on the same config and prints the same line, with a
+``reference_triton`` object: the unmodified reference (installed in baseline/_ref)
+running its own Triton path on one B200.
 """
 
 import argparse
@@ -36,21 +50,31 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s @128K ctx"
 UNIT = "tok/s"
-REQUESTS, HEADS, WIDTH, CONTEXT, LAYER = 8, 12, 64, 131072, 0
+REQUESTS, HEADS, WIDTH, CONTEXT, LAYER, DECODE_STEPS = 8, 12, 64, 131072, 0, 256
 L2_FLUSH_BYTES = 1 << 30   # also keeps the GPU busy while the host enqueues the step
 L2_CLEAN_BYTES = 1 << 28   # read after the memset: its dirty lines are written back before timing
+# DRAM bytes (read + write) of one decode_fused_kernel launch at this workload, from
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none \
+#       -k regex:decode_fused_kernel -s 8 -c 3 python bench.py --steps 3 --warmup 3 --no-train
+# (profiles/decode_fused_kernel_decode128k.md); None until captured for this build.
+DECODE_TRAFFIC_BYTES = None
+# The same for read_bwd_kernel in the train8k workload
+#   (profiles/read_bwd_kernel_train8k.md, capture command there).
+READ_BWD_TRAFFIC_BYTES = None
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=248)
-    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--requests", type=int, default=REQUESTS)
     ap.add_argument("--context", type=int, default=CONTEXT)
     ap.add_argument("--cpu-sample-steps", type=int, default=4)
     ap.add_argument("--workload", default="decode128k", choices=["decode128k", "train8k"])
+    ap.add_argument("--no-train", action="store_true", help="leave the nested train8k leg out")
+    ap.add_argument("--no-parity", action="store_true", help="leave the oracle parity check out")
     ap.add_argument("--decode-variant", type=int, default=None,
                     help="decode kernel of tao_decode_step (0 persistent, 1 CTA/item, 2 warp/item)")
     return ap.parse_args()
@@ -67,22 +91,9 @@ def measured_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return p, "measured"
     except Exception:
-        return 6650.0, "fallback"
-
-
-def profile_traffic():
-    """Per-launch DRAM bytes of the main decode kernel from the committed ncu
-    summary (line 'traffic_bytes_per_launch: N'), or None."""
-    path = os.path.join(ROOT, "profiles", "decode_fused_kernel_decode128k.md")
-    try:
-        for line in open(path):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                return int(float(line.split(":", 1)[1]))
-    except OSError:
-        pass
-    return None
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
 class ClockSampler:
@@ -134,8 +145,33 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
+class Events:
+    """CUDA events through the library (recorded on the launching stream)."""
+
+    def __init__(self, lib, n):
+        from tao_memory_b200 import _lib
+        self.lib, self._lib = lib, _lib
+        self.ev = []
+        for _ in range(n):
+            e = ctypes.c_void_p()
+            _lib.check(lib.tao_event_create(ctypes.byref(e)))
+            self.ev.append(e)
+
+    def __getitem__(self, i):
+        return self.ev[i]
+
+    def elapsed(self, a, b):
+        ms = ctypes.c_float()
+        self._lib.check(self.lib.tao_event_elapsed(self.ev[a], self.ev[b], ctypes.byref(ms)))
+        return ms.value
+
+    def close(self):
+        for e in self.ev:
+            self.lib.tao_event_destroy(e)
+
+
 # ---------------------------------------------------------------------------
-# B200 arm
+# B200 arm: decode128k
 # ---------------------------------------------------------------------------
 
 def prefill_states(tb, preset, n, context, device, seed):
@@ -162,13 +198,45 @@ def prefill_states(tb, preset, n, context, device, seed):
     return states, fa, fb
 
 
+def decode_parity(exported, inputs, outs, fa, fb, states):
+    """Continue the exported states on the CPU oracle with the timed steps' inputs;
+    compare every output element and the final route ids with the GPU's."""
+    import torch
+    from oracle import tao_oracle as o
+    torch.set_num_threads(os.cpu_count() or 1)
+    fa, fb = fa.cpu(), fb.cpu()
+    xs = inputs.cpu()                 # [K, 5, R, 1, H, D]
+    got = outs.float().cpu()          # [K, R, 1, H, D]
+    bad, worst, elems, route_bad = 0, 0.0, 0, 0
+    hosts = []
+    for r, snap in enumerate(exported):
+        st = o.OracleStream.from_export(snap)
+        ref = torch.cat([st.step(*(xs[i, j, r:r + 1] for j in range(5)), fa, fb, 0.5)
+                         for i in range(xs.shape[0])], 1).float()          # [1, K, H, D]
+        mine = got[:, r].permute(1, 0, 2, 3)                                # [1, K, H, D]
+        err = (mine - ref).abs()
+        bad += int((err > 2e-2 + 2e-2 * ref.abs()).sum())
+        worst = max(worst, err.max().item())
+        elems += ref.numel()
+        gpu_ids = states[r].export()["route_ids"][1].cpu()
+        route_bad += int(not torch.equal(gpu_ids, st.route_ids[1]))
+        hosts.append(st)
+    return {"checked": "every output element of the timed steps, all requests and heads, and the "
+                       "final route ids, against oracle/tao_oracle.py continuing the states "
+                       "exported before the window on the same inputs",
+            "requests": len(exported), "steps": int(xs.shape[0]), "elements": elems,
+            "tolerance": "|a-b| <= 2e-2 + 2e-2|b|", "out_of_tolerance": bad,
+            "max_abs_err": round(worst, 6), "route_mismatches": route_bad}, hosts
+
+
 def run_b200(args, world, rank, local):
     import torch
     import torch.distributed as dist
     import tao_memory_b200 as tb
     from tao_memory_b200 import _lib
     from tao_memory_b200.presets import index_only_page_memo
-    from tao_memory_b200.stream import BatchDecoder, decode_bytes
+    from tao_memory_b200.shard import OutputGather
+    from tao_memory_b200.stream import BatchDecoder, decode_bytes, is_refresh, window_start
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -183,19 +251,26 @@ def run_b200(args, world, rank, local):
     torch.cuda.synchronize()
     prefill_s = time.time() - t0
 
-    gen = torch.Generator(device=device).manual_seed(10_000 + rank)
+    # decode schedule: [lead untimed][e2e: E2E_WARM + K][warm-up W][timed K], ending at the
+    # config's last decode step (256) when it fits
     E2E_WARM = 3                      # untimed e2e calls: eager, graph capture, first replay
-    total_steps = W + 2 * K + E2E_WARM
+    n_e2e = E2E_WARM + K
+    lead = max(0, DECODE_STEPS - (n_e2e + W + K))
+    total_steps = lead + n_e2e + W + K
+    gen = torch.Generator(device=device).manual_seed(10_000 + rank)
     inputs = torch.randn(total_steps, 5, R, 1, HEADS, WIDTH, device=device, generator=gen).to(torch.bfloat16)
-    out = torch.empty(R, 1, HEADS, WIDTH, dtype=torch.bfloat16, device=device)
+    outs = torch.empty(K, R, 1, HEADS, WIDTH, dtype=torch.bfloat16, device=device)
+    scratch_out = torch.empty(R, 1, HEADS, WIDTH, dtype=torch.bfloat16, device=device)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     clean = torch.ones(L2_CLEAN_BYTES // 4, dtype=torch.float32, device=device)
+    gather = OutputGather(dist.group.WORLD if world > 1 else None, (R, 1, HEADS, WIDTH), torch.bfloat16, device)
 
     def flush_l2():
         """Evict L2 outside the timed window: write 1 GiB, then read 256 MB of clean
         lines so the memset's dirty lines are written back now, not by the step."""
         flush.zero_()
         clean.sum()
+
     dec = BatchDecoder(states, fa, fb, 0.5, device)
     dec.reserve(total_steps + 1)
 
@@ -203,99 +278,89 @@ def run_b200(args, world, rank, local):
         x = inputs[i]
         return [x[j].data_ptr() for j in range(5)]
 
-    for i in range(W):
-        dec.step(*step_ptrs(i), out.data_ptr())
+    for i in range(lead):
+        dec.step(*step_ptrs(i), scratch_out.data_ptr())
     torch.cuda.synchronize()
     dec.check()
-
-    def ev():
-        e = ctypes.c_void_p()
-        _lib.check(lib.tao_event_create(ctypes.byref(e)))
-        return e
-
-    starts, stops = [ev() for _ in range(K)], [ev() for _ in range(K)]
-    mstarts, mstops = [ev() for _ in range(K)], [ev() for _ in range(K)]
-    algo_bytes = []
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    if world > 1:
-        dist.barrier()
+
+    # ---- e2e: public API, operands in page-locked host memory, output back to host,
+    # host clock per step with the device synchronised at the end of each step
+    host_in = inputs[lead:lead + n_e2e].cpu().pin_memory()
+    host_x = torch.empty(5, R, 1, HEADS, WIDTH, dtype=torch.bfloat16).pin_memory()
+    host_out = torch.empty(R, 1, HEADS, WIDTH, dtype=torch.bfloat16).pin_memory()
+    e2e_s = []
+    for i in range(n_e2e):
+        flush_l2()
+        torch.cuda.synchronize()
+        if world > 1 and i == E2E_WARM:
+            dist.barrier()
+        t_a = time.perf_counter()
+        host_x.copy_(host_in[i])                                  # the caller's bytes into its buffer
+        tb.tao_attention_decode_batch(host_x[0], host_x[1], host_x[2], raw_q=host_x[3], raw_k=host_x[4],
+                                      fusion_a=fa, fusion_b=fb, alpha=0.5, states=states, out=host_out)
+        torch.cuda.current_stream(device).synchronize()
+        e2e_s.append(time.perf_counter() - t_a)
+    e2e_s = e2e_s[E2E_WARM:]
+    dec._sync_ptrs()
+
+    # ---- warm-up and the timed window (C ABI, inputs resident in HBM)
+    for i in range(W):
+        dec.step(*step_ptrs(lead + n_e2e + i), scratch_out.data_ptr())
     torch.cuda.synchronize()
-    torch.cuda.nvtx.range_push("timed_decode")
-    # algorithmic bytes of each timed step, from the cursors it will run at
+    dec.check()
+    exported = [st.export() for st in states] if (rank == 0 and not args.no_parity) else None
+    ev = Events(lib, 4 * K)
     base_pos = [st.position for st in states]
+    algo_bytes = []
     for i in range(K):
         for st, p in zip(states, base_pos):
             st.position = p + i
         algo_bytes.append(decode_bytes(states))
     for st, p in zip(states, base_pos):
         st.position = p
+    timed0 = lead + n_e2e + W
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("timed_decode")
     for i in range(K):
         flush_l2()                        # evict L2 (outside the timed window)
-        lib.tao_event_record(starts[i], stream)
-        lib.tao_stream_profile_next(mstarts[i], mstops[i])
-        dec.step(*step_ptrs(W + i), out.data_ptr())
-        lib.tao_event_record(stops[i], stream)
+        lib.tao_event_record(ev[4 * i], stream)
+        lib.tao_stream_profile_next(ev[4 * i + 2], ev[4 * i + 3])
+        dec.step(*step_ptrs(timed0 + i), outs[i].data_ptr())
+        gather.start(outs[i])            # side stream; overlaps the next step
+        lib.tao_event_record(ev[4 * i + 1], stream)
+    gather.finish()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     dec.check()
-
-    def elapsed(a, b):
-        ms = ctypes.c_float()
-        _lib.check(lib.tao_event_elapsed(a, b, ctypes.byref(ms)))
-        return ms.value
-
-    step_ms = [elapsed(a, b) for a, b in zip(starts, stops)]
-    main_ms = [elapsed(a, b) for a, b in zip(mstarts, mstops)]
-    # one fused kernel per step, plus routing on refresh tokens and a seal when a window fills
-    from tao_memory_b200.stream import is_refresh, window_start
+    clocks.stop()
+    step_ms = [ev.elapsed(4 * i, 4 * i + 1) for i in range(K)]
+    main_ms = [ev.elapsed(4 * i + 2, 4 * i + 3) for i in range(K)]
+    ev.close()
     cfg = states[0].config
-    p0 = args.context + W
+    p0 = base_pos[0]
     gpu_launches = sum(1 + any(is_refresh(p0 + i, st.layer_index, cfg) for st in states)
                        + any(p0 + i + 1 - window_start(p0 + i) == 768 for st in states) for i in range(K))
-    for e in starts + stops + mstarts + mstops:
-        lib.tao_event_destroy(e)
+    seals = sum(p0 + i + 1 - window_start(p0 + i) == 768 for i in range(K))
+    refreshes = sum(is_refresh(p0 + i, LAYER, cfg) for i in range(K))
     total_ms = sum(step_ms)
+    e2e_ms = sum(e2e_s) * 1e3
 
-    # ---- e2e: public API, pinned host inputs in, output back to host
-    host_in = inputs[W + K:W + 2 * K + E2E_WARM].cpu().pin_memory()
-    host_out = torch.empty(R, 1, HEADS, WIDTH, dtype=torch.bfloat16).pin_memory()
-    stage = torch.empty(5, R, 1, HEADS, WIDTH, dtype=torch.bfloat16, device=device)
-    e_start = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    e_stop = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    def e2e_step(i):
-        tb.copy_to_device(stage, host_in[i])
-        y, _ = tb.tao_attention_decode_batch(stage[0], stage[1], stage[2], raw_q=stage[3], raw_k=stage[4],
-                                             fusion_a=fa, fusion_b=fb, alpha=0.5, states=states, out=out)
-        tb.copy_to_host(host_out, y)
-
-    for i in range(E2E_WARM):
-        e2e_step(i)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    for i in range(K):
-        flush_l2()
-        e_start[i].record()
-        e2e_step(E2E_WARM + i)
-        e_stop[i].record()
-    torch.cuda.synchronize()
-    clocks.stop()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in zip(e_start, e_stop))
-
-    # ---- max over ranks
     tot = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
     total_ms, e2e_ms = tot.tolist()
     tokens = world * R * K
 
-    peak, peak_kind = measured_peaks()
+    peaks, peak_kind = measured_peaks()
+    peak = float(peaks["hbm_gbs"])
     achieved = sum(algo_bytes) / (sum(main_ms) * 1e-3) / 1e9
-    traffic = profile_traffic()
     result = {
         "metric": METRIC, "value": round(tokens / (total_ms * 1e-3), 1), "unit": UNIT,
         "n_gpus": world, "steps": K, "warmup": W,
@@ -303,22 +368,33 @@ def run_b200(args, world, rank, local):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic ~N(0,1), seeded",
         "config": {"workload": "decode128k (BASELINE.json config 4)", "requests_per_gpu": R,
                    "context": args.context, "heads": HEADS, "head_dim": WIDTH, "layer_index": LAYER,
-                   "preset": "index_only_page_memo(graph=True)", "l2": "flushed between timed steps (1 GiB memset, then a 256 MB read so the memset's dirty lines are written back outside the timed window)",
+                   "preset": "index_only_page_memo(graph=True)",
+                   "timed_positions": [p0, p0 + K - 1], "seals_in_window": seals,
+                   "refreshes_in_window": refreshes,
+                   "l2": "flushed between timed steps (1 GiB memset, then a 256 MB read so the memset's "
+                         "dirty lines are written back outside the timed window)",
+                   "parallelism": f"{world} GPU(s), requests sharded, outputs gathered to rank 0 over NCCL"
+                                  if world > 1 else "1 GPU",
                    "prefill_s": round(prefill_s, 2),
                    "prefill_tok_s": round(R * args.context / prefill_s, 1)},
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": 5 * R * HEADS * WIDTH * 2,
-                "d2h_bytes_per_step": R * HEADS * WIDTH * 2},
-        "roofline": {"bound": "hbm", "kernel": "tao_decode_step main kernel (variant %s)" % (1 if args.decode_variant is None else args.decode_variant),
+                "d2h_bytes_per_step": R * HEADS * WIDTH * 2,
+                "timing": "host clock per step: caller's bytes into its page-locked buffer, "
+                          "tao_attention_decode_batch (host operands; one captured graph: copy in, "
+                          "decode, copy out), stream synchronised; max over ranks",
+                "ms_per_step_median": round(statistics.median(e2e_s) * 1e3, 4)},
+        "roofline": {"bound": "hbm", "kernel": "decode_fused_kernel (tao_decode_step main kernel, variant %s)"
+                     % (1 if args.decode_variant is None else args.decode_variant),
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind + " (copy bandwidth)",
                      "algorithmic_bytes_per_launch": int(statistics.mean(algo_bytes)),
                      "kernel_ms_mean": round(statistics.mean(main_ms), 5),
-                     "traffic": traffic},
+                     "traffic": DECODE_TRAFFIC_BYTES},
         "gpu_launches": gpu_launches,
         "clocks": clocks.summary(),
     }
-    return result, states
+    return result, states, exported, inputs[timed0:timed0 + K], outs, fa, fb
 
 
 # ---------------------------------------------------------------------------
@@ -370,47 +446,18 @@ def time_oracle_decode(states, steps, seed, budget_s=None):
     return done, time.perf_counter() - t0
 
 
-def cpu_baseline_from_gpu(states, sample_steps):
-    """Time the CPU oracle on a bounded sample of the same workload: the GPU
-    states are exported and continued on the host cores."""
+def cpu_baseline_decode(host_states, sample_steps):
+    """Time the CPU oracle on a bounded sample of the same workload: GPU states
+    exported and continued on the host cores."""
     import torch
-    from oracle import tao_oracle as o
     torch.set_num_threads(os.cpu_count() or 1)
-    picked = states[:2]
-    host = [o.OracleStream.from_export(st.export()) for st in picked]
-    time_oracle_decode(host, 2, seed=7)                         # warm-up
-    n, secs = time_oracle_decode(host, sample_steps * len(host), seed=8, budget_s=30)
+    picked = host_states[:2]
+    time_oracle_decode(picked, 2, seed=7)                       # warm-up
+    n, secs = time_oracle_decode(picked, sample_steps * len(picked), seed=8, budget_s=30)
     return {"value": round(n / secs, 2), "unit": UNIT, "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{n} decode tokens over {len(host)} exported 128K-context requests "
+            "sample": f"{n} decode tokens over {len(picked)} exported 128K-context requests "
                       f"(H{HEADS} D{WIDTH}), oracle/tao_oracle.py on the host CPU"}
-
-
-def run_reference(args):
-    import torch
-    torch.set_num_threads(os.cpu_count() or 1)
-    t0 = time.time()
-    states = [synthetic_oracle_state(LAYER, args.context, seed=100 + r) for r in range(args.requests)]
-    setup_s = time.time() - t0
-    time_oracle_decode(states, max(args.warmup, 1), seed=1)
-    n, secs = time_oracle_decode(states, args.steps, seed=2, budget_s=240)
-    value = n / secs
-    cores = torch.get_num_threads()
-    return {
-        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus,
-        "steps": n, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / n, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic ~N(0,1), seeded", "impl": "reference",
-        "config": {"workload": "decode128k (BASELINE.json config 4)", "requests": args.requests,
-                   "context": args.context, "heads": HEADS, "head_dim": WIDTH,
-                   "preset": "index_only_page_memo", "step": "one decode token of one request (round robin)",
-                   "setup_s": round(setup_s, 1)},
-        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{n} decode tokens round-robin over {args.requests} synthetic "
-                                   f"128K-context states (oracle/tao_oracle.py: the reference's "
-                                   f"algorithm restated in PyTorch CPU ops)"},
-        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
 
 
 # ---------------------------------------------------------------------------
@@ -426,6 +473,21 @@ def local_attention_flops(tokens, heads, width, batch):
         lo = max(0, 256 * (t // 256) - 512)
         total += t - lo + 1
     return 4 * width * total * heads * batch
+
+
+def read_backward_flops(tokens, heads, width, batch, cfg):
+    """Algorithmic FLOPs of the selected-read backward: every query of 256-query tile t
+    selects exactly M(t) fines, and each (query, fine) pair costs dA = gn.C^T and its
+    share of dC = A^T.gn, 2 x 2 x width^2 FLOPs."""
+    from tao_memory_b200.config import routed_counts
+    pairs = 0
+    for tile in range((tokens + 255) // 256):
+        visible = max(0, tile - 2)
+        if visible == 0:
+            continue
+        m = routed_counts(visible // 8, visible % 8, cfg)[2]
+        pairs += min(256, tokens - tile * 256) * m
+    return 4 * width * width * pairs * heads * batch
 
 
 def train_inputs(device, seed, batch=TB, tokens=TT):
@@ -460,18 +522,12 @@ def run_train_bench(args, world, rank, local):
         out.backward(grad)
         return out
 
-    K, W = args.steps, args.warmup
+    K, W = args.steps, max(args.warmup, 3)
     for _ in range(W):
         step()
     torch.cuda.synchronize()
-
-    def ev():
-        e = ctypes.c_void_p()
-        _lib.check(lib.tao_event_create(ctypes.byref(e)))
-        return e
-
     stream = torch.cuda.current_stream(device).cuda_stream
-    starts, stops, a0, a1, r0, r1 = ([ev() for _ in range(K)] for _ in range(6))
+    ev = Events(lib, 6 * K)
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
@@ -480,30 +536,25 @@ def run_train_bench(args, world, rank, local):
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_push("timed_train")
     for i in range(K):
-        lib.tao_event_record(starts[i], stream)
-        lib.tao_stream_profile_next(a0[i], a1[i])        # forward: local attention kernel
+        lib.tao_event_record(ev[6 * i], stream)
+        lib.tao_stream_profile_next(ev[6 * i + 2], ev[6 * i + 3])   # forward: local attention kernel
         for t in leaves:
             t.grad = None
         out = tb.tao_attention(leaves[0], leaves[1], leaves[2], raw_q=leaves[3], raw_k=leaves[4],
                                fusion_a=leaves[5], fusion_b=leaves[6], alpha=alpha, config=cfg)
-        lib.tao_stream_profile_next(r0[i], r1[i])        # backward: selected-read backward kernel
+        lib.tao_stream_profile_next(ev[6 * i + 4], ev[6 * i + 5])   # backward: selected-read backward
         out.backward(grad)
-        lib.tao_event_record(stops[i], stream)
+        lib.tao_event_record(ev[6 * i + 1], stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
-
-    def elapsed(a, b):
-        ms = ctypes.c_float()
-        _lib.check(lib.tao_event_elapsed(a, b, ctypes.byref(ms)))
-        return ms.value
-
-    step_ms = [elapsed(a, b) for a, b in zip(starts, stops)]
-    attn_ms = [elapsed(a, b) for a, b in zip(a0, a1)]
-    rbwd_ms = [elapsed(a, b) for a, b in zip(r0, r1)]
+    step_ms = [ev.elapsed(6 * i, 6 * i + 1) for i in range(K)]
+    attn_ms = [ev.elapsed(6 * i + 2, 6 * i + 3) for i in range(K)]
+    rbwd_ms = [ev.elapsed(6 * i + 4, 6 * i + 5) for i in range(K)]
+    ev.close()
     # e2e: operands from pinned host memory each step, loss scalar back to the host.
     # The next step's host->device copies run on a copy stream into the other half of
     # a double buffer while this step computes (an input pipeline); every step's
-    # copies and its loss read-back are inside the timed window.
+    # copies and its loss read-back are inside the timed window (host clock).
     host = [t.detach().cpu().pin_memory() for t in x] + [grad.cpu().pin_memory()]
     bufs = [[torch.empty_like(h, device=device) for h in host] for _ in range(2)]
     copy_stream = torch.cuda.Stream(device)
@@ -519,10 +570,10 @@ def run_train_bench(args, world, rank, local):
                 d.copy_(h, non_blocking=True)
             ready[i % 2].record(copy_stream)
 
-    e_s = [torch.cuda.Event(enable_timing=True)]
-    e_e = [torch.cuda.Event(enable_timing=True)]
     torch.cuda.synchronize()
-    e_s[0].record(main)
+    if world > 1:
+        dist.barrier()
+    t_a = time.perf_counter()
     stage_inputs(0)
     for i in range(K):
         if i + 1 < K:
@@ -535,10 +586,9 @@ def run_train_bench(args, world, rank, local):
         loss.backward()
         loss_host.copy_(loss.detach(), non_blocking=True)
         free[i % 2].record(main)
-    e_e[0].record(main)
     torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t_a) * 1e3
     clocks.stop()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in zip(e_s, e_e))
     total_ms = sum(step_ms)
     tot = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
@@ -551,11 +601,9 @@ def run_train_bench(args, world, rank, local):
     rb_achieved = rb_flops / (statistics.mean(rbwd_ms) * 1e-3) / 1e12
     step_flops = 260.9e9  # per step, fwd + bwd = 3 x the forward's 86.96 GFLOP (config 2 work count)
     step_achieved = step_flops / (total_ms / K * 1e-3) / 1e12
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        peak, kind = float(peaks["bf16_tflops_sustained"]), "measured (sustained)"
-    except Exception:
-        peak, kind = 1400.0, "fallback (sustained)"
+    peaks, kind = measured_peaks()
+    peak = float(peaks["bf16_tflops_sustained"])
+    kind += " (cuBLAS bf16, sustained)"
     return {
         "metric": "train fwd+bwd tokens/s @8K", "value": round(tokens / (total_ms * 1e-3), 1),
         "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -563,16 +611,18 @@ def run_train_bench(args, world, rank, local):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic ~N(0,1), seeded",
         "config": {"workload": "train8k (BASELINE.json config 2)", "batch": TB, "seq_len": TT,
                    "heads": TH, "head_dim": TD, "alpha": "U(0,1) per head",
-                   "preset": "index_only_page_memo", "l2": "inputs (5 x 50 MB) larger than L2"},
+                   "preset": "index_only_page_memo", "l2": "inputs (5 x 50 MB) larger than L2",
+                   "parallelism": f"{world} GPU(s), one batch of 4 per GPU" if world > 1 else "1 GPU"},
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": 6 * TB * TT * TH * TD * 2, "d2h_bytes_per_step": 4,
-                "pipeline": "next step's inputs copied on a second stream during this step"},
+                "timing": "host clock over the K steps, device synchronised at both ends; next step's "
+                          "inputs copied on a second stream during this step"},
         # the step's dominant kernel (about a third of the step): selected-read backward
         "roofline": {"bound": "tensor", "kernel": "read_bwd_kernel (selected-read backward)",
                      "achieved": round(rb_achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(rb_achieved / peak, 4), "peak_kind": kind,
                      "algorithmic_flops_per_launch": rb_flops,
-                     "kernel_ms_mean": round(statistics.mean(rbwd_ms), 4), "traffic": read_bwd_traffic()},
+                     "kernel_ms_mean": round(statistics.mean(rbwd_ms), 4), "traffic": READ_BWD_TRAFFIC_BYTES},
         "roofline_step": {"bound": "tensor", "achieved": round(step_achieved, 1), "peak": peak,
                           "unit": "TFLOP/s", "frac": round(step_achieved / peak, 4),
                           "algorithmic_flops_per_step": step_flops},
@@ -583,34 +633,6 @@ def run_train_bench(args, world, rank, local):
         "gpu_launches": 10 * K,
         "clocks": clocks.summary(),
     }
-
-
-def read_backward_flops(tokens, heads, width, batch, cfg):
-    """Algorithmic FLOPs of the selected-read backward: every query of 256-query tile t
-    selects exactly M(t) fines, and each (query, fine) pair costs dA = gn.C^T and its
-    share of dC = A^T.gn, 2 x 2 x width^2 FLOPs."""
-    from tao_memory_b200.config import routed_counts
-    pairs = 0
-    for tile in range((tokens + 255) // 256):
-        visible = max(0, tile - 2)
-        if visible == 0:
-            continue
-        m = routed_counts(visible // 8, visible % 8, cfg)[2]
-        pairs += min(256, tokens - tile * 256) * m
-    return 4 * width * width * pairs * heads * batch
-
-
-def read_bwd_traffic():
-    """Per-launch DRAM bytes of read_bwd_kernel from the committed ncu summary
-    (line 'traffic_bytes_per_launch: N'), or None."""
-    path = os.path.join(ROOT, "profiles", "read_bwd_kernel_train8k.md")
-    try:
-        for line in open(path):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                return int(float(line.split(":", 1)[1]))
-    except OSError:
-        pass
-    return None
 
 
 def cpu_train_baseline(budget_tokens=8192):
@@ -634,6 +656,145 @@ def cpu_train_baseline(budget_tokens=8192):
                       f"oracle/tao_oracle.py; value scaled to all {TH} heads"}
 
 
+# ---------------------------------------------------------------------------
+# Reference arm: the oracle port on the host CPU, plus the unmodified reference's
+# own Triton path on one B200 (reference_triton)
+# ---------------------------------------------------------------------------
+
+def run_reference_cpu(args):
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    t0 = time.time()
+    states = [synthetic_oracle_state(LAYER, args.context, seed=100 + r) for r in range(args.requests)]
+    setup_s = time.time() - t0
+    time_oracle_decode(states, max(args.warmup, 1), seed=1)
+    n, secs = time_oracle_decode(states, args.steps, seed=2, budget_s=240)
+    value = n / secs
+    cores = torch.get_num_threads()
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": n, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / n, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic ~N(0,1), seeded", "impl": "reference",
+        "config": {"workload": "decode128k (BASELINE.json config 4)", "requests": args.requests,
+                   "context": args.context, "heads": HEADS, "head_dim": WIDTH,
+                   "preset": "index_only_page_memo", "step": "one decode token of one request (round robin)",
+                   "state": "synthetic 128K-context states of the prefilled shapes (a CPU prefill of "
+                            "131,072 tokens takes minutes; values do not change decode cost)",
+                   "setup_s": round(setup_s, 1)},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{n} decode tokens round-robin over {args.requests} synthetic "
+                                   f"128K-context states (oracle/tao_oracle.py: the reference's "
+                                   f"algorithm restated in PyTorch CPU ops)"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def reference_triton(args):
+    """The unmodified reference (baseline/_ref) through its own public API on one
+    B200: decode at 128K context (graph=True, one request at a time as its batch-1
+    API serves them) and tao_attention forward + backward at the training config.
+    Returns a dict (or {"unavailable": why})."""
+    import torch
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "tao_attention")):
+        return {"unavailable": "baseline/_ref is not installed"}
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    sys.path.insert(0, ref_root)
+    try:
+        import triton
+        import tao_attention as ref
+        from tao_attention.presets import index_only_page_memo as ref_preset
+    except Exception as e:   # noqa: BLE001 - report why the comparator cannot run
+        return {"unavailable": f"import failed: {type(e).__name__}: {e}"}
+    out = {"versions": {"torch": torch.__version__, "triton": triton.__version__},
+           "source": "baseline/_ref (pip install --no-deps of the reference, unmodified)"}
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    # decode @128K: one request prefilled, then decode steps timed by CUDA events
+    try:
+        gen = torch.Generator(device=dev).manual_seed(4242)
+        fa = (torch.randn(HEADS, WIDTH, 3, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        fb = (torch.randn(HEADS, WIDTH, 3, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        K, W = args.steps, max(args.warmup, 3)
+        t0 = time.time()
+        with torch.inference_mode():
+            st = ref.new_state(LAYER, ref_preset(graph=True))
+            pos = 0
+            while pos < args.context:
+                w = min(16384, args.context - pos)
+                x = [torch.randn(1, w, HEADS, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+                     for _ in range(5)]
+                _, st = ref.tao_attention_prefill(x[0], x[1], x[2], raw_q=x[3], raw_k=x[4], fusion_a=fa,
+                                                  fusion_b=fb, alpha=0.5, state=st, position=pos)
+                pos += w
+            torch.cuda.synchronize()
+            prefill_s = time.time() - t0
+            xs = torch.randn(W + K, 5, 1, 1, HEADS, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+            for i in range(W):
+                _, st = ref.tao_attention_decode(*xs[i, :3], raw_q=xs[i, 3], raw_k=xs[i, 4], fusion_a=fa,
+                                                 fusion_b=fb, alpha=0.5, state=st, position=st.get_pos())
+            torch.cuda.synchronize()
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+            stops = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+            t_host = time.perf_counter()
+            for i in range(K):
+                starts[i].record()
+                _, st = ref.tao_attention_decode(*xs[W + i, :3], raw_q=xs[W + i, 3], raw_k=xs[W + i, 4],
+                                                 fusion_a=fa, fusion_b=fb, alpha=0.5, state=st,
+                                                 position=st.get_pos())
+                stops[i].record()
+            torch.cuda.synchronize()
+            host_s = time.perf_counter() - t_host
+            ms = [a.elapsed_time(b) for a, b in zip(starts, stops)]
+            st.release_execution()
+        per_tok = max(sum(ms) / K, host_s * 1e3 / K)
+        out["decode128k"] = {
+            "value": round(1e3 / per_tok, 1), "unit": UNIT,
+            "ms_per_token": round(per_tok, 4), "device_ms_per_token": round(sum(ms) / K, 4),
+            "host_ms_per_token": round(host_s * 1e3 / K, 4), "steps": K, "warmup": W,
+            "prefill_s": round(prefill_s, 1),
+            "how": "one 131,072-token request (H12 D64 bf16, index_only_page_memo(graph=True)); the "
+                   "reference serves batch 1, so 8 requests run one after another and the rate is "
+                   "1 / time per token (the larger of the device and host time)"}
+    except Exception as e:   # noqa: BLE001
+        out["decode128k"] = {"unavailable": f"{type(e).__name__}: {e}"}
+    torch.cuda.empty_cache()
+    # training fwd+bwd at config 2
+    try:
+        x, fa, fb, alpha, grad = train_inputs(dev, seed=77)
+        leaves = [t.requires_grad_(True) for t in x] + [fa.requires_grad_(True), fb.requires_grad_(True)]
+        # the reference API takes one Python alpha for all heads; the work does not depend on its value
+        a0 = float(sum(alpha) / len(alpha))
+
+        def step():
+            for t in leaves:
+                t.grad = None
+            y = ref.tao_attention(leaves[0], leaves[1], leaves[2], raw_q=leaves[3], raw_k=leaves[4],
+                                  fusion_a=leaves[5], fusion_b=leaves[6], alpha=a0, config=ref_preset())
+            y.backward(grad)
+
+        K, W = max(3, min(args.steps, 10)), 2
+        for _ in range(W):
+            step()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(K):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+        ms = s0.elapsed_time(s1) / K
+        out["train8k"] = {"value": round(TB * TT / (ms * 1e-3), 1), "unit": "tok/s",
+                          "ms_per_step": round(ms, 3), "steps": K, "warmup": W,
+                          "how": "tao_attention forward + backward, B4 T8192 H12 D64 bf16, "
+                                 "index_only_page_memo(), one scalar alpha (the API's form)"}
+    except Exception as e:   # noqa: BLE001
+        out["train8k"] = {"unavailable": f"{type(e).__name__}: {e}"}
+    return out
+
+
 def main():
     args = parse()
     world, rank, local = dist_env()
@@ -642,23 +803,24 @@ def main():
             return 0
         if args.workload == "train8k":
             cb = cpu_train_baseline()
-            print(json.dumps({"metric": "train fwd+bwd tokens/s @8K", "value": cb["value"], "unit": "tok/s",
-                              "n_gpus": args.gpus, "steps": 1, "warmup": 0, "higher_is_better": True,
-                              "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                              "data": "synthetic ~N(0,1), seeded", "impl": "reference",
-                              "config": {"workload": "train8k (BASELINE.json config 2)"},
-                              "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tok/s",
-                                                          "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
-                  flush=True)
-            return 0
-        print(json.dumps(run_reference(args)), flush=True)
+            line = {"metric": "train fwd+bwd tokens/s @8K", "value": cb["value"], "unit": "tok/s",
+                    "n_gpus": args.gpus, "steps": 1, "warmup": 0, "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                    "data": "synthetic ~N(0,1), seeded", "impl": "reference",
+                    "config": {"workload": "train8k (BASELINE.json config 2)"},
+                    "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tok/s",
+                                                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        else:
+            line = run_reference_cpu(args)
+        line["reference_triton"] = reference_triton(args)
+        print(json.dumps(line), flush=True)
         return 0
     import torch
     import torch.distributed as dist
     from datetime import timedelta
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
         if args.workload == "train8k":
@@ -666,11 +828,19 @@ def main():
             if rank == 0:
                 result["cpu_baseline"] = cpu_train_baseline() if world == 1 else None
         else:
-            result, states = run_b200(args, world, rank, local)
-            if rank == 0 and world == 1:
-                result["cpu_baseline"] = cpu_baseline_from_gpu(states, args.cpu_sample_steps)
+            result, states, exported, timed_inputs, outs, fa, fb = run_b200(args, world, rank, local)
+            if rank == 0 and exported is not None:
+                result["parity"], hosts = decode_parity(exported, timed_inputs, outs, fa, fb, states)
+                result["cpu_baseline"] = cpu_baseline_decode(hosts, args.cpu_sample_steps) if world == 1 else None
             elif rank == 0:
                 result["cpu_baseline"] = None
+            del states, exported, timed_inputs, outs
+            torch.cuda.empty_cache()
+            if not args.no_train:
+                train = run_train_bench(args, world, rank, local)
+                if rank == 0:
+                    train["cpu_baseline"] = cpu_train_baseline() if world == 1 else None
+                    result["train8k"] = train
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:

@@ -161,10 +161,19 @@ int tao_stream_check(void* workspace, int* flags, void* stream);
  * buffer must be page-locked with a device mapping (checked with
  * cudaPointerGetAttributes; otherwise TAO_ERR_ARG and nothing is accessed), the
  * other must be device memory of the calling thread's current device (where the
- * kernel runs), both 16-byte aligned and `bytes` a multiple of 16.
+ * kernel runs), both 16-byte aligned and `bytes` a multiple of 16.  The device
+ * range must lie inside one allocation (its extent comes from the driver,
+ * cuMemGetAddressRange; otherwise TAO_ERR_ARG); the host range is the caller's to
+ * keep in bounds.
  * No counterpart in the reference (its operands are already on the device). */
 int tao_copy_host_to_device(void* dst, const void* host_src, size_t bytes, void* stream);
 int tao_copy_device_to_host(void* host_dst, const void* src, size_t bytes, void* stream);
+
+/* The same transfer for n (1..8) buffers in one launch: dst[i] <- host_src[i],
+ * bytes[i] each, with the checks above on every pair.  A decode step's five
+ * operands cross in one launch.  No counterpart in the reference. */
+int tao_copy_host_to_device_many(void* const* dst, const void* const* host_src, const size_t* bytes,
+                                 int n, void* stream);
 
 /* Decode step (one token for each of n_states requests) that allocates nothing:
  * same arguments and results as tao_stream_step with tokens = 1, but its scratch
@@ -180,6 +189,13 @@ int tao_stream_decode_noalloc(void* const* states, int n_states, const int64_t* 
                               int width, const void* q, const void* k, const void* v,
                               const void* raw_q, const void* raw_k, const void* fusion_a,
                               const void* fusion_b, float alpha, void* out, void* stream);
+
+/* The device error word of tao_stream_decode_noalloc on the calling thread's
+ * current device (route overflow, expired bounded wait), which lives in the same
+ * static array: synchronises `stream`, stores the word in *flags, clears it and
+ * returns TAO_ERR_DEVICE when it was set.  Read it after the calls whose result
+ * matters, before the next call clears it.  No counterpart in the reference. */
+int tao_stream_decode_noalloc_check(int* flags, void* stream);
 
 /* CUDA events for timing (thin wrappers over the runtime, so callers need no
  * other binding).  tao_stream_profile_next(start, stop) makes the next library

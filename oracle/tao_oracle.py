@@ -639,6 +639,61 @@ def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False, writ
     return local, torch.cat(fine_parts, dim=1), ids
 
 
+def training_routes(raw_q, raw_k, v, fine=256, group=8):
+    """The routing decisions of read_training (tao_stream.py:596-665) for every
+    256-query tile, with the scores behind them, so a test can tell a real routing
+    difference from a near-tie: per tile a dict with ``sel`` [B,L,H,M] (selected
+    fine ids in rank order, as ``_tile_read``), ``page_mass`` [B,L,H,completed]
+    (bf16 sum_d hv of each completed page), ``chosen`` [B,L,H,K] (pages kept) and
+    ``fine_score`` [B,L,H,visible] (bf16 sum_d bf16(hv[page] * w) of every visible
+    fine, candidate or not: the score it would have as a candidate)."""
+    b, total, heads, d = raw_q.shape
+    if total <= keep_plus(fine):
+        return []
+    fine_z, _ = seal_all(raw_k, v, fine)
+    dt = raw_q.dtype
+    tiles = []
+    for tile, query in enumerate(raw_q.split(fine, dim=1)):
+        visible = max(0, tile - 2)
+        if not visible:
+            continue
+        completed, pending = divmod(visible, group)
+        pz = []
+        if completed:
+            zc = fine_z[:, :, :completed * group].reshape(b, heads, completed, group, d)
+            pz.append(torch.logsumexp(zc, dim=3).to(dt))
+        if pending:
+            zp = fine_z[:, :, completed * group:visible].reshape(b, heads, 1, pending, d)
+            pz.append(torch.logsumexp(zp, dim=3).to(dt))
+        page_z = torch.cat(pz, dim=2)
+        length = query.shape[1]
+        h = F.softmax(query, dim=-1).to(dt)
+        hv = (h.unsqueeze(3) * F.softmax(page_z, dim=2).to(dt)[:, None]).to(dt)
+        coarse, _, count = routed_counts(completed, pending, group)
+        fz = fine_z[:, :, :visible]
+        fine_page = torch.arange(visible) // group
+        w = (fz - page_z.index_select(2, fine_page)).exp().to(dt)            # [B,H,V,D]
+        hv_f = hv.index_select(3, fine_page)                                   # [B,L,H,V,D]
+        score = (hv_f.float() * w[:, None].float()).to(BF16).sum(-1)           # [B,L,H,V]
+        info = dict(tile=tile, coarse=coarse, count=count, completed=completed, pending=pending,
+                    fine_score=score.float())
+        ids = []
+        if coarse:
+            mass = hv[..., :completed, :].sum(-1)
+            chosen = topk_oldest(mass, coarse).sort(-1).values
+            info["page_mass"] = mass.float()
+            info["chosen"] = chosen
+            ids.append((chosen.unsqueeze(-1) * group + torch.arange(group)).reshape(b, length, heads, -1))
+        if pending:
+            ids.append((completed * group + torch.arange(pending)).view(1, 1, 1, pending).expand(b, length, heads,
+                                                                                                 pending))
+        cand = torch.cat(ids, -1)
+        cand_score = score.gather(-1, cand)
+        info["sel"] = cand.gather(-1, topk_oldest(cand_score, count))
+        tiles.append(info)
+    return tiles
+
+
 def keep_plus(fine):
     return 512 + fine
 

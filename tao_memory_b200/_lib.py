@@ -61,12 +61,15 @@ _SIGNATURES = {
     "tao_stream_decode_noalloc": (_I, [_VP, _I, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_int32),
                                        ctypes.POINTER(TaoPolicy), _I, _I, _VP, _VP, _VP, _VP, _VP,
                                        _VP, _VP, _F, _VP, _VP]),
+    "tao_stream_decode_noalloc_check": (_I, [ctypes.POINTER(_I), _VP]),
     "tao_ring_gather": (_I, [_VP, _I, _I, _I64, _I, _VP, _VP]),
     "tao_ring_scatter": (_I, [_VP, _I, _I, _I64, _I, _VP, _VP]),
     "tao_state_rebuild_memo": (_I, [_VP, _I, _I, _I, _VP]),
     "tao_state_refresh_page_weights": (_I, [_VP, _I, _I, _I, _VP]),
     "tao_copy_host_to_device": (_I, [_VP, _VP, _SZ, _VP]),
     "tao_copy_device_to_host": (_I, [_VP, _VP, _SZ, _VP]),
+    "tao_copy_host_to_device_many": (_I, [ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.POINTER(_SZ), _I,
+                                          _VP]),
     "tao_window_attention": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP]),
     "tao_train_geometry": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "tao_train_forward": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP, _VP, _VP]),

@@ -6,6 +6,7 @@
 // buffers and the workspace are owned by the caller.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -199,6 +200,19 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
 // or seals, so one captured launch sequence serves every token.
 thread_local int g_graph_mode = 0;
 
+constexpr int kMaxDevices = 64;
+
+// Streaming multiprocessors of a device, queried once per device.
+int device_sm_count(int dev) {
+  static std::atomic<int> sms_of[kMaxDevices];
+  int sms = sms_of[dev].load(std::memory_order_relaxed);
+  if (sms <= 0) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    sms_of[dev].store(sms, std::memory_order_relaxed);
+  }
+  return sms;
+}
+
 template <int D>
 int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaStream_t s) {
   using namespace tao;
@@ -213,13 +227,10 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
   f.s = a;
   f.ms = ms;
   const int total = a.R * a.H * (FusedCfg<D>::KB + ms);
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(TAO_ERR_CUDA, "no current CUDA device (or device index above %d)", kMaxDevices - 1);
+  const int sms = device_sm_count(dev);
   cudaEvent_t prof0, prof1;
   tao_take_profile_events(&prof0, &prof1);
   if (prof0) cudaEventRecord(prof0, s);
@@ -238,14 +249,16 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
     // persistent: as many CTAs as are resident at once, each walking items by the grid stride
     const size_t smem = FusedCfg<D>::STAGE;
     if ((rc = set_smem(decode_fused_kernel<D>, smem))) return rc;
-    static int resident = 0;
-    if (!resident) {
-      int per_sm = 0;
+    // resident CTAs per SM: one occupancy query per (device, width), kept for the process
+    static std::atomic<int> per_sm_of[kMaxDevices];
+    int per_sm = per_sm_of[dev].load(std::memory_order_relaxed);
+    if (per_sm <= 0) {
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel<D>, 128, smem) != cudaSuccess ||
           per_sm <= 0)
         per_sm = 1;
-      resident = per_sm * sms;
+      per_sm_of[dev].store(per_sm, std::memory_order_relaxed);
     }
+    const int resident = per_sm * sms;
     // balanced: every CTA walks the same number of items (give or take one)
     const int rounds = (total + resident - 1) / resident;
     decode_fused_kernel<D><<<(total + rounds - 1) / rounds, 128, smem, s>>>(f);

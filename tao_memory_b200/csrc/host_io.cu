@@ -11,9 +11,13 @@
 // The host pointer is checked with cudaPointerGetAttributes before any launch: it must
 // be page-locked host memory with a device mapping, 16-byte aligned, and the size a
 // multiple of 16 bytes; anything else returns TAO_ERR_ARG and nothing is accessed.
+// The device side must be one allocation holding all `bytes` (its extent is asked of
+// the driver, cuMemGetAddressRange); the caller keeps the host range in bounds.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "../../include/tao_b200.h"
 
@@ -25,6 +29,25 @@ __global__ void __launch_bounds__(256) copy16_kernel(uint4* __restrict__ dst, co
                                                      long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     dst[i] = src[i];
+}
+
+// Up to kMaxCopies buffers in one launch (a decode step's five operands).
+constexpr int kMaxCopies = 8;
+struct CopyList {
+  uint4* dst[kMaxCopies];
+  const uint4* src[kMaxCopies];
+  long long n[kMaxCopies];  // 16-byte vectors
+  int count;
+};
+
+__global__ void __launch_bounds__(256) copy16_many_kernel(CopyList L) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long first = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  for (int c = 0; c < L.count; ++c) {
+    uint4* __restrict__ d = L.dst[c];
+    const uint4* __restrict__ sp = L.src[c];
+    for (long long i = first; i < L.n[c]; i += stride) d[i] = sp[i];
+  }
 }
 
 // Device address of mapped page-locked host memory, or nullptr.
@@ -46,7 +69,22 @@ const void* mapped_host(const void* host, const char** why) {
   return attr.devicePointer;
 }
 
-int checked_device(const void* p, const char** why) {
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q{};
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(p);
+  });
+  return fn;
+}
+
+int checked_device(const void* p, size_t bytes, const char** why) {
   cudaPointerAttributes attr{};
   if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
     cudaGetLastError();
@@ -61,6 +99,18 @@ int checked_device(const void* p, const char** why) {
   if (cudaGetDevice(&current) != cudaSuccess || attr.device != current) {
     cudaGetLastError();
     *why = "device buffer is not on the calling thread's current device";
+    return 0;
+  }
+  AddressRangeFn range = address_range_fn();
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (!range || range(&base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) {
+    *why = "device buffer extent is unknown to the driver";
+    return 0;
+  }
+  const uintptr_t first = reinterpret_cast<uintptr_t>(p);
+  if (first < base || bytes > size || first - base > size - bytes) {
+    *why = "transfer runs past the end of the device allocation";
     return 0;
   }
   return 1;
@@ -100,11 +150,46 @@ extern "C" int tao_copy_host_to_device(void* dst, const void* host_src, size_t b
   if (rc) return rc;
   const char* why = nullptr;
   const void* src = mapped_host(host_src, &why);
-  if (!src || !checked_device(dst, &why)) {
+  if (!src || !checked_device(dst, bytes, &why)) {
     tao_set_last_error(why);
     return TAO_ERR_ARG;
   }
   return launch_copy(dst, src, bytes, stream);
+}
+
+extern "C" int tao_copy_host_to_device_many(void* const* dst, const void* const* host_src, const size_t* bytes,
+                                            int n, void* stream) {
+  if (!dst || !host_src || !bytes || n <= 0 || n > kMaxCopies) {
+    tao_set_last_error("host copy list: null arrays or count outside 1..8");
+    return TAO_ERR_ARG;
+  }
+  CopyList L{};
+  long long most = 0;
+  for (int c = 0; c < n; ++c) {
+    int rc = check_args(dst[c], host_src[c], bytes[c]);
+    if (rc) return rc;
+    const char* why = nullptr;
+    const void* src = mapped_host(host_src[c], &why);
+    if (!src || !checked_device(dst[c], bytes[c], &why)) {
+      tao_set_last_error(why);
+      return TAO_ERR_ARG;
+    }
+    L.dst[c] = static_cast<uint4*>(dst[c]);
+    L.src[c] = static_cast<const uint4*>(src);
+    L.n[c] = (long long)(bytes[c] / 16);
+    if (L.n[c] > most) most = L.n[c];
+  }
+  L.count = n;
+  if (most == 0) return TAO_OK;
+  long long blocks = (most + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  copy16_many_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(L);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    tao_set_last_error(cudaGetErrorString(e));
+    return TAO_ERR_CUDA;
+  }
+  return TAO_OK;
 }
 
 extern "C" int tao_copy_device_to_host(void* host_dst, const void* src, size_t bytes, void* stream) {
@@ -112,7 +197,7 @@ extern "C" int tao_copy_device_to_host(void* host_dst, const void* src, size_t b
   if (rc) return rc;
   const char* why = nullptr;
   void* dst = const_cast<void*>(mapped_host(host_dst, &why));
-  if (!dst || !checked_device(src, &why)) {
+  if (!dst || !checked_device(src, bytes, &why)) {
     tao_set_last_error(why);
     return TAO_ERR_ARG;
   }

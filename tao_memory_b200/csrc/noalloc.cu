@@ -205,3 +205,26 @@ extern "C" int tao_stream_decode_noalloc(void* const* states, int n_states, cons
   a.pmax = pmax;
   return width == 64 ? na_launch<64>(a, s) : na_launch<128>(a, s);
 }
+
+// Device error word of the allocation-free decode on the current device: the
+// kernels of tao_stream_decode_noalloc record a route overflow or a wait timeout
+// there (the word a workspace caller reads with tao_stream_check).  Synchronises
+// `stream`, returns the word in *flags and clears it.
+extern "C" int tao_stream_decode_noalloc_check(int* flags, void* stream) {
+  void* base = nullptr;
+  int rc = scratch_address(&base);
+  if (rc) return rc;
+  int host = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(&host, base, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && host) e = cudaMemsetAsync(base, 0, sizeof(int), s);
+  if (e != cudaSuccess) return na_fail(TAO_ERR_CUDA, cudaGetErrorString(e));
+  if (flags) *flags = host;
+  if (host) {
+    char buf[128];
+    snprintf(buf, sizeof(buf), "device error flags 0x%x", host);
+    return na_fail(TAO_ERR_DEVICE, buf);
+  }
+  return TAO_OK;
+}

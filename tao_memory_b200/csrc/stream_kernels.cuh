@@ -113,8 +113,14 @@ __global__ void __launch_bounds__(256) prep_kernel(StepArgs a) {
       *reinterpret_cast<uint4*>(vr + dst) = *reinterpret_cast<const uint4*>(a.v + src);
       *reinterpret_cast<uint4*>(rr + dst) = *reinterpret_cast<const uint4*>(a.raw_k + src);
     }
-    // slot 0: routes currently stored in the state
+    // slot 0: routes currently stored in the state (a state holding more routes
+    // than this call's slots is flagged and read with no fines, never copied past
+    // the slot)
     int n = st.n_route, kc = st.n_chosen;
+    if (n > a.route_cap || kc > a.route_cap || n > st.route_cap || kc > st.route_cap) {
+      if (tid == 0) atomicOr(a.err, kErrRouteCap);
+      n = kc = 0;
+    }
     for (int m = tid; m < n; m += blockDim.x)
       a.slot_ids[base * a.route_cap + m] = st.route_ids[(long long)h * st.route_cap + m];
     for (int m = tid; m < kc; m += blockDim.x)

@@ -9,6 +9,8 @@ non_blocking=True)``.  No counterpart in the reference (its operands live on the
 device already).
 """
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -41,3 +43,22 @@ def copy_to_host(host, dev):
     with torch.cuda.device(dev.device):
         _lib.check(_lib.lib().tao_copy_device_to_host(host.data_ptr(), dev.data_ptr(), nbytes, stream))
     return host
+
+
+def copy_to_device_many(devs, hosts):
+    """devs[i] <- hosts[i] (page-locked) for up to 8 pairs in one launch; returns devs.
+    All device tensors must be on one device."""
+    if not 0 < len(devs) == len(hosts) <= 8:
+        raise ValueError("copy_to_device_many takes 1 to 8 (device, host) pairs")
+    sizes = [_check(h, d)[0] for d, h in zip(devs, hosts)]
+    device = devs[0].device
+    if any(d.device != device for d in devs):
+        raise ValueError("copy_to_device_many: device tensors on different devices")
+    n = len(devs)
+    dst = (ctypes.c_void_p * n)(*[d.data_ptr() for d in devs])
+    src = (ctypes.c_void_p * n)(*[h.data_ptr() for h in hosts])
+    nbytes = (ctypes.c_size_t * n)(*sizes)
+    with torch.cuda.device(device):
+        _lib.check(_lib.lib().tao_copy_host_to_device_many(dst, src, nbytes, n,
+                                                           torch.cuda.current_stream(device).cuda_stream))
+    return devs

@@ -14,7 +14,7 @@ independent requests by one token each in one set of kernel launches.
 import torch
 
 from .config import TaoConfig
-from .stream import StreamCache, run_batch, WINDOW
+from .stream import StreamCache, run_batch, run_batch_host, WINDOW
 
 DEFAULT_CONFIG = TaoConfig()
 
@@ -73,6 +73,10 @@ def tao_attention_decode_batch(q, k, v, *, raw_q, raw_k, fusion_a, fusion_b, alp
     q, k, v, raw_q, raw_k: [R, 1, H, D] bf16 (row r belongs to states[r]); all
     states share fusion_a/fusion_b/alpha (one layer's parameters).  Each state
     advances by one; the result equals R separate ``tao_attention_decode`` calls.
+    The operands may be page-locked host tensors: the library then moves them in
+    and the result out itself (in the same captured step for graph-configured
+    states) and returns a page-locked host tensor, valid after the current stream
+    is synchronised.
     """
     if q.dim() != 4 or q.shape[1] != 1 or q.shape[0] != len(states):
         raise ValueError("batched decode takes [len(states), 1, heads, width] operands")
@@ -82,6 +86,14 @@ def tao_attention_decode_batch(q, k, v, *, raw_q, raw_k, fusion_a, fusion_b, alp
                 raise ValueError("position must match this request's causal cursor")
     if len({id(s) for s in states}) != len(states):
         raise ValueError("a state may appear only once per batch")
+    if q.device.type == "cpu":
+        # operands in page-locked host memory: the result goes to page-locked host
+        # memory too, valid once the device's current stream has reached the step
+        if out is None:
+            out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        with torch.no_grad():
+            run_batch_host(list(states), (q, k, v, raw_q, raw_k), fusion_a, fusion_b, alpha, out)
+        return out, states
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     with torch.no_grad():

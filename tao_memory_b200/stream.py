@@ -18,6 +18,7 @@ snapshots move between the two implementations.
 
 import ctypes
 import math
+import weakref
 
 import torch
 
@@ -90,18 +91,32 @@ def policy_for(config):
                           int(config.fine_writer in FEATURE_WRITERS))
 
 
+def _policy_key(config):
+    """The configuration fields a captured or cached decode step bakes in."""
+    return (config.route_period, config.layer_stagger, config.budget_root_scale, config.budget_offset,
+            config.fine_writer in FEATURE_WRITERS)
+
+
 class _Workspace:
-    """Grow-only device scratch shared by calls on one device."""
+    """Grow-only device scratch, one per (device, stream).  Calls on one stream run
+    in order and share it; calls on two streams of one device get separate
+    scratch, so requests decoded concurrently on different streams do not race on
+    route slots, partials or the error word."""
 
     cache = {}
 
     @classmethod
-    def get(cls, device, nbytes):
-        buf = cls.cache.get(device)
+    def get(cls, device, stream, nbytes):
+        key = (device, stream)
+        buf = cls.cache.get(key)
         if buf is None or buf.numel() < nbytes:
             buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-            cls.cache[device] = buf
+            cls.cache[key] = buf
         return buf
+
+    @classmethod
+    def on_device(cls, device):
+        return [(stream, buf) for (dev, stream), buf in list(cls.cache.items()) if dev == device]
 
 
 class StreamCache:
@@ -483,10 +498,8 @@ class _BatchArgs:
     def get(cls, states, w, heads, width, dev):
         # everything the cached arrays hold is part of the key: a freed state's
         # descriptor address can be reused by a new state with another layer index
-        c = states[0].config
         key = (tuple((st._desc.data_ptr(), st.cap_fines, st.layer_index) for st in states), w, heads, width,
-               c.route_period, c.layer_stagger, c.budget_root_scale, c.budget_offset,
-               c.fine_writer in FEATURE_WRITERS)
+               _policy_key(states[0].config))
         args = cls.cache.get(key)
         if args is None:
             if len(cls.cache) > 256:
@@ -495,7 +508,7 @@ class _BatchArgs:
         return args
 
 
-def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
+def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out, allow_graph=True):
     """Advance every state by q.shape[1] tokens in one set of kernel launches.
 
     q, k, v, raw_q, raw_k, out: [len(states), tokens, H, D] bf16 on one device.
@@ -519,8 +532,7 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
         raise ValueError("a batch mixes feature-read writers with other fine writers")
     for st in states:
         st._ensure(heads, width, dev, w)
-    if (w == 1 and dev.type == "cuda" and all(st.config.q1_history_region_graph and st.config.fine_writer == "softmax"
-                                              for st in states)
+    if (allow_graph and w == 1 and dev.type == "cuda" and _graph_states(states)
             and _BatchGraph.run(states, ops, fa, fb, alpha, out, heads, width)):
         for st in states:
             _bookkeep(st, 1)
@@ -528,8 +540,8 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
     args = _BatchArgs.get(states, w, heads, width, dev)
     for i, st in enumerate(states):
         args.pos[i] = st.position
-    ws = _Workspace.get(dev, args.nbytes)
     stream = torch.cuda.current_stream(dev).cuda_stream
+    ws = _Workspace.get(dev, stream, args.nbytes)
     if w == 1:
         _lib.check(lib.tao_decode_step(args.ptrs.data_ptr(), r, args.pos, args.layers, args.cap,
                                        ctypes.byref(args.policy), heads, width,
@@ -546,6 +558,69 @@ def run_batch(states, q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, out):
             if end - window_start(end - 1) == WINDOW:   # this chunk sealed a block
                 st._seal_writer(sealed_at(end - 1))
         _bookkeep(st, w)
+
+
+def _graph_states(states):
+    return all(st.config.q1_history_region_graph and st.config.fine_writer == "softmax" for st in states)
+
+
+class _HostStage:
+    """Device staging of decode operands that arrive in page-locked host memory:
+    one [6, R, 1, H, D] bf16 buffer (q, k, v, raw_q, raw_k, output) per (device,
+    stream, shape), reused by every call with that shape."""
+
+    cache = {}
+
+    @classmethod
+    def get(cls, device, stream, shape):
+        key = (device, stream, tuple(shape))
+        buf = cls.cache.get(key)
+        if buf is None:
+            if len(cls.cache) >= 64:
+                cls.cache.clear()
+            buf = cls.cache[key] = torch.empty((6,) + tuple(shape), dtype=_BF16, device=device)
+        return buf
+
+
+def run_batch_host(states, host_ops, fusion_a, fusion_b, alpha, host_out):
+    """One decode token for every state with the operands in page-locked host memory
+    and the result written to page-locked host memory.  The SMs move the bytes over
+    the host link (one launch in, one out); with graph-configured states the copies
+    and the decode step are captured together and a step is one graph launch.  The
+    host output is valid once the current stream has reached the step."""
+    from .host_io import copy_to_device_many, copy_to_host
+    r, w, heads, width = host_ops[0].shape
+    if w != 1:
+        raise ValueError("host operands are taken one decode token at a time")
+    for t in tuple(host_ops) + (host_out,):
+        if t.device.type != "cpu" or not t.is_pinned() or t.dtype != _BF16 or not t.is_contiguous():
+            raise ValueError("host operands and output must be contiguous page-locked bf16 tensors")
+        if t.shape != host_ops[0].shape:
+            raise ValueError("q, k, v, raw_q, raw_k and out must have the same shape")
+    devs = {st.device for st in states if st.device is not None}
+    if len(devs) > 1:
+        raise ValueError("a batch spans one device")
+    dev = devs.pop() if devs else torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    stage = _HostStage.get(dev, stream, host_ops[0].shape)
+    ops, out = [stage[i] for i in range(5)], stage[5]
+    if _graph_states(states):
+        fa = fusion_a if (fusion_a.dtype == _BF16 and fusion_a.is_contiguous() and fusion_a.device == dev) \
+            else fusion_a.detach().to(dev, _BF16).contiguous()
+        fb = fusion_b if (fusion_b.dtype == _BF16 and fusion_b.is_contiguous() and fusion_b.device == dev) \
+            else fusion_b.detach().to(dev, _BF16).contiguous()
+        if fa.shape != (heads, width, 3) or fb.shape != (heads, width, 3):
+            raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
+        for st in states:
+            st._ensure(heads, width, dev, 1)
+        if _BatchGraph.run(states, ops, fa, fb, alpha, out, heads, width, host=(host_ops, host_out)):
+            for st in states:
+                _bookkeep(st, 1)
+            return host_out
+    copy_to_device_many(ops, list(host_ops))
+    run_batch(states, *ops, fusion_a, fusion_b, alpha, out, allow_graph=False)
+    copy_to_host(host_out, out)
+    return host_out
 
 
 def _bookkeep(st, w):
@@ -579,7 +654,7 @@ class _DecodeGraph:
     def __init__(self, st, heads, width, alpha):
         dev = st.device
         lib = _lib.lib()
-        self.key = (st.cap_fines, st._desc.data_ptr(), heads, width, float(alpha))
+        self.key = (st.cap_fines, st._desc.data_ptr(), heads, width, float(alpha), _policy_key(st.config))
         self.inp = torch.zeros(5, 1, 1, heads, width, dtype=_BF16, device=dev)   # q, k, v, raw_q, raw_k
         self.fab = torch.zeros(2, heads, width, 3, dtype=_BF16, device=dev)      # fusion_a, fusion_b
         self.out = torch.zeros(1, 1, heads, width, dtype=_BF16, device=dev)
@@ -590,7 +665,7 @@ class _DecodeGraph:
         self.layer = (ctypes.c_int32 * 1)(st.layer_index)
         nbytes = lib.tao_stream_workspace_bytes(1, 1, heads, width, ROUTE_CAP, ctypes.byref(self.policy))
         self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
-        _GRAPH_WORKSPACES.setdefault(dev, []).append(self.ws)
+        _graph_workspaces(dev).add(self.ws)
         self.graph = torch.cuda.CUDAGraph()
         rc = 0
         lib.tao_decode_graph_mode(1)
@@ -621,7 +696,7 @@ class _DecodeGraph:
             raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
         st._ensure(heads, width, dev, 1)   # may grow the fine bank (new buffers)
         g = st._graph
-        key = (st.cap_fines, st._desc.data_ptr(), heads, width, float(alpha))
+        key = (st.cap_fines, st._desc.data_ptr(), heads, width, float(alpha), _policy_key(st.config))
         if g is None or g.key != key:
             g = st._graph = _DecodeGraph(st, heads, width, alpha)
         for i, t in enumerate(ops):
@@ -633,7 +708,13 @@ class _DecodeGraph:
         _bookkeep(st, 1)
 
 
+# Workspaces of live captured graphs, per device (weak: a graph that is replaced
+# or evicted frees its workspace and drops out of the error check).
 _GRAPH_WORKSPACES = {}
+
+
+def _graph_workspaces(device):
+    return _GRAPH_WORKSPACES.setdefault(device, weakref.WeakSet())
 
 
 class _BatchGraph:
@@ -647,10 +728,18 @@ class _BatchGraph:
     cache = {}      # key -> _BatchGraph
     last = None     # key of the previous eager call
 
-    def __init__(self, states, ops, fa, fb, alpha, out, heads, width):
+    def __init__(self, states, ops, fa, fb, alpha, out, heads, width, host=None):
         dev = ops[0].device
         lib = _lib.lib()
         r = len(states)
+        if host is not None:   # page-locked host operands and output: copies captured with the step
+            host_ops, host_out = host
+            n = len(ops)
+            self.copy_dst = (ctypes.c_void_p * n)(*[t.data_ptr() for t in ops])
+            self.copy_src = (ctypes.c_void_p * n)(*[t.data_ptr() for t in host_ops])
+            self.copy_bytes = (ctypes.c_size_t * n)(*[t.numel() * t.element_size() for t in host_ops])
+            self.host_out = host_out
+        self.host = host is not None
         self.ptrs = torch.tensor([st._desc.data_ptr() for st in states], dtype=torch.int64, device=dev)
         self.policy = policy_for(states[0].config)
         self.pos = (ctypes.c_int64 * r)(*[st.position for st in states])
@@ -658,26 +747,38 @@ class _BatchGraph:
         self.layers = (ctypes.c_int32 * r)(*[st.layer_index for st in states])
         nbytes = lib.tao_stream_workspace_bytes(r, 1, heads, width, ROUTE_CAP, ctypes.byref(self.policy))
         self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
-        _GRAPH_WORKSPACES.setdefault(dev, []).append(self.ws)
+        _graph_workspaces(dev).add(self.ws)
         self.graph = torch.cuda.CUDAGraph()
         rc = 0
         lib.tao_decode_graph_mode(1)
         try:
             with torch.cuda.graph(self.graph, capture_error_mode="relaxed"):
-                rc = lib.tao_decode_step(self.ptrs.data_ptr(), r, self.pos, self.layers, self.cap,
-                                         ctypes.byref(self.policy), heads, width,
-                                         *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
-                                         float(alpha), out.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
-                                         torch.cuda.current_stream(dev).cuda_stream)
+                stream = torch.cuda.current_stream(dev).cuda_stream
+                if self.host:
+                    rc = lib.tao_copy_host_to_device_many(self.copy_dst, self.copy_src, self.copy_bytes,
+                                                          len(ops), stream)
+                if rc == 0:
+                    rc = lib.tao_decode_step(self.ptrs.data_ptr(), r, self.pos, self.layers, self.cap,
+                                             ctypes.byref(self.policy), heads, width,
+                                             *(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(),
+                                             float(alpha), out.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                                             stream)
+                if rc == 0 and self.host:
+                    rc = lib.tao_copy_device_to_host(self.host_out.data_ptr(), out.data_ptr(),
+                                                     out.numel() * out.element_size(), stream)
         finally:
             lib.tao_decode_graph_mode(0)
         _lib.check(rc)
 
     @classmethod
-    def run(cls, states, ops, fa, fb, alpha, out, heads, width):
-        """Replay (or capture and replay) the batch step; False = run it eagerly."""
+    def run(cls, states, ops, fa, fb, alpha, out, heads, width, host=None):
+        """Replay (or capture and replay) the batch step; False = run it eagerly.
+        ``host`` = (host operands, host output) when the step's operands arrive in,
+        and its result goes back to, page-locked host memory."""
         key = (tuple((st._desc.data_ptr(), st.cap_fines, st.layer_index) for st in states), heads, width,
-               float(alpha), tuple(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(), out.data_ptr())
+               float(alpha), tuple(t.data_ptr() for t in ops), fa.data_ptr(), fb.data_ptr(), out.data_ptr(),
+               _policy_key(states[0].config),
+               None if host is None else (tuple(t.data_ptr() for t in host[0]), host[1].data_ptr()))
         g = cls.cache.get(key)
         if g is None:
             if cls.last != key:
@@ -685,7 +786,7 @@ class _BatchGraph:
                 return False
             if len(cls.cache) >= 8:
                 cls.cache.clear()
-            g = cls.cache[key] = cls(states, ops, fa, fb, alpha, out, heads, width)
+            g = cls.cache[key] = cls(states, ops, fa, fb, alpha, out, heads, width, host)
         g.graph.replay()
         return True
 
@@ -693,13 +794,14 @@ class _BatchGraph:
 def check_device(device=None):
     """Raise if a kernel on ``device`` reported an error since the last check."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    current = torch.cuda.current_stream(dev).cuda_stream
     flags = ctypes.c_int(0)
     total = 0
-    for ws in [_Workspace.cache.get(dev)] + _GRAPH_WORKSPACES.get(dev, []):
-        if ws is None:
-            continue
-        _lib.check(_lib.lib().tao_stream_check(ws.data_ptr(), ctypes.byref(flags), stream))
+    # the words of every stream's workspace are read on the current stream after a
+    # device-wide synchronisation (another stream's handle may be gone by now)
+    torch.cuda.synchronize(dev)
+    for ws in [buf for _, buf in _Workspace.on_device(dev)] + list(_GRAPH_WORKSPACES.get(dev, ())):
+        _lib.check(_lib.lib().tao_stream_check(ws.data_ptr(), ctypes.byref(flags), current))
         total |= flags.value
     return total
 

@@ -1,6 +1,10 @@
 """tao_attention (training) on the GPU vs the reference goldens and the oracle.
-Tolerance: outputs |a-b| <= 2e-2 + 2e-2|b| on >= 99.9% of elements (bf16; a query
-whose routing sits on a near-tie may legitimately differ), gradients rel-L2 <= 2e-2."""
+
+Tolerance: outputs |a-b| <= 2e-2 + 2e-2|b| for every element (bf16), gradients
+rel-L2 <= 2e-2.  The routing selections of every query are compared with the
+oracle's (which is pinned to the reference's routing); a query whose selection
+differs must sit on a near-tie of the oracle's scores (tests/_parity.py), and only
+such queries are exempt from the output check."""
 import os
 
 import pytest
@@ -8,6 +12,7 @@ import torch
 
 from oracle import tao_oracle as o
 from oracle.inputs import make_inputs
+from _parity import assert_close, training_route_flips
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
@@ -32,6 +37,27 @@ def run(x, alpha, grad=None, config=None):
     return out.detach(), None
 
 
+def selections(x, alpha):
+    """The library's training selections [B, T, H, mmax] (int16, -1 padded)."""
+    from tao_memory_b200 import training
+    xs = {k: t.cuda() for k, t in x.items()}
+    with torch.no_grad():
+        gains = training._gains(alpha, x["q"].shape[2], xs["q"].device)
+        _, bufs = training._forward(*(xs[k] for k in KEYS), xs["fusion_a"], xs["fusion_b"], gains)
+    return bufs["sel"].cpu()
+
+
+def check_output(x, alpha, out, ref, what, row_stride=1):
+    """Every element within tolerance, except queries whose selection differs from
+    the oracle's at a proven near-tie."""
+    heads = list(range(x["q"].shape[2]))
+    tiles = o.training_routes(x["raw_q"], x["raw_k"], x["v"])
+    flipped, n_flip, problems = training_route_flips(selections(x, alpha), tiles, heads)
+    assert not problems, problems[:5]
+    assert_close(out[:, ::row_stride], ref, what, exempt=flipped[:, ::row_stride])
+    return n_flip
+
+
 GOLDEN_TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages", "train_regularized"]
 
 
@@ -47,8 +73,7 @@ def test_forward_matches_reference_golden(name):
     x, _ = make_inputs(b, t, h, d, seed)
     with torch.no_grad():
         out, _ = run(x, alpha, config=_config(g))
-    s = g.get("row_stride", 1)
-    assert frac_bad(out[:, ::s], g["output"]) <= 1e-3
+    check_output(x, alpha, out, g["output"], name, g.get("row_stride", 1))
 
 
 @pytest.mark.parametrize("b,t,h,d,alpha", [(2, 4096, 3, 64, [0.1, 0.5, 0.9]), (1, 1536, 2, 128, 0.4), (1, 700, 1, 64, 0.5)])
@@ -57,7 +82,7 @@ def test_forward_matches_oracle(b, t, h, d, alpha, one_thread):
     with torch.no_grad():
         out, _ = run(x, alpha)
         ref = o.tao_attention(*(x[k] for k in KEYS), x["fusion_a"], x["fusion_b"], alpha)
-    assert frac_bad(out, ref) <= 1e-3
+    check_output(x, alpha, out, ref, f"b{b} t{t} h{h} d{d}")
 
 
 def rel_l2(a, b):
@@ -73,7 +98,7 @@ def test_backward_matches_reference_golden(name):
     grad = torch.randn(b, t, h, d, generator=gen).to(torch.bfloat16)
     out, grads = run(x, alpha, grad, config=_config(g))
     s = g.get("row_stride", 1)
-    assert frac_bad(out[:, ::s], g["output"]) <= 1e-3
+    check_output(x, alpha, out, g["output"], name, s)
     for k, ref in g["grads"].items():
         mine = grads[k][:, ::s] if k in KEYS else grads[k]
         assert rel_l2(mine, ref) <= 2e-2, (k, rel_l2(mine, ref))
@@ -125,6 +150,26 @@ def test_regularized_writer_training_matches_oracle(one_thread):
     ref = o.tao_attention(*(leaves[k] for k in KEYS), leaves["fusion_a"], leaves["fusion_b"], alpha,
                           "regularized_association")
     ref.backward(grad)
-    assert frac_bad(out, ref.detach()) <= 1e-3
+    check_output(x, alpha, out, ref.detach(), "regularized writer")
     for k in leaves:
         assert rel_l2(grads[k], leaves[k].grad) <= 2e-2, (k, rel_l2(grads[k], leaves[k].grad))
+
+
+def test_fp32_operands_raise_like_the_reference():
+    """Config 1 of the measurement plan (B1 T2048 H4 D64) is fp32.  The reference's
+    training path raises on fp32 operands (its selected read takes tl.dot of a bf16
+    and an fp32 operand, selected_read.py:32: "Both operands must be same dtype"),
+    so tao_attention on B200 raises ValueError for them, before any launch; the same
+    inputs in bf16 run."""
+    import tao_memory_b200 as tb
+    from tao_memory_b200.presets import index_only_page_memo
+    x, _ = make_inputs(1, 2048, 4, 64, seed=0, dtype=torch.float32)
+    xs = {k: t.cuda() for k, t in x.items()}
+    with pytest.raises(ValueError, match="bf16"):
+        tb.tao_attention(*(xs[k] for k in KEYS[:3]), raw_q=xs["raw_q"], raw_k=xs["raw_k"],
+                         fusion_a=xs["fusion_a"], fusion_b=xs["fusion_b"], alpha=0.5,
+                         config=index_only_page_memo())
+    out = tb.tao_attention(*(xs[k].to(torch.bfloat16) for k in KEYS[:3]), raw_q=xs["raw_q"].to(torch.bfloat16),
+                           raw_k=xs["raw_k"].to(torch.bfloat16), fusion_a=xs["fusion_a"],
+                           fusion_b=xs["fusion_b"], alpha=0.5, config=index_only_page_memo())
+    assert out.dtype == torch.bfloat16 and torch.isfinite(out.float()).all()
