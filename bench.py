@@ -13,17 +13,20 @@ Reported (one JSON line on rank 0):
 * value      -- decode tokens/s over all ranks, inputs resident in HBM, steps
                 launched through the C ABI (BatchDecoder), L2 flushed between
                 timed steps (1 GiB memset outside the timed window);
-* e2e        -- the same metric through the public Python API
-                (tao_attention_decode_batch) with the step's inputs handed over in
-                page-locked host memory and the output read back to host memory;
-                host clock per step, the device synchronised at the end of every
-                step (a caller that needs each token's output before the next);
+* e2e        -- the same metric through the public Python API (DecodeSession:
+                the step's inputs handed over in page-locked host memory, the
+                output back in host memory, one captured graph per step); host
+                clock per step, the device synchronised at the end of every step
+                (a caller that needs each token's output before the next);
 * parity     -- the timed steps' outputs and route ids against the CPU oracle
                 continuing the same states (exported before the window) on the
                 same inputs: every element, every request, every head;
 * roofline   -- achieved HBM GB/s of the main decode kernel = algorithmic bytes /
                 CUDA-event duration, against the measured copy bandwidth;
 * cpu_baseline -- the CPU oracle (reference port) on a bounded sample;
+* serving    -- BASELINE.json config 5 (64 requests, prompts 2K-128K, H16 D128,
+                snapshots mid-stream), requests x head groups planned over the
+                ranks by LPT, with the whole step's HBM roofline;
 * train8k    -- BASELINE.json config 2 (tao_attention forward + backward, B4 T8192
                 H12 D64 bf16) with its own value / e2e / roofline / cpu_baseline.
 With N > 1 ranks every rank decodes its own 8 requests and the step's outputs are
@@ -74,6 +77,7 @@ def parse():
     ap.add_argument("--cpu-sample-steps", type=int, default=4)
     ap.add_argument("--workload", default="decode128k", choices=["decode128k", "train8k"])
     ap.add_argument("--no-train", action="store_true", help="leave the nested train8k leg out")
+    ap.add_argument("--no-serving", action="store_true", help="leave the nested serving (config 5) leg out")
     ap.add_argument("--no-parity", action="store_true", help="leave the oracle parity check out")
     ap.add_argument("--decode-variant", type=int, default=None,
                     help="decode kernel of tao_decode_step (0 persistent, 1 CTA/item, 2 warp/item)")
@@ -253,7 +257,7 @@ def run_b200(args, world, rank, local):
 
     # decode schedule: [lead untimed][e2e: E2E_WARM + K][warm-up W][timed K], ending at the
     # config's last decode step (256) when it fits
-    E2E_WARM = 3                      # untimed e2e calls: eager, graph capture, first replay
+    E2E_WARM = 3                      # untimed e2e steps: graph capture, first replays
     n_e2e = E2E_WARM + K
     lead = max(0, DECODE_STEPS - (n_e2e + W + K))
     total_steps = lead + n_e2e + W + K
@@ -289,8 +293,7 @@ def run_b200(args, world, rank, local):
     # ---- e2e: public API, operands in page-locked host memory, output back to host,
     # host clock per step with the device synchronised at the end of each step
     host_in = inputs[lead:lead + n_e2e].cpu().pin_memory()
-    host_x = torch.empty(5, R, 1, HEADS, WIDTH, dtype=torch.bfloat16).pin_memory()
-    host_out = torch.empty(R, 1, HEADS, WIDTH, dtype=torch.bfloat16).pin_memory()
+    session = tb.DecodeSession(states, fa, fb, 0.5, reserve=total_steps + 1)
     e2e_s = []
     for i in range(n_e2e):
         flush_l2()
@@ -298,11 +301,11 @@ def run_b200(args, world, rank, local):
         if world > 1 and i == E2E_WARM:
             dist.barrier()
         t_a = time.perf_counter()
-        host_x.copy_(host_in[i])                                  # the caller's bytes into its buffer
-        tb.tao_attention_decode_batch(host_x[0], host_x[1], host_x[2], raw_q=host_x[3], raw_k=host_x[4],
-                                      fusion_a=fa, fusion_b=fb, alpha=0.5, states=states, out=host_out)
-        torch.cuda.current_stream(device).synchronize()
+        session.inputs.copy_(host_in[i])                          # the caller's bytes into the session
+        session.step()
+        session.wait()                                            # the step's output is in host memory
         e2e_s.append(time.perf_counter() - t_a)
+    session.check()
     e2e_s = e2e_s[E2E_WARM:]
     dec._sync_ptrs()
 
@@ -380,9 +383,9 @@ def run_b200(args, world, rank, local):
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": 5 * R * HEADS * WIDTH * 2,
                 "d2h_bytes_per_step": R * HEADS * WIDTH * 2,
-                "timing": "host clock per step: caller's bytes into its page-locked buffer, "
-                          "tao_attention_decode_batch (host operands; one captured graph: copy in, "
-                          "decode, copy out), stream synchronised; max over ranks",
+                "timing": "host clock per step: the caller's bytes into the session's page-locked "
+                          "buffer, DecodeSession.step() (one captured graph: copy in, decode, copy out), "
+                          "wait() for the output in host memory; max over ranks",
                 "ms_per_step_median": round(statistics.median(e2e_s) * 1e3, 4)},
         "roofline": {"bound": "hbm", "kernel": "decode_fused_kernel (tao_decode_step main kernel, variant %s)"
                      % (1 if args.decode_variant is None else args.decode_variant),
@@ -458,6 +461,130 @@ def cpu_baseline_decode(host_states, sample_steps):
             "kind": "port",
             "sample": f"{n} decode tokens over {len(picked)} exported 128K-context requests "
                       f"(H{HEADS} D{WIDTH}), oracle/tao_oracle.py on the host CPU"}
+
+
+# ---------------------------------------------------------------------------
+# Serving workload: 64 requests, prompts log-uniform in
+# 2K-128K, H16 D128, 128 decode steps, snapshots exported / imported after step 64,
+# requests x head groups planned over the ranks by LPT (tao_memory_b200.shard)
+# ---------------------------------------------------------------------------
+SV_REQUESTS, SV_HEADS, SV_WIDTH, SV_STEPS, SV_SNAPSHOT_AT = 64, 16, 128, 128, 64
+
+
+def serving_lengths(n=SV_REQUESTS, seed=71):
+    import math
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    lo, hi = math.log(2048), math.log(131072)
+    return [int(round(math.exp(lo + (hi - lo) * torch.rand(1, generator=g).item()))) for _ in range(n)]
+
+
+def run_serving(args, world, rank, local):
+    """Config 5 on this rank's LPT shards: prefill every shard (its head group of its
+    request), decode the config's 128 steps with every request's state exported and
+    imported after step 64, time the last K steps (device events, L2 flushed between
+    steps).  A step decodes one token of every request on the rank; states of one head
+    count decode as one batch."""
+    import torch
+    import torch.distributed as dist
+    import tao_memory_b200 as tb
+    from tao_memory_b200 import StreamCache
+    from tao_memory_b200.presets import index_only_page_memo
+    from tao_memory_b200.shard import plan_imbalance, plan_lpt
+    from tao_memory_b200.stream import decode_bytes
+    device = torch.device("cuda", local)
+    lengths = serving_lengths()
+    plan = plan_lpt(lengths, SV_HEADS, SV_WIDTH, world)
+    mine = [s for s in plan if s.rank == rank]
+    K, W = args.steps, args.warmup
+    lead = max(0, SV_STEPS - W - K)
+    gen = torch.Generator(device=device)
+    fa = (torch.randn(SV_HEADS, SV_WIDTH, 3, device=device, generator=gen.manual_seed(5)) * 0.02).to(torch.bfloat16)
+    fb = (torch.randn(SV_HEADS, SV_WIDTH, 3, device=device, generator=gen) * 0.02).to(torch.bfloat16)
+    t0 = time.time()
+    states, groups = [], {}
+    for i, sh in enumerate(mine):
+        hh = sh.head_hi - sh.head_lo
+        st = tb.new_state(1, index_only_page_memo())
+        gen.manual_seed(20_000 + sh.request)
+        pos, L = 0, lengths[sh.request]
+        while pos < L:
+            w = min(16384, L - pos)
+            x = torch.randn(5, 1, w, SV_HEADS, SV_WIDTH, device=device, generator=gen).to(torch.bfloat16)
+            x = x[:, :, :, sh.head_lo:sh.head_hi].contiguous()
+            tb.tao_attention_prefill(x[0], x[1], x[2], raw_q=x[3], raw_k=x[4], fusion_a=fa[sh.head_lo:sh.head_hi],
+                                     fusion_b=fb[sh.head_lo:sh.head_hi], alpha=0.6, state=st, position=pos)
+            pos += w
+        states.append(st)
+        groups.setdefault((hh, sh.head_lo), []).append(i)
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    steps = lead + W + K
+    tokens_in = {key: torch.randn(steps, 5, len(idx), 1, key[0], SV_WIDTH, device=device,
+                                  generator=gen.manual_seed(30_000 + rank * 97 + key[1])).to(torch.bfloat16)
+                 for key, idx in groups.items()}
+    outs = {key: torch.empty(len(idx), 1, key[0], SV_WIDTH, dtype=torch.bfloat16, device=device)
+            for key, idx in groups.items()}
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    clean = torch.ones(L2_CLEAN_BYTES // 4, dtype=torch.float32, device=device)
+
+    def step(i):
+        for (hh, lo), idx in groups.items():
+            x = tokens_in[(hh, lo)][i]
+            tb.tao_attention_decode_batch(x[0], x[1], x[2], raw_q=x[3], raw_k=x[4], fusion_a=fa[lo:lo + hh],
+                                          fusion_b=fb[lo:lo + hh], alpha=0.6,
+                                          states=[states[j] for j in idx], out=outs[(hh, lo)])
+
+    for i in range(lead + W):
+        if i == min(SV_SNAPSHOT_AT, lead):
+            states[:] = [StreamCache.from_export(st.export()) for st in states]
+        step(i)
+    torch.cuda.synchronize()
+    algo = 0
+    base = [st.position for st in states]
+    for i in range(K):
+        for st, p in zip(states, base):
+            st.position = p + i
+        algo += decode_bytes(states)
+    for st, p in zip(states, base):
+        st.position = p
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    if world > 1:
+        dist.barrier()
+    for i in range(K):
+        flush.zero_()
+        clean.sum()
+        starts[i].record()
+        step(lead + W + i)
+        stops[i].record()
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in zip(starts, stops))
+    tot = torch.tensor([ms, algo], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(tot[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot[1:], op=dist.ReduceOp.SUM)
+    ms, algo = tot.tolist()
+    peaks, kind = measured_peaks()
+    achieved = algo / (ms * 1e-3) / 1e9   # all ranks' bytes over the slowest rank's time
+    return {
+        "metric": "serving decode tok/s (64 requests, 2K-128K prompts)", "unit": "tok/s",
+        "value": round(SV_REQUESTS * K / (ms * 1e-3), 1), "steps": K, "warmup": W,
+        "ms_per_step": round(ms / K, 4), "n_gpus": world, "scaling": "strong",
+        "config": {"workload": "serving (BASELINE.json config 5)", "requests": SV_REQUESTS, "heads": SV_HEADS,
+                   "head_dim": SV_WIDTH, "prompts": "log-uniform 2K-128K (seed 71)",
+                   "decode_steps": SV_STEPS, "timed": f"steps {lead + W}..{lead + W + K - 1}",
+                   "snapshot": f"every state exported and imported after decode step {min(SV_SNAPSHOT_AT, lead)}",
+                   "plan": f"LPT over requests x head groups, {len(plan)} shards, imbalance "
+                           f"{plan_imbalance(plan, world):.3f}" if world > 1 else "1 GPU",
+                   "prefill_s": round(prefill_s, 1),
+                   "l2": "flushed between timed steps"},
+        "roofline_step": {"bound": "hbm", "achieved": round(achieved, 1), "peak": float(peaks["hbm_gbs"]),
+                          "unit": "GB/s", "frac": round(achieved / float(peaks["hbm_gbs"]), 4),
+                          "peak_kind": kind + " (copy bandwidth)",
+                          "algorithmic_bytes_per_step": int(algo / K),
+                          "basis": "whole decode step (all launches of every batch) on the device clock"},
+    }
 
 
 # ---------------------------------------------------------------------------
@@ -712,7 +839,12 @@ def reference_triton(args):
            "source": "baseline/_ref (pip install --no-deps of the reference, unmodified)"}
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    # decode @128K: one request prefilled, then decode steps timed by CUDA events
+    # decode @128K: one request prefilled, then timed decode steps in both configurations
+    # (eager and graph); the state moves between them through export / from_export.  The
+    # local attention of this torch build runs through cuDNN, which plans once per new
+    # (query, key) length: a decode token's key count cycles through 513..768, so one full
+    # cycle of 256 untimed decode steps first leaves every plan built and the timed steps
+    # measure the steady state.
     try:
         gen = torch.Generator(device=dev).manual_seed(4242)
         fa = (torch.randn(HEADS, WIDTH, 3, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
@@ -720,7 +852,7 @@ def reference_triton(args):
         K, W = args.steps, max(args.warmup, 3)
         t0 = time.time()
         with torch.inference_mode():
-            st = ref.new_state(LAYER, ref_preset(graph=True))
+            st = ref.new_state(LAYER, ref_preset(graph=False))
             pos = 0
             while pos < args.context:
                 w = min(16384, args.context - pos)
@@ -731,33 +863,51 @@ def reference_triton(args):
                 pos += w
             torch.cuda.synchronize()
             prefill_s = time.time() - t0
-            xs = torch.randn(W + K, 5, 1, 1, HEADS, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
-            for i in range(W):
-                _, st = ref.tao_attention_decode(*xs[i, :3], raw_q=xs[i, 3], raw_k=xs[i, 4], fusion_a=fa,
+            snap = st.export()
+            t0 = time.time()
+            warm = torch.randn(256, 5, 1, 1, HEADS, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+            for i in range(256):
+                _, st = ref.tao_attention_decode(*warm[i, :3], raw_q=warm[i, 3], raw_k=warm[i, 4], fusion_a=fa,
                                                  fusion_b=fb, alpha=0.5, state=st, position=st.get_pos())
             torch.cuda.synchronize()
-            starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-            stops = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-            t_host = time.perf_counter()
-            for i in range(K):
-                starts[i].record()
-                _, st = ref.tao_attention_decode(*xs[W + i, :3], raw_q=xs[W + i, 3], raw_k=xs[W + i, 4],
-                                                 fusion_a=fa, fusion_b=fb, alpha=0.5, state=st,
-                                                 position=st.get_pos())
-                stops[i].record()
-            torch.cuda.synchronize()
-            host_s = time.perf_counter() - t_host
-            ms = [a.elapsed_time(b) for a, b in zip(starts, stops)]
+            plan_warm_s = time.time() - t0
             st.release_execution()
-        per_tok = max(sum(ms) / K, host_s * 1e3 / K)
+            modes = {}
+            for graph in (False, True):
+                saved = dict(snap, config=dict(snap["config"], q1_history_region_graph=graph))
+                run = ref.StreamCache.from_export(saved)
+                xs = torch.randn(W + K, 5, 1, 1, HEADS, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+                for i in range(W):
+                    _, run = ref.tao_attention_decode(*xs[i, :3], raw_q=xs[i, 3], raw_k=xs[i, 4], fusion_a=fa,
+                                                      fusion_b=fb, alpha=0.5, state=run, position=run.get_pos())
+                torch.cuda.synchronize()
+                starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+                stops = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+                t_host = time.perf_counter()
+                for i in range(K):
+                    starts[i].record()
+                    _, run = ref.tao_attention_decode(*xs[W + i, :3], raw_q=xs[W + i, 3], raw_k=xs[W + i, 4],
+                                                      fusion_a=fa, fusion_b=fb, alpha=0.5, state=run,
+                                                      position=run.get_pos())
+                    stops[i].record()
+                torch.cuda.synchronize()
+                host_s = time.perf_counter() - t_host
+                ms = [a.elapsed_time(b) for a, b in zip(starts, stops)]
+                run.release_execution()
+                per_tok = max(sum(ms) / K, host_s * 1e3 / K)
+                modes["graph" if graph else "eager"] = {
+                    "value": round(1e3 / per_tok, 1), "ms_per_token": round(per_tok, 4),
+                    "device_ms_per_token": round(sum(ms) / K, 4), "host_ms_per_token": round(host_s * 1e3 / K, 4)}
+        best = max(modes.values(), key=lambda m: m["value"])
         out["decode128k"] = {
-            "value": round(1e3 / per_tok, 1), "unit": UNIT,
-            "ms_per_token": round(per_tok, 4), "device_ms_per_token": round(sum(ms) / K, 4),
-            "host_ms_per_token": round(host_s * 1e3 / K, 4), "steps": K, "warmup": W,
-            "prefill_s": round(prefill_s, 1),
-            "how": "one 131,072-token request (H12 D64 bf16, index_only_page_memo(graph=True)); the "
-                   "reference serves batch 1, so 8 requests run one after another and the rate is "
-                   "1 / time per token (the larger of the device and host time)"}
+            "value": best["value"], "unit": UNIT, "modes": modes, "steps": K, "warmup": W,
+            "prefill_s": round(prefill_s, 1), "plan_warmup_s": round(plan_warm_s, 1),
+            "how": "one 131,072-token request (H12 D64 bf16, index_only_page_memo(graph=False) for the prefill), "
+                   "256 untimed decode steps (one cycle of key lengths, so torch's cuDNN attention plans are "
+                   "built), then decoded from the 131,072-token snapshot in index_only_page_memo(graph=False) "
+                   "and (graph=True) through export / from_export; "
+                   "the reference serves batch 1, so 8 requests run one after another and the rate is "
+                   "1 / time per token (the larger of the device and host time); value = the faster mode"}
     except Exception as e:   # noqa: BLE001
         out["decode128k"] = {"unavailable": f"{type(e).__name__}: {e}"}
     torch.cuda.empty_cache()
@@ -836,6 +986,11 @@ def main():
                 result["cpu_baseline"] = None
             del states, exported, timed_inputs, outs
             torch.cuda.empty_cache()
+            if not args.no_serving:
+                serving = run_serving(args, world, rank, local)
+                if rank == 0:
+                    result["serving"] = serving
+                torch.cuda.empty_cache()
             if not args.no_train:
                 train = run_train_bench(args, world, rank, local)
                 if rank == 0:

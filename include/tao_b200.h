@@ -43,7 +43,13 @@ extern "C" {
  * 1 = feature-mass read (feature-mass writer, association_writer.py:43-53 via
  * tao_stream.py:362-367); tao_decode_step serves fine_read 1 with its default
  * decode kernel (variant 1) for up to 256 selected fines, tao_stream_decode_noalloc
- * refuses it. */
+ * refuses it.  coarse = 1 selects the coarse value branch (TaoConfig
+ * coarse_index_only=False, the historical default): every completed page carries a
+ * coarse matrix C_page = bf16(sum_s bf16(exp(bf16(z_s - page_z))) * C_s) built when the
+ * page closes (tao_stream.py:486-500), every query reads all completed pages'
+ * matrices (tao_stream.py:299-305) and the pointwise fusion gains its coarse term;
+ * it needs fine_read 0 and states with page_c / coarse_w buffers; decode steps then
+ * run through the tao_stream_step kernels. */
 typedef struct TaoPolicy {
   int32_t fine_tokens;
   int32_t local_keep;
@@ -54,6 +60,7 @@ typedef struct TaoPolicy {
   int32_t budget_offset;
   int32_t route_cap;
   int32_t fine_read;
+  int32_t coarse;
 } TaoPolicy;
 
 /* Device-resident descriptor of one request's one-layer state.  The host writes
@@ -70,6 +77,10 @@ typedef struct TaoPolicy {
  *   route_pages             : int32 [H][route_cap]   pages kept by the page top-K
  *   counters                : int32 [H], zero-initialised; per-head arrival counters
  *                             of the fused decode kernel (reset by their last user)
+ *   page_c                  : [H][cap_fines/8 + 1][D][D]  coarse matrix of each
+ *                             completed page (coarse value branch only, else NULL)
+ *   coarse_w                : [H][cap_fines/8 + 1][D]  softmax over the completed
+ *                             pages of page_z (coarse value branch only, else NULL)
  */
 typedef struct TaoState {
   void* k_ring;
@@ -93,6 +104,8 @@ typedef struct TaoState {
   int32_t arrive;        /* internal: per-step arrival counter, keep 0 */
   int32_t route_refreshes;
   int32_t seal_events;
+  void* page_c;
+  void* coarse_w;
 } TaoState;
 
 const char* tao_last_error(void);
@@ -284,6 +297,13 @@ typedef struct TaoTrainBuffers {
  * softmax writer's z), and tao_train_backward returns dC in grads->dC for the caller
  * to differentiate; the library's writer backward then carries the z path only. */
 #define TAO_TRAIN_CALLER_FINE_C 1
+/* TaoTrainBuffers.flags bit for callers that apply the pointwise fusion themselves
+ * (the coarse value branch fuses three terms, operator.py:21-39): tao_train_forward
+ * then writes out = fine = bf16(bf16(num) / den) (zero before position 768) instead
+ * of the fused output, and tao_train_backward takes grad_out = d(fine) and the
+ * caller's d(local) in grads->d_local (read, not written); it returns no raw_q
+ * gradient of the gate and no fusion-parameter gradients (zero). */
+#define TAO_TRAIN_EXTERNAL_FUSION 2
 
 /* S = T/256 - 1 sealed blocks (0 for T <= 768), pages = ceil(S/8), and the
  * largest number of selected fines any query of a T-token sequence reads. */

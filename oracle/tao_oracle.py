@@ -252,14 +252,37 @@ def fusion_weighted_sum(rho, local, coarse, fine, gain):
     return _r(_r(lt + ct) + ft).to(local.dtype)
 
 
-def fuse_inference(raw_q, local, fine, fa, fb, alpha, fine_on):
+def fuse_inference(raw_q, local, fine, fa, fb, alpha, fine_on, coarse=None, coarse_on=False):
     """operator.py:86-99: 3-way pointwise gate; no history -> local."""
-    if not fine_on:
+    if not (fine_on or coarse_on):
         return local
-    score = fusion_scores(raw_q, fa, fb, False, True)
+    score = fusion_scores(raw_q, fa, fb, coarse_on, fine_on)
     rho = F.softmax(score, dim=-1).to(raw_q.dtype)
     gain = torch.full((), 2 * alpha, dtype=raw_q.dtype)
-    return fusion_weighted_sum(rho, local, torch.zeros_like(fine), fine, gain)
+    return fusion_weighted_sum(rho, local, torch.zeros_like(fine) if coarse is None else coarse, fine, gain)
+
+
+def page_matrix(page_fine_z, page_z, page_fine_c):
+    """Coarse page matrix of a completed page (tao_stream.py:486-500, softmax
+    writer): w_s = bf16(exp(bf16(z_s - page_z))) per fine s of the page, then
+    C_page = bf16(sum_s w_s[d] * C_s[d, e]) (einsum in fp32, one rounding).
+    page_fine_z [B,H,8,D], page_z [B,H,D], page_fine_c [B,H,8,D,D] -> [B,H,D,D]."""
+    dt = page_fine_z.dtype
+    weight = (page_fine_z - page_z.unsqueeze(2)).exp().to(dt)
+    with torch.autocast(device_type="cpu", enabled=False):
+        return torch.einsum("bhsd,bhsde->bhde", weight, page_fine_c).to(dt)
+
+
+def coarse_read(h, page_z, page_c):
+    """Coarse value read (tao_stream.py:299-305): over the completed pages p,
+    coarse = bf16(sum_p sum_d bf16(h[d] * softmax_p(page_z)[p, d]) * C_p[d, e]).
+    h [B,T,H,D] (bf16 softmax of raw_q), page_z [B,H,P,D] (completed pages only),
+    page_c [B,H,P,D,D]."""
+    dt = h.dtype
+    weight = F.softmax(page_z, dim=2).to(dt)
+    chv = (h.unsqueeze(3) * weight[:, None]).to(dt)
+    with torch.autocast(device_type="cpu", enabled=False):
+        return torch.einsum("bthpd,bhpde->bthe", chv, page_c).to(dt)
 
 
 # --------------------------------------------------------------------------
@@ -271,9 +294,12 @@ class OracleStream:
 
     FINE, KEEP, GROUP, PERIOD, STAGGER = 256, 512, 8, 24, 2
 
-    def __init__(self, layer_index=0, fine_writer="softmax"):
+    def __init__(self, layer_index=0, fine_writer="softmax", coarse_index_only=True):
         self.layer_index = layer_index
         self.fine_writer = fine_writer
+        self.coarse_index_only = coarse_index_only
+        self.page_c = []               # [1,H,D,D] per completed page (coarse value branch only)
+        self.coarse_parts, self.last_coarse = [], None
         self.pending_gram = self.pending_cross = None   # fp32 writer statistics (association writers)
         self.pending_mass = None                        # fp32 feature mass (feature-mass writers)
         self.pending_square_mass = None                 # fp32 sum u*u (structured-Gram writer)
@@ -344,6 +370,9 @@ class OracleStream:
         page_z, fine_z = self._page_tables(dtype)
         page_weight = F.softmax(page_z, dim=2).to(dtype)
         hv = (h.unsqueeze(3) * page_weight[:, None]).to(dtype)
+        if self.pages and not self.coarse_index_only:
+            self.coarse_parts.append(coarse_read(h, page_z[:, :, :len(self.pages)],
+                                                 torch.stack(self.page_c, dim=2)))
         if refresh:
             self._route(hv[:, :1], page_z, fine_z)
         ids = self.route_ids[1].expand(-1, raw_q.shape[1], -1, -1)
@@ -355,7 +384,11 @@ class OracleStream:
         return fine_read(hv, page_z, fine_z, ids, self.fine_c, self.GROUP)[-1]
 
     def read(self, raw_q, position):
-        """_read_progressive (tao_stream.py:196-227); returns (fine, fine_on)."""
+        """_read_progressive (tao_stream.py:196-227); returns (fine, fine_on); the
+        coarse read of the same segments is left in ``last_coarse`` (None when no
+        page is complete or the pages are index-only)."""
+        self.coarse_parts = []
+        self.last_coarse = None
         if not self.pages and not self.pending:
             return torch.zeros_like(raw_q), False
         first_fine = self.serve_limit
@@ -373,6 +406,8 @@ class OracleStream:
             if refresh:
                 self.route_refreshes += 1
             offset += count
+        if self.coarse_parts:
+            self.last_coarse = torch.cat(self.coarse_parts, dim=1)
         return torch.cat(out, dim=1), True
 
     def seal(self, raw_k, v):
@@ -412,6 +447,10 @@ class OracleStream:
             zs = torch.stack(self.pending, dim=2)
             pz = (self.pending_mass.log().to(zs.dtype) if self.fine_writer in FEATURE_WRITERS
                   else torch.logsumexp(zs, dim=2).to(zs.dtype))
+            if not self.coarse_index_only:
+                if self.fine_writer != "softmax":
+                    raise NotImplementedError("coarse value pages are restated for the softmax writer")
+                self.page_c.append(page_matrix(zs, pz, self.fine_c[:, :, -self.GROUP:]))
             self.pages.append((pz, zs))
             self.pending = []
 
@@ -427,6 +466,7 @@ class OracleStream:
             raise ValueError("chunk crosses a fine seal boundary")
         local = local_attention(q, ak, av)
         fine, fine_on = self.read(raw_q, self.position)
+        coarse = self.last_coarse
         if ak.shape[1] == self.serve_limit:
             self.fine_seal_events += 1
             self.seal(ar[:, :self.FINE], av[:, :self.FINE])
@@ -434,7 +474,7 @@ class OracleStream:
                           ar[:, -self.KEEP:].clone())
         else:
             self.local = (ak, av, ar)
-        return local, fine, fine_on
+        return local, fine, fine_on, coarse
 
     def step(self, q, k, v, raw_q, raw_k, fa, fb, alpha):
         """tao_attention_prefill (operator.py:70-127): chunked at seal boundaries."""
@@ -443,8 +483,9 @@ class OracleStream:
         while start < q.shape[1]:
             width = self.next_chunk(q.shape[1] - start)
             sl = slice(start, start + width)
-            local, fine, fine_on = self.process(raw_q[:, sl], raw_k[:, sl], q[:, sl], k[:, sl], v[:, sl])
-            outs.append(fuse_inference(raw_q[:, sl], local, fine, fa, fb, alpha, fine_on))
+            local, fine, fine_on, coarse = self.process(raw_q[:, sl], raw_k[:, sl], q[:, sl], k[:, sl], v[:, sl])
+            outs.append(fuse_inference(raw_q[:, sl], local, fine, fa, fb, alpha, fine_on,
+                                       coarse, coarse is not None))
             self.position += width
             start += width
         return torch.cat(outs, dim=1)
@@ -458,7 +499,8 @@ class OracleStream:
             "position": self.position,
             "local": None if self.local is None else tuple(map(clone, self.local)),
             "packed_fine_c": None if self.fine_c is None else clone(self.fine_c),
-            "pages": [(clone(pz), None, clone(fz)) for pz, fz in self.pages],
+            "pages": [(clone(pz), clone(self.page_c[i]) if self.page_c else None, clone(fz))
+                      for i, (pz, fz) in enumerate(self.pages)],
             "pending_z": [clone(z) for z in self.pending],
             "pending_gram": None if self.pending_gram is None else clone(self.pending_gram),
             "pending_cross": None if self.pending_cross is None else clone(self.pending_cross),
@@ -472,12 +514,14 @@ class OracleStream:
 
     @classmethod
     def from_export(cls, saved):
-        st = cls(saved["layer_index"], saved.get("config", {}).get("fine_writer", "softmax"))
+        config = saved.get("config", {})
+        st = cls(saved["layer_index"], config.get("fine_writer", "softmax"), config.get("coarse_index_only", True))
         st.position = saved["position"]
         cpu = lambda t: t.detach().to("cpu").clone()
         st.local = None if saved["local"] is None else tuple(map(cpu, saved["local"]))
         st.fine_c = None if saved["packed_fine_c"] is None else cpu(saved["packed_fine_c"])
         st.pages = [(cpu(pz), cpu(fz)) for pz, _, fz in saved["pages"]]
+        st.page_c = [] if st.coarse_index_only else [cpu(pc) for _, pc, _ in saved["pages"]]
         st.pending = [cpu(z) for z in saved["pending_z"]]
         st.pending_gram = None if saved.get("pending_gram") is None else cpu(saved["pending_gram"])
         st.pending_cross = None if saved.get("pending_cross") is None else cpu(saved["pending_cross"])
@@ -569,11 +613,16 @@ def _local_training(q, k, v, fine=256, keep=512):
     return torch.cat((first, second, later.reshape(b, total - 512, heads, d)), dim=1)
 
 
-def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8):
-    """_read_training_group for one 256-query tile (tao_stream.py:596-665)."""
+def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8, page_c=None):
+    """_read_training_group for one 256-query tile (tao_stream.py:596-665);
+    with ``page_c`` (the completed pages' matrices) also the coarse read
+    (tao_stream.py:611-617).  Returns (fine, selected ids, coarse or None)."""
     b, length, heads, d = query.shape
     dt = query.dtype
     h = F.softmax(query, dim=-1).to(dt)
+    coarse_out = None
+    if page_c is not None and completed:
+        coarse_out = coarse_read(h, page_z[:, :, :completed], page_c[:, :, :completed])
     page_weight = F.softmax(page_z, dim=2).to(dt)
     hv = (h.unsqueeze(3) * page_weight[:, None]).to(dt)
     coarse, _, count = routed_counts(completed, pending, group)
@@ -605,22 +654,46 @@ def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8):
         sel_id = cand_ids.gather(-1, sel)
         sel_page = cand_pages.gather(-1, sel)
     num, den = _SelectedRead.apply(hv, seg_w, sel_id, sel_page, fine_c)
-    return (num / den).to(dt), sel_id
+    return (num / den).to(dt), sel_id, coarse_out
 
 
-def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False, writer="softmax"):
+def training_page_matrices(fine_z, fine_c, group=8):
+    """Coarse page matrices of every completed page in training
+    (_training_metadata with n == group, tao_stream.py:552-573): the page's
+    log-partition, then the page matrix as in streaming."""
+    b, heads, s, d = fine_z.shape
+    full = s // group
+    if not full:
+        return None
+    zc = fine_z[:, :, :full * group].reshape(b, heads, full, group, d)
+    pz = torch.logsumexp(zc, dim=3).to(fine_z.dtype)
+    cc = fine_c[:, :, :full * group].reshape(b, heads, full, group, d, d)
+    weight = (zc - pz.unsqueeze(3)).exp().to(fine_z.dtype)
+    with torch.autocast(device_type="cpu", enabled=False):
+        return torch.einsum("bhpsd,bhpsde->bhpde", weight, cc).to(fine_z.dtype)
+
+
+def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False, writer="softmax",
+                  coarse_index_only=True):
     """read_training (tao_stream.py:668-757) with route_interval=1; returns
-    (local, fine, [selected ids per tile])."""
+    (local, fine, [selected ids per tile]); with coarse_index_only=False also the
+    coarse value read as a fourth element (zeros before the first complete page)."""
     local = _local_training(q, k, v)
     b, total, heads, d = q.shape
     if total <= keep_plus(fine):
+        if not coarse_index_only:
+            return local, torch.zeros_like(local), [], torch.zeros_like(local)
         return local, torch.zeros_like(local), []
     fine_z, fine_c = seal_all(raw_k, v, fine, writer)
-    fine_parts, ids = [], []
+    if not coarse_index_only and writer != "softmax":
+        raise NotImplementedError("coarse value pages are restated for the softmax writer")
+    page_c = None if coarse_index_only else training_page_matrices(fine_z, fine_c, group)
+    fine_parts, ids, coarse_parts = [], [], []
     for tile, query in enumerate(raw_q.split(fine, dim=1)):
         visible = max(0, tile - 2)
         if not visible:
             fine_parts.append(torch.zeros_like(query))
+            coarse_parts.append(torch.zeros_like(query))
             continue
         completed, pending = divmod(visible, group)
         pz = []
@@ -631,11 +704,14 @@ def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False, writ
             zp = fine_z[:, :, completed * group:visible].reshape(b, heads, 1, pending, d)
             pz.append(torch.logsumexp(zp, dim=3).to(fine_z.dtype))
         page_z = torch.cat(pz, dim=2)
-        out, sel = _tile_read(query, page_z, fine_z[:, :, :visible], fine_c[:, :, :visible],
-                              completed, pending, group)
+        out, sel, coarse = _tile_read(query, page_z, fine_z[:, :, :visible], fine_c[:, :, :visible],
+                                      completed, pending, group, page_c)
         fine_parts.append(out)
+        coarse_parts.append(torch.zeros_like(query) if coarse is None else coarse)
         if keep_ids:
             ids.append(sel)
+    if not coarse_index_only:
+        return local, torch.cat(fine_parts, dim=1), ids, torch.cat(coarse_parts, dim=1)
     return local, torch.cat(fine_parts, dim=1), ids
 
 
@@ -698,38 +774,48 @@ def keep_plus(fine):
     return 512 + fine
 
 
-def fuse_training(local, raw_q, fine, fine_present, fa, fb, alpha):
-    """operator._fuse_training (operator.py:21-39) with the index-only preset
-    (coarse never present)."""
+def fuse_training(local, raw_q, fine, fine_present, fa, fb, alpha, coarse=None, coarse_present=None):
+    """operator._fuse_training (operator.py:21-39); the coarse term is absent with
+    index-only pages (coarse=None)."""
     dtype = raw_q.dtype
     score = (fa.to(dtype) * raw_q.unsqueeze(-1)).to(dtype)
     score = (score + fb.to(dtype)).to(dtype)
-    count = fine_present.to(torch.int32)
+    if coarse_present is None:
+        coarse_present = torch.zeros_like(fine_present)
+    count = fine_present.to(torch.int32) + coarse_present.to(torch.int32)
     local_bias = count.clamp_min(1).to(dtype).log().to(dtype)
-    coarse_present = torch.zeros_like(fine_present)
     score = torch.stack(((score[..., 0] + local_bias).to(dtype), score[..., 1], score[..., 2]), -1)
     score = torch.stack((score[..., 0], score[..., 1].masked_fill(~coarse_present, -torch.inf),
                          score[..., 2].masked_fill(~fine_present, -torch.inf)), -1)
     rho = F.softmax(score, dim=-1).to(dtype)
     gain = torch.full((), 2 * alpha, dtype=dtype)
-    coarse = torch.zeros_like(local)
+    if coarse is None:
+        coarse = torch.zeros_like(local)
     lt = (rho[..., 0] * (2 * local).to(dtype)).to(dtype)
     ct = (rho[..., 1] * (gain * coarse).to(dtype)).to(dtype)
     ft = (rho[..., 2] * (gain * fine).to(dtype)).to(dtype)
     fused = ((lt + ct).to(dtype) + ft).to(dtype)
-    return torch.where(fine_present, fused, local)
+    return torch.where(coarse_present | fine_present, fused, local)
 
 
-def tao_attention(q, k, v, raw_q, raw_k, fa, fb, alpha, writer="softmax"):
-    """operator.tao_attention (operator.py:42-54), index-only preset.  ``alpha``
-    may be a float or a per-head sequence (heads are independent, so per-head
-    alpha equals one reference call per head slice)."""
-    local, fine, _ = training_read(raw_q, raw_k, v, q, k, writer=writer)
+def tao_attention(q, k, v, raw_q, raw_k, fa, fb, alpha, writer="softmax", coarse_index_only=True):
+    """operator.tao_attention (operator.py:42-54).  ``alpha`` may be a float or a
+    per-head sequence (heads are independent, so per-head alpha equals one
+    reference call per head slice).  coarse_index_only=False adds the coarse value
+    read, present from position 512 + 8 * 256 on (config.first_coarse)."""
+    coarse = coarse_present = None
+    if coarse_index_only:
+        local, fine, _ = training_read(raw_q, raw_k, v, q, k, writer=writer)
+    else:
+        local, fine, _, coarse = training_read(raw_q, raw_k, v, q, k, writer=writer, coarse_index_only=False)
     positions = torch.arange(q.shape[1])[None, :, None, None]
     present = positions >= 768
+    if not coarse_index_only:
+        coarse_present = positions >= 512 + 8 * 256
     if isinstance(alpha, (int, float)):
-        return fuse_training(local, raw_q, fine, present, fa, fb, alpha)
+        return fuse_training(local, raw_q, fine, present, fa, fb, alpha, coarse, coarse_present)
     outs = [fuse_training(local[:, :, i:i + 1], raw_q[:, :, i:i + 1], fine[:, :, i:i + 1],
-                          present, fa[i:i + 1], fb[i:i + 1], float(alpha[i]))
+                          present, fa[i:i + 1], fb[i:i + 1], float(alpha[i]),
+                          None if coarse is None else coarse[:, :, i:i + 1], coarse_present)
             for i in range(q.shape[2])]
     return torch.cat(outs, dim=2)

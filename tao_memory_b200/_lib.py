@@ -19,7 +19,7 @@ class TaoPolicy(ctypes.Structure):
                 ("coarse_group", ctypes.c_int32), ("route_period", ctypes.c_int32),
                 ("layer_stagger", ctypes.c_int32), ("budget_root_scale", ctypes.c_int32),
                 ("budget_offset", ctypes.c_int32), ("route_cap", ctypes.c_int32),
-                ("fine_read", ctypes.c_int32)]
+                ("fine_read", ctypes.c_int32), ("coarse", ctypes.c_int32)]
 
 
 class TaoState(ctypes.Structure):
@@ -33,7 +33,8 @@ class TaoState(ctypes.Structure):
                 ("cap_fines", ctypes.c_int32), ("route_cap", ctypes.c_int32),
                 ("layer_index", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("width", ctypes.c_int32), ("arrive", ctypes.c_int32),
-                ("route_refreshes", ctypes.c_int32), ("seal_events", ctypes.c_int32)]
+                ("route_refreshes", ctypes.c_int32), ("seal_events", ctypes.c_int32),
+                ("page_c", ctypes.c_void_p), ("coarse_w", ctypes.c_void_p)]
 
 
 class TaoError(RuntimeError):

@@ -80,7 +80,7 @@ int fpc_for(int width) { return width == 64 ? 4 : 1; }
 int kblocks_for(int width) { return width == 64 ? 6 : 12; }
 
 struct Layout {
-  size_t err, slot_ids, slot_pages, slot_n, local_part, local_out, fine_part, total;
+  size_t err, slot_ids, slot_pages, slot_n, local_part, local_out, fine_part, coarse_out, total;
   int nslot, msplit, kblocks;
 };
 
@@ -94,7 +94,7 @@ int nslot_for(int w, int period) {
 // feature: the feature-mass read, which serves w == 1 through the prefill kernels
 // (window attention output + one fine partial per query).
 Layout make_layout(int R, int w, int H, int D, int route_cap, int msplit_decode, int period,
-                   bool feature = false) {
+                   bool feature = false, bool coarse = false) {
   Layout L{};
   L.nslot = nslot_for(w, period);
   L.kblocks = kblocks_for(D);
@@ -115,6 +115,8 @@ Layout make_layout(int R, int w, int H, int D, int route_cap, int msplit_decode,
   if (w > 1 || feature) off = align256(off + (size_t)R * w * H * D * 2);
   L.fine_part = off;
   off = align256(off + (size_t)R * w * H * L.msplit * (D + 1) * 4);
+  L.coarse_out = off;   // coarse value branch: bf16 coarse read of every query
+  if (coarse) off = align256(off + (size_t)R * w * H * D * 2);
   L.total = off;
   return L;
 }
@@ -138,9 +140,11 @@ void tao_take_profile_events(cudaEvent_t* start, cudaEvent_t* stop) {
 
 namespace {
 
+// Opt in to more than the default dynamic shared memory when a launch needs most of
+// the default 48 KB (static shared memory of the kernel counts against it too).
 template <typename F>
 int set_smem(F* fn, size_t bytes) {
-  if (bytes > 48 * 1024) {
+  if (bytes > 40 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return fail(TAO_ERR_CUDA, "smem attribute: %s", cudaGetErrorString(e));
   }
@@ -189,6 +193,16 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
     if ((rc = check_launch("prefill_fine_kernel"))) return rc;
   }
   if (prof1) cudaEventRecord(prof1, s);
+  if (a.coarse) {
+    // coarse value read: tiles of qt queries (a power of two, at most QTMAX)
+    using CC = CoarseCfg<D>;
+    int qt = 1;
+    while (qt < a.w && qt < CC::QTMAX) qt *= 2;
+    const size_t cs = CC::smem(qt);
+    if ((rc = set_smem(coarse_read_kernel<D>, cs))) return rc;
+    coarse_read_kernel<D><<<dim3(a.R * a.H, (a.w + qt - 1) / qt), 256, cs, s>>>(a, qt);
+    if ((rc = check_launch("coarse_read_kernel"))) return rc;
+  }
   const size_t fin_smem = (size_t)2 * kFine * D * 2 + (size_t)2 * D * 4;
   if ((rc = set_smem(finalize_kernel<D>, fin_smem))) return rc;
   finalize_kernel<D><<<a.R * a.H, 256, fin_smem, s>>>(a);
@@ -286,6 +300,9 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
                     size_t workspace_bytes, void* stream) {
   if (!states || n_states <= 0 || !host_pos || !host_cap || !host_layer || !policy)
     return fail(TAO_ERR_ARG, "null state, cursor, layer, capacity or policy array");
+  if (policy->coarse)   // the coarse value branch decodes through the stream-step kernels
+    return tao_stream_step(states, n_states, host_pos, host_cap, policy, 1, heads, width, q, k, v, raw_q, raw_k,
+                           fusion_a, fusion_b, alpha, out, workspace, workspace_bytes, stream);
   if (width != 64 && width != 128) return fail(TAO_ERR_ARG, "head width must be 64 or 128, got %d", width);
   if (heads <= 0) return fail(TAO_ERR_ARG, "heads must be positive");
   if (policy->fine_tokens != 256 || policy->local_keep != 512 || policy->coarse_group != 8)
@@ -377,7 +394,7 @@ size_t tao_stream_workspace_bytes(int n_states, int tokens, int heads, int width
     return 0;
   // one fine partial per selected fine covers every decode kernel variant
   return make_layout(n_states, tokens, heads, width, route_cap, route_cap, policy->route_period,
-                     policy->fine_read != 0).total;
+                     policy->fine_read != 0, policy->coarse != 0).total;
 }
 
 int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
@@ -399,6 +416,10 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
     return fail(TAO_ERR_ARG, "invalid routing policy");
   if (policy->fine_read != 0 && policy->fine_read != 1)
     return fail(TAO_ERR_ARG, "policy.fine_read must be 0 or 1, got %d", policy->fine_read);
+  if (policy->coarse != 0 && policy->coarse != 1)
+    return fail(TAO_ERR_ARG, "policy.coarse must be 0 or 1, got %d", policy->coarse);
+  if (policy->coarse && policy->fine_read)
+    return fail(TAO_ERR_ARG, "the coarse value branch is served with the normalised fine read (fine_read 0)");
   const void* ptrs[] = {q, k, v, raw_q, raw_k, fusion_a, fusion_b, out, workspace};
   for (const void* p : ptrs)
     if (!p) return fail(TAO_ERR_ARG, "null tensor pointer");
@@ -433,7 +454,7 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
 
   const int fpc = fpc_for(width);
   const Layout L = make_layout(n_states, tokens, heads, width, route_cap, (mbound + fpc - 1) / fpc,
-                               policy->route_period, policy->fine_read != 0);
+                               policy->route_period, policy->fine_read != 0, policy->coarse != 0);
   if (workspace_bytes < L.total)
     return fail(TAO_ERR_ARG, "workspace too small: %zu < %zu", workspace_bytes, L.total);
 
@@ -466,6 +487,8 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
   a.fine_part = reinterpret_cast<float*>(ws + L.fine_part);
   a.pmax = pmax;
   a.feature = policy->fine_read;
+  a.coarse = policy->coarse;
+  a.coarse_out = reinterpret_cast<tao::bf16*>(ws + L.coarse_out);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return width == 64 ? launch_step<64>(a, L, s) : launch_step<128>(a, L, s);
 }

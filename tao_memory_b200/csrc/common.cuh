@@ -18,6 +18,8 @@ constexpr int kFine = 256;        // tokens per sealed fine block (TaoConfig.fin
 constexpr int kKeep = 512;        // exact tokens kept after a seal (TaoConfig.local_keep)
 constexpr int kWindow = 768;      // serve limit = ring capacity in tokens
 constexpr int kGroup = 8;         // fines per coarse page (TaoConfig.coarse_group)
+// bf16(log 2): the fusion's local bias with two history terms (coarse and fine)
+constexpr float kLocalBiasTwo = 0.69140625f;
 
 // Device error word bits (workspace[0]); read back by tao_stream_check.
 constexpr int kErrWaitTimeout = 1;
@@ -46,6 +48,11 @@ TAO_DEVI uint32_t hmul2u(uint32_t a, uint32_t b) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 // Low / high bf16 of a pair as fp32.
+// Two floats rounded to bf16 (nearest even) and packed, lo in the low half.
+TAO_DEVI uint32_t bf16x2(float lo, float hi) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
 TAO_DEVI float lo_f(uint32_t x) { return __uint_as_float(x << 16); }
 TAO_DEVI float hi_f(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
 

@@ -126,6 +126,8 @@ extern "C" int tao_stream_decode_noalloc(void* const* states, int n_states, cons
     return na_fail(TAO_ERR_ARG, "invalid routing policy");
   if (policy->fine_read != 0)
     return na_fail(TAO_ERR_ARG, "the feature-mass read (policy.fine_read = 1) is served by tao_stream_step");
+  if (policy->coarse != 0)
+    return na_fail(TAO_ERR_ARG, "the coarse value branch (policy.coarse = 1) is served by tao_stream_step");
   for (const void* p : {q, k, v, raw_q, raw_k, fusion_a, fusion_b, (const void*)out})
     if (!p) return na_fail(TAO_ERR_ARG, "null tensor pointer");
   for (const void* p : {q, k, v, raw_q, raw_k, (const void*)out})

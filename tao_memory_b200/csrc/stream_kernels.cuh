@@ -11,10 +11,13 @@
 //   main      : decode: split-K local attention + split-M selected fine read
 //               (query_fresh_fine.py:8-49), HBM-bound, bulk copies into smem
 //   prefill   : window attention (tensor cores) + fine read per 16-query tile
+//   coarse    : coarse value branch only: every query reads the matrices of all
+//               completed pages (tao_stream.py:299-305)
 //   finalize  : combine partials, fine = bf16(bf16(num)/bf16(den)), pointwise
 //               fusion (fusion_pointwise.py:10-92), commit routes, seal the
 //               oldest block when the window reaches 768 (tao_stream.py:56-77,
-//               435-512), refresh the page memo (tao_stream.py:399-416), advance
+//               435-512), refresh the page memo (tao_stream.py:399-416), close a
+//               coarse page (tao_stream.py:486-500), advance
 #pragma once
 #include "../../include/tao_b200.h"
 #include "common.cuh"
@@ -42,6 +45,8 @@ struct StepArgs {
   float* fine_part;     // [R][w][H][msplit][D+1]
   int pmax;             // max pages over the batch (smem sizing)
   int feature;          // 1: feature-mass read of the selected fines (TaoPolicy.fine_read)
+  int coarse;           // 1: coarse value branch (TaoPolicy.coarse)
+  bf16* coarse_out;     // coarse branch: [R][w][H][D] coarse read of the chunk's queries
 };
 
 // Position-derived plan of one chunk (constant history inside a chunk).
@@ -700,6 +705,187 @@ TAO_DEVI void refresh_memo(const TaoState& st, int h, int S, int p_from) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// coarse value branch (TaoPolicy.coarse): page matrices and their read
+// ---------------------------------------------------------------------------
+// Coarse matrix of completed page p of head h (tao_stream.py:486-500):
+// w_s[d] = bf16(exp(bf16(z_s[d] - page_z[p][d]))) for the page's 8 fines, then
+// C_page[d][e] = bf16(sum_s w_s[d] * C_s[d][e]) (fp32 sum in fine order, one rounding).
+// page_z[p] must be final (written by refresh_memo before a barrier).
+template <int D>
+TAO_DEVI void build_page_c(const TaoState& st, int h, int p) {
+  __shared__ float wts[kGroup * 128];
+  const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
+  const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + ((long long)h * st.cap_fines + p * kGroup) * D;
+  const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + h * pstride + (long long)p * D;
+  const bf16* fc = reinterpret_cast<const bf16*>(st.fine_c) + ((long long)h * st.cap_fines + p * kGroup) * D * D;
+  bf16* pc = reinterpret_cast<bf16*>(st.page_c) + (h * pstride + (long long)p * D) * D;
+  for (int idx = threadIdx.x; idx < kGroup * D; idx += blockDim.x) {
+    const int sf = idx / D, d = idx % D;
+    wts[idx] = rb(expf(rb(__fsub_rn(bf(fz[(long long)sf * D + d]), bf(pz[d])))));
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < D * D / 8; idx += blockDim.x) {
+    const int d = idx / (D / 8), e0 = (idx % (D / 8)) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int sf = 0; sf < kGroup; ++sf) {
+      const float w = wts[sf * D + d];
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(fc + ((long long)sf * D + d) * D + e0), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(w, f[e]));
+    }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ow[e] = bf16x2(acc[2 * e], acc[2 * e + 1]);
+    *reinterpret_cast<uint4*>(pc + (long long)d * D + e0) = o;
+  }
+  __syncthreads();
+}
+
+// coarse_w[p][d] = bf16(softmax over the completed pages p < completed of page_z[p][d])
+// (tao_stream.py:299: F.softmax(page_z[:, :, :len(pages)], dim=2)).
+template <int D>
+TAO_DEVI void refresh_coarse_w(const TaoState& st, int h, int completed) {
+  const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
+  const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + h * pstride;
+  bf16* cw = reinterpret_cast<bf16*>(st.coarse_w) + h * pstride;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float mx = -INFINITY;
+    for (int p = 0; p < completed; ++p) mx = fmaxf(mx, bf(pz[(long long)p * D + d]));
+    float sum = 0.f;
+    for (int p = 0; p < completed; ++p) sum += expf(bf(pz[(long long)p * D + d]) - mx);
+    for (int p = 0; p < completed; ++p)
+      cw[(long long)p * D + d] = tobf(__fdiv_rn(expf(bf(pz[(long long)p * D + d]) - mx), sum));
+  }
+}
+
+template <int D>
+struct CoarseCfg {
+  static constexpr int EPT = 16;           // output channels per thread
+  static constexpr int EG = D / EPT;       // threads per query row (4 or 8)
+  static constexpr int QTMAX = 256 / EG;   // queries per CTA at most (64 or 32)
+  static constexpr size_t smem(int qt) { return (size_t)2 * D * D * 2 + (size_t)qt * D * 4 + (size_t)256 * EPT * 4; }
+};
+
+// Coarse value read of a chunk's queries (tao_stream.py:299-305):
+// coarse[q][e] = bf16(sum_p sum_d bf16(h[q][d] * coarse_w[p][d]) * C_p[d][e]) over the
+// completed pages p, with h = bf16(softmax_d(raw_q[q])).  CTA = (request, head) x a
+// tile of qt queries (qt a power of two <= QTMAX); the page matrices stream through a
+// two-stage shared-memory buffer filled by bulk copies (one per page, mbarrier
+// completion, bounded waits).  Thread = (query, 16 output channels, one slice of the
+// d range); slices are summed in order through shared memory.
+// The history of a chunk is fixed (it seals only after its last query), so the pages
+// read are those complete at the chunk's first position.
+template <int D>
+__global__ void __launch_bounds__(256) coarse_read_kernel(StepArgs a, int qt) {
+  using Cfg = CoarseCfg<D>;
+  constexpr int EPT = Cfg::EPT, EG = Cfg::EG;
+  const int r = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  const TaoState& st = *a.states[r];
+  const Plan pl = make_plan(st, a.w);
+  const int Pc = pl.completed;
+  const int q0 = blockIdx.y * qt, nq = min(qt, a.w - q0);
+  if (nq <= 0 || Pc == 0) return;
+  if (!st.page_c || !st.coarse_w) {   // a state without coarse buffers: reported, nothing read
+    if (threadIdx.x == 0) atomicOr(a.err, kErrState);
+    return;
+  }
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int slices = 256 / (qt * EG);
+  const int sl = tid % slices, eg = (tid / slices) % EG, qi = tid / (slices * EG);
+  const int dlen = D / slices, d0 = sl * dlen;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  bf16* cS = reinterpret_cast<bf16*>(dsm);                                // [2][D][D]
+  float* hS = reinterpret_cast<float*>(dsm + (size_t)2 * D * D * 2);      // [qt][D]
+  float* red = hS + qt * D;                                               // [256][EPT]
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ int okflag;
+  const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
+  const bf16* pcb = reinterpret_cast<const bf16*>(st.page_c) + h * pstride * D;
+  const bf16* cwb = reinterpret_cast<const bf16*>(st.coarse_w) + h * pstride;
+  constexpr uint32_t kPageBytes = D * D * 2;
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_expect_tx(&bars[0], kPageBytes);
+    bulk_g2s(cS, pcb, kPageBytes, &bars[0]);
+  }
+  // h = bf16(softmax_d(raw_q)) of the tile's queries, one warp per query
+  for (int i = warp; i < nq; i += 8) {
+    const bf16* x = a.raw_q + (((long long)r * a.w + q0 + i) * a.H + h) * D;
+    float vals[D / 32];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+      vals[j] = bf(x[lane + 32 * j]);
+      mx = fmaxf(mx, vals[j]);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+      vals[j] = expf(vals[j] - mx);
+      sum += vals[j];
+    }
+    sum = warp_sum(sum);
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) hS[i * D + lane + 32 * j] = rb(__fdiv_rn(vals[j], sum));
+  }
+  float acc[EPT];
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) acc[e] = 0.f;
+  const bool live = qi < nq;
+  uint32_t phase[2] = {0, 0};
+  for (int p = 0; p < Pc; ++p) {
+    const int buf = p & 1;
+    if (tid == 0 && p + 1 < Pc) {   // buffer buf ^ 1 was released by the barrier ending p - 1
+      mbar_expect_tx(&bars[buf ^ 1], kPageBytes);
+      bulk_g2s(cS + (buf ^ 1) * D * D, pcb + (long long)(p + 1) * D * D, kPageBytes, &bars[buf ^ 1]);
+    }
+    if (!wait_uniform(&bars[buf], phase[buf], a.err, &okflag)) {
+      // give the copy still in flight its bounded wait before the CTA leaves
+      if (tid == 0 && p + 1 < Pc) mbar_wait(&bars[buf ^ 1], phase[buf ^ 1], a.err);
+      return;
+    }
+    phase[buf] ^= 1;
+    if (live) {
+      const bf16* cp = cS + buf * D * D;
+      for (int d = d0; d < d0 + dlen; ++d) {
+        const float av = rb(__fmul_rn(hS[qi * D + d], bf(cwb[(long long)p * D + d])));
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(cp + d * D + eg * EPT), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(av, f[e]));
+        unpack8(*reinterpret_cast<const uint4*>(cp + d * D + eg * EPT + 8), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[8 + e] = __fadd_rn(acc[8 + e], __fmul_rn(av, f[e]));
+      }
+    }
+    __syncthreads();  // buffer `buf` is refilled at p + 2
+  }
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) red[tid * EPT + e] = acc[e];
+  __syncthreads();
+  if (live && sl == 0) {
+    float sum[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) sum[e] = 0.f;
+    for (int k = 0; k < slices; ++k)
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) sum[e] = __fadd_rn(sum[e], red[(tid + k) * EPT + e]);
+    bf16* o = a.coarse_out + (((long long)r * a.w + q0 + qi) * a.H + h) * D + eg * EPT;
+#pragma unroll
+    for (int e = 0; e < EPT; e += 2) *reinterpret_cast<uint32_t*>(o + e) = bf16x2(sum[e], sum[e + 1]);
+  }
+}
+
 // Softmax writer for one 256-token block of head h (tao_stream.py:66-76).
 template <int D>
 TAO_DEVI void seal_block(const TaoState& st, int h, long long block_pos, int S, uint8_t* smem) {
@@ -809,19 +995,25 @@ __global__ void __launch_bounds__(256) finalize_kernel(StepArgs a) {
       }
       // feature-mass read: bf16 of the fp32 sum, no denominator (association_writer.py:53)
       const float fine = a.feature ? rb(acc) : rb(__fdiv_rn(rb(acc), rb(den)));
-      // pointwise fusion, reference cast chain (fusion_pointwise.py:19-92)
+      // pointwise fusion, reference cast chain (fusion_pointwise.py:19-92); the
+      // coarse term is present once a page is complete in the coarse value branch,
+      // and the local bias is then bf16(log 2) (two history terms)
+      const bool coarse_on = a.coarse && pl.completed > 0;
       const float q = bf(a.raw_q[row * D + d]);
       const bf16* fa = a.fa + ((long long)h * D + d) * 3;
       const bf16* fb = a.fb + ((long long)h * D + d) * 3;
       float s0 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[0]), q)), bf(fb[0])));
-      s0 = rb(__fadd_rn(s0, 0.f));  // local bias log(1) = 0
+      s0 = rb(__fadd_rn(s0, coarse_on ? kLocalBiasTwo : 0.f));  // local bias log(#history terms)
+      const float s1 = coarse_on ? rb(__fadd_rn(rb(__fmul_rn(bf(fa[1]), q)), bf(fb[1]))) : -INFINITY;
       const float s2 = rb(__fadd_rn(rb(__fmul_rn(bf(fa[2]), q)), bf(fb[2])));
-      const float mx = fmaxf(s0, s2);
-      const float e0 = expf(s0 - mx), e2 = expf(s2 - mx);
-      const float sum = e0 + e2;
+      const float mx = fmaxf(fmaxf(s0, s1), s2);
+      const float e0 = expf(s0 - mx), e1 = coarse_on ? expf(s1 - mx) : 0.f, e2 = expf(s2 - mx);
+      const float sum = (e0 + e1) + e2;
       const float rho0 = rb(__fdiv_rn(e0, sum)), rho2 = rb(__fdiv_rn(e2, sum));
+      const float cval = coarse_on ? bf(a.coarse_out[row * D + d]) : 0.f;
+      const float rho1 = coarse_on ? rb(__fdiv_rn(e1, sum)) : 0.f;
       const float lt = rb(__fmul_rn(rho0, rb(__fmul_rn(2.f, local))));
-      const float ct = rb(__fmul_rn(0.f, rb(__fmul_rn(a.gain, 0.f))));
+      const float ct = rb(__fmul_rn(rho1, rb(__fmul_rn(a.gain, cval))));
       const float ft = rb(__fmul_rn(rho2, rb(__fmul_rn(a.gain, fine))));
       outv = rb(__fadd_rn(rb(__fadd_rn(lt, ct)), ft));
     }
@@ -848,6 +1040,12 @@ __global__ void __launch_bounds__(256) finalize_kernel(StepArgs a) {
     seal_block<D>(st, h, pl.start, pl.S, dsm);
     const int p_from = pl.S / kGroup;  // only the page that received the fine changes
     refresh_memo<D>(st, h, pl.S + 1, p_from);
+    if (a.coarse && (pl.S + 1) % kGroup == 0 && st.page_c && st.coarse_w) {
+      // the page closed: its coarse matrix and the softmax over completed pages
+      __syncthreads();
+      build_page_c<D>(st, h, p_from);
+      refresh_coarse_w<D>(st, h, p_from + 1);
+    }
   }
 
   // ---- last CTA of this request advances the cursor
@@ -875,6 +1073,10 @@ __global__ void __launch_bounds__(256) finalize_kernel(StepArgs a) {
 template <int D>
 __global__ void __launch_bounds__(256) memo_rebuild_kernel(TaoState* st, int S, int weights_only) {
   refresh_memo<D>(*st, blockIdx.x, S, weights_only ? S / kGroup + (S % kGroup > 0) : 0);
+  if (st->coarse_w && S >= kGroup) {   // coarse value branch: softmax over the completed pages
+    __syncthreads();
+    refresh_coarse_w<D>(*st, blockIdx.x, S / kGroup);
+  }
 }
 
 }  // namespace tao

@@ -4,6 +4,7 @@
 #include <cstdio>
 
 #include "../../include/tao_b200.h"
+#include "tc_writer.cuh"
 #include "train_backward.cuh"
 
 void tao_set_last_error(const char* msg);
@@ -79,12 +80,20 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
     return rc;
   if (ev1) cudaEventRecord(ev1, s);
   if (g.S > 0) {
-    // 2. writer over all sealed blocks, 3. page prefix table
-    const size_t wsmem = (size_t)2 * 256 * D * 2 + 2 * D * 4;
-    if (!tsmem(writer_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
-    writer_kernel<D><<<B * H * g.S, 128, wsmem, s>>>(rk, v, static_cast<bf16*>(tb.fine_z),
-                                                      static_cast<bf16*>(tb.fine_c), dm,
-                                                      (tb.flags & TAO_TRAIN_CALLER_FINE_C) ? 0 : 1);
+    // 2. writer over all sealed blocks (tcgen05 by default, mma.sync with attention
+    // variant 0), 3. page prefix table
+    const int write_c = (tb.flags & TAO_TRAIN_CALLER_FINE_C) ? 0 : 1;
+    if (attention_variant() == 1) {
+      const size_t wsmem = TcWriterCfg<D>::SMEM;
+      if (!tsmem(tc_writer_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+      tc_writer_kernel<D><<<B * H * g.S, 128, wsmem, s>>>(rk, v, static_cast<bf16*>(tb.fine_z),
+                                                          static_cast<bf16*>(tb.fine_c), dm, write_c, tb.err);
+    } else {
+      const size_t wsmem = (size_t)2 * 256 * D * 2 + 2 * D * 4;
+      if (!tsmem(writer_kernel<D>, wsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+      writer_kernel<D><<<B * H * g.S, 128, wsmem, s>>>(rk, v, static_cast<bf16*>(tb.fine_z),
+                                                        static_cast<bf16*>(tb.fine_c), dm, write_c);
+    }
     const long long n = (long long)B * H * g.pages * D;
     page_prefix_kernel<D><<<(int)((n + 255) / 256), 256, 0, s>>>(
         static_cast<const bf16*>(tb.fine_z), static_cast<bf16*>(tb.page_prefix), dm, g.pages);
@@ -107,6 +116,7 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
   a.pages = g.pages;
   a.mmax = g.mmax;
   a.err = tb.err;
+  a.external_fusion = (tb.flags & TAO_TRAIN_EXTERNAL_FUSION) ? 1 : 0;
   const size_t rsmem = ReadSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the training read kernel");
   if (!tsmem(train_read_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
@@ -137,7 +147,11 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   if (ReadBwdSmem<D>::NQ < 256 && a.npairs > 0 &&
       cudaMemsetAsync(a.dcp, 0, (size_t)B * H * a.npairs * D * D * 2, s) != cudaSuccess)
     return tfail(TAO_ERR_CUDA, "dc_partial memset");
-  fusion_bwd_kernel<D><<<dim3((T + 8 * kFusionRowsPerWarp - 1) / (8 * kFusionRowsPerWarp), B * H), 256, 0, s>>>(a);
+  const dim3 fgrid((T + 8 * kFusionRowsPerWarp - 1) / (8 * kFusionRowsPerWarp), B * H);
+  if (a.external_fusion)
+    split_bwd_kernel<D><<<fgrid, 256, 0, s>>>(a);
+  else
+    fusion_bwd_kernel<D><<<fgrid, 256, 0, s>>>(a);
   if (D == 64 && a.dq_acc && attention_variant() == 1) {
     if (int rc = launch_attention_backward_tc(a.q, a.k, a.v, a.d_local, a.lse, a.dv_row, a.dq, a.dk, a.dv,
                                               a.dq_acc, B, T, H, a.err, s))
@@ -203,6 +217,7 @@ int tao_train_backward(const void* grad_out, const void* q, const void* k, const
   a.mmax = g.mmax;
   a.err = saved->err;
   a.caller_c = (saved->flags & TAO_TRAIN_CALLER_FINE_C) ? 1 : 0;
+  a.external_fusion = (saved->flags & TAO_TRAIN_EXTERNAL_FUSION) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return width == 64 ? train_backward<64>(a, s) : train_backward<128>(a, s);
 }

@@ -24,11 +24,75 @@ struct BwdArgs {
   bf16* dcp;                     // per-(tile, fine) dC partials [B,H,npairs,D,D]
   float* dq_acc;                 // fp32 [B,T,H,D] dQ accumulator (tensor-core path) or null
   int caller_c;                  // 1: fine C came from the caller; writer backward: z path only
+  int external_fusion;           // 1: g is d(fine), d_local comes from the caller (split_bwd_kernel)
   int npairs;                    // sum over tiles of visible fines
   TrainDims dm;
   int pages, mmax;
   int* err;
 };
+
+// Rows (tokens) of one warp in the fusion backward and the external-fusion split.
+constexpr int kFusionRowsPerWarp = 16;
+
+// ---------------------------------------------------------------------------
+// External fusion (the caller applied the pointwise gate to the local and fine
+// outputs and returns their gradients): g holds d(fine), d_local holds the
+// caller's d(local).  This kernel takes the place of fusion_bwd_kernel: it forms
+// the gradients of fine = bf16(bf16(num) / den) (torch's division backward, each
+// op rounded: d num = bf16(d fine / den), d den = -sum_d bf16(d fine * bf16(fine / den)))
+// for rows with history, the attention row dot sum_d d(local) * local, and no
+// raw_q or fusion-parameter gradient (the caller's gate owns those).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) split_bwd_kernel(BwdArgs a) {
+  constexpr int NP = D / 64;
+  const int tile = blockIdx.x, b = blockIdx.y / a.dm.H, h = blockIdx.y % a.dm.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = tile * 8 * kFusionRowsPerWarp + warp * kFusionRowsPerWarp;
+  const int rows = min(kFusionRowsPerWarp, a.dm.T - t0);
+  for (int rr = 0; rr < rows; ++rr) {
+    const int t = t0 + rr;
+    const long long base = ((long long)b * a.dm.T + t) * a.dm.row + (long long)h * D + 2 * lane;
+    const bool present = t >= kWindow;
+    const float den = present ? a.den[((long long)b * a.dm.T + t) * a.dm.H + h] : 1.f;
+    float rowdot = 0.f, dden = 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      const uint32_t dl2 = *reinterpret_cast<const uint32_t*>(a.d_local + base + 64 * p);
+      const uint32_t l2 = __ldg(reinterpret_cast<const unsigned int*>(a.local + base + 64 * p));
+      rowdot += lo_f(dl2) * lo_f(l2) + hi_f(dl2) * hi_f(l2);
+      float dn[2] = {0.f, 0.f};
+      if (present) {
+        const uint32_t g2 = __ldg(reinterpret_cast<const unsigned int*>(a.g + base + 64 * p));
+        const uint32_t n2 = __ldg(reinterpret_cast<const unsigned int*>(a.num + base + 64 * p));
+        const float dfine[2] = {lo_f(g2), hi_f(g2)}, nums[2] = {lo_f(n2), hi_f(n2)};
+        float fine[2], t2[2], dd[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          fine[x] = __fdiv_rn(nums[x], den);
+          dn[x] = __fdiv_rn(dfine[x], den);
+        }
+        rb2(fine[0], fine[1]);
+        rb2(dn[0], dn[1]);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) t2[x] = __fdiv_rn(fine[x], den);
+        rb2(t2[0], t2[1]);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) dd[x] = __fmul_rn(dfine[x], t2[x]);
+        rb2(dd[0], dd[1]);
+        dden += -dd[0] + -dd[1];
+      }
+      *reinterpret_cast<uint32_t*>(a.gn + base + 64 * p) = pack_exact(dn[0], dn[1]);
+      *reinterpret_cast<uint32_t*>(a.d_rq_f + base + 64 * p) = 0u;
+    }
+    rowdot = warp_sum(rowdot);
+    dden = warp_sum(dden);
+    if (lane == 0) {
+      a.gd[((long long)b * a.dm.T + t) * a.dm.H + h] = rb(dden);
+      a.dv_row[((long long)b * a.dm.H + h) * a.dm.T + t] = rowdot;
+    }
+  }
+}
 
 // ---------------------------------------------------------------------------
 // Fusion backward: one warp per (token, head) row, each lane a pair of adjacent
@@ -36,7 +100,6 @@ struct BwdArgs {
 // packed conversion; each warp takes kFusionRowsPerWarp consecutive tokens (the
 // next row's inputs are loaded while the current one is processed), a CTA 8 warps.
 // ---------------------------------------------------------------------------
-constexpr int kFusionRowsPerWarp = 16;
 
 template <int D>
 __global__ void __launch_bounds__(256) fusion_bwd_kernel(BwdArgs a) {

@@ -215,6 +215,7 @@ struct ReadArgs {
   TrainDims dm;
   int pages, mmax, umax;
   int* err;
+  int external_fusion;                   // 1: out = fine (the caller fuses), no pointwise gate here
 };
 
 template <int D>
@@ -248,11 +249,12 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   const long long row = a.dm.row;
   const long long hoff = (long long)h * D;
 
-  if (V == 0) {  // no history: output = local (operator.py:39)
+  if (V == 0) {  // no history: output = local (operator.py:39); external fusion: fine = 0
     for (int idx = tid; idx < nq * (D / 8); idx += 256) {
       const int q = idx / (D / 8), c = idx % (D / 8);
       const long long off = ((long long)b * a.dm.T + q0 + q) * row + hoff + c * 8;
-      *reinterpret_cast<uint4*>(a.out + off) = *reinterpret_cast<const uint4*>(a.local + off);
+      *reinterpret_cast<uint4*>(a.out + off) =
+          a.external_fusion ? make_uint4(0, 0, 0, 0) : *reinterpret_cast<const uint4*>(a.local + off);
     }
     return;
   }
@@ -563,6 +565,11 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
           s2[x] = __fmul_rn(fa[2], qv[x]);
         }
         rb2(fine[0], fine[1]);
+        if (a.external_fusion) {   // the caller applies the pointwise gate: out = fine
+          *reinterpret_cast<uint32_t*>(a.out + base + e) = pack_exact(fine[0], fine[1]);
+          *reinterpret_cast<uint32_t*>(a.num_out + base + e) = pack_exact(nums[0], nums[1]);
+          continue;
+        }
         rb2(s0[0], s0[1]);
         rb2(s2[0], s2[1]);
 #pragma unroll

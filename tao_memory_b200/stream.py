@@ -32,6 +32,7 @@ WRITERS_B200 = ("softmax", "regularized_association", "feature_mass_association"
 # writers whose fines are read with the feature-mass mixture (tao_stream.py:362-367)
 FEATURE_WRITERS = ("feature_mass_association", "structured_gram_association")
 _BF16 = torch.bfloat16
+TRAIN_COARSE = True    # the training path's coarse value branch (tao_memory_b200.training_coarse)
 
 
 def window_start(pos):
@@ -51,8 +52,9 @@ def is_refresh(pos, layer, config):
 
 def check_config(config, training=False):
     """The sm_100a kernels implement the index-only preset with the softmax and
-    regularised-association writers, and for streaming the feature-mass and
-    structured-Gram writers."""
+    regularised-association writers, for streaming also the feature-mass and
+    structured-Gram writers, and the coarse value branch (coarse_index_only=False,
+    the historical default) with the softmax writer."""
     if (config.fine_tokens, config.local_keep, config.coarse_group) != (FINE, KEEP, GROUP):
         raise ValueError("kernels are specialised for fine_tokens=256, local_keep=512, coarse_group=8")
     writers = WRITERS_B200[:2] if training else WRITERS_B200
@@ -60,7 +62,11 @@ def check_config(config, training=False):
         raise NotImplementedError("fine_writer=%r is not implemented on B200 %s(implemented: %s)"
                                   % (config.fine_writer, "training " if training else "", ", ".join(writers)))
     if not config.coarse_index_only:
-        raise NotImplementedError("only coarse_index_only=True (index_only_page_memo) is implemented on B200")
+        if config.fine_writer != "softmax":
+            raise NotImplementedError("the coarse value branch (coarse_index_only=False) is implemented on "
+                                      "B200 with the softmax fine writer")
+        if training and not TRAIN_COARSE:
+            raise NotImplementedError("the coarse value branch is implemented on B200 for streaming")
 
 
 def _structured_matrix(square, cross, mass, count):
@@ -88,13 +94,13 @@ def _structured_matrix(square, cross, mass, count):
 def policy_for(config):
     return _lib.TaoPolicy(FINE, KEEP, GROUP, config.route_period, config.layer_stagger,
                           config.budget_root_scale, config.budget_offset, ROUTE_CAP,
-                          int(config.fine_writer in FEATURE_WRITERS))
+                          int(config.fine_writer in FEATURE_WRITERS), int(not config.coarse_index_only))
 
 
 def _policy_key(config):
     """The configuration fields a captured or cached decode step bakes in."""
     return (config.route_period, config.layer_stagger, config.budget_root_scale, config.budget_offset,
-            config.fine_writer in FEATURE_WRITERS)
+            config.fine_writer in FEATURE_WRITERS, config.coarse_index_only)
 
 
 class _Workspace:
@@ -194,11 +200,15 @@ class StreamCache:
             route_ids=z(heads, ROUTE_CAP, dt=torch.int32),
             route_pages=z(heads, ROUTE_CAP, dt=torch.int32),
             counters=z(heads, dt=torch.int32))
+        if not self.config.coarse_index_only:   # coarse value branch: page matrices and page softmax
+            self._buf["page_c"] = z(heads, pages, width, width)
+            self._buf["coarse_w"] = z(heads, pages, width)
         self.heads, self.width, self.device, self.cap_fines = heads, width, device, cap
         h = _lib.TaoState()
         for name in ("k_ring", "v_ring", "rk_ring", "fine_c", "fine_z", "page_z", "page_w",
-                     "route_ids", "route_pages", "counters"):
-            setattr(h, name, self._buf[name].data_ptr())
+                     "route_ids", "route_pages", "counters", "page_c", "coarse_w"):
+            if name in self._buf:
+                setattr(h, name, self._buf[name].data_ptr())
         h.position = self.position
         h.cap_fines, h.route_cap, h.layer_index = cap, ROUTE_CAP, self.layer_index
         h.heads, h.width = heads, width
@@ -236,6 +246,9 @@ class StreamCache:
         self._buf["fine_z"][:, :s].copy_(old["fine_z"][:, :s])
         self._buf["page_z"][:, :p].copy_(old["page_z"][:, :p])
         self._buf["page_w"][:, :p].copy_(old["page_w"][:, :p])
+        if "page_c" in old:
+            self._buf["page_c"][:, :p].copy_(old["page_c"][:, :p])
+            self._buf["coarse_w"][:, :p].copy_(old["coarse_w"][:, :p])
         for f in ("n_route", "n_chosen", "route_refreshes", "seal_events"):
             setattr(self._host, f, getattr(host, f))
         self._host.position = self.position
@@ -340,8 +353,10 @@ class StreamCache:
                 fine_c = self._buf["fine_c"][:, :s].unsqueeze(0).clone()
                 fz = self._buf["fine_z"]
                 pz = self._buf["page_z"]
+                pc = self._buf.get("page_c")
                 for p in range(s // GROUP):
-                    pages.append((pz[:, p].unsqueeze(0).clone(), None,
+                    pages.append((pz[:, p].unsqueeze(0).clone(),
+                                  None if pc is None else pc[:, p].unsqueeze(0).clone(),
                                   fz[:, p * GROUP:(p + 1) * GROUP].unsqueeze(0).clone()))
                 for i in range((s // GROUP) * GROUP, s):
                     pending.append(fz[:, i].unsqueeze(0).clone())
@@ -399,6 +414,11 @@ class StreamCache:
                 raise ValueError("snapshot fine count does not match its position")
             b["fine_z"][:, :s].copy_(torch.cat(fz, dim=1).to(dev, _BF16))
             b["fine_c"][:, :s].copy_(saved["packed_fine_c"][0].to(dev, _BF16))
+        if "page_c" in b:
+            for p, (_, pc, _) in enumerate(saved["pages"]):
+                if pc is None:
+                    raise ValueError("snapshot of a coarse-value configuration without page matrices")
+                b["page_c"][:, p].copy_(pc.reshape(heads, width, width).to(dev, _BF16))
         h = state._host
         route = saved["route_ids"]
         if route is not None:
@@ -445,7 +465,8 @@ class StreamCache:
         heads, width = self.heads or 0, self.width or 0
         pages, pending = s // GROUP, s % GROUP
         history = (pages * (GROUP + 1) + pending) * (width * width + width) * heads * 2
-        history -= pages * width * width * heads * 2  # index-only pages hold no matrix
+        if self.config.coarse_index_only:
+            history -= pages * width * width * heads * 2  # index-only pages hold no matrix
         local = self.position - window_start(self.position)
         logical_local = local * 2 * heads * width * 2
         physical = 0 if self._buf is None else sum(t.numel() * t.element_size() for t in self._buf.values())
@@ -889,3 +910,130 @@ class BatchDecoder:
         flags = ctypes.c_int(0)
         _lib.check(self.lib.tao_stream_check(self.ws.data_ptr(), ctypes.byref(flags),
                                              torch.cuda.current_stream(self.dev).cuda_stream))
+
+
+class DecodeSession:
+    """A fixed batch of requests decoded one token per step, operands and results
+    in page-locked host memory: the serving loop of one layer for callers whose
+    tokens arrive in, and leave through, host memory.
+
+    ``inputs``: page-locked [5, R, 1, H, D] bf16 (q, k, v, raw_q, raw_k of the next
+    token of every request), filled by the caller before each ``step()``;
+    ``output``: page-locked [R, 1, H, D] bf16, valid after ``wait()``.  ``step()``
+    launches the copy in, the decode step and the copy out; with states configured
+    for graphs (``q1_history_region_graph``) the three are captured once and a step
+    is one graph launch.  ``reserve`` tokens of fine-bank capacity are allocated up
+    front, so the loop allocates nothing and the graph is not captured again within
+    them.  The states advance exactly as with ``tao_attention_decode_batch``.
+    """
+
+    def __init__(self, states, fusion_a, fusion_b, alpha, reserve=4096):
+        self.states = list(states)
+        if not self.states or len({id(s) for s in self.states}) != len(self.states):
+            raise ValueError("a session takes distinct states")
+        devs = {st.device for st in self.states}
+        if None in devs or len(devs) != 1:
+            raise ValueError("the states of a session must be allocated on one device (prefill them first)")
+        self.dev = devs.pop()
+        st0 = self.states[0]
+        self.heads, self.width = st0.heads, st0.width
+        if any((st.heads, st.width) != (self.heads, self.width) for st in self.states):
+            raise ValueError("the states of a session share one head count and width")
+        if any(_policy_key(st.config) != _policy_key(st0.config) for st in self.states):
+            raise ValueError("the states of a session share one routing policy")
+        if st0.config.fine_writer != "softmax":
+            raise ValueError("sessions serve the softmax fine writer")
+        self.r = len(self.states)
+        self.graph_mode = _graph_states(self.states)
+        self.lib = _lib.lib()
+        self.stream = torch.cuda.current_stream(self.dev)
+        with torch.cuda.device(self.dev):
+            self.fa = fusion_a.detach().to(self.dev, _BF16).contiguous()
+            self.fb = fusion_b.detach().to(self.dev, _BF16).contiguous()
+            if self.fa.shape != (self.heads, self.width, 3) or self.fb.shape != self.fa.shape:
+                raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
+            self.alpha = float(alpha)
+            shape = (self.r, 1, self.heads, self.width)
+            self.inputs = torch.zeros((5,) + shape, dtype=_BF16).pin_memory()
+            self.output = torch.zeros(shape, dtype=_BF16).pin_memory()
+            self.stage = torch.zeros((6,) + shape, dtype=_BF16, device=self.dev)
+            self.policy = policy_for(st0.config)
+            self.layers = (ctypes.c_int32 * self.r)(*[st.layer_index for st in self.states])
+            self.pos = (ctypes.c_int64 * self.r)()
+            self.cap = (ctypes.c_int32 * self.r)()
+            nbytes = self.lib.tao_stream_workspace_bytes(self.r, 1, self.heads, self.width, ROUTE_CAP,
+                                                         ctypes.byref(self.policy))
+            self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.dev)
+            _graph_workspaces(self.dev).add(self.ws)
+            nb = self.stage[0].numel() * 2
+            self.copy_dst = (ctypes.c_void_p * 5)(*[self.stage[i].data_ptr() for i in range(5)])
+            self.copy_src = (ctypes.c_void_p * 5)(*[self.inputs[i].data_ptr() for i in range(5)])
+            self.copy_bytes = (ctypes.c_size_t * 5)(*([nb] * 5))
+            self.graph = None
+            self.reserve(reserve)
+
+    def reserve(self, tokens):
+        """Fine-bank capacity for ``tokens`` more tokens of every request (may grow
+        the banks; a captured step is then captured again at the next step)."""
+        grew = False
+        for st in self.states:
+            need = sealed_at(st.position + tokens) + 1
+            if need > st.cap_fines:
+                st._grow(need)
+                grew = True
+        self.ptrs = torch.tensor([st._desc.data_ptr() for st in self.states], dtype=torch.int64,
+                                 device=self.dev)
+        for i, st in enumerate(self.states):
+            self.cap[i] = st.cap_fines
+        if grew:
+            self.graph = None
+
+    def _launch(self, stream):
+        rc = self.lib.tao_copy_host_to_device_many(self.copy_dst, self.copy_src, self.copy_bytes, 5, stream)
+        if rc == 0:
+            rc = self.lib.tao_decode_step(self.ptrs.data_ptr(), self.r, self.pos, self.layers, self.cap,
+                                          ctypes.byref(self.policy), self.heads, self.width,
+                                          *(self.stage[i].data_ptr() for i in range(5)), self.fa.data_ptr(),
+                                          self.fb.data_ptr(), self.alpha, self.stage[5].data_ptr(),
+                                          self.ws.data_ptr(), self.ws.numel(), stream)
+        if rc == 0:
+            rc = self.lib.tao_copy_device_to_host(self.output.data_ptr(), self.stage[5].data_ptr(),
+                                                  self.output.numel() * 2, stream)
+        return rc
+
+    def _capture(self):
+        self.graph = torch.cuda.CUDAGraph()
+        rc = 0
+        self.lib.tao_decode_graph_mode(1)
+        try:
+            with torch.cuda.graph(self.graph, capture_error_mode="relaxed"):
+                rc = self._launch(torch.cuda.current_stream(self.dev).cuda_stream)
+        finally:
+            self.lib.tao_decode_graph_mode(0)
+        _lib.check(rc)
+
+    def step(self):
+        """Decode the token in ``inputs`` for every request (asynchronous)."""
+        for i, st in enumerate(self.states):
+            self.pos[i] = st.position
+            if sealed_at(st.position + 1) + 1 > st.cap_fines:
+                self.reserve(4096)
+        if self.graph_mode:
+            with torch.cuda.stream(self.stream):
+                if self.graph is None:
+                    self._capture()
+                self.graph.replay()
+        else:
+            _lib.check(self._launch(self.stream.cuda_stream))
+        for st in self.states:
+            _bookkeep(st, 1)
+
+    def wait(self):
+        """Block until the last step's ``output`` is in host memory."""
+        self.stream.synchronize()
+        return self.output
+
+    def check(self):
+        """Raise if a kernel of this session reported an error."""
+        flags = ctypes.c_int(0)
+        _lib.check(self.lib.tao_stream_check(self.ws.data_ptr(), ctypes.byref(flags), self.stream.cuda_stream))

@@ -63,7 +63,7 @@ def _regularized_matrices(raw_k, v, s):
     return torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(_BF16)
 
 
-def _forward(q, k, v, raw_q, raw_k, fa, fb, gain, writer="softmax"):
+def _forward(q, k, v, raw_q, raw_k, fa, fb, gain, writer="softmax", flags=0):
     b, t, h, d = q.shape
     dev = q.device
     s, pages, mmax = _geometry(t)
@@ -75,10 +75,9 @@ def _forward(q, k, v, raw_q, raw_k, fa, fb, gain, writer="softmax"):
         num=torch.empty_like(q), den=torch.empty(b, t, h, dtype=torch.float32, device=dev),
         sel=torch.empty(b, t, h, mmax, dtype=torch.int16, device=dev),
         err=torch.zeros(1, dtype=torch.int32, device=dev))
-    flags = 0
     if writer != "softmax" and s > 0:
         bufs["fine_c"].copy_(_regularized_matrices(raw_k, v, s))
-        flags = TAO_TRAIN_CALLER_FINE_C
+        flags |= TAO_TRAIN_CALLER_FINE_C
     desc = _Buffers(*(bufs[n].data_ptr() for n in ("local", "lse", "fine_z", "fine_c", "page_prefix",
                                                    "num", "den", "sel", "err")), mmax, flags)
     out = torch.empty_like(q)
@@ -96,6 +95,7 @@ class _TaoAttention(torch.autograd.Function):
         ctx.save_for_backward(q, k, v, raw_q, raw_k, fa, fb, gain, out, *bufs.values())
         ctx.names = tuple(bufs)
         ctx.writer = writer
+        ctx.external = False
         return out
 
     @staticmethod
@@ -120,6 +120,9 @@ def tao_attention_train(q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, config
     if fusion_a.shape != (heads, width, 3) or fusion_b.shape != (heads, width, 3):
         raise ValueError("fusion_a and fusion_b must have shape [heads, width, 3]")
     gain = _gains(alpha, heads, q.device)
+    if not config.coarse_index_only:
+        from .training_coarse import tao_attention_coarse
+        return tao_attention_coarse(*(t.contiguous() for t in ops), fusion_a, fusion_b, gain)
     fa = fusion_a.to(_BF16)
     fb = fusion_b.to(_BF16)
     return _TaoAttention.apply(*(t.contiguous() for t in ops), fa.contiguous(), fb.contiguous(), gain,

@@ -41,7 +41,9 @@ def _regularized_backward(saved, gr, s):
     gr["dv"][:, :n] += dv
 
 
-def backward(ctx, grad):
+def backward(ctx, grad, d_local=None):
+    """grad: gradient of the fused output, or with ctx.external of the unfused fine
+    output; d_local: the caller's gradient of the local output (external fusion)."""
     from .training import _Buffers
     saved = dict(zip(("q", "k", "v", "raw_q", "raw_k", "fa", "fb", "gain", "out") + ctx.names,
                      ctx.saved_tensors))
@@ -54,7 +56,7 @@ def backward(ctx, grad):
     gr = dict(dq=e(), dk=e(), dv=e(), d_raw_q=e(), d_raw_k=e(),
               d_fusion_a=torch.zeros(h, d, 3, dtype=torch.float32, device=dev),
               d_fusion_b=torch.zeros(h, d, 3, dtype=torch.float32, device=dev),
-              d_local=e(), gn=e(), d_rq_f=e(),
+              d_local=e() if d_local is None else d_local, gn=e(), d_rq_f=e(),
               gd=torch.empty(b, t, h, dtype=torch.float32, device=dev),
               row_dot=torch.empty(b, h, t, dtype=torch.float32, device=dev),
               dC=torch.empty(b, h, s, d, d, dtype=torch.float32, device=dev),
@@ -65,9 +67,11 @@ def backward(ctx, grad):
     gdesc = _Grads(*(gr[n].data_ptr() for n, _ in _Grads._fields_))
     caller_c = ctx.writer != "softmax" and t > 768
     from .training import TAO_TRAIN_CALLER_FINE_C
+    from .training_coarse import TAO_TRAIN_EXTERNAL_FUSION
+    flags = (TAO_TRAIN_CALLER_FINE_C if caller_c else 0) | (TAO_TRAIN_EXTERNAL_FUSION if ctx.external else 0)
     sdesc = _Buffers(*(saved[n].data_ptr() for n in ("local", "lse", "fine_z", "fine_c", "page_prefix",
                                                     "num", "den", "sel", "err")),
-                     saved["sel"].shape[-1], TAO_TRAIN_CALLER_FINE_C if caller_c else 0)
+                     saved["sel"].shape[-1], flags)
     stream = torch.cuda.current_stream(dev).cuda_stream
     _lib.check(_lib.lib().tao_train_backward(
         grad.data_ptr(), *(saved[n].data_ptr() for n in ("q", "k", "v", "raw_q", "raw_k", "fa", "fb", "gain")),

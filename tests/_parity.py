@@ -5,9 +5,10 @@ the parity target), and every element must agree: a failure names how many
 elements are out, the largest error and where it is.
 
 Routing: selections are integers and must be equal.  The one accepted exception
-is a near-tie in the reference's own scores: two candidates whose bf16 scores are
-within one bf16 ulp of the selection threshold can change places when an fp32 sum
-is taken in another order.  ``training_route_flips`` lists every query whose
+is a near-tie in the reference's own scores.  A score is a bf16 rounding of an
+fp32 sum; summed in another order it can land one bf16 ulp away, so two scores
+within two ulps of each other (each may move by one, in opposite directions) can
+change places.  ``training_route_flips`` lists every query whose
 selection differs, proves each difference is such a near-tie against the
 oracle's scores, and the output check then exempts only those queries.
 """
@@ -48,7 +49,8 @@ def bf16_ulp(x):
 
 
 def _near(a, b):
-    return abs(a - b) <= max(bf16_ulp(a), bf16_ulp(b))
+    """Within two bf16 ulps: each of two independently rounded scores may move one."""
+    return abs(a - b) <= 2 * max(bf16_ulp(a), bf16_ulp(b))
 
 
 def training_route_flips(gpu_sel, tiles, heads):
@@ -98,7 +100,8 @@ def _explain(g, r, score, info, bi, qi, hi):
     if set(g) == set(r):   # same fines, another order: neighbours must tie
         for a, c in zip(g, r):
             if a != c and not _near(score[a].item(), score[c].item()):
-                return f"order differs beyond a tie: {g} vs {r}"
+                return (f"order differs beyond a tie: {g} vs {r} (oracle scores of fines {a}, {c}: "
+                        f"{score[a].item()}, {score[c].item()})")
         return ""
     for f in set(g) - set(r):
         if not (_near(score[f].item(), thr) or page_near_tie(f)):

@@ -147,6 +147,15 @@ TRAIN_WRITER_CASES = {
     "train_regularized": ((1, 2048, 2, 64, 0.5, 9), "regularized_association"),
 }
 
+# cases on the historical default TaoConfig() (coarse_index_only=False: completed
+# pages carry a coarse value matrix that every query reads), softmax writer
+DEFAULT_CONFIG_STREAM_CASES = {
+    "stream_coarse": (2, 64, 1, (1500, 1800, 1600), 40, 14),
+}
+DEFAULT_CONFIG_TRAIN_CASES = {
+    "train_coarse": (1, 4608, 1, 64, 0.6, 15),
+}
+
 TRAIN_CASES = {
     # name: (batch, tokens, heads, width, alpha, seed)
     "train_t2048_h2": (1, 2048, 2, 64, 0.5, 4),
@@ -164,6 +173,8 @@ def run_stream(name, mode):
         case, writer = WRITER_CASES[name]
         base = index_only_page_memo()
         config = TaoConfig(**{**base.export(), "fine_writer": writer})
+    elif name in DEFAULT_CONFIG_STREAM_CASES:
+        case, config = DEFAULT_CONFIG_STREAM_CASES[name], TaoConfig()
     else:
         case, config = STREAM_CASES[name], index_only_page_memo()
     heads, width, layer, splits, steps, seed = case
@@ -216,6 +227,8 @@ def run_train(name, mode):
     if name in TRAIN_WRITER_CASES:
         case, writer = TRAIN_WRITER_CASES[name]
         config = TaoConfig(**{**index_only_page_memo().export(), "fine_writer": writer})
+    elif name in DEFAULT_CONFIG_TRAIN_CASES:
+        case, config = DEFAULT_CONFIG_TRAIN_CASES[name], TaoConfig()
     else:
         case, config = TRAIN_CASES[name], index_only_page_memo()
     batch, tokens, heads, width, alpha, seed = case
@@ -237,7 +250,7 @@ def run_train(name, mode):
 
 # Row subsampling applied before saving, to keep the committed fixtures small.
 STRIDE = {"train_pages": 4, "train_t3072_b2": 2, "train_t2048_h2": 2, "stream_pages": 3,
-          "stream_h2d64": 2}
+          "stream_h2d64": 2, "stream_coarse": 2, "train_coarse": 2}
 
 
 def compact(name, result):
@@ -250,7 +263,8 @@ def compact(name, result):
         for k in ("q", "k", "v", "raw_q", "raw_k"):
             result["grads"][k] = result["grads"][k][:, ::stride].clone()
     else:
-        steps = (WRITER_CASES[name][0] if name in WRITER_CASES else STREAM_CASES[name])[4]
+        steps = (WRITER_CASES[name][0] if name in WRITER_CASES else
+                 DEFAULT_CONFIG_STREAM_CASES.get(name) or STREAM_CASES[name])[4]
         out = result["output"]
         result["decode_output"] = out[:, -steps:].clone()
         result["output"] = out[:, ::stride].clone()
@@ -274,7 +288,8 @@ def main():
         check_fast()
         install_fast(args.reference)
     mode = "reference+fast-inference-kernels" if args.fast else "reference (interpreted Triton, patched)"
-    cases = args.cases or [*STREAM_CASES, *WRITER_CASES, *TRAIN_CASES, *TRAIN_WRITER_CASES]
+    cases = args.cases or [*STREAM_CASES, *WRITER_CASES, *TRAIN_CASES, *TRAIN_WRITER_CASES,
+                           *DEFAULT_CONFIG_STREAM_CASES, *DEFAULT_CONFIG_TRAIN_CASES]
     if args.compact_only:
         for name in cases:
             path = os.path.join(HERE, name + ".pt")
@@ -284,7 +299,8 @@ def main():
         return
     for name in cases:
         t0 = time.time()
-        result = run_stream(name, mode) if name in STREAM_CASES or name in WRITER_CASES else run_train(name, mode)
+        streaming = name in STREAM_CASES or name in WRITER_CASES or name in DEFAULT_CONFIG_STREAM_CASES
+        result = run_stream(name, mode) if streaming else run_train(name, mode)
         torch.save(compact(name, result), os.path.join(HERE, name + ".pt"))
         print(f"{name}: {time.time() - t0:.1f}s ({mode})", flush=True)
 

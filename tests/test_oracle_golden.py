@@ -10,8 +10,9 @@ from oracle.inputs import make_inputs, digest
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 STREAM = ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized", "stream_feature_mass",
-          "stream_structured_gram"]
-TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages", "train_regularized"]
+          "stream_structured_gram", "stream_coarse"]
+TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages", "train_regularized",
+         "train_coarse"]
 KEYS = ("q", "k", "v", "raw_q", "raw_k")
 
 
@@ -25,7 +26,8 @@ def test_stream_oracle_matches_reference(name, one_thread):
     heads, width, layer, splits, steps, seed = g["case"]
     x, _ = make_inputs(1, sum(splits) + steps, heads, width, seed)
     assert digest(*(x[k] for k in (*KEYS, "fusion_a", "fusion_b"))) == g["input_digest"]
-    st = o.OracleStream(layer, g.get("config", {}).get("fine_writer", "softmax"))
+    config = g.get("config", {})
+    st = o.OracleStream(layer, config.get("fine_writer", "softmax"), config.get("coarse_index_only", True))
     outs, ids, pos = [], [], 0
     for n in list(splits) + [1] * steps:
         sl = slice(pos, pos + n)
@@ -51,8 +53,11 @@ def test_stream_oracle_matches_reference(name, one_thread):
     mine_snap = st.export()
     assert mine_snap["position"] == snap["position"]
     assert torch.equal(mine_snap["packed_fine_c"], snap["packed_fine_c"])
-    for (pz, _, fz), (rpz, _, rfz) in zip(mine_snap["pages"], snap["pages"]):
+    for (pz, pc, fz), (rpz, rpc, rfz) in zip(mine_snap["pages"], snap["pages"]):
         assert torch.equal(pz, rpz) and torch.equal(fz, rfz)
+        assert (pc is None) == (rpc is None)
+        if rpc is not None:   # coarse page matrix (coarse_index_only=False)
+            assert torch.equal(pc, rpc)
     for z, rz in zip(mine_snap["pending_z"], snap["pending_z"]):
         assert torch.equal(z, rz)
     for key in ("pending_gram", "pending_cross", "pending_mass", "pending_square_mass"):
@@ -70,7 +75,9 @@ def test_training_oracle_matches_reference(name, one_thread):
     assert digest(*(x[k] for k in (*KEYS, "fusion_a", "fusion_b")), grad) == g["input_digest"]
     leaves = {k: x[k].clone().requires_grad_(True) for k in x}
     writer = g.get("config", {}).get("fine_writer", "softmax")
-    out = o.tao_attention(*(leaves[k] for k in KEYS), leaves["fusion_a"], leaves["fusion_b"], alpha, writer)
+    index_only = g.get("config", {}).get("coarse_index_only", True)
+    out = o.tao_attention(*(leaves[k] for k in KEYS), leaves["fusion_a"], leaves["fusion_b"], alpha, writer,
+                          coarse_index_only=index_only)
     out.backward(grad)
     s = g.get("row_stride", 1)
     ref = g["output"]

@@ -135,10 +135,11 @@ def test_two_ranks_gather_every_requests_outputs():
 
 
 def _failing_worker(rank, world, mode):
-    check = PeerCheck(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=2.0,
-                      prefix=f"tao/{mode}")
-    check.wait(0)                                       # both ranks run step 0
+    # a peer that aborts is seen at once, whatever the timeout; a silent one only at the timeout
+    check = PeerCheck(dist.distributed_c10d._get_default_store(), rank, world,
+                      timeout_s=30.0 if mode == "raise" else 2.0, prefix=f"tao/{mode}")
     if rank == 1:
+        check.wait(0)                                   # step 0 runs on both ranks
         if mode == "raise":
             try:
                 raise RuntimeError("decode failed on rank 1")
@@ -147,7 +148,9 @@ def _failing_worker(rank, world, mode):
                 return ("left", str(e))
         return ("left", "silently")
     try:
-        check.wait(1)                                   # rank 1 never posts step 1
+        # rank 1 never posts step 1; its abort may already show while rank 0 checks step 0
+        check.wait(0)
+        check.wait(1)
     except RankFailure as e:
         return ("failure", str(e))
     return ("no failure detected",)

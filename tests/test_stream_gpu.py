@@ -347,3 +347,40 @@ def test_host_transfers_by_the_sms():
         outs.append(y.cpu())
     assert torch.equal(outs[0], outs[1])
     assert check_device() == 0
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_decode_session_equals_decode_batch(graph):
+    """DecodeSession (operands and results in page-locked host memory; one graph
+    launch per step for graph-configured states) decodes exactly like
+    tao_attention_decode_batch, across route refreshes and a seal."""
+    tb, preset, check_device = _tb()
+    dev = torch.device("cuda")
+    R, H, D, P, N = 3, 2, 64, 1000, 40
+    xs = [{k: t.to(dev) for k, t in make_inputs(1, P + N, H, D, seed=95 + r)[0].items()} for r in range(R)]
+    fa, fb = xs[0]["fusion_a"], xs[0]["fusion_b"]
+    sets = []
+    for _ in range(2):
+        states = []
+        for r in range(R):
+            st = tb.new_state(r, preset(graph=graph))
+            tb.tao_attention_prefill(*(xs[r][k][:, :P] for k in KEYS[:3]), raw_q=xs[r]["raw_q"][:, :P],
+                                     raw_k=xs[r]["raw_k"][:, :P], fusion_a=fa, fusion_b=fb, alpha=0.3,
+                                     state=st, position=0)
+            states.append(st)
+        sets.append(states)
+    session = tb.DecodeSession(sets[1], fa, fb, 0.3, reserve=N)
+    for t in range(P, P + N):
+        stack = torch.stack([torch.cat([xs[r][k][:, t:t + 1] for r in range(R)], 0) for k in KEYS])
+        ref, _ = tb.tao_attention_decode_batch(*stack[:3], raw_q=stack[3], raw_k=stack[4], fusion_a=fa,
+                                               fusion_b=fb, alpha=0.3, states=sets[0])
+        session.inputs.copy_(stack.cpu())
+        session.step()
+        got = session.wait()
+        assert torch.equal(got, ref.cpu()), f"position {t}"
+    assert (session.graph is not None) == graph
+    session.check()
+    assert check_device() == 0
+    for a, b in zip(*sets):
+        assert a.position == b.position == P + N
+        assert torch.equal(a.export()["packed_fine_c"], b.export()["packed_fine_c"])

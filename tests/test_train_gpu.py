@@ -67,7 +67,7 @@ def _config(g):
 
 
 @pytest.mark.parametrize("name", GOLDEN_TRAIN)
-def test_forward_matches_reference_golden(name):
+def test_forward_matches_reference_golden(name, one_thread):
     g = torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
     b, t, h, d, alpha, seed = g["case"]
     x, _ = make_inputs(b, t, h, d, seed)
@@ -91,7 +91,7 @@ def rel_l2(a, b):
 
 
 @pytest.mark.parametrize("name", GOLDEN_TRAIN)
-def test_backward_matches_reference_golden(name):
+def test_backward_matches_reference_golden(name, one_thread):
     g = torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
     b, t, h, d, alpha, seed = g["case"]
     x, gen = make_inputs(b, t, h, d, seed)
