@@ -56,11 +56,12 @@ UNIT = "tok/s"
 REQUESTS, HEADS, WIDTH, CONTEXT, LAYER, DECODE_STEPS = 8, 12, 64, 131072, 0, 256
 L2_FLUSH_BYTES = 1 << 30   # also keeps the GPU busy while the host enqueues the step
 L2_CLEAN_BYTES = 1 << 28   # read after the memset: its dirty lines are written back before timing
-# DRAM bytes (read + write) of one decode_fused_kernel launch at this workload, from
-#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none \
-#       -k regex:decode_fused_kernel -s 8 -c 3 python bench.py --steps 3 --warmup 3 --no-train
-# (profiles/decode_fused_kernel_decode128k.md); None until captured for this build.
-DECODE_TRAFFIC_BYTES = None
+# DRAM bytes (read + write) of one decode_fused_kernel launch at this workload (the
+# timed window's last steps), from the full capture
+#   ncu --set full --clock-control none -k regex:decode_fused_kernel --nvtx --nvtx-include "timed_decode/" \
+#       -c 1 -o fused64 python bench.py --no-train --no-serving --no-parity --steps 6 --warmup 3
+# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/decode_fused_kernel_decode128k.md).
+DECODE_TRAFFIC_BYTES = 46556160
 # The same for read_bwd_kernel in the train8k workload
 #   (profiles/read_bwd_kernel_train8k.md, capture command there).
 READ_BWD_TRAFFIC_BYTES = None
@@ -75,7 +76,9 @@ def parse():
     ap.add_argument("--requests", type=int, default=REQUESTS)
     ap.add_argument("--context", type=int, default=CONTEXT)
     ap.add_argument("--cpu-sample-steps", type=int, default=4)
-    ap.add_argument("--workload", default="decode128k", choices=["decode128k", "train8k"])
+    ap.add_argument("--workload", default="decode128k", choices=["decode128k", "train8k", "serving"])
+    ap.add_argument("--serving-requests", type=int, default=None,
+                    help="serving leg: the first N requests of the 64 (profiling captures of a smaller case)")
     ap.add_argument("--no-train", action="store_true", help="leave the nested train8k leg out")
     ap.add_argument("--no-serving", action="store_true", help="leave the nested serving (config 5) leg out")
     ap.add_argument("--no-parity", action="store_true", help="leave the oracle parity check out")
@@ -493,7 +496,8 @@ def run_serving(args, world, rank, local):
     from tao_memory_b200.shard import plan_imbalance, plan_lpt
     from tao_memory_b200.stream import decode_bytes
     device = torch.device("cuda", local)
-    lengths = serving_lengths()
+    lengths = serving_lengths()[:args.serving_requests or SV_REQUESTS]
+    n_req = len(lengths)
     plan = plan_lpt(lengths, SV_HEADS, SV_WIDTH, world)
     mine = [s for s in plan if s.rank == rank]
     K, W = args.steps, args.warmup
@@ -569,9 +573,9 @@ def run_serving(args, world, rank, local):
     achieved = algo / (ms * 1e-3) / 1e9   # all ranks' bytes over the slowest rank's time
     return {
         "metric": "serving decode tok/s (64 requests, 2K-128K prompts)", "unit": "tok/s",
-        "value": round(SV_REQUESTS * K / (ms * 1e-3), 1), "steps": K, "warmup": W,
+        "value": round(n_req * K / (ms * 1e-3), 1), "steps": K, "warmup": W,
         "ms_per_step": round(ms / K, 4), "n_gpus": world, "scaling": "strong",
-        "config": {"workload": "serving (BASELINE.json config 5)", "requests": SV_REQUESTS, "heads": SV_HEADS,
+        "config": {"workload": "serving (BASELINE.json config 5)", "requests": n_req, "heads": SV_HEADS,
                    "head_dim": SV_WIDTH, "prompts": "log-uniform 2K-128K (seed 71)",
                    "decode_steps": SV_STEPS, "timed": f"steps {lead + W}..{lead + W + K - 1}",
                    "snapshot": f"every state exported and imported after decode step {min(SV_SNAPSHOT_AT, lead)}",
@@ -977,6 +981,8 @@ def main():
             result = run_train_bench(args, world, rank, local)
             if rank == 0:
                 result["cpu_baseline"] = cpu_train_baseline() if world == 1 else None
+        elif args.workload == "serving":
+            result = run_serving(args, world, rank, local)
         else:
             result, states, exported, timed_inputs, outs, fa, fb = run_b200(args, world, rank, local)
             if rank == 0 and exported is not None:

@@ -148,9 +148,11 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
                     const void* fusion_b, float alpha, void* out, void* workspace,
                     size_t workspace_bytes, void* stream);
 
-/* Select the decode kernel of tao_decode_step for this process: 1 = one CTA per work
- * item (default), 0 = warp-specialised persistent kernel, 2 = one warp per 8 KB
- * work item.  Results agree to fp32 summation order. */
+/* Select the decode kernel of tao_decode_step for this process: 1 = persistent fused
+ * kernel with one copy stage per CTA (default), 3 = the same with two stages per CTA
+ * (half the resident CTAs; measured slower), 0 = warp-specialised persistent kernel,
+ * 2 = one warp per 8 KB work item.  Variants 1 and 3 give identical results; the
+ * others agree to fp32 summation order. */
 int tao_decode_variant(int variant);
 
 /* Graph mode for the calling host thread (on != 0): tao_decode_step then always

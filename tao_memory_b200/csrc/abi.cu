@@ -16,6 +16,7 @@
 #include "../../include/tao_b200.h"
 #include "decode_fused.cuh"
 #include "stream_kernels.cuh"
+#include "tc_writer.cuh"
 #include "window_attention.cuh"
 
 namespace tao {
@@ -31,8 +32,9 @@ thread_local std::string g_last_error;
 // the backward on its own thread); cleared when taken.
 std::mutex g_prof_mutex;
 cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
-// Decode kernel choice: 1 = one CTA per item (default), 0 = warp-specialised
-// persistent, 2 = one warp per 8 KB item.
+// Decode kernel choice: 1 = persistent fused kernel, one stage per CTA (default),
+// 3 = the same with two stages (fewer resident CTAs: measured slower), 0 =
+// warp-specialised persistent, 2 = one warp per 8 KB item.
 int g_decode_variant = 1;
 
 int fail(int code, const char* fmt, ...) {
@@ -227,6 +229,29 @@ int device_sm_count(int dev) {
   return sms;
 }
 
+// Persistent fused decode kernel with NS stages per CTA: as many CTAs as are resident
+// at once, each walking the same number of items (give or take one) by the grid stride.
+template <int D, int NS>
+int launch_fused(const tao::FusedArgs& f, int total, int sms, int dev, cudaStream_t s) {
+  using namespace tao;
+  const size_t smem = (size_t)NS * FusedCfg<D>::STAGE;
+  int rc;
+  if ((rc = set_smem(decode_fused_kernel<D, NS>, smem))) return rc;
+  // resident CTAs per SM: one occupancy query per (device, width, stages), kept for the process
+  static std::atomic<int> per_sm_of[kMaxDevices];
+  int per_sm = per_sm_of[dev].load(std::memory_order_relaxed);
+  if (per_sm <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel<D, NS>, 128, smem) != cudaSuccess ||
+        per_sm <= 0)
+      per_sm = 1;
+    per_sm_of[dev].store(per_sm, std::memory_order_relaxed);
+  }
+  const int resident = per_sm * sms;
+  const int rounds = (total + resident - 1) / resident;
+  decode_fused_kernel<D, NS><<<(total + rounds - 1) / rounds, 128, smem, s>>>(f);
+  return TAO_OK;
+}
+
 template <int D>
 int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaStream_t s) {
   using namespace tao;
@@ -259,31 +284,19 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
     const int need = (total + kWsMaxItems - 1) / kWsMaxItems;
     if (grid < need) grid = need;
     decode_ws_kernel<D><<<grid, 288, smem, s>>>(f);
+  } else if (g_decode_variant == 3) {
+    if ((rc = launch_fused<D, 2>(f, total, sms, dev, s))) return rc;   // two stages per CTA
   } else {
-    // persistent: as many CTAs as are resident at once, each walking items by the grid stride
-    const size_t smem = FusedCfg<D>::STAGE;
-    if ((rc = set_smem(decode_fused_kernel<D>, smem))) return rc;
-    // resident CTAs per SM: one occupancy query per (device, width), kept for the process
-    static std::atomic<int> per_sm_of[kMaxDevices];
-    int per_sm = per_sm_of[dev].load(std::memory_order_relaxed);
-    if (per_sm <= 0) {
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel<D>, 128, smem) != cudaSuccess ||
-          per_sm <= 0)
-        per_sm = 1;
-      per_sm_of[dev].store(per_sm, std::memory_order_relaxed);
-    }
-    const int resident = per_sm * sms;
-    // balanced: every CTA walks the same number of items (give or take one)
-    const int rounds = (total + resident - 1) / resident;
-    decode_fused_kernel<D><<<(total + rounds - 1) / rounds, 128, smem, s>>>(f);
+    if ((rc = launch_fused<D, 1>(f, total, sms, dev, s))) return rc;   // one stage per CTA
   }
   if (prof1) cudaEventRecord(prof1, s);
   if ((rc = check_launch("decode_fused_kernel"))) return rc;
   if (seal) {
-    const size_t ss = (size_t)2 * kFine * D * 2 + (size_t)2 * D * 4;
-    if ((rc = set_smem(decode_seal_kernel<D>, ss))) return rc;
-    decode_seal_kernel<D><<<a.R * a.H, 256, ss, s>>>(a);
-    if ((rc = check_launch("decode_seal_kernel"))) return rc;
+    // the block writer on the tensor cores (C = p^T v by tcgen05.mma into TMEM)
+    const size_t ss = TcWriterCfg<D>::SMEM;
+    if ((rc = set_smem(tc_seal_kernel<D>, ss))) return rc;
+    tc_seal_kernel<D><<<a.R * a.H, 128, ss, s>>>(a);
+    if ((rc = check_launch("tc_seal_kernel"))) return rc;
   }
   return TAO_OK;
 }
@@ -312,8 +325,8 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
     return fail(TAO_ERR_ARG, "invalid routing policy");
   if (policy->fine_read != 0 && policy->fine_read != 1)
     return fail(TAO_ERR_ARG, "policy.fine_read must be 0 or 1, got %d", policy->fine_read);
-  if (policy->fine_read == 1 && g_decode_variant != 1)
-    return fail(TAO_ERR_ARG, "the feature-mass read runs in the default decode kernel (variant 1)");
+  if (policy->fine_read == 1 && g_decode_variant != 1 && g_decode_variant != 3)
+    return fail(TAO_ERR_ARG, "the feature-mass read runs in the fused decode kernel (variant 1 or 3)");
   for (const void* p : {q, k, v, raw_q, raw_k, fusion_a, fusion_b, (const void*)out, (const void*)workspace})
     if (!p) return fail(TAO_ERR_ARG, "null tensor pointer");
   for (const void* p : {q, k, v, raw_q, raw_k, (const void*)out})
@@ -529,7 +542,7 @@ int tao_stream_profile_next(void* start, void* stop) {
 }
 
 int tao_decode_variant(int variant) {
-  if (variant < 0 || variant > 2) return fail(TAO_ERR_ARG, "decode variant must be 0, 1 or 2");
+  if (variant < 0 || variant > 3) return fail(TAO_ERR_ARG, "decode variant must be 0, 1, 2 or 3");
   g_decode_variant = variant;
   return TAO_OK;
 }

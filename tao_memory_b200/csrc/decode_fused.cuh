@@ -133,20 +133,36 @@ TAO_DEVI void softmax_row(const bf16* x, float* hq, int lane) {
   for (int j = 0; j < D / 32; ++j) hq[lane + 32 * j] = rb(__fdiv_rn(vals[j], s));
 }
 
+// After a wait that gave up: thread 0 gives every other stage's copy still in flight
+// its own bounded wait, so no bulk copy outlives the CTA's shared memory.
+template <int NS>
+TAO_DEVI void drain_stages(uint64_t* bars, const uint32_t* armed, const uint32_t* phases, int cur, int* err) {
+  if (threadIdx.x != 0) return;
+#pragma unroll
+  for (int x = 0; x < NS; ++x)
+    if (x != cur && armed[x]) mbar_wait(&bars[x], phases[x], err);
+}
+
 // Persistent form: the grid holds as many CTAs as fit on the GPU at once and each
 // walks the items i = blockIdx.x, + gridDim.x, ...  While an item's copy is in
 // flight, thread 0 resolves the next item's sources; the next copy is issued as
 // soon as the item's compute has released the stage (before its arrival atomic),
 // so a CTA's next load overlaps its own arrival and combine.  The combine reads
 // the partials from L2 and leaves the stage to the copy in flight.
-template <int D>
+//
+// NS pipeline stages per CTA (the dynamic shared memory holds NS * STAGE bytes): the
+// CTA's items rotate through them, item j in stage j % NS, so with NS = 2 the copy of
+// the CTA's next item is already in flight while the current one computes; an item's
+// successor in its stage (i + NS * gridDim.x) is issued as soon as the item has
+// released the stage.
+template <int D, int NS>
 __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   using Cfg = FusedCfg<D>;
   const StepArgs& a = f.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  extern __shared__ __align__(128) uint8_t dsm[];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t armed_s;
+  extern __shared__ __align__(128) uint8_t dsm_all[];
+  __shared__ __align__(8) uint64_t bars[NS];
+  __shared__ uint32_t armed_s[NS];
   __shared__ int flag;
   __shared__ float qv[D];
   __shared__ float red[128 + 8];
@@ -159,19 +175,35 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   ItemCopy<D> next_copy;
   next_copy.n = 0;
   if (tid == 0) {
-    mbar_init(&bar, 1);
+#pragma unroll
+    for (int x = 0; x < NS; ++x) mbar_init(&bars[x], 1);
     fence_mbar_init();
-    armed_s = (blockIdx.x < total) ? issue_copy<D>(resolve_item<D>(f, item_of(blockIdx.x, a.R, a.H)), dsm, &bar) : 0u;
+#pragma unroll
+    for (int x = 0; x < NS; ++x) {
+      const int first = blockIdx.x + x * gridDim.x;
+      armed_s[x] = (first < total)
+                       ? issue_copy<D>(resolve_item<D>(f, item_of(first, a.R, a.H)), dsm_all + x * Cfg::STAGE, &bars[x])
+                       : 0u;
+    }
   }
-  uint32_t phase = 0;
-  for (int i = blockIdx.x; i < total; i += gridDim.x) {
+  uint32_t phases[NS];
+#pragma unroll
+  for (int x = 0; x < NS; ++x) phases[x] = 0;
+  int sidx = 0;   // stage of the current item
+  for (int i = blockIdx.x; i < total; i += gridDim.x, sidx = (sidx + 1 == NS) ? 0 : sidx + 1) {
     const Item it = item_of(i, a.R, a.H);
     TaoState& st = *a.states[it.r];
     const long long t = st.position;
     const int n_route = st.n_route;
-    const int nxt = i + gridDim.x;
+    const int nxt = i + NS * gridDim.x;   // the next item of this stage
+    uint8_t* const dsm = dsm_all + sidx * Cfg::STAGE;
+    uint64_t& bar = bars[sidx];
+    uint32_t phase = 0;
+#pragma unroll
+    for (int x = 0; x < NS; ++x)
+      if (x == sidx) phase = phases[x];
     __syncthreads();
-    const uint32_t armed = armed_s;
+    const uint32_t armed = armed_s[sidx];
     if (tid == 0 && nxt < total) next_copy = resolve_item<D>(f, item_of(nxt, a.R, a.H));  // overlaps the copy
     const long long src = ((long long)it.r * a.H + it.h) * D;
     if (it.slot < Cfg::KB) {
@@ -184,7 +216,10 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
       if (!armed) {
         if (tid == 0) { part[D] = -INFINITY; part[D + 1] = 0.f; }
       } else {
-        if (!wait_uniform(&bar, phase, a.err, &flag)) return;
+        if (!wait_uniform(&bar, phase, a.err, &flag)) {
+          drain_stages<NS>(bars, armed_s, phases, sidx, a.err);
+          return;
+        }
         bf16* sk = reinterpret_cast<bf16*>(dsm);
         bf16* sv = sk + Cfg::SLOTS * D;
         const int tm = (int)(t % kWindow);
@@ -301,7 +336,10 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
           sum = warp_sum(sum);
           if (lane == 0) red[x] = rb(sum);
         }
-        if (!wait_uniform(&bar, phase, a.err, &flag)) return;
+        if (!wait_uniform(&bar, phase, a.err, &flag)) {
+          drain_stages<NS>(bars, armed_s, phases, sidx, a.err);
+          return;
+        }
         constexpr int ECH = D / 8, RG = 128 / ECH, RPG = D / RG;
         const int ec = tid % ECH, rg = tid / ECH;
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -335,14 +373,18 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
         }
       }
     }
-    if (armed) phase ^= 1u;
+    if (armed) {
+#pragma unroll
+      for (int x = 0; x < NS; ++x)
+        if (x == sidx) phases[x] ^= 1u;
+    }
     // ---- the stage is free: issue the next item, then arrive; the CTA completing
     // the last item of (r, h) finalises it.  Every thread orders its shared-memory
     // writes of this item (generic proxy) before the next bulk copy (async proxy).
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (tid == 0) {
-      armed_s = (nxt < total) ? issue_copy<D>(next_copy, dsm, &bar) : 0u;
+      armed_s[sidx] = (nxt < total) ? issue_copy<D>(next_copy, dsm, &bar) : 0u;
       last_rh = (atomic_add_release(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
       if (last_rh) {
         st.counters[it.h] = 0;
@@ -1159,22 +1201,6 @@ __global__ void __launch_bounds__(1024) decode_route_kernel(StepArgs a) {
     st.n_chosen = K;
     st.route_refreshes += 1;
   }
-}
-
-// Seal after a decode step (the cursor has advanced): if the window now holds
-// 768 tokens, write the oldest block's fine and refresh the page memo.
-template <int D>
-__global__ void __launch_bounds__(256) decode_seal_kernel(StepArgs a) {
-  const int r = blockIdx.x / a.H, h = blockIdx.x % a.H;
-  TaoState& st = *a.states[r];
-  const long long t = st.position - 1;  // the token just served
-  const long long start = window_start(t);
-  if (t + 1 - start != kWindow) return;
-  extern __shared__ __align__(128) uint8_t dsm[];
-  const int S = sealed_at(t);
-  seal_block<D>(st, h, start, S, dsm);
-  refresh_memo<D>(st, h, S + 1, S / kGroup);
-  if (h == 0 && threadIdx.x == 0) st.seal_events += 1;
 }
 
 }  // namespace tao

@@ -17,7 +17,8 @@
 // it as bf16.  The wait on the MMA is bounded; on a timeout the CTA records the error,
 // frees its TMEM and returns.
 #pragma once
-#include "tc_attention.cuh"
+#include "stream_kernels.cuh"
+#include "tcgen05.cuh"
 #include "train_kernels.cuh"
 
 namespace tao {
@@ -40,14 +41,16 @@ TAO_DEVI uint32_t tw_off(int t, int d) {
          ((uint32_t)(((d & 63) >> 3) ^ (t & 7)) << 4) + ((uint32_t)(d & 7) << 1);
 }
 
+// One 256-token block: the softmax writer's z (z_out[D]) and, when write_c, C
+// (c_out[D][D]) from keys and values with rows `row` elements apart.  128 threads;
+// `sm_raw` is the kernel's dynamic shared memory (TcWriterCfg<D>::SMEM bytes).
+// Returns false when the wait on the MMA gave up (the error word is set).
 template <int D>
-__global__ void __launch_bounds__(128) tc_writer_kernel(const bf16* __restrict__ raw_k,
-                                                        const bf16* __restrict__ v, bf16* z_out, bf16* c_out,
-                                                        TrainDims dm, int write_c, int* err) {
+TAO_DEVI bool tc_block_writer(const bf16* __restrict__ kb, const bf16* __restrict__ vb, long long row,
+                              bf16* zo, bf16* co, int write_c, int* err, uint8_t* sm_raw) {
   using namespace tc;
   using Cfg = TcWriterCfg<D>;
   constexpr int NT = 256, CH = D / 8;
-  extern __shared__ uint8_t sm_raw[];
   const uint32_t raw = smem_u32(sm_raw);
   uint8_t* const sm = sm_raw + (((raw + 1023u) & ~1023u) - raw);   // 1024-byte aligned window
   uint8_t* const sP = sm;                  // keys, then probabilities (A operand)
@@ -57,16 +60,12 @@ __global__ void __launch_bounds__(128) tc_writer_kernel(const bf16* __restrict__
   float* const scratch = zp + D;                                        // [2 * 128]
   uint64_t* const bar = reinterpret_cast<uint64_t*>(scratch + 2 * 128);
   uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
-  __shared__ int okflag;
-
-  const int s = blockIdx.x % dm.S, h = (blockIdx.x / dm.S) % dm.H, b = blockIdx.x / (dm.S * dm.H);
+  int* const okflag = reinterpret_cast<int*>(tmem_slot + 1);
   const int tid = threadIdx.x, warp = tid >> 5;
-  const bf16* kb = raw_k + ((long long)b * dm.T + (long long)s * NT) * dm.row + (long long)h * D;
-  const bf16* vb = v + ((long long)b * dm.T + (long long)s * NT) * dm.row + (long long)h * D;
   for (int idx = tid; idx < NT * CH; idx += 128) {
     const int r = idx / CH, c = idx % CH;
-    wa::cp_async16(smem_u32(sP + tw_off<D>(r, c * 8)), kb + (long long)r * dm.row + c * 8, true);
-    wa::cp_async16(smem_u32(sV + tw_off<D>(r, c * 8)), vb + (long long)r * dm.row + c * 8, true);
+    wa::cp_async16(smem_u32(sP + tw_off<D>(r, c * 8)), kb + (long long)r * row + c * 8, true);
+    wa::cp_async16(smem_u32(sV + tw_off<D>(r, c * 8)), vb + (long long)r * row + c * 8, true);
   }
   wa::cp_commit();
   if (write_c && warp == 0) {
@@ -91,9 +90,8 @@ __global__ void __launch_bounds__(128) tc_writer_kernel(const bf16* __restrict__
     const uint32_t e2 = *cell;
     *cell = wa::pack_bf16(__fdiv_rn(lo_f(e2), zp[d]), __fdiv_rn(hi_f(e2), zp[d + 1]));
   }
-  bf16* zo = z_out + (((long long)b * dm.H + h) * dm.S + s) * D;
   for (int d = tid; d < D; d += 128) zo[d] = tobf(__fadd_rn(mx[d], rb(logf(zp[d]))));
-  if (!write_c) return;  // the caller supplies C (another fine writer); no TMEM was taken
+  if (!write_c) return true;  // the caller supplies C (another fine writer); no TMEM was taken
 
   // C = p^T v: the generic-proxy writes of p become visible to the tensor core
   fence_proxy_async();
@@ -110,13 +108,13 @@ __global__ void __launch_bounds__(128) tc_writer_kernel(const bf16* __restrict__
     commit(bar);
   }
   // every thread waits (bounded) for the accumulator; a timeout skips the epilogue
-  if (tid == 0) okflag = mbar_wait(bar, 0, err) ? 1 : 0;
+  if (tid == 0) *okflag = mbar_wait(bar, 0, err) ? 1 : 0;
   __syncthreads();
   fence_after();
-  if (okflag && warp < D / 32) {
+  const bool ok = *okflag != 0;
+  if (ok && warp < D / 32) {
     // warp w reads TMEM lanes 32w..32w+31: thread d holds row d of C
-    const int d = tid;
-    bf16* co = c_out + ((((long long)b * dm.H + h) * dm.S + s) * D + d) * (long long)D;
+    bf16* crow = co + (long long)tid * D;
 #pragma unroll
     for (int c0 = 0; c0 < D; c0 += 32) {
       float vals[32];
@@ -128,10 +126,10 @@ __global__ void __launch_bounds__(128) tc_writer_kernel(const bf16* __restrict__
         o.y = wa::pack_bf16(vals[e + 2], vals[e + 3]);
         o.z = wa::pack_bf16(vals[e + 4], vals[e + 5]);
         o.w = wa::pack_bf16(vals[e + 6], vals[e + 7]);
-        *reinterpret_cast<uint4*>(co + c0 + e) = o;
+        *reinterpret_cast<uint4*>(crow + c0 + e) = o;
       }
     }
-  } else if (!okflag && tid == 0) {
+  } else if (!ok && tid == 0) {
     // give the MMA still in flight its bounded wait before the TMEM goes back
     mbar_wait(bar, 0, err);
   }
@@ -139,6 +137,43 @@ __global__ void __launch_bounds__(128) tc_writer_kernel(const bf16* __restrict__
   __syncthreads();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(Cfg::TMEM_COLS));
+  return ok;
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) tc_writer_kernel(const bf16* __restrict__ raw_k,
+                                                        const bf16* __restrict__ v, bf16* z_out, bf16* c_out,
+                                                        TrainDims dm, int write_c, int* err) {
+  extern __shared__ uint8_t sm_raw[];
+  const int s = blockIdx.x % dm.S, h = (blockIdx.x / dm.S) % dm.H, b = blockIdx.x / (dm.S * dm.H);
+  const long long first = ((long long)b * dm.T + (long long)s * 256) * dm.row + (long long)h * D;
+  tc_block_writer<D>(raw_k + first, v + first, dm.row, z_out + (((long long)b * dm.H + h) * dm.S + s) * D,
+                     c_out + (((long long)b * dm.H + h) * dm.S + s) * (long long)D * D, write_c, err, sm_raw);
+}
+
+// Decode seal (the window of a request reached 768 tokens on the token just served):
+// the oldest 256-token block of head h is sealed as fine S with the same block writer
+// (its keys and values are 256 consecutive ring slots), then the page memo of the page
+// receiving it is refreshed (tao_stream.py:435-512, 399-416).  One CTA of 128 threads
+// per (request, head); CTAs of requests that do not seal return at once.
+template <int D>
+__global__ void __launch_bounds__(128) tc_seal_kernel(StepArgs a) {
+  extern __shared__ uint8_t sm_raw[];
+  const int r = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  TaoState& st = *a.states[r];
+  const long long t = st.position - 1;  // the token just served
+  const long long start = window_start(t);
+  if (t + 1 - start != kWindow) return;
+  const int S = sealed_at(t);
+  const long long slot0 = (long long)h * kWindow + start % kWindow;
+  bf16* zo = reinterpret_cast<bf16*>(st.fine_z) + ((long long)h * st.cap_fines + S) * D;
+  bf16* co = reinterpret_cast<bf16*>(st.fine_c) + ((long long)h * st.cap_fines + S) * (long long)D * D;
+  if (!tc_block_writer<D>(reinterpret_cast<const bf16*>(st.rk_ring) + slot0 * D,
+                          reinterpret_cast<const bf16*>(st.v_ring) + slot0 * D, D, zo, co, 1, a.err, sm_raw))
+    return;
+  __syncthreads();
+  refresh_memo<D>(st, h, S + 1, S / kGroup);
+  if (h == 0 && threadIdx.x == 0) st.seal_events += 1;
 }
 
 }  // namespace tao
