@@ -149,10 +149,12 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
                     size_t workspace_bytes, void* stream);
 
 /* Select the decode kernel of tao_decode_step for this process: 1 = persistent fused
- * kernel with one copy stage per CTA (default), 3 = the same with two stages per CTA
- * (half the resident CTAs; measured slower), 0 = warp-specialised persistent kernel,
- * 2 = one warp per 8 KB work item.  Variants 1 and 3 give identical results; the
- * others agree to fp32 summation order. */
+ * kernel with one 32 KB copy stage per CTA (default), 3 = the same with two 32 KB
+ * stages per CTA (half the resident CTAs; measured slower), 4 = the same with two
+ * 16 KB stages per CTA and half-size items (64 keys or 2 fines; width 64, width 128
+ * runs variant 1), 0 = warp-specialised persistent kernel, 2 = one warp per 8 KB work
+ * item.  Variants 1 and 3 give identical results; the others agree to fp32
+ * summation order. */
 int tao_decode_variant(int variant);
 
 /* Graph mode for the calling host thread (on != 0): tao_decode_step then always

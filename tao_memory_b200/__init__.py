@@ -5,8 +5,9 @@ Drop-in for the reference package's public API (``tao_attention/__init__.py``):
 ``tao_attention_decode``, ``StreamCache`` and ``TaoConfig``; plus
 ``tao_attention_decode_batch`` for many requests per launch, and
 ``copy_to_device`` / ``copy_to_host`` for a decode step's operands in page-locked
-host memory, and ``DecodeSession`` for a serving loop over a fixed batch whose
-tokens arrive in and leave through page-locked host memory.  All compute runs in
+host memory, ``DecodeSession`` for a serving loop over a fixed batch whose
+tokens arrive in and leave through page-locked host memory, and the serving caller
+(``RequestStates``, ``DecodeScheduler``, ``save_snapshot`` / ``load_snapshot``).  All compute runs in
 ``libtao_b200.so`` (hand-written CUDA for sm_100a) behind a C ABI.
 """
 
@@ -14,8 +15,10 @@ from .config import TaoConfig
 from .host_io import copy_to_device, copy_to_host
 from .operator import (new_state, tao_attention, tao_attention_decode,
                        tao_attention_decode_batch, tao_attention_prefill)
+from .serving import DecodeScheduler, RequestStates, load_snapshot, save_snapshot
 from .stream import DecodeSession, StreamCache
 
 __all__ = ["new_state", "tao_attention", "tao_attention_prefill",
            "tao_attention_decode", "tao_attention_decode_batch", "StreamCache",
-           "TaoConfig", "copy_to_device", "copy_to_host", "DecodeSession"]
+           "TaoConfig", "copy_to_device", "copy_to_host", "DecodeSession", "RequestStates",
+           "DecodeScheduler", "save_snapshot", "load_snapshot"]

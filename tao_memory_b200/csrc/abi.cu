@@ -79,6 +79,12 @@ int h_sealed_at(long long pos) { return pos >= 768 ? (int)((pos - 768) / 256) + 
 long long h_window_start(long long pos) { return pos < 768 ? 0 : 256LL * ((pos - 512) / 256); }
 
 int fpc_for(int width) { return width == 64 ? 4 : 1; }
+// selected fines per fine item of the decode kernel of the current variant
+int fused_fpc(int width) {
+  if (g_decode_variant == 2) return 1;
+  if (g_decode_variant == 4 && width == 64) return 2;
+  return fpc_for(width);
+}
 int kblocks_for(int width) { return width == 64 ? 6 : 12; }
 
 struct Layout {
@@ -231,24 +237,25 @@ int device_sm_count(int dev) {
 
 // Persistent fused decode kernel with NS stages per CTA: as many CTAs as are resident
 // at once, each walking the same number of items (give or take one) by the grid stride.
-template <int D, int NS>
-int launch_fused(const tao::FusedArgs& f, int total, int sms, int dev, cudaStream_t s) {
+template <int D, int NS, int IB>
+int launch_fused(const tao::FusedArgs& f, int sms, int dev, cudaStream_t s) {
   using namespace tao;
-  const size_t smem = (size_t)NS * FusedCfg<D>::STAGE;
+  const size_t smem = (size_t)NS * FusedCfg<D, IB>::STAGE;
+  const int total = f.s.R * f.s.H * (FusedCfg<D, IB>::KB + f.ms);
   int rc;
-  if ((rc = set_smem(decode_fused_kernel<D, NS>, smem))) return rc;
+  if ((rc = set_smem(decode_fused_kernel<D, NS, IB>, smem))) return rc;
   // resident CTAs per SM: one occupancy query per (device, width, stages), kept for the process
   static std::atomic<int> per_sm_of[kMaxDevices];
   int per_sm = per_sm_of[dev].load(std::memory_order_relaxed);
   if (per_sm <= 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel<D, NS>, 128, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel<D, NS, IB>, 128, smem) != cudaSuccess ||
         per_sm <= 0)
       per_sm = 1;
     per_sm_of[dev].store(per_sm, std::memory_order_relaxed);
   }
   const int resident = per_sm * sms;
   const int rounds = (total + resident - 1) / resident;
-  decode_fused_kernel<D, NS><<<(total + rounds - 1) / rounds, 128, smem, s>>>(f);
+  decode_fused_kernel<D, NS, IB><<<(total + rounds - 1) / rounds, 128, smem, s>>>(f);
   return TAO_OK;
 }
 
@@ -285,9 +292,14 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
     if (grid < need) grid = need;
     decode_ws_kernel<D><<<grid, 288, smem, s>>>(f);
   } else if (g_decode_variant == 3) {
-    if ((rc = launch_fused<D, 2>(f, total, sms, dev, s))) return rc;   // two stages per CTA
+    if ((rc = launch_fused<D, 2, 32768>(f, sms, dev, s))) return rc;   // two 32 KB stages per CTA
+  } else if (D == 64 && g_decode_variant == 4) {
+    // two 16 KB stages per CTA: items of 64 keys or 2 fines
+    if constexpr (D == 64) {
+      if ((rc = launch_fused<D, 2, 16384>(f, sms, dev, s))) return rc;
+    }
   } else {
-    if ((rc = launch_fused<D, 1>(f, total, sms, dev, s))) return rc;   // one stage per CTA
+    if ((rc = launch_fused<D, 1, 32768>(f, sms, dev, s))) return rc;   // one 32 KB stage per CTA
   }
   if (prof1) cudaEventRecord(prof1, s);
   if ((rc = check_launch("decode_fused_kernel"))) return rc;
@@ -325,8 +337,8 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
     return fail(TAO_ERR_ARG, "invalid routing policy");
   if (policy->fine_read != 0 && policy->fine_read != 1)
     return fail(TAO_ERR_ARG, "policy.fine_read must be 0 or 1, got %d", policy->fine_read);
-  if (policy->fine_read == 1 && g_decode_variant != 1 && g_decode_variant != 3)
-    return fail(TAO_ERR_ARG, "the feature-mass read runs in the fused decode kernel (variant 1 or 3)");
+  if (policy->fine_read == 1 && (g_decode_variant == 0 || g_decode_variant == 2))
+    return fail(TAO_ERR_ARG, "the feature-mass read runs in the fused decode kernel (variant 1, 3 or 4)");
   for (const void* p : {q, k, v, raw_q, raw_k, fusion_a, fusion_b, (const void*)out, (const void*)workspace})
     if (!p) return fail(TAO_ERR_ARG, "null tensor pointer");
   for (const void* p : {q, k, v, raw_q, raw_k, (const void*)out})
@@ -355,7 +367,7 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
   if (policy->fine_read == 1 && mbound > tao::kRouteCapMax)
     return fail(TAO_ERR_CAPACITY, "feature-mass decode holds at most %d selected fines", tao::kRouteCapMax);
   // fine partials per (r, h): one per selected fine (warp kernel) or per group of fpc
-  const int fpc = (g_decode_variant == 2) ? 1 : fpc_for(width);
+  const int fpc = fused_fpc(width);
   const int ms = (mbound + fpc - 1) / fpc;
   const Layout L = make_layout(n_states, 1, heads, width, route_cap, ms, policy->route_period);
   if (workspace_bytes < L.total) return fail(TAO_ERR_ARG, "workspace too small: %zu < %zu", workspace_bytes, L.total);
@@ -542,7 +554,7 @@ int tao_stream_profile_next(void* start, void* stop) {
 }
 
 int tao_decode_variant(int variant) {
-  if (variant < 0 || variant > 3) return fail(TAO_ERR_ARG, "decode variant must be 0, 1, 2 or 3");
+  if (variant < 0 || variant > 4) return fail(TAO_ERR_ARG, "decode variant must be 0, 1, 2, 3 or 4");
   g_decode_variant = variant;
   return TAO_OK;
 }

@@ -30,12 +30,17 @@ struct FusedArgs {
   int ms;            // fine items per (r, h)
 };
 
-template <int D>
+// Item geometry: an item's copies fill one IB-byte stage, either the K and V rows of
+// SLOTS ring slots or the C matrices of FPC selected fines.  IB = 32 KB: 128 keys or 4
+// fines at width 64, 64 keys or 1 fine at width 128; IB = 16 KB (width 64 only): 64
+// keys or 2 fines.
+template <int D, int IB = 32768>
 struct FusedCfg {
-  static constexpr int SLOTS = DecodeCfg<D>::SLOTS;
-  static constexpr int FPC = DecodeCfg<D>::FPC;
-  static constexpr int KB = DecodeCfg<D>::KBLOCKS;
-  static constexpr int STAGE = 32768;  // bytes per pipeline stage
+  static constexpr int STAGE = IB;              // bytes per pipeline stage
+  static constexpr int SLOTS = IB / (4 * D);    // keys per local block
+  static constexpr int FPC = IB / (2 * D * D);  // fines per selected-fine group
+  static constexpr int KB = kWindow / SLOTS;    // local blocks per (r, h)
+  static_assert(FPC >= 1 && FPC <= 4 && SLOTS >= 64 && SLOTS <= 128, "item geometry");
 };
 
 // Item i -> (rh, slot): slots of one (r, h) are spread over the grid.
@@ -58,20 +63,23 @@ TAO_DEVI bool local_block_live(long long t, long long start, int s0, int slots) 
 
 // Source addresses of one item's bulk copies (resolved ahead of the copy so a CTA
 // can issue its next item the moment its stage is free).
-template <int D>
+template <int D, int IB = 32768>
 struct ItemCopy {
-  static constexpr int N = FusedCfg<D>::FPC > 2 ? FusedCfg<D>::FPC : 2;
+  static constexpr int N = FusedCfg<D, IB>::FPC > 2 ? FusedCfg<D, IB>::FPC : 2;
   const void* src[N];
-  uint32_t bytes;  // per copy
-  int n;           // copies (0: nothing to load)
+  int id[FusedCfg<D, IB>::FPC];  // selected-fine items: the fine ids (their channel rows are read by id)
+  uint32_t bytes;            // per copy
+  int n;                     // copies (0: nothing to load)
 };
 
-template <int D>
-TAO_DEVI ItemCopy<D> resolve_item(const FusedArgs& f, const Item& it) {
-  using Cfg = FusedCfg<D>;
-  ItemCopy<D> c;
+template <int D, int IB>
+TAO_DEVI ItemCopy<D, IB> resolve_item(const FusedArgs& f, const Item& it) {
+  using Cfg = FusedCfg<D, IB>;
+  ItemCopy<D, IB> c;
   c.n = 0;
   c.bytes = 0;
+#pragma unroll
+  for (int i = 0; i < Cfg::FPC; ++i) c.id[i] = 0;
   const TaoState& st = *f.s.states[it.r];
   const long long t = st.position;
   if (it.slot < Cfg::KB) {
@@ -94,33 +102,33 @@ TAO_DEVI ItemCopy<D> resolve_item(const FusedArgs& f, const Item& it) {
 #pragma unroll
   for (int i = 0; i < Cfg::FPC; ++i) id[i] = i < nf ? ids[i] : 0;
 #pragma unroll
-  for (int i = 0; i < Cfg::FPC; ++i) c.src[i] = fc + (long long)id[i] * D * D;
+  for (int i = 0; i < Cfg::FPC; ++i) {
+    c.src[i] = fc + (long long)id[i] * D * D;
+    c.id[i] = id[i];
+  }
   c.bytes = D * D * 2;
   c.n = nf;
   return c;
 }
 
 // Issue the bulk copies of a resolved item into `stage`; returns the bytes armed.
-template <int D>
-TAO_DEVI uint32_t issue_copy(const ItemCopy<D>& c, uint8_t* stage, uint64_t* bar) {
+template <int D, int IB>
+TAO_DEVI uint32_t issue_copy(const ItemCopy<D, IB>& c, uint8_t* stage, uint64_t* bar) {
   if (c.n == 0) return 0;
   mbar_expect_tx(bar, c.n * c.bytes);
 #pragma unroll
-  for (int i = 0; i < ItemCopy<D>::N; ++i)
+  for (int i = 0; i < ItemCopy<D, IB>::N; ++i)
     if (i < c.n) bulk_g2s(stage + i * c.bytes, c.src[i], c.bytes, bar);
   return c.n * c.bytes;
 }
 
 // h = bf16(softmax_d(raw_q)) of request r, head h (one warp), into hq[D].
+// vals[j] holds channel lane + 32 j (loaded by the caller ahead of other work).
 template <int D>
-TAO_DEVI void softmax_row(const bf16* x, float* hq, int lane) {
-  float vals[D / 32];
+TAO_DEVI void softmax_vals(float (&vals)[D / 32], float* hq, int lane) {
   float mx = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < D / 32; ++j) {
-    vals[j] = bf(x[lane + 32 * j]);
-    mx = fmaxf(mx, vals[j]);
-  }
+  for (int j = 0; j < D / 32; ++j) mx = fmaxf(mx, vals[j]);
   mx = warp_max(mx);
   float s = 0.f;
 #pragma unroll
@@ -131,6 +139,14 @@ TAO_DEVI void softmax_row(const bf16* x, float* hq, int lane) {
   s = warp_sum(s);
 #pragma unroll
   for (int j = 0; j < D / 32; ++j) hq[lane + 32 * j] = rb(__fdiv_rn(vals[j], s));
+}
+
+template <int D>
+TAO_DEVI void softmax_row(const bf16* x, float* hq, int lane) {
+  float vals[D / 32];
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) vals[j] = bf(x[lane + 32 * j]);
+  softmax_vals<D>(vals, hq, lane);
 }
 
 // After a wait that gave up: thread 0 gives every other stage's copy still in flight
@@ -154,10 +170,10 @@ TAO_DEVI void drain_stages(uint64_t* bars, const uint32_t* armed, const uint32_t
 // CTA's items rotate through them, item j in stage j % NS, so with NS = 2 the copy of
 // the CTA's next item is already in flight while the current one computes; an item's
 // successor in its stage (i + NS * gridDim.x) is issued as soon as the item has
-// released the stage.
-template <int D, int NS>
-__global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
-  using Cfg = FusedCfg<D>;
+// released the stage.  Registers are capped for 5 resident CTAs per SM.
+template <int D, int NS, int IB>
+__global__ void __launch_bounds__(128, 5) decode_fused_kernel(FusedArgs f) {
+  using Cfg = FusedCfg<D, IB>;
   const StepArgs& a = f.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   extern __shared__ __align__(128) uint8_t dsm_all[];
@@ -169,21 +185,24 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
   __shared__ float chs[Cfg::FPC * D];
   __shared__ float mass_s[kRouteCapMax];  // feature read: mass of every selected fine
   __shared__ int last_rh;
+  __shared__ int ids_s[NS][Cfg::FPC];     // fine ids of the item in each stage
   const int per = Cfg::KB + f.ms;
   const int total = a.R * a.H * per;
   constexpr int kArriver = (D < 128) ? D : 0;  // a thread with no channel in the combine (D = 64)
-  ItemCopy<D> next_copy;
-  next_copy.n = 0;
+  ItemCopy<D, IB> next_copy{};
   if (tid == 0) {
 #pragma unroll
     for (int x = 0; x < NS; ++x) mbar_init(&bars[x], 1);
     fence_mbar_init();
+    ItemCopy<D, IB> c[NS] = {};  // every stage's sources first, so their loads overlap
+#pragma unroll
+    for (int x = 0; x < NS; ++x)
+      if (blockIdx.x + x * gridDim.x < total) c[x] = resolve_item<D, IB>(f, item_of(blockIdx.x + x * gridDim.x, a.R, a.H));
 #pragma unroll
     for (int x = 0; x < NS; ++x) {
-      const int first = blockIdx.x + x * gridDim.x;
-      armed_s[x] = (first < total)
-                       ? issue_copy<D>(resolve_item<D>(f, item_of(first, a.R, a.H)), dsm_all + x * Cfg::STAGE, &bars[x])
-                       : 0u;
+#pragma unroll
+      for (int y = 0; y < Cfg::FPC; ++y) ids_s[x][y] = c[x].id[y];
+      armed_s[x] = issue_copy<D, IB>(c[x], dsm_all + x * Cfg::STAGE, &bars[x]);
     }
   }
   uint32_t phases[NS];
@@ -204,8 +223,19 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
       if (x == sidx) phase = phases[x];
     __syncthreads();
     const uint32_t armed = armed_s[sidx];
-    if (tid == 0 && nxt < total) next_copy = resolve_item<D>(f, item_of(nxt, a.R, a.H));  // overlaps the copy
+    if (tid == 0 && nxt < total) next_copy = resolve_item<D, IB>(f, item_of(nxt, a.R, a.H));  // overlaps the copy
     const long long src = ((long long)it.r * a.H + it.h) * D;
+    // The combine's per-channel operands (raw_q, fusion_a terms 0 and 2, fusion_b terms
+    // 0 and 2 of channel d = tid), loaded now so that their latency is off the
+    // combine's path; only the CTA that completes the last item of (r, h) uses them.
+    uint32_t fin[3] = {0u, 0u, 0u};
+    if (tid < D && t >= kWindow) {
+      const bf16* fa = a.fa + ((long long)it.h * D + tid) * 3;
+      const bf16* fb = a.fb + ((long long)it.h * D + tid) * 3;
+      fin[0] = *reinterpret_cast<const uint16_t*>(a.raw_q + src + tid);
+      fin[1] = *reinterpret_cast<const uint16_t*>(fa) | ((uint32_t)*reinterpret_cast<const uint16_t*>(fa + 2) << 16);
+      fin[2] = *reinterpret_cast<const uint16_t*>(fb) | ((uint32_t)*reinterpret_cast<const uint16_t*>(fb + 2) << 16);
+    }
     if (it.slot < Cfg::KB) {
       // ------------------------------------------------ local attention block
       const int s0 = it.slot * Cfg::SLOTS;
@@ -294,13 +324,31 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
       const int m0 = (it.slot - Cfg::KB) * Cfg::FPC;
       const int nf = min(Cfg::FPC, st.n_route - m0);
       if (nf > 0) {
-        const int32_t* ids = st.route_ids + (long long)it.h * st.route_cap + m0;
         const long long pstride = (long long)(st.cap_fines / kGroup + 1) * D;
         const bf16* fz = reinterpret_cast<const bf16*>(st.fine_z) + (long long)it.h * st.cap_fines * D;
         const bf16* pz = reinterpret_cast<const bf16*>(st.page_z) + it.h * pstride;
         const bf16* pw = reinterpret_cast<const bf16*>(st.page_w) + it.h * pstride;
-        // channels do not depend on the matrices in flight: compute them first
-        if (warp == 0) softmax_row<D>(a.raw_q + src, qv, lane);
+        // The channels do not depend on the matrices in flight: compute them first.
+        // Warp x reads the z, page z and page weight rows of fine x (its id came with
+        // the copy) while warp 0 also reads raw_q, so the loads overlap.
+        static_assert(Cfg::FPC <= 4, "one fine per warp");
+        const bool mine = !a.feature && warp < nf;
+        float hraw[D / 32], wv[D / 32], pwv[D / 32];
+        if (warp == 0) {
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j) hraw[j] = bf(a.raw_q[src + lane + 32 * j]);
+        }
+        if (mine) {
+          const int id = ids_s[sidx][warp], page = id / kGroup;
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j) {
+            const int d = lane + 32 * j;
+            const float zz = bf(fz[(long long)id * D + d]), pp = bf(pz[(long long)page * D + d]);
+            pwv[j] = bf(pw[(long long)page * D + d]);
+            wv[j] = rb(expf(rb(__fsub_rn(zz, pp))));
+          }
+        }
+        if (warp == 0) softmax_vals<D>(hraw, qv, lane);
         __syncthreads();
         if (a.feature) {
           // masses of all n_route selected fines (each item forms the same total)
@@ -323,18 +371,17 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
           }
           if (tid < nf) red[tid] = 0.f;
         }
-        for (int x = warp; x < nf && !a.feature; x += 4) {
-          const int id = ids[x], page = id / kGroup;
+        if (mine) {
           float sum = 0.f;
-          for (int d = lane; d < D; d += 32) {
-            const float hv = rb(__fmul_rn(qv[d], bf(pw[(long long)page * D + d])));
-            const float w = rb(expf(rb(__fsub_rn(bf(fz[(long long)id * D + d]), bf(pz[(long long)page * D + d])))));
-            const float c = rb(__fmul_rn(hv, w));
-            chs[x * D + d] = c;
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j) {
+            const int d = lane + 32 * j;
+            const float c = rb(__fmul_rn(rb(__fmul_rn(qv[d], pwv[j])), wv[j]));
+            chs[warp * D + d] = c;
             sum += c;
           }
           sum = warp_sum(sum);
-          if (lane == 0) red[x] = rb(sum);
+          if (lane == 0) red[warp] = rb(sum);
         }
         if (!wait_uniform(&bar, phase, a.err, &flag)) {
           drain_stages<NS>(bars, armed_s, phases, sidx, a.err);
@@ -384,7 +431,11 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (tid == 0) {
-      armed_s[sidx] = (nxt < total) ? issue_copy<D>(next_copy, dsm, &bar) : 0u;
+#pragma unroll
+      for (int y = 0; y < Cfg::FPC; ++y) ids_s[sidx][y] = next_copy.id[y];
+      armed_s[sidx] = (nxt < total) ? issue_copy<D, IB>(next_copy, dsm, &bar) : 0u;
+    }
+    if (tid == 32) {  // warp 1 arrives while warp 0 issues the copy
       last_rh = (atomic_add_release(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
       if (last_rh) {
         st.counters[it.h] = 0;
@@ -405,13 +456,12 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
       const int d = tid;
       const float* lg = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
       const float* fg = a.fine_part + ((long long)it.r * a.H + it.h) * f.ms * (D + 1);
-      uint32_t fin[3] = {0u, 0u, 0u};  // raw_q, fusion_a (terms 0, 2), fusion_b (terms 0, 2) of channel d
-      if (hist) {
-        const bf16* fa = a.fa + ((long long)it.h * D + d) * 3;
-        const bf16* fb = a.fb + ((long long)it.h * D + d) * 3;
-        fin[0] = *reinterpret_cast<const uint16_t*>(a.raw_q + src + d);
-        fin[1] = *reinterpret_cast<const uint16_t*>(fa) | ((uint32_t)*reinterpret_cast<const uint16_t*>(fa + 2) << 16);
-        fin[2] = *reinterpret_cast<const uint16_t*>(fb) | ((uint32_t)*reinterpret_cast<const uint16_t*>(fb + 2) << 16);
+      // the first 16 fine partials go out with the local ones: one round trip to L2
+      float va[16], vd[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        va[u] = u < nparts ? __ldcg(fg + u * (D + 1) + d) : 0.f;
+        vd[u] = u < nparts ? __ldcg(fg + u * (D + 1) + D) : 0.f;
       }
       float lm[Cfg::KB], ll[Cfg::KB], lo[Cfg::KB];
 #pragma unroll
@@ -436,12 +486,13 @@ __global__ void __launch_bounds__(128) decode_fused_kernel(FusedArgs f) {
       if (hist) {
         float acc = 0.f, den = 0.f;
         for (int p0 = 0; p0 < nparts; p0 += 16) {  // 16 partials' loads in flight, then summed in order
-          float va[16], vd[16];
+          if (p0 > 0) {
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int p2 = p0 + u;
-            va[u] = p2 < nparts ? __ldcg(fg + p2 * (D + 1) + d) : 0.f;
-            vd[u] = p2 < nparts ? __ldcg(fg + p2 * (D + 1) + D) : 0.f;
+            for (int u = 0; u < 16; ++u) {
+              const int p2 = p0 + u;
+              va[u] = p2 < nparts ? __ldcg(fg + p2 * (D + 1) + d) : 0.f;
+              vd[u] = p2 < nparts ? __ldcg(fg + p2 * (D + 1) + D) : 0.f;
+            }
           }
 #pragma unroll
           for (int u = 0; u < 16; ++u)

@@ -113,6 +113,31 @@ def test_stream_matches_oracle(heads, width, layer, splits, steps, one_thread):
     assert sum(int(not torch.equal(a, b)) for a, b in zip(ids, ref_ids)) == 0
 
 
+@pytest.mark.parametrize("variant", [1, 3, 4, 0, 2])
+@pytest.mark.parametrize("width", [64, 128])
+def test_decode_kernel_variants_match_oracle(variant, width, one_thread):
+    """Every decode kernel of tao_decode_variant against the oracle: 40 decode steps
+    after a 3050-token prefill, across route refreshes and the seal at position 3071."""
+    from tao_memory_b200 import _lib
+    heads, layer, prefill, steps = 2, 1, 3050, 40
+    x, _ = make_inputs(1, prefill + steps, heads, width, seed=90 + width)
+    _lib.check(_lib.lib().tao_decode_variant(variant))
+    try:
+        out, ids, st, _ = run_gpu(x, layer, (prefill,), steps, 0.4)
+    finally:
+        _lib.check(_lib.lib().tao_decode_variant(1))
+    orc = o.OracleStream(layer)
+    orc.step(*(x[k][:, :prefill] for k in KEYS), x["fusion_a"], x["fusion_b"], 0.4)
+    ref, ref_ids = [], []
+    for pos in range(prefill, prefill + steps):
+        sl = slice(pos, pos + 1)
+        ref.append(orc.step(*(x[k][:, sl] for k in KEYS), x["fusion_a"], x["fusion_b"], 0.4))
+        ref_ids.append(orc.route_ids[1].clone())
+    assert_close(out[:, prefill:], torch.cat(ref, 1), f"decode variant {variant} d{width}")
+    assert all(torch.equal(a, b) for a, b in zip(ids, ref_ids))
+    assert st.export()["fine_seal_events"] == orc.state_version
+
+
 def test_batch_decode_equals_single_requests():
     tb, preset, check_device = _tb()
     dev = torch.device("cuda")
