@@ -570,7 +570,9 @@ def run_serving(args, world, rank, local):
         dist.all_reduce(tot[1:], op=dist.ReduceOp.SUM)
     ms, algo = tot.tolist()
     peaks, kind = measured_peaks()
-    achieved = algo / (ms * 1e-3) / 1e9   # all ranks' bytes over the slowest rank's time
+    # all ranks' bytes over the slowest rank's time, against the peak of all ranks' HBM
+    achieved = algo / (ms * 1e-3) / 1e9
+    peak_all = float(peaks["hbm_gbs"]) * world
     return {
         "metric": "serving decode tok/s (64 requests, 2K-128K prompts)", "unit": "tok/s",
         "value": round(n_req * K / (ms * 1e-3), 1), "steps": K, "warmup": W,
@@ -583,9 +585,9 @@ def run_serving(args, world, rank, local):
                            f"{plan_imbalance(plan, world):.3f}" if world > 1 else "1 GPU",
                    "prefill_s": round(prefill_s, 1),
                    "l2": "flushed between timed steps"},
-        "roofline_step": {"bound": "hbm", "achieved": round(achieved, 1), "peak": float(peaks["hbm_gbs"]),
-                          "unit": "GB/s", "frac": round(achieved / float(peaks["hbm_gbs"]), 4),
-                          "peak_kind": kind + " (copy bandwidth)",
+        "roofline_step": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_all,
+                          "unit": "GB/s", "frac": round(achieved / peak_all, 4),
+                          "peak_kind": kind + f" (copy bandwidth x {world} GPU(s))",
                           "algorithmic_bytes_per_step": int(algo / K),
                           "basis": "whole decode step (all launches of every batch) on the device clock"},
     }

@@ -172,12 +172,37 @@ def feature_read(h, selected_z, selected_id, fine_c):
         mass = (query * selected_z.float().exp()).sum(-1)
         mixture = mass / mass.sum(-1, keepdim=True)
         channel = (mixture.unsqueeze(-1) * query).to(h.dtype)
-        b, q, hh, m = selected_id.shape
+        return _SelectedContraction.apply(channel, selected_id, fine_c)
+
+
+class _SelectedContraction(torch.autograd.Function):
+    """selected_fine_numerator / _SelectedContraction (indirect_fine.py:65-133)
+    restated: out = bf16(sum_m channel_m . C_m) in fp32; the adjoints with the
+    reference's rounding points: d channel = bf16(g . C^T) per selected pair and
+    dC = bf16(fp32 sum over the pairs that selected the fine of channel^T g)."""
+
+    @staticmethod
+    def forward(ctx, channel, ids, fine_c):
+        b, q, h, m = ids.shape
         bi = torch.arange(b)[:, None, None, None]
-        hi = torch.arange(hh)[None, None, :, None]
-        csel = fine_c[bi, hi, selected_id].float()
-        acc = torch.einsum("bqhmd,bqhmde->bqhe", channel.float(), csel)
-        return acc.to(h.dtype)
+        hi = torch.arange(h)[None, None, :, None]
+        csel = fine_c[bi, hi, ids].float()
+        ctx.save_for_backward(channel, ids, fine_c)
+        return torch.einsum("bqhmd,bqhmde->bqhe", channel.float(), csel).to(channel.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        channel, ids, fine_c = ctx.saved_tensors
+        b, q, h, m = ids.shape
+        bi = torch.arange(b)[:, None, None, None]
+        hi = torch.arange(h)[None, None, :, None]
+        csel = fine_c[bi, hi, ids].float()
+        gf = g.float()
+        d_channel = torch.einsum("bqhe,bqhmde->bqhmd", gf, csel).to(channel.dtype)
+        outer = torch.einsum("bqhmd,bqhe->bqhmde", channel.float(), gf)
+        dc = torch.zeros(fine_c.shape, dtype=F32)
+        dc.index_put_((bi.expand(b, q, h, m), hi.expand(b, q, h, m), ids), outer, accumulate=True)
+        return d_channel, None, dc.to(fine_c.dtype)
 
 
 def seal_all(raw_k, v, fine=256, writer="softmax"):
@@ -203,6 +228,36 @@ def seal_all(raw_k, v, fine=256, writer="softmax"):
     with torch.autocast(device_type="cpu", enabled=False):
         c = torch.einsum("bsihd,bsihe->bhsde", prob, values).to(dt)
     return z.permute(0, 2, 1, 3), c
+
+
+def seal_all_feature(raw_k, v, writer, fine=256):
+    """Training writer of the feature-read writers over all complete blocks but the
+    last (_seal_training_all, tao_stream.py:87-106): z = bf16(log mass) per block and
+    C from the unchecked regularised solve (feature-mass) or the structured inverse
+    (structured-Gram, count = 256).  Returns z [B,H,S,D], C [B,H,S,D,D] and the fp32
+    feature mass [B,H,S,D] that the page log-masses are built from."""
+    b, total, heads, d = raw_k.shape
+    s = total // fine - 1
+    keys = raw_k[:, :s * fine].reshape(b * s, fine, heads, d)
+    values = v[:, :s * fine].reshape(b * s, fine, heads, d)
+    if writer == "structured_gram_association":
+        square, cross, mass = structured_statistics(keys, values)
+        c = structured_matrix(square, cross, mass, fine)
+    else:
+        gram, cross, mass = association_statistics(keys, values, with_mass=True)
+        c = association_matrix(gram, cross, unchecked=True)
+    c = c.reshape(b, s, heads, d, d).permute(0, 2, 1, 3, 4)
+    mass = mass.reshape(b, s, heads, d).permute(0, 2, 1, 3)
+    return mass.log().to(raw_k.dtype), c, mass
+
+
+def chronological_sum(x, dim):
+    """Sum along ``dim`` one element after another in index order (fp32), the order of
+    chronological_sum (association_writer.py:35-40)."""
+    total = x.select(dim, 0)
+    for i in range(1, x.shape[dim]):
+        total = total + x.select(dim, i)
+    return total
 
 
 def fine_read(hv, page_z, fine_z, selected_id, fine_c, group=8):
@@ -613,13 +668,16 @@ def _local_training(q, k, v, fine=256, keep=512):
     return torch.cat((first, second, later.reshape(b, total - 512, heads, d)), dim=1)
 
 
-def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8, page_c=None):
+def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8, page_c=None, feature=False):
     """_read_training_group for one 256-query tile (tao_stream.py:596-665);
     with ``page_c`` (the completed pages' matrices) also the coarse read
-    (tao_stream.py:611-617).  Returns (fine, selected ids, coarse or None)."""
+    (tao_stream.py:611-617); with ``feature`` (the feature-read writers) h is the
+    fp32 softmax rounded once and the read is the feature-mass read of the selected
+    fines, no denominator (tao_stream.py:600-601, 658-661).  Returns (fine, selected
+    ids, coarse or None)."""
     b, length, heads, d = query.shape
     dt = query.dtype
-    h = F.softmax(query, dim=-1).to(dt)
+    h = F.softmax(query.float() if feature else query, dim=-1).to(dt)
     coarse_out = None
     if page_c is not None and completed:
         coarse_out = coarse_read(h, page_z[:, :, :completed], page_c[:, :, :completed])
@@ -653,6 +711,10 @@ def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8, page_
         sel = topk_oldest(scores, count)
         sel_id = cand_ids.gather(-1, sel)
         sel_page = cand_pages.gather(-1, sel)
+    if feature:
+        bi = torch.arange(b)[:, None, None, None]
+        hi = torch.arange(heads)[None, None, :, None]
+        return feature_read(h, fine_z[bi, hi, sel_id], sel_id, fine_c), sel_id, coarse_out
     num, den = _SelectedRead.apply(hv, seg_w, sel_id, sel_page, fine_c)
     return (num / den).to(dt), sel_id, coarse_out
 
@@ -684,7 +746,11 @@ def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False, writ
         if not coarse_index_only:
             return local, torch.zeros_like(local), [], torch.zeros_like(local)
         return local, torch.zeros_like(local), []
-    fine_z, fine_c = seal_all(raw_k, v, fine, writer)
+    feature = writer in FEATURE_WRITERS
+    if feature:
+        fine_z, fine_c, fine_mass = seal_all_feature(raw_k, v, writer, fine)
+    else:
+        fine_z, fine_c = seal_all(raw_k, v, fine, writer)
     if not coarse_index_only and writer != "softmax":
         raise NotImplementedError("coarse value pages are restated for the softmax writer")
     page_c = None if coarse_index_only else training_page_matrices(fine_z, fine_c, group)
@@ -697,15 +763,23 @@ def training_read(raw_q, raw_k, v, q, k, fine=256, group=8, keep_ids=False, writ
             continue
         completed, pending = divmod(visible, group)
         pz = []
-        if completed:
-            zc = fine_z[:, :, :completed * group].reshape(b, heads, completed, group, d)
-            pz.append(torch.logsumexp(zc, dim=3).to(fine_z.dtype))
-        if pending:
-            zp = fine_z[:, :, completed * group:visible].reshape(b, heads, 1, pending, d)
-            pz.append(torch.logsumexp(zp, dim=3).to(fine_z.dtype))
+        if feature:   # page z = bf16(log of the page's fp32 mass summed in fine order)
+            if completed:
+                mc = fine_mass[:, :, :completed * group].reshape(b, heads, completed, group, d)
+                pz.append(chronological_sum(mc, 3).log().to(fine_z.dtype))
+            if pending:
+                mp = fine_mass[:, :, completed * group:visible].reshape(b, heads, 1, pending, d)
+                pz.append(chronological_sum(mp, 3).log().to(fine_z.dtype))
+        else:
+            if completed:
+                zc = fine_z[:, :, :completed * group].reshape(b, heads, completed, group, d)
+                pz.append(torch.logsumexp(zc, dim=3).to(fine_z.dtype))
+            if pending:
+                zp = fine_z[:, :, completed * group:visible].reshape(b, heads, 1, pending, d)
+                pz.append(torch.logsumexp(zp, dim=3).to(fine_z.dtype))
         page_z = torch.cat(pz, dim=2)
         out, sel, coarse = _tile_read(query, page_z, fine_z[:, :, :visible], fine_c[:, :, :visible],
-                                      completed, pending, group, page_c)
+                                      completed, pending, group, page_c, feature=feature)
         fine_parts.append(out)
         coarse_parts.append(torch.zeros_like(query) if coarse is None else coarse)
         if keep_ids:

@@ -145,6 +145,8 @@ WRITER_CASES = {
 # training cases with another fine writer on the index-only preset
 TRAIN_WRITER_CASES = {
     "train_regularized": ((1, 2048, 2, 64, 0.5, 9), "regularized_association"),
+    "train_feature_mass": ((1, 2048, 2, 64, 0.5, 23), "feature_mass_association"),
+    "train_structured_gram": ((1, 3072, 1, 64, 0.4, 24), "structured_gram_association"),
 }
 
 # cases on the historical default TaoConfig() (coarse_index_only=False: completed

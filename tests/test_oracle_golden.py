@@ -12,7 +12,7 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 STREAM = ["stream_h2d64", "stream_h1d128", "stream_pages", "stream_regularized", "stream_feature_mass",
           "stream_structured_gram", "stream_coarse"]
 TRAIN = ["train_t2048_h2", "train_t3072_b2", "train_t2000_ragged", "train_pages", "train_regularized",
-         "train_coarse"]
+         "train_coarse", "train_feature_mass", "train_structured_gram"]
 KEYS = ("q", "k", "v", "raw_q", "raw_k")
 
 
