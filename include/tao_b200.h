@@ -308,6 +308,16 @@ typedef struct TaoTrainBuffers {
  * caller's d(local) in grads->d_local (read, not written); it returns no raw_q
  * gradient of the gate and no fusion-parameter gradients (zero). */
 #define TAO_TRAIN_EXTERNAL_FUSION 2
+/* TaoTrainBuffers.flags bit for the feature-read fine writers (feature-mass and
+ * structured-Gram, reference tao_stream.py:87-106, 538-549, 600-601, 658-661): the
+ * caller fills fine_z (bf16 log feature mass) and page_prefix (bf16 log of each
+ * page's fine-order mass prefix) before tao_train_forward, which then computes the
+ * local attention into buffers.local and the routing into buffers.sel only (no
+ * writer, no read, `out` untouched); the caller reads the selected fines with
+ * tao_feature_read_forward.  tao_train_backward then takes the caller's d(local) in
+ * grads->d_local and returns the local attention's dq, dk, dv with zero d_raw_q and
+ * d_raw_k (grad_out is not read). */
+#define TAO_TRAIN_ROUTE_ONLY 4
 
 /* S = T/256 - 1 sealed blocks (0 for T <= 768), pages = ceil(S/8), and the
  * largest number of selected fines any query of a T-token sequence reads. */
@@ -365,6 +375,33 @@ int tao_train_backward(const void* grad_out, const void* q, const void* k, const
                        const void* fusion_b, const float* gain, int batch, int tokens, int heads,
                        int width, const void* out, const TaoTrainBuffers* saved,
                        const TaoTrainGrads* grads, void* stream);
+
+/* Feature-mass read of training (reference _read_training_group with a feature-read
+ * writer, tao_stream.py:600-601, 658-661; feature_read_coefficients and
+ * selected_fine_numerator, association_writer.py:43-53, indirect_fine.py:65-133):
+ * for query t of head h, h = bf16(fp32 softmax(raw_q)); for each selected fine m
+ * (sel[b][t][h][0..mmax), -1 pads, from TAO_TRAIN_ROUTE_ONLY)
+ * mass_m = sum_d h_d exp(z_m,d) in fp32, w_m = mass_m / sum_m mass_m,
+ * coefficient_m,d = bf16(w_m h_d) and out = bf16(sum_m sum_d coefficient_m,d C_m[d][:])
+ * with fp32 accumulation (queries of the first three tiles read nothing: zero).
+ * raw_q, out: bf16 [B][T][H][D]; fine_z: bf16 [B][H][S][D]; fine_c: bf16
+ * [B][H][S][D][D].  The contraction runs per 128-query block and per selected fine
+ * on the tensor cores (tcgen05.mma, TMEM accumulator). */
+int tao_feature_read_forward(const void* raw_q, const void* fine_z, const void* fine_c,
+                             const int16_t* sel, int batch, int tokens, int heads, int width,
+                             int mmax, void* out, int* err, void* stream);
+
+/* Backward of tao_feature_read_forward for grad [B][T][H][D] bf16 (the gradient of
+ * out): d_raw_q bf16 [B][T][H][D] (written completely), and accumulated into the
+ * caller's zero-filled fp32 buffers dz [B][H][S][D] (sum over queries of
+ * bf16(d mass * h * exp(z)), the gradient of the selected z) and dc [B][H][S][D][D]
+ * (sum over the selecting queries of coefficient^T grad).  Reference rounding points:
+ * d coefficient = bf16(grad . C^T) (indirect_fine.py:185-206), the d z terms rounded
+ * to bf16 per (query, fine, channel); the caller rounds dz and dc to bf16. */
+int tao_feature_read_backward(const void* grad, const void* raw_q, const void* fine_z,
+                              const void* fine_c, const int16_t* sel, int batch, int tokens,
+                              int heads, int width, int mmax, void* d_raw_q, float* dz, float* dc,
+                              int* err, void* stream);
 
 #ifdef __cplusplus
 }

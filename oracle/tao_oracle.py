@@ -711,10 +711,9 @@ def _tile_read(query, page_z, fine_z, fine_c, completed, pending, group=8, page_
         sel = topk_oldest(scores, count)
         sel_id = cand_ids.gather(-1, sel)
         sel_page = cand_pages.gather(-1, sel)
-    if feature:
-        bi = torch.arange(b)[:, None, None, None]
-        hi = torch.arange(heads)[None, None, :, None]
-        return feature_read(h, fine_z[bi, hi, sel_id], sel_id, fine_c), sel_id, coarse_out
+    if feature:   # the selected z by expand + gather, as the reference (its adjoint sums in fp32)
+        sel_z = fine_z[:, None].expand(-1, length, -1, -1, -1).gather(3, sel_id.unsqueeze(-1).expand(-1, -1, -1, -1, d))
+        return feature_read(h, sel_z, sel_id, fine_c), sel_id, coarse_out
     num, den = _SelectedRead.apply(hv, seg_w, sel_id, sel_page, fine_c)
     return (num / den).to(dt), sel_id, coarse_out
 

@@ -79,7 +79,8 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
   if (int rc = launch_window_attention(q, k, v, static_cast<bf16*>(tb.local), tb.lse, B, T, H, D, tb.err, s))
     return rc;
   if (ev1) cudaEventRecord(ev1, s);
-  if (g.S > 0) {
+  const bool route_only = (tb.flags & TAO_TRAIN_ROUTE_ONLY) != 0;  // z and page prefixes from the caller
+  if (g.S > 0 && !route_only) {
     // 2. writer over all sealed blocks (tcgen05 by default, mma.sync with attention
     // variant 0), 3. page prefix table
     const int write_c = (tb.flags & TAO_TRAIN_CALLER_FINE_C) ? 0 : 1;
@@ -117,6 +118,7 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
   a.mmax = g.mmax;
   a.err = tb.err;
   a.external_fusion = (tb.flags & TAO_TRAIN_EXTERNAL_FUSION) ? 1 : 0;
+  a.route_only = route_only ? 1 : 0;
   const size_t rsmem = ReadSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the training read kernel");
   if (!tsmem(train_read_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
@@ -144,11 +146,17 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
       return tfail(TAO_ERR_CUDA, "d_raw_k tail memset");
   }
   // width 128 splits a tile's queries over two CTAs that add into the same dC partial
-  if (ReadBwdSmem<D>::NQ < 256 && a.npairs > 0 &&
+  if (!a.route_only && ReadBwdSmem<D>::NQ < 256 && a.npairs > 0 &&
       cudaMemsetAsync(a.dcp, 0, (size_t)B * H * a.npairs * D * D * 2, s) != cudaSuccess)
     return tfail(TAO_ERR_CUDA, "dc_partial memset");
+  if (a.route_only) {
+    // the caller differentiates the writer and the read: no raw_q / raw_k gradient here
+    const size_t bytes = (size_t)B * T * H * D * 2;
+    if (cudaMemsetAsync(a.d_raw_q, 0, bytes, s) != cudaSuccess || cudaMemsetAsync(a.d_raw_k, 0, bytes, s) != cudaSuccess)
+      return tfail(TAO_ERR_CUDA, "route-only gradient memset");
+  }
   const dim3 fgrid((T + 8 * kFusionRowsPerWarp - 1) / (8 * kFusionRowsPerWarp), B * H);
-  if (a.external_fusion)
+  if (a.external_fusion || a.route_only)
     split_bwd_kernel<D><<<fgrid, 256, 0, s>>>(a);
   else
     fusion_bwd_kernel<D><<<fgrid, 256, 0, s>>>(a);
@@ -162,6 +170,10 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
       return tfail(TAO_ERR_CUDA, "smem attribute");
     attn_bwd_kv_kernel<D><<<dim3((T + 63) / 64, B * H), 128, asmem, s>>>(a);
     attn_bwd_q_kernel<D><<<dim3((T + 63) / 64, B * H), 128, asmem, s>>>(a);
+  }
+  if (a.route_only) {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TAO_OK : tfail(TAO_ERR_CUDA, cudaGetErrorString(e));
   }
   const size_t rsmem = ReadBwdSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the read backward kernel");
@@ -218,6 +230,7 @@ int tao_train_backward(const void* grad_out, const void* q, const void* k, const
   a.err = saved->err;
   a.caller_c = (saved->flags & TAO_TRAIN_CALLER_FINE_C) ? 1 : 0;
   a.external_fusion = (saved->flags & TAO_TRAIN_EXTERNAL_FUSION) ? 1 : 0;
+  a.route_only = (saved->flags & TAO_TRAIN_ROUTE_ONLY) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return width == 64 ? train_backward<64>(a, s) : train_backward<128>(a, s);
 }

@@ -25,6 +25,7 @@ struct BwdArgs {
   float* dq_acc;                 // fp32 [B,T,H,D] dQ accumulator (tensor-core path) or null
   int caller_c;                  // 1: fine C came from the caller; writer backward: z path only
   int external_fusion;           // 1: g is d(fine), d_local comes from the caller (split_bwd_kernel)
+  int route_only;                // 1: only the local attention's gradients (the caller reads the fines)
   int npairs;                    // sum over tiles of visible fines
   TrainDims dm;
   int pages, mmax;
@@ -53,7 +54,7 @@ __global__ void __launch_bounds__(256) split_bwd_kernel(BwdArgs a) {
   for (int rr = 0; rr < rows; ++rr) {
     const int t = t0 + rr;
     const long long base = ((long long)b * a.dm.T + t) * a.dm.row + (long long)h * D + 2 * lane;
-    const bool present = t >= kWindow;
+    const bool present = t >= kWindow && !a.route_only;
     const float den = present ? a.den[((long long)b * a.dm.T + t) * a.dm.H + h] : 1.f;
     float rowdot = 0.f, dden = 0.f;
 #pragma unroll

@@ -216,6 +216,7 @@ struct ReadArgs {
   int pages, mmax, umax;
   int* err;
   int external_fusion;                   // 1: out = fine (the caller fuses), no pointwise gate here
+  int route_only;                        // 1: routing into sel_out only (the caller reads the fines)
 };
 
 template <int D>
@@ -250,6 +251,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   const long long hoff = (long long)h * D;
 
   if (V == 0) {  // no history: output = local (operator.py:39); external fusion: fine = 0
+    if (a.route_only) return;
     for (int idx = tid; idx < nq * (D / 8); idx += 256) {
       const int q = idx / (D / 8), c = idx % (D / 8);
       const long long off = ((long long)b * a.dm.T + q0 + q) * row + hoff + c * 8;
@@ -451,6 +453,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
     nused = n;
   }
   __syncthreads();
+  if (a.route_only) return;  // the caller reads the selected fines itself
 
   // ---- 3. dense per-fine GEMMs on the tensor cores
   constexpr int NTL = D / 8;

@@ -51,13 +51,13 @@ def is_refresh(pos, layer, config):
 
 
 def check_config(config, training=False):
-    """The sm_100a kernels implement the index-only preset with the softmax and
-    regularised-association writers, for streaming also the feature-mass and
-    structured-Gram writers, and the coarse value branch (coarse_index_only=False,
+    """The sm_100a kernels implement the index-only preset with all four fine
+    writers (softmax, regularised-association, feature-mass and structured-Gram),
+    in streaming and in training, and the coarse value branch (coarse_index_only=False,
     the historical default) with the softmax writer."""
     if (config.fine_tokens, config.local_keep, config.coarse_group) != (FINE, KEEP, GROUP):
         raise ValueError("kernels are specialised for fine_tokens=256, local_keep=512, coarse_group=8")
-    writers = WRITERS_B200[:2] if training else WRITERS_B200
+    writers = WRITERS_B200
     if config.fine_writer not in writers:
         raise NotImplementedError("fine_writer=%r is not implemented on B200 %s(implemented: %s)"
                                   % (config.fine_writer, "training " if training else "", ", ".join(writers)))

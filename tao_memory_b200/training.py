@@ -123,7 +123,11 @@ def tao_attention_train(q, k, v, raw_q, raw_k, fusion_a, fusion_b, alpha, config
     if not config.coarse_index_only:
         from .training_coarse import tao_attention_coarse
         return tao_attention_coarse(*(t.contiguous() for t in ops), fusion_a, fusion_b, gain)
+    if config.fine_writer in ("feature_mass_association", "structured_gram_association") and q.shape[1] > 768:
+        from .training_feature import tao_attention_feature
+        return tao_attention_feature(*(t.contiguous() for t in ops), fusion_a, fusion_b, gain, config.fine_writer)
     fa = fusion_a.to(_BF16)
     fb = fusion_b.to(_BF16)
-    return _TaoAttention.apply(*(t.contiguous() for t in ops), fa.contiguous(), fb.contiguous(), gain,
-                               config.fine_writer)
+    writer = "softmax" if config.fine_writer in ("feature_mass_association", "structured_gram_association") \
+        else config.fine_writer   # <= 768 tokens: no sealed fine, the output is the local attention
+    return _TaoAttention.apply(*(t.contiguous() for t in ops), fa.contiguous(), fb.contiguous(), gain, writer)

@@ -100,12 +100,13 @@ def coarse_read(raw_q, raw_k, v):
     return torch.cat(pieces, dim=1)
 
 
-def fuse(local, raw_q, coarse, fine, fusion_a, fusion_b, gains):
-    """Three-term pointwise gate (operator.py:21-39); gains [H] = bf16(2 * alpha_h)."""
+def fuse(local, raw_q, coarse, fine, fusion_a, fusion_b, gains, with_coarse=True):
+    """Three-term pointwise gate (operator.py:21-39); gains [H] = bf16(2 * alpha_h).
+    with_coarse=False: index-only pages (the coarse term is absent everywhere)."""
     t = raw_q.shape[1]
     pos = torch.arange(t, device=raw_q.device)[None, :, None, None]
     fine_present = pos >= FIRST_FINE
-    coarse_present = pos >= FIRST_COARSE
+    coarse_present = (pos >= FIRST_COARSE) & with_coarse
     score = (fusion_a.to(_BF16) * raw_q.unsqueeze(-1)).to(_BF16)
     score = (score + fusion_b.to(_BF16)).to(_BF16)
     count = coarse_present.to(torch.int32) + fine_present.to(torch.int32)

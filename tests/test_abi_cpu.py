@@ -107,16 +107,17 @@ def test_config_validation_matches_reference():
 
 
 @pytest.mark.parametrize("writer", ["feature_mass_association", "structured_gram_association"])
-def test_feature_read_writers_are_streaming_only(writer):
-    """The feature-mass and structured-Gram writers run in streaming (prefill/decode)
-    on B200 with the feature-mass read; training with them is refused loudly rather
-    than computed with another read."""
+def test_feature_read_writers_policy(writer):
+    """The feature-mass and structured-Gram writers run in streaming and in training
+    on the index-only preset with the feature-mass read; with the coarse value branch
+    they are refused loudly rather than computed with another read."""
     from tao_memory_b200.stream import check_config, policy_for
     cfg = TaoConfig(**{**index_only_page_memo().export(), "fine_writer": writer})
     check_config(cfg)
+    check_config(cfg, training=True)
     assert policy_for(cfg).fine_read == 1 and policy_for(index_only_page_memo()).fine_read == 0
     with pytest.raises(NotImplementedError):
-        check_config(cfg, training=True)
+        check_config(TaoConfig(fine_writer=writer), training=True)
 
 
 def test_batch_argument_cache_keys_on_layer_and_policy():
