@@ -403,6 +403,21 @@ int tao_feature_read_backward(const void* grad, const void* raw_q, const void* f
                               int heads, int width, int mmax, void* d_raw_q, float* dz, float* dc,
                               int* err, void* stream);
 
+/* Model-side neighbour (reference examples/common.py:6-20): split a fused Q/K/V
+ * projection projected [rows][3][heads][width] bf16 (x W^T of the caller's GEMM) into
+ * raw_q, raw_k, v [rows][heads][width] and q = rms_norm(raw_q), k = rms_norm(raw_k)
+ * over the width: x * rsqrt(mean(x^2) + eps) in fp32 (torch's rms_norm default eps is
+ * the fp32 epsilon 2^-23, its compute type's).  One warp per (row, head). */
+int tao_qkv_split_norm(const void* projected, long long rows, int heads, int width, float eps, void* q,
+                       void* k, void* v, void* raw_q, void* raw_k, void* stream);
+
+/* Backward of tao_qkv_split_norm: d_projected [rows][3][heads][width] bf16 =
+ * [d_raw_q + bf16(dx_q), d_raw_k + bf16(dx_k), dv] with the RMS-norm adjoint
+ * dx = r dy - x r^3 sum_j(x_j dy_j) / width in fp32. */
+int tao_qkv_split_norm_backward(const void* raw_q, const void* raw_k, const void* dq, const void* dk,
+                                const void* dv, const void* d_raw_q, const void* d_raw_k, long long rows,
+                                int heads, int width, float eps, void* d_projected, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

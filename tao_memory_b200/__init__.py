@@ -7,7 +7,8 @@ Drop-in for the reference package's public API (``tao_attention/__init__.py``):
 ``copy_to_device`` / ``copy_to_host`` for a decode step's operands in page-locked
 host memory, ``DecodeSession`` for a serving loop over a fixed batch whose
 tokens arrive in and leave through page-locked host memory, and the serving caller
-(``RequestStates``, ``DecodeScheduler``, ``save_snapshot`` / ``load_snapshot``).  All compute runs in
+(``RequestStates``, ``DecodeScheduler``, ``save_snapshot`` / ``load_snapshot``);
+``tao_memory_b200.model`` holds the model-side neighbours (``ProjectedInputs``).  All compute runs in
 ``libtao_b200.so`` (hand-written CUDA for sm_100a) behind a C ABI.
 """
 

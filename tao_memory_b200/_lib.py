@@ -75,6 +75,8 @@ _SIGNATURES = {
     "tao_train_geometry": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "tao_train_forward": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP, _VP, _VP]),
     "tao_train_backward": (_I, [_VP] * 9 + [_I, _I, _I, _I, _VP, _VP, _VP, _VP]),
+    "tao_qkv_split_norm": (_I, [_VP, _I64, _I, _I, _F, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "tao_qkv_split_norm_backward": (_I, [_VP] * 7 + [_I64, _I, _I, _F, _VP, _VP]),
     "tao_feature_read_forward": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _VP, _VP]),
     "tao_feature_read_backward": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _VP, _VP, _VP, _VP]),
     "tao_train_pairs": (_I, [_I]),

@@ -18,27 +18,24 @@ class _Grads(ctypes.Structure):
 def _regularized_backward(saved, gr, s):
     """C path of fine_writer="regularized_association": the library returned dC
     (fp32 sum of the per-tile bf16 partials) and the z path; differentiate
-    C = association_matrix(association_statistics(raw_k, v)) per sealed block with
-    torch autograd, as the reference does (association_writer.py:11-32 under
-    tao_stream.py:113-117), and add the result to d raw_k and dv in bf16."""
+    C = association_matrix(association_statistics(raw_k, v)) per sealed block
+    (association_writer.py:11-32 under tao_stream.py:113-117): the statistics come
+    from the library's writer-statistics kernel with their explicit adjoint
+    (training_feature._WriterStats), torch autograd runs through the regularised
+    Cholesky solve only; the result is added to d raw_k and dv in bf16."""
+    from .training_feature import _WriterStats
     raw_k, v = saved["raw_k"], saved["v"]
-    b, t, h, d = raw_k.shape
-    n = s * 256
+    d = raw_k.shape[-1]
     with torch.enable_grad():
-        kb = raw_k[:, :n].detach().requires_grad_(True)
-        vb = v[:, :n].detach().requires_grad_(True)
-        keys = kb.reshape(b * s, 256, h, d)
-        values = vb.reshape(b * s, 256, h, d)
-        u = keys.float().softmax(dim=-1).to(_BF16).transpose(1, 2).float()
-        vals = values.transpose(1, 2).float()
-        gram, cross = u.transpose(-1, -2) @ u, u.transpose(-1, -2) @ vals
+        kb = raw_k.detach().requires_grad_(True)
+        vb = v.detach().requires_grad_(True)
+        gram, cross, _ = _WriterStats.apply(kb, vb, s)
         reg = gram.diagonal(dim1=-2, dim2=-1).sum(-1) / d
         system = gram + reg[..., None, None] * torch.eye(d, dtype=torch.float32, device=raw_k.device)
         c = torch.cholesky_solve(cross, torch.linalg.cholesky(system)).to(_BF16)
-        c = c.reshape(b, s, h, d, d).permute(0, 2, 1, 3, 4)
         dk, dv = torch.autograd.grad(c, (kb, vb), gr["dC"].to(_BF16))
-    gr["d_raw_k"][:, :n] += dk
-    gr["dv"][:, :n] += dv
+    gr["d_raw_k"] += dk
+    gr["dv"] += dv
 
 
 def backward(ctx, grad, d_local=None):
