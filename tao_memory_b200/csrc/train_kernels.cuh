@@ -5,6 +5,7 @@
 // (fusion).  Every query routes (route_interval = 1): tile t of 256 queries sees
 // the first max(0, t - 2) sealed fines.
 #pragma once
+#include "tcgen05.cuh"
 #include "common.cuh"
 #include "window_attention.cuh"
 
@@ -217,6 +218,7 @@ struct ReadArgs {
   int* err;
   int external_fusion;                   // 1: out = fine (the caller fuses), no pointwise gate here
   int route_only;                        // 1: routing into sel_out only (the caller reads the fines)
+  int tc;                                // 1 (width 64): the selected read on tcgen05 (TMEM accumulators)
 };
 
 template <int D>
@@ -233,11 +235,75 @@ struct ReadSmem {
     s += 256 * (size_t)(mmax + 1) * 4;  // top ids
     s += 256 * 4 + (size_t)(V + 8) * 4 * 2 + 256;   // den, use flags + list, misc
     s += (size_t)(V + 31) / 32 * 256 * 4;          // selection bits [word][query]
-    return s;
+    return s + 1024;                               // slack to align the window to 1024 bytes
+
   }
 };
 
-template <int D>
+// Epilogue of the selected read for channels e, e + 1 of one query (operator.py:21-39,
+// index-only preset): fine = bf16(bf16(num) / den), the pointwise gate with raw_q q2
+// and the local output l2 (bf16 pairs), or with external fusion fine alone; every
+// rounding point rounds the pair with one conversion; bf16(x + 0) and bf16(2 * local)
+// are exact and not re-rounded (x + 0 is kept: it turns -0 into +0).
+TAO_DEVI void read_epilogue_pair(const ReadArgs& a, long long base, int e, float n0, float n1, float den,
+                                 uint32_t q2, uint32_t l2, const float* fab0, const float* fab1, float gain) {
+  const float qv[2] = {lo_f(q2), hi_f(q2)}, loc[2] = {lo_f(l2), hi_f(l2)};
+  float nums[2] = {n0, n1};
+  rb2(nums[0], nums[1]);
+  float fine[2], s0[2], s2[2], rho0[2], rho2[2], lt[2], fg[2], res[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const float* fa = fab0 + (e + x) * 3;
+    fine[x] = __fdiv_rn(nums[x], den);
+    s0[x] = __fmul_rn(fa[0], qv[x]);
+    s2[x] = __fmul_rn(fa[2], qv[x]);
+  }
+  rb2(fine[0], fine[1]);
+  if (a.external_fusion) {   // the caller applies the pointwise gate: out = fine
+    *reinterpret_cast<uint32_t*>(a.out + base + e) = pack_exact(fine[0], fine[1]);
+    *reinterpret_cast<uint32_t*>(a.num_out + base + e) = pack_exact(nums[0], nums[1]);
+    return;
+  }
+  rb2(s0[0], s0[1]);
+  rb2(s2[0], s2[1]);
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const float* fb = fab1 + (e + x) * 3;
+    s0[x] = __fadd_rn(s0[x], fb[0]);
+    s2[x] = __fadd_rn(s2[x], fb[2]);
+    fg[x] = __fmul_rn(gain, fine[x]);
+  }
+  rb2(s0[0], s0[1]);
+  rb2(s2[0], s2[1]);
+  rb2(fg[0], fg[1]);
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const float mx = fmaxf(s0[x], s2[x]);
+    // the larger term is exp(0) = 1 exactly: one exponential per element
+    const float eo = expf(fminf(s0[x], s2[x]) - mx);
+    const float e0 = s0[x] >= s2[x] ? 1.f : eo, e2 = s0[x] >= s2[x] ? eo : 1.f;
+    rho0[x] = __fdiv_rn(e0, e0 + e2);
+    rho2[x] = __fdiv_rn(e2, e0 + e2);
+  }
+  rb2(rho0[0], rho0[1]);
+  rb2(rho2[0], rho2[1]);
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    lt[x] = __fmul_rn(rho0[x], __fmul_rn(2.f, loc[x]));
+    res[x] = __fmul_rn(rho2[x], fg[x]);
+  }
+  rb2(lt[0], lt[1]);
+  rb2(res[0], res[1]);
+#pragma unroll
+  for (int x = 0; x < 2; ++x) res[x] = __fadd_rn(__fadd_rn(lt[x], 0.f), res[x]);
+  rb2(res[0], res[1]);
+  *reinterpret_cast<uint32_t*>(a.out + base + e) = pack_exact(res[0], res[1]);
+  *reinterpret_cast<uint32_t*>(a.num_out + base + e) = pack_exact(nums[0], nums[1]);
+}
+
+// TC (width 64): the selected read on tcgen05 (a separate instantiation, so that each
+// kernel carries the code of one contraction path only).
+template <int D, bool TC = false>
 __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   using namespace wa;
   constexpr int NBUF = ReadSmem<D>::NBUF;
@@ -269,7 +335,9 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
     return;
   }
 
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // 1024-byte aligned window: the A and C tiles are 128B-swizzled tensor-core operands
+  uint8_t* const smem = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
   uint8_t* ptr = smem;
   const uint32_t sH = smem_u32(ptr);   ptr += 256 * D * 2;
   const uint32_t sA = smem_u32(ptr);   ptr += 256 * D * 2;
@@ -454,7 +522,159 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   }
   __syncthreads();
   if (a.route_only) return;  // the caller reads the selected fines itself
+  __shared__ float fabS[2][D * 3];   // the epilogue's fusion parameters of this head
 
+  if constexpr (D == 64 && TC) {
+    {
+      // ---- 3'. the selected read on the 5th-generation tensor cores.  Per listed fine i:
+      // each thread writes its query's row of A_i = bf16(hv * w) (zero when the query
+      // did not select the fine) into TMEM (tcgen05.st: lane = row, a 32-bit column =
+      // two channels), then one thread issues NUM[rows 0-127] += A_i[0:128] C_i and
+      // NUM[rows 128-255] += A_i[128:256] C_i as tcgen05.mma with A read from TMEM
+      // (M = 128, N = 64, K = 64; C_i [d][e] from shared memory, 128B-swizzled, read
+      // MN-major) into two TMEM accumulators, and commits to the mbarrier of A buffer
+      // i % 2.  A has two TMEM buffers and C four shared-memory buffers: while MMA i runs
+      // the threads form A_{i+1} and C_{i+2} is in flight; a buffer is reused only after
+      // the MMA that read it has committed (bounded waits).
+      // TMEM: accumulators at columns 0-127, A buffers at 128-191 and 192-255.
+      using namespace tc;
+      __shared__ __align__(8) uint64_t tbar[2];
+      __shared__ uint32_t tslot;
+      __shared__ int tok;
+      if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tslot)),
+                     "r"(256));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+      }
+      if (tid == 0) {
+        mbar_init(&tbar[0], 1);
+        mbar_init(&tbar[1], 1);
+        fence_mbar_init();
+      }
+      fence_before();
+      __syncthreads();
+      fence_after();
+      const uint32_t tacc = tslot;
+      const bf16* cbt = a.C + ((long long)b * a.dm.H + h) * a.dm.S * (long long)D * D;
+      // C buffers 0, 1 in the C region, 2, 3 in the (now unused) A tile
+      auto cbuf = [&](int k) -> uint32_t { return k < 2 ? sC + k * D * D * 2 : sA + (k - 2) * D * D * 2; };
+      auto load_ct = [&](int s2, int k) {
+        const bf16* src = cbt + (long long)s2 * D * D;
+        for (int idx = tid; idx < D * D / 8; idx += 256) {
+          const int r = idx / (D / 8), c = idx % (D / 8);
+          cp_async16(cbuf(k) + swz(r, c * 8, D), src + r * D + c * 8, true);
+        }
+        cp_commit();
+      };
+      constexpr uint32_t I = idesc_bf16(128, 64, 0, 1);
+      const int nu = nused;
+      const uint32_t arow = (uint32_t)((warp & 3) * 32) << 16;   // this warp's TMEM lanes
+      const int half = warp >> 2;                                  // rows 0-127 or 128-255
+      bool ok = true;
+      int issued = 0;   // MMA groups committed
+      if (nu > 0) load_ct(list[0], 0);
+      if (nu > 1) load_ct(list[1], 1);
+      for (int i = 0; i < nu; ++i) {
+        const int s2 = list[i], ab = i & 1;
+        if (i >= 2) {   // MMA i-2 read A buffer ab and C buffer (i-2) % 4
+          if (tid == 0) tok = mbar_wait(&tbar[ab], (uint32_t)(((i >> 1) - 1) & 1), a.err) ? 1 : 0;
+          __syncthreads();
+          fence_after();
+          if (!tok) {
+            ok = false;
+            break;
+          }
+        }
+        if (i + 2 < nu) load_ct(list[i + 2], (i + 2) & 3);
+        uint32_t arow_v[32];
+        const bool sel = live && ((selB[(s2 >> 5) * 256 + q] >> (s2 & 31)) & 1u);
+        if (sel) {
+          uint32_t hv[D / 2];
+          page_hv(s2 / kGroup, hv);
+#pragma unroll
+          for (int c = 0; c < D / 2; ++c) arow_v[c] = hmul2u(hv[c], sw2[s2 * (D / 2) + c]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < D / 2; ++c) arow_v[c] = 0u;
+        }
+        tmem_st32u(tacc + 128 + ab * 64 + half * 32 + arow, arow_v);
+        // C_i complete: at most the two later loads stay in flight
+        if (i + 2 < nu) cp_wait<2>();
+        else if (i + 1 < nu) cp_wait<1>();
+        else cp_wait<0>();
+        fence_proxy_async();
+        fence_before();
+        __syncthreads();
+        if (tid == 0) {
+          fence_after();
+          const uint32_t cB = cbuf(i & 3);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t accf = (i > 0 || k > 0) ? 1u : 0u;
+            mma_ts(tacc, tacc + 128 + ab * 64 + k * 8, sdesc(cB + k * 2048, 8192, 1024), I, accf);
+            mma_ts(tacc + 64, tacc + 128 + ab * 64 + 32 + k * 8, sdesc(cB + k * 2048, 8192, 1024), I, accf);
+          }
+          commit(&tbar[ab]);
+        }
+        issued = i + 1;
+      }
+      // the last committed group covers every earlier MMA (also after a failed wait:
+      // nothing is left in flight when the TMEM is freed)
+      if (issued > 0) {
+        const int last = issued - 1;
+        if (tid == 0) tok = mbar_wait(&tbar[last & 1], (uint32_t)((last >> 1) & 1), a.err) ? 1 : 0;
+        __syncthreads();
+        fence_after();
+        ok = ok && tok != 0;
+      }
+      // epilogue: raw_q and local rows staged (coalesced) into the h and A tiles
+      for (int idx = tid; idx < nq * (D / 8); idx += 256) {
+        const int r = idx / (D / 8), c = idx % (D / 8);
+        const long long off = ((long long)b * a.dm.T + q0 + r) * row + hoff + c * 8;
+        cp_async16(sH + swz(r, c * 8, D), a.raw_q + off, true);
+        cp_async16(sA + swz(r, c * 8, D), a.local + off, true);
+      }
+      cp_commit();
+      for (int idx = tid; idx < D * 3; idx += 256) {
+        fabS[0][idx] = bf(a.fa[(long long)h * D * 3 + idx]);
+        fabS[1][idx] = bf(a.fb[(long long)h * D * 3 + idx]);
+      }
+      cp_wait<0>();
+      __syncthreads();
+      if (ok) {
+        // thread t holds query row t: warps 0-3 read accumulator 0 (rows 0-127), warps
+        // 4-7 accumulator 1 (rows 128-255), each its 32 TMEM lanes
+        const float gain = a.gain[h];
+        const int r = tid;
+        const uint32_t tl = tacc + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(warp >> 2) * 64;
+        const long long base = ((long long)b * a.dm.T + q0 + r) * row + hoff;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          float v[32];
+          if (nu > 0) {
+            tmem_ld32(tl + c0, v);
+          } else {
+#pragma unroll
+            for (int x = 0; x < 32; ++x) v[x] = 0.f;
+          }
+          if (r < nq) {
+            const float den = denS[r];
+#pragma unroll
+            for (int x = 0; x < 32; x += 2) {
+              const int e = c0 + x;
+              const uint32_t q2 = *reinterpret_cast<const uint32_t*>(smem + swz(r, e, D));
+              const uint32_t l2 = *reinterpret_cast<const uint32_t*>(smem + 256 * D * 2 + swz(r, e, D));
+              read_epilogue_pair(a, base, e, v[x], v[x + 1], den, q2, l2, fabS[0], fabS[1], gain);
+            }
+          }
+        }
+      }
+      fence_before();
+      __syncthreads();
+      if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tacc), "r"(256));
+      return;
+    }
+  } else {
   // ---- 3. dense per-fine GEMMs on the tensor cores
   constexpr int NTL = D / 8;
   float acc[2][NTL][4];
@@ -524,7 +744,6 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   // ---- 4. epilogue: num, fine, fusion (operator.py:21-39, index-only preset).
   // The tile's raw_q and local rows are staged (coalesced) into the h and A
   // buffers, free now, and the fusion parameters of this head into shared memory.
-  __shared__ float fabS[2][D * 3];
   for (int idx = tid; idx < nq * (D / 8); idx += 256) {
     const int r = idx / (D / 8), c = idx % (D / 8);
     const long long off = ((long long)b * a.dm.T + q0 + r) * row + hoff + c * 8;
@@ -556,61 +775,12 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
         const int e = j * 8 + c4 * 2;
         const uint32_t q2 = *reinterpret_cast<const uint32_t*>(smem + swz(r, e, D));
         const uint32_t l2 = *reinterpret_cast<const uint32_t*>(smem + 256 * D * 2 + swz(r, e, D));
-        const float qv[2] = {lo_f(q2), hi_f(q2)}, loc[2] = {lo_f(l2), hi_f(l2)};
-        float nums[2] = {acc[mi][j][hr * 2], acc[mi][j][hr * 2 + 1]};
-        rb2(nums[0], nums[1]);
-        float fine[2], s0[2], s2[2], rho0[2], rho2[2], lt[2], fg[2], res[2];
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float* fa = fabS[0] + (e + x) * 3;
-          fine[x] = __fdiv_rn(nums[x], den);
-          s0[x] = __fmul_rn(fa[0], qv[x]);
-          s2[x] = __fmul_rn(fa[2], qv[x]);
-        }
-        rb2(fine[0], fine[1]);
-        if (a.external_fusion) {   // the caller applies the pointwise gate: out = fine
-          *reinterpret_cast<uint32_t*>(a.out + base + e) = pack_exact(fine[0], fine[1]);
-          *reinterpret_cast<uint32_t*>(a.num_out + base + e) = pack_exact(nums[0], nums[1]);
-          continue;
-        }
-        rb2(s0[0], s0[1]);
-        rb2(s2[0], s2[1]);
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float* fb = fabS[1] + (e + x) * 3;
-          s0[x] = __fadd_rn(s0[x], fb[0]);
-          s2[x] = __fadd_rn(s2[x], fb[2]);
-          fg[x] = __fmul_rn(gain, fine[x]);
-        }
-        rb2(s0[0], s0[1]);
-        rb2(s2[0], s2[1]);
-        rb2(fg[0], fg[1]);
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float mx = fmaxf(s0[x], s2[x]);
-          // the larger term is exp(0) = 1 exactly: one exponential per element
-          const float eo = expf(fminf(s0[x], s2[x]) - mx);
-          const float e0 = s0[x] >= s2[x] ? 1.f : eo, e2 = s0[x] >= s2[x] ? eo : 1.f;
-          rho0[x] = __fdiv_rn(e0, e0 + e2);
-          rho2[x] = __fdiv_rn(e2, e0 + e2);
-        }
-        rb2(rho0[0], rho0[1]);
-        rb2(rho2[0], rho2[1]);
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          lt[x] = __fmul_rn(rho0[x], __fmul_rn(2.f, loc[x]));
-          res[x] = __fmul_rn(rho2[x], fg[x]);
-        }
-        rb2(lt[0], lt[1]);
-        rb2(res[0], res[1]);
-#pragma unroll
-        for (int x = 0; x < 2; ++x) res[x] = __fadd_rn(__fadd_rn(lt[x], 0.f), res[x]);
-        rb2(res[0], res[1]);
-        *reinterpret_cast<uint32_t*>(a.out + base + e) = pack_exact(res[0], res[1]);
-        *reinterpret_cast<uint32_t*>(a.num_out + base + e) = pack_exact(nums[0], nums[1]);
+        read_epilogue_pair(a, base, e, acc[mi][j][hr * 2], acc[mi][j][hr * 2 + 1], den, q2, l2, fabS[0], fabS[1],
+                           gain);
       }
     }
   }
+  }  // the mma.sync path
 }
 
 }  // namespace tao
