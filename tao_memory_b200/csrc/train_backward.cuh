@@ -5,6 +5,7 @@
 // _SelectedRead.backward (selected_read.py:175-187) and of the writer and page
 // summaries (tao_stream.py:80-123, 530-593).  Rounding points follow those ops.
 #pragma once
+#include "tcgen05.cuh"
 #include "common.cuh"
 #include "window_attention.cuh"
 #include "train_kernels.cuh"
@@ -610,7 +611,7 @@ struct ReadBwdSmem {
   static constexpr int CB = (D == 64) ? 2 : 1;      // C_s buffers (2: next fine prefetched)
   static size_t bytes(int P, int V, int /*mmax*/) {
     const size_t words = (size_t)(V + 31) / 32;
-    return 3 * (size_t)NQ * D * 2 + (size_t)CB * D * D * 2 + (size_t)NQ * D * 4 + 4 * (size_t)P * D * 4 +
+    return 1024 + 3 * (size_t)NQ * D * 2 + (size_t)CB * D * D * 2 + (size_t)NQ * (D + 2) * 4 + 4 * (size_t)P * D * 4 +
            (size_t)P * D * 2 + (size_t)D * 2 + words * NQ * 4 + NQ * 4 + NQ + (size_t)(NT / 32) * D * 4 +
            (size_t)(V + 8) * 4 * 2 + 64;
   }
@@ -623,7 +624,9 @@ TAO_DEVI int dhv_off(int r, int d) {
   return r * D + ((((d >> 2) ^ (r & 7))) << 2) + (d & 3);
 }
 
-template <int D>
+// TC (width 64): dA and dC on tcgen05 over the tile's dense query rows (a separate
+// instantiation: each kernel carries one contraction path).
+template <int D, bool TC = false>
 __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs a) {
   using namespace wa;
   constexpr int NQ = ReadBwdSmem<D>::NQ, NT = ReadBwdSmem<D>::NT, CB = ReadBwdSmem<D>::CB, QS = 256 / NQ;
@@ -644,7 +647,9 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
   }
   const int completed = V / kGroup, pending = V % kGroup, P = completed + (pending > 0);
   const int M = a.mmax, VW = (V + 31) / 32;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // 1024-byte aligned window: the tiles are 128B-swizzled tensor-core operands
+  uint8_t* const smem = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
   uint8_t* ptr = smem;
   const uint32_t sH = smem_u32(ptr);  ptr += NQ * D * 2;
   const uint32_t sG = smem_u32(ptr);  ptr += NQ * D * 2;
@@ -652,7 +657,11 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
   const uint32_t sC = smem_u32(ptr);  ptr += CB * D * D * 2;
   uint8_t* hB = smem;
   uint8_t* aB = smem + 2 * NQ * D * 2;
-  float* dhvS = reinterpret_cast<float*>(ptr);  ptr += (size_t)NQ * D * 4;  // dhv of the current page
+  float* dhvS = reinterpret_cast<float*>(ptr);  ptr += (size_t)NQ * (D + 2) * 4;  // dhv of the current page
+  // dhv cell of (row, channel pair): swizzled rows for the fragment accesses of the
+  // mma.sync path; padded rows (D + 2 floats) for the row-per-thread accesses of the
+  // tcgen05 path (two 64-bit wavefronts per warp)
+  auto dho = [](int r, int d) -> int { return TC ? r * (D + 2) + d : dhv_off<D>(r, d); };
   float* pwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* pzS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* dpwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
@@ -666,6 +675,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
   int* useS = reinterpret_cast<int*>(ptr);
   int* list = useS + V;
   __shared__ int cntS[NW];
+  __shared__ unsigned balS[NW];   // the selecting queries of each warp for the current fine
 
   // ---- tables (as in the forward)
   const bf16* pzb = a.pzpre + ((long long)b * a.dm.H + h) * a.pages * kGroup * D;
@@ -677,7 +687,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
     dpzS[idx] = 0.f;
   }
   for (int i = tid; i < V; i += NT) useS[i] = 0;
-  for (int i = tid; i < NQ * D; i += NT) dhvS[i] = 0.f;
+  for (int i = tid; i < NQ * (D + 2); i += NT) dhvS[i] = 0.f;
   __syncthreads();
   for (int d = tid; d < D; d += NT) {
     float mx = -INFINITY;
@@ -836,12 +846,12 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {  // all loads before the stores that clear the cells
         const int d = j * 8 + c4 * 2;
-        acc[j] = *reinterpret_cast<const float2*>(dhvS + dhv_off<D>(r, d));
+        acc[j] = *reinterpret_cast<const float2*>(dhvS + dho(r, d));
         hp[j] = pair_at(hB, r, d);
       }
 #pragma unroll
       for (int j = 0; j < NTL; ++j)
-        *reinterpret_cast<float2*>(dhvS + dhv_off<D>(r, j * 8 + c4 * 2)) = make_float2(0.f, 0.f);
+        *reinterpret_cast<float2*>(dhvS + dho(r, j * 8 + c4 * 2)) = make_float2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {
         const int d = j * 8 + c4 * 2;
@@ -871,6 +881,28 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
     fetch_c(list[0], 0);
     cp_commit();
   }
+  // tcgen05 path: TMEM columns 0-127 hold dA of query rows 0-127 / 128-255, columns
+  // 128-191 dC_s (lanes 0-63 = rows d); one mbarrier for the MMA group of a fine
+  __shared__ __align__(8) uint64_t tbar;
+  __shared__ uint32_t tslot;
+  __shared__ int tok;
+  uint32_t tbase = 0, tphase = 0;
+  bool tc_ok = true;
+  if constexpr (TC) {
+    if (warp == 0) {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tslot)),
+                   "r"(256));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (tid == 0) {
+      mbar_init(&tbar, 1);
+      fence_mbar_init();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    tbase = tslot;
+  }
   for (int i = 0; i < nu; ++i) {
     const int sf = list[i], pg = sf / kGroup;
     const int buf = (CB == 2) ? (i & 1) : 0;
@@ -892,8 +924,153 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
     cp_commit();
     const bool sel = first && ((selB[(sf >> 5) * NQ + q] >> (sf & 31)) & 1u);
     const unsigned ballot = __ballot_sync(0xffffffffu, sel);
-    if (lane == 0) cntS[warp] = __popc(ballot);
+    if (lane == 0) {
+      cntS[warp] = __popc(ballot);
+      balS[warp] = ballot;
+    }
     __syncthreads();
+    if constexpr (TC) {
+      // ---- phase 2': A_s over the dense query rows (row q = query q, zero unless it
+      // selected fine sf), K-major 128B-swizzled like the h and gn tiles
+      uint32_t hvw[D / 2];   // hv = bf16(h * pw[pg]) of this query, kept for the dA epilogue
+      {
+        const bool selq = sel;
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+          uint4 o = make_uint4(0, 0, 0, 0);
+          if (selq) {
+            const uint4 hc = *reinterpret_cast<const uint4*>(hB + swz(q, c * 8, D));
+            const uint4 pc = *reinterpret_cast<const uint4*>(pw2 + (pg * D + c * 8) / 2);
+            const uint4 wc = *reinterpret_cast<const uint4*>(w2 + c * 4);
+            hvw[c * 4] = hmul2u(hc.x, pc.x);
+            hvw[c * 4 + 1] = hmul2u(hc.y, pc.y);
+            hvw[c * 4 + 2] = hmul2u(hc.z, pc.z);
+            hvw[c * 4 + 3] = hmul2u(hc.w, pc.w);
+            o = make_uint4(hmul2u(hvw[c * 4], wc.x), hmul2u(hvw[c * 4 + 1], wc.y), hmul2u(hvw[c * 4 + 2], wc.z),
+                           hmul2u(hvw[c * 4 + 3], wc.w));
+          } else {
+            hvw[c * 4] = hvw[c * 4 + 1] = hvw[c * 4 + 2] = hvw[c * 4 + 3] = 0u;
+          }
+          *reinterpret_cast<uint4*>(aB + swz(q, c * 8, D)) = o;
+        }
+      }
+      if (CB == 2) cp_wait<1>();
+      else cp_wait<0>();
+      tc::fence_proxy_async();
+      tc::fence_before();
+      __syncthreads();
+      // ---- phase 3': dA = gn . C_s^T (M = 128 x 2 query halves, N = 64, K = 64; gn and
+      // C_s K-major) and dC_s = A_s^T . gn (M = 128 over d, K = 256 queries, both read
+      // MN-major; rows 64-127 of that instruction take the next 32 KB of shared memory
+      // as a stand-in and land in TMEM lanes nobody reads); bounded wait
+      const uint32_t cbuf = sC + buf * D * D * 2;
+      if (tid == 0) {
+        tc::fence_after();
+        if (tc_ok) {
+          constexpr uint32_t IA = tc::idesc_bf16(128, D, 0, 0), IC = tc::idesc_bf16(128, D, 1, 1);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            tc::mma(tbase, tc::sdesc(sG + k * 32, 16, 1024), tc::sdesc(cbuf + k * 32, 16, 1024), IA, k > 0 ? 1u : 0u);
+            tc::mma(tbase + 64, tc::sdesc(sG + 16384 + k * 32, 16, 1024), tc::sdesc(cbuf + k * 32, 16, 1024), IA,
+                    k > 0 ? 1u : 0u);
+          }
+#pragma unroll
+          for (int k = 0; k < NQ / 16; ++k)
+            tc::mma(tbase + 128, tc::sdesc(sA + k * 2048, NQ * 128, 1024), tc::sdesc(sG + k * 2048, NQ * 128, 1024),
+                    IC, k > 0 ? 1u : 0u);
+          tc::commit(&tbar);
+          tok = mbar_wait(&tbar, tphase, a.err) ? 1 : 0;
+        } else {
+          tok = 0;
+        }
+      }
+      __syncthreads();
+      tc::fence_after();
+      const bool okf = tok != 0;
+      if (tc_ok && !okf) {
+        tc_ok = false;   // the group stays in flight: drained (bounded) before the TMEM is freed
+      } else if (okf) {
+        tphase ^= 1u;
+      }
+      // dC_s of this tile: TMEM lanes 0-63 (warps 0 and 1), the reference's per-tile bf16
+      const long long pair = (long long)(tile - 3) * (tile - 2) / 2 + sf;
+      bf16* dcb = a.dcp + (((long long)b * a.dm.H + h) * a.npairs + pair) * (long long)D * D;
+      if (warp < D / 32) {
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          float v[32];
+          if (okf) {
+            tc::tmem_ld32(tbase + 128 + ((uint32_t)(warp * 32) << 16) + c0, v);
+          } else {
+#pragma unroll
+            for (int x = 0; x < 32; ++x) v[x] = 0.f;
+          }
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 o;
+            o.x = wa::pack_bf16(v[x], v[x + 1]);
+            o.y = wa::pack_bf16(v[x + 2], v[x + 3]);
+            o.z = wa::pack_bf16(v[x + 4], v[x + 5]);
+            o.w = wa::pack_bf16(v[x + 6], v[x + 7]);
+            *reinterpret_cast<uint4*>(dcb + (long long)tid * D + c0 + x) = o;
+          }
+        }
+      }
+      // dA of this thread's query row (TMEM lane q % 128 of accumulator q / 128):
+      // dA = bf16(bf16(gn . C^T) + gd); dhv += bf16(dA * w_s); the products
+      // bf16(dA * hv) go channel-major ([d][query], conflict-free) to the (now free) A
+      // tile for the column sums of dw_s
+      {
+        const float gdv = gdS[q];
+        bf16* phT = reinterpret_cast<bf16*>(aB) + q;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          float v[32];
+          if (okf) {
+            tc::tmem_ld32(tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(warp >> 2) * 64 + c0, v);
+          } else {
+#pragma unroll
+            for (int x = 0; x < 32; ++x) v[x] = 0.f;
+          }
+          if (sel) {
+#pragma unroll
+            for (int x = 0; x < 32; x += 2) {
+              const int d = c0 + x;
+              const uint32_t dav = wa::pack_bf16(__fadd_rn(rb(v[x]), gdv), __fadd_rn(rb(v[x + 1]), gdv));
+              const uint32_t pw_ = hmul2u(dav, w2[d / 2]);
+              const uint32_t ph = hmul2u(dav, hvw[d / 2]);
+              float2* cell = reinterpret_cast<float2*>(dhvS + dho(q, d));
+              float2 acc = *cell;
+              acc.x += lo_f(pw_);
+              acc.y += hi_f(pw_);
+              *cell = acc;
+              phT[(long long)d * NQ] = __ushort_as_bfloat16((unsigned short)(ph & 0xffffu));
+              phT[(long long)(d + 1) * NQ] = __ushort_as_bfloat16((unsigned short)(ph >> 16));
+            }
+          }
+        }
+      }
+      __syncthreads();
+      // dw_s partials: the NW groups of 32 queries (one warp's), summed over the groups in
+      // phase 4; only the selecting queries' products are read (the others hold A values)
+      static_assert(NQ / NW == 32, "one warp's queries per dw group");
+      for (int idx = tid; idx < NW * D; idx += NT) {
+        const int part = idx % NW, d = idx / NW;
+        const unsigned m = balS[part];
+        const uint4* col = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(aB) + (long long)d * NQ +
+                                                          part * 32);
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float f[8];
+          unpack8(col[c], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if ((m >> (c * 8 + e)) & 1u) sum += f[e];
+        }
+        dwS[part * D + d] = sum;
+      }
+    } else {
     // ---- phase 2: compacted row list and A_s = bf16(bf16(h * pw) * w_s) of the selecting queries
     int before = 0, ns = 0;
 #pragma unroll
@@ -965,7 +1142,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
 #pragma unroll
         for (int j = 0; j < NTL; ++j) {  // all loads before the stores
           const int d = j * 8 + c4 * 2;
-          acc[j] = *reinterpret_cast<const float2*>(dhvS + dhv_off<D>(r, d));
+          acc[j] = *reinterpret_cast<const float2*>(dhvS + dho(r, d));
           hp[j] = pair_at(hB, r, d);
         }
 #pragma unroll
@@ -980,7 +1157,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
           wpart[j][1] += hi_f(ph);
         }
 #pragma unroll
-        for (int j = 0; j < NTL; ++j) *reinterpret_cast<float2*>(dhvS + dhv_off<D>(r, j * 8 + c4 * 2)) = acc[j];
+        for (int j = 0; j < NTL; ++j) *reinterpret_cast<float2*>(dhvS + dho(r, j * 8 + c4 * 2)) = acc[j];
       }
     }
 #pragma unroll
@@ -1038,6 +1215,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
         }
       }
     }
+    }  // the mma.sync path
     __syncthreads();
     // ---- phase 4: dw_s -> d(z - pz) = bf16(bf16(dw) * w) : dz[s] += ., d page_z[pg] -= .
     for (int d = tid; d < D; d += NT) {
@@ -1048,6 +1226,12 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
       atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d, ddiff);
       dpzS[pg * D + d] -= ddiff;
     }
+  }
+  if constexpr (TC) {
+    if (!tc_ok && tid == 0) mbar_wait(&tbar, tphase, a.err);   // the group still in flight
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(256));
   }
   if (cur_page >= 0) flush_page(cur_page);
   __syncthreads();
