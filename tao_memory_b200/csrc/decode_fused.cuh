@@ -170,9 +170,10 @@ TAO_DEVI void drain_stages(uint64_t* bars, const uint32_t* armed, const uint32_t
 // CTA's items rotate through them, item j in stage j % NS, so with NS = 2 the copy of
 // the CTA's next item is already in flight while the current one computes; an item's
 // successor in its stage (i + NS * gridDim.x) is issued as soon as the item has
-// released the stage.  Registers are capped for 5 resident CTAs per SM.
+// released the stage.  Registers are capped for 6 resident CTAs per SM (the shared
+// memory's limit with one 32 KB stage).
 template <int D, int NS, int IB>
-__global__ void __launch_bounds__(128, 5) decode_fused_kernel(FusedArgs f) {
+__global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
   using Cfg = FusedCfg<D, IB>;
   const StepArgs& a = f.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
