@@ -61,7 +61,7 @@ L2_CLEAN_BYTES = 1 << 28   # read after the memset: its dirty lines are written 
 #   ncu --set full --clock-control none -k regex:decode_fused_kernel --nvtx --nvtx-include "timed_decode/" \
 #       -c 1 -o fused64 python bench.py --no-train --no-serving --no-parity --steps 6 --warmup 3
 # (dram__bytes_read.sum + dram__bytes_write.sum; profiles/decode_fused_kernel_decode128k.md).
-DECODE_TRAFFIC_BYTES = 46556160
+DECODE_TRAFFIC_BYTES = 46640896
 # The same for read_bwd_kernel in the train8k workload, one launch of
 #   ncu --section SpeedOfLight --section MemoryWorkloadAnalysis --section WarpStateStats \
 #       --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none \
