@@ -644,6 +644,22 @@ def run_batch_host(states, host_ops, fusion_a, fusion_b, alpha, host_out):
     return host_out
 
 
+def _bookkeep_decode(st):
+    """``_bookkeep(st, 1)`` for the softmax writer, with the local-length peak settled
+    once the window is full (the per-token path of a serving loop)."""
+    c = st._counters
+    if st.position >= WINDOW:
+        c["fusion_pointwise_calls"] += 1
+        c["fused_fine_calls"] += 1
+        st.position += 1
+        if c["peak_local_tokens"] < WINDOW:
+            local = st.position - window_start(st.position - 1)
+            if local > c["peak_local_tokens"]:
+                c["peak_local_tokens"] = local
+    else:
+        _bookkeep(st, 1)
+
+
 def _bookkeep(st, w):
     """Host-side cursor and counters after a chunk of ``w`` tokens."""
     c = st._counters
@@ -924,7 +940,9 @@ class DecodeSession:
     for graphs (``q1_history_region_graph``) the three are captured once and a step
     is one graph launch.  ``reserve`` tokens of fine-bank capacity are allocated up
     front, so the loop allocates nothing and the graph is not captured again within
-    them.  The states advance exactly as with ``tao_attention_decode_batch``.
+    them.  The states advance exactly as with ``tao_attention_decode_batch``; while a
+    session runs they advance only through it (a caller that advances one otherwise
+    calls ``reserve`` before the next ``step``, which re-derives when the banks grow).
     """
 
     def __init__(self, states, fusion_a, fusion_b, alpha, reserve=4096):
@@ -987,6 +1005,9 @@ class DecodeSession:
             self.cap[i] = st.cap_fines
         if grew:
             self.graph = None
+        # steps until some state's next seal would exceed its fine-bank capacity
+        # (sealed_at(p + 1) + 1 > cap from p = 767 + 256 (cap - 1) on)
+        self._steps_left = min(767 + FINE * (st.cap_fines - 1) - st.position for st in self.states)
 
     def _launch(self, stream):
         rc = self.lib.tao_copy_host_to_device_many(self.copy_dst, self.copy_src, self.copy_bytes, 5, stream)
@@ -1014,19 +1035,29 @@ class DecodeSession:
 
     def step(self):
         """Decode the token in ``inputs`` for every request (asynchronous)."""
-        for i, st in enumerate(self.states):
-            self.pos[i] = st.position
-            if sealed_at(st.position + 1) + 1 > st.cap_fines:
-                self.reserve(4096)
+        if self._steps_left <= 0:
+            self.reserve(4096)
+        self._steps_left -= 1
         if self.graph_mode:
-            with torch.cuda.stream(self.stream):
-                if self.graph is None:
+            if self.graph is None:
+                self._sync_positions()
+                with torch.cuda.stream(self.stream):
                     self._capture()
+            if torch.cuda.current_stream(self.dev) == self.stream:
                 self.graph.replay()
+            else:
+                with torch.cuda.stream(self.stream):
+                    self.graph.replay()
         else:
+            self._sync_positions()
             _lib.check(self._launch(self.stream.cuda_stream))
         for st in self.states:
-            _bookkeep(st, 1)
+            _bookkeep_decode(st)
+
+    def _sync_positions(self):
+        # the host cursors the C ABI validates (a captured step decides on the device)
+        for i, st in enumerate(self.states):
+            self.pos[i] = st.position
 
     def wait(self):
         """Block until the last step's ``output`` is in host memory."""

@@ -409,3 +409,38 @@ def test_decode_session_equals_decode_batch(graph):
     for a, b in zip(*sets):
         assert a.position == b.position == P + N
         assert torch.equal(a.export()["packed_fine_c"], b.export()["packed_fine_c"])
+
+
+def test_decode_session_grows_its_banks(monkeypatch):
+    """A session whose states reach their fine-bank capacity mid-loop grows the banks
+    before the step that seals past it (and captures its graph again), decoding
+    exactly like tao_attention_decode_batch."""
+    from tao_memory_b200 import stream
+    tb, preset, check_device = _tb()
+    monkeypatch.setattr(stream, "MIN_CAP", 8)
+    dev = torch.device("cuda")
+    R, H, D, P, N = 2, 2, 64, 2300, 300     # capacity 8 fines: the seal at 2559 needs a ninth
+    xs = [{k: t.to(dev) for k, t in make_inputs(1, P + N, H, D, seed=97 + r)[0].items()} for r in range(R)]
+    fa, fb = xs[0]["fusion_a"], xs[0]["fusion_b"]
+    sets = []
+    for _ in range(2):
+        states = []
+        for r in range(R):
+            st = tb.new_state(r, preset(graph=True))
+            tb.tao_attention_prefill(*(xs[r][k][:, :P] for k in KEYS[:3]), raw_q=xs[r]["raw_q"][:, :P],
+                                     raw_k=xs[r]["raw_k"][:, :P], fusion_a=fa, fusion_b=fb, alpha=0.3,
+                                     state=st, position=0)
+            states.append(st)
+        sets.append(states)
+    session = tb.DecodeSession(sets[1], fa, fb, 0.3, reserve=1)
+    caps = [st.cap_fines for st in sets[1]]
+    for t in range(P, P + N):
+        stack = torch.stack([torch.cat([xs[r][k][:, t:t + 1] for r in range(R)], 0) for k in KEYS])
+        ref, _ = tb.tao_attention_decode_batch(*stack[:3], raw_q=stack[3], raw_k=stack[4], fusion_a=fa,
+                                               fusion_b=fb, alpha=0.3, states=sets[0])
+        session.inputs.copy_(stack.cpu())
+        session.step()
+        assert torch.equal(session.wait(), ref.cpu()), f"position {t}"
+    assert all(st.cap_fines > c for st, c in zip(sets[1], caps))
+    session.check()
+    assert check_device() == 0
