@@ -72,7 +72,7 @@ namespace tao {
 // tao_window_attention).  Returns TAO_OK or a status (message recorded).
 int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* out, float* lse, int B,
                             int T, int H, int D, int* err, cudaStream_t s) {
-  const bool tc = g_attention_variant == 1 && D == tc::kTcD && aligned(q) && aligned(k) && aligned(v);
+  const bool tc = g_attention_variant == 1 && (D == 64 || D == 128) && aligned(q) && aligned(k) && aligned(v);
   if (tc) {
     CUtensorMap mq, mk, mv;
     const unsigned long long rows = (unsigned long long)B * T, cols = (unsigned long long)H * D;
@@ -80,12 +80,22 @@ int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* o
       tao_set_last_error("cuTensorMapEncodeTiled failed");
       return TAO_ERR_CUDA;
     }
-    if (!smem_attr(tc_window_attention_kernel, tc::kTcSmem)) {
-      tao_set_last_error("smem attribute");
-      return TAO_ERR_CUDA;
+    const dim3 grid((T + tc::kTcBM - 1) / tc::kTcBM, B * H);
+    if (D == 64) {
+      if (!smem_attr(tc_window_attention_kernel<64>, tc::TcAttnCfg<64>::SMEM)) {
+        tao_set_last_error("smem attribute");
+        return TAO_ERR_CUDA;
+      }
+      tc_window_attention_kernel<64><<<grid, tc::kTcThreads, tc::TcAttnCfg<64>::SMEM, s>>>(mq, mk, mv, out, lse, T, H,
+                                                                                          err);
+    } else {
+      if (!smem_attr(tc_window_attention_kernel<128>, tc::TcAttnCfg<128>::SMEM)) {
+        tao_set_last_error("smem attribute");
+        return TAO_ERR_CUDA;
+      }
+      tc_window_attention_kernel<128><<<grid, tc::kTcThreads, tc::TcAttnCfg<128>::SMEM, s>>>(mq, mk, mv, out, lse, T,
+                                                                                            H, err);
     }
-    tc_window_attention_kernel<<<dim3((T + tc::kTcBM - 1) / tc::kTcBM, B * H), tc::kTcThreads, tc::kTcSmem, s>>>(mq, mk, mv, out, lse,
-                                                                                         T, H, err);
     return TAO_OK;
   }
   WinAttnParams p{};

@@ -1,17 +1,17 @@
 // Windowed causal attention forward on the 5th-generation tensor cores (sm_100a).
 //
 // Same semantics as window_attention_kernel (tao_stream.py:760-787 through
-// flash_attention.py:16-37): query t of [B][T][H][64] bf16 operands reads keys
-// [max(0, 256*floor(t/256) - 512), t] with scale 1/8.
+// flash_attention.py:16-37): query t of [B][T][H][D] bf16 operands (D = 64 or 128)
+// reads keys [max(0, 256*floor(t/256) - 512), t] with scale 1/sqrt(D).
 //
 // One CTA (one warpgroup, 128 threads) owns 128 queries of one (batch, head):
 //   * Q, K and V tiles arrive by TMA (cp.async.bulk.tensor, 128B swizzle) into
 //     1024-byte-aligned shared memory; K and V have two stages each
-//   * S = Q K^T: tcgen05.mma kind::f16, M=128 N=128 K=64, fp32 accumulator in TMEM
+//   * S = Q K^T: tcgen05.mma kind::f16, M=128 N=128 K=D, fp32 accumulator in TMEM
 //   * each thread owns one query row: tcgen05.ld of its S row, window mask,
 //     online softmax in registers, P (bf16 pairs) written back to TMEM with
 //     tcgen05.st (shared memory bandwidth is left to the MMA operands)
-//   * O += P V: tcgen05.mma M=128 N=64 K=128, A = P read from TMEM, V an MN-major
+//   * O += P V: tcgen05.mma M=128 N=D K=128, A = P read from TMEM, V an MN-major
 //     shared-memory operand; O
 //     stays in TMEM for the whole CTA and is rescaled there only when a row
 //     maximum grows by more than 2^8 (p = 2^(s - stale max) stays <= 256)
@@ -28,11 +28,21 @@ namespace tao {
 namespace tc {
 
 constexpr int kTcBM = 128, kTcBN = 128, kTcD = 64;
-constexpr int kTcTile = kTcBM * kTcD * 2;  // 16 KB: 128 rows x 128 B
+constexpr int kTcAtom = kTcBM * 64 * 2;    // 16 KB: 128 rows x 128 B (64 channels)
+constexpr int kTcTile = kTcBM * kTcD * 2;  // one operand tile at width 64
 constexpr int kTcThreads = 160;            // warps 0-3: softmax rows, warp 4: TMA + MMA issue
-// Q, K[2], V[2] tiles, then 9 mbarriers, the TMEM address slot and the abort flag.
-constexpr int kTcSmem = 5 * kTcTile + 128;
-// TMEM columns: S fp32 0-127, O fp32 128-191, P bf16 pairs 192-255.
+// Per width: Q, K[2], V[2] tiles of D/64 atoms each, then 9 mbarriers, the TMEM
+// address slot and the abort flag; TMEM columns S fp32 0-127, O fp32 128..128+D-1,
+// P bf16 pairs after O (width 64: 256 columns, two CTAs per SM; width 128: 320 of a
+// 512-column allocation, one CTA per SM).
+template <int D>
+struct TcAttnCfg {
+  static constexpr int TILE = kTcBM * D * 2;
+  static constexpr int SMEM = 5 * TILE + 128;
+  static constexpr int TMEM_COLS = D == 64 ? 256 : 512;
+  static constexpr int CTAS = D == 64 ? 2 : 1;
+};
+constexpr int kTcSmem = TcAttnCfg<64>::SMEM;
 constexpr int kTcTmemCols = 256;
 // O is rescaled only when a row maximum grows by more than this (log2 units):
 // until then scores are exponentiated against the stale maximum (p <= 2^8).
@@ -65,11 +75,13 @@ TAO_DEVI bool warp_wait(uint64_t* bar, uint32_t phase, int* err, volatile int* a
 //   softmax (warps 0-3, one query row per thread): sfull(j) -> tcgen05.ld S row ->
 //     sfree -> mask, row max -> ofull(j-1) -> rescale the O row in TMEM if its
 //     maximum moved by more than 2^8 -> P(j) (bf16 pairs) to TMEM -> pfull.
-__global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
+template <int D>
+__global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_window_attention_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
     const __grid_constant__ CUtensorMap tv, bf16* __restrict__ out, float* __restrict__ lse, int T,
     int H, int* err) {
   using namespace tc;
+  constexpr int TILE = TcAttnCfg<D>::TILE, NA = D / 64;
   // 128B-swizzled tiles need 1024-byte alignment; the kernel uses no static
   // shared memory, so the dynamic window starts aligned (checked, never assumed).
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -78,9 +90,9 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
     return;
   }
   uint8_t* const sQ = sm;
-  uint8_t* const sK = sm + kTcTile;      // [2] stages
-  uint8_t* const sV = sm + 3 * kTcTile;  // [2] stages
-  uint64_t* const bars = reinterpret_cast<uint64_t*>(sm + 5 * kTcTile);
+  uint8_t* const sK = sm + TILE;      // [2] stages
+  uint8_t* const sV = sm + 3 * TILE;  // [2] stages
+  uint64_t* const bars = reinterpret_cast<uint64_t*>(sm + 5 * TILE);
   uint64_t* const qbar = bars;
   uint64_t* const kfull = bars + 1;  // [2]
   uint64_t* const vfull = bars + 3;  // [2]
@@ -99,11 +111,11 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
   const int kend = min(q0 + kTcBM, T);
   const int nblk = (kend - kstart + kTcBN - 1) / kTcBN;
   const int row0 = b * T;
-  const int col = h * kTcD;
+  const int col = h * D;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTcTmemCols));
+                 "r"(TcAttnCfg<D>::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
@@ -123,27 +135,31 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
   __syncthreads();
   fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t tS = tbase, tO = tbase + 128, tP = tbase + 192;
+  const uint32_t tS = tbase, tO = tbase + 128, tP = tbase + 128 + D;
 
   if (warp == 4) {
     // ================= issuer (the whole warp walks the schedule; lane 0 issues) =====
-    constexpr uint32_t IS = idesc_bf16(128, 128, 0, 0), IO = idesc_bf16(128, 64, 0, 1);
+    constexpr uint32_t IS = idesc_bf16(128, 128, 0, 0), IO = idesc_bf16(128, D, 0, 1);
     const bool leader = lane == 0;
     int k_armed[2] = {0, 0}, k_done[2] = {0, 0}, v_armed[2] = {0, 0}, v_done[2] = {0, 0};
     int s_issued = 0, o_issued = 0;
     auto load_k = [&](int j) {
       const int st = j & 1;
       if (leader) {
-        mbar_expect_tx(&kfull[st], kTcTile);
-        tma_2d(sK + st * kTcTile, &tk, col, row0 + kstart + j * kTcBN, &kfull[st]);
+        mbar_expect_tx(&kfull[st], TILE);
+#pragma unroll
+        for (int at = 0; at < NA; ++at)
+          tma_2d(sK + st * TILE + at * kTcAtom, &tk, col + 64 * at, row0 + kstart + j * kTcBN, &kfull[st]);
       }
       ++k_armed[st];
     };
     auto load_v = [&](int j) {
       const int st = j & 1;
       if (leader) {
-        mbar_expect_tx(&vfull[st], kTcTile);
-        tma_2d(sV + st * kTcTile, &tv, col, row0 + kstart + j * kTcBN, &vfull[st]);
+        mbar_expect_tx(&vfull[st], TILE);
+#pragma unroll
+        for (int at = 0; at < NA; ++at)
+          tma_2d(sV + st * TILE + at * kTcAtom, &tv, col + 64 * at, row0 + kstart + j * kTcBN, &vfull[st]);
       }
       ++v_armed[st];
     };
@@ -153,10 +169,11 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
       ++k_done[st];
       fence_after();
       if (leader) {
-        const uint32_t kaddr = smem_u32(sK + st * kTcTile), qaddr = smem_u32(sQ);
+        const uint32_t kaddr = smem_u32(sK + st * TILE), qaddr = smem_u32(sQ);
 #pragma unroll
-        for (int k = 0; k < kTcD / 16; ++k)
-          mma(tS, sdesc(qaddr + k * 32, 16, 1024), sdesc(kaddr + k * 32, 16, 1024), IS, k > 0);
+        for (int k = 0; k < D / 16; ++k)   // 64-channel atoms of 16 KB, 4 K-steps each
+          mma(tS, sdesc(qaddr + (k >> 2) * kTcAtom + (k & 3) * 32, 16, 1024),
+              sdesc(kaddr + (k >> 2) * kTcAtom + (k & 3) * 32, 16, 1024), IS, k > 0);
         commit(sfull);
       }
       __syncwarp();
@@ -164,8 +181,9 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
       return true;
     };
     if (leader) {
-      mbar_expect_tx(qbar, kTcTile);
-      tma_2d(sQ, &tq, col, row0 + q0, qbar);
+      mbar_expect_tx(qbar, TILE);
+#pragma unroll
+      for (int at = 0; at < NA; ++at) tma_2d(sQ + at * kTcAtom, &tq, col + 64 * at, row0 + q0, qbar);
     }
     for (int j = 0; j < 2 && j < nblk; ++j) {
       load_k(j);
@@ -190,10 +208,11 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
       ++v_done[st];
       fence_after();
       if (leader) {
-        const uint32_t vaddr = smem_u32(sV + st * kTcTile);
+        const uint32_t vaddr = smem_u32(sV + st * TILE);
 #pragma unroll
-        for (int k = 0; k < kTcBN / 16; ++k)  // A = P(j) from TMEM, 16 keys = 8 columns per step
-          mma_ts(tO, tP + k * 8, sdesc(vaddr + k * 2048, 8192, 1024), IO, (j > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < kTcBN / 16; ++k)  // A = P(j) from TMEM, 16 keys = 8 columns per step;
+          // V MN-major: 64-channel atoms 16 KB apart (LBO)
+          mma_ts(tO, tP + k * 8, sdesc(vaddr + k * 2048, kTcAtom, 1024), IO, (j > 0 || k > 0) ? 1u : 0u);
         commit(ofull);
       }
       __syncwarp();
@@ -215,7 +234,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
     // ================= softmax rows =================
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const int qpos = q0 + tid;
-    const float sl = 1.4426950408889634f * 0.125f;  // log2(e) / sqrt(64)
+    const float sl = 1.4426950408889634f / sqrtf((float)D);  // log2(e) / sqrt(D)
     float mu = -INFINITY;  // exponent base of P and O (scaled log2 units)
     float l = 0.f;
     bool ok = true;
@@ -269,7 +288,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
       }
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {  // after the exponentials: sc[] is dead
 #pragma unroll
-        for (int c = 0; c < kTcD / 32; ++c) {
+        for (int c = 0; c < D / 32; ++c) {
           float ov[32];
           tmem_ld32(tO + lane_off + c * 32, ov);
 #pragma unroll
@@ -284,14 +303,14 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
     // ---- epilogue: O complete -> normalise -> bf16 rows; lse in natural log
     if (ok && warp_wait(ofull, (nblk - 1) & 1, err, abort_flag)) {
       fence_after();
-      float ov[kTcD];
+      float ov[D];
 #pragma unroll
-      for (int c = 0; c < kTcD / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ov + c * 32);
+      for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ov + c * 32);
       if (qpos < T) {
         const float inv = 1.f / l;
-        bf16* orow = out + ((long long)(row0 + qpos) * H + h) * kTcD;
+        bf16* orow = out + ((long long)(row0 + qpos) * H + h) * D;
 #pragma unroll
-        for (int c8 = 0; c8 < kTcD / 8; ++c8) {
+        for (int c8 = 0; c8 < D / 8; ++c8) {
           uint32_t pk[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -309,7 +328,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, 2) tc_window_attention_kernel(
   __syncthreads();
   fence_after();
   if (warp == 0) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kTcTmemCols));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TcAttnCfg<D>::TMEM_COLS));
   }
 }
 

@@ -48,12 +48,13 @@ def test_window_attention_matches_oracle(b, t, h, d, variant):
         assert abs(torch.logsumexp(s, 0).item() - lse[0, 0, tq].item()) < 1e-2
 
 
-@pytest.mark.parametrize("b,t,h", [(1, 8192, 12), (2, 3000, 4), (1, 100, 3)])
-def test_tcgen05_matches_mma_sync(b, t, h):
-    """The tcgen05/TMEM kernel and the mma.sync kernel agree on every row: outputs to
-    one bf16 rounding (|a-b| <= 1e-2 + 1e-2|b|), log-sum-exp to 1e-3."""
+@pytest.mark.parametrize("b,t,h,d", [(1, 8192, 12, 64), (2, 3000, 4, 64), (1, 100, 3, 64), (1, 4096, 6, 128),
+                                     (2, 1000, 2, 128)])
+def test_tcgen05_matches_mma_sync(b, t, h, d):
+    """The tcgen05/TMEM kernel and the mma.sync kernel agree on every row (widths 64 and
+    128): outputs to one bf16 rounding (|a-b| <= 1e-2 + 1e-2|b|), log-sum-exp to 1e-3."""
     g = torch.Generator().manual_seed(11)
-    q, k, v = (torch.randn(b, t, h, 64, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
+    q, k, v = (torch.randn(b, t, h, d, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
     o1, l1 = _run(q, k, v, 1)
     o0, l0 = _run(q, k, v, 0)
     diff = (o1.float() - o0.float()).abs()
