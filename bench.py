@@ -86,7 +86,7 @@ def parse():
     ap.add_argument("--no-serving", action="store_true", help="leave the nested serving (config 5) leg out")
     ap.add_argument("--no-parity", action="store_true", help="leave the oracle parity check out")
     ap.add_argument("--decode-variant", type=int, default=None,
-                    help="decode kernel of tao_decode_step (0 persistent, 1 CTA/item, 2 warp/item)")
+                    help="decode kernel of tao_decode_step (tao_decode_variant: 1 default, 0, 2, 3, 4)")
     return ap.parse_args()
 
 
@@ -261,12 +261,15 @@ def run_b200(args, world, rank, local):
     torch.cuda.synchronize()
     prefill_s = time.time() - t0
 
-    # decode schedule: [lead untimed][e2e: E2E_WARM + K][warm-up W][timed K], ending at the
-    # config's last decode step (256) when it fits
+    # decode schedule: [lead untimed][e2e: E2E_WARM + K][warm-up W][kernel window K][timed K],
+    # ending at the config's last decode step (256) when it fits.  The kernel window times
+    # the fused kernel alone (events around it, for the roofline); the timed window has
+    # events around whole steps only, since every event pair recorded inside a step adds
+    # its own latency to the step (about 5 us on this GPU).
     E2E_WARM = 3                      # untimed e2e steps: graph capture, first replays
     n_e2e = E2E_WARM + K
-    lead = max(0, DECODE_STEPS - (n_e2e + W + K))
-    total_steps = lead + n_e2e + W + K
+    lead = max(0, DECODE_STEPS - (n_e2e + W + 2 * K))
+    total_steps = lead + n_e2e + W + 2 * K
     gen = torch.Generator(device=device).manual_seed(10_000 + rank)
     inputs = torch.randn(total_steps, 5, R, 1, HEADS, WIDTH, device=device, generator=gen).to(torch.bfloat16)
     outs = torch.empty(K, R, 1, HEADS, WIDTH, dtype=torch.bfloat16, device=device)
@@ -315,22 +318,37 @@ def run_b200(args, world, rank, local):
     e2e_s = e2e_s[E2E_WARM:]
     dec._sync_ptrs()
 
-    # ---- warm-up and the timed window (C ABI, inputs resident in HBM)
+    def window_bytes():
+        base = [st.position for st in states]
+        per = []
+        for i in range(K):
+            for st, p in zip(states, base):
+                st.position = p + i
+            per.append(decode_bytes(states))
+        for st, p in zip(states, base):
+            st.position = p
+        return per
+
+    # ---- warm-up, the kernel window and the timed window (C ABI, inputs resident in HBM)
     for i in range(W):
         dec.step(*step_ptrs(lead + n_e2e + i), scratch_out.data_ptr())
     torch.cuda.synchronize()
     dec.check()
-    exported = [st.export() for st in states] if (rank == 0 and not args.no_parity) else None
+    kern0 = lead + n_e2e + W
+    algo_bytes = window_bytes()
     ev = Events(lib, 4 * K)
-    base_pos = [st.position for st in states]
-    algo_bytes = []
+    torch.cuda.synchronize()
     for i in range(K):
-        for st, p in zip(states, base_pos):
-            st.position = p + i
-        algo_bytes.append(decode_bytes(states))
-    for st, p in zip(states, base_pos):
-        st.position = p
-    timed0 = lead + n_e2e + W
+        flush_l2()
+        lib.tao_stream_profile_next(ev[4 * i + 2], ev[4 * i + 3])
+        dec.step(*step_ptrs(kern0 + i), scratch_out.data_ptr())
+    torch.cuda.synchronize()
+    dec.check()
+    main_ms = [ev.elapsed(4 * i + 2, 4 * i + 3) for i in range(K)]
+    kernel_positions = [states[0].position - K, states[0].position - 1]
+    exported = [st.export() for st in states] if (rank == 0 and not args.no_parity) else None
+    timed0 = kern0 + K
+    timed_bytes = window_bytes()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -338,7 +356,6 @@ def run_b200(args, world, rank, local):
     for i in range(K):
         flush_l2()                        # evict L2 (outside the timed window)
         lib.tao_event_record(ev[4 * i], stream)
-        lib.tao_stream_profile_next(ev[4 * i + 2], ev[4 * i + 3])
         dec.step(*step_ptrs(timed0 + i), outs[i].data_ptr())
         gather.start(outs[i])            # side stream; overlaps the next step
         lib.tao_event_record(ev[4 * i + 1], stream)
@@ -350,10 +367,9 @@ def run_b200(args, world, rank, local):
     dec.check()
     clocks.stop()
     step_ms = [ev.elapsed(4 * i, 4 * i + 1) for i in range(K)]
-    main_ms = [ev.elapsed(4 * i + 2, 4 * i + 3) for i in range(K)]
     ev.close()
     cfg = states[0].config
-    p0 = base_pos[0]
+    p0 = states[0].position - K
     gpu_launches = sum(1 + any(is_refresh(p0 + i, st.layer_index, cfg) for st in states)
                        + any(p0 + i + 1 - window_start(p0 + i) == 768 for st in states) for i in range(K))
     seals = sum(p0 + i + 1 - window_start(p0 + i) == 768 for i in range(K))
@@ -399,6 +415,12 @@ def run_b200(args, world, rank, local):
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind + " (copy bandwidth)",
                      "algorithmic_bytes_per_launch": int(statistics.mean(algo_bytes)),
                      "kernel_ms_mean": round(statistics.mean(main_ms), 5),
+                     "kernel_timing": "CUDA events around the fused kernel on its stream, L2 flushed "
+                                      "before each launch, over the K steps just before the timed "
+                                      "window (positions %d-%d), step bytes %.1f MB there and %.1f MB "
+                                      "in the timed window" % (kernel_positions[0], kernel_positions[1],
+                                                               statistics.mean(algo_bytes) / 1e6,
+                                                               statistics.mean(timed_bytes) / 1e6),
                      "traffic": DECODE_TRAFFIC_BYTES},
         "gpu_launches": gpu_launches,
         "clocks": clocks.summary(),
@@ -497,8 +519,11 @@ def run_serving(args, world, rank, local):
     from tao_memory_b200 import StreamCache
     from tao_memory_b200.presets import index_only_page_memo
     from tao_memory_b200.shard import plan_imbalance, plan_lpt
+    from tao_memory_b200 import _lib
     from tao_memory_b200.stream import decode_bytes
     device = torch.device("cuda", local)
+    if args.decode_variant is not None:
+        _lib.check(_lib.lib().tao_decode_variant(args.decode_variant))
     lengths = serving_lengths()[:args.serving_requests or SV_REQUESTS]
     n_req = len(lengths)
     plan = plan_lpt(lengths, SV_HEADS, SV_WIDTH, world)
