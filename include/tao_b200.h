@@ -34,6 +34,7 @@ extern "C" {
 #define TAO_ERR_CAPACITY 4   /* fine bank or route capacity too small              */
 #define TAO_ERR_CUDA 5       /* CUDA launch / runtime error                        */
 #define TAO_ERR_DEVICE 6     /* a kernel reported an error (bounded wait expired)  */
+#define TAO_ERR_TIMEOUT 7    /* a host wait (tao_host_wait) expired                */
 
 /* Geometry of the preset (TaoConfig, config.py:7-19).  fine_tokens, local_keep and
  * coarse_group must be 256, 512 and 8; the schedule fields are free.  route_cap is
@@ -147,6 +148,42 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
                     const void* raw_q, const void* raw_k, const void* fusion_a,
                     const void* fusion_b, float alpha, void* out, void* workspace,
                     size_t workspace_bytes, void* stream);
+
+/* tao_decode_step for a caller whose operands arrive in, and whose result leaves
+ * through, page-locked host memory:
+ *   host_in   : page-locked [5][n_states][1][H][D] bf16 (q, k, v, raw_q, raw_k)
+ *   stage     : device [5][n_states][1][H][D] bf16 (the operands' device copy)
+ *   host_out  : page-locked [n_states][1][H][D] bf16
+ *   host_done : page-locked int32 completion word, or NULL
+ * Host buffers need a device mapping (see tao_host_device_pointer); operands, stage
+ * and output 16-byte aligned.  The step's routing kernel is always launched: it
+ * first copies host_in to stage over the host link (and reads raw_q from host memory
+ * itself), and the fused kernel writes each (request, head)'s output row straight
+ * into host_out.  With host_done, once every row of the step is in host memory the
+ * fused kernel stores the step's sequence number there: the count of steps with a
+ * completion word run on this workspace (1 for the first), so a host thread can
+ * wait for the result with tao_host_wait instead of synchronising the stream (a
+ * seal kernel may still run after it, in stream order).  A completion word needs
+ * decode variant 1, 3 or 4.  Results are those of tao_copy_host_to_device_many +
+ * tao_decode_step + tao_copy_device_to_host, with two kernels fewer per step.  The
+ * coarse value branch is refused (TAO_ERR_ARG).  No counterpart in the reference. */
+int tao_decode_step_host(void* const* states, int n_states, const int64_t* host_pos,
+                         const int32_t* host_layer, const int32_t* host_cap, const TaoPolicy* policy,
+                         int heads, int width, const void* host_in, void* stage, void* host_out,
+                         void* host_done, const void* fusion_a, const void* fusion_b, float alpha,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* The device address of page-locked host memory (*device), or TAO_ERR_ARG when
+ * `host` is not page-locked memory with a device mapping. */
+int tao_host_device_pointer(const void* host, void** device);
+
+/* Spin (without the Python interpreter's lock, for ctypes callers) until the int32 at
+ * `word` (page-locked host memory written by a kernel) reaches `value` (wrap-around
+ * order: word - value >= 0), or `timeout_us` microseconds pass (TAO_ERR_TIMEOUT). */
+int tao_host_wait(const void* word, int value, long long timeout_us);
+
+/* cudaGraphLaunch of an instantiated graph (cudaGraphExec_t) on `stream`. */
+int tao_graph_launch(void* graph_exec, void* stream);
 
 /* Select the decode kernel of tao_decode_step for this process: 1 = persistent fused
  * kernel with one 32 KB copy stage per CTA (default), 3 = the same with two 32 KB

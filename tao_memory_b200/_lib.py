@@ -11,7 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libtao_b200.so")
 
 TAO_OK, TAO_ERR_ARG, TAO_ERR_POSITION, TAO_ERR_SEAL = 0, 1, 2, 3
-TAO_ERR_CAPACITY, TAO_ERR_CUDA, TAO_ERR_DEVICE = 4, 5, 6
+TAO_ERR_CAPACITY, TAO_ERR_CUDA, TAO_ERR_DEVICE, TAO_ERR_TIMEOUT = 4, 5, 6, 7
 
 
 class TaoPolicy(ctypes.Structure):
@@ -67,6 +67,12 @@ _SIGNATURES = {
     "tao_ring_scatter": (_I, [_VP, _I, _I, _I64, _I, _VP, _VP]),
     "tao_state_rebuild_memo": (_I, [_VP, _I, _I, _I, _VP]),
     "tao_state_refresh_page_weights": (_I, [_VP, _I, _I, _I, _VP]),
+    "tao_decode_step_host": (_I, [_VP, _I, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_int32),
+                                  ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(TaoPolicy), _I, _I,
+                                  _VP, _VP, _VP, _VP, _VP, _VP, _F, _VP, _SZ, _VP]),
+    "tao_host_device_pointer": (_I, [_VP, ctypes.POINTER(_VP)]),
+    "tao_host_wait": (_I, [_VP, _I, ctypes.c_longlong]),
+    "tao_graph_launch": (_I, [_VP, _VP]),
     "tao_copy_host_to_device": (_I, [_VP, _VP, _SZ, _VP]),
     "tao_copy_device_to_host": (_I, [_VP, _VP, _SZ, _VP]),
     "tao_copy_host_to_device_many": (_I, [ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.POINTER(_SZ), _I,

@@ -259,14 +259,33 @@ int launch_fused(const tao::FusedArgs& f, int sms, int dev, cudaStream_t s) {
   return TAO_OK;
 }
 
+// Operands of a host-staged decode step (tao_decode_step_host): the route kernel copies
+// `vecs` 16-byte vectors from page-locked host memory `in` to the device stage and reads
+// raw_q from host memory itself.
+struct HostStage {
+  const uint4* in;
+  uint4* stage;
+  int vecs;
+  const tao::bf16* raw_q;
+  int* host_done;  // device address of the page-locked completion word (or null)
+};
+
 template <int D>
-int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaStream_t s) {
+int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaStream_t s,
+                  const HostStage* hs = nullptr) {
   using namespace tao;
   int rc;
-  if (refresh) {
+  if (refresh || hs) {  // a host-staged step always launches it: it brings the operands in
+    StepArgs ar = a;
+    if (hs) {
+      ar.h_in = hs->in;
+      ar.h_stage = hs->stage;
+      ar.h_vecs = hs->vecs;
+      ar.raw_q = hs->raw_q;
+    }
     const size_t smem = (size_t)D * 4 + (size_t)a.pmax * 4 + (size_t)(8 * a.pmax + 8) * 8 + (size_t)a.pmax * 8;
     if ((rc = set_smem(decode_route_kernel<D>, smem))) return rc;
-    decode_route_kernel<D><<<a.R * a.H, 1024, smem, s>>>(a);
+    decode_route_kernel<D><<<a.R * a.H, 1024, smem, s>>>(ar);
     if ((rc = check_launch("decode_route_kernel"))) return rc;
   }
   FusedArgs f{};
@@ -315,16 +334,19 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
 
 }  // namespace
 
-extern "C" {
+namespace {
 
-int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
-                    const int32_t* host_layer, const int32_t* host_cap, const TaoPolicy* policy,
-                    int heads, int width, const void* q, const void* k, const void* v,
-                    const void* raw_q, const void* raw_k, const void* fusion_a,
-                    const void* fusion_b, float alpha, void* out, void* workspace,
-                    size_t workspace_bytes, void* stream) {
+int decode_step_impl(void* const* states, int n_states, const int64_t* host_pos, const int32_t* host_layer,
+                     const int32_t* host_cap, const TaoPolicy* policy, int heads, int width, const void* q,
+                     const void* k, const void* v, const void* raw_q, const void* raw_k, const void* fusion_a,
+                     const void* fusion_b, float alpha, void* out, void* workspace, size_t workspace_bytes,
+                     void* stream, const HostStage* hs) {
   if (!states || n_states <= 0 || !host_pos || !host_cap || !host_layer || !policy)
     return fail(TAO_ERR_ARG, "null state, cursor, layer, capacity or policy array");
+  if (policy->coarse && hs)
+    return fail(TAO_ERR_ARG, "the coarse value branch decodes through tao_decode_step (device operands)");
+  if (hs && hs->host_done && (g_decode_variant == 0 || g_decode_variant == 2))
+    return fail(TAO_ERR_ARG, "a completion word needs the fused decode kernel (variant 1, 3 or 4)");
   if (policy->coarse)   // the coarse value branch decodes through the stream-step kernels
     return tao_stream_step(states, n_states, host_pos, host_cap, policy, 1, heads, width, q, k, v, raw_q, raw_k,
                            fusion_a, fusion_b, alpha, out, workspace, workspace_bytes, stream);
@@ -396,9 +418,54 @@ int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
   a.fine_part = reinterpret_cast<float*>(ws + L.fine_part);
   a.pmax = pmax;
   a.feature = policy->fine_read;
+  if (hs && hs->host_done) {
+    a.done = reinterpret_cast<int*>(ws + L.err) + 4;  // inside the error word's 256-byte block
+    a.host_done = hs->host_done;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (g_graph_mode) refresh = seal = true;
-  return width == 64 ? launch_decode<64>(a, ms, refresh, seal, s) : launch_decode<128>(a, ms, refresh, seal, s);
+  return width == 64 ? launch_decode<64>(a, ms, refresh, seal, s, hs) : launch_decode<128>(a, ms, refresh, seal, s, hs);
+}
+
+}  // namespace
+
+extern "C" {
+
+int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
+                    const int32_t* host_layer, const int32_t* host_cap, const TaoPolicy* policy,
+                    int heads, int width, const void* q, const void* k, const void* v,
+                    const void* raw_q, const void* raw_k, const void* fusion_a,
+                    const void* fusion_b, float alpha, void* out, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  return decode_step_impl(states, n_states, host_pos, host_layer, host_cap, policy, heads, width, q, k, v, raw_q,
+                          raw_k, fusion_a, fusion_b, alpha, out, workspace, workspace_bytes, stream, nullptr);
+}
+
+int tao_decode_step_host(void* const* states, int n_states, const int64_t* host_pos, const int32_t* host_layer,
+                         const int32_t* host_cap, const TaoPolicy* policy, int heads, int width,
+                         const void* host_in, void* stage, void* host_out, void* host_done,
+                         const void* fusion_a, const void* fusion_b, float alpha, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (!host_in || !stage || !host_out) return fail(TAO_ERR_ARG, "null host operand, stage or host output");
+  if (n_states <= 0 || heads <= 0 || (width != 64 && width != 128))
+    return fail(TAO_ERR_ARG, "invalid request count, heads or width");
+  void* in_dev = nullptr;
+  void* out_dev = nullptr;
+  void* done_dev = nullptr;
+  int rc;
+  if ((rc = tao_host_device_pointer(host_in, &in_dev))) return rc;
+  if ((rc = tao_host_device_pointer(host_out, &out_dev))) return rc;
+  if (host_done && (rc = tao_host_device_pointer(host_done, &done_dev))) return rc;
+  if (reinterpret_cast<uintptr_t>(done_dev) & 3) return fail(TAO_ERR_ARG, "completion word must be 4-byte aligned");
+  const size_t row = (size_t)n_states * heads * width;  // elements of one operand
+  if (!aligned16(in_dev) || !aligned16(stage) || !aligned16(out_dev))
+    return fail(TAO_ERR_ARG, "host operands, stage and host output must be 16-byte aligned");
+  const tao::bf16* st = static_cast<const tao::bf16*>(stage);
+  HostStage hs{static_cast<const uint4*>(in_dev), static_cast<uint4*>(stage), (int)(5 * row * 2 / 16),
+               static_cast<const tao::bf16*>(in_dev) + 3 * row, static_cast<int*>(done_dev)};
+  return decode_step_impl(states, n_states, host_pos, host_layer, host_cap, policy, heads, width, st, st + row,
+                          st + 2 * row, st + 3 * row, st + 4 * row, fusion_a, fusion_b, alpha, out_dev, workspace,
+                          workspace_bytes, stream, &hs);
 }
 
 int tao_decode_graph_mode(int on) {

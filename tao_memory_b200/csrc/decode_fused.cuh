@@ -515,6 +515,19 @@ __global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
       }
       a.out[src + d] = tobf(outv);
     }
+    if (a.host_done) {  // host-staged step: publish it once every row is in host memory
+      __syncthreads();  // this CTA's row is written (the fence below is cumulative)
+      if (tid == 0) {
+        __threadfence_system();
+        if (atomicAdd(a.done, 1) == a.R * a.H - 1) {
+          __threadfence_system();
+          a.done[0] = 0;
+          const int seq = a.done[1] + 1;
+          a.done[1] = seq;
+          *reinterpret_cast<volatile int*>(a.host_done) = seq;
+        }
+      }
+    }
     if (tid == kArriver && arrived == a.H - 1) {  // the request's last head: advance its cursor
       fence_acquire();
       st.arrive = 0;
@@ -1168,6 +1181,11 @@ template <int D>
 // 1024 threads: the page and candidate loops are latency chains of row loads (cold
 // after other work evicted them), so more warps cut the serial iterations per warp.
 __global__ void __launch_bounds__(1024) decode_route_kernel(StepArgs a) {
+  // host-staged step: bring the step's operands in first (one vector per thread,
+  // spread over the CTAs); this launch reads raw_q from host memory itself
+  for (long long g = (long long)threadIdx.x * gridDim.x + blockIdx.x; g < a.h_vecs;
+       g += (long long)gridDim.x * blockDim.x)
+    a.h_stage[g] = a.h_in[g];
   const int r = blockIdx.x / a.H, h = blockIdx.x % a.H;
   TaoState& st = *a.states[r];
   const long long t = st.position;

@@ -16,6 +16,9 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <immintrin.h>
+
+#include <chrono>
 #include <cstdint>
 #include <mutex>
 
@@ -144,6 +147,55 @@ int check_args(const void* a, const void* b, size_t bytes) {
 }
 
 }  // namespace
+
+extern "C" int tao_host_device_pointer(const void* host, void** device) {
+  if (!host || !device) {
+    tao_set_last_error("null host buffer or result pointer");
+    return TAO_ERR_ARG;
+  }
+  const char* why = nullptr;
+  const void* p = mapped_host(host, &why);
+  if (!p) {
+    tao_set_last_error(why);
+    return TAO_ERR_ARG;
+  }
+  *device = const_cast<void*>(p);
+  return TAO_OK;
+}
+
+extern "C" int tao_host_wait(const void* word, int value, long long timeout_us) {
+  if (!word) {
+    tao_set_last_error("null completion word");
+    return TAO_ERR_ARG;
+  }
+  const volatile int* p = static_cast<const volatile int*>(word);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    for (int i = 0; i < 64; ++i) {
+      if ((int)((unsigned)*p - (unsigned)value) >= 0) return TAO_OK;
+      _mm_pause();
+    }
+    if (std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count() >
+        timeout_us) {
+      tao_set_last_error("host wait for a completion word expired");
+      return TAO_ERR_TIMEOUT;
+    }
+  }
+}
+
+extern "C" int tao_graph_launch(void* graph_exec, void* stream) {
+  if (!graph_exec) {
+    tao_set_last_error("null graph");
+    return TAO_ERR_ARG;
+  }
+  cudaError_t e = cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    tao_set_last_error(cudaGetErrorString(e));
+    return TAO_ERR_CUDA;
+  }
+  return TAO_OK;
+}
 
 extern "C" int tao_copy_host_to_device(void* dst, const void* host_src, size_t bytes, void* stream) {
   int rc = check_args(dst, host_src, bytes);

@@ -47,6 +47,16 @@ struct StepArgs {
   int feature;          // 1: feature-mass read of the selected fines (TaoPolicy.fine_read)
   int coarse;           // 1: coarse value branch (TaoPolicy.coarse)
   bf16* coarse_out;     // coarse branch: [R][w][H][D] coarse read of the chunk's queries
+  // host-staged decode (tao_decode_step_host): the route kernel first copies h_vecs
+  // 16-byte vectors of the step's operands from page-locked host memory into the stage
+  const uint4* h_in;
+  uint4* h_stage;
+  int h_vecs;
+  // completion word of a host-staged step (null: none): once every output row of the
+  // step is in host memory the fused kernel stores the step's sequence number (kept in
+  // done[1]; done[0] counts the (request, head) rows finished) into *host_done
+  int* done;
+  int* host_done;
 };
 
 // Position-derived plan of one chunk (constant history inside a chunk).

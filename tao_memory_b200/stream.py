@@ -936,9 +936,11 @@ class DecodeSession:
     ``inputs``: page-locked [5, R, 1, H, D] bf16 (q, k, v, raw_q, raw_k of the next
     token of every request), filled by the caller before each ``step()``;
     ``output``: page-locked [R, 1, H, D] bf16, valid after ``wait()``.  ``step()``
-    launches the copy in, the decode step and the copy out; with states configured
-    for graphs (``q1_history_region_graph``) the three are captured once and a step
-    is one graph launch.  ``reserve`` tokens of fine-bank capacity are allocated up
+    launches the decode step through ``tao_decode_step_host``: its routing launch
+    brings the operands in over the host link and the fused kernel writes the output
+    rows, then a completion word, into page-locked memory; with states configured
+    for graphs (``q1_history_region_graph``) the step is captured once and a step is
+    one graph launch, and ``wait()`` spins on the completion word.  ``reserve`` tokens of fine-bank capacity are allocated up
     front, so the loop allocates nothing and the graph is not captured again within
     them.  The states advance exactly as with ``tao_attention_decode_batch``; while a
     session runs they advance only through it (a caller that advances one otherwise
@@ -974,7 +976,11 @@ class DecodeSession:
             shape = (self.r, 1, self.heads, self.width)
             self.inputs = torch.zeros((5,) + shape, dtype=_BF16).pin_memory()
             self.output = torch.zeros(shape, dtype=_BF16).pin_memory()
-            self.stage = torch.zeros((6,) + shape, dtype=_BF16, device=self.dev)
+            self.stage = torch.zeros((5,) + shape, dtype=_BF16, device=self.dev)
+            self.done = torch.zeros(1, dtype=torch.int32).pin_memory()   # completion word
+            self._done_ptr = ctypes.c_void_p(self.done.data_ptr())
+            self.seq = 0                                                 # steps launched
+            self._stream_ptr = ctypes.c_void_p(self.stream.cuda_stream)
             self.policy = policy_for(st0.config)
             self.layers = (ctypes.c_int32 * self.r)(*[st.layer_index for st in self.states])
             self.pos = (ctypes.c_int64 * self.r)()
@@ -983,10 +989,6 @@ class DecodeSession:
                                                          ctypes.byref(self.policy))
             self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.dev)
             _graph_workspaces(self.dev).add(self.ws)
-            nb = self.stage[0].numel() * 2
-            self.copy_dst = (ctypes.c_void_p * 5)(*[self.stage[i].data_ptr() for i in range(5)])
-            self.copy_src = (ctypes.c_void_p * 5)(*[self.inputs[i].data_ptr() for i in range(5)])
-            self.copy_bytes = (ctypes.c_size_t * 5)(*([nb] * 5))
             self.graph = None
             self.reserve(reserve)
 
@@ -1010,17 +1012,15 @@ class DecodeSession:
         self._steps_left = min(767 + FINE * (st.cap_fines - 1) - st.position for st in self.states)
 
     def _launch(self, stream):
-        rc = self.lib.tao_copy_host_to_device_many(self.copy_dst, self.copy_src, self.copy_bytes, 5, stream)
-        if rc == 0:
-            rc = self.lib.tao_decode_step(self.ptrs.data_ptr(), self.r, self.pos, self.layers, self.cap,
-                                          ctypes.byref(self.policy), self.heads, self.width,
-                                          *(self.stage[i].data_ptr() for i in range(5)), self.fa.data_ptr(),
-                                          self.fb.data_ptr(), self.alpha, self.stage[5].data_ptr(),
-                                          self.ws.data_ptr(), self.ws.numel(), stream)
-        if rc == 0:
-            rc = self.lib.tao_copy_device_to_host(self.output.data_ptr(), self.stage[5].data_ptr(),
-                                                  self.output.numel() * 2, stream)
-        return rc
+        # one routing launch that also brings the operands in over the host link, the
+        # fused kernel writing the outputs straight into the page-locked output and
+        # then the step's sequence number into the completion word
+        return self.lib.tao_decode_step_host(self.ptrs.data_ptr(), self.r, self.pos, self.layers, self.cap,
+                                             ctypes.byref(self.policy), self.heads, self.width,
+                                             self.inputs.data_ptr(), self.stage.data_ptr(),
+                                             self.output.data_ptr(), self.done.data_ptr(), self.fa.data_ptr(),
+                                             self.fb.data_ptr(), self.alpha, self.ws.data_ptr(), self.ws.numel(),
+                                             stream)
 
     def _capture(self):
         self.graph = torch.cuda.CUDAGraph()
@@ -1032,25 +1032,23 @@ class DecodeSession:
         finally:
             self.lib.tao_decode_graph_mode(0)
         _lib.check(rc)
+        self._exec = ctypes.c_void_p(self.graph.raw_cuda_graph_exec())
 
     def step(self):
         """Decode the token in ``inputs`` for every request (asynchronous)."""
         if self._steps_left <= 0:
             self.reserve(4096)
-        self._steps_left -= 1
         if self.graph_mode:
             if self.graph is None:
                 self._sync_positions()
                 with torch.cuda.stream(self.stream):
                     self._capture()
-            if torch.cuda.current_stream(self.dev) == self.stream:
-                self.graph.replay()
-            else:
-                with torch.cuda.stream(self.stream):
-                    self.graph.replay()
+            _lib.check(self.lib.tao_graph_launch(self._exec, self._stream_ptr))
         else:
             self._sync_positions()
-            _lib.check(self._launch(self.stream.cuda_stream))
+            _lib.check(self._launch(self._stream_ptr))
+        self._steps_left -= 1
+        self.seq += 1
         for st in self.states:
             _bookkeep_decode(st)
 
@@ -1060,8 +1058,16 @@ class DecodeSession:
             self.pos[i] = st.position
 
     def wait(self):
-        """Block until the last step's ``output`` is in host memory."""
-        self.stream.synchronize()
+        """Block until the last step's ``output`` is in host memory.
+
+        The host thread spins on the completion word the fused kernel writes after the
+        step's last output row; the step's seal kernel (when a window fills) may still
+        be running, in order on the session's stream, when this returns.  On a device
+        error (no completion) the stream is synchronised and the error raised."""
+        if self.lib.tao_host_wait(self._done_ptr, self.seq, 5_000_000) != 0:
+            self.stream.synchronize()
+            self.check()
+            _lib.check(self.lib.tao_host_wait(self._done_ptr, self.seq, 0))
         return self.output
 
     def check(self):

@@ -81,6 +81,29 @@ def test_host_transfer_argument_checks_without_gpu():
     assert lib.tao_copy_device_to_host(16, 32, 40, None) == _lib.TAO_ERR_ARG
     assert lib.tao_copy_host_to_device(None, 32, 64, None) == _lib.TAO_ERR_ARG
     assert b"16-byte" in lib.tao_last_error() or b"null" in lib.tao_last_error()
+    # the host-staged decode step refuses missing buffers before any CUDA call
+    pos = (ctypes.c_int64 * 1)(1000)
+    one = (ctypes.c_int32 * 1)(64)
+    pol = _lib.TaoPolicy()
+    assert lib.tao_decode_step_host(None, 1, pos, one, one, ctypes.byref(pol), 2, 64, None, None, None,
+                                    None, None, None, 0.5, None, 0, None) == _lib.TAO_ERR_ARG
+    assert b"null" in lib.tao_last_error()
+    dev = ctypes.c_void_p()
+    assert lib.tao_host_device_pointer(None, ctypes.byref(dev)) == _lib.TAO_ERR_ARG
+
+
+def test_host_wait_on_a_completion_word():
+    """tao_host_wait returns once the word has reached the value (wrap-around order)
+    and reports a timeout otherwise."""
+    lib = _lib.lib()
+    word = ctypes.c_int32(7)
+    assert lib.tao_host_wait(ctypes.addressof(word), 7, 0) == _lib.TAO_OK
+    assert lib.tao_host_wait(ctypes.addressof(word), 5, 0) == _lib.TAO_OK
+    assert lib.tao_host_wait(ctypes.addressof(word), 8, 2000) == _lib.TAO_ERR_TIMEOUT
+    word.value = -2147483648          # one past INT_MAX: later than it in wrap-around order
+    assert lib.tao_host_wait(ctypes.addressof(word), 2147483647, 0) == _lib.TAO_OK
+    assert lib.tao_host_wait(None, 1, 0) == _lib.TAO_ERR_ARG
+    assert lib.tao_graph_launch(None, None) == _lib.TAO_ERR_ARG
 
 
 def test_schedule_matches_reference_policy():

@@ -375,13 +375,16 @@ def test_host_transfers_by_the_sms():
 
 
 @pytest.mark.parametrize("graph", [False, True])
-def test_decode_session_equals_decode_batch(graph):
-    """DecodeSession (operands and results in page-locked host memory; one graph
-    launch per step for graph-configured states) decodes exactly like
-    tao_attention_decode_batch, across route refreshes and a seal."""
+@pytest.mark.parametrize("width", [64, 128])
+def test_decode_session_equals_decode_batch(graph, width):
+    """DecodeSession (operands and results in page-locked host memory, brought in by
+    the routing launch and written back by the fused kernel, completion signalled by a
+    word in host memory; one graph launch per step for graph-configured states)
+    decodes exactly like tao_attention_decode_batch, across route refreshes and a
+    seal."""
     tb, preset, check_device = _tb()
     dev = torch.device("cuda")
-    R, H, D, P, N = 3, 2, 64, 1000, 40
+    R, H, D, P, N = 3, 2, width, 1000, 40
     xs = [{k: t.to(dev) for k, t in make_inputs(1, P + N, H, D, seed=95 + r)[0].items()} for r in range(R)]
     fa, fb = xs[0]["fusion_a"], xs[0]["fusion_b"]
     sets = []
@@ -404,6 +407,7 @@ def test_decode_session_equals_decode_batch(graph):
         got = session.wait()
         assert torch.equal(got, ref.cpu()), f"position {t}"
     assert (session.graph is not None) == graph
+    assert int(session.done[0]) == session.seq == N
     session.check()
     assert check_device() == 0
     for a, b in zip(*sets):
