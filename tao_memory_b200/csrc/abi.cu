@@ -237,11 +237,58 @@ int device_sm_count(int dev) {
 
 // Persistent fused decode kernel with NS stages per CTA: as many CTAs as are resident
 // at once, each walking the same number of items (give or take one) by the grid stride.
+// Slot-major item tables of the fused kernel from each request's bound on its selected
+// fines (mb[r]): a request gets KB local items and ceil(mb[r] / FPC) fine items per
+// head, so short requests in a mixed batch launch no empty fine items.  Past the
+// tables' limits (or without bounds) every request gets KB + ms items (nslots = 0).
+template <int D, int IB>
+void fused_tables(tao::FusedArgs& f, const int* mb) {
+  using Cfg = tao::FusedCfg<D, IB>;
+  const int R = f.s.R, H = f.s.H;
+  f.nslots = 0;
+  if (!mb || R > tao::kFusedMaxReq) return;
+  int per[tao::kFusedMaxReq], order[tao::kFusedMaxReq];
+  int most = 0;
+  for (int r = 0; r < R; ++r) {
+    int fi = (mb[r] + Cfg::FPC - 1) / Cfg::FPC;
+    if (fi > f.ms) fi = f.ms;  // within the partial buffers' stride
+    per[r] = Cfg::KB + fi;
+    if (per[r] > most) most = per[r];
+    order[r] = r;
+  }
+  if (most > tao::kFusedMaxSlots) return;
+  bool uniform = true;  // every request at the full count: the plain item order
+  for (int r = 0; r < R; ++r) uniform = uniform && per[r] == Cfg::KB + f.ms;
+  if (uniform) return;
+  for (int i = 1; i < R; ++i) {  // stable: most items first
+    const int x = order[i];
+    int j = i;
+    while (j > 0 && per[order[j - 1]] < per[x]) {
+      order[j] = order[j - 1];
+      --j;
+    }
+    order[j] = x;
+  }
+  int base = 0, active = R;
+  for (int sl = 0; sl < most; ++sl) {
+    while (active > 0 && per[order[active - 1]] <= sl) --active;
+    f.slot_base[sl] = base;
+    base += active * H;
+  }
+  f.slot_base[most] = base;
+  for (int r = 0; r < R; ++r) {
+    f.rorder[r] = (int16_t)order[r];
+    f.per_r[r] = (int16_t)per[r];
+  }
+  f.nslots = most;
+}
+
 template <int D, int NS, int IB>
-int launch_fused(const tao::FusedArgs& f, int sms, int dev, cudaStream_t s) {
+int launch_fused(tao::FusedArgs f, int sms, int dev, cudaStream_t s, const int* mb) {
   using namespace tao;
   const size_t smem = (size_t)NS * FusedCfg<D, IB>::STAGE;
-  const int total = f.s.R * f.s.H * (FusedCfg<D, IB>::KB + f.ms);
+  fused_tables<D, IB>(f, mb);
+  const int total = f.nslots ? f.slot_base[f.nslots] : f.s.R * f.s.H * (FusedCfg<D, IB>::KB + f.ms);
   int rc;
   if ((rc = set_smem(decode_fused_kernel<D, NS, IB>, smem))) return rc;
   // resident CTAs per SM: one occupancy query per (device, width, stages), kept for the process
@@ -272,7 +319,7 @@ struct HostStage {
 
 template <int D>
 int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaStream_t s,
-                  const HostStage* hs = nullptr) {
+                  const HostStage* hs = nullptr, const int* mb = nullptr) {
   using namespace tao;
   int rc;
   if (refresh || hs) {  // a host-staged step always launches it: it brings the operands in
@@ -311,14 +358,14 @@ int launch_decode(const tao::StepArgs& a, int ms, bool refresh, bool seal, cudaS
     if (grid < need) grid = need;
     decode_ws_kernel<D><<<grid, 288, smem, s>>>(f);
   } else if (g_decode_variant == 3) {
-    if ((rc = launch_fused<D, 2, 32768>(f, sms, dev, s))) return rc;   // two 32 KB stages per CTA
+    if ((rc = launch_fused<D, 2, 32768>(f, sms, dev, s, mb))) return rc;   // two 32 KB stages per CTA
   } else if (D == 64 && g_decode_variant == 4) {
     // two 16 KB stages per CTA: items of 64 keys or 2 fines
     if constexpr (D == 64) {
-      if ((rc = launch_fused<D, 2, 16384>(f, sms, dev, s))) return rc;
+      if ((rc = launch_fused<D, 2, 16384>(f, sms, dev, s, mb))) return rc;
     }
   } else {
-    if ((rc = launch_fused<D, 1, 32768>(f, sms, dev, s))) return rc;   // one 32 KB stage per CTA
+    if ((rc = launch_fused<D, 1, 32768>(f, sms, dev, s, mb))) return rc;   // one 32 KB stage per CTA
   }
   if (prof1) cudaEventRecord(prof1, s);
   if ((rc = check_launch("decode_fused_kernel"))) return rc;
@@ -368,6 +415,10 @@ int decode_step_impl(void* const* states, int n_states, const int64_t* host_pos,
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(TAO_ERR_ARG, "workspace must be 256-byte aligned");
   int pmax = 1, mbound = 1;
   bool refresh = false, seal = false;
+  // per-request bound on the selected fines the fused kernel reads: the budget of the
+  // fines sealed now (routes refreshed this step or earlier never select more); a
+  // step that may be captured and replayed at later positions bounds by capacity
+  int mb_req[tao::kFusedMaxReq];
   for (int r = 0; r < n_states; ++r) {
     const long long pos = host_pos[r];
     if (pos < 0) return fail(TAO_ERR_POSITION, "negative position");
@@ -383,6 +434,10 @@ int decode_step_impl(void* const* states, int n_states, const int64_t* host_pos,
     if (cap / 8 + 1 > pmax) pmax = cap / 8 + 1;
     const int mb = h_budget(cap, *policy);
     if (mb > mbound) mbound = mb;
+    if (r < tao::kFusedMaxReq) {
+      const int m = g_graph_mode ? mb : h_budget(S, *policy);
+      mb_req[r] = m < policy->route_cap ? m : policy->route_cap;
+    }
   }
   const int route_cap = policy->route_cap;
   if (mbound > route_cap) mbound = route_cap;
@@ -424,7 +479,9 @@ int decode_step_impl(void* const* states, int n_states, const int64_t* host_pos,
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (g_graph_mode) refresh = seal = true;
-  return width == 64 ? launch_decode<64>(a, ms, refresh, seal, s, hs) : launch_decode<128>(a, ms, refresh, seal, s, hs);
+  const int* mbp = n_states <= tao::kFusedMaxReq ? mb_req : nullptr;
+  return width == 64 ? launch_decode<64>(a, ms, refresh, seal, s, hs, mbp)
+                     : launch_decode<128>(a, ms, refresh, seal, s, hs, mbp);
 }
 
 }  // namespace

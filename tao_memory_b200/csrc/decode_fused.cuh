@@ -25,9 +25,22 @@ namespace tao {
 // Feature-mass read: the host refuses batches whose route budget could exceed this.
 constexpr int kRouteCapMax = 256;
 
+// Per-request item counts of the fused kernel (requests with fewer selected fines get
+// fewer fine items instead of empty ones), for up to kFusedMaxReq requests and
+// kFusedMaxSlots items per head; larger batches give every request KB + ms items.
+constexpr int kFusedMaxReq = 64;
+constexpr int kFusedMaxSlots = 12 + kRouteCapMax;
+
 struct FusedArgs {
   StepArgs s;        // states, shapes, inputs, outputs, policy, partial buffers
-  int ms;            // fine items per (r, h)
+  int ms;            // fine items per (r, h) allotted in the partial buffers (their stride)
+  // Item order, slot-major: slot s holds one item per head of every request with more
+  // than s items per head, requests with more items first.  nslots = 0: every request
+  // has KB + ms items per head and item i is (request, head) i % (R H), slot i / (R H).
+  int nslots;
+  int slot_base[kFusedMaxSlots + 1];  // first item of each slot; slot_base[nslots] = items
+  int16_t rorder[kFusedMaxReq];       // requests by items per head, most first
+  int16_t per_r[kFusedMaxReq];        // items per head of each request
 };
 
 // Item geometry: an item's copies fill one IB-byte stage, either the K and V rows of
@@ -50,6 +63,22 @@ struct Item {
 TAO_DEVI Item item_of(int i, int R, int H) {
   const int rh = i % (R * H);
   return {rh / H, rh % H, i / (R * H)};
+}
+
+// Item i of a fused launch.
+TAO_DEVI Item fused_item(const FusedArgs& f, int i) {
+  if (f.nslots == 0) {
+    const int rh = i % (f.s.R * f.s.H);
+    return {rh / f.s.H, rh % f.s.H, i / (f.s.R * f.s.H)};
+  }
+  int lo = 0, hi = f.nslots - 1;  // the last slot starting at or before i
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (f.slot_base[mid] <= i) lo = mid;
+    else hi = mid - 1;
+  }
+  const int j = i - f.slot_base[lo];
+  return {f.rorder[j / f.s.H], j % f.s.H, lo};
 }
 
 template <int D>
@@ -173,7 +202,7 @@ TAO_DEVI void drain_stages(uint64_t* bars, const uint32_t* armed, const uint32_t
 // released the stage.  Registers are capped for 6 resident CTAs per SM (the shared
 // memory's limit with one 32 KB stage).
 template <int D, int NS, int IB>
-__global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
+__global__ void __launch_bounds__(128, 6) decode_fused_kernel(const __grid_constant__ FusedArgs f) {
   using Cfg = FusedCfg<D, IB>;
   const StepArgs& a = f.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -187,8 +216,7 @@ __global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
   __shared__ float mass_s[kRouteCapMax];  // feature read: mass of every selected fine
   __shared__ int last_rh;
   __shared__ int ids_s[NS][Cfg::FPC];     // fine ids of the item in each stage
-  const int per = Cfg::KB + f.ms;
-  const int total = a.R * a.H * per;
+  const int total = f.nslots ? f.slot_base[f.nslots] : a.R * a.H * (Cfg::KB + f.ms);
   constexpr int kArriver = (D < 128) ? D : 0;  // a thread with no channel in the combine (D = 64)
   ItemCopy<D, IB> next_copy{};
   if (tid == 0) {
@@ -198,7 +226,7 @@ __global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
     ItemCopy<D, IB> c[NS] = {};  // every stage's sources first, so their loads overlap
 #pragma unroll
     for (int x = 0; x < NS; ++x)
-      if (blockIdx.x + x * gridDim.x < total) c[x] = resolve_item<D, IB>(f, item_of(blockIdx.x + x * gridDim.x, a.R, a.H));
+      if (blockIdx.x + x * gridDim.x < total) c[x] = resolve_item<D, IB>(f, fused_item(f, blockIdx.x + x * gridDim.x));
 #pragma unroll
     for (int x = 0; x < NS; ++x) {
 #pragma unroll
@@ -211,7 +239,7 @@ __global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
   for (int x = 0; x < NS; ++x) phases[x] = 0;
   int sidx = 0;   // stage of the current item
   for (int i = blockIdx.x; i < total; i += gridDim.x, sidx = (sidx + 1 == NS) ? 0 : sidx + 1) {
-    const Item it = item_of(i, a.R, a.H);
+    const Item it = fused_item(f, i);
     TaoState& st = *a.states[it.r];
     const long long t = st.position;
     const int n_route = st.n_route;
@@ -224,7 +252,7 @@ __global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
       if (x == sidx) phase = phases[x];
     __syncthreads();
     const uint32_t armed = armed_s[sidx];
-    if (tid == 0 && nxt < total) next_copy = resolve_item<D, IB>(f, item_of(nxt, a.R, a.H));  // overlaps the copy
+    if (tid == 0 && nxt < total) next_copy = resolve_item<D, IB>(f, fused_item(f, nxt));  // overlaps the copy
     const long long src = ((long long)it.r * a.H + it.h) * D;
     // The combine's per-channel operands (raw_q, fusion_a terms 0 and 2, fusion_b terms
     // 0 and 2 of channel d = tid), loaded now so that their latency is off the
@@ -437,6 +465,7 @@ __global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
       armed_s[sidx] = (nxt < total) ? issue_copy<D, IB>(next_copy, dsm, &bar) : 0u;
     }
     if (tid == 32) {  // warp 1 arrives while warp 0 issues the copy
+      const int per = f.nslots ? f.per_r[it.r] : Cfg::KB + f.ms;  // items of (r, h)
       last_rh = (atomic_add_release(&st.counters[it.h], 1) == per - 1) ? 1 : 0;
       if (last_rh) {
         st.counters[it.h] = 0;
@@ -453,6 +482,8 @@ __global__ void __launch_bounds__(128, 6) decode_fused_kernel(FusedArgs f) {
     if (tid == kArriver) arrived = atomic_add_release(&st.arrive, 1);
     const bool hist = t >= kWindow;
     const int nparts = hist ? (n_route + Cfg::FPC - 1) / Cfg::FPC : 0;
+    if (tid == 0 && nparts > (f.nslots ? f.per_r[it.r] : Cfg::KB + f.ms) - Cfg::KB)
+      atomicOr(a.err, kErrRouteCap);  // more routes than the launch gave fine items
     if (tid < D) {  // D <= 128: one channel per thread; partials straight from L2
       const int d = tid;
       const float* lg = a.local_part + ((long long)it.r * a.H + it.h) * Cfg::KB * (D + 2);
