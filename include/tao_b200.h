@@ -140,8 +140,9 @@ int tao_stream_step(void* const* states, int n_states, const int64_t* host_pos,
  * (plus a routing kernel on refresh tokens and a seal kernel when a window fills).
  * Same arguments as tao_stream_step with tokens = 1, plus host_layer (the layer
  * index of each state, used to decide on the host whether any request refreshes).
- * Workspace: tao_stream_workspace_bytes(n_states, 1, ...).  Results are identical
- * to tao_stream_step.  Reference: tao_attention_decode (operator.py:130-137). */
+ * Workspace: tao_stream_workspace_bytes(n_states, 1, ...).  Results agree with
+ * tao_stream_step up to fp32 summation order (routes identical).  Reference:
+ * tao_attention_decode (operator.py:130-137). */
 int tao_decode_step(void* const* states, int n_states, const int64_t* host_pos,
                     const int32_t* host_layer, const int32_t* host_cap, const TaoPolicy* policy,
                     int heads, int width, const void* q, const void* k, const void* v,
