@@ -305,11 +305,13 @@ int tao_writer_stats(const void* k, const void* v, long long token_stride, long 
                      long long block_stride, int blocks, int heads, int width, float* gram,
                      float* cross, float* mass, void* stream);
 
-/* Select the windowed-attention kernel for this process (tao_window_attention and
- * the training forward): 1 = tcgen05/TMEM kernel with TMA tile loads for width 64
- * (default; width 128 uses the mma.sync kernel), 0 = mma.sync kernel for every
- * width.  Outputs agree to fp32 summation order.  No counterpart in the reference
- * (it has one attention path, flash_attention.py:16-37). */
+/* Select the windowed-attention kernels for this process (tao_window_attention, the
+ * training forward and backward and the streaming prefill chunk over the ring):
+ * 1 = tcgen05/TMEM kernels (default: forward at widths 64 and 128, TMA tiles for
+ * contiguous operands and cp.async tiles for the ring; backward at width 64, width
+ * 128 on mma.sync), 0 = mma.sync kernels everywhere.  Outputs agree to fp32
+ * summation order.  No counterpart in the reference (it has one attention path,
+ * flash_attention.py:16-37). */
 int tao_attention_variant(int variant);
 
 /* ---- training (tao_attention, operator.py:42-54) -------------------------

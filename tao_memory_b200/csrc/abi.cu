@@ -22,6 +22,9 @@
 namespace tao {
 int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* out, float* lse, int B,
                             int T, int H, int D, int* err, cudaStream_t s);
+int launch_ring_attention(TaoState* const* states, const bf16* q, bf16* out, int R, int w, int H, int D, int* err,
+                          cudaStream_t s);
+int attention_variant();
 }  // namespace tao
 
 namespace {
@@ -191,10 +194,15 @@ int launch_step(tao::StepArgs a, const Layout& L, cudaStream_t s) {
     p.nq = a.w;
     p.ring = 1;
     p.states = a.states;
-    const size_t attn_smem = (size_t)(64 + 4 * 64) * D * 2;
-    if ((rc = set_smem(window_attention_kernel<D>, attn_smem))) return rc;
-    window_attention_kernel<D><<<dim3((a.w + 63) / 64, a.R * a.H), 128, attn_smem, s>>>(p);
-    if ((rc = check_launch("window_attention_kernel"))) return rc;
+    if (attention_variant() == 1) {
+      // tcgen05 / TMEM over each state's ring (cp.async tiles in the TMA layout)
+      if ((rc = launch_ring_attention(a.states, a.q, a.local_out, a.R, a.w, a.H, D, a.err, s))) return rc;
+    } else {
+      const size_t attn_smem = (size_t)(64 + 4 * 64) * D * 2;
+      if ((rc = set_smem(window_attention_kernel<D>, attn_smem))) return rc;
+      window_attention_kernel<D><<<dim3((a.w + 63) / 64, a.R * a.H), 128, attn_smem, s>>>(p);
+      if ((rc = check_launch("window_attention_kernel"))) return rc;
+    }
     const size_t pf_smem = (size_t)2 * D * D * 2 + (size_t)(2 * 16 * D + 2 * D) * 4;
     if ((rc = set_smem(prefill_fine_kernel<D>, pf_smem))) return rc;
     prefill_fine_kernel<D><<<dim3(a.R * a.H, (a.w + 15) / 16), 128, pf_smem, s>>>(a);

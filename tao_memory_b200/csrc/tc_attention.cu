@@ -87,14 +87,14 @@ int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* o
         return TAO_ERR_CUDA;
       }
       tc_window_attention_kernel<64><<<grid, tc::kTcThreads, tc::TcAttnCfg<64>::SMEM, s>>>(mq, mk, mv, out, lse, T, H,
-                                                                                          err);
+                                                                                          err, tc::TcRing{});
     } else {
       if (!smem_attr(tc_window_attention_kernel<128>, tc::TcAttnCfg<128>::SMEM)) {
         tao_set_last_error("smem attribute");
         return TAO_ERR_CUDA;
       }
       tc_window_attention_kernel<128><<<grid, tc::kTcThreads, tc::TcAttnCfg<128>::SMEM, s>>>(mq, mk, mv, out, lse, T,
-                                                                                            H, err);
+                                                                                            H, err, tc::TcRing{});
     }
     return TAO_OK;
   }
@@ -131,6 +131,40 @@ int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* o
 }
 
 int attention_variant() { return g_attention_variant; }
+
+// Attention of a streaming chunk (w queries of each of R states, at their cursors)
+// over each state's ring on the tensor cores: q and out [R][w][H][D].  Returns
+// TAO_ERR_ARG (nothing launched) for widths other than 64 and 128.
+int launch_ring_attention(TaoState* const* states, const bf16* q, bf16* out, int R, int w, int H, int D, int* err,
+                          cudaStream_t s) {
+  const CUtensorMap none{};
+  const dim3 grid((w + tc::kTcBM - 1) / tc::kTcBM, R * H);
+  const tc::TcRing ring{states, q, w};
+  if (D == 64) {
+    if (!smem_attr(tc_window_attention_kernel<64, true>, tc::TcAttnCfg<64>::SMEM)) {
+      tao_set_last_error("smem attribute");
+      return TAO_ERR_CUDA;
+    }
+    tc_window_attention_kernel<64, true><<<grid, tc::kTcThreads, tc::TcAttnCfg<64>::SMEM, s>>>(none, none, none, out,
+                                                                                               nullptr, 0, H, err, ring);
+  } else if (D == 128) {
+    if (!smem_attr(tc_window_attention_kernel<128, true>, tc::TcAttnCfg<128>::SMEM)) {
+      tao_set_last_error("smem attribute");
+      return TAO_ERR_CUDA;
+    }
+    tc_window_attention_kernel<128, true><<<grid, tc::kTcThreads, tc::TcAttnCfg<128>::SMEM, s>>>(
+        none, none, none, out, nullptr, 0, H, err, ring);
+  } else {
+    tao_set_last_error("ring attention on the tensor cores takes widths 64 and 128");
+    return TAO_ERR_ARG;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    tao_set_last_error(cudaGetErrorString(e));
+    return TAO_ERR_CUDA;
+  }
+  return TAO_OK;
+}
 
 // Windowed attention backward on the tensor cores (width 64): dK, dV and dQ of
 // contiguous [B][T][H][64] operands.  dq_acc is fp32 scratch of the same shape.

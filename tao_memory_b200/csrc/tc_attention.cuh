@@ -21,6 +21,7 @@
 #pragma once
 #include <cuda.h>
 
+#include "../../include/tao_b200.h"
 #include "common.cuh"
 #include "tcgen05.cuh"
 
@@ -47,6 +48,40 @@ constexpr int kTcTmemCols = 256;
 // O is rescaled only when a row maximum grows by more than this (log2 units):
 // until then scores are exponentiated against the stale maximum (p <= 2^8).
 constexpr float kTcRescale = 8.f;
+
+// Streaming prefill form (RING): the chunk's queries q [B][w][H][D] at positions
+// states[b]->position + i read the state's ring of keys and values ([H][768][D], row =
+// position % 768), written for the chunk before the launch; the output goes to
+// [B][w][H][D].  A 128-key block of a window is 128 consecutive ring rows (windows
+// start at multiples of 256), so its tiles are loaded by cp.async into the same
+// 128B-swizzled layout a TMA box has, 16 bytes per lane, each lane arriving on the
+// tile's mbarrier when its copies land.
+struct TcRing {
+  TaoState* const* states;
+  const bf16* q;
+  int w;
+};
+
+// Byte offset of channel chunk c (8 bf16) of tile row r in a 128B-swizzled tile of
+// 64-channel atoms: the layout of a TMA box of 64 columns x 128 rows per atom.
+TAO_DEVI uint32_t sw128_off(int r, int c) {
+  return (uint32_t)((c >> 3) * kTcAtom + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+// One lane's share of a 128-row tile: rows[r * D .. + D) -> dst (rows >= nrows zero),
+// then an arrival on `bar` once this lane's copies have landed.
+template <int D>
+TAO_DEVI void cp_tile(uint8_t* dst, const bf16* rows, long long row_stride, int nrows, uint64_t* bar, int lane) {
+  constexpr int CH = D / 8;
+  for (int idx = lane; idx < kTcBM * CH; idx += 32) {
+    const int r = idx / CH, c = idx % CH;
+    const bool ok = r < nrows;
+    const bf16* src = rows + (long long)(ok ? r : 0) * row_stride + c * 8;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst + sw128_off(r, c))), "l"(src),
+                 "r"(ok ? 16 : 0)
+                 : "memory");
+  }
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 // Bounded wait that also gives up as soon as another thread of the CTA raised
 // the abort flag (so one timeout ends every wait of the CTA promptly).
@@ -75,11 +110,14 @@ TAO_DEVI bool warp_wait(uint64_t* bar, uint32_t phase, int* err, volatile int* a
 //   softmax (warps 0-3, one query row per thread): sfull(j) -> tcgen05.ld S row ->
 //     sfree -> mask, row max -> ofull(j-1) -> rescale the O row in TMEM if its
 //     maximum moved by more than 2^8 -> P(j) (bf16 pairs) to TMEM -> pfull.
-template <int D>
+//
+// RING: the streaming prefill form (see TcRing); the tensor maps are unused, lse is
+// not written and T is ignored.
+template <int D, bool RING = false>
 __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_window_attention_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
     const __grid_constant__ CUtensorMap tv, bf16* __restrict__ out, float* __restrict__ lse, int T,
-    int H, int* err) {
+    int H, int* err, tc::TcRing ring) {
   using namespace tc;
   constexpr int TILE = TcAttnCfg<D>::TILE, NA = D / 64;
   // 128B-swizzled tiles need 1024-byte alignment; the kernel uses no static
@@ -106,10 +144,23 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y / H, h = blockIdx.y % H;
   const int q0 = blockIdx.x * kTcBM;  // the 128 queries share one 256-token tile
-  int kstart = (q0 / kFine) * kFine - kKeep;
+  // absolute position of query row 0, rows that exist, the bound on key positions
+  long long qa0 = q0, tlimit = T;
+  int nrow = T - q0;
+  const bf16* kring = nullptr;
+  const bf16* vring = nullptr;
+  if constexpr (RING) {
+    const TaoState& st = *ring.states[b];
+    qa0 = st.position + q0;
+    nrow = ring.w - q0;
+    tlimit = 0x7fffffffffffffffll;
+    kring = reinterpret_cast<const bf16*>(st.k_ring) + (long long)h * kWindow * D;
+    vring = reinterpret_cast<const bf16*>(st.v_ring) + (long long)h * kWindow * D;
+  }
+  long long kstart = (qa0 / kFine) * kFine - kKeep;
   if (kstart < 0) kstart = 0;
-  const int kend = min(q0 + kTcBM, T);
-  const int nblk = (kend - kstart + kTcBN - 1) / kTcBN;
+  const long long kend = min(qa0 + kTcBM, qa0 + nrow);
+  const int nblk = (int)((kend - kstart + kTcBN - 1) / kTcBN);
   const int row0 = b * T;
   const int col = h * D;
 
@@ -119,10 +170,11 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(qbar, 1);
+    constexpr int LOADERS = RING ? 32 : 1;  // cp.async: every issuer lane arrives
+    mbar_init(qbar, LOADERS);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kfull[i], 1);
-      mbar_init(&vfull[i], 1);
+      mbar_init(&kfull[i], LOADERS);
+      mbar_init(&vfull[i], LOADERS);
     }
     mbar_init(sfull, 1);
     mbar_init(sfree, kTcBM);
@@ -145,7 +197,10 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
     int s_issued = 0, o_issued = 0;
     auto load_k = [&](int j) {
       const int st = j & 1;
-      if (leader) {
+      if constexpr (RING) {
+        cp_tile<D>(sK + st * TILE, kring + ((kstart + (long long)j * kTcBN) % kWindow) * D, D, kTcBN, &kfull[st],
+                   lane);
+      } else if (leader) {
         mbar_expect_tx(&kfull[st], TILE);
 #pragma unroll
         for (int at = 0; at < NA; ++at)
@@ -155,7 +210,10 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
     };
     auto load_v = [&](int j) {
       const int st = j & 1;
-      if (leader) {
+      if constexpr (RING) {
+        cp_tile<D>(sV + st * TILE, vring + ((kstart + (long long)j * kTcBN) % kWindow) * D, D, kTcBN, &vfull[st],
+                   lane);
+      } else if (leader) {
         mbar_expect_tx(&vfull[st], TILE);
 #pragma unroll
         for (int at = 0; at < NA; ++at)
@@ -167,6 +225,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
       const int st = j & 1;
       if (!warp_wait(&kfull[st], k_done[st] & 1, err, abort_flag)) return false;
       ++k_done[st];
+      if constexpr (RING) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async -> MMA
       fence_after();
       if (leader) {
         const uint32_t kaddr = smem_u32(sK + st * TILE), qaddr = smem_u32(sQ);
@@ -180,7 +239,10 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
       ++s_issued;
       return true;
     };
-    if (leader) {
+    if constexpr (RING) {
+      cp_tile<D>(sQ, ring.q + (((long long)b * ring.w + q0) * H + h) * D, (long long)H * D, min(nrow, kTcBM), qbar,
+                 lane);
+    } else if (leader) {
       mbar_expect_tx(qbar, TILE);
 #pragma unroll
       for (int at = 0; at < NA; ++at) tma_2d(sQ + at * kTcAtom, &tq, col + 64 * at, row0 + q0, qbar);
@@ -189,7 +251,9 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
       load_k(j);
       load_v(j);
     }
-    bool fine = warp_wait(qbar, 0, err, abort_flag) && issue_s(0);
+    bool fine = warp_wait(qbar, 0, err, abort_flag);
+    if constexpr (RING) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async -> MMA
+    fine = fine && issue_s(0);
     for (int j = 0; fine && j < nblk; ++j) {
       // S(j) has been read: the S columns and K stage j&1 are free
       if (!(fine = warp_wait(sfree, j & 1, err, abort_flag))) break;
@@ -206,6 +270,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
       const int st = j & 1;
       if (!(fine = warp_wait(&vfull[st], v_done[st] & 1, err, abort_flag))) break;
       ++v_done[st];
+      if constexpr (RING) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async -> MMA
       fence_after();
       if (leader) {
         const uint32_t vaddr = smem_u32(sV + st * TILE);
@@ -233,7 +298,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
   } else {
     // ================= softmax rows =================
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const int qpos = q0 + tid;
+    const long long qpos = qa0 + tid;
     const float sl = 1.4426950408889634f / sqrtf((float)D);  // log2(e) / sqrt(D)
     float mu = -INFINITY;  // exponent base of P and O (scaled log2 units)
     float l = 0.f;
@@ -246,12 +311,12 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
       for (int c = 0; c < kTcBN / 32; ++c) tmem_ld32(tS + lane_off + c * 32, sc + c * 32);
       fence_before();
       mbar_arrive(sfree);
-      const int kb0 = kstart + j * kTcBN;
-      if (kb0 + kTcBN - 1 > q0 || kb0 + kTcBN > T) {  // block reaches the diagonal or the end
+      const long long kb0 = kstart + (long long)j * kTcBN;
+      if (kb0 + kTcBN - 1 > qa0 || kb0 + kTcBN > tlimit) {  // block reaches the diagonal or the end
 #pragma unroll
         for (int c = 0; c < kTcBN; ++c) {
-          const int kp = kb0 + c;
-          if (kp > qpos || kp >= T) sc[c] = -INFINITY;
+          const long long kp = kb0 + c;
+          if (kp > qpos || kp >= tlimit) sc[c] = -INFINITY;
         }
       }
       float m4[4];  // four independent chains, then a tree
@@ -306,9 +371,10 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
       float ov[D];
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ov + c * 32);
-      if (qpos < T) {
+      if (tid < nrow) {
         const float inv = 1.f / l;
-        bf16* orow = out + ((long long)(row0 + qpos) * H + h) * D;
+        bf16* orow = RING ? out + (((long long)b * ring.w + q0 + tid) * H + h) * D
+                          : out + ((long long)(row0 + qpos) * H + h) * D;
 #pragma unroll
         for (int c8 = 0; c8 < D / 8; ++c8) {
           uint32_t pk[4];
@@ -320,7 +386,7 @@ __global__ void __launch_bounds__(tc::kTcThreads, tc::TcAttnCfg<D>::CTAS) tc_win
           }
           *reinterpret_cast<uint4*>(orow + c8 * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
-        if (lse) lse[((long long)b * H + h) * T + qpos] = (mu + log2f(l)) * 0.6931471805599453f;
+        if (!RING && lse) lse[((long long)b * H + h) * T + qpos] = (mu + log2f(l)) * 0.6931471805599453f;
       }
     }
   }

@@ -113,6 +113,34 @@ def test_stream_matches_oracle(heads, width, layer, splits, steps, one_thread):
     assert sum(int(not torch.equal(a, b)) for a, b in zip(ids, ref_ids)) == 0
 
 
+@pytest.mark.parametrize("width", [64, 128])
+def test_prefill_ring_attention_tcgen05_matches_mma_sync_and_oracle(width, one_thread):
+    """The streaming prefill's chunk attention over the ring runs on tcgen05 (attention
+    variant 1) or on mma.sync (variant 0): both prefill the same prompt (chunks that
+    start mid-tile, fill a window and wrap the ring) to outputs within the bf16
+    tolerance of the oracle, with identical routes."""
+    from tao_memory_b200 import _lib
+    heads, layer = 2, 1
+    splits = (300, 500, 1200, 77, 1000)      # 3077 tokens: seals, wraps, ragged chunks
+    x, _ = make_inputs(1, sum(splits) + 4, heads, width, seed=70 + width)
+    outs = {}
+    for variant in (0, 1):
+        _lib.check(_lib.lib().tao_attention_variant(variant))
+        try:
+            outs[variant] = run_gpu(x, layer, splits, 4, 0.4)
+        finally:
+            _lib.check(_lib.lib().tao_attention_variant(1))
+    orc = o.OracleStream(layer)
+    ref = torch.cat([orc.step(*(x[k][:, sl] for k in KEYS), x["fusion_a"], x["fusion_b"], 0.4)
+                     for sl in [slice(a, a + n) for a, n in zip((0, 300, 800, 2000, 2077), splits)]], 1)
+    n = sum(splits)
+    for variant in (0, 1):
+        assert_close(outs[variant][0][:, :n], ref, f"prefill attention variant {variant} d{width}")
+    assert all(torch.equal(a, b) for a, b in zip(outs[0][1], outs[1][1]))
+    e0, e1 = outs[0][2].export(), outs[1][2].export()
+    assert torch.equal(e0["packed_fine_c"], e1["packed_fine_c"])
+
+
 @pytest.mark.parametrize("variant", [1, 3, 4, 0, 2])
 @pytest.mark.parametrize("width", [64, 128])
 def test_decode_kernel_variants_match_oracle(variant, width, one_thread):
