@@ -166,37 +166,48 @@ int launch_ring_attention(TaoState* const* states, const bf16* q, bf16* out, int
   return TAO_OK;
 }
 
-// Windowed attention backward on the tensor cores (width 64): dK, dV and dQ of
-// contiguous [B][T][H][64] operands.  dq_acc is fp32 scratch of the same shape.
+// Windowed attention backward on the tensor cores (widths 64 and 128): dK, dV and dQ
+// of contiguous [B][T][H][D] operands.  dq_acc is fp32 scratch of the same shape.  At
+// width 128 each key block runs as two CTAs, one per half of the gradient channels.
 int launch_attention_backward_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* dout, const float* lse,
                                  const float* rowdot, bf16* dq, bf16* dk, bf16* dv, float* dq_acc, int B, int T,
-                                 int H, int* err, cudaStream_t s) {
+                                 int H, int D, int* err, cudaStream_t s) {
+  if (D != 64 && D != 128) {
+    tao_set_last_error("attention backward on the tensor cores takes widths 64 and 128");
+    return TAO_ERR_ARG;
+  }
   for (const void* p : {(const void*)q, (const void*)k, (const void*)v, (const void*)dout, (const void*)dq_acc})
     if (!aligned(p)) {
       tao_set_last_error("attention backward operands must be 16-byte aligned");
       return TAO_ERR_ARG;
     }
   CUtensorMap mq, mk, mv, mo, mdq;
-  const unsigned long long rows = (unsigned long long)B * T, cols = (unsigned long long)H * tb::kD;
+  const unsigned long long rows = (unsigned long long)B * T, cols = (unsigned long long)H * D;
   if (!row_map(&mq, q, rows, cols) || !row_map(&mk, k, rows, cols) || !row_map(&mv, v, rows, cols) ||
       !row_map(&mo, dout, rows, cols) || !f32_map(&mdq, dq_acc, rows, cols)) {
     tao_set_last_error("cuTensorMapEncodeTiled failed");
     return TAO_ERR_CUDA;
   }
-  if (!smem_attr(tc_attention_bwd_kernel, tb::kSmem)) {
+  const bool attr = D == 64 ? smem_attr(tc_attention_bwd_kernel<64>, tb::Cfg<64>::SMEM)
+                            : smem_attr(tc_attention_bwd_kernel<128>, tb::Cfg<128>::SMEM);
+  if (!attr) {
     tao_set_last_error("smem attribute");
     return TAO_ERR_CUDA;
   }
-  const long long n = (long long)B * T * H * tb::kD;
+  const long long n = (long long)B * T * H * D;
   if (cudaMemsetAsync(dq_acc, 0, (size_t)n * sizeof(float), s) != cudaSuccess) {
     tao_set_last_error("dq accumulator memset failed");
     return TAO_ERR_CUDA;
   }
   TcBwdArgs a{lse, rowdot, dk, dv, T, H, err};
-  tc_attention_bwd_kernel<<<dim3((T + tb::kBN - 1) / tb::kBN, B * H), tb::kThreads, tb::kSmem, s>>>(mq, mk, mv, mo,
-                                                                                                    mdq, a);
+  const dim3 grid((T + tb::kBN - 1) / tb::kBN, B * H, D / 64);
+  if (D == 64)
+    tc_attention_bwd_kernel<64><<<grid, tb::kThreads, tb::Cfg<64>::SMEM, s>>>(mq, mk, mv, mo, mdq, a);
+  else
+    tc_attention_bwd_kernel<128><<<grid, tb::kThreads, tb::Cfg<128>::SMEM, s>>>(mq, mk, mv, mo, mdq, a);
   const long long n8 = n / 8;
-  dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, dq, n8);
+  dq_convert_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(dq_acc, dq, n8, D == 64 ? 0.125f
+                                                                                        : 0.08838834764831845f);
   return TAO_OK;
 }
 

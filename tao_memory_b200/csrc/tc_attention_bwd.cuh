@@ -47,6 +47,27 @@ constexpr int kOffBar = kOffStat + 2 * 2 * 128 * 4;
 constexpr int kSmem = kOffBar + 128;
 constexpr int kTmemCols = 512;
 
+// Layout by width.  Width 64: the layout above.  Width 128: each CTA computes half of
+// the gradient channels (blockIdx.z; S^T and dP^T are full-width contractions, so the
+// two halves each form them), K, V, Q[2], dO[2] are full-width tiles of two 64-channel
+// atoms, P^T lives in TMEM (columns 448-511, bf16 pairs, the A operand of the dV
+// product) instead of shared memory, and each warp stages its dQ box in its own rows
+// of the dS^T buffer (free between the block's products and the next dS^T).
+template <int D>
+struct Cfg {
+  static constexpr int TILE = 128 * D * 2;  // K, V, Q, dO tiles
+  static constexpr int NA = D / 64;         // 64-channel atoms per tile
+  static constexpr bool PT_TMEM = D == 128;
+  static constexpr int OFF_K = 0, OFF_V = TILE, OFF_Q = 2 * TILE, OFF_O = 4 * TILE, OFF_DS = 6 * TILE;
+  static constexpr int OFF_DQ = PT_TMEM ? OFF_DS : OFF_DS + 2 * kTile;
+  static constexpr int OFF_PT = OFF_DQ + 8 * 4096;  // width 64 only
+  static constexpr int OFF_STAT = PT_TMEM ? OFF_DS + 2 * kTile : OFF_PT + 2 * kTile;
+  static constexpr int OFF_BAR = OFF_STAT + 2 * 2 * 128 * 4;
+  static constexpr int SMEM = OFF_BAR + 128;
+};
+static_assert(Cfg<64>::SMEM == kSmem, "width-64 layout");
+static_assert(Cfg<128>::SMEM <= 232448, "width-128 layout exceeds shared memory");
+
 // Bulk tensor reduce-add of a shared-memory box into global memory (TMA).
 TAO_DEVI void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
   asm volatile(
@@ -77,20 +98,26 @@ struct TcBwdArgs {
   int* err;
 };
 
+template <int D>
 __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
     const __grid_constant__ CUtensorMap tdq, TcBwdArgs a) {
   using namespace tc;
   using namespace tb;
+  using C = tb::Cfg<D>;
+  constexpr int TILE = C::TILE, NA = C::NA;
+  constexpr int kOffK = C::OFF_K, kOffV = C::OFF_V, kOffQ = C::OFF_Q, kOffO = C::OFF_O, kOffDS = C::OFF_DS;
+  constexpr int kOffDQ = C::OFF_DQ, kOffPT = C::OFF_PT;
+  constexpr float kScale = D == 64 ? 0.125f : 0.08838834764831845f;  // 1 / sqrt(D)
   extern __shared__ __align__(1024) uint8_t sm[];
   if (smem_u32(sm) & 1023u) {
     if (threadIdx.x == 0 && a.err) atomicOr(a.err, kErrState);
     return;
   }
-  float* const lseS = reinterpret_cast<float*>(sm + kOffStat);  // [2][128] lse * log2(e)
-  float* const rdS = lseS + 2 * 128;                              // [2][128]
-  uint64_t* const bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  float* const lseS = reinterpret_cast<float*>(sm + C::OFF_STAT);  // [2][128] lse * log2(e)
+  float* const rdS = lseS + 2 * 128;                                // [2][128]
+  uint64_t* const bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
   uint64_t* const kvbar = bars;
   uint64_t* const qbar = bars + 1;     // [2] Q_i and dO_i
   uint64_t* const statbar = bars + 3;  // [2] lse / rowdot of block i
@@ -109,7 +136,8 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
   int qend = (k0 / kFine + 3) * kFine;  // queries whose window reaches this key block
   if (qend > T) qend = T;
   const int nq = (qend - k0 + kBQ - 1) / kBQ;
-  const int row0 = b * T, col = h * kD;
+  const int half = D == 128 ? (int)blockIdx.z : 0;  // gradient channels 64 half .. + 63
+  const int row0 = b * T, col = h * D, ccol = col + 64 * half;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -135,6 +163,7 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
   fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t tS = tbase, tDP = tbase + 128, tDV = tbase + 256, tDK = tbase + 320, tDQ = tbase + 384;
+  const uint32_t tPT = tbase + 448;  // width 128: P^T (bf16 pairs)
   const float* lse_g = a.lse + ((long long)b * H + h) * T;
   const float* rd_g = a.rowdot + ((long long)b * H + h) * T;
 
@@ -150,9 +179,12 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
     auto load_q = [&](int i) {
       const int st = i & 1;
       if (leader) {
-        mbar_expect_tx(&qbar[st], 2 * kTile);
-        tma_2d(sm + kOffQ + st * kTile, &tq, col, row0 + k0 + i * kBQ, &qbar[st]);
-        tma_2d(sm + kOffO + st * kTile, &tdo, col, row0 + k0 + i * kBQ, &qbar[st]);
+        mbar_expect_tx(&qbar[st], 2 * TILE);
+#pragma unroll
+        for (int at = 0; at < NA; ++at) {
+          tma_2d(sm + kOffQ + st * TILE + at * kTile, &tq, col + 64 * at, row0 + k0 + i * kBQ, &qbar[st]);
+          tma_2d(sm + kOffO + st * TILE + at * kTile, &tdo, col + 64 * at, row0 + k0 + i * kBQ, &qbar[st]);
+        }
       }
       ++q_armed[st];
     };
@@ -174,9 +206,12 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
       mbar_arrive(&statbar[st]);
     };
     if (leader) {
-      mbar_expect_tx(kvbar, 2 * kTile);
-      tma_2d(sm + kOffK, &tk, col, row0 + k0, kvbar);
-      tma_2d(sm + kOffV, &tv, col, row0 + k0, kvbar);
+      mbar_expect_tx(kvbar, 2 * TILE);
+#pragma unroll
+      for (int at = 0; at < NA; ++at) {
+        tma_2d(sm + kOffK + at * kTile, &tk, col + 64 * at, row0 + k0, kvbar);
+        tma_2d(sm + kOffV + at * kTile, &tv, col + 64 * at, row0 + k0, kvbar);
+      }
     }
     for (int i = 0; i < 2 && i < nq; ++i) load_q(i);
     fetch_stats(0);
@@ -192,14 +227,16 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
       if (!warp_wait(&qbar[st], q_done[st] & 1, a.err, abort_flag)) return false;
       ++q_done[st];
       fence_after();
-      const uint32_t aQ = smem_u32(sm + kOffQ + st * kTile), aO = smem_u32(sm + kOffO + st * kTile);
-      if (leader) {
+      const uint32_t aQ = smem_u32(sm + kOffQ + st * TILE), aO = smem_u32(sm + kOffO + st * TILE);
+      if (leader) {  // full-width contractions: 64-channel atoms 16 KB apart, 4 K-steps each
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k)
-          mma(tS, sdesc(aK + k * 32, 16, 1024), sdesc(aQ + k * 32, 16, 1024), I_S, k > 0);
+        for (int k = 0; k < D / 16; ++k)
+          mma(tS, sdesc(aK + (k >> 2) * kTile + (k & 3) * 32, 16, 1024),
+              sdesc(aQ + (k >> 2) * kTile + (k & 3) * 32, 16, 1024), I_S, k > 0);
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k)
-          mma(tDP, sdesc(aV + k * 32, 16, 1024), sdesc(aO + k * 32, 16, 1024), I_S, k > 0);
+        for (int k = 0; k < D / 16; ++k)
+          mma(tDP, sdesc(aV + (k >> 2) * kTile + (k & 3) * 32, 16, 1024),
+              sdesc(aO + (k >> 2) * kTile + (k & 3) * 32, 16, 1024), I_S, k > 0);
         commit(sfull);
       }
       __syncwarp();
@@ -220,19 +257,26 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
       if (!(fine = warp_wait(pfull, i & 1, a.err, abort_flag))) break;
       if (i > 0 && !(fine = warp_wait(dqfree, (i - 1) & 1, a.err, abort_flag))) break;
       fence_after();
-      const uint32_t aQ = smem_u32(sm + kOffQ + st * kTile), aO = smem_u32(sm + kOffO + st * kTile);
+      // this CTA's gradient channels: the `half` atom of Q, dO and K
+      const uint32_t aQ = smem_u32(sm + kOffQ + st * TILE) + half * kTile;
+      const uint32_t aO = smem_u32(sm + kOffO + st * TILE) + half * kTile;
+      const uint32_t aKh = aK + half * kTile;
       if (leader) {
 #pragma unroll
-        for (int k = 0; k < kBQ / 16; ++k)  // A = P^T (keys x queries), K-major, 16 queries per step
-          mma(tDV, sdesc(aPT + (k >> 2) * kTile + (k & 3) * 32, 16, 1024), sdesc(aO + k * 2048, 8192, 1024),
-              I_KV, (i > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < kBQ / 16; ++k) {  // A = P^T (keys x queries), 16 queries per step
+          if constexpr (C::PT_TMEM)
+            mma_ts(tDV, tPT + k * 8, sdesc(aO + k * 2048, 8192, 1024), I_KV, (i > 0 || k > 0) ? 1u : 0u);
+          else
+            mma(tDV, sdesc(aPT + (k >> 2) * kTile + (k & 3) * 32, 16, 1024), sdesc(aO + k * 2048, 8192, 1024),
+                I_KV, (i > 0 || k > 0) ? 1u : 0u);
+        }
 #pragma unroll
         for (int k = 0; k < kBQ / 16; ++k)
           mma(tDK, sdesc(aDS + (k >> 2) * kTile + (k & 3) * 32, 16, 1024), sdesc(aQ + k * 2048, 8192, 1024),
               I_KV, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < kBN / 16; ++k)
-          mma(tDQ, sdesc(aDS + k * 2048, kTile, 1024), sdesc(aK + k * 2048, 8192, 1024), I_Q, k > 0);
+          mma(tDQ, sdesc(aDS + k * 2048, kTile, 1024), sdesc(aKh + k * 2048, 8192, 1024), I_Q, k > 0);
         commit(ofull);
       }
       __syncwarp();
@@ -259,7 +303,7 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
     const int kr = qd * 32 + lane;  // key row of this thread
     const int key = k0 + kr;
-    const float sl = 1.4426950408889634f * 0.125f;  // log2(e) / sqrt(64)
+    const float sl = 1.4426950408889634f * kScale;  // log2(e) / sqrt(D)
     uint8_t* const dsrow = sm + kOffDS + ch * kTile + kr * 128;
     uint8_t* const ptrow = sm + kOffPT + ch * kTile + kr * 128;
     uint8_t* const stage = sm + kOffDQ + warp * 4096;
@@ -281,9 +325,12 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) {
-        tma_reduce_add_2d(&tdq, stage, col + ch * 32, row0 + qj + qd * 32);
+        tma_reduce_add_2d(&tdq, stage, ccol + ch * 32, row0 + qj + qd * 32);
         bulk_commit();
+        // width 128: the box sits in this warp's dS^T rows, written next
+        if constexpr (C::PT_TMEM) bulk_wait_read0();
       }
+      if constexpr (C::PT_TMEM) __syncwarp();
     };
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
@@ -344,8 +391,13 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
           const int chunk = (c * 4 + u) ^ (kr & 7);
           const int o = c * 16 + 4 * u;
           *reinterpret_cast<uint4*>(dsrow + chunk * 16) = make_uint4(dd[o], dd[o + 1], dd[o + 2], dd[o + 3]);
-          *reinterpret_cast<uint4*>(ptrow + chunk * 16) = make_uint4(pp[o], pp[o + 1], pp[o + 2], pp[o + 3]);
+          if constexpr (!C::PT_TMEM)
+            *reinterpret_cast<uint4*>(ptrow + chunk * 16) = make_uint4(pp[o], pp[o + 1], pp[o + 2], pp[o + 3]);
         }
+      if constexpr (C::PT_TMEM) {
+        tmem_st32u(tPT + lane_off + ch * 32, pp);  // this thread's 64 query columns as 32 pairs
+        fence_before();
+      }
       fence_proxy_async();
       mbar_arrive(pfull);
     }
@@ -363,7 +415,7 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
       tmem_ld32(tDV + lane_off + ch * 32, dvv);
       tmem_ld32(tDK + lane_off + ch * 32, dkk);
       if (key < T) {
-        const long long off = ((long long)(row0 + key) * H + h) * kD + ch * 32;
+        const long long off = ((long long)(row0 + key) * H + h) * D + 64 * half + ch * 32;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint4 pv, pk;
@@ -371,10 +423,10 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
           pv.y = pack2(dvv[8 * u + 2], dvv[8 * u + 3]);
           pv.z = pack2(dvv[8 * u + 4], dvv[8 * u + 5]);
           pv.w = pack2(dvv[8 * u + 6], dvv[8 * u + 7]);
-          pk.x = pack2(dkk[8 * u] * 0.125f, dkk[8 * u + 1] * 0.125f);
-          pk.y = pack2(dkk[8 * u + 2] * 0.125f, dkk[8 * u + 3] * 0.125f);
-          pk.z = pack2(dkk[8 * u + 4] * 0.125f, dkk[8 * u + 5] * 0.125f);
-          pk.w = pack2(dkk[8 * u + 6] * 0.125f, dkk[8 * u + 7] * 0.125f);
+          pk.x = pack2(dkk[8 * u] * kScale, dkk[8 * u + 1] * kScale);
+          pk.y = pack2(dkk[8 * u + 2] * kScale, dkk[8 * u + 3] * kScale);
+          pk.z = pack2(dkk[8 * u + 4] * kScale, dkk[8 * u + 5] * kScale);
+          pk.w = pack2(dkk[8 * u + 6] * kScale, dkk[8 * u + 7] * kScale);
           *reinterpret_cast<uint4*>(a.dv + off + 8 * u) = pv;
           *reinterpret_cast<uint4*>(a.dk + off + 8 * u) = pk;
         }
@@ -389,17 +441,17 @@ __global__ void __launch_bounds__(tb::kThreads, 1) tc_attention_bwd_kernel(
   }
 }
 
-// dq = bf16(dq_acc / 8), eight elements per thread.
-__global__ void dq_convert_kernel(const float* __restrict__ acc, bf16* __restrict__ dq, long long n8) {
+// dq = bf16(dq_acc * scale) (scale = 1 / sqrt(D)), eight elements per thread.
+__global__ void dq_convert_kernel(const float* __restrict__ acc, bf16* __restrict__ dq, long long n8, float scale) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   const float4 x = reinterpret_cast<const float4*>(acc)[2 * i];
   const float4 y = reinterpret_cast<const float4*>(acc)[2 * i + 1];
   uint4 o;
-  o.x = tb::pack2(x.x * 0.125f, x.y * 0.125f);
-  o.y = tb::pack2(x.z * 0.125f, x.w * 0.125f);
-  o.z = tb::pack2(y.x * 0.125f, y.y * 0.125f);
-  o.w = tb::pack2(y.z * 0.125f, y.w * 0.125f);
+  o.x = tb::pack2(x.x * scale, x.y * scale);
+  o.y = tb::pack2(x.z * scale, x.w * scale);
+  o.z = tb::pack2(y.x * scale, y.y * scale);
+  o.w = tb::pack2(y.z * scale, y.w * scale);
   reinterpret_cast<uint4*>(dq)[i] = o;
 }
 

@@ -14,7 +14,7 @@ int launch_window_attention(const bf16* q, const bf16* k, const bf16* v, bf16* o
                             int T, int H, int D, int* err, cudaStream_t s);
 int launch_attention_backward_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* dout, const float* lse,
                                  const float* rowdot, bf16* dq, bf16* dk, bf16* dv, float* dq_acc, int B, int T,
-                                 int H, int* err, cudaStream_t s);
+                                 int H, int D, int* err, cudaStream_t s);
 int attention_variant();
 }  // namespace tao
 
@@ -171,9 +171,9 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
     split_bwd_kernel<D><<<fgrid, 256, 0, s>>>(a);
   else
     fusion_bwd_kernel<D><<<fgrid, 256, 0, s>>>(a);
-  if (D == 64 && a.dq_acc && attention_variant() == 1) {
+  if (a.dq_acc && attention_variant() == 1) {
     if (int rc = launch_attention_backward_tc(a.q, a.k, a.v, a.d_local, a.lse, a.dv_row, a.dq, a.dk, a.dv,
-                                              a.dq_acc, B, T, H, a.err, s))
+                                              a.dq_acc, B, T, H, D, a.err, s))
       return rc;
   } else {
     const size_t asmem = (size_t)(2 * 64 + 4 * 64) * D * 2 + 256 * 4;

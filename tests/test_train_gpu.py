@@ -116,14 +116,16 @@ def test_backward_matches_oracle(b, t, h, d, alpha, one_thread):
         assert rel_l2(grads[k], leaves[k].grad) <= 2e-2, (k, rel_l2(grads[k], leaves[k].grad))
 
 
-@pytest.mark.parametrize("b,t,h", [(2, 4096, 3), (1, 2000, 2), (1, 300, 1)])
-def test_tcgen05_attention_backward_matches_mma_sync(b, t, h):
-    """Gradients through the tcgen05 attention kernels (default) and through the
+@pytest.mark.parametrize("b,t,h,d", [(2, 4096, 3, 64), (1, 2000, 2, 64), (1, 300, 1, 64), (1, 2000, 2, 128),
+                                     (1, 300, 1, 128)])
+def test_tcgen05_attention_backward_matches_mma_sync(b, t, h, d):
+    """Gradients through the tcgen05 attention kernels (default; width 128 as two
+    CTAs per key block, one per half of the gradient channels) and through the
     mma.sync kernels agree: q/k/v rel-L2 <= 1e-2 (bf16 operands, different fp32
     summation order and dQ accumulation by atomics)."""
     from tao_memory_b200 import _lib
-    x, _ = make_inputs(b, t, h, 64, seed=21)
-    grad = torch.randn(b, t, h, 64, generator=torch.Generator().manual_seed(22)).to(torch.bfloat16)
+    x, _ = make_inputs(b, t, h, d, seed=21)
+    grad = torch.randn(b, t, h, d, generator=torch.Generator().manual_seed(22)).to(torch.bfloat16)
     out1, g1 = run(x, 0.5, grad)
     _lib.check(_lib.lib().tao_attention_variant(0))
     try:
