@@ -119,16 +119,14 @@ int train_forward(const tao::bf16* q, const tao::bf16* k, const tao::bf16* v, co
   a.err = tb.err;
   a.external_fusion = (tb.flags & TAO_TRAIN_EXTERNAL_FUSION) ? 1 : 0;
   a.route_only = route_only ? 1 : 0;
-  a.tc = attention_variant() == 1 ? 1 : 0;   // width 64: the selected read on tcgen05
+  a.tc = attention_variant() == 1 ? 1 : 0;   // the selected read on tcgen05
   const size_t rsmem = ReadSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the training read kernel");
   bool launched = false;
-  if constexpr (D == 64) {
-    if (a.tc) {
-      if (!tsmem(train_read_kernel<D, true>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
-      train_read_kernel<D, true><<<dim3(B * H, g.tiles), 256, rsmem, s>>>(a);
-      launched = true;
-    }
+  if (a.tc) {
+    if (!tsmem(train_read_kernel<D, true>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+    train_read_kernel<D, true><<<dim3(B * H, g.tiles), 256, rsmem, s>>>(a);
+    launched = true;
   }
   if (!launched) {
     if (!tsmem(train_read_kernel<D>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");

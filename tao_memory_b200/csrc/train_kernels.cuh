@@ -301,8 +301,8 @@ TAO_DEVI void read_epilogue_pair(const ReadArgs& a, long long base, int e, float
   *reinterpret_cast<uint32_t*>(a.num_out + base + e) = pack_exact(nums[0], nums[1]);
 }
 
-// TC (width 64): the selected read on tcgen05 (a separate instantiation, so that each
-// kernel carries the code of one contraction path only).
+// TC: the selected read on tcgen05 (a separate instantiation, so that each kernel
+// carries the code of one contraction path only).
 template <int D, bool TC = false>
 __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   using namespace wa;
@@ -524,7 +524,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
   if (a.route_only) return;  // the caller reads the selected fines itself
   __shared__ float fabS[2][D * 3];   // the epilogue's fusion parameters of this head
 
-  if constexpr (D == 64 && TC) {
+  if constexpr (TC) {
     {
       // ---- 3'. the selected read on the 5th-generation tensor cores.  Per listed fine i:
       // each thread writes its query's row of A_i = bf16(hv * w) (zero when the query
@@ -536,14 +536,22 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
       // i % 2.  A has two TMEM buffers and C four shared-memory buffers: while MMA i runs
       // the threads form A_{i+1} and C_{i+2} is in flight; a buffer is reused only after
       // the MMA that read it has committed (bounded waits).
-      // TMEM: accumulators at columns 0-127, A buffers at 128-191 and 192-255.
+      // TMEM: accumulators at columns 0 and D, A buffers (both row halves, D/2 columns
+      // each) at 2D and 3D: 256 columns at width 64, 512 at width 128.  Width 128 keeps
+      // three C buffers (one in the C region, two in the A tile) and loads one fine
+      // ahead instead of two.
       using namespace tc;
+      constexpr int TCOLS = D == 64 ? 256 : 512;
+      constexpr int NCR = NBUF;        // C buffers in the C region
+      constexpr int NC = NCR + 2;      // ring of C buffers (two more in the A tile)
+      constexpr int PF = NC - 2;       // fines loaded ahead
+      constexpr uint32_t CLBO = D == 64 ? 8192 : 16384;  // MN-major C: 64-column atoms 16 KB apart
       __shared__ __align__(8) uint64_t tbar[2];
       __shared__ uint32_t tslot;
       __shared__ int tok;
       if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tslot)),
-                     "r"(256));
+                     "r"(TCOLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
       }
       if (tid == 0) {
@@ -556,24 +564,27 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
       fence_after();
       const uint32_t tacc = tslot;
       const bf16* cbt = a.C + ((long long)b * a.dm.H + h) * a.dm.S * (long long)D * D;
-      // C buffers 0, 1 in the C region, 2, 3 in the (now unused) A tile
-      auto cbuf = [&](int k) -> uint32_t { return k < 2 ? sC + k * D * D * 2 : sA + (k - 2) * D * D * 2; };
+      // C buffers 0 .. NCR-1 in the C region, two more in the (now unused) A tile; a C
+      // tile [d][e] in 64-column 128B-swizzled atoms (the layout of a TMA box)
+      auto cbuf = [&](int k) -> uint32_t { return k < NCR ? sC + k * D * D * 2 : sA + (k - NCR) * D * D * 2; };
       auto load_ct = [&](int s2, int k) {
         const bf16* src = cbt + (long long)s2 * D * D;
         for (int idx = tid; idx < D * D / 8; idx += 256) {
           const int r = idx / (D / 8), c = idx % (D / 8);
-          cp_async16(cbuf(k) + swz(r, c * 8, D), src + r * D + c * 8, true);
+          const uint32_t off = (uint32_t)((c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+          cp_async16(cbuf(k) + off, src + r * D + c * 8, true);
         }
         cp_commit();
       };
-      constexpr uint32_t I = idesc_bf16(128, 64, 0, 1);
+      constexpr uint32_t I = idesc_bf16(128, D, 0, 1);
       const int nu = nused;
       const uint32_t arow = (uint32_t)((warp & 3) * 32) << 16;   // this warp's TMEM lanes
       const int half = warp >> 2;                                  // rows 0-127 or 128-255
       bool ok = true;
       int issued = 0;   // MMA groups committed
-      if (nu > 0) load_ct(list[0], 0);
-      if (nu > 1) load_ct(list[1], 1);
+#pragma unroll
+      for (int p0 = 0; p0 < PF; ++p0)
+        if (nu > p0) load_ct(list[p0], p0);
       for (int i = 0; i < nu; ++i) {
         const int s2 = list[i], ab = i & 1;
         if (i >= 2) {   // MMA i-2 read A buffer ab and C buffer (i-2) % 4
@@ -585,34 +596,66 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
             break;
           }
         }
-        if (i + 2 < nu) load_ct(list[i + 2], (i + 2) & 3);
-        uint32_t arow_v[32];
+        if (i + PF < nu) load_ct(list[i + PF], (i + PF) % NC);
         const bool sel = live && ((selB[(s2 >> 5) * 256 + q] >> (s2 & 31)) & 1u);
-        if (sel) {
-          uint32_t hv[D / 2];
-          page_hv(s2 / kGroup, hv);
+        const uint32_t tA = tacc + 2 * D + ab * D + half * (D / 2) + arow;
+        if constexpr (D == 64) {
+          uint32_t arow_v[32];
+          if (sel) {
+            uint32_t hv[D / 2];
+            page_hv(s2 / kGroup, hv);
 #pragma unroll
-          for (int c = 0; c < D / 2; ++c) arow_v[c] = hmul2u(hv[c], sw2[s2 * (D / 2) + c]);
+            for (int c = 0; c < D / 2; ++c) arow_v[c] = hmul2u(hv[c], sw2[s2 * (D / 2) + c]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < D / 2; ++c) arow_v[c] = 0u;
+          }
+          tmem_st32u(tA, arow_v);
         } else {
+          // the row in 64-channel pieces: bf16(bf16(h * page w) * fine w)
+          const int page = s2 / kGroup;
 #pragma unroll
-          for (int c = 0; c < D / 2; ++c) arow_v[c] = 0u;
+          for (int j = 0; j < D / 64; ++j) {
+            uint32_t arow_v[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int cc = j * 8 + c;
+              if (sel) {
+                const uint4 hc = hchunk(cc);
+                const uint4 pc = *reinterpret_cast<const uint4*>(pw2 + page * (D / 2) + cc * 4);
+                const uint4 wc = *reinterpret_cast<const uint4*>(sw2 + s2 * (D / 2) + cc * 4);
+                arow_v[c * 4 + 0] = hmul2u(hmul2u(hc.x, pc.x), wc.x);
+                arow_v[c * 4 + 1] = hmul2u(hmul2u(hc.y, pc.y), wc.y);
+                arow_v[c * 4 + 2] = hmul2u(hmul2u(hc.z, pc.z), wc.z);
+                arow_v[c * 4 + 3] = hmul2u(hmul2u(hc.w, pc.w), wc.w);
+              } else {
+                arow_v[c * 4 + 0] = arow_v[c * 4 + 1] = arow_v[c * 4 + 2] = arow_v[c * 4 + 3] = 0u;
+              }
+            }
+            tmem_st32u(tA + j * 32, arow_v);
+          }
         }
-        tmem_st32u(tacc + 128 + ab * 64 + half * 32 + arow, arow_v);
-        // C_i complete: at most the two later loads stay in flight
-        if (i + 2 < nu) cp_wait<2>();
-        else if (i + 1 < nu) cp_wait<1>();
-        else cp_wait<0>();
+        // C_i complete: at most the PF later loads stay in flight
+        if constexpr (PF == 2) {
+          if (i + 2 < nu) cp_wait<2>();
+          else if (i + 1 < nu) cp_wait<1>();
+          else cp_wait<0>();
+        } else {
+          if (i + 1 < nu) cp_wait<1>();
+          else cp_wait<0>();
+        }
         fence_proxy_async();
         fence_before();
         __syncthreads();
         if (tid == 0) {
           fence_after();
-          const uint32_t cB = cbuf(i & 3);
+          const uint32_t cB = cbuf(i % NC);
+          const uint32_t tAb = tacc + 2 * D + ab * D;
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint32_t accf = (i > 0 || k > 0) ? 1u : 0u;
-            mma_ts(tacc, tacc + 128 + ab * 64 + k * 8, sdesc(cB + k * 2048, 8192, 1024), I, accf);
-            mma_ts(tacc + 64, tacc + 128 + ab * 64 + 32 + k * 8, sdesc(cB + k * 2048, 8192, 1024), I, accf);
+            mma_ts(tacc, tAb + k * 8, sdesc(cB + k * 2048, CLBO, 1024), I, accf);
+            mma_ts(tacc + D, tAb + D / 2 + k * 8, sdesc(cB + k * 2048, CLBO, 1024), I, accf);
           }
           commit(&tbar[ab]);
         }
@@ -646,7 +689,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
         // 4-7 accumulator 1 (rows 128-255), each its 32 TMEM lanes
         const float gain = a.gain[h];
         const int r = tid;
-        const uint32_t tl = tacc + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(warp >> 2) * 64;
+        const uint32_t tl = tacc + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(warp >> 2) * D;
         const long long base = ((long long)b * a.dm.T + q0 + r) * row + hoff;
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
@@ -671,7 +714,7 @@ __global__ void __launch_bounds__(256, 2) train_read_kernel(ReadArgs a) {
       }
       fence_before();
       __syncthreads();
-      if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tacc), "r"(256));
+      if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tacc), "r"(TCOLS));
       return;
     }
   } else {
