@@ -186,17 +186,16 @@ int train_backward(const tao::BwdArgs& a0, cudaStream_t s) {
   }
   const size_t rsmem = ReadBwdSmem<D>::bytes(g.pmax, g.vmax, g.mmax);
   if (rsmem > 227 * 1024) return tfail(TAO_ERR_CAPACITY, "sequence too long for the read backward kernel");
-  bool tc_bwd = false;
-  if constexpr (D == 64) tc_bwd = attention_variant() == 1;   // dA / dC on tcgen05
+  const bool tc_bwd = attention_variant() == 1;   // dA / dC on tcgen05
   if (tc_bwd) {
-    if (!tsmem(read_bwd_kernel<64, true>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
+    if (!tsmem(read_bwd_kernel<D, true>, rsmem)) return tfail(TAO_ERR_CUDA, "smem attribute");
   } else if (!tsmem(read_bwd_kernel<D>, rsmem)) {
     return tfail(TAO_ERR_CUDA, "smem attribute");
   }
   constexpr int NQ = ReadBwdSmem<D>::NQ;
   if (ev0) cudaEventRecord(ev0, s);
   if (tc_bwd)
-    read_bwd_kernel<64, true><<<dim3(B * H * (256 / NQ), g.tiles), ReadBwdSmem<D>::NT, rsmem, s>>>(a);
+    read_bwd_kernel<D, true><<<dim3(B * H * (256 / NQ), g.tiles), ReadBwdSmem<D>::NT, rsmem, s>>>(a);
   else
     read_bwd_kernel<D><<<dim3(B * H * (256 / NQ), g.tiles), ReadBwdSmem<D>::NT, rsmem, s>>>(a);
   if (ev1) cudaEventRecord(ev1, s);

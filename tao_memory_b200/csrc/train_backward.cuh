@@ -624,8 +624,11 @@ TAO_DEVI int dhv_off(int r, int d) {
   return r * D + ((((d >> 2) ^ (r & 7))) << 2) + (d & 3);
 }
 
-// TC (width 64): dA and dC on tcgen05 over the tile's dense query rows (a separate
-// instantiation: each kernel carries one contraction path).
+// TC: dA and dC on tcgen05 over the tile's dense query rows (a separate instantiation:
+// each kernel carries one contraction path).  The gn, A and C tiles are then laid out
+// as 64-channel 128B-swizzled atoms (the layout of a TMA box; at width 64 the same as
+// the ldmatrix swizzle of the mma.sync path).  Width 128 (128 queries, two threads per
+// query): each thread forms and consumes one 64-channel half of its query's rows.
 template <int D, bool TC = false>
 __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs a) {
   using namespace wa;
@@ -662,6 +665,13 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
   // mma.sync path; padded rows (D + 2 floats) for the row-per-thread accesses of the
   // tcgen05 path (two 64-bit wavefronts per warp)
   auto dho = [](int r, int d) -> int { return TC ? r * (D + 2) + d : dhv_off<D>(r, d); };
+  // byte offset of chunk c8 (8 channels) of row r in an operand tile of `rows` rows
+  auto opnd = [](int r, int c8, int rows) -> uint32_t {
+    if constexpr (TC)
+      return (uint32_t)((c8 >> 3) * rows * 128 + r * 128 + (((c8 & 7) ^ (r & 7)) << 4));
+    else
+      return (uint32_t)swz(r, c8 * 8, D);
+  };
   float* pwS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* pzS = reinterpret_cast<float*>(ptr);   ptr += (size_t)P * D * 4;
   float* dpwS = reinterpret_cast<float*>(ptr);  ptr += (size_t)P * D * 4;
@@ -771,7 +781,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
       for (int c = 0; c < D / 8; ++c) gv[c] = make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(hB + NQ * D * 2 + swz(q, c * 8, D)) = gv[c];
+    for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(hB + NQ * D * 2 + opnd(q, c, NQ)) = gv[c];
     gdS[q] = gdv;
     if (live) {
       const short* so = reinterpret_cast<const short*>(a.sel) + (((long long)b * a.dm.T + q0 + q) * a.dm.H + h) * a.mmax;
@@ -829,7 +839,7 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
   auto fetch_c = [&](int sf, int buf) {
     for (int idx = tid; idx < D * D / 8; idx += NT) {
       const int r = idx / (D / 8), c = idx % (D / 8);
-      cp_async16(sC + buf * D * D * 2 + swz(r, c * 8, D), cb + (long long)sf * D * D + r * D + c * 8, true);
+      cp_async16(sC + buf * D * D * 2 + opnd(r, c, D), cb + (long long)sf * D * D + r * D + c * 8, true);
     }
   };
   auto flush_page = [&](int pg) {
@@ -932,26 +942,30 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
     if constexpr (TC) {
       // ---- phase 2': A_s over the dense query rows (row q = query q, zero unless it
       // selected fine sf), K-major 128B-swizzled like the h and gn tiles
-      uint32_t hvw[D / 2];   // hv = bf16(h * pw[pg]) of this query, kept for the dA epilogue
+      // this thread's channels: all 64 at width 64, half tid / NQ of 128 at width 128
+      constexpr int DH = 64;
+      const int dch = (D == 64) ? 0 : (tid / NQ) * 64;
+      const bool selq = live && ((selB[(sf >> 5) * NQ + q] >> (sf & 31)) & 1u);
+      uint32_t hvw[DH / 2];  // hv = bf16(h * pw[pg]) of this query's channels, kept for the dA epilogue
       {
-        const bool selq = sel;
 #pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
+        for (int cc = 0; cc < DH / 8; ++cc) {
+          const int c = dch / 8 + cc;
           uint4 o = make_uint4(0, 0, 0, 0);
           if (selq) {
             const uint4 hc = *reinterpret_cast<const uint4*>(hB + swz(q, c * 8, D));
             const uint4 pc = *reinterpret_cast<const uint4*>(pw2 + (pg * D + c * 8) / 2);
             const uint4 wc = *reinterpret_cast<const uint4*>(w2 + c * 4);
-            hvw[c * 4] = hmul2u(hc.x, pc.x);
-            hvw[c * 4 + 1] = hmul2u(hc.y, pc.y);
-            hvw[c * 4 + 2] = hmul2u(hc.z, pc.z);
-            hvw[c * 4 + 3] = hmul2u(hc.w, pc.w);
-            o = make_uint4(hmul2u(hvw[c * 4], wc.x), hmul2u(hvw[c * 4 + 1], wc.y), hmul2u(hvw[c * 4 + 2], wc.z),
-                           hmul2u(hvw[c * 4 + 3], wc.w));
+            hvw[cc * 4] = hmul2u(hc.x, pc.x);
+            hvw[cc * 4 + 1] = hmul2u(hc.y, pc.y);
+            hvw[cc * 4 + 2] = hmul2u(hc.z, pc.z);
+            hvw[cc * 4 + 3] = hmul2u(hc.w, pc.w);
+            o = make_uint4(hmul2u(hvw[cc * 4], wc.x), hmul2u(hvw[cc * 4 + 1], wc.y), hmul2u(hvw[cc * 4 + 2], wc.z),
+                           hmul2u(hvw[cc * 4 + 3], wc.w));
           } else {
-            hvw[c * 4] = hvw[c * 4 + 1] = hvw[c * 4 + 2] = hvw[c * 4 + 3] = 0u;
+            hvw[cc * 4] = hvw[cc * 4 + 1] = hvw[cc * 4 + 2] = hvw[cc * 4 + 3] = 0u;
           }
-          *reinterpret_cast<uint4*>(aB + swz(q, c * 8, D)) = o;
+          *reinterpret_cast<uint4*>(aB + opnd(q, c, NQ)) = o;
         }
       }
       if (CB == 2) cp_wait<1>();
@@ -969,10 +983,11 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
         if (tc_ok) {
           constexpr uint32_t IA = tc::idesc_bf16(128, D, 0, 0), IC = tc::idesc_bf16(128, D, 1, 1);
 #pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            tc::mma(tbase, tc::sdesc(sG + k * 32, 16, 1024), tc::sdesc(cbuf + k * 32, 16, 1024), IA, k > 0 ? 1u : 0u);
-            tc::mma(tbase + 64, tc::sdesc(sG + 16384 + k * 32, 16, 1024), tc::sdesc(cbuf + k * 32, 16, 1024), IA,
-                    k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; ++k) {  // K = e in 64-channel atoms: gn atoms NQ rows, C atoms D rows
+            const uint32_t ga = sG + (k >> 2) * NQ * 128 + (k & 3) * 32, ca = cbuf + (k >> 2) * D * 128 + (k & 3) * 32;
+            tc::mma(tbase, tc::sdesc(ga, 16, 1024), tc::sdesc(ca, 16, 1024), IA, k > 0 ? 1u : 0u);
+            if constexpr (NQ == 256)   // query rows 128-255
+              tc::mma(tbase + 64, tc::sdesc(ga + 16384, 16, 1024), tc::sdesc(ca, 16, 1024), IA, k > 0 ? 1u : 0u);
           }
 #pragma unroll
           for (int k = 0; k < NQ / 16; ++k)
@@ -992,27 +1007,43 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
       } else if (okf) {
         tphase ^= 1u;
       }
-      // dC_s of this tile: TMEM lanes 0-63 (warps 0 and 1), the reference's per-tile bf16
+      // dC_s of this tile: TMEM lanes 0-(D-1) (warps 0 .. D/32-1), the reference's per-tile bf16
       const long long pair = (long long)(tile - 3) * (tile - 2) / 2 + sf;
       bf16* dcb = a.dcp + (((long long)b * a.dm.H + h) * a.npairs + pair) * (long long)D * D;
-      if (warp < D / 32) {
+      // width 64: warps 0-1, all 64 columns; width 128: every warp, lanes 32 (w % 4) and
+      // columns 64 (w / 4) .. + 63 (the adds of the two half tiles spread over 8 warps)
+      constexpr int DCW = 64;  // columns per warp
+      const int drow = (D == 64) ? tid : (warp & 3) * 32 + lane;
+      const int dcol0 = (D == 64) ? 0 : (warp >> 2) * 64;
+      if (D == 128 || warp < D / 32) {
 #pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int cc = 0; cc < DCW; cc += 32) {
+          const int c0 = dcol0 + cc;
           float v[32];
           if (okf) {
-            tc::tmem_ld32(tbase + 128 + ((uint32_t)(warp * 32) << 16) + c0, v);
+            tc::tmem_ld32(tbase + 128 + ((uint32_t)((warp & 3) * 32) << 16) + c0, v);
           } else {
 #pragma unroll
             for (int x = 0; x < 32; ++x) v[x] = 0.f;
           }
+          if constexpr (QS == 1) {
 #pragma unroll
-          for (int x = 0; x < 32; x += 8) {
-            uint4 o;
-            o.x = wa::pack_bf16(v[x], v[x + 1]);
-            o.y = wa::pack_bf16(v[x + 2], v[x + 3]);
-            o.z = wa::pack_bf16(v[x + 4], v[x + 5]);
-            o.w = wa::pack_bf16(v[x + 6], v[x + 7]);
-            *reinterpret_cast<uint4*>(dcb + (long long)tid * D + c0 + x) = o;
+            for (int x = 0; x < 32; x += 8) {
+              uint4 o;
+              o.x = wa::pack_bf16(v[x], v[x + 1]);
+              o.y = wa::pack_bf16(v[x + 2], v[x + 3]);
+              o.z = wa::pack_bf16(v[x + 4], v[x + 5]);
+              o.w = wa::pack_bf16(v[x + 6], v[x + 7]);
+              *reinterpret_cast<uint4*>(dcb + (long long)drow * D + c0 + x) = o;
+            }
+          } else {  // half tiles: both halves add into the zero-initialised partial
+#pragma unroll
+            for (int x = 0; x < 32; x += 8)  // eight bf16 adds per vector reduction
+              asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(
+                               dcb + (long long)drow * D + c0 + x),
+                           "r"(wa::pack_bf16(v[x], v[x + 1])), "r"(wa::pack_bf16(v[x + 2], v[x + 3])),
+                           "r"(wa::pack_bf16(v[x + 4], v[x + 5])), "r"(wa::pack_bf16(v[x + 6], v[x + 7]))
+                           : "memory");
           }
         }
       }
@@ -1024,21 +1055,21 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
         const float gdv = gdS[q];
         bf16* phT = reinterpret_cast<bf16*>(aB) + q;
 #pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int c0 = 0; c0 < DH; c0 += 32) {
           float v[32];
-          if (okf) {
-            tc::tmem_ld32(tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(warp >> 2) * 64 + c0, v);
+          if (okf) {  // accumulator of this query half (width 64) or this channel half (width 128)
+            tc::tmem_ld32(tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(tid / 128) * 64 + c0, v);
           } else {
 #pragma unroll
             for (int x = 0; x < 32; ++x) v[x] = 0.f;
           }
-          if (sel) {
+          if (selq) {
 #pragma unroll
             for (int x = 0; x < 32; x += 2) {
-              const int d = c0 + x;
+              const int d = dch + c0 + x;
               const uint32_t dav = wa::pack_bf16(__fadd_rn(rb(v[x]), gdv), __fadd_rn(rb(v[x + 1]), gdv));
               const uint32_t pw_ = hmul2u(dav, w2[d / 2]);
-              const uint32_t ph = hmul2u(dav, hvw[d / 2]);
+              const uint32_t ph = hmul2u(dav, hvw[(c0 + x) / 2]);
               float2* cell = reinterpret_cast<float2*>(dhvS + dho(q, d));
               float2 acc = *cell;
               acc.x += lo_f(pw_);
@@ -1053,9 +1084,9 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
       __syncthreads();
       // dw_s partials: the NW groups of 32 queries (one warp's), summed over the groups in
       // phase 4; only the selecting queries' products are read (the others hold A values)
-      static_assert(NQ / NW == 32, "one warp's queries per dw group");
-      for (int idx = tid; idx < NW * D; idx += NT) {
-        const int part = idx % NW, d = idx / NW;
+      constexpr int NPART = NQ / 32;  // groups of 32 queries: the first NQ threads' warps
+      for (int idx = tid; idx < NPART * D; idx += NT) {
+        const int part = idx % NPART, d = idx / NPART;
         const unsigned m = balS[part];
         const uint4* col = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(aB) + (long long)d * NQ +
                                                           part * 32);
@@ -1220,8 +1251,9 @@ __global__ void __launch_bounds__(ReadBwdSmem<D>::NT, 1) read_bwd_kernel(BwdArgs
     // ---- phase 4: dw_s -> d(z - pz) = bf16(bf16(dw) * w) : dz[s] += ., d page_z[pg] -= .
     for (int d = tid; d < D; d += NT) {
       float dw = 0.f;
+      constexpr int NDW = TC ? NQ / 32 : NW;  // dw partial groups written in phase 3 (3')
 #pragma unroll
-      for (int w = 0; w < NW; ++w) dw += dwS[w * D + d];
+      for (int w = 0; w < NDW; ++w) dw += dwS[w * D + d];
       const float ddiff = rb(__fmul_rn(rb(dw), bf(wS[d])));
       atomicAdd(a.dz + (((long long)b * a.dm.H + h) * a.dm.S + sf) * D + d, ddiff);
       dpzS[pg * D + d] -= ddiff;
