@@ -305,11 +305,11 @@ int tao_writer_stats(const void* k, const void* v, long long token_stride, long 
                      long long block_stride, int blocks, int heads, int width, float* gram,
                      float* cross, float* mass, void* stream);
 
-/* Select the windowed-attention kernels for this process (tao_window_attention, the
- * training forward and backward and the streaming prefill chunk over the ring):
- * 1 = tcgen05/TMEM kernels (default: forward and backward at widths 64 and 128, TMA
- * tiles for contiguous operands and cp.async tiles for the ring), 0 = mma.sync
- * kernels everywhere.  Outputs agree to fp32
+/* Select the tensor-core form of the windowed attention (tao_window_attention, the
+ * training forward and backward, the streaming prefill chunk over the ring) and of
+ * the training selected read and its backward, for this process: 1 = tcgen05/TMEM
+ * kernels (default, widths 64 and 128; TMA tiles for contiguous operands, cp.async
+ * tiles for the ring), 0 = mma.sync kernels everywhere.  Outputs agree to fp32
  * summation order.  No counterpart in the reference (it has one attention path,
  * flash_attention.py:16-37). */
 int tao_attention_variant(int variant);
