@@ -60,13 +60,13 @@ L2_CLEAN_BYTES = 1 << 28   # read after the memset: its dirty lines are written 
 # timed window's last steps), from the full capture
 #   ncu --set full --clock-control none -k regex:decode_fused_kernel --nvtx --nvtx-include "timed_decode/" \
 #       -c 1 -o fused64 python bench.py --no-train --no-serving --no-parity --steps 6 --warmup 3
-# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/decode_fused_kernel_decode128k.md).
+# (dram__bytes_read.sum + dram__bytes_write.sum of that capture).
 DECODE_TRAFFIC_BYTES = 46640896
 # The same for read_bwd_kernel in the train8k workload, one launch of
 #   ncu --section SpeedOfLight --section MemoryWorkloadAnalysis --section WarpStateStats \
 #       --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none \
 #       -k regex:read_bwd_kernel -s 3 -c 1 python bench.py --workload train8k --steps 2 --warmup 3
-# (profiles/read_bwd_kernel_train8k.md).
+# (dram__bytes_read.sum + dram__bytes_write.sum of that capture).
 READ_BWD_TRAFFIC_BYTES = 348393216
 
 
